@@ -1,0 +1,181 @@
+/*
+ * wave_b200.h -- C ABI of the B200 (sm_100a) wave-attention library.
+ *
+ * This is the drop-in boundary for wave-engine's causal multi-head wave
+ * attention forward.  Each entry point replaces one reference interface
+ * (cited as path:line inside the wave-engine source tree):
+ *
+ *   wb_attn_forward   <- src/common/attn.rs:90  wave_attention_forward(...)
+ *                        (callers: src/cpu/forward.rs:113,240,
+ *                         src/common/block.rs:47, and the Candle CustomOp
+ *                         src/candle_tier/custom_attn.rs:89-130 cpu_fwd)
+ *   wb_kv_prefill     <- src/common/kv_cache.rs:121-193 (attention part of
+ *                        prefill: phases, values, buckets, scores, out_proj)
+ *   wb_kv_decode      <- src/common/kv_cache.rs:263-335 (attention part of
+ *                        forward_one)
+ *   wb_attn_layer_*   <- src/common/attn.rs:19-46 WaveAttnHeadWeights /
+ *                        WaveAttnWeights (device-resident copy)
+ *   wb_kv_cache_*     <- src/common/kv_cache.rs:36-54 HeadCache/LayerCache/
+ *                        KvCache (device-resident, one slot per sequence)
+ *
+ * Conventions
+ *   - Every function returns int status: WB_OK (0) or a negative WB_E*.
+ *     No exceptions cross the ABI; nothing aborts or traps.  The message of
+ *     the last failure on the calling thread is returned by wb_last_error().
+ *   - All floating point data is fp32, row-major, in the reference's
+ *     layouts (a Rust Vec<Vec<f32>> [rows][cols] flattened row by row).
+ *   - Data pointers may be host or device memory; the library detects which
+ *     (cudaPointerGetAttributes).  Host inputs are copied into the
+ *     context's device staging buffer with cudaMemcpyAsync (pinned host
+ *     memory makes that copy asynchronous); when an output is host memory
+ *     the call synchronises the context's stream before returning.  With
+ *     device pointers only, the call is asynchronous on the context's
+ *     stream.
+ *   - A context is bound to one device and one stream and is not
+ *     thread-safe; use one context per thread (the reference runs attention
+ *     on a thread per batch element / per HTTP request).
+ *   - Results are pure functions of (weights, x, flags).  The prefill path
+ *     WB_PATH_TENSOR computes scores and PV on tcgen05 tensor cores in bf16
+ *     with fp32 accumulation (max-abs error vs the reference <= 2e-3);
+ *     WB_PATH_EXACT runs all-fp32 SIMT kernels that follow the reference's
+ *     operation order (max-abs error <= 1e-5).
+ */
+#ifndef WAVE_B200_H
+#define WAVE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define WB_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define WB_API __attribute__((visibility("default")))
+#else
+#define WB_API
+#endif
+
+/* status codes */
+#define WB_OK 0
+#define WB_EINVAL -1    /* bad argument or shape */
+#define WB_ENOMEM -2    /* device or pinned allocation failed */
+#define WB_ECUDA -3     /* CUDA runtime / driver error */
+#define WB_ENOTSUP -4   /* feature not supported (e.g. pathway cache) */
+#define WB_ETIMEOUT -5  /* a device-side bounded wait gave up */
+#define WB_ENODEV -6    /* no usable sm_100 device */
+
+/* flags for wb_attn_forward / wb_kv_prefill / wb_kv_decode */
+#define WB_PATH_TENSOR 0x0      /* default: tcgen05 bf16 scores + PV */
+#define WB_PATH_EXACT 0x1       /* all-fp32 SIMT kernels, reference order */
+#define WB_NO_CONTENT 0x2       /* ignore content_proj even if present */
+#define WB_RETURN_PATHWAY 0x4   /* return_pathway_cache=true: WB_ENOTSUP */
+
+typedef struct wb_context wb_context;
+typedef struct wb_attn_layer wb_attn_layer;
+typedef struct wb_kv_cache wb_kv_cache;
+
+/* Host-side view of one block's attention weights (attn.rs:19-46),
+ * flattened per head.  All pointers are HOST memory and are only read
+ * during wb_attn_layer_create.
+ *   harmonic_raw  [n_head]                 (n_h = softplus(harmonic_raw))
+ *   phase_proj_w  [n_head][2][n_embd]      phase_proj_b [n_head][2]
+ *   v_proj_w      [n_head][hd][hd]         v_proj_b     [n_head][hd]
+ *   content_proj_w[n_head][C][n_embd]      content_proj_b [n_head][C]
+ *                 (C = content_dim, 0 or 16; NULL when 0)
+ *   out_proj_w    [n_embd][n_embd]         out_proj_b   [n_embd]
+ * with hd = n_embd / n_head. */
+typedef struct {
+    int32_t n_embd;
+    int32_t n_head;
+    int32_t content_dim;
+    const float *harmonic_raw;
+    const float *phase_proj_w;
+    const float *phase_proj_b;
+    const float *v_proj_w;
+    const float *v_proj_b;
+    const float *content_proj_w;
+    const float *content_proj_b;
+    const float *out_proj_w;
+    const float *out_proj_b;
+} wb_attn_weights_desc;
+
+/* ---- library / context ------------------------------------------------ */
+WB_API int wb_abi_version(void);
+/* Thread-local message for the last non-zero status on this thread. */
+WB_API const char *wb_last_error(void);
+/* Create a context on `device` (CUDA ordinal) using its own stream. */
+WB_API int wb_context_create(int device, wb_context **out);
+WB_API int wb_context_destroy(wb_context *ctx);
+/* Use an external cudaStream_t (NULL = the context's own stream). */
+WB_API int wb_context_set_stream(wb_context *ctx, void *cuda_stream);
+WB_API int wb_context_synchronize(wb_context *ctx);
+/* Device error word: non-zero when a bounded device-side wait gave up or a
+ * kernel-side check failed since the last reset.  Resets it. */
+WB_API int wb_context_take_device_error(wb_context *ctx, uint32_t *code_out);
+
+/* ---- weights (attn.rs:19-46) ------------------------------------------ */
+WB_API int wb_attn_layer_create(wb_context *ctx, const wb_attn_weights_desc *w, wb_attn_layer **out);
+WB_API int wb_attn_layer_destroy(wb_attn_layer *layer);
+/* Reference weight initialisation (src/common/wave_model.rs:39-81,
+ * init_linear + init_block_attn) on the xorshift64 stream of
+ * src/common/rng.rs:24-39.  *rng_state advances exactly as the reference's
+ * Rng does.  Buffers are host memory in the layouts above. */
+WB_API int wb_init_block_attn(uint64_t *rng_state, int n_head, int n_embd, int content_dim,
+                       float *harmonic_raw, float *phase_proj_w, float *phase_proj_b,
+                       float *v_proj_w, float *v_proj_b, float *content_proj_w,
+                       float *content_proj_b, float *out_proj_w, float *out_proj_b);
+
+/* ---- prefill forward (attn.rs:90-305) --------------------------------- */
+/* x [batch][seq_len][n_embd] -> y [batch][seq_len][n_embd]; each sequence is
+ * an independent call of the reference.  att_w (nullable) receives the
+ * reference's second return value [batch][n_head][seq_len][seq_len]
+ * (softmax weights, -inf above the diagonal exactly as attn.rs:240 leaves
+ * them); requesting it routes the scores through WB_PATH_EXACT.
+ * phases_out (nullable) receives the per-head phases [batch][n_head][seq_len]
+ * used for the bucket mask. */
+WB_API int wb_attn_forward(wb_context *ctx, const wb_attn_layer *layer, const float *x, int batch,
+                    int seq_len, int flags, float *y, float *att_w, float *phases_out);
+
+/* ---- KV cache (kv_cache.rs:36-54) ------------------------------------- */
+/* One cache holds n_layers x max_seqs slots of capacity max_ctx positions,
+ * each with per-head phases (f32), buckets (u8) and values (f32 [hd]). */
+WB_API int wb_kv_cache_create(wb_context *ctx, int n_layers, int n_head, int head_dim, int max_seqs,
+                       int max_ctx, wb_kv_cache **out);
+WB_API int wb_kv_cache_destroy(wb_kv_cache *cache);
+/* Number of cached positions of (layer, seq). */
+WB_API int wb_kv_cache_length(wb_kv_cache *cache, int layer, int seq, int *len_out);
+/* Empty a sequence slot in every layer (a new request). */
+WB_API int wb_kv_cache_reset_seq(wb_kv_cache *cache, int seq);
+/* Load n positions of one (layer, seq) slot from raw arrays: phases
+ * [n_head][n], values [n_head][n][head_dim] (host or device).  Buckets are
+ * derived from the phases exactly as kv_cache.rs:66-70.  Replaces the slot's
+ * contents. */
+WB_API int wb_kv_cache_load(wb_context *ctx, wb_kv_cache *cache, int layer, int seq, int n,
+                     const float *phases, const float *values);
+/* Read one (layer, seq) slot back: phases [n_head][len], buckets
+ * [n_head][len] (u8), values [n_head][len][head_dim]; any may be NULL. */
+WB_API int wb_kv_cache_read(wb_context *ctx, wb_kv_cache *cache, int layer, int seq, float *phases,
+                     uint8_t *buckets, float *values);
+
+/* kv_cache.rs:121-193: prompt attention for n_seq sequences of seq_len
+ * positions each (x [n_seq][seq_len][n_embd]) into EMPTY slots seq_ids[i]
+ * of `layer_idx`; writes y [n_seq][seq_len][n_embd] and fills the slots.
+ * The serve copy of the math never adds the content bias. */
+WB_API int wb_kv_prefill(wb_context *ctx, wb_kv_cache *cache, int layer_idx, const wb_attn_layer *layer,
+                  const int32_t *seq_ids, int n_seq, const float *x, int seq_len, int flags,
+                  float *y);
+
+/* kv_cache.rs:263-335: one new position per sequence (x [n_seq][n_embd])
+ * against slots seq_ids[i] of `layer_idx`; writes y [n_seq][n_embd] and
+ * appends the new phase/bucket/value to each slot.  seq_ids may be host or
+ * device memory. */
+WB_API int wb_kv_decode(wb_context *ctx, wb_kv_cache *cache, int layer_idx, const wb_attn_layer *layer,
+                 const int32_t *seq_ids, int n_seq, const float *x, int flags, float *y);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* WAVE_B200_H */

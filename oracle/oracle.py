@@ -1,0 +1,187 @@
+"""ctypes wrapper of the CPU oracle (``oracle/wave_oracle.c``).
+
+TEST INFRASTRUCTURE ONLY: imported by ``tests/``, by
+``__graft_entry__.smoke()`` and by the CPU-baseline leg of ``bench.py``, as
+the checker and the timed CPU restatement of the reference.  The product
+path (``wave_engine_b200``) never imports it.
+
+Parity status: unpinned by reference outputs (the Rust reference cannot be
+built here and ships no forward golden vectors); pinned by hand-derived
+known-answer cases, see ``tests/golden/make_golden.py``.
+
+Weights are a dict of numpy float32 arrays in the reference layouts:
+    harmonic_raw [H]; phase_proj_w [H,2,E]; phase_proj_b [H,2];
+    v_proj_w [H,d,d]; v_proj_b [H,d]; content_proj_w [H,C,E] or None;
+    content_proj_b [H,C] or None; out_proj_w [E,E]; out_proj_b [E].
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+from . import build as _build
+
+_F = C.POINTER(C.c_float)
+_I = C.POINTER(C.c_int)
+
+
+class _Weights(C.Structure):
+    _fields_ = [
+        ("n_embd", C.c_int), ("n_head", C.c_int), ("content_dim", C.c_int),
+        ("harmonic_raw", _F), ("phase_w", _F), ("phase_b", _F), ("v_w", _F), ("v_b", _F),
+        ("content_w", _F), ("content_b", _F), ("out_w", _F), ("out_b", _F),
+    ]
+
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        path = _build.build()
+        l = C.CDLL(str(path))
+        l.wo_attn_forward.argtypes = [C.POINTER(_Weights), _F, C.c_int, _F, _F, _F, _F, C.c_int]
+        l.wo_attn_forward_batch.argtypes = [C.POINTER(_Weights), _F, C.c_int, C.c_int, _F, C.c_int]
+        l.wo_kv_prefill.argtypes = [C.POINTER(_Weights), _F, C.c_int, _F, _F, _I, _F, C.c_int, _I]
+        l.wo_kv_decode.argtypes = [C.POINTER(_Weights), _F, _F, _F, _I, _F, C.c_int, _I]
+        l.wo_phase_to_bucket.argtypes = [C.c_float]
+        l.wo_phase_to_bucket.restype = C.c_int
+        l.wo_softplus.argtypes = [C.c_float]
+        l.wo_softplus.restype = C.c_float
+        l.wo_init_block_attn.argtypes = [C.POINTER(C.c_uint64), C.c_int, C.c_int, C.c_int] + [_F] * 9
+        _lib = l
+    return _lib
+
+
+def _fp(a):
+    return None if a is None else a.ctypes.data_as(_F)
+
+
+def _f32(a):
+    return None if a is None else np.ascontiguousarray(a, dtype=np.float32)
+
+
+class _Packed:
+    """Keeps contiguous float32 copies alive while the C struct points at them."""
+
+    def __init__(self, w: dict):
+        self.arrs = {k: _f32(w.get(k)) for k in (
+            "harmonic_raw", "phase_proj_w", "phase_proj_b", "v_proj_w", "v_proj_b",
+            "content_proj_w", "content_proj_b", "out_proj_w", "out_proj_b")}
+        a = self.arrs
+        H = a["harmonic_raw"].shape[0]
+        E = a["out_proj_w"].shape[0]
+        cw = a["content_proj_w"]
+        Cd = 0 if cw is None or cw.size == 0 else cw.shape[1]
+        if Cd == 0:
+            a["content_proj_w"] = a["content_proj_b"] = None
+        self.H, self.E, self.C = H, E, Cd
+        self.s = _Weights(E, H, Cd, _fp(a["harmonic_raw"]), _fp(a["phase_proj_w"]), _fp(a["phase_proj_b"]),
+                          _fp(a["v_proj_w"]), _fp(a["v_proj_b"]), _fp(a["content_proj_w"]),
+                          _fp(a["content_proj_b"]), _fp(a["out_proj_w"]), _fp(a["out_proj_b"]))
+
+
+def softplus(x: float) -> float:
+    return float(lib().wo_softplus(C.c_float(x)))
+
+
+def phase_to_bucket(theta) -> np.ndarray:
+    t = np.asarray(theta, dtype=np.float32)
+    f = np.vectorize(lambda v: lib().wo_phase_to_bucket(C.c_float(v)), otypes=[np.int32])
+    return f(t)
+
+
+def attn_forward(w: dict, x: np.ndarray, *, want_att_w: bool = False, phase_override=None,
+                 n_threads: int = 1):
+    """wave_attention_forward for one sequence x [T,E] (attn.rs:90-305).
+
+    Returns (y [T,E], att_w [H,T,T] or None, phases [H,T])."""
+    p = _Packed(w)
+    x = _f32(x)
+    T = x.shape[0]
+    y = np.empty((T, p.E), np.float32)
+    aw = np.empty((p.H, T, T), np.float32) if want_att_w else None
+    ph = np.empty((p.H, T), np.float32)
+    po = _f32(phase_override)
+    rc = lib().wo_attn_forward(C.byref(p.s), _fp(x), T, _fp(y), _fp(aw), _fp(po), _fp(ph), n_threads)
+    if rc != 0:
+        raise RuntimeError("oracle wo_attn_forward failed")
+    return y, aw, ph
+
+
+def attn_forward_batch(w: dict, x: np.ndarray, n_threads: int | None = None) -> np.ndarray:
+    """x [B,T,E] -> y [B,T,E]; (sequence, head) items on n_threads threads."""
+    p = _Packed(w)
+    x = _f32(x)
+    B, T, _ = x.shape
+    y = np.empty_like(x)
+    nt = n_threads or os.cpu_count() or 1
+    if lib().wo_attn_forward_batch(C.byref(p.s), _fp(x), B, T, _fp(y), nt) != 0:
+        raise RuntimeError("oracle wo_attn_forward_batch failed")
+    return y
+
+
+class KvState:
+    """One layer's cache of one sequence (kv_cache.rs:36-41 HeadCache per head)."""
+
+    def __init__(self, n_head: int, head_dim: int, cap: int):
+        self.cap = cap
+        self.phases = np.zeros((n_head, cap), np.float32)
+        self.buckets = np.zeros((n_head, cap), np.int32)
+        self.values = np.zeros((n_head, cap, head_dim), np.float32)
+        self.n = C.c_int(0)
+
+    @property
+    def n_cached(self) -> int:
+        return self.n.value
+
+
+def kv_prefill(w: dict, x: np.ndarray, cap: int) -> tuple[np.ndarray, KvState]:
+    """Attention part of kv_cache.rs:121-193 for one prompt x [T,E]."""
+    p = _Packed(w)
+    x = _f32(x)
+    T = x.shape[0]
+    st = KvState(p.H, p.E // p.H, cap)
+    y = np.empty((T, p.E), np.float32)
+    rc = lib().wo_kv_prefill(C.byref(p.s), _fp(x), T, _fp(y), _fp(st.phases),
+                             st.buckets.ctypes.data_as(_I), _fp(st.values), cap, C.byref(st.n))
+    if rc != 0:
+        raise RuntimeError("oracle wo_kv_prefill failed")
+    return y, st
+
+
+def kv_decode(w: dict, x: np.ndarray, st: KvState) -> np.ndarray:
+    """Attention part of kv_cache.rs:263-335 for one new position x [E]."""
+    p = _Packed(w)
+    x = _f32(x)
+    y = np.empty((p.E,), np.float32)
+    rc = lib().wo_kv_decode(C.byref(p.s), _fp(x), _fp(y), _fp(st.phases), st.buckets.ctypes.data_as(_I),
+                            _fp(st.values), st.cap, C.byref(st.n))
+    if rc != 0:
+        raise RuntimeError("oracle wo_kv_decode failed")
+    return y
+
+
+def init_block_attn(state: int, n_head: int, n_embd: int, content_dim: int) -> tuple[dict, int]:
+    """wave_model.rs:57-81 on the xorshift64 stream; returns (weights, new state)."""
+    d = n_embd // n_head
+    w = {
+        "harmonic_raw": np.empty(n_head, np.float32),
+        "phase_proj_w": np.empty((n_head, 2, n_embd), np.float32),
+        "phase_proj_b": np.empty((n_head, 2), np.float32),
+        "v_proj_w": np.empty((n_head, d, d), np.float32),
+        "v_proj_b": np.empty((n_head, d), np.float32),
+        "content_proj_w": np.empty((n_head, content_dim, n_embd), np.float32) if content_dim else None,
+        "content_proj_b": np.empty((n_head, content_dim), np.float32) if content_dim else None,
+        "out_proj_w": np.empty((n_embd, n_embd), np.float32),
+        "out_proj_b": np.empty(n_embd, np.float32),
+    }
+    s = C.c_uint64(state)
+    lib().wo_init_block_attn(C.byref(s), n_head, n_embd, content_dim,
+                             *[_fp(w[k]) for k in ("harmonic_raw", "phase_proj_w", "phase_proj_b", "v_proj_w",
+                                                   "v_proj_b", "content_proj_w", "content_proj_b",
+                                                   "out_proj_w", "out_proj_b")])
+    return w, s.value

@@ -1,0 +1,110 @@
+"""CPU tests of the oracle (oracle/wave_oracle.c) against the known-answer
+fixtures and the reference's invariants.  No GPU needed."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from oracle import oracle
+from tests.parity import buckets_of, check
+
+KAT_TOL = (2e-6, 2e-6)
+
+
+@pytest.mark.parametrize("name", ["kat_t1", "kat_uniform", "kat_mask"])
+def test_oracle_matches_known_answers(kat, name):
+    c = kat[name]
+    y, aw, _ = oracle.attn_forward(c["w"], c["x"], want_att_w=True)
+    r = check(name + "/y", y, c["y"], KAT_TOL)
+    assert r.passed, str(r)
+    r = check(name + "/att", aw, c["att"], KAT_TOL)
+    assert r.passed, str(r)
+
+
+def test_oracle_mask_pattern(kat):
+    """Masked keys get weight exactly 0 and keys above the diagonal -inf
+    (attn.rs:187 initialises scores to -inf; :233 zeroes masked ones)."""
+    c = kat["kat_mask"]
+    _, aw, _ = oracle.attn_forward(c["w"], c["x"], want_att_w=True)
+    exp = c["att"]
+    assert np.array_equal(aw == 0.0, exp == 0.0)
+    assert np.array_equal(np.isneginf(aw), np.isneginf(exp))
+
+
+def test_oracle_decode_equals_prefill_last_row(kat):
+    """forward_one after prefill(T) == prefill(T+1) last row (kv_cache.rs)."""
+    c = kat["kat_decode"]
+    x = c["x"]
+    T = x.shape[0] - 1
+    y_full, st_full = oracle.kv_prefill(c["w"], x, cap=T + 1)
+    y_pre, st = oracle.kv_prefill(c["w"], x[:T], cap=T + 1)
+    y_dec = oracle.kv_decode(c["w"], x[T], st)
+    assert np.array_equal(y_pre, y_full[:T])
+    assert np.array_equal(y_dec, y_full[T])
+    assert st.n_cached == T + 1
+    assert np.array_equal(st.phases, st_full.phases)
+    assert np.array_equal(st.values, st_full.values)
+    r = check("kat_decode/y", y_full, c["y"], KAT_TOL)
+    assert r.passed, str(r)
+
+
+def test_oracle_threads_do_not_change_results():
+    w, _ = oracle.init_block_attn(42, 4, 32, 16)
+    x = np.random.default_rng(0).standard_normal((40, 32)).astype(np.float32)
+    y1, a1, p1 = oracle.attn_forward(w, x, want_att_w=True, n_threads=1)
+    y4, a4, p4 = oracle.attn_forward(w, x, want_att_w=True, n_threads=4)
+    assert np.array_equal(y1, y4) and np.array_equal(a1, a4) and np.array_equal(p1, p4)
+    yb = oracle.attn_forward_batch(w, np.stack([x, x[::-1].copy()]), n_threads=3)
+    assert np.array_equal(yb[0], y1)
+    assert np.array_equal(yb[1], oracle.attn_forward(w, x[::-1].copy())[0])
+
+
+def test_oracle_phase_override_reproduces_own_phases():
+    w, _ = oracle.init_block_attn(7, 2, 16, 16)
+    x = np.random.default_rng(1).standard_normal((20, 16)).astype(np.float32)
+    y, aw, ph = oracle.attn_forward(w, x, want_att_w=True)
+    y2, aw2, _ = oracle.attn_forward(w, x, want_att_w=True, phase_override=ph)
+    assert np.array_equal(y, y2) and np.array_equal(aw, aw2)
+
+
+def test_oracle_bucket_function_edges():
+    tau = np.float32(6.2831855)
+    w = tau / np.float32(8)
+    # +pi lands in bucket 3, not 4: fmodf(pi, tau) + tau rounds 3*pi down in
+    # f32, so the normalised phase is just below pi (kv_cache.rs:68).
+    cases = {0.0: 0, -0.0: 0, float(np.float32(np.pi)): 3, float(-np.float32(np.pi)): 4,
+             float(w * np.float32(0.999)): 0, float(w * np.float32(1.001)): 1,
+             float(np.float32(-1e-6)): 7, float(np.nextafter(np.float32(0), np.float32(-1))): 0, float("nan"): 0}
+    for th, b in cases.items():
+        assert oracle.phase_to_bucket(th) == b, (th, oracle.phase_to_bucket(th), b)
+    grid = np.random.default_rng(3).uniform(-np.pi, np.pi, 20000).astype(np.float32)
+    assert np.array_equal(oracle.phase_to_bucket(grid), buckets_of(grid))
+
+
+def test_oracle_softplus_and_harmonic_init():
+    # math/core.rs:5 and wave_model.rs:73: n_h = softplus(ln((h+1)/2)) = ln(1 + (h+1)/2)
+    for h in range(12):
+        raw = np.float32(np.log(np.float32((h + 1) * 0.5)))
+        assert abs(oracle.softplus(float(raw)) - np.log1p((h + 1) / 2)) < 1e-6
+    assert oracle.softplus(25.0) == 25.0
+
+
+def test_oracle_init_block_attn_draw_order():
+    """init_linear draws U(+-1/sqrt(in)) row by row (wave_model.rs:39-46) in
+    init_block_attn order (wave_model.rs:64-80); check the first draws by
+    restating xorshift64 (rng.rs:24-39) in Python."""
+    def xs(s):
+        s ^= (s << 13) & 0xFFFFFFFFFFFFFFFF
+        s ^= s >> 7
+        s ^= (s << 17) & 0xFFFFFFFFFFFFFFFF
+        return s
+    s = 1234
+    draws = []
+    for _ in range(3):
+        s = xs(s)
+        f = np.float32(s >> 40) / np.float32(1 << 24)
+        draws.append((f * np.float32(2) - np.float32(1)) * (np.float32(1) / np.sqrt(np.float32(32))))
+    w, _ = oracle.init_block_attn(1234, 4, 32, 16)
+    assert np.array_equal(w["phase_proj_w"][0, 0, :3], np.array(draws, np.float32))
+    assert np.all(np.abs(w["out_proj_w"]) <= 1 / np.sqrt(32) + 1e-7)
+    assert np.all(w["phase_proj_b"] == 0) and np.all(w["out_proj_b"] == 0)

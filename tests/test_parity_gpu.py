@@ -1,0 +1,200 @@
+"""GPU parity of the CUDA library against the CPU oracle (reference math).
+
+Every case runs through the C ABI (wave_engine_b200 -> libwave_b200.so).
+Tolerances: WB_PATH_EXACT (all-fp32 SIMT) max-abs 1e-5; WB_PATH_TENSOR
+(tcgen05 bf16 scores/PV, fp32 accumulation) max-abs 2e-3.
+
+Phases go through atan2f, whose CUDA and glibc implementations differ in the
+last bits, so a phase within a few ulps of a bucket boundary can land in the
+neighbouring bucket.  The comparison therefore checks the phases to 2e-6 rad,
+allows bucket differences only within 1e-5 rad of a boundary, and in that
+case recomputes the oracle with the GPU's phases (mask-conditioned parity) so
+that the rest of the math is still compared element by element.
+"""
+from __future__ import annotations
+
+import os
+
+import numpy as np
+import pytest
+
+from oracle import oracle
+from tests.parity import EXACT_TOL, TENSOR_TOL, boundary_distance, buckets_of, check, phase_diff
+
+pytestmark = pytest.mark.gpu
+
+NT = os.cpu_count() or 1
+
+
+def make_case(E, H, C, B, T, seed, init="gauss"):
+    import wave_engine_b200 as wb
+    if init == "gauss":
+        w = wb.gaussian_block_attn(seed, H, E, C)
+    else:
+        w = wb.init_block_attn(wb.Rng(seed), H, E, C)
+    x = np.random.default_rng(seed + 1).standard_normal((B, T, E)).astype(np.float32)
+    return w, x
+
+
+def oracle_for(wp, x, gpu_phases, use_content=True):
+    """Oracle outputs per sequence, conditioned on the GPU's buckets where
+    (and only where) a phase sits within 1e-5 rad of a bucket boundary."""
+    if not use_content:
+        wp = dict(wp, content_proj_w=None, content_proj_b=None)
+    ys, aws, flips = [], [], 0
+    for b in range(x.shape[0]):
+        y, aw, ph = oracle.attn_forward(wp, x[b], want_att_w=True, n_threads=NT)
+        gp = gpu_phases[b]
+        assert phase_diff(gp, ph).max() <= 2e-6, f"phase mismatch {phase_diff(gp, ph).max()}"
+        diff = buckets_of(gp) != buckets_of(ph)
+        if diff.any():
+            assert (boundary_distance(ph)[diff] < 1e-5).all(), "bucket differs away from a boundary"
+            flips += int(diff.sum())
+            y, aw, _ = oracle.attn_forward(wp, x[b], want_att_w=True, phase_override=gp, n_threads=NT)
+        ys.append(y)
+        aws.append(aw)
+    return np.stack(ys), np.stack(aws), flips
+
+
+SHAPES = [
+    # E, H, C, B, T
+    (168, 4, 16, 2, 64),    # 168-dim research model (head_dim 42)
+    (384, 8, 16, 1, 129),   # 384-dim grammar model (head_dim 48), ragged T
+    (768, 12, 16, 2, 130),  # 768-dim production model (head_dim 64)
+    (768, 12, 0, 1, 17),    # --freeze-ode: no content projection
+    (64, 1, 16, 3, 1),      # T = 1
+    (64, 2, 16, 2, 2),      # T = 2
+]
+
+
+@pytest.mark.parametrize("E,H,C,B,T", SHAPES)
+@pytest.mark.parametrize("init", ["gauss", "reference"])
+def test_exact_path_matches_oracle(ctx, E, H, C, B, T, init):
+    import wave_engine_b200 as wb
+    w, x = make_case(E, H, C, B, T, seed=E + T, init=init)
+    y, aw, _, ph = wb.wave_attention_forward(w, x, E // 2, path="exact", return_att_weights=True,
+                                            return_phases=True, ctx=ctx)
+    oy, oaw, flips = oracle_for(w.packed(), x, ph)
+    r = check("y", y, oy, EXACT_TOL)
+    assert r.passed, str(r)
+    r = check("att_w", aw, oaw, EXACT_TOL)
+    assert r.passed, str(r)
+    assert ctx.take_device_error() == 0
+
+
+@pytest.mark.parametrize("E,H,C,B,T", SHAPES + [(768, 12, 16, 2, 1024), (4096, 32, 16, 1, 48)])
+def test_tensor_path_matches_oracle(ctx, E, H, C, B, T):
+    import wave_engine_b200 as wb
+    w, x = make_case(E, H, C, B, T, seed=3 * E + T)
+    y, _, _, ph = wb.wave_attention_forward(w, x, E // 2, path="tensor", return_phases=True, ctx=ctx)
+    oy, _, flips = oracle_for(w.packed(), x, ph)
+    r = check("y", y, oy, TENSOR_TOL)
+    assert r.passed, str(r)
+    assert ctx.take_device_error() == 0
+
+
+def test_tensor_path_reference_init_and_no_content(ctx):
+    import wave_engine_b200 as wb
+    w, x = make_case(384, 8, 16, 2, 200, seed=5, init="reference")
+    for use_content in (True, False):
+        y, _, _, ph = wb.wave_attention_forward(w, x, 192, path="tensor", use_content=use_content,
+                                                return_phases=True, ctx=ctx)
+        oy, _, _ = oracle_for(w.packed(), x, ph, use_content=use_content)
+        r = check(f"y content={use_content}", y, oy, TENSOR_TOL)
+        assert r.passed, str(r)
+
+
+def test_single_sequence_and_torch_inputs(ctx):
+    import torch
+    import wave_engine_b200 as wb
+    w, x = make_case(168, 4, 16, 1, 33, seed=11)
+    y_np, att, cache = wb.wave_attention_forward(w, x[0], 84, path="exact", ctx=ctx)
+    assert y_np.shape == (33, 168) and att == [] and cache is None
+    xt = torch.from_numpy(x[0]).cuda()
+    y_t, _, _ = wb.wave_attention_forward(w, xt, 84, path="exact", ctx=ctx)
+    torch.cuda.synchronize()
+    assert y_t.is_cuda and np.array_equal(y_t.cpu().numpy(), y_np)
+
+
+def test_argument_errors(ctx):
+    import wave_engine_b200 as wb
+    w, x = make_case(168, 4, 16, 1, 8, seed=2)
+    with pytest.raises(ValueError):
+        wb.wave_attention_forward(w, x, 80, ctx=ctx)  # n_bands mismatch
+    with pytest.raises(NotImplementedError):
+        wb.wave_attention_forward(w, x, 84, return_pathway_cache=True, ctx=ctx)
+    with pytest.raises(ValueError):
+        wb.wave_attention_forward(w, x[0, :, :100], 50, ctx=ctx)  # weights for another n_embd
+
+
+# ---------------------------------------------------------------------------
+# KV cache: prefill + decode (kv_cache.rs)
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("path,tol", [("exact", EXACT_TOL), ("tensor", TENSOR_TOL)])
+@pytest.mark.parametrize("E,H", [(168, 4), (768, 12)])
+def test_kv_prefill_and_decode_match_oracle(ctx, path, tol, E, H):
+    import wave_engine_b200 as wb
+    n_seq, T, steps = 3, 40, 6
+    w, x = make_case(E, H, 16, n_seq, T + steps, seed=E + 17)
+    wp = w.packed()
+    d = E // H
+    cache = wb.KvCache(1, H, d, max_seqs=4, max_ctx=T + steps, ctx=ctx)
+    seq_ids = np.array([2, 0, 3], np.int32)
+    y = cache.prefill(0, w, x[:, :T], seq_ids, path=path)
+    states = []
+    for i in range(n_seq):
+        oy, st = oracle.kv_prefill(wp, x[i, :T], cap=T + steps)
+        states.append(st)
+        ph, bk, vv = cache.read(0, int(seq_ids[i]))
+        assert phase_diff(ph, st.phases[:, :T]).max() <= 2e-6
+        same = bk == st.buckets[:, :T]
+        assert (same | (boundary_distance(st.phases[:, :T]) < 1e-5)).all()
+        if same.all():
+            r = check(f"prefill y seq{i}", y[i], oy, tol)
+            assert r.passed, str(r)
+        assert check("values", vv, st.values[:, :T], EXACT_TOL).passed
+    for s in range(steps):
+        yd = cache.forward_one(0, w, x[:, T + s].copy(), seq_ids, path=path)
+        for i in range(n_seq):
+            oyd = oracle.kv_decode(wp, x[i, T + s], states[i])
+            r = check(f"decode step {s} seq{i}", yd[i], oyd, tol)
+            assert r.passed, str(r)
+    for i in range(n_seq):
+        assert cache.n_cached(0, int(seq_ids[i])) == T + steps
+    assert cache.n_cached(0, 1) == 0
+    assert ctx.take_device_error() == 0
+
+
+def test_kv_decode_equals_prefill_last_row(ctx):
+    """GPU forward_one after prefill(T) agrees with prefill(T+1)'s last row."""
+    import wave_engine_b200 as wb
+    w, x = make_case(768, 12, 0, 2, 65, seed=9)
+    c1 = wb.KvCache(1, 12, 64, max_seqs=2, max_ctx=65, ctx=ctx)
+    c2 = wb.KvCache(1, 12, 64, max_seqs=2, max_ctx=65, ctx=ctx)
+    y_full = c1.prefill(0, w, x, [0, 1], path="exact")
+    c2.prefill(0, w, x[:, :64].copy(), [0, 1], path="exact")
+    y_dec = c2.forward_one(0, w, x[:, 64].copy(), [0, 1], path="exact")
+    r = check("decode vs prefill", y_dec, y_full[:, 64], (1e-6, 1e-6))
+    assert r.passed, str(r)
+
+
+def test_kv_cache_load_read_and_errors(ctx):
+    import wave_engine_b200 as wb
+    H, d, n = 4, 42, 50
+    cache = wb.KvCache(2, H, d, max_seqs=2, max_ctx=64, ctx=ctx)
+    g = np.random.default_rng(4)
+    ph = np.arctan2(g.standard_normal((H, n)), g.standard_normal((H, n))).astype(np.float32)
+    vv = g.standard_normal((H, n, d)).astype(np.float32)
+    cache.load(1, 1, ph, vv)
+    rp, rb, rv = cache.read(1, 1)
+    assert np.array_equal(rp, ph) and np.array_equal(rv, vv)
+    assert np.array_equal(rb, oracle.phase_to_bucket(ph).astype(np.uint8))
+    w, x = make_case(168, 4, 16, 1, 70, seed=3)
+    with pytest.raises(wb.WaveB200Error):
+        cache.prefill(0, w, x, [0])  # seq_len > max_ctx
+    with pytest.raises(wb.WaveB200Error):
+        cache.prefill(1, w, x[:, :10].copy(), [1])  # slot not empty
+    with pytest.raises(wb.WaveB200Error):
+        cache.forward_one(0, w, x[:, 0].copy(), [5])  # seq id out of range
+    cache.reset_seq(1)
+    assert cache.n_cached(1, 1) == 0

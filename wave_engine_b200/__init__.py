@@ -1,0 +1,18 @@
+"""B200-native (sm_100a) wave attention: prefill and KV-cache decode.
+
+The hot path of wave-engine's causal multi-head wave attention forward
+(src/common/attn.rs:90, src/common/kv_cache.rs:93/:241) behind a C ABI
+(include/wave_b200.h) implemented by the in-tree CUDA library
+``libwave_b200.so``.  This package is the host-side mirror of the
+reference's interface for that path.
+"""
+from .weights import CONTENT_DIM, Rng, WaveAttnHeadWeights, WaveAttnWeights, gaussian_block_attn, init_block_attn
+from .runtime import AttnLayer, Context, default_context
+from .attn import wave_attention_forward
+from .kv_cache import KvCache
+from ._lib import WaveB200Error
+
+__all__ = [
+    "CONTENT_DIM", "Rng", "WaveAttnHeadWeights", "WaveAttnWeights", "gaussian_block_attn", "init_block_attn",
+    "AttnLayer", "Context", "default_context", "wave_attention_forward", "KvCache", "WaveB200Error",
+]

@@ -1,0 +1,677 @@
+// wb_api.cu -- C ABI entry points (include/wave_b200.h): argument checks,
+// device-resident weights, workspace management and kernel sequencing.
+#include "wave_b200.h"
+#include "wb_internal.h"
+#include "wb_tc.h"
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const std::string &msg) {
+    g_err = msg;
+    return code;
+}
+
+#define WB_CUDA(expr)                                                                     \
+    do {                                                                                  \
+        cudaError_t e_ = (expr);                                                          \
+        if (e_ != cudaSuccess)                                                            \
+            return fail(WB_ECUDA, std::string(#expr) + ": " + cudaGetErrorString(e_));   \
+    } while (0)
+
+#define WB_TRY(expr)                 \
+    do {                             \
+        int rc_ = (expr);            \
+        if (rc_ != WB_OK) return rc_; \
+    } while (0)
+
+using DevBuf = wb::Workspace;
+
+int ensure(DevBuf &b, size_t bytes) {
+    std::string msg;
+    int rc = wb::ws_ensure(&b, bytes, &msg);
+    return rc == WB_OK ? rc : fail(rc, msg);
+}
+
+using wb::Carve;
+
+// Restores the calling thread's current device on scope exit.
+struct DeviceGuard {
+    int prev = -1;
+    bool ok = false;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) == cudaSuccess && cudaSetDevice(dev) == cudaSuccess) ok = true;
+    }
+    ~DeviceGuard() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
+
+bool is_device_ptr(const void *p) {
+    if (!p) return false;
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+}
+
+template <class T>
+int upload(T **dst, const std::vector<T> &src) {
+    *dst = nullptr;
+    if (src.empty()) return WB_OK;
+    if (cudaMalloc(dst, src.size() * sizeof(T)) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(WB_ENOMEM, "cudaMalloc for weights failed");
+    }
+    WB_CUDA(cudaMemcpy(*dst, src.data(), src.size() * sizeof(T), cudaMemcpyHostToDevice));
+    return WB_OK;
+}
+
+}  // namespace
+
+struct wb_context {
+    int device = 0;
+    int sm_count = 0;
+    cudaStream_t own = nullptr;
+    cudaStream_t stream = nullptr;
+    DevBuf ws;    // per-call scratch
+    DevBuf io;    // staging of host inputs/outputs
+    uint32_t *dev_err = nullptr;
+};
+
+struct wb_attn_layer {
+    wb_context *ctx = nullptr;
+    int E = 0, H = 0, hd = 0, C = 0;
+    std::vector<float> hn_host;  // softplus(harmonic_raw)
+    float *harmonic_n = nullptr; // [H]
+    // SIMT layouts (transposed so threads read consecutive outputs)
+    float *wrs_t = nullptr, *brs = nullptr;  // [E][H][2], [H][2]
+    float *wc_t = nullptr, *bc = nullptr;    // [E][H*C], [H*C]
+    float *wv_t = nullptr, *bv = nullptr;    // [H][hd][hd] (in, out), [H][hd]
+    float *wo_t = nullptr, *bo = nullptr;    // [E][E] (in, out), [E]
+    // tensor-core layouts
+    wb::TcLayerWeights tc;
+};
+
+struct wb_kv_cache {
+    wb_context *ctx = nullptr;
+    int L = 0, H = 0, hd = 0, S = 0, cap = 0;
+    float *theta = nullptr;
+    uint8_t *bucket = nullptr;
+    float *v = nullptr;
+    int32_t *len = nullptr;            // device [L][S]
+    std::vector<int32_t> len_host;     // host mirror [L][S]
+    WbSeqView view(int layer, const int32_t *slots) const {
+        const long long per_layer = (long long)S * H * cap;
+        WbSeqView s;
+        s.theta = theta + layer * per_layer;
+        s.bucket = bucket + layer * per_layer;
+        s.v = v + layer * per_layer * hd;
+        s.seq_stride = (long long)H * cap;
+        s.cap = cap;
+        s.slot = slots;
+        return s;
+    }
+};
+
+extern "C" {
+
+int wb_abi_version(void) { return WB_ABI_VERSION; }
+
+const char *wb_last_error(void) { return g_err.c_str(); }
+
+int wb_context_create(int device, wb_context **out) {
+    if (!out) return fail(WB_EINVAL, "out is NULL");
+    *out = nullptr;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n <= 0) {
+        cudaGetLastError();
+        return fail(WB_ENODEV, "no CUDA device visible");
+    }
+    if (device < 0 || device >= n) return fail(WB_EINVAL, "device ordinal out of range");
+    cudaDeviceProp prop;
+    WB_CUDA(cudaGetDeviceProperties(&prop, device));
+    if (prop.major != 10) return fail(WB_ENODEV, std::string("device is not sm_100 (B200): ") + prop.name);
+    DeviceGuard g(device);
+    if (!g.ok) return fail(WB_ECUDA, "cudaSetDevice failed");
+    wb_context *c = new wb_context();
+    c->device = device;
+    c->sm_count = prop.multiProcessorCount;
+    if (cudaStreamCreateWithFlags(&c->own, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaMalloc(&c->dev_err, sizeof(uint32_t)) != cudaSuccess ||
+        cudaMemset(c->dev_err, 0, sizeof(uint32_t)) != cudaSuccess) {
+        cudaGetLastError();
+        if (c->own) cudaStreamDestroy(c->own);
+        if (c->dev_err) cudaFree(c->dev_err);
+        delete c;
+        return fail(WB_ECUDA, "context allocation failed");
+    }
+    c->stream = c->own;
+    *out = c;
+    return WB_OK;
+}
+
+int wb_context_destroy(wb_context *ctx) {
+    if (!ctx) return WB_OK;
+    DeviceGuard g(ctx->device);
+    cudaStreamSynchronize(ctx->stream);
+    if (ctx->ws.p) cudaFree(ctx->ws.p);
+    if (ctx->io.p) cudaFree(ctx->io.p);
+    if (ctx->dev_err) cudaFree(ctx->dev_err);
+    if (ctx->own) cudaStreamDestroy(ctx->own);
+    delete ctx;
+    return WB_OK;
+}
+
+int wb_context_set_stream(wb_context *ctx, void *cuda_stream) {
+    if (!ctx) return fail(WB_EINVAL, "ctx is NULL");
+    ctx->stream = cuda_stream ? (cudaStream_t)cuda_stream : ctx->own;
+    return WB_OK;
+}
+
+int wb_context_synchronize(wb_context *ctx) {
+    if (!ctx) return fail(WB_EINVAL, "ctx is NULL");
+    DeviceGuard g(ctx->device);
+    WB_CUDA(cudaStreamSynchronize(ctx->stream));
+    return WB_OK;
+}
+
+int wb_context_take_device_error(wb_context *ctx, uint32_t *code_out) {
+    if (!ctx) return fail(WB_EINVAL, "ctx is NULL");
+    DeviceGuard g(ctx->device);
+    uint32_t v = 0;
+    WB_CUDA(cudaMemcpyAsync(&v, ctx->dev_err, sizeof(v), cudaMemcpyDeviceToHost, ctx->stream));
+    WB_CUDA(cudaStreamSynchronize(ctx->stream));
+    WB_CUDA(cudaMemsetAsync(ctx->dev_err, 0, sizeof(uint32_t), ctx->stream));
+    if (code_out) *code_out = v;
+    return WB_OK;
+}
+
+// ---------------------------------------------------------------------------
+// weights
+// ---------------------------------------------------------------------------
+int wb_attn_layer_create(wb_context *ctx, const wb_attn_weights_desc *w, wb_attn_layer **out) {
+    if (!ctx || !w || !out) return fail(WB_EINVAL, "NULL argument");
+    *out = nullptr;
+    const int E = w->n_embd, H = w->n_head, C = w->content_dim;
+    if (E <= 0 || H <= 0 || E % H) return fail(WB_EINVAL, "n_embd must be a positive multiple of n_head");
+    if (C != 0 && C != 16) return fail(WB_EINVAL, "content_dim must be 0 or 16");
+    const int hd = E / H;
+    if (hd > 256) return fail(WB_EINVAL, "head_dim > 256 not supported");
+    if (!w->harmonic_raw || !w->phase_proj_w || !w->phase_proj_b || !w->v_proj_w || !w->v_proj_b ||
+        !w->out_proj_w || !w->out_proj_b || (C && (!w->content_proj_w || !w->content_proj_b)))
+        return fail(WB_EINVAL, "missing weight array");
+    DeviceGuard g(ctx->device);
+    wb_attn_layer *L = new wb_attn_layer();
+    L->ctx = ctx;
+    L->E = E; L->H = H; L->hd = hd; L->C = C;
+    L->hn_host.resize(H);
+    for (int h = 0; h < H; h++) L->hn_host[h] = wb::softplus_ref(w->harmonic_raw[h]);
+
+    std::vector<float> wrs((size_t)E * H * 2), brs((size_t)H * 2);
+    for (int h = 0; h < H; h++)
+        for (int c = 0; c < 2; c++) {
+            brs[h * 2 + c] = w->phase_proj_b[h * 2 + c];
+            for (int j = 0; j < E; j++) wrs[((size_t)j * H + h) * 2 + c] = w->phase_proj_w[((size_t)h * 2 + c) * E + j];
+        }
+    std::vector<float> wc, bc;
+    if (C) {
+        wc.resize((size_t)E * H * C);
+        bc.resize((size_t)H * C);
+        for (int h = 0; h < H; h++)
+            for (int d = 0; d < C; d++) {
+                bc[h * C + d] = w->content_proj_b[h * C + d];
+                for (int j = 0; j < E; j++)
+                    wc[(size_t)j * H * C + h * C + d] = w->content_proj_w[((size_t)h * C + d) * E + j];
+            }
+    }
+    std::vector<float> wv((size_t)H * hd * hd), bv((size_t)H * hd);
+    for (int h = 0; h < H; h++)
+        for (int dd = 0; dd < hd; dd++) {
+            bv[h * hd + dd] = w->v_proj_b[h * hd + dd];
+            for (int j = 0; j < hd; j++)
+                wv[((size_t)h * hd + j) * hd + dd] = w->v_proj_w[((size_t)h * hd + dd) * hd + j];
+        }
+    std::vector<float> wo((size_t)E * E), bo(w->out_proj_b, w->out_proj_b + E);
+    for (int i = 0; i < E; i++)
+        for (int j = 0; j < E; j++) wo[(size_t)j * E + i] = w->out_proj_w[(size_t)i * E + j];
+
+    int rc = WB_OK;
+    if (rc == WB_OK) rc = upload(&L->harmonic_n, L->hn_host);
+    if (rc == WB_OK) rc = upload(&L->wrs_t, wrs);
+    if (rc == WB_OK) rc = upload(&L->brs, brs);
+    if (rc == WB_OK) rc = upload(&L->wc_t, wc);
+    if (rc == WB_OK) rc = upload(&L->bc, bc);
+    if (rc == WB_OK) rc = upload(&L->wv_t, wv);
+    if (rc == WB_OK) rc = upload(&L->bv, bv);
+    if (rc == WB_OK) rc = upload(&L->wo_t, wo);
+    if (rc == WB_OK) rc = upload(&L->bo, bo);
+    if (rc == WB_OK) {
+        std::string msg;
+        rc = wb::tc_layer_upload(&L->tc, w, L->hn_host.data(), &msg);
+        if (rc != WB_OK) fail(rc, msg);
+    }
+    if (rc != WB_OK) {
+        wb_attn_layer_destroy(L);
+        return rc;
+    }
+    *out = L;
+    return WB_OK;
+}
+
+int wb_attn_layer_destroy(wb_attn_layer *L) {
+    if (!L) return WB_OK;
+    DeviceGuard g(L->ctx->device);
+    float *ptrs[] = {L->harmonic_n, L->wrs_t, L->brs, L->wc_t, L->bc, L->wv_t, L->bv, L->wo_t, L->bo};
+    for (float *p : ptrs)
+        if (p) cudaFree(p);
+    wb::tc_layer_free(&L->tc);
+    delete L;
+    return WB_OK;
+}
+
+int wb_init_block_attn(uint64_t *rng_state, int n_head, int n_embd, int content_dim, float *harmonic_raw,
+                       float *phase_proj_w, float *phase_proj_b, float *v_proj_w, float *v_proj_b,
+                       float *content_proj_w, float *content_proj_b, float *out_proj_w, float *out_proj_b) {
+    if (!rng_state || n_head <= 0 || n_embd <= 0 || n_embd % n_head || content_dim < 0)
+        return fail(WB_EINVAL, "bad init_block_attn arguments");
+    if (!harmonic_raw || !phase_proj_w || !phase_proj_b || !v_proj_w || !v_proj_b || !out_proj_w ||
+        !out_proj_b || (content_dim && (!content_proj_w || !content_proj_b)))
+        return fail(WB_EINVAL, "NULL buffer");
+    // xorshift64 of src/common/rng.rs:24-39.
+    uint64_t s = *rng_state;
+    auto uniform = [&s](float limit) {
+        s ^= s << 13;
+        s ^= s >> 7;
+        s ^= s << 17;
+        float f = (float)(s >> 40) / (float)(1ull << 24);
+        return (f * 2.0f - 1.0f) * limit;
+    };
+    const int hd = n_embd / n_head;
+    const float le = 1.0f / std::sqrt((float)n_embd), ld = 1.0f / std::sqrt((float)hd);
+    // init_block_attn (wave_model.rs:57-81): per head phase, value, content; then out_proj.
+    for (int h = 0; h < n_head; h++) {
+        for (size_t i = 0; i < (size_t)2 * n_embd; i++) phase_proj_w[(size_t)h * 2 * n_embd + i] = uniform(le);
+        phase_proj_b[2 * h] = phase_proj_b[2 * h + 1] = 0.0f;
+        for (size_t i = 0; i < (size_t)hd * hd; i++) v_proj_w[(size_t)h * hd * hd + i] = uniform(ld);
+        for (int i = 0; i < hd; i++) v_proj_b[h * hd + i] = 0.0f;
+        if (content_dim) {
+            for (size_t i = 0; i < (size_t)content_dim * n_embd; i++)
+                content_proj_w[(size_t)h * content_dim * n_embd + i] = uniform(le);
+            for (int i = 0; i < content_dim; i++) content_proj_b[h * content_dim + i] = 0.0f;
+        }
+        harmonic_raw[h] = std::log((float)(h + 1) * 0.5f);
+    }
+    for (size_t i = 0; i < (size_t)n_embd * n_embd; i++) out_proj_w[i] = uniform(le);
+    for (int i = 0; i < n_embd; i++) out_proj_b[i] = 0.0f;
+    *rng_state = s;
+    return WB_OK;
+}
+
+// ---------------------------------------------------------------------------
+// prefill forward
+// ---------------------------------------------------------------------------
+static int run_projections_exact(wb_context *ctx, const wb_attn_layer *L, const float *x, int B, int T,
+                                 const WbSeqView &sv, float *rs, float *content, bool use_content) {
+    cudaStream_t st = ctx->stream;
+    const int R = B * T, E = L->E, H = L->H, hd = L->hd;
+    wb::OutMap dense{wb::OUT_DENSE, rs, 2LL * H, sv, 0, T};
+    wb::launch_seqdot(x, R, E, E, L->wrs_t, 2 * H, L->brs, 1, dense, st);
+    wb::launch_phase(rs, R, H, T, sv, st);
+    if (use_content) {
+        wb::OutMap cm{wb::OUT_DENSE, content, (long long)H * L->C, sv, 0, T};
+        wb::launch_seqdot(x, R, E, E, L->wc_t, H * L->C, L->bc, 1, cm, st);
+    }
+    for (int h = 0; h < H; h++) {
+        wb::OutMap vm{wb::OUT_SEQ_V, nullptr, 0, sv, h, T};
+        wb::launch_seqdot(x + (size_t)h * hd, R, hd, E, L->wv_t + (size_t)h * hd * hd, hd, L->bv + (size_t)h * hd,
+                          0, vm, st);
+    }
+    WB_CUDA(cudaGetLastError());
+    return WB_OK;
+}
+
+int wb_attn_forward(wb_context *ctx, const wb_attn_layer *L, const float *x, int B, int T, int flags,
+                    float *y, float *att_w, float *phases_out) {
+    if (!ctx || !L || !x || !y) return fail(WB_EINVAL, "NULL argument");
+    if (L->ctx != ctx) return fail(WB_EINVAL, "layer belongs to another context");
+    if (flags & WB_RETURN_PATHWAY)
+        return fail(WB_ENOTSUP, "return_pathway_cache (WaveAttnCache for backward) is not supported");
+    if (flags & ~(WB_PATH_EXACT | WB_NO_CONTENT)) return fail(WB_EINVAL, "unknown flag bits");
+    if (B < 0 || T < 0) return fail(WB_EINVAL, "negative batch or seq_len");
+    if (B == 0 || T == 0) return WB_OK;
+    const long long R = (long long)B * T;
+    if (R > (1LL << 30)) return fail(WB_EINVAL, "batch*seq_len too large");
+    DeviceGuard g(ctx->device);
+    cudaStream_t st = ctx->stream;
+    const int E = L->E, H = L->H, hd = L->hd;
+    const bool use_content = L->C > 0 && !(flags & WB_NO_CONTENT);
+    const bool exact = (flags & WB_PATH_EXACT) || att_w != nullptr;
+    const bool x_dev = is_device_ptr(x), y_dev = is_device_ptr(y);
+    const bool aw_dev = att_w && is_device_ptr(att_w), ph_dev = phases_out && is_device_ptr(phases_out);
+
+    // staging for host buffers
+    Carve io;
+    size_t o_x = x_dev ? 0 : io.take<float>(R * E);
+    size_t o_y = y_dev ? 0 : io.take<float>(R * E);
+    size_t o_aw = (att_w && !aw_dev) ? io.take<float>((size_t)B * H * T * T) : 0;
+    size_t o_ph = (phases_out && !ph_dev) ? io.take<float>((size_t)B * H * T) : 0;
+    WB_TRY(ensure(ctx->io, io.off));
+    char *iob = (char *)ctx->io.p;
+    const float *xd = x_dev ? x : (const float *)(iob + o_x);
+    float *yd = y_dev ? y : (float *)(iob + o_y);
+    float *awd = att_w ? (aw_dev ? att_w : (float *)(iob + o_aw)) : nullptr;
+    if (!x_dev) WB_CUDA(cudaMemcpyAsync((void *)xd, x, R * E * sizeof(float), cudaMemcpyHostToDevice, st));
+
+    int rc;
+    if (exact) {
+        Carve c;
+        size_t o_rs = c.take<float>(R * 2 * H);
+        size_t o_ct = c.take<float>(use_content ? R * H * L->C : 1);
+        size_t o_th = c.take<float>(R * H);
+        size_t o_bk = c.take<uint8_t>(R * H);
+        size_t o_v = c.take<float>(R * H * hd);
+        size_t o_o = c.take<float>(R * E);
+        WB_TRY(ensure(ctx->ws, c.off));
+        char *w = (char *)ctx->ws.p;
+        WbSeqView sv;
+        sv.theta = (float *)(w + o_th);
+        sv.bucket = (uint8_t *)(w + o_bk);
+        sv.v = (float *)(w + o_v);
+        sv.seq_stride = (long long)H * T;
+        sv.cap = T;
+        sv.slot = nullptr;
+        float *content = (float *)(w + o_ct), *o = (float *)(w + o_o);
+        WB_TRY(run_projections_exact(ctx, L, xd, B, T, sv, (float *)(w + o_rs), content, use_content));
+        wb::launch_attn_simt(sv, use_content ? content : nullptr, use_content ? L->C : 0,
+                             use_content ? 1.0f / std::sqrt((float)L->C) : 0.0f, L->harmonic_n, B, H, T, hd, o,
+                             awd, st);
+        wb::OutMap om{wb::OUT_DENSE, yd, E, sv, 0, T};
+        wb::launch_seqdot(o, (int)R, E, E, L->wo_t, E, L->bo, 0, om, st);
+        if (phases_out) {
+            float *phd = ph_dev ? phases_out : (float *)(iob + o_ph);
+            WB_CUDA(cudaMemcpyAsync(phd, sv.theta, R * H * sizeof(float), cudaMemcpyDeviceToDevice, st));
+        }
+        WB_CUDA(cudaGetLastError());
+    } else {
+        std::string msg;
+        float *phd = phases_out ? (ph_dev ? phases_out : (float *)(iob + o_ph)) : nullptr;
+        rc = wb::tc_attn_forward(L->tc, xd, B, T, use_content, yd, phd, &ctx->ws, ctx->dev_err,
+                                 ctx->sm_count, st, &msg);
+        if (rc != WB_OK) return fail(rc, msg);
+    }
+    if (!y_dev) WB_CUDA(cudaMemcpyAsync(y, yd, R * E * sizeof(float), cudaMemcpyDeviceToHost, st));
+    if (att_w && !aw_dev)
+        WB_CUDA(cudaMemcpyAsync(att_w, awd, (size_t)B * H * T * T * sizeof(float), cudaMemcpyDeviceToHost, st));
+    if (phases_out && !ph_dev)
+        WB_CUDA(cudaMemcpyAsync(phases_out, iob + o_ph, R * H * sizeof(float), cudaMemcpyDeviceToHost, st));
+    if (!y_dev || (att_w && !aw_dev) || (phases_out && !ph_dev)) {
+        WB_CUDA(cudaStreamSynchronize(st));
+        uint32_t derr = 0;
+        WB_CUDA(cudaMemcpy(&derr, ctx->dev_err, sizeof(derr), cudaMemcpyDeviceToHost));
+        if (derr) return fail(WB_ETIMEOUT, "device-side check failed, error word " + std::to_string(derr));
+    }
+    return WB_OK;
+}
+
+// ---------------------------------------------------------------------------
+// KV cache
+// ---------------------------------------------------------------------------
+int wb_kv_cache_create(wb_context *ctx, int n_layers, int n_head, int head_dim, int max_seqs, int max_ctx,
+                       wb_kv_cache **out) {
+    if (!ctx || !out) return fail(WB_EINVAL, "NULL argument");
+    *out = nullptr;
+    if (n_layers <= 0 || n_head <= 0 || head_dim <= 0 || head_dim > 256 || max_seqs <= 0 || max_ctx <= 0)
+        return fail(WB_EINVAL, "bad cache dimensions");
+    DeviceGuard g(ctx->device);
+    wb_kv_cache *c = new wb_kv_cache();
+    c->ctx = ctx;
+    c->L = n_layers; c->H = n_head; c->hd = head_dim; c->S = max_seqs; c->cap = max_ctx;
+    const size_t n = (size_t)n_layers * max_seqs * n_head * max_ctx;
+    if (cudaMalloc(&c->theta, n * sizeof(float)) != cudaSuccess ||
+        cudaMalloc(&c->bucket, n) != cudaSuccess ||
+        cudaMalloc(&c->v, n * head_dim * sizeof(float)) != cudaSuccess ||
+        cudaMalloc(&c->len, (size_t)n_layers * max_seqs * sizeof(int32_t)) != cudaSuccess) {
+        cudaGetLastError();
+        wb_kv_cache_destroy(c);
+        return fail(WB_ENOMEM, "KV cache allocation failed (" + std::to_string(n * (5 + 4 * head_dim)) + " bytes)");
+    }
+    if (cudaMemset(c->len, 0, (size_t)n_layers * max_seqs * sizeof(int32_t)) != cudaSuccess) {
+        cudaGetLastError();
+        wb_kv_cache_destroy(c);
+        return fail(WB_ECUDA, "cudaMemset failed");
+    }
+    c->len_host.assign((size_t)n_layers * max_seqs, 0);
+    *out = c;
+    return WB_OK;
+}
+
+int wb_kv_cache_destroy(wb_kv_cache *c) {
+    if (!c) return WB_OK;
+    DeviceGuard g(c->ctx->device);
+    cudaStreamSynchronize(c->ctx->stream);
+    if (c->theta) cudaFree(c->theta);
+    if (c->bucket) cudaFree(c->bucket);
+    if (c->v) cudaFree(c->v);
+    if (c->len) cudaFree(c->len);
+    delete c;
+    return WB_OK;
+}
+
+int wb_kv_cache_length(wb_kv_cache *c, int layer, int seq, int *len_out) {
+    if (!c || !len_out) return fail(WB_EINVAL, "NULL argument");
+    if (layer < 0 || layer >= c->L || seq < 0 || seq >= c->S) return fail(WB_EINVAL, "layer/seq out of range");
+    *len_out = c->len_host[(size_t)layer * c->S + seq];
+    return WB_OK;
+}
+
+int wb_kv_cache_reset_seq(wb_kv_cache *c, int seq) {
+    if (!c) return fail(WB_EINVAL, "NULL argument");
+    if (seq < 0 || seq >= c->S) return fail(WB_EINVAL, "seq out of range");
+    DeviceGuard g(c->ctx->device);
+    for (int l = 0; l < c->L; l++) {
+        c->len_host[(size_t)l * c->S + seq] = 0;
+        WB_CUDA(cudaMemsetAsync(c->len + (size_t)l * c->S + seq, 0, sizeof(int32_t), c->ctx->stream));
+    }
+    return WB_OK;
+}
+
+int wb_kv_cache_load(wb_context *ctx, wb_kv_cache *c, int layer, int seq, int n, const float *phases,
+                     const float *values) {
+    if (!ctx || !c || !phases || !values) return fail(WB_EINVAL, "NULL argument");
+    if (c->ctx != ctx) return fail(WB_EINVAL, "cache belongs to another context");
+    if (layer < 0 || layer >= c->L || seq < 0 || seq >= c->S) return fail(WB_EINVAL, "layer/seq out of range");
+    if (n < 0 || n > c->cap) return fail(WB_EINVAL, "n exceeds cache capacity");
+    DeviceGuard g(ctx->device);
+    cudaStream_t st = ctx->stream;
+    WbSeqView sv = c->view(layer, nullptr);
+    const bool dev = is_device_ptr(phases);
+    const cudaMemcpyKind kind = dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+    for (int h = 0; h < c->H; h++) {
+        const long long base = (long long)seq * sv.seq_stride + (long long)h * c->cap;
+        if (n) {
+            WB_CUDA(cudaMemcpyAsync(sv.theta + base, phases + (size_t)h * n, n * sizeof(float), kind, st));
+            WB_CUDA(cudaMemcpyAsync(sv.v + base * c->hd, values + (size_t)h * n * c->hd,
+                                    (size_t)n * c->hd * sizeof(float),
+                                    is_device_ptr(values) ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, st));
+            wb::launch_bucket_from_theta(sv.theta + base, sv.bucket + base, n, st);
+        }
+    }
+    const int32_t nn = n;
+    WB_CUDA(cudaMemcpyAsync(c->len + (size_t)layer * c->S + seq, &nn, sizeof(int32_t), cudaMemcpyHostToDevice, st));
+    WB_CUDA(cudaStreamSynchronize(st));
+    c->len_host[(size_t)layer * c->S + seq] = n;
+    return WB_OK;
+}
+
+int wb_kv_cache_read(wb_context *ctx, wb_kv_cache *c, int layer, int seq, float *phases, uint8_t *buckets,
+                     float *values) {
+    if (!ctx || !c) return fail(WB_EINVAL, "NULL argument");
+    if (layer < 0 || layer >= c->L || seq < 0 || seq >= c->S) return fail(WB_EINVAL, "layer/seq out of range");
+    DeviceGuard g(ctx->device);
+    cudaStream_t st = ctx->stream;
+    WB_CUDA(cudaStreamSynchronize(st));
+    const int n = c->len_host[(size_t)layer * c->S + seq];
+    WbSeqView sv = c->view(layer, nullptr);
+    for (int h = 0; h < c->H && n > 0; h++) {
+        const long long base = (long long)seq * sv.seq_stride + (long long)h * c->cap;
+        if (phases) WB_CUDA(cudaMemcpy(phases + (size_t)h * n, sv.theta + base, n * sizeof(float), cudaMemcpyDefault));
+        if (buckets) WB_CUDA(cudaMemcpy(buckets + (size_t)h * n, sv.bucket + base, n, cudaMemcpyDefault));
+        if (values)
+            WB_CUDA(cudaMemcpy(values + (size_t)h * n * c->hd, sv.v + base * c->hd, (size_t)n * c->hd * sizeof(float),
+                               cudaMemcpyDefault));
+    }
+    return WB_OK;
+}
+
+static int copy_seq_ids(wb_context *ctx, const int32_t *seq_ids, int n_seq, std::vector<int32_t> &host) {
+    host.resize(n_seq);
+    WB_CUDA(cudaMemcpy(host.data(), seq_ids, n_seq * sizeof(int32_t), cudaMemcpyDefault));
+    return WB_OK;
+}
+
+int wb_kv_prefill(wb_context *ctx, wb_kv_cache *c, int layer_idx, const wb_attn_layer *L, const int32_t *seq_ids,
+                  int n_seq, const float *x, int T, int flags, float *y) {
+    if (!ctx || !c || !L || !seq_ids || !x || !y) return fail(WB_EINVAL, "NULL argument");
+    if (c->ctx != ctx || L->ctx != ctx) return fail(WB_EINVAL, "objects belong to another context");
+    if (flags & ~(WB_PATH_EXACT | WB_NO_CONTENT)) return fail(WB_EINVAL, "unknown flag bits");
+    if (layer_idx < 0 || layer_idx >= c->L) return fail(WB_EINVAL, "layer out of range");
+    if (L->H != c->H || L->hd != c->hd) return fail(WB_EINVAL, "layer shape does not match cache");
+    if (n_seq < 0 || T < 0) return fail(WB_EINVAL, "negative n_seq or seq_len");
+    if (n_seq == 0 || T == 0) return WB_OK;
+    if (T > c->cap) return fail(WB_EINVAL, "seq_len exceeds cache capacity");
+    DeviceGuard g(ctx->device);
+    std::vector<int32_t> ids;
+    WB_TRY(copy_seq_ids(ctx, seq_ids, n_seq, ids));
+    for (int i = 0; i < n_seq; i++) {
+        if (ids[i] < 0 || ids[i] >= c->S) return fail(WB_EINVAL, "seq id out of range");
+        if (c->len_host[(size_t)layer_idx * c->S + ids[i]] != 0)
+            return fail(WB_EINVAL, "prefill needs an empty slot (kv_cache.rs prefill starts from KvCache::new)");
+        for (int j = 0; j < i; j++)
+            if (ids[j] == ids[i]) return fail(WB_EINVAL, "duplicate seq id");
+    }
+    cudaStream_t st = ctx->stream;
+    const long long R = (long long)n_seq * T;
+    const int E = L->E, H = L->H, hd = L->hd;
+    const bool x_dev = is_device_ptr(x), y_dev = is_device_ptr(y);
+    Carve io;
+    size_t o_x = x_dev ? 0 : io.take<float>(R * E);
+    size_t o_y = y_dev ? 0 : io.take<float>(R * E);
+    size_t o_ids = io.take<int32_t>(n_seq);
+    WB_TRY(ensure(ctx->io, io.off));
+    char *iob = (char *)ctx->io.p;
+    const float *xd = x_dev ? x : (const float *)(iob + o_x);
+    float *yd = y_dev ? y : (float *)(iob + o_y);
+    int32_t *ids_d = (int32_t *)(iob + o_ids);
+    WB_CUDA(cudaMemcpyAsync(ids_d, ids.data(), n_seq * sizeof(int32_t), cudaMemcpyHostToDevice, st));
+    if (!x_dev) WB_CUDA(cudaMemcpyAsync((void *)xd, x, R * E * sizeof(float), cudaMemcpyHostToDevice, st));
+    WbSeqView sv = c->view(layer_idx, ids_d);
+    if (flags & WB_PATH_EXACT) {
+        Carve cv;
+        size_t o_rs = cv.take<float>(R * 2 * H);
+        size_t o_o = cv.take<float>(R * E);
+        WB_TRY(ensure(ctx->ws, cv.off));
+        char *w = (char *)ctx->ws.p;
+        float *o = (float *)(w + o_o);
+        WB_TRY(run_projections_exact(ctx, L, xd, n_seq, T, sv, (float *)(w + o_rs), nullptr, false));
+        wb::launch_attn_simt(sv, nullptr, 0, 0.0f, L->harmonic_n, n_seq, H, T, hd, o, nullptr, st);
+        wb::OutMap om{wb::OUT_DENSE, yd, E, sv, 0, T};
+        wb::launch_seqdot(o, (int)R, E, E, L->wo_t, E, L->bo, 0, om, st);
+        WB_CUDA(cudaGetLastError());
+    } else {
+        std::string msg;
+        int rc = wb::tc_kv_prefill(L->tc, sv, xd, n_seq, T, yd, &ctx->ws, ctx->dev_err,
+                                   ctx->sm_count, st, &msg);
+        if (rc != WB_OK) return fail(rc, msg);
+    }
+    wb::launch_len_update(c->len + (size_t)layer_idx * c->S, ids_d, n_seq, T, 1, st);
+    WB_CUDA(cudaGetLastError());
+    for (int i = 0; i < n_seq; i++) c->len_host[(size_t)layer_idx * c->S + ids[i]] = T;
+    if (!y_dev) {
+        WB_CUDA(cudaMemcpyAsync(y, yd, R * E * sizeof(float), cudaMemcpyDeviceToHost, st));
+        WB_CUDA(cudaStreamSynchronize(st));
+    }
+    return WB_OK;
+}
+
+int wb_kv_decode(wb_context *ctx, wb_kv_cache *c, int layer_idx, const wb_attn_layer *L, const int32_t *seq_ids,
+                 int n_seq, const float *x, int flags, float *y) {
+    if (!ctx || !c || !L || !seq_ids || !x || !y) return fail(WB_EINVAL, "NULL argument");
+    if (c->ctx != ctx || L->ctx != ctx) return fail(WB_EINVAL, "objects belong to another context");
+    if (flags & ~(WB_PATH_EXACT | WB_NO_CONTENT)) return fail(WB_EINVAL, "unknown flag bits");
+    if (layer_idx < 0 || layer_idx >= c->L) return fail(WB_EINVAL, "layer out of range");
+    if (L->H != c->H || L->hd != c->hd) return fail(WB_EINVAL, "layer shape does not match cache");
+    if (n_seq < 0) return fail(WB_EINVAL, "negative n_seq");
+    if (n_seq == 0) return WB_OK;
+    DeviceGuard g(ctx->device);
+    std::vector<int32_t> ids;
+    WB_TRY(copy_seq_ids(ctx, seq_ids, n_seq, ids));
+    for (int i = 0; i < n_seq; i++) {
+        if (ids[i] < 0 || ids[i] >= c->S) return fail(WB_EINVAL, "seq id out of range");
+        if (c->len_host[(size_t)layer_idx * c->S + ids[i]] >= c->cap) return fail(WB_EINVAL, "cache slot is full");
+        for (int j = 0; j < i; j++)
+            if (ids[j] == ids[i]) return fail(WB_EINVAL, "duplicate seq id");
+    }
+    cudaStream_t st = ctx->stream;
+    const int E = L->E, H = L->H, hd = L->hd;
+    const bool x_dev = is_device_ptr(x), y_dev = is_device_ptr(y);
+    Carve io;
+    size_t o_x = x_dev ? 0 : io.take<float>((size_t)n_seq * E);
+    size_t o_y = y_dev ? 0 : io.take<float>((size_t)n_seq * E);
+    size_t o_ids = io.take<int32_t>(n_seq);
+    WB_TRY(ensure(ctx->io, io.off));
+    char *iob = (char *)ctx->io.p;
+    const float *xd = x_dev ? x : (const float *)(iob + o_x);
+    float *yd = y_dev ? y : (float *)(iob + o_y);
+    int32_t *ids_d = (int32_t *)(iob + o_ids);
+    WB_CUDA(cudaMemcpyAsync(ids_d, ids.data(), n_seq * sizeof(int32_t), cudaMemcpyHostToDevice, st));
+    if (!x_dev) WB_CUDA(cudaMemcpyAsync((void *)xd, x, (size_t)n_seq * E * sizeof(float), cudaMemcpyHostToDevice, st));
+    WbSeqView sv = c->view(layer_idx, ids_d);
+    int32_t *len_l = c->len + (size_t)layer_idx * c->S;
+    if (flags & WB_PATH_EXACT) {
+        Carve cv;
+        size_t o_rs = cv.take<float>((size_t)n_seq * 2 * H);
+        size_t o_th = cv.take<float>((size_t)n_seq * H);
+        size_t o_vn = cv.take<float>((size_t)n_seq * H * hd);
+        size_t o_o = cv.take<float>((size_t)n_seq * E);
+        WB_TRY(ensure(ctx->ws, cv.off));
+        char *w = (char *)ctx->ws.p;
+        float *rs = (float *)(w + o_rs), *th = (float *)(w + o_th), *vn = (float *)(w + o_vn), *o = (float *)(w + o_o);
+        wb::OutMap rm{wb::OUT_DENSE, rs, 2LL * H, sv, 0, 1};
+        wb::launch_seqdot(xd, n_seq, E, E, L->wrs_t, 2 * H, L->brs, 1, rm, st);
+        wb::launch_theta_only(rs, n_seq * H, th, st);
+        for (int h = 0; h < H; h++) {
+            wb::OutMap vm{wb::OUT_DENSE, vn + (size_t)h * hd, (long long)H * hd, sv, 0, 1};
+            wb::launch_seqdot(xd + (size_t)h * hd, n_seq, hd, E, L->wv_t + (size_t)h * hd * hd, hd,
+                              L->bv + (size_t)h * hd, 0, vm, st);
+        }
+        wb::launch_decode_simt(sv, len_l, th, vn, L->harmonic_n, n_seq, H, hd, o, st);
+        wb::OutMap om{wb::OUT_DENSE, yd, E, sv, 0, 1};
+        wb::launch_seqdot(o, n_seq, E, E, L->wo_t, E, L->bo, 0, om, st);
+        WB_CUDA(cudaGetLastError());
+    } else {
+        std::string msg;
+        int rc = wb::tc_kv_decode(L->tc, sv, len_l, c->cap, xd, n_seq, yd, &ctx->ws, ctx->dev_err,
+                                  ctx->sm_count, st, &msg);
+        if (rc != WB_OK) return fail(rc, msg);
+    }
+    wb::launch_len_update(len_l, ids_d, n_seq, 1, 0, st);
+    WB_CUDA(cudaGetLastError());
+    for (int i = 0; i < n_seq; i++) c->len_host[(size_t)layer_idx * c->S + ids[i]] += 1;
+    if (!y_dev) {
+        WB_CUDA(cudaMemcpyAsync(y, yd, (size_t)n_seq * E * sizeof(float), cudaMemcpyDeviceToHost, st));
+        WB_CUDA(cudaStreamSynchronize(st));
+    }
+    return WB_OK;
+}
+
+}  // extern "C"

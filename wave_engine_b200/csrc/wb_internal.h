@@ -1,0 +1,69 @@
+// wb_internal.h -- declarations shared by the library's translation units.
+#pragma once
+#include "wb_common.cuh"
+
+#include <string>
+
+namespace wb {
+
+// Grow-only device buffer owned by a context.
+struct Workspace {
+    void *p = nullptr;
+    size_t n = 0;
+};
+
+// Make *w at least `bytes` long.  Growing frees the old buffer (cudaFree
+// synchronises the device, so no kernel still uses it).  Returns WB_OK or
+// WB_ENOMEM with *msg set.
+inline int ws_ensure(Workspace *w, size_t bytes, std::string *msg) {
+    if (bytes <= w->n) return 0;
+    if (w->p) cudaFree(w->p);
+    w->p = nullptr;
+    w->n = 0;
+    const size_t want = bytes + bytes / 8;
+    if (cudaMalloc(&w->p, want) != cudaSuccess) {
+        cudaGetLastError();
+        if (msg) *msg = "cudaMalloc of " + std::to_string(want) + " bytes failed";
+        return -2;  // WB_ENOMEM
+    }
+    w->n = want;
+    return 0;
+}
+
+// Bump allocator handing out 256-byte aligned offsets into one buffer.
+struct Carve {
+    size_t off = 0;
+    template <class T>
+    size_t take(size_t count) {
+        size_t o = off;
+        off += (count * sizeof(T) + 255) & ~size_t(255);
+        return o;
+    }
+};
+
+enum { OUT_DENSE = 0, OUT_SEQ_V = 1 };
+struct OutMap {
+    int mode;
+    float *y;       // OUT_DENSE: Y[r*ldy + n]
+    long long ldy;
+    WbSeqView sv;   // OUT_SEQ_V: value rows of head h
+    int h;
+    int T;
+};
+
+// ---- SIMT (exact) kernels: wb_simt.cu ----
+void launch_seqdot(const float *X, int R, int K, long long ldx, const float *Wt, int N,
+                   const float *bias, int bias_first, const OutMap &om, cudaStream_t st);
+void launch_phase(const float *rs, int R, int H, int T, const WbSeqView &sv, cudaStream_t st);
+void launch_attn_simt(const WbSeqView &sv, const float *content, int C, float content_scale,
+                      const float *harmonic_n, int B, int H, int T, int hd, float *o,
+                      float *att_w, cudaStream_t st);
+void launch_decode_simt(const WbSeqView &sv, const int32_t *len, const float *theta_new,
+                        const float *v_new, const float *harmonic_n, int n_seq, int H, int hd,
+                        float *o, cudaStream_t st);
+void launch_theta_only(const float *rs, int n, float *theta, cudaStream_t st);
+void launch_len_update(int32_t *len, const int32_t *slots, int n_seq, int value, int set,
+                       cudaStream_t st);
+void launch_bucket_from_theta(const float *theta, uint8_t *bucket, long long n, cudaStream_t st);
+
+}  // namespace wb

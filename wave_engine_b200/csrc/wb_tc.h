@@ -1,0 +1,36 @@
+// wb_tc.h -- tensor-core (tcgen05) path: device weight layouts and the
+// prefill / decode sequences of WB_PATH_TENSOR.
+#pragma once
+#include "wave_b200.h"
+#include "wb_internal.h"
+
+#include <string>
+
+namespace wb {
+
+struct TcLayerWeights {
+    int E = 0, H = 0, hd = 0, C = 0;
+    float *harmonic_n = nullptr;   // [H]
+    float *w_rs = nullptr;         // [E][H][2] phase projection, input-major
+    float *b_rs = nullptr;         // [H][2]
+    float *w_c = nullptr;          // [H*C][E] content projection rows (tf32 B operand)
+    float *b_c = nullptr;          // [H*C]
+    float *w_v = nullptr;          // [H][hd][hd] value projection rows (out, in)
+    float *b_v = nullptr;          // [H][hd]
+    __nv_bfloat16 *w_o = nullptr;  // [E][E] out_proj rows (bf16 K-major B operand)
+    float *b_o = nullptr;          // [E]
+};
+
+int tc_layer_upload(TcLayerWeights *t, const wb_attn_weights_desc *w, const float *hn_host, std::string *msg);
+void tc_layer_free(TcLayerWeights *t);
+
+int tc_attn_forward(const TcLayerWeights &t, const float *x, int B, int T, bool use_content, float *y,
+                    float *phases_out, Workspace *ws, uint32_t *dev_err, int sm_count, cudaStream_t st,
+                    std::string *msg);
+int tc_kv_prefill(const TcLayerWeights &t, const WbSeqView &sv, const float *x, int n_seq, int T, float *y,
+                  Workspace *ws, uint32_t *dev_err, int sm_count, cudaStream_t st, std::string *msg);
+int tc_kv_decode(const TcLayerWeights &t, const WbSeqView &sv, const int32_t *len, int cap, const float *x,
+                 int n_seq, float *y, Workspace *ws, uint32_t *dev_err, int sm_count, cudaStream_t st,
+                 std::string *msg);
+
+}  // namespace wb
