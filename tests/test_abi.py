@@ -16,8 +16,10 @@ HEADER = ROOT / "include" / "wave_b200.h"
 
 
 def declared_symbols():
-    text = HEADER.read_text()
-    return sorted(set(re.findall(r"^WB_API\s+[\w\s\*]*?\b(wb_\w+)\s*\(", text, flags=re.M)))
+    syms = set()
+    for h in sorted((ROOT / "include").glob("*.h")):
+        syms |= set(re.findall(r"^WB_API\s+[\w\s\*]*?\b(wb_\w+)\s*\(", h.read_text(), flags=re.M))
+    return sorted(syms)
 
 
 def test_header_declares_the_boundary():

@@ -1,0 +1,25 @@
+"""The tcgen05 bf16 GEMM behind out_proj, against torch in fp32."""
+from __future__ import annotations
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 128, 64), (256, 768, 768), (300, 168, 168), (1000, 384, 384),
+                                   (129, 4096, 4096)])
+def test_gemm_bf16_matches_torch(ctx, M, N, K):
+    import torch
+    from wave_engine_b200 import _lib
+    g = torch.Generator(device="cuda").manual_seed(M + N + K)
+    A = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+    B = torch.randn(N, K, device="cuda", generator=g).to(torch.bfloat16)
+    bias = torch.randn(N, device="cuda", generator=g)
+    C = torch.full((M, N), float("nan"), device="cuda")
+    torch.cuda.synchronize()
+    _lib.call("wb_test_gemm_bf16", ctx.handle, A.data_ptr(), B.data_ptr(), bias.data_ptr(), C.data_ptr(), M, N, K)
+    ctx.synchronize()
+    ref = A.float() @ B.float().T + bias
+    err = (C - ref).abs().max().item()
+    assert err <= 1e-3 * max(1.0, K ** 0.5), err
+    assert ctx.take_device_error() == 0

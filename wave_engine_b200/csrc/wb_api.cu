@@ -1,6 +1,7 @@
 // wb_api.cu -- C ABI entry points (include/wave_b200.h): argument checks,
 // device-resident weights, workspace management and kernel sequencing.
 #include "wave_b200.h"
+#include "wave_b200_testing.h"
 #include "wb_internal.h"
 #include "wb_tc.h"
 
@@ -101,6 +102,10 @@ struct wb_attn_layer {
     // tensor-core layouts
     wb::TcLayerWeights tc;
 };
+
+static wb::ProjWeights proj_weights(const wb_attn_layer *L) {
+    return wb::ProjWeights{L->E, L->H, L->hd, L->C, L->wrs_t, L->brs, L->wc_t, L->bc, L->wv_t, L->bv};
+}
 
 struct wb_kv_cache {
     wb_context *ctx = nullptr;
@@ -257,7 +262,11 @@ int wb_attn_layer_create(wb_context *ctx, const wb_attn_weights_desc *w, wb_attn
     if (rc == WB_OK) rc = upload(&L->bo, bo);
     if (rc == WB_OK) {
         std::string msg;
-        rc = wb::tc_layer_upload(&L->tc, w, L->hn_host.data(), &msg);
+        L->tc.pw = proj_weights(L);
+        L->tc.harmonic_n = L->harmonic_n;
+        L->tc.b_o = L->bo;
+        L->tc.wo_t = L->wo_t;
+        rc = wb::tc_layer_upload(&L->tc, w, &msg);
         if (rc != WB_OK) fail(rc, msg);
     }
     if (rc != WB_OK) {
@@ -322,20 +331,7 @@ int wb_init_block_attn(uint64_t *rng_state, int n_head, int n_embd, int content_
 // ---------------------------------------------------------------------------
 static int run_projections_exact(wb_context *ctx, const wb_attn_layer *L, const float *x, int B, int T,
                                  const WbSeqView &sv, float *rs, float *content, bool use_content) {
-    cudaStream_t st = ctx->stream;
-    const int R = B * T, E = L->E, H = L->H, hd = L->hd;
-    wb::OutMap dense{wb::OUT_DENSE, rs, 2LL * H, sv, 0, T};
-    wb::launch_seqdot(x, R, E, E, L->wrs_t, 2 * H, L->brs, 1, dense, st);
-    wb::launch_phase(rs, R, H, T, sv, st);
-    if (use_content) {
-        wb::OutMap cm{wb::OUT_DENSE, content, (long long)H * L->C, sv, 0, T};
-        wb::launch_seqdot(x, R, E, E, L->wc_t, H * L->C, L->bc, 1, cm, st);
-    }
-    for (int h = 0; h < H; h++) {
-        wb::OutMap vm{wb::OUT_SEQ_V, nullptr, 0, sv, h, T};
-        wb::launch_seqdot(x + (size_t)h * hd, R, hd, E, L->wv_t + (size_t)h * hd * hd, hd, L->bv + (size_t)h * hd,
-                          0, vm, st);
-    }
+    wb::launch_projections_exact(proj_weights(L), x, B, T, sv, rs, use_content ? content : nullptr, ctx->stream);
     WB_CUDA(cudaGetLastError());
     return WB_OK;
 }
@@ -672,6 +668,16 @@ int wb_kv_decode(wb_context *ctx, wb_kv_cache *c, int layer_idx, const wb_attn_l
         WB_CUDA(cudaStreamSynchronize(st));
     }
     return WB_OK;
+}
+
+int wb_test_gemm_bf16(wb_context *ctx, const uint16_t *A, const uint16_t *B, const float *bias, float *C, int M,
+                      int N, int K) {
+    if (!ctx || !A || !B || !bias || !C) return fail(WB_EINVAL, "NULL argument");
+    DeviceGuard g(ctx->device);
+    std::string msg;
+    int rc = wb::tc_gemm_bf16((const __nv_bfloat16 *)A, (const __nv_bfloat16 *)B, bias, C, M, N, K, ctx->dev_err,
+                              ctx->stream, &msg);
+    return rc == WB_OK ? rc : fail(rc, msg);
 }
 
 }  // extern "C"

@@ -51,7 +51,22 @@ struct OutMap {
     int T;
 };
 
+// Device weights in the SIMT (input-major) layouts used by the projections.
+struct ProjWeights {
+    int E, H, hd, C;
+    const float *wrs_t, *brs;  // [E][H][2], [H][2]
+    const float *wc_t, *bc;    // [E][H*C], [H*C]
+    const float *wv_t, *bv;    // [H][hd][hd] (in, out), [H][hd]
+};
+
 // ---- SIMT (exact) kernels: wb_simt.cu ----
+// phases/buckets/values into sv, (r,s) into rs [R][H][2], content into
+// content [R][H*C] when non-null.
+void launch_projections_exact(const ProjWeights &w, const float *x, int B, int T, const WbSeqView &sv, float *rs,
+                              float *content, cudaStream_t st);
+void launch_attn_simt_fallback_bf16(const WbSeqView &sv, const float *content, int C, float content_scale,
+                                    const float *harmonic_n, int B, int H, int T, int hd, __nv_bfloat16 *o,
+                                    const int *tile_flags, cudaStream_t st);
 void launch_seqdot(const float *X, int R, int K, long long ldx, const float *Wt, int N,
                    const float *bias, int bias_first, const OutMap &om, cudaStream_t st);
 void launch_phase(const float *rs, int R, int H, int T, const WbSeqView &sv, cudaStream_t st);

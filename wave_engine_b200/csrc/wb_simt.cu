@@ -105,16 +105,21 @@ struct AttnSimtArgs {
     float content_scale;
     const float *harmonic_n;  // [H]
     int B, H, T, hd;
-    float *o;        // [B*T][H*hd] merged heads
+    void *o;         // [B*T][H*hd] merged heads (float or bf16)
     float *att_w;    // [B][H][T][T] or nullptr
+    const int *tile_flags;  // [B*H][ceil(T/128)]: only flagged query tiles (nullptr = all)
 };
 
-template <int DPL>  // head dims per lane (hd <= 32*DPL)
+__device__ __forceinline__ void store_out(float *p, float v) { *p = v; }
+__device__ __forceinline__ void store_out(__nv_bfloat16 *p, float v) { *p = __float2bfloat16_rn(v); }
+
+template <int DPL, class OutT>  // head dims per lane (hd <= 32*DPL)
 __global__ void __launch_bounds__(256) attn_simt_kernel(AttnSimtArgs a) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int q = blockIdx.x * 8 + warp;
     const int h = blockIdx.y, b = blockIdx.z;
     if (q >= a.T) return;
+    if (a.tile_flags && !a.tile_flags[((long long)b * a.H + h) * ((a.T + 127) / 128) + q / 128]) return;
     const long long base = wb_slot_base(a.sv, b, h);
     const float *theta = a.sv.theta + base;
     const uint8_t *bucket = a.sv.bucket + base;
@@ -185,23 +190,52 @@ __global__ void __launch_bounds__(256) attn_simt_kernel(AttnSimtArgs a) {
     }
     if (aw)
         for (int k = q + 1 + lane; k < a.T; k += 32) aw[k] = -INFINITY;
-    float *orow = a.o + ((long long)b * a.T + q) * ((long long)a.H * a.hd) + (long long)h * a.hd;
+    OutT *orow = (OutT *)a.o + ((long long)b * a.T + q) * ((long long)a.H * a.hd) + (long long)h * a.hd;
 #pragma unroll
     for (int i = 0; i < DPL; i++) {
         const int dd = lane + 32 * i;
-        if (dd < a.hd) orow[dd] = acc[i];
+        if (dd < a.hd) store_out(orow + dd, acc[i]);
     }
+}
+
+template <class OutT>
+static void launch_attn_simt_t(const AttnSimtArgs &a, cudaStream_t st) {
+    dim3 grid((a.T + 7) / 8, a.H, a.B);
+    if (a.hd <= 32) attn_simt_kernel<1, OutT><<<grid, 256, 0, st>>>(a);
+    else if (a.hd <= 64) attn_simt_kernel<2, OutT><<<grid, 256, 0, st>>>(a);
+    else if (a.hd <= 128) attn_simt_kernel<4, OutT><<<grid, 256, 0, st>>>(a);
+    else attn_simt_kernel<8, OutT><<<grid, 256, 0, st>>>(a);
 }
 
 void launch_attn_simt(const WbSeqView &sv, const float *content, int C, float content_scale,
                       const float *harmonic_n, int B, int H, int T, int hd, float *o,
                       float *att_w, cudaStream_t st) {
-    AttnSimtArgs a{sv, content, C, content_scale, harmonic_n, B, H, T, hd, o, att_w};
-    dim3 grid((T + 7) / 8, H, B);
-    if (hd <= 32) attn_simt_kernel<1><<<grid, 256, 0, st>>>(a);
-    else if (hd <= 64) attn_simt_kernel<2><<<grid, 256, 0, st>>>(a);
-    else if (hd <= 128) attn_simt_kernel<4><<<grid, 256, 0, st>>>(a);
-    else attn_simt_kernel<8><<<grid, 256, 0, st>>>(a);
+    AttnSimtArgs a{sv, content, C, content_scale, harmonic_n, B, H, T, hd, o, att_w, nullptr};
+    launch_attn_simt_t<float>(a, st);
+}
+
+void launch_attn_simt_fallback_bf16(const WbSeqView &sv, const float *content, int C, float content_scale,
+                                    const float *harmonic_n, int B, int H, int T, int hd, __nv_bfloat16 *o,
+                                    const int *tile_flags, cudaStream_t st) {
+    AttnSimtArgs a{sv, content, C, content_scale, harmonic_n, B, H, T, hd, o, nullptr, tile_flags};
+    launch_attn_simt_t<__nv_bfloat16>(a, st);
+}
+
+void launch_projections_exact(const ProjWeights &w, const float *x, int B, int T, const WbSeqView &sv, float *rs,
+                              float *content, cudaStream_t st) {
+    const int R = B * T, E = w.E, H = w.H, hd = w.hd;
+    OutMap dense{OUT_DENSE, rs, 2LL * H, sv, 0, T};
+    launch_seqdot(x, R, E, E, w.wrs_t, 2 * H, w.brs, 1, dense, st);
+    launch_phase(rs, R, H, T, sv, st);
+    if (content) {
+        OutMap cm{OUT_DENSE, content, (long long)H * w.C, sv, 0, T};
+        launch_seqdot(x, R, E, E, w.wc_t, H * w.C, w.bc, 1, cm, st);
+    }
+    for (int h = 0; h < H; h++) {
+        OutMap vm{OUT_SEQ_V, nullptr, 0, sv, h, T};
+        launch_seqdot(x + (size_t)h * hd, R, hd, E, w.wv_t + (size_t)h * hd * hd, hd, w.bv + (size_t)h * hd, 0,
+                      vm, st);
+    }
 }
 
 // ---------------------------------------------------------------------------

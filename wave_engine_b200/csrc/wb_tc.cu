@@ -1,32 +1,790 @@
-// wb_tc.cu -- WB_PATH_TENSOR sequencing (placeholder until the tcgen05
-// kernels land: every entry reports WB_ENOTSUP).
+// wb_tc.cu -- WB_PATH_TENSOR: tcgen05 tensor-core prefill attention.
+//
+// Wave attention scores are cos(n*(theta_q - theta_k)) + c_q.c_k/4 over
+// keys whose phase bucket is within one of the query's (src/common/attn.rs
+// :185-224).  By cos(a-b) = cos a cos b + sin a sin b the score is a dot
+// product of two 32-wide feature rows, so S = Qf Kf^T runs on tcgen05:
+//
+//   cols  0..5   cos/sin(n theta) as a bf16 hi/lo split:
+//                Q = [cH, cL, cH, sH, sL, sH], K = [cH, cH, cL, sH, sH, sL]
+//                (products hi*hi + lo*hi + hi*lo: ~2^-16 relative error)
+//   cols  6..21  content: Q = c_q/4, K = c_k (bf16)
+//   cols 22..29  bucket mask: Q = 0 for the 3 allowed buckets, -512 for
+//                the other 5; K = one-hot of the key's bucket.  A masked
+//                key's score is pushed to about -512 and its exp is 0.
+//   cols 30..31  zero
+//
+// Softmax needs no running max: every score is bounded by
+// 1 + |c_q| max_k|c_k| / 4 and the self score 1 + |c_q|^2/4 is always
+// present, so exp(s - s_self) neither overflows nor loses the row as long
+// as |c_q| (max|c_k| - |c_q|) / 4 <= 64.  Query tiles where that bound fails
+// are flagged and recomputed by the fp32 SIMT kernel.  The reference's
+// "always score the previous position" rule (attn.rs:212-221) is a single
+// extra term per query, added exactly in the epilogue when the previous
+// key is bucket-masked.
+#include "wb_ptx.cuh"
 #include "wb_tc.h"
+
+#include <cudaTypedefs.h>
+
+#include <cmath>
 
 namespace wb {
 
-int tc_layer_upload(TcLayerWeights *t, const wb_attn_weights_desc *w, const float *, std::string *) {
+static constexpr int QT = 128;      // queries per CTA (TMEM lanes)
+static constexpr int KT = 128;      // keys per tile
+static constexpr int FEAT = 32;     // feature width of Qf / Kf
+static constexpr float MASK_BIAS = -512.0f;
+static constexpr float BOUND_LIMIT = 64.0f;
+
+// ---------------------------------------------------------------------------
+// Tensor maps (driver entry point fetched at run time; no libcuda link).
+// ---------------------------------------------------------------------------
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
+        else
+            cudaGetLastError();
+    }
+    return fn;
+}
+
+static int make_tmap(CUtensorMap *m, const void *base, CUtensorMapDataType dt, int rank, const uint64_t *dims,
+                     const uint64_t *strides, const uint32_t *box, CUtensorMapSwizzle sw, std::string *msg) {
+    auto fn = encode_fn();
+    if (!fn) {
+        *msg = "cuTensorMapEncodeTiled unavailable";
+        return WB_ECUDA;
+    }
+    uint32_t estr[5] = {1, 1, 1, 1, 1};
+    CUresult r = fn(m, dt, rank, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        *msg = "cuTensorMapEncodeTiled failed with CUresult " + std::to_string((int)r);
+        return WB_ECUDA;
+    }
+    return WB_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Feature pre-pass: one thread per (b, h, t).
+// ---------------------------------------------------------------------------
+struct FeatArgs {
+    WbSeqView sv;
+    const float *content;  // [B*T][H*C] or nullptr
+    int C;
+    float cscale;
+    const float *hn;
+    int B, H, T, hd, hdp;
+    __nv_bfloat16 *qf, *kf, *vb;  // [BH][T][32], [BH][T][32], [BH][T][hdp]
+    float *m0, *sprev, *cnorm;    // [BH][T]
+    unsigned int *cmax;           // [BH], float bits
+};
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&v);
+}
+
+__global__ void __launch_bounds__(256) feat_kernel(FeatArgs a) {
+    const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    const long long BH = (long long)a.B * a.H;
+    if (i >= BH * a.T) return;
+    const int bh = (int)(i / a.T), t = (int)(i - (long long)bh * a.T);
+    const int b = bh / a.H, h = bh - b * a.H;
+    const long long base = wb_slot_base(a.sv, b, h);
+    const float th = a.sv.theta[base + t];
+    const int bk = a.sv.bucket[base + t];
+    const float n = a.hn[h];
+    float sn, cs;
+    sincosf(n * th, &sn, &cs);
+    const float csh = __bfloat162float(__float2bfloat16_rn(cs));
+    const float snh = __bfloat162float(__float2bfloat16_rn(sn));
+    const float csl = cs - csh, snl = sn - snh;
+    float c[16];
+    float c2 = 0.0f;
+    const int C = a.content ? a.C : 0;
+#pragma unroll
+    for (int d = 0; d < 16; d++) {
+        c[d] = (d < C) ? a.content[((long long)b * a.T + t) * ((long long)a.H * C) + (long long)h * C + d] : 0.0f;
+        c2 = fmaf(c[d], c[d], c2);
+    }
+    uint32_t q[16], k[16];
+    q[0] = pack_bf16(csh, csl);
+    q[1] = pack_bf16(csh, snh);
+    q[2] = pack_bf16(snl, snh);
+    k[0] = pack_bf16(csh, csh);
+    k[1] = pack_bf16(csl, snh);
+    k[2] = pack_bf16(snh, snl);
+#pragma unroll
+    for (int d = 0; d < 8; d++) {
+        q[3 + d] = pack_bf16(c[2 * d] * a.cscale, c[2 * d + 1] * a.cscale);
+        k[3 + d] = pack_bf16(c[2 * d], c[2 * d + 1]);
+    }
+    const uint32_t allow = allowed_bucket_mask(bk);
+#pragma unroll
+    for (int d = 0; d < 4; d++) {
+        const int b0 = 2 * d, b1 = 2 * d + 1;
+        q[11 + d] = pack_bf16((allow >> b0) & 1u ? 0.0f : MASK_BIAS, (allow >> b1) & 1u ? 0.0f : MASK_BIAS);
+        k[11 + d] = pack_bf16(bk == b0 ? 1.0f : 0.0f, bk == b1 ? 1.0f : 0.0f);
+    }
+    q[15] = k[15] = 0u;
+    uint4 *qd = reinterpret_cast<uint4 *>(a.qf + i * FEAT);
+    uint4 *kd = reinterpret_cast<uint4 *>(a.kf + i * FEAT);
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+        qd[u] = make_uint4(q[4 * u], q[4 * u + 1], q[4 * u + 2], q[4 * u + 3]);
+        kd[u] = make_uint4(k[4 * u], k[4 * u + 1], k[4 * u + 2], k[4 * u + 3]);
+    }
+    // values, zero padded to hdp
+    const float *vrow = a.sv.v + (base + t) * a.hd;
+    __nv_bfloat16 *vd = a.vb + i * a.hdp;
+    for (int d = 0; d < a.hdp; d += 8) {
+        uint32_t w[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int d0 = d + 2 * u, d1 = d0 + 1;
+            w[u] = pack_bf16(d0 < a.hd ? vrow[d0] : 0.0f, d1 < a.hd ? vrow[d1] : 0.0f);
+        }
+        *reinterpret_cast<uint4 *>(vd + d) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    // self score, previous-position term, content norm
+    const float self = 1.0f + c2 * a.cscale;
+    a.m0[i] = self;
+    const float cn = sqrtf(c2);
+    a.cnorm[i] = cn;
+    atomicMax(a.cmax + bh, __float_as_uint(cn));
+    float sp = -INFINITY;
+    if (t > 0) {
+        const int bkp = a.sv.bucket[base + t - 1];
+        if (!((allow >> bkp) & 1u)) {
+            sp = cosf(n * (th - a.sv.theta[base + t - 1]));
+            if (C) {
+                const float *cp = a.content + ((long long)b * a.T + t - 1) * ((long long)a.H * C) + (long long)h * C;
+                float dot = 0.0f;
+#pragma unroll
+                for (int d = 0; d < 16; d++)
+                    if (d < C) dot = fmaf(c[d], cp[d], dot);
+                sp += dot * a.cscale;
+            }
+        }
+    }
+    a.sprev[i] = sp;
+}
+
+// ---------------------------------------------------------------------------
+// Attention kernel: one CTA = 128 queries of one (b, h); 128 threads, thread
+// i owns query row i (TMEM lane i).  Thread 0 also issues the TMA loads and
+// the tcgen05.mma instructions.  Per key tile j (keys 128j..128j+127):
+//   S = Qf Kf_j^T (TMEM, fp32) -> P = exp(S - s_self) (bf16, smem, masked
+//   causally on the diagonal tile) -> O += P V_j (TMEM, fp32).
+// ---------------------------------------------------------------------------
+struct AttnTcArgs {
+    int BH, H, T, hd, n_qt;
+    const float *m0, *sprev, *cnorm;
+    const unsigned int *cmax;
+    WbSeqView sv;               // fp32 values for the previous-position term
+    __nv_bfloat16 *o;           // [B*T][E]
+    int E;
+    int *tile_flags;            // [BH][n_qt]
+    uint32_t *dev_err;
+};
+
+__device__ __forceinline__ float fast_exp2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+template <int HDP>
+struct AttnSmem {
+    static constexpr int Q_BYTES = QT * FEAT * 2;   // 8 KB
+    static constexpr int K_BYTES = KT * FEAT * 2;   // 8 KB
+    static constexpr int V_BYTES = KT * HDP * 2;    // 16 / 32 KB
+    static constexpr int P_BYTES = QT * KT * 2;     // 32 KB
+    static constexpr int OFF_Q = 0;
+    static constexpr int OFF_K = OFF_Q + Q_BYTES;
+    static constexpr int OFF_V = OFF_K + 2 * K_BYTES;
+    static constexpr int OFF_P = OFF_V + 2 * V_BYTES;
+    static constexpr int OFF_BAR = OFF_P + P_BYTES;
+    static constexpr int BYTES = OFF_BAR + 128 + 1024;  // barriers + alignment slack
+};
+
+template <int HDP>
+__global__ void __launch_bounds__(128, 1)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                   const __grid_constant__ CUtensorMap tm_v, AttnTcArgs a, int hdn) {
+    using L = AttnSmem<HDP>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sm + L::OFF_BAR);
+    uint64_t *full = bars;       // [2]
+    uint64_t *empty = bars + 2;  // [2]
+    uint64_t *qbar = bars + 4;
+    uint64_t *sbar = bars + 5;
+    uint64_t *obar = bars + 6;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 7);
+
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const int bh = blockIdx.x % a.BH;
+    const int qt = a.n_qt - 1 - (int)(blockIdx.x / a.BH);  // heaviest (longest) tiles first
+    const int b = bh / a.H, h = bh - b * a.H;
+    const int q0 = qt * QT, row = tid, q = q0 + row;
+    const long long rq = (long long)bh * a.T + q;
+
+    float m0 = 0.0f;
+    bool violate = false;
+    if (q < a.T) {
+        m0 = a.m0[rq];
+        const float cn = a.cnorm[rq], cm = __uint_as_float(a.cmax[bh]);
+        violate = 0.25f * cn * (cm - cn) > BOUND_LIMIT;
+    }
+    if (__syncthreads_or(violate)) {
+        if (tid == 0) a.tile_flags[(long long)bh * a.n_qt + qt] = 1;
+        return;
+    }
+    if (tid == 0) {
+        for (int i = 0; i < 7; i++) ptx::mbar_init(bars + i, 1);
+        ptx::fence_mbar_init();
+    }
+    if (warp == 0) {
+        ptx::tmem_alloc(tmem_slot, 256);
+        ptx::tmem_relinquish();
+    }
+    ptx::tc_fence_before();
+    __syncthreads();
+    ptx::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t S_t = tmem, O_t = tmem + 128;
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+
+    const int n_kt = qt + 1;
+    constexpr uint32_t IDESC_QK = ptx::idesc_bf16(128, 128, 0, 0);
+    const uint32_t idesc_pv = ptx::idesc_bf16(128, hdn, 0, 1);
+    const uint32_t sQ = ptx::smem_u32(sm + L::OFF_Q);
+    const uint32_t sK0 = ptx::smem_u32(sm + L::OFF_K);
+    const uint32_t sV0 = ptx::smem_u32(sm + L::OFF_V);
+    const uint32_t sP = ptx::smem_u32(sm + L::OFF_P);
+    constexpr uint32_t STAGE_TX = L::K_BYTES + L::V_BYTES;
+
+    bool ok = true;
+    auto load_tile = [&](int j) {
+        const int s = j & 1;
+        ptx::mbar_arrive_expect_tx(full + s, STAGE_TX);
+        ptx::tma_load_3d(sm + L::OFF_K + s * L::K_BYTES, &tm_k, full + s, 0, j * KT, bh);
+#pragma unroll
+        for (int c = 0; c < HDP / 64; c++)
+            ptx::tma_load_3d(sm + L::OFF_V + s * L::V_BYTES + c * (KT * 128), &tm_v, full + s, c * 64, j * KT, bh);
+    };
+    auto issue_qk = [&](int j) {
+        const uint32_t sK = sK0 + (j & 1) * L::K_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < FEAT / 16; kk++) {
+            const uint64_t ad = ptx::smem_desc(sQ + kk * 32, 16, 512, ptx::UMMA_SW64);
+            const uint64_t bd = ptx::smem_desc(sK + kk * 32, 16, 512, ptx::UMMA_SW64);
+            ptx::mma_bf16(S_t, ad, bd, IDESC_QK, kk > 0);
+        }
+        ptx::mma_commit(sbar);
+    };
+
+    if (tid == 0) {
+        ptx::prefetch_tmap(&tm_q);
+        ptx::prefetch_tmap(&tm_k);
+        ptx::prefetch_tmap(&tm_v);
+        ptx::mbar_arrive_expect_tx(qbar, L::Q_BYTES);
+        ptx::tma_load_3d(sm + L::OFF_Q, &tm_q, qbar, 0, q0, bh);
+        load_tile(0);
+        if (n_kt > 1) load_tile(1);
+        if (ptx::mbar_wait(qbar, 0) && ptx::mbar_wait(full, 0)) {
+            ptx::tc_fence_after();
+            issue_qk(0);
+        } else {
+            ok = false;
+            atomicOr(a.dev_err, WB_DERR_TIMEOUT_TMA);
+        }
+    }
+
+    const float LOG2E = 1.4426950408889634f;
+    const float nm0 = -m0 * LOG2E;
+    float l = 0.0f;
+    uint8_t *prow = sm + L::OFF_P + (row >> 3) * 1024 + (row & 7) * 128;
+    for (int j = 0; j < n_kt; j++) {
+        if (!ptx::mbar_wait(sbar, j & 1)) {
+            ok = false;
+            atomicOr(a.dev_err, WB_DERR_TIMEOUT_SOFTMAX);
+        }
+        if (__syncthreads_or(!ok)) break;
+        ptx::tc_fence_after();
+        const bool diag = (j == qt);
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+            uint32_t r[32];
+            ptx::tmem_ld32(S_t + lane_base + c * 32, r);
+            ptx::tmem_ld_wait();
+            uint32_t pk[16];
+#pragma unroll
+            for (int i = 0; i < 16; i++) {
+                float e0 = fast_exp2(fmaf(__uint_as_float(r[2 * i]), LOG2E, nm0));
+                float e1 = fast_exp2(fmaf(__uint_as_float(r[2 * i + 1]), LOG2E, nm0));
+                if (diag) {
+                    if (c * 32 + 2 * i > row) e0 = 0.0f;
+                    if (c * 32 + 2 * i + 1 > row) e1 = 0.0f;
+                }
+                l += e0 + e1;
+                pk[i] = pack_bf16(e0, e1);
+            }
+            uint8_t *half = prow + (c >> 1) * (QT * 128);
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int ch = (((c & 1) * 4) + u) ^ (row & 7);
+                *reinterpret_cast<uint4 *>(half + ch * 16) =
+                    make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+            }
+        }
+        ptx::fence_proxy_async_smem();
+        ptx::tc_fence_before();
+        __syncthreads();
+        if (tid == 0 && ok) {
+            ptx::tc_fence_after();
+            const uint32_t sV = sV0 + (j & 1) * L::V_BYTES;
+#pragma unroll
+            for (int kk = 0; kk < KT / 16; kk++) {
+                const uint64_t ad = ptx::smem_desc(sP + (kk >> 2) * (QT * 128) + (kk & 3) * 32, 16, 1024,
+                                                   ptx::UMMA_SW128);
+                const uint64_t bd = ptx::smem_desc(sV + kk * 2048, KT * 128, 1024, ptx::UMMA_SW128);
+                ptx::mma_bf16(O_t, ad, bd, idesc_pv, (j > 0 || kk > 0));
+            }
+            ptx::mma_commit(empty + (j & 1));
+            if (j + 1 < n_kt) {
+                if (ptx::mbar_wait(full + ((j + 1) & 1), ((j + 1) >> 1) & 1)) {
+                    ptx::tc_fence_after();
+                    issue_qk(j + 1);
+                } else {
+                    ok = false;
+                    atomicOr(a.dev_err, WB_DERR_TIMEOUT_TMA);
+                }
+            } else {
+                ptx::mma_commit(obar);
+            }
+            if (ok && j + 2 < n_kt) {
+                if (ptx::mbar_wait(empty + (j & 1), (j >> 1) & 1)) {
+                    load_tile(j + 2);
+                } else {
+                    ok = false;
+                    atomicOr(a.dev_err, WB_DERR_TIMEOUT_MMA);
+                }
+            }
+        }
+    }
+
+    // epilogue: O / l plus the previous-position term
+    bool done = ok && ptx::mbar_wait(obar, 0);
+    if (ok && !done) atomicOr(a.dev_err, WB_DERR_TIMEOUT_MMA);
+    ptx::tc_fence_after();
+    if (done) {
+        float o[HDP];
+#pragma unroll
+        for (int c = 0; c < HDP / 32; c++) {
+            uint32_t r[32];
+            ptx::tmem_ld32(O_t + lane_base + c * 32, r);
+            ptx::tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; i++) o[c * 32 + i] = __uint_as_float(r[i]);
+        }
+        if (q < a.T) {
+            const float sp = a.sprev[rq];
+            const long long vbase = wb_slot_base(a.sv, b, h);
+            if (sp > -INFINITY) {
+                const float e = __expf(sp - m0);
+                const float *vp = a.sv.v + (vbase + q - 1) * a.hd;
+                l += e;
+#pragma unroll
+                for (int d = 0; d < HDP; d++)
+                    if (d < a.hd) o[d] = fmaf(e, vp[d], o[d]);
+            }
+            const float inv = 1.0f / l;
+            __nv_bfloat16 *dst = a.o + ((long long)b * a.T + q) * a.E + (long long)h * a.hd;
+#pragma unroll
+            for (int d = 0; d < HDP; d++)
+                if (d < a.hd) dst[d] = __float2bfloat16_rn(o[d] * inv);
+        }
+    }
+    ptx::tc_fence_before();
+    __syncthreads();
+    if (warp == 0) ptx::tmem_dealloc(tmem, 256);
+}
+
+// ---------------------------------------------------------------------------
+// bf16 GEMM with fp32 output and bias: C[m][n] = sum_k A[m][k] B[n][k] + bias[n]
+// (A, B K-major).  128x128 tile per CTA, 64-wide K blocks in a 3-stage TMA
+// ring; warp 0 lane 0 loads, warp 1 lane 0 issues tcgen05.mma; all four
+// warps run the epilogue from TMEM.
+// ---------------------------------------------------------------------------
+static constexpr int GBM = 128, GBN = 128, GBK = 64, GST = 3;
+static constexpr int G_STAGE = (GBM + GBN) * GBK * 2;  // 32 KB
+static constexpr int G_SMEM = GST * G_STAGE + 128 + 1024;
+
+__global__ void __launch_bounds__(128, 1)
+    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                     const float *__restrict__ bias, float *__restrict__ C, int M, int N, int K, long long ldc,
+                     uint32_t *dev_err) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sm + GST * G_STAGE);
+    uint64_t *full = bars, *empty = bars + GST, *done = bars + 2 * GST;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * GST + 1);
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const int m0 = blockIdx.x * GBM, n0 = blockIdx.y * GBN;
+    const int nk = (K + GBK - 1) / GBK;
+    if (tid == 0) {
+        for (int i = 0; i < 2 * GST + 1; i++) ptx::mbar_init(bars + i, 1);
+        ptx::fence_mbar_init();
+    }
+    if (warp == 0) {
+        ptx::tmem_alloc(tmem_slot, 128);
+        ptx::tmem_relinquish();
+    }
+    ptx::tc_fence_before();
+    __syncthreads();
+    ptx::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    bool ok = true;
+    if (tid == 0) {
+        ptx::prefetch_tmap(&tm_a);
+        ptx::prefetch_tmap(&tm_b);
+        for (int kb = 0; kb < nk; kb++) {
+            const int s = kb % GST;
+            if (kb >= GST && !ptx::mbar_wait(empty + s, ((kb / GST) - 1) & 1)) {
+                atomicOr(dev_err, WB_DERR_TIMEOUT_MMA);
+                ok = false;
+                break;
+            }
+            uint8_t *st = sm + s * G_STAGE;
+            ptx::mbar_arrive_expect_tx(full + s, G_STAGE);
+            ptx::tma_load_2d(st, &tm_a, full + s, kb * GBK, m0);
+            ptx::tma_load_2d(st + GBM * GBK * 2, &tm_b, full + s, kb * GBK, n0);
+        }
+    } else if (tid == 32) {
+        constexpr uint32_t IDESC = ptx::idesc_bf16(GBM, GBN, 0, 0);
+        for (int kb = 0; kb < nk; kb++) {
+            const int s = kb % GST;
+            if (!ptx::mbar_wait(full + s, (kb / GST) & 1)) {
+                atomicOr(dev_err, WB_DERR_TIMEOUT_TMA);
+                ok = false;
+                break;
+            }
+            ptx::tc_fence_after();
+            const uint32_t sa = ptx::smem_u32(sm + s * G_STAGE), sb = sa + GBM * GBK * 2;
+#pragma unroll
+            for (int k = 0; k < GBK / 16; k++)
+                ptx::mma_bf16(tmem, ptx::smem_desc(sa + k * 32, 16, 1024, ptx::UMMA_SW128),
+                              ptx::smem_desc(sb + k * 32, 16, 1024, ptx::UMMA_SW128), IDESC, (kb > 0 || k > 0));
+            ptx::mma_commit(empty + s);
+        }
+        ptx::mma_commit(done);
+    }
+    const bool fin = ptx::mbar_wait(done, 0);
+    if (!fin && tid == 0) atomicOr(dev_err, WB_DERR_TIMEOUT_MMA);
+    ptx::tc_fence_after();
+    if (fin) {
+        const int m = m0 + tid;
+#pragma unroll 1
+        for (int c = 0; c < GBN / 32; c++) {
+            uint32_t r[32];
+            ptx::tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + c * 32, r);
+            ptx::tmem_ld_wait();
+            if (m < M) {
+                float *dst = C + (long long)m * ldc + n0 + c * 32;
+#pragma unroll
+                for (int i = 0; i < 32; i++) {
+                    const int n = n0 + c * 32 + i;
+                    if (n < N) dst[i] = __uint_as_float(r[i]) + bias[n];
+                }
+            }
+        }
+    }
+    ptx::tc_fence_before();
+    __syncthreads();
+    if (warp == 0) ptx::tmem_dealloc(tmem, 128);
+    (void)ok;
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+__global__ void f32_to_bf16_kernel(const float *in, __nv_bfloat16 *out, long long n) {
+    const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    if (i < n) out[i] = __float2bfloat16_rn(in[i]);
+}
+
+int tc_layer_upload(TcLayerWeights *t, const wb_attn_weights_desc *w, std::string *msg) {
     t->E = w->n_embd;
     t->H = w->n_head;
     t->hd = w->n_embd / w->n_head;
     t->C = w->content_dim;
+    const size_t n = (size_t)t->E * t->E;
+    float *tmp = nullptr;
+    if (cudaMalloc(&t->w_o, n * sizeof(__nv_bfloat16)) != cudaSuccess || cudaMalloc(&tmp, n * sizeof(float)) != cudaSuccess) {
+        cudaGetLastError();
+        if (tmp) cudaFree(tmp);
+        *msg = "cudaMalloc for bf16 out_proj failed";
+        return WB_ENOMEM;
+    }
+    if (cudaMemcpy(tmp, w->out_proj_w, n * sizeof(float), cudaMemcpyHostToDevice) != cudaSuccess) {
+        cudaFree(tmp);
+        *msg = "upload of out_proj failed";
+        return WB_ECUDA;
+    }
+    f32_to_bf16_kernel<<<(unsigned)((n + 255) / 256), 256>>>(tmp, t->w_o, (long long)n);
+    cudaError_t e = cudaDeviceSynchronize();
+    cudaFree(tmp);
+    if (e != cudaSuccess) {
+        *msg = std::string("bf16 conversion failed: ") + cudaGetErrorString(e);
+        return WB_ECUDA;
+    }
     return WB_OK;
 }
-void tc_layer_free(TcLayerWeights *) {}
 
-int tc_attn_forward(const TcLayerWeights &, const float *, int, int, bool, float *, float *, Workspace *,
-                    uint32_t *, int, cudaStream_t, std::string *msg) {
-    *msg = "WB_PATH_TENSOR not built yet";
-    return WB_ENOTSUP;
+void tc_layer_free(TcLayerWeights *t) {
+    if (t->w_o) cudaFree(t->w_o);
+    t->w_o = nullptr;
 }
-int tc_kv_prefill(const TcLayerWeights &, const WbSeqView &, const float *, int, int, float *, Workspace *,
-                  uint32_t *, int, cudaStream_t, std::string *msg) {
-    *msg = "WB_PATH_TENSOR not built yet";
-    return WB_ENOTSUP;
+
+// Workspace pieces of the attention core, carved after `off`.
+struct CoreLayout {
+    size_t qf, kf, vb, m0, sp, cn, cm, fl, o, end;
+};
+static CoreLayout core_layout(const TcLayerWeights &t, int B, int T, size_t off) {
+    const int hdp = t.hd <= 64 ? 64 : 128;
+    const long long BH = (long long)B * t.H, R = (long long)B * T;
+    const int n_qt = (T + QT - 1) / QT;
+    Carve cv;
+    cv.off = off;
+    CoreLayout c;
+    c.qf = cv.take<__nv_bfloat16>(BH * T * FEAT);
+    c.kf = cv.take<__nv_bfloat16>(BH * T * FEAT);
+    c.vb = cv.take<__nv_bfloat16>(BH * T * hdp);
+    c.m0 = cv.take<float>(BH * T);
+    c.sp = cv.take<float>(BH * T);
+    c.cn = cv.take<float>(BH * T);
+    c.cm = cv.take<unsigned int>(BH);
+    c.fl = cv.take<int>(BH * n_qt);
+    c.o = cv.take<__nv_bfloat16>(R * t.E);
+    c.end = cv.off;
+    return c;
 }
-int tc_kv_decode(const TcLayerWeights &, const WbSeqView &, const int32_t *, int, const float *, int, float *,
-                 Workspace *, uint32_t *, int, cudaStream_t, std::string *msg) {
-    *msg = "WB_PATH_TENSOR not built yet";
-    return WB_ENOTSUP;
+
+// Runs features -> tcgen05 attention -> SIMT fallback for flagged tiles ->
+// tcgen05 out_proj, given phases/buckets/values already in `sv` and (when
+// use_content) content vectors in `content`.  The workspace must already
+// hold core_layout(...).end bytes.
+static int tc_attention_core(const TcLayerWeights &t, const WbSeqView &sv, const float *content, int B, int T,
+                             float *y, Workspace *ws, const CoreLayout &lay, uint32_t *dev_err, cudaStream_t st,
+                             std::string *msg) {
+    const int H = t.H, hd = t.hd, E = t.E;
+    const int hdp = hd <= 64 ? 64 : 128;
+    const int hdn = (hd + 15) / 16 * 16;
+    const long long BH = (long long)B * H, R = (long long)B * T;
+    const int n_qt = (T + QT - 1) / QT;
+    int rc;
+    const size_t o_qf = lay.qf, o_kf = lay.kf, o_vb = lay.vb, o_m0 = lay.m0, o_sp = lay.sp, o_cn = lay.cn,
+                 o_cm = lay.cm, o_fl = lay.fl, o_o = lay.o;
+    char *w = (char *)ws->p;
+    __nv_bfloat16 *qf = (__nv_bfloat16 *)(w + o_qf), *kf = (__nv_bfloat16 *)(w + o_kf),
+                  *vb = (__nv_bfloat16 *)(w + o_vb), *ob = (__nv_bfloat16 *)(w + o_o);
+    float *m0 = (float *)(w + o_m0), *sp = (float *)(w + o_sp), *cn = (float *)(w + o_cn);
+    unsigned int *cm = (unsigned int *)(w + o_cm);
+    int *fl = (int *)(w + o_fl);
+    if (cudaMemsetAsync(cm, 0, BH * sizeof(unsigned int), st) != cudaSuccess ||
+        cudaMemsetAsync(fl, 0, BH * n_qt * sizeof(int), st) != cudaSuccess) {
+        *msg = "cudaMemsetAsync failed";
+        return WB_ECUDA;
+    }
+    const float cscale = content ? 1.0f / std::sqrt((float)t.C) : 0.0f;
+    FeatArgs fa{sv, content, content ? t.C : 0, cscale, t.harmonic_n, B, H, T, hd, hdp, qf, kf, vb, m0, sp, cn, cm};
+    feat_kernel<<<(unsigned)((BH * T + 255) / 256), 256, 0, st>>>(fa);
+
+    CUtensorMap tq, tk, tv;
+    {
+        const uint64_t dims[3] = {FEAT, (uint64_t)T, (uint64_t)BH};
+        const uint64_t strides[2] = {FEAT * 2, (uint64_t)T * FEAT * 2};
+        const uint32_t box[3] = {FEAT, 128, 1};
+        if ((rc = make_tmap(&tq, qf, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, dims, strides, box,
+                            CU_TENSOR_MAP_SWIZZLE_64B, msg)))
+            return rc;
+        if ((rc = make_tmap(&tk, kf, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, dims, strides, box,
+                            CU_TENSOR_MAP_SWIZZLE_64B, msg)))
+            return rc;
+        const uint64_t vdims[3] = {(uint64_t)hdp, (uint64_t)T, (uint64_t)BH};
+        const uint64_t vstr[2] = {(uint64_t)hdp * 2, (uint64_t)T * hdp * 2};
+        const uint32_t vbox[3] = {64, 128, 1};
+        if ((rc = make_tmap(&tv, vb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, vdims, vstr, vbox,
+                            CU_TENSOR_MAP_SWIZZLE_128B, msg)))
+            return rc;
+    }
+    AttnTcArgs aa{(int)BH, H, T, hd, n_qt, m0, sp, cn, cm, sv, ob, E, fl, dev_err};
+    const unsigned grid = (unsigned)(BH * n_qt);
+    if (hdp == 64) {
+        cudaFuncSetAttribute(attn_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnSmem<64>::BYTES);
+        attn_tc_kernel<64><<<grid, 128, AttnSmem<64>::BYTES, st>>>(tq, tk, tv, aa, hdn);
+    } else {
+        cudaFuncSetAttribute(attn_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             AttnSmem<128>::BYTES);
+        attn_tc_kernel<128><<<grid, 128, AttnSmem<128>::BYTES, st>>>(tq, tk, tv, aa, hdn);
+    }
+    launch_attn_simt_fallback_bf16(sv, content, content ? t.C : 0, cscale, t.harmonic_n, B, H, T, hd, ob, fl, st);
+
+    // out_proj: y = o W_o^T + b_o
+    CUtensorMap ta, tb;
+    {
+        const uint64_t adims[2] = {(uint64_t)E, (uint64_t)R};
+        const uint64_t astr[1] = {(uint64_t)E * 2};
+        const uint32_t abox[2] = {GBK, GBM};
+        if ((rc = make_tmap(&ta, ob, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, adims, astr, abox,
+                            CU_TENSOR_MAP_SWIZZLE_128B, msg)))
+            return rc;
+        const uint64_t bdims[2] = {(uint64_t)E, (uint64_t)E};
+        const uint32_t bbox[2] = {GBK, GBN};
+        if ((rc = make_tmap(&tb, t.w_o, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, bdims, astr, bbox,
+                            CU_TENSOR_MAP_SWIZZLE_128B, msg)))
+            return rc;
+    }
+    cudaFuncSetAttribute(gemm_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, G_SMEM);
+    dim3 gg((unsigned)((R + GBM - 1) / GBM), (unsigned)((E + GBN - 1) / GBN));
+    gemm_bf16_kernel<<<gg, 128, G_SMEM, st>>>(ta, tb, t.b_o, y, (int)R, E, E, E, dev_err);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        *msg = std::string("tensor path launch failed: ") + cudaGetErrorString(e);
+        return WB_ECUDA;
+    }
+    return WB_OK;
+}
+
+int tc_gemm_bf16(const __nv_bfloat16 *A, const __nv_bfloat16 *B, const float *bias, float *C, int M, int N, int K,
+                 uint32_t *dev_err, cudaStream_t st, std::string *msg) {
+    if (M <= 0 || N <= 0 || K <= 0 || K % 8) {
+        *msg = "bad GEMM shape (K must be a positive multiple of 8)";
+        return WB_EINVAL;
+    }
+    CUtensorMap ta, tb;
+    int rc;
+    const uint64_t adims[2] = {(uint64_t)K, (uint64_t)M};
+    const uint64_t str[1] = {(uint64_t)K * 2};
+    const uint32_t abox[2] = {GBK, GBM};
+    if ((rc = make_tmap(&ta, A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, adims, str, abox, CU_TENSOR_MAP_SWIZZLE_128B,
+                        msg)))
+        return rc;
+    const uint64_t bdims[2] = {(uint64_t)K, (uint64_t)N};
+    const uint32_t bbox[2] = {GBK, GBN};
+    if ((rc = make_tmap(&tb, B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, bdims, str, bbox, CU_TENSOR_MAP_SWIZZLE_128B,
+                        msg)))
+        return rc;
+    cudaFuncSetAttribute(gemm_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, G_SMEM);
+    dim3 gg((unsigned)((M + GBM - 1) / GBM), (unsigned)((N + GBN - 1) / GBN));
+    gemm_bf16_kernel<<<gg, 128, G_SMEM, st>>>(ta, tb, bias, C, M, N, K, N, dev_err);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        *msg = std::string("gemm launch failed: ") + cudaGetErrorString(e);
+        return WB_ECUDA;
+    }
+    return WB_OK;
+}
+
+int tc_attn_forward(const TcLayerWeights &t, const float *x, int B, int T, bool use_content, float *y,
+                    float *phases_out, Workspace *ws, uint32_t *dev_err, int sm_count, cudaStream_t st,
+                    std::string *msg) {
+    (void)sm_count;
+    const int H = t.H, hd = t.hd;
+    const long long R = (long long)B * T;
+    if ((t.E * 2) % 16) {
+        *msg = "n_embd must be a multiple of 8 for the tensor path";
+        return WB_ENOTSUP;
+    }
+    if (hd > 128) {
+        *msg = "WB_PATH_TENSOR supports head_dim <= 128";
+        return WB_ENOTSUP;
+    }
+    Carve cv;
+    const size_t o_rs = cv.take<float>(R * 2 * H);
+    const size_t o_ct = cv.take<float>(use_content ? R * H * t.C : 1);
+    const size_t o_th = cv.take<float>(R * H);
+    const size_t o_bk = cv.take<uint8_t>(R * H);
+    const size_t o_v = cv.take<float>(R * H * hd);
+    const CoreLayout lay = core_layout(t, B, T, cv.off);
+    if (ws_ensure(ws, lay.end, msg)) return WB_ENOMEM;
+    char *w = (char *)ws->p;
+    WbSeqView sv;
+    sv.theta = (float *)(w + o_th);
+    sv.bucket = (uint8_t *)(w + o_bk);
+    sv.v = (float *)(w + o_v);
+    sv.seq_stride = (long long)H * T;
+    sv.cap = T;
+    sv.slot = nullptr;
+    float *content = use_content ? (float *)(w + o_ct) : nullptr;
+    launch_projections_exact(t.pw, x, B, T, sv, (float *)(w + o_rs), content, st);
+    int rc = tc_attention_core(t, sv, content, B, T, y, ws, lay, dev_err, st, msg);
+    if (rc) return rc;
+    if (phases_out &&
+        cudaMemcpyAsync(phases_out, sv.theta, R * H * sizeof(float), cudaMemcpyDeviceToDevice, st) != cudaSuccess) {
+        *msg = "phase copy failed";
+        return WB_ECUDA;
+    }
+    return WB_OK;
+}
+
+int tc_kv_prefill(const TcLayerWeights &t, const WbSeqView &sv, const float *x, int n_seq, int T, float *y,
+                  Workspace *ws, uint32_t *dev_err, int sm_count, cudaStream_t st, std::string *msg) {
+    (void)sm_count;
+    if (t.hd > 128) {
+        *msg = "WB_PATH_TENSOR supports head_dim <= 128";
+        return WB_ENOTSUP;
+    }
+    const long long R = (long long)n_seq * T;
+    Carve cv;
+    const size_t o_rs = cv.take<float>(R * 2 * t.H);
+    const CoreLayout lay = core_layout(t, n_seq, T, cv.off);
+    if (ws_ensure(ws, lay.end, msg)) return WB_ENOMEM;
+    launch_projections_exact(t.pw, x, n_seq, T, sv, (float *)((char *)ws->p + o_rs), nullptr, st);
+    return tc_attention_core(t, sv, nullptr, n_seq, T, y, ws, lay, dev_err, st, msg);
+}
+
+int tc_kv_decode(const TcLayerWeights &t, const WbSeqView &sv, const int32_t *len, int cap, const float *x,
+                 int n_seq, float *y, Workspace *ws, uint32_t *dev_err, int sm_count, cudaStream_t st,
+                 std::string *msg) {
+    (void)cap;
+    (void)dev_err;
+    (void)sm_count;
+    const int E = t.E, H = t.H, hd = t.hd;
+    Carve cv;
+    const size_t o_rs = cv.take<float>((size_t)n_seq * 2 * H);
+    const size_t o_th = cv.take<float>((size_t)n_seq * H);
+    const size_t o_vn = cv.take<float>((size_t)n_seq * H * hd);
+    const size_t o_o = cv.take<float>((size_t)n_seq * E);
+    if (ws_ensure(ws, cv.off, msg)) return WB_ENOMEM;
+    char *w = (char *)ws->p;
+    float *rs = (float *)(w + o_rs), *th = (float *)(w + o_th), *vn = (float *)(w + o_vn), *o = (float *)(w + o_o);
+    OutMap rm{OUT_DENSE, rs, 2LL * H, sv, 0, 1};
+    launch_seqdot(x, n_seq, E, E, t.pw.wrs_t, 2 * H, t.pw.brs, 1, rm, st);
+    launch_theta_only(rs, n_seq * H, th, st);
+    for (int h = 0; h < H; h++) {
+        OutMap vm{OUT_DENSE, vn + (size_t)h * hd, (long long)H * hd, sv, 0, 1};
+        launch_seqdot(x + (size_t)h * hd, n_seq, hd, E, t.pw.wv_t + (size_t)h * hd * hd, hd, t.pw.bv + (size_t)h * hd,
+                      0, vm, st);
+    }
+    launch_decode_simt(sv, len, th, vn, t.harmonic_n, n_seq, H, hd, o, st);
+    OutMap om{OUT_DENSE, y, E, sv, 0, 1};
+    launch_seqdot(o, n_seq, E, E, t.wo_t, E, t.b_o, 0, om, st);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        *msg = std::string("decode launch failed: ") + cudaGetErrorString(e);
+        return WB_ECUDA;
+    }
+    return WB_OK;
 }
 
 }  // namespace wb

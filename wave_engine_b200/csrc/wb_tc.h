@@ -10,18 +10,14 @@ namespace wb {
 
 struct TcLayerWeights {
     int E = 0, H = 0, hd = 0, C = 0;
-    float *harmonic_n = nullptr;   // [H]
-    float *w_rs = nullptr;         // [E][H][2] phase projection, input-major
-    float *b_rs = nullptr;         // [H][2]
-    float *w_c = nullptr;          // [H*C][E] content projection rows (tf32 B operand)
-    float *b_c = nullptr;          // [H*C]
-    float *w_v = nullptr;          // [H][hd][hd] value projection rows (out, in)
-    float *b_v = nullptr;          // [H][hd]
-    __nv_bfloat16 *w_o = nullptr;  // [E][E] out_proj rows (bf16 K-major B operand)
-    float *b_o = nullptr;          // [E]
+    ProjWeights pw{};                  // fp32 projection weights (shared with the SIMT path)
+    const float *harmonic_n = nullptr; // [H] softplus(harmonic_raw)
+    const float *b_o = nullptr;        // [E] out_proj bias
+    const float *wo_t = nullptr;       // [E][E] out_proj, input-major fp32 (decode rows)
+    __nv_bfloat16 *w_o = nullptr;      // [E][E] out_proj rows, bf16 (K-major B operand)
 };
 
-int tc_layer_upload(TcLayerWeights *t, const wb_attn_weights_desc *w, const float *hn_host, std::string *msg);
+int tc_layer_upload(TcLayerWeights *t, const wb_attn_weights_desc *w, std::string *msg);
 void tc_layer_free(TcLayerWeights *t);
 
 int tc_attn_forward(const TcLayerWeights &t, const float *x, int B, int T, bool use_content, float *y,
@@ -29,6 +25,8 @@ int tc_attn_forward(const TcLayerWeights &t, const float *x, int B, int T, bool 
                     std::string *msg);
 int tc_kv_prefill(const TcLayerWeights &t, const WbSeqView &sv, const float *x, int n_seq, int T, float *y,
                   Workspace *ws, uint32_t *dev_err, int sm_count, cudaStream_t st, std::string *msg);
+int tc_gemm_bf16(const __nv_bfloat16 *A, const __nv_bfloat16 *B, const float *bias, float *C, int M, int N, int K,
+                 uint32_t *dev_err, cudaStream_t st, std::string *msg);
 int tc_kv_decode(const TcLayerWeights &t, const WbSeqView &sv, const int32_t *len, int cap, const float *x,
                  int n_seq, float *y, Workspace *ws, uint32_t *dev_err, int sm_count, cudaStream_t st,
                  std::string *msg);
