@@ -1,0 +1,425 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 wave-attention hot path (prefill + KV-cache decode).
+
+Workload (the configuration its metric is quoted
+on): the 768-dim production model -- n_embd 768, 12 heads of 64, 24 attention
+layers -- with batch 32: a 1024-token prefill through all 24 layers, then 256
+greedy decode steps, each one new position per sequence through all 24
+layers.  One bench step is that whole job.  Weights are seeded N(0, 0.02)
+(the reference's harmonic init for n_h), the per-layer attention inputs are
+seeded N(0, 1) rows standing in for the LayerNorm output (synthetic data: no
+datasets here).  Every per-layer input is 100 MB (prefill) and all inputs
+(3 GB) are resident in HBM, larger than the 126 MB L2.
+
+``value`` = (prefill + decode tokens of all ranks) / device time of a step
+(CUDA events, max over ranks).  ``e2e`` = the same through the public API
+with pinned HOST buffers (host->device copies of every layer's input and
+device->host copies of every output inside the timed region).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+Under torchrun each rank runs the full batch-32 job on its own GPU (the
+attention forward shards by sequence with no data-path collective): weak
+scaling.  ``--impl reference`` times the reference algorithm on the host CPU
+(the C restatement in oracle/, the Rust reference cannot be built here) on a
+bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "attn prefill tok/s + decode tok/s @768-dim, 1/2/4/8 GPU; % TC/HBM roofline"
+CFG = dict(n_embd=768, n_head=12, head_dim=64, content_dim=16, n_layers=24, batch=32, seq_len=1024,
+           decode_steps=256)
+WORKLOAD = ("768-dim production model (12 heads x 64, 24 layers): batch 32, 1024-token prefill "
+            "then 256 greedy KV-cache decode steps")
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+class Clocks:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9 and parts[1].isdigit():
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = sorted(int(r[1]) for r in rows)
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": int(rows[0][2]), "reasons": reasons,
+                "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows if r[3].replace('.', '').isdigit())}
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d.get("hbm_gbs", 6650.0), d.get("bf16_tflops", 1590.0), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# algorithmic work (per SURVEY 8(d) formulas, restated here)
+# ---------------------------------------------------------------------------
+def decode_bytes_exact(bucket_slots, T0, S, H, hd):
+    """Algorithmic HBM bytes of every decode attention launch of a step: for
+    each new position p (p = T0..T0+S-1) of each (layer, seq, head), the
+    phase+bucket of all p cached keys (5 B each) plus the fp32 value row
+    (4*hd B) of each key the mask lets through (bucket b-1..b+1 or the
+    previous position), plus the query/output rows.  bucket_slots is a
+    numpy u8 array [L][B][H][T0+S] of the cache's buckets after the step."""
+    import numpy as np
+    b = bucket_slots.astype(np.int64)
+    L, B, Hh, n = b.shape
+    onehot = np.zeros((L, B, Hh, n + 1, 8), np.int32)
+    onehot[:, :, :, 1:, :] = (b[..., None] == np.arange(8)).astype(np.int32)
+    cnt = np.cumsum(onehot, axis=3)  # cnt[..., p, k] = #keys < p in bucket k
+    total_keys = 0
+    unmasked = 0
+    for p in range(T0, T0 + S):
+        qb = b[:, :, :, p]
+        c = cnt[:, :, :, p, :]
+        adj = sum(np.take_along_axis(c, ((qb + d) % 8)[..., None], axis=3)[..., 0] for d in (-1, 0, 1))
+        prev_b = b[:, :, :, p - 1]
+        prev_masked = ((prev_b - qb) % 8)
+        prev_masked = ~np.isin(prev_masked, (0, 1, 7))
+        unmasked += int(adj.sum() + prev_masked.sum())
+        total_keys += L * B * Hh * p
+    return total_keys * 5 + unmasked * hd * 4, unmasked, total_keys
+
+
+def prefill_flops_per_layer(B, T, E, H, hd, C):
+    """2*B*T*E*H*(2+C) + 2*B*T*E*hd + P*2*(2+C+hd) + 2*B*T*E^2 with the dense
+    causal pair count P = B*H*T(T+1)/2."""
+    P = B * H * T * (T + 1) // 2
+    return 2 * B * T * E * H * (2 + C) + 2 * B * T * E * hd + P * 2 * (2 + C + hd) + 2 * B * T * E * E
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def run_ours(args):
+    import numpy as np
+    import torch
+    import wave_engine_b200 as wb
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+    E, H, hd, C, L = CFG["n_embd"], CFG["n_head"], CFG["head_dim"], CFG["content_dim"], CFG["n_layers"]
+    B, T, S = CFG["batch"], CFG["seq_len"], args.decode_steps
+    ctx = wb.Context(local)
+    stream = torch.cuda.current_stream(dev)
+    ctx.set_stream(stream.cuda_stream)
+    layers = [wb.AttnLayer(ctx, wb.gaussian_block_attn(1000 + l, H, E, C)) for l in range(L)]
+    cache = wb.KvCache(L, H, hd, max_seqs=B, max_ctx=T + S, ctx=ctx)
+    g = torch.Generator(device=dev).manual_seed(1234 + 7919 * rank)
+    x_pre = torch.randn((L, B, T, E), generator=g, device=dev)
+    x_dec = torch.randn((S, L, B, E), generator=g, device=dev)
+    y_pre = torch.empty((B, T, E), device=dev)
+    y_dec = torch.empty((B, E), device=dev)
+    ids = np.arange(B, dtype=np.int32)
+
+    def step(xp, xd, yp, yd, ev=None):
+        cache.reset()
+        for l in range(L):
+            cache.prefill(l, layers[l], xp[l], ids, out=yp)
+        if ev is not None:
+            ev.record(stream)
+        for s in range(S):
+            for l in range(L):
+                cache.forward_one(l, layers[l], xd[s, l], ids, out=yd)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        import torch.distributed as dist
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # launch count of one step (every named kernel of the library)
+    ctx.profile("")
+    step(x_pre, x_dec, y_pre, y_dec)
+    launches_per_step = sum(n for n, _ in ctx.profile_report().values())
+    ctx.profile(None)
+
+    for _ in range(max(0, args.warmup - 1)):
+        step(x_pre, x_dec, y_pre, y_dec)
+    barrier()
+
+    dominant = args.roofline_kernel
+    ctx.profile(dominant)
+    clocks = Clocks(local)
+    clocks.start()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    mids = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    e0.record(stream)
+    for k in range(args.steps):
+        starts[k].record(stream)
+        step(x_pre, x_dec, y_pre, y_dec, ev=mids[k])
+        ends[k].record(stream)
+    e1.record(stream)
+    barrier()
+    clk = clocks.stop()
+    ms_total = e0.elapsed_time(e1)
+    pre_ms = sum(starts[k].elapsed_time(mids[k]) for k in range(args.steps)) / args.steps
+    dec_ms = sum(mids[k].elapsed_time(ends[k]) for k in range(args.steps)) / args.steps
+    prof = ctx.profile_report()
+    ctx.profile(None)
+    ms_step = max_over_ranks(ms_total / args.steps)
+    pre_ms = max_over_ranks(pre_ms)
+    dec_ms = max_over_ranks(dec_ms)
+    tok_step = B * T + B * S
+    value = world * tok_step / (ms_step / 1e3)
+
+    # roofline of the dominant kernel
+    hbm, bf16, peak_kind = peaks()
+    roof = None
+    if dominant in prof:
+        n, tot = prof[dominant]
+        per_launch_ms = tot / n
+        if "decode" in dominant:
+            bk = np.stack([np.stack([cache.read(l, b)[1] for b in range(B)]) for l in range(L)])
+            byts, unmasked, keys = decode_bytes_exact(bk, T, S, H, hd)
+            alg = byts / (S * L)
+            q_out = B * E * 4 * 2
+            alg += q_out
+            ach = alg / (per_launch_ms / 1e3) / 1e9
+            roof = {"kernel": dominant, "bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
+                    "frac": round(ach / hbm, 4), "traffic": None, "peak_kind": peak_kind,
+                    "algorithmic_bytes_per_launch": int(alg), "launch_ms": round(per_launch_ms, 5),
+                    "unmasked_key_fraction": round(unmasked / keys, 4)}
+        else:
+            fl = prefill_flops_per_layer(B, T, E, H, hd, C)
+            ach = fl / (per_launch_ms / 1e3) / 1e12
+            roof = {"kernel": dominant, "bound": "tensor", "achieved": round(ach, 2), "peak": bf16,
+                    "unit": "TFLOP/s", "frac": round(ach / bf16, 4), "traffic": None, "peak_kind": peak_kind,
+                    "launch_ms": round(per_launch_ms, 5)}
+
+    # end to end through the public API with pinned host buffers
+    e2e = None
+    if not args.no_e2e:
+        xp_h = x_pre.cpu().pin_memory()
+        xd_h = x_dec.cpu().pin_memory()
+        yp_h = torch.empty((B, T, E)).pin_memory()
+        yd_h = torch.empty((B, E)).pin_memory()
+        del x_pre, x_dec
+        n_e2e = max(1, min(args.steps, args.e2e_steps))
+        step(xp_h, xd_h, yp_h, yd_h)
+        barrier()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for _ in range(n_e2e):
+            step(xp_h, xd_h, yp_h, yd_h)
+        f1.record(stream)
+        barrier()
+        e2e_ms = max_over_ranks(f0.elapsed_time(f1) / n_e2e)
+        e2e = {"value": round(world * tok_step / (e2e_ms / 1e3), 1), "unit": "tok/s",
+               "h2d_bytes_per_step": int(xp_h.numel() * 4 + xd_h.numel() * 4 + (L + S * L) * B * 4),
+               "d2h_bytes_per_step": int((L * B * T * E + S * L * B * E) * 4), "ms_per_step": round(e2e_ms, 3),
+               "steps": n_e2e}
+
+    out = {
+        "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_step, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp32 io; bf16 hi/lo + tf32 tensor MMA, fp32 accumulate",
+        "data": "synthetic (seeded N(0,0.02) weights, N(0,1) layer inputs)",
+        "config": {"workload": WORKLOAD, "n_embd": E, "n_head": H, "head_dim": hd, "layers": L, "batch_per_gpu": B,
+                   "seq_len": T, "decode_steps": S, "content_dim": C,
+                   "l2": "inputs larger than L2 (100 MB per prefill layer input)",
+                   "parallelism": f"dp{world} (sequences sharded, no collective)"},
+        "prefill": {"tok_s": round(world * B * T / (pre_ms / 1e3), 1), "ms": round(pre_ms, 3)},
+        "decode": {"tok_s": round(world * B * S / (dec_ms / 1e3), 1), "ms": round(dec_ms, 3)},
+        "roofline": roof,
+        "kernel_ms": {k: round(v[1] / args.steps, 3) for k, v in prof.items()},
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clk,
+        "e2e": e2e,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# CPU: the reference algorithm (oracle restatement) on the host cores
+# ---------------------------------------------------------------------------
+def cpu_sample(seconds_budget: float):
+    """Bounded sample of the workload on all host threads: rounds of one-layer
+    prefills of `nt` 1024-token sequences in parallel (one per thread) for
+    about half the budget, then decode steps of those sequences for about a
+    third of it.  Returns rates in token-layers/s."""
+    import numpy as np
+    from oracle import build as obuild
+    from oracle import oracle
+    import wave_engine_b200 as wb
+    obuild.build()
+    E, H, hd, C = CFG["n_embd"], CFG["n_head"], CFG["head_dim"], CFG["content_dim"]
+    T, extra = CFG["seq_len"], 64
+    nt = os.cpu_count() or 1
+    w = wb.gaussian_block_attn(1000, H, E, C).packed()
+    rng = np.random.default_rng(5)
+    xs = [rng.standard_normal((T + extra, E)).astype(np.float32) for _ in range(nt)]
+    states = [None] * nt
+
+    def pre(i):
+        _, states[i] = oracle.kv_prefill(w, xs[i][:T], cap=T + extra)
+
+    rounds = 0
+    t0 = time.perf_counter()
+    while True:
+        th = [threading.Thread(target=pre, args=(i,)) for i in range(nt)]
+        [t.start() for t in th]
+        [t.join() for t in th]
+        rounds += 1
+        if time.perf_counter() - t0 >= 0.5 * seconds_budget or rounds >= 16:
+            break
+    t_pre = time.perf_counter() - t0
+    counts = [0] * nt
+    t_end = time.perf_counter() + 0.3 * seconds_budget
+
+    def dec(i):
+        for s in range(extra):
+            oracle.kv_decode(w, xs[i][T + s], states[i])
+            counts[i] += 1
+            if time.perf_counter() >= t_end:
+                break
+
+    t0 = time.perf_counter()
+    th = [threading.Thread(target=dec, args=(i,)) for i in range(nt)]
+    [t.start() for t in th]
+    [t.join() for t in th]
+    t_dec = time.perf_counter() - t0
+    return {"nt": nt, "pre_rate": rounds * nt * T / t_pre, "dec_rate": sum(counts) / t_dec, "t_pre": t_pre,
+            "t_dec": t_dec, "n_pre": rounds * nt, "n_dec": sum(counts)}
+
+
+def cpu_value(r):
+    L, B, T, S = CFG["n_layers"], CFG["batch"], CFG["seq_len"], CFG["decode_steps"]
+    t = B * T * L / r["pre_rate"] + B * S * L / r["dec_rate"]
+    return (B * T + B * S) / t
+
+
+def cpu_desc(r):
+    return (f"1 layer of the 768-dim workload on {r['nt']} threads (one sequence each): kv prefill of "
+            f"{r['n_pre']} x 1024-token sequences ({r['t_pre']:.1f} s), then {r['n_dec']} single-position decode "
+            f"calls at ctx 1024-1088 ({r['t_dec']:.1f} s); extrapolated linearly to batch 32 x 24 layers and "
+            f"256 decode steps (decode at ctx ~1050 instead of 1024-1280)")
+
+
+def cpu_baseline(seconds):
+    r = cpu_sample(seconds)
+    return {"value": round(cpu_value(r), 3), "unit": "tok/s", "cores": r["nt"], "kind": "port",
+            "sample": cpu_desc(r)}
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    vals = []
+    for _ in range(args.warmup):
+        cpu_sample(args.cpu_seconds / 4)
+    last = None
+    for _ in range(args.steps):
+        last = cpu_sample(args.cpu_seconds / 4)
+        vals.append(cpu_value(last))
+    v = sorted(vals)[len(vals) // 2]
+    out = {"impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": "tok/s", "n_gpus": world,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+           "config": {"workload": WORKLOAD, "host_cpu": True},
+           "cpu_baseline": {"value": round(v, 3), "unit": "tok/s", "cores": last["nt"], "kind": "port",
+                            "sample": cpu_desc(last)},
+           "e2e": {"value": round(v, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(out), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--decode-steps", type=int, default=CFG["decode_steps"])
+    ap.add_argument("--roofline-kernel", default="decode_simt")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=2)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=20.0)
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        print("warning: fewer than 3 warm-up steps", file=sys.stderr)
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

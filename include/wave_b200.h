@@ -106,7 +106,10 @@ typedef struct {
 WB_API int wb_abi_version(void);
 /* Thread-local message for the last non-zero status on this thread. */
 WB_API const char *wb_last_error(void);
-/* Create a context on `device` (CUDA ordinal) using its own stream. */
+/* Create a context on `device` (CUDA ordinal) using its own stream.
+ * Layers and caches created on a context must be destroyed before it;
+ * their destroy functions stay safe to call after it (they only free
+ * device memory). */
 WB_API int wb_context_create(int device, wb_context **out);
 WB_API int wb_context_destroy(wb_context *ctx);
 /* Use an external cudaStream_t (NULL = the context's own stream). */
@@ -115,6 +118,16 @@ WB_API int wb_context_synchronize(wb_context *ctx);
 /* Device error word: non-zero when a bounded device-side wait gave up or a
  * kernel-side check failed since the last reset.  Resets it. */
 WB_API int wb_context_take_device_error(wb_context *ctx, uint32_t *code_out);
+
+/* Kernel timing: with name_filter non-NULL, every later compute call on this
+ * context brackets its named kernels whose name contains name_filter ("" =
+ * all) with CUDA events on the context's stream; NULL turns timing off.
+ * Replaces the reference's --monitor PROFILE timers (src/common/dims.rs:14,
+ * src/cpu/forward.rs:60) with device-side timing. */
+WB_API int wb_context_profile(wb_context *ctx, const char *name_filter);
+/* Synchronise, then write "kernel<TAB>launches<TAB>total_ms" lines for the
+ * launches recorded since the last report into buf (NUL-terminated). */
+WB_API int wb_context_profile_report(wb_context *ctx, char *buf, size_t len);
 
 /* ---- weights (attn.rs:19-46) ------------------------------------------ */
 WB_API int wb_attn_layer_create(wb_context *ctx, const wb_attn_weights_desc *w, wb_attn_layer **out);

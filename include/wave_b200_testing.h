@@ -20,6 +20,11 @@ extern "C" {
 WB_API int wb_test_gemm_bf16(wb_context *ctx, const uint16_t *A, const uint16_t *B, const float *bias,
                              float *C, int M, int N, int K);
 
+/* Same with fp32 A, B on the kind::tf32 path (wide layers' out_proj);
+ * K a multiple of 4. */
+WB_API int wb_test_gemm_tf32(wb_context *ctx, const float *A, const float *B, const float *bias, float *C, int M,
+                             int N, int K);
+
 #ifdef __cplusplus
 }
 #endif

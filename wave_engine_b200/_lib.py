@@ -36,6 +36,8 @@ SIGNATURES = {
     "wb_context_set_stream": (C.c_int, [_VP, _VP]),
     "wb_context_synchronize": (C.c_int, [_VP]),
     "wb_context_take_device_error": (C.c_int, [_VP, C.POINTER(C.c_uint32)]),
+    "wb_context_profile": (C.c_int, [_VP, C.c_char_p]),
+    "wb_context_profile_report": (C.c_int, [_VP, C.c_char_p, C.c_size_t]),
     "wb_attn_layer_create": (C.c_int, [_VP, _VP, C.POINTER(_VP)]),
     "wb_attn_layer_destroy": (C.c_int, [_VP]),
     "wb_init_block_attn": (C.c_int, [C.POINTER(C.c_uint64), C.c_int, C.c_int, C.c_int] + [_VP] * 9),
@@ -50,6 +52,7 @@ SIGNATURES = {
     "wb_kv_decode": (C.c_int, [_VP, _VP, C.c_int, _VP, _VP, C.c_int, _VP, C.c_int, _VP]),
     # include/wave_b200_testing.h
     "wb_test_gemm_bf16": (C.c_int, [_VP, _VP, _VP, _VP, _VP, C.c_int, C.c_int, C.c_int]),
+    "wb_test_gemm_tf32": (C.c_int, [_VP, _VP, _VP, _VP, _VP, C.c_int, C.c_int, C.c_int]),
 }
 
 

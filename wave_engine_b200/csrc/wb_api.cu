@@ -87,10 +87,19 @@ struct wb_context {
     DevBuf ws;    // per-call scratch
     DevBuf io;    // staging of host inputs/outputs
     uint32_t *dev_err = nullptr;
+    wb::Profiler *prof = nullptr;
+};
+
+// Makes ctx's profiler the calling thread's current one for one API call.
+struct ProfBind {
+    wb::Profiler *prev;
+    explicit ProfBind(wb_context *c) : prev(wb::prof_current()) { wb::prof_current() = c->prof; }
+    ~ProfBind() { wb::prof_current() = prev; }
 };
 
 struct wb_attn_layer {
     wb_context *ctx = nullptr;
+    int device = 0;  // destroy must not touch ctx (it may already be gone)
     int E = 0, H = 0, hd = 0, C = 0;
     std::vector<float> hn_host;  // softplus(harmonic_raw)
     float *harmonic_n = nullptr; // [H]
@@ -109,6 +118,7 @@ static wb::ProjWeights proj_weights(const wb_attn_layer *L) {
 
 struct wb_kv_cache {
     wb_context *ctx = nullptr;
+    int device = 0;  // destroy must not touch ctx (it may already be gone)
     int L = 0, H = 0, hd = 0, S = 0, cap = 0;
     float *theta = nullptr;
     uint8_t *bucket = nullptr;
@@ -173,6 +183,7 @@ int wb_context_destroy(wb_context *ctx) {
     if (ctx->io.p) cudaFree(ctx->io.p);
     if (ctx->dev_err) cudaFree(ctx->dev_err);
     if (ctx->own) cudaStreamDestroy(ctx->own);
+    wb::prof_destroy(ctx->prof);
     delete ctx;
     return WB_OK;
 }
@@ -201,6 +212,29 @@ int wb_context_take_device_error(wb_context *ctx, uint32_t *code_out) {
     return WB_OK;
 }
 
+int wb_context_profile(wb_context *ctx, const char *name_filter) {
+    if (!ctx) return fail(WB_EINVAL, "ctx is NULL");
+    DeviceGuard g(ctx->device);
+    if (ctx->prof) {
+        cudaStreamSynchronize(ctx->stream);
+        wb::prof_destroy(ctx->prof);
+        ctx->prof = nullptr;
+    }
+    if (name_filter) ctx->prof = wb::prof_create(name_filter);
+    return WB_OK;
+}
+
+int wb_context_profile_report(wb_context *ctx, char *buf, size_t len) {
+    if (!ctx || !buf || len == 0) return fail(WB_EINVAL, "NULL argument");
+    if (!ctx->prof) return fail(WB_EINVAL, "profiling is off (wb_context_profile)");
+    DeviceGuard g(ctx->device);
+    WB_CUDA(cudaStreamSynchronize(ctx->stream));
+    std::string r = wb::prof_report(ctx->prof);
+    if (r.size() + 1 > len) return fail(WB_EINVAL, "report buffer too small");
+    memcpy(buf, r.c_str(), r.size() + 1);
+    return WB_OK;
+}
+
 // ---------------------------------------------------------------------------
 // weights
 // ---------------------------------------------------------------------------
@@ -218,6 +252,7 @@ int wb_attn_layer_create(wb_context *ctx, const wb_attn_weights_desc *w, wb_attn
     DeviceGuard g(ctx->device);
     wb_attn_layer *L = new wb_attn_layer();
     L->ctx = ctx;
+    L->device = ctx->device;
     L->E = E; L->H = H; L->hd = hd; L->C = C;
     L->hn_host.resize(H);
     for (int h = 0; h < H; h++) L->hn_host[h] = wb::softplus_ref(w->harmonic_raw[h]);
@@ -279,7 +314,7 @@ int wb_attn_layer_create(wb_context *ctx, const wb_attn_weights_desc *w, wb_attn
 
 int wb_attn_layer_destroy(wb_attn_layer *L) {
     if (!L) return WB_OK;
-    DeviceGuard g(L->ctx->device);
+    DeviceGuard g(L->device);
     float *ptrs[] = {L->harmonic_n, L->wrs_t, L->brs, L->wc_t, L->bc, L->wv_t, L->bv, L->wo_t, L->bo};
     for (float *p : ptrs)
         if (p) cudaFree(p);
@@ -348,6 +383,7 @@ int wb_attn_forward(wb_context *ctx, const wb_attn_layer *L, const float *x, int
     const long long R = (long long)B * T;
     if (R > (1LL << 30)) return fail(WB_EINVAL, "batch*seq_len too large");
     DeviceGuard g(ctx->device);
+    ProfBind pb(ctx);
     cudaStream_t st = ctx->stream;
     const int E = L->E, H = L->H, hd = L->hd;
     const bool use_content = L->C > 0 && !(flags & WB_NO_CONTENT);
@@ -431,6 +467,7 @@ int wb_kv_cache_create(wb_context *ctx, int n_layers, int n_head, int head_dim, 
     DeviceGuard g(ctx->device);
     wb_kv_cache *c = new wb_kv_cache();
     c->ctx = ctx;
+    c->device = ctx->device;
     c->L = n_layers; c->H = n_head; c->hd = head_dim; c->S = max_seqs; c->cap = max_ctx;
     const size_t n = (size_t)n_layers * max_seqs * n_head * max_ctx;
     if (cudaMalloc(&c->theta, n * sizeof(float)) != cudaSuccess ||
@@ -453,8 +490,7 @@ int wb_kv_cache_create(wb_context *ctx, int n_layers, int n_head, int head_dim, 
 
 int wb_kv_cache_destroy(wb_kv_cache *c) {
     if (!c) return WB_OK;
-    DeviceGuard g(c->ctx->device);
-    cudaStreamSynchronize(c->ctx->stream);
+    DeviceGuard g(c->device);  // cudaFree below waits for work using the buffers
     if (c->theta) cudaFree(c->theta);
     if (c->bucket) cudaFree(c->bucket);
     if (c->v) cudaFree(c->v);
@@ -473,7 +509,7 @@ int wb_kv_cache_length(wb_kv_cache *c, int layer, int seq, int *len_out) {
 int wb_kv_cache_reset_seq(wb_kv_cache *c, int seq) {
     if (!c) return fail(WB_EINVAL, "NULL argument");
     if (seq < 0 || seq >= c->S) return fail(WB_EINVAL, "seq out of range");
-    DeviceGuard g(c->ctx->device);
+    DeviceGuard g(c->device);
     for (int l = 0; l < c->L; l++) {
         c->len_host[(size_t)l * c->S + seq] = 0;
         WB_CUDA(cudaMemsetAsync(c->len + (size_t)l * c->S + seq, 0, sizeof(int32_t), c->ctx->stream));
@@ -546,6 +582,7 @@ int wb_kv_prefill(wb_context *ctx, wb_kv_cache *c, int layer_idx, const wb_attn_
     if (n_seq == 0 || T == 0) return WB_OK;
     if (T > c->cap) return fail(WB_EINVAL, "seq_len exceeds cache capacity");
     DeviceGuard g(ctx->device);
+    ProfBind pb(ctx);
     std::vector<int32_t> ids;
     WB_TRY(copy_seq_ids(ctx, seq_ids, n_seq, ids));
     for (int i = 0; i < n_seq; i++) {
@@ -609,6 +646,7 @@ int wb_kv_decode(wb_context *ctx, wb_kv_cache *c, int layer_idx, const wb_attn_l
     if (n_seq < 0) return fail(WB_EINVAL, "negative n_seq");
     if (n_seq == 0) return WB_OK;
     DeviceGuard g(ctx->device);
+    ProfBind pb(ctx);
     std::vector<int32_t> ids;
     WB_TRY(copy_seq_ids(ctx, seq_ids, n_seq, ids));
     for (int i = 0; i < n_seq; i++) {
@@ -677,6 +715,15 @@ int wb_test_gemm_bf16(wb_context *ctx, const uint16_t *A, const uint16_t *B, con
     std::string msg;
     int rc = wb::tc_gemm_bf16((const __nv_bfloat16 *)A, (const __nv_bfloat16 *)B, bias, C, M, N, K, ctx->dev_err,
                               ctx->stream, &msg);
+    return rc == WB_OK ? rc : fail(rc, msg);
+}
+
+int wb_test_gemm_tf32(wb_context *ctx, const float *A, const float *B, const float *bias, float *C, int M, int N,
+                      int K) {
+    if (!ctx || !A || !B || !bias || !C) return fail(WB_EINVAL, "NULL argument");
+    DeviceGuard g(ctx->device);
+    std::string msg;
+    int rc = wb::tc_gemm_tf32(A, B, bias, C, M, N, K, ctx->dev_err, ctx->stream, &msg);
     return rc == WB_OK ? rc : fail(rc, msg);
 }
 

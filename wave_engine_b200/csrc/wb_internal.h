@@ -41,6 +41,23 @@ struct Carve {
     }
 };
 
+// ---- kernel timing (wb_context_profile) ---------------------------------
+// When a profiler is active on the calling thread, prof_begin/prof_end
+// bracket a named kernel launch with CUDA events on its stream.
+struct Profiler;
+Profiler *&prof_current();
+void prof_begin(const char *name, cudaStream_t st);
+void prof_end(cudaStream_t st);
+Profiler *prof_create(const char *filter);
+void prof_destroy(Profiler *p);
+std::string prof_report(Profiler *p);
+// RAII bracket used at launch sites.
+struct ProfScope {
+    cudaStream_t st;
+    ProfScope(const char *name, cudaStream_t s) : st(s) { prof_begin(name, s); }
+    ~ProfScope() { prof_end(st); }
+};
+
 enum { OUT_DENSE = 0, OUT_SEQ_V = 1 };
 struct OutMap {
     int mode;
@@ -64,6 +81,9 @@ struct ProjWeights {
 // content [R][H*C] when non-null.
 void launch_projections_exact(const ProjWeights &w, const float *x, int B, int T, const WbSeqView &sv, float *rs,
                               float *content, cudaStream_t st);
+void launch_attn_simt_fallback_f32(const WbSeqView &sv, const float *content, int C, float content_scale,
+                                   const float *harmonic_n, int B, int H, int T, int hd, float *o,
+                                   const int *tile_flags, cudaStream_t st);
 void launch_attn_simt_fallback_bf16(const WbSeqView &sv, const float *content, int C, float content_scale,
                                     const float *harmonic_n, int B, int H, int T, int hd, __nv_bfloat16 *o,
                                     const int *tile_flags, cudaStream_t st);

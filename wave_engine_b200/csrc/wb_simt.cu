@@ -60,6 +60,7 @@ __global__ void __launch_bounds__(256) seqdot_kernel(const float *__restrict__ X
 void launch_seqdot(const float *X, int R, int K, long long ldx, const float *Wt, int N,
                    const float *bias, int bias_first, const OutMap &om, cudaStream_t st) {
     if (R <= 0 || N <= 0) return;
+    ProfScope ps("proj_seqdot", st);
     const size_t smem32 = (size_t)32 * K * sizeof(float);
     if (smem32 <= 160 * 1024 && R >= 64) {
         cudaFuncSetAttribute(seqdot_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem32);
@@ -90,6 +91,7 @@ __global__ void phase_kernel(const float *__restrict__ rs, int R, int H, int T, 
 void launch_phase(const float *rs, int R, int H, int T, const WbSeqView &sv, cudaStream_t st) {
     const int n = R * H;
     if (n <= 0) return;
+    ProfScope ps("phase", st);
     phase_kernel<<<(n + 255) / 256, 256, 0, st>>>(rs, R, H, T, sv);
 }
 
@@ -200,6 +202,7 @@ __global__ void __launch_bounds__(256) attn_simt_kernel(AttnSimtArgs a) {
 
 template <class OutT>
 static void launch_attn_simt_t(const AttnSimtArgs &a, cudaStream_t st) {
+    ProfScope ps(a.tile_flags ? "attn_simt_fallback" : "attn_simt", st);
     dim3 grid((a.T + 7) / 8, a.H, a.B);
     if (a.hd <= 32) attn_simt_kernel<1, OutT><<<grid, 256, 0, st>>>(a);
     else if (a.hd <= 64) attn_simt_kernel<2, OutT><<<grid, 256, 0, st>>>(a);
@@ -219,6 +222,13 @@ void launch_attn_simt_fallback_bf16(const WbSeqView &sv, const float *content, i
                                     const int *tile_flags, cudaStream_t st) {
     AttnSimtArgs a{sv, content, C, content_scale, harmonic_n, B, H, T, hd, o, nullptr, tile_flags};
     launch_attn_simt_t<__nv_bfloat16>(a, st);
+}
+
+void launch_attn_simt_fallback_f32(const WbSeqView &sv, const float *content, int C, float content_scale,
+                                   const float *harmonic_n, int B, int H, int T, int hd, float *o,
+                                   const int *tile_flags, cudaStream_t st) {
+    AttnSimtArgs a{sv, content, C, content_scale, harmonic_n, B, H, T, hd, o, nullptr, tile_flags};
+    launch_attn_simt_t<float>(a, st);
 }
 
 void launch_projections_exact(const ProjWeights &w, const float *x, int B, int T, const WbSeqView &sv, float *rs,
@@ -333,6 +343,7 @@ void launch_decode_simt(const WbSeqView &sv, const int32_t *len, const float *th
                         float *o, cudaStream_t st) {
     DecodeSimtArgs a{sv, len, theta_new, v_new, harmonic_n, n_seq, H, hd, o};
     dim3 grid((H + 3) / 4, n_seq);
+    ProfScope ps("decode_simt", st);
     if (hd <= 32) decode_simt_kernel<1><<<grid, 128, 0, st>>>(a);
     else if (hd <= 64) decode_simt_kernel<2><<<grid, 128, 0, st>>>(a);
     else if (hd <= 128) decode_simt_kernel<4><<<grid, 128, 0, st>>>(a);

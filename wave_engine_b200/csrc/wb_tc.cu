@@ -14,6 +14,14 @@
 //                key's score is pushed to about -512 and its exp is 0.
 //   cols 30..31  zero
 //
+// Split precision (the default, "wide" in the code): 64 feature columns
+// with the content as a bf16 hi/lo split as well (cols 6..53, bucket mask at
+// 54..61), values as a bf16 hi/lo pair (two PV MMAs), an fp32 merged output
+// and a tf32 out_proj.  Single bf16 features/values/output (32 columns, the
+// layout above) keep ~3x less headroom: with the reference's own uniform
+// init (src/common/wave_model.rs:39-46) they exceed a 2e-3 max-abs error at
+// every model size, so that mode is only selectable for experiments.
+//
 // Softmax needs no running max: every score is bounded by
 // 1 + |c_q| max_k|c_k| / 4 and the self score 1 + |c_q|^2/4 is always
 // present, so exp(s - s_self) neither overflows nor loses the row as long
@@ -33,7 +41,6 @@ namespace wb {
 
 static constexpr int QT = 128;      // queries per CTA (TMEM lanes)
 static constexpr int KT = 128;      // keys per tile
-static constexpr int FEAT = 32;     // feature width of Qf / Kf
 static constexpr float MASK_BIAS = -512.0f;
 static constexpr float BOUND_LIMIT = 64.0f;
 
@@ -81,7 +88,8 @@ struct FeatArgs {
     float cscale;
     const float *hn;
     int B, H, T, hd, hdp;
-    __nv_bfloat16 *qf, *kf, *vb;  // [BH][T][32], [BH][T][32], [BH][T][hdp]
+    __nv_bfloat16 *qf, *kf;       // [BH][T][FW]
+    __nv_bfloat16 *vh, *vl;       // [BH][T][hdp] value hi / lo (lo only in wide mode)
     float *m0, *sprev, *cnorm;    // [BH][T]
     unsigned int *cmax;           // [BH], float bits
 };
@@ -90,8 +98,12 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
     __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
     return *reinterpret_cast<uint32_t *>(&v);
 }
+__device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
+template <bool WIDE>
 __global__ void __launch_bounds__(256) feat_kernel(FeatArgs a) {
+    constexpr int FW = WIDE ? 64 : 32;        // feature width
+    constexpr int BB = WIDE ? 54 : 22;        // first bucket column
     const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
     const long long BH = (long long)a.B * a.H;
     if (i >= BH * a.T) return;
@@ -103,8 +115,7 @@ __global__ void __launch_bounds__(256) feat_kernel(FeatArgs a) {
     const float n = a.hn[h];
     float sn, cs;
     sincosf(n * th, &sn, &cs);
-    const float csh = __bfloat162float(__float2bfloat16_rn(cs));
-    const float snh = __bfloat162float(__float2bfloat16_rn(sn));
+    const float csh = bf16_round(cs), snh = bf16_round(sn);
     const float csl = cs - csh, snl = sn - snh;
     float c[16];
     float c2 = 0.0f;
@@ -114,44 +125,54 @@ __global__ void __launch_bounds__(256) feat_kernel(FeatArgs a) {
         c[d] = (d < C) ? a.content[((long long)b * a.T + t) * ((long long)a.H * C) + (long long)h * C + d] : 0.0f;
         c2 = fmaf(c[d], c[d], c2);
     }
-    uint32_t q[16], k[16];
-    q[0] = pack_bf16(csh, csl);
-    q[1] = pack_bf16(csh, snh);
-    q[2] = pack_bf16(snl, snh);
-    k[0] = pack_bf16(csh, csh);
-    k[1] = pack_bf16(csl, snh);
-    k[2] = pack_bf16(snh, snl);
+    float qv[FW], kv[FW];
 #pragma unroll
-    for (int d = 0; d < 8; d++) {
-        q[3 + d] = pack_bf16(c[2 * d] * a.cscale, c[2 * d + 1] * a.cscale);
-        k[3 + d] = pack_bf16(c[2 * d], c[2 * d + 1]);
+    for (int u = 0; u < FW; u++) qv[u] = kv[u] = 0.0f;
+    qv[0] = csh; qv[1] = csl; qv[2] = csh; qv[3] = snh; qv[4] = snl; qv[5] = snh;
+    kv[0] = csh; kv[1] = csh; kv[2] = csl; kv[3] = snh; kv[4] = snh; kv[5] = snl;
+#pragma unroll
+    for (int d = 0; d < 16; d++) {
+        const float cq = c[d] * a.cscale;
+        if (WIDE) {
+            const float qh = bf16_round(cq), kh = bf16_round(c[d]);
+            qv[6 + 3 * d] = qh; qv[7 + 3 * d] = cq - qh; qv[8 + 3 * d] = qh;
+            kv[6 + 3 * d] = kh; kv[7 + 3 * d] = kh; kv[8 + 3 * d] = c[d] - kh;
+        } else {
+            qv[6 + d] = cq;
+            kv[6 + d] = c[d];
+        }
     }
     const uint32_t allow = allowed_bucket_mask(bk);
 #pragma unroll
-    for (int d = 0; d < 4; d++) {
-        const int b0 = 2 * d, b1 = 2 * d + 1;
-        q[11 + d] = pack_bf16((allow >> b0) & 1u ? 0.0f : MASK_BIAS, (allow >> b1) & 1u ? 0.0f : MASK_BIAS);
-        k[11 + d] = pack_bf16(bk == b0 ? 1.0f : 0.0f, bk == b1 ? 1.0f : 0.0f);
+    for (int u = 0; u < 8; u++) {
+        qv[BB + u] = ((allow >> u) & 1u) ? 0.0f : MASK_BIAS;
+        kv[BB + u] = (bk == u) ? 1.0f : 0.0f;
     }
-    q[15] = k[15] = 0u;
-    uint4 *qd = reinterpret_cast<uint4 *>(a.qf + i * FEAT);
-    uint4 *kd = reinterpret_cast<uint4 *>(a.kf + i * FEAT);
+    uint4 *qd = reinterpret_cast<uint4 *>(a.qf + i * FW);
+    uint4 *kd = reinterpret_cast<uint4 *>(a.kf + i * FW);
 #pragma unroll
-    for (int u = 0; u < 4; u++) {
-        qd[u] = make_uint4(q[4 * u], q[4 * u + 1], q[4 * u + 2], q[4 * u + 3]);
-        kd[u] = make_uint4(k[4 * u], k[4 * u + 1], k[4 * u + 2], k[4 * u + 3]);
+    for (int u = 0; u < FW / 8; u++) {
+        qd[u] = make_uint4(pack_bf16(qv[8 * u], qv[8 * u + 1]), pack_bf16(qv[8 * u + 2], qv[8 * u + 3]),
+                           pack_bf16(qv[8 * u + 4], qv[8 * u + 5]), pack_bf16(qv[8 * u + 6], qv[8 * u + 7]));
+        kd[u] = make_uint4(pack_bf16(kv[8 * u], kv[8 * u + 1]), pack_bf16(kv[8 * u + 2], kv[8 * u + 3]),
+                           pack_bf16(kv[8 * u + 4], kv[8 * u + 5]), pack_bf16(kv[8 * u + 6], kv[8 * u + 7]));
     }
-    // values, zero padded to hdp
+    // values (hi, and lo in wide mode), zero padded to hdp
     const float *vrow = a.sv.v + (base + t) * a.hd;
-    __nv_bfloat16 *vd = a.vb + i * a.hdp;
+    __nv_bfloat16 *vdh = a.vh + i * a.hdp;
+    __nv_bfloat16 *vdl = WIDE ? a.vl + i * a.hdp : nullptr;
     for (int d = 0; d < a.hdp; d += 8) {
-        uint32_t w[4];
+        float v[8], vlo[8];
 #pragma unroll
-        for (int u = 0; u < 4; u++) {
-            const int d0 = d + 2 * u, d1 = d0 + 1;
-            w[u] = pack_bf16(d0 < a.hd ? vrow[d0] : 0.0f, d1 < a.hd ? vrow[d1] : 0.0f);
+        for (int u = 0; u < 8; u++) {
+            v[u] = (d + u < a.hd) ? vrow[d + u] : 0.0f;
+            vlo[u] = v[u] - bf16_round(v[u]);
         }
-        *reinterpret_cast<uint4 *>(vd + d) = make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4 *>(vdh + d) = make_uint4(pack_bf16(v[0], v[1]), pack_bf16(v[2], v[3]),
+                                                         pack_bf16(v[4], v[5]), pack_bf16(v[6], v[7]));
+        if (WIDE)
+            *reinterpret_cast<uint4 *>(vdl + d) = make_uint4(pack_bf16(vlo[0], vlo[1]), pack_bf16(vlo[2], vlo[3]),
+                                                             pack_bf16(vlo[4], vlo[5]), pack_bf16(vlo[6], vlo[7]));
     }
     // self score, previous-position term, content norm
     const float self = 1.0f + c2 * a.cscale;
@@ -189,7 +210,7 @@ struct AttnTcArgs {
     const float *m0, *sprev, *cnorm;
     const unsigned int *cmax;
     WbSeqView sv;               // fp32 values for the previous-position term
-    __nv_bfloat16 *o;           // [B*T][E]
+    void *o;                    // [B*T][E], bf16 (narrow) or fp32 (wide)
     int E;
     int *tile_flags;            // [BH][n_qt]
     uint32_t *dev_err;
@@ -201,11 +222,13 @@ __device__ __forceinline__ float fast_exp2(float x) {
     return y;
 }
 
-template <int HDP>
+template <int HDP, bool WIDE>
 struct AttnSmem {
-    static constexpr int Q_BYTES = QT * FEAT * 2;   // 8 KB
-    static constexpr int K_BYTES = KT * FEAT * 2;   // 8 KB
-    static constexpr int V_BYTES = KT * HDP * 2;    // 16 / 32 KB
+    static constexpr int FW = WIDE ? 64 : 32;        // feature width
+    static constexpr int Q_BYTES = QT * FW * 2;      // 8 / 16 KB
+    static constexpr int K_BYTES = KT * FW * 2;      // 8 / 16 KB
+    static constexpr int VPART = KT * HDP * 2;       // one bf16 value tile: 16 / 32 KB
+    static constexpr int V_BYTES = VPART * (WIDE ? 2 : 1);  // hi (+ lo)
     static constexpr int P_BYTES = QT * KT * 2;     // 32 KB
     static constexpr int OFF_Q = 0;
     static constexpr int OFF_K = OFF_Q + Q_BYTES;
@@ -215,11 +238,12 @@ struct AttnSmem {
     static constexpr int BYTES = OFF_BAR + 128 + 1024;  // barriers + alignment slack
 };
 
-template <int HDP>
+template <int HDP, bool WIDE>
 __global__ void __launch_bounds__(128, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                   const __grid_constant__ CUtensorMap tm_v, AttnTcArgs a, int hdn) {
-    using L = AttnSmem<HDP>;
+                   const __grid_constant__ CUtensorMap tm_vh, const __grid_constant__ CUtensorMap tm_vl,
+                   AttnTcArgs a, int hdn) {
+    using L = AttnSmem<HDP, WIDE>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *bars = reinterpret_cast<uint64_t *>(sm + L::OFF_BAR);
@@ -278,15 +302,23 @@ __global__ void __launch_bounds__(128, 1)
         ptx::mbar_arrive_expect_tx(full + s, STAGE_TX);
         ptx::tma_load_3d(sm + L::OFF_K + s * L::K_BYTES, &tm_k, full + s, 0, j * KT, bh);
 #pragma unroll
-        for (int c = 0; c < HDP / 64; c++)
-            ptx::tma_load_3d(sm + L::OFF_V + s * L::V_BYTES + c * (KT * 128), &tm_v, full + s, c * 64, j * KT, bh);
+        for (int c = 0; c < HDP / 64; c++) {
+            ptx::tma_load_3d(sm + L::OFF_V + s * L::V_BYTES + c * (KT * 128), &tm_vh, full + s, c * 64, j * KT, bh);
+            if (WIDE)
+                ptx::tma_load_3d(sm + L::OFF_V + s * L::V_BYTES + L::VPART + c * (KT * 128), &tm_vl, full + s,
+                                 c * 64, j * KT, bh);
+        }
     };
+    // Feature rows are 64 B (SW64, 8-row groups of 512 B) or 128 B (SW128,
+    // 1024 B groups); each MMA consumes 16 features = 32 B of the row.
+    constexpr uint32_t F_SW = WIDE ? ptx::UMMA_SW128 : ptx::UMMA_SW64;
+    constexpr uint32_t F_SBO = WIDE ? 1024 : 512;
     auto issue_qk = [&](int j) {
         const uint32_t sK = sK0 + (j & 1) * L::K_BYTES;
 #pragma unroll
-        for (int kk = 0; kk < FEAT / 16; kk++) {
-            const uint64_t ad = ptx::smem_desc(sQ + kk * 32, 16, 512, ptx::UMMA_SW64);
-            const uint64_t bd = ptx::smem_desc(sK + kk * 32, 16, 512, ptx::UMMA_SW64);
+        for (int kk = 0; kk < L::FW / 16; kk++) {
+            const uint64_t ad = ptx::smem_desc(sQ + kk * 32, 16, F_SBO, F_SW);
+            const uint64_t bd = ptx::smem_desc(sK + kk * 32, 16, F_SBO, F_SW);
             ptx::mma_bf16(S_t, ad, bd, IDESC_QK, kk > 0);
         }
         ptx::mma_commit(sbar);
@@ -295,7 +327,8 @@ __global__ void __launch_bounds__(128, 1)
     if (tid == 0) {
         ptx::prefetch_tmap(&tm_q);
         ptx::prefetch_tmap(&tm_k);
-        ptx::prefetch_tmap(&tm_v);
+        ptx::prefetch_tmap(&tm_vh);
+        if (WIDE) ptx::prefetch_tmap(&tm_vl);
         ptx::mbar_arrive_expect_tx(qbar, L::Q_BYTES);
         ptx::tma_load_3d(sm + L::OFF_Q, &tm_q, qbar, 0, q0, bh);
         load_tile(0);
@@ -358,6 +391,10 @@ __global__ void __launch_bounds__(128, 1)
                                                    ptx::UMMA_SW128);
                 const uint64_t bd = ptx::smem_desc(sV + kk * 2048, KT * 128, 1024, ptx::UMMA_SW128);
                 ptx::mma_bf16(O_t, ad, bd, idesc_pv, (j > 0 || kk > 0));
+                if (WIDE) {
+                    const uint64_t bl = ptx::smem_desc(sV + L::VPART + kk * 2048, KT * 128, 1024, ptx::UMMA_SW128);
+                    ptx::mma_bf16(O_t, ad, bl, idesc_pv, 1);
+                }
             }
             ptx::mma_commit(empty + (j & 1));
             if (j + 1 < n_kt) {
@@ -408,10 +445,18 @@ __global__ void __launch_bounds__(128, 1)
                     if (d < a.hd) o[d] = fmaf(e, vp[d], o[d]);
             }
             const float inv = 1.0f / l;
-            __nv_bfloat16 *dst = a.o + ((long long)b * a.T + q) * a.E + (long long)h * a.hd;
+            const long long off = ((long long)b * a.T + q) * a.E + (long long)h * a.hd;
+            if (WIDE) {
+                float *dst = (float *)a.o + off;
 #pragma unroll
-            for (int d = 0; d < HDP; d++)
-                if (d < a.hd) dst[d] = __float2bfloat16_rn(o[d] * inv);
+                for (int d = 0; d < HDP; d++)
+                    if (d < a.hd) dst[d] = o[d] * inv;
+            } else {
+                __nv_bfloat16 *dst = (__nv_bfloat16 *)a.o + off;
+#pragma unroll
+                for (int d = 0; d < HDP; d++)
+                    if (d < a.hd) dst[d] = __float2bfloat16_rn(o[d] * inv);
+            }
         }
     }
     ptx::tc_fence_before();
@@ -425,14 +470,19 @@ __global__ void __launch_bounds__(128, 1)
 // ring; warp 0 lane 0 loads, warp 1 lane 0 issues tcgen05.mma; all four
 // warps run the epilogue from TMEM.
 // ---------------------------------------------------------------------------
-static constexpr int GBM = 128, GBN = 128, GBK = 64, GST = 3;
-static constexpr int G_STAGE = (GBM + GBN) * GBK * 2;  // 32 KB
+// TF32 = true: A and B are fp32 in memory and the MMA is kind::tf32 (K = 8
+// per instruction); the 128-byte K block then holds 32 elements instead of 64.
+static constexpr int GBM = 128, GBN = 128, GST = 3;
+static constexpr int G_ROW = 128;                       // bytes of one K block row
+static constexpr int G_STAGE = (GBM + GBN) * G_ROW;     // 32 KB
 static constexpr int G_SMEM = GST * G_STAGE + 128 + 1024;
 
+template <bool TF32>
 __global__ void __launch_bounds__(128, 1)
-    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
-                     const float *__restrict__ bias, float *__restrict__ C, int M, int N, int K, long long ldc,
-                     uint32_t *dev_err) {
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                   const float *__restrict__ bias, float *__restrict__ C, int M, int N, int K, long long ldc,
+                   uint32_t *dev_err) {
+    constexpr int GBK = TF32 ? 32 : 64;  // elements per K block
     extern __shared__ uint8_t smem_raw[];
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *bars = reinterpret_cast<uint64_t *>(sm + GST * G_STAGE);
@@ -467,10 +517,10 @@ __global__ void __launch_bounds__(128, 1)
             uint8_t *st = sm + s * G_STAGE;
             ptx::mbar_arrive_expect_tx(full + s, G_STAGE);
             ptx::tma_load_2d(st, &tm_a, full + s, kb * GBK, m0);
-            ptx::tma_load_2d(st + GBM * GBK * 2, &tm_b, full + s, kb * GBK, n0);
+            ptx::tma_load_2d(st + GBM * G_ROW, &tm_b, full + s, kb * GBK, n0);
         }
     } else if (tid == 32) {
-        constexpr uint32_t IDESC = ptx::idesc_bf16(GBM, GBN, 0, 0);
+        constexpr uint32_t IDESC = TF32 ? ptx::idesc_tf32(GBM, GBN) : ptx::idesc_bf16(GBM, GBN, 0, 0);
         for (int kb = 0; kb < nk; kb++) {
             const int s = kb % GST;
             if (!ptx::mbar_wait(full + s, (kb / GST) & 1)) {
@@ -479,11 +529,16 @@ __global__ void __launch_bounds__(128, 1)
                 break;
             }
             ptx::tc_fence_after();
-            const uint32_t sa = ptx::smem_u32(sm + s * G_STAGE), sb = sa + GBM * GBK * 2;
+            const uint32_t sa = ptx::smem_u32(sm + s * G_STAGE), sb = sa + GBM * G_ROW;
 #pragma unroll
-            for (int k = 0; k < GBK / 16; k++)
-                ptx::mma_bf16(tmem, ptx::smem_desc(sa + k * 32, 16, 1024, ptx::UMMA_SW128),
-                              ptx::smem_desc(sb + k * 32, 16, 1024, ptx::UMMA_SW128), IDESC, (kb > 0 || k > 0));
+            for (int k = 0; k < 4; k++) {  // 32 bytes of K per instruction
+                const uint64_t ad = ptx::smem_desc(sa + k * 32, 16, 1024, ptx::UMMA_SW128);
+                const uint64_t bd = ptx::smem_desc(sb + k * 32, 16, 1024, ptx::UMMA_SW128);
+                if (TF32)
+                    ptx::mma_tf32(tmem, ad, bd, IDESC, (kb > 0 || k > 0));
+                else
+                    ptx::mma_bf16(tmem, ad, bd, IDESC, (kb > 0 || k > 0));
+            }
             ptx::mma_commit(empty + s);
         }
         ptx::mma_commit(done);
@@ -527,7 +582,19 @@ int tc_layer_upload(TcLayerWeights *t, const wb_attn_weights_desc *w, std::strin
     t->H = w->n_head;
     t->hd = w->n_embd / w->n_head;
     t->C = w->content_dim;
+    t->wide = true;
     const size_t n = (size_t)t->E * t->E;
+    if (t->wide) {
+        if (cudaMalloc(&t->w_o32, n * sizeof(float)) != cudaSuccess) {
+            cudaGetLastError();
+            *msg = "cudaMalloc for fp32 out_proj failed";
+            return WB_ENOMEM;
+        }
+        if (cudaMemcpy(t->w_o32, w->out_proj_w, n * sizeof(float), cudaMemcpyHostToDevice) != cudaSuccess) {
+            *msg = "upload of out_proj failed";
+            return WB_ECUDA;
+        }
+    }
     float *tmp = nullptr;
     if (cudaMalloc(&t->w_o, n * sizeof(__nv_bfloat16)) != cudaSuccess || cudaMalloc(&tmp, n * sizeof(float)) != cudaSuccess) {
         cudaGetLastError();
@@ -552,31 +619,81 @@ int tc_layer_upload(TcLayerWeights *t, const wb_attn_weights_desc *w, std::strin
 
 void tc_layer_free(TcLayerWeights *t) {
     if (t->w_o) cudaFree(t->w_o);
+    if (t->w_o32) cudaFree(t->w_o32);
     t->w_o = nullptr;
+    t->w_o32 = nullptr;
 }
 
 // Workspace pieces of the attention core, carved after `off`.
 struct CoreLayout {
-    size_t qf, kf, vb, m0, sp, cn, cm, fl, o, end;
+    size_t qf, kf, vh, vl, m0, sp, cn, cm, fl, o, end;
 };
 static CoreLayout core_layout(const TcLayerWeights &t, int B, int T, size_t off) {
     const int hdp = t.hd <= 64 ? 64 : 128;
+    const int fw = t.wide ? 64 : 32;
     const long long BH = (long long)B * t.H, R = (long long)B * T;
     const int n_qt = (T + QT - 1) / QT;
     Carve cv;
     cv.off = off;
     CoreLayout c;
-    c.qf = cv.take<__nv_bfloat16>(BH * T * FEAT);
-    c.kf = cv.take<__nv_bfloat16>(BH * T * FEAT);
-    c.vb = cv.take<__nv_bfloat16>(BH * T * hdp);
+    c.qf = cv.take<__nv_bfloat16>(BH * T * fw);
+    c.kf = cv.take<__nv_bfloat16>(BH * T * fw);
+    c.vh = cv.take<__nv_bfloat16>(BH * T * hdp);
+    c.vl = cv.take<__nv_bfloat16>(t.wide ? BH * T * hdp : 1);
     c.m0 = cv.take<float>(BH * T);
     c.sp = cv.take<float>(BH * T);
     c.cn = cv.take<float>(BH * T);
     c.cm = cv.take<unsigned int>(BH);
     c.fl = cv.take<int>(BH * n_qt);
-    c.o = cv.take<__nv_bfloat16>(R * t.E);
+    c.o = t.wide ? cv.take<float>(R * t.E) : cv.take<__nv_bfloat16>(R * t.E);
     c.end = cv.off;
     return c;
+}
+
+// y = A W^T + bias on the tcgen05 GEMM: A [M][K] and W [N][K] bf16 (tf32 =
+// false) or fp32 (tf32 = true), K-major; C [M][ldc] fp32.
+static int launch_gemm(bool tf32, const void *A, const void *W, const float *bias, float *C, int M, int N, int K,
+                       long long ldc, uint32_t *dev_err, cudaStream_t st, std::string *msg) {
+    const int esz = tf32 ? 4 : 2;
+    if (M <= 0 || N <= 0 || K <= 0 || ((long long)K * esz) % 16) {
+        *msg = "bad GEMM shape (rows of A and W must be multiples of 16 bytes)";
+        return WB_EINVAL;
+    }
+    const CUtensorMapDataType dt = tf32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    const uint32_t bk = G_ROW / esz;
+    CUtensorMap ta, tb;
+    int rc;
+    const uint64_t adims[2] = {(uint64_t)K, (uint64_t)M};
+    const uint64_t str[1] = {(uint64_t)K * esz};
+    const uint32_t abox[2] = {bk, GBM};
+    if ((rc = make_tmap(&ta, A, dt, 2, adims, str, abox, CU_TENSOR_MAP_SWIZZLE_128B, msg))) return rc;
+    const uint64_t bdims[2] = {(uint64_t)K, (uint64_t)N};
+    const uint32_t bbox[2] = {bk, GBN};
+    if ((rc = make_tmap(&tb, W, dt, 2, bdims, str, bbox, CU_TENSOR_MAP_SWIZZLE_128B, msg))) return rc;
+    dim3 gg((unsigned)((M + GBM - 1) / GBM), (unsigned)((N + GBN - 1) / GBN));
+    ProfScope ps(tf32 ? "gemm_tf32" : "gemm_bf16", st);
+    if (tf32) {
+        cudaFuncSetAttribute(gemm_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, G_SMEM);
+        gemm_tc_kernel<true><<<gg, 128, G_SMEM, st>>>(ta, tb, bias, C, M, N, K, ldc, dev_err);
+    } else {
+        cudaFuncSetAttribute(gemm_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, G_SMEM);
+        gemm_tc_kernel<false><<<gg, 128, G_SMEM, st>>>(ta, tb, bias, C, M, N, K, ldc, dev_err);
+    }
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        *msg = std::string("gemm launch failed: ") + cudaGetErrorString(e);
+        return WB_ECUDA;
+    }
+    return WB_OK;
+}
+
+template <int HDP, bool WIDE>
+static void launch_attn_tc(const CUtensorMap &tq, const CUtensorMap &tk, const CUtensorMap &tvh,
+                           const CUtensorMap &tvl, const AttnTcArgs &aa, int hdn, unsigned grid, cudaStream_t st) {
+    using L = AttnSmem<HDP, WIDE>;
+    ProfScope ps("attn_tc", st);
+    cudaFuncSetAttribute(attn_tc_kernel<HDP, WIDE>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES);
+    attn_tc_kernel<HDP, WIDE><<<grid, 128, L::BYTES, st>>>(tq, tk, tvh, tvl, aa, hdn);
 }
 
 // Runs features -> tcgen05 attention -> SIMT fallback for flagged tiles ->
@@ -587,112 +704,83 @@ static int tc_attention_core(const TcLayerWeights &t, const WbSeqView &sv, const
                              float *y, Workspace *ws, const CoreLayout &lay, uint32_t *dev_err, cudaStream_t st,
                              std::string *msg) {
     const int H = t.H, hd = t.hd, E = t.E;
+    const bool wide = t.wide;
     const int hdp = hd <= 64 ? 64 : 128;
     const int hdn = (hd + 15) / 16 * 16;
+    const int fw = wide ? 64 : 32;
     const long long BH = (long long)B * H, R = (long long)B * T;
     const int n_qt = (T + QT - 1) / QT;
     int rc;
-    const size_t o_qf = lay.qf, o_kf = lay.kf, o_vb = lay.vb, o_m0 = lay.m0, o_sp = lay.sp, o_cn = lay.cn,
-                 o_cm = lay.cm, o_fl = lay.fl, o_o = lay.o;
     char *w = (char *)ws->p;
-    __nv_bfloat16 *qf = (__nv_bfloat16 *)(w + o_qf), *kf = (__nv_bfloat16 *)(w + o_kf),
-                  *vb = (__nv_bfloat16 *)(w + o_vb), *ob = (__nv_bfloat16 *)(w + o_o);
-    float *m0 = (float *)(w + o_m0), *sp = (float *)(w + o_sp), *cn = (float *)(w + o_cn);
-    unsigned int *cm = (unsigned int *)(w + o_cm);
-    int *fl = (int *)(w + o_fl);
+    __nv_bfloat16 *qf = (__nv_bfloat16 *)(w + lay.qf), *kf = (__nv_bfloat16 *)(w + lay.kf);
+    __nv_bfloat16 *vh = (__nv_bfloat16 *)(w + lay.vh), *vl = (__nv_bfloat16 *)(w + lay.vl);
+    void *ob = (void *)(w + lay.o);
+    float *m0 = (float *)(w + lay.m0), *sp = (float *)(w + lay.sp), *cn = (float *)(w + lay.cn);
+    unsigned int *cm = (unsigned int *)(w + lay.cm);
+    int *fl = (int *)(w + lay.fl);
     if (cudaMemsetAsync(cm, 0, BH * sizeof(unsigned int), st) != cudaSuccess ||
         cudaMemsetAsync(fl, 0, BH * n_qt * sizeof(int), st) != cudaSuccess) {
         *msg = "cudaMemsetAsync failed";
         return WB_ECUDA;
     }
     const float cscale = content ? 1.0f / std::sqrt((float)t.C) : 0.0f;
-    FeatArgs fa{sv, content, content ? t.C : 0, cscale, t.harmonic_n, B, H, T, hd, hdp, qf, kf, vb, m0, sp, cn, cm};
-    feat_kernel<<<(unsigned)((BH * T + 255) / 256), 256, 0, st>>>(fa);
-
-    CUtensorMap tq, tk, tv;
+    FeatArgs fa{sv, content, content ? t.C : 0, cscale, t.harmonic_n, B, H, T, hd, hdp, qf, kf, vh, vl, m0, sp, cn, cm};
+    const unsigned fgrid = (unsigned)((BH * T + 255) / 256);
     {
-        const uint64_t dims[3] = {FEAT, (uint64_t)T, (uint64_t)BH};
-        const uint64_t strides[2] = {FEAT * 2, (uint64_t)T * FEAT * 2};
-        const uint32_t box[3] = {FEAT, 128, 1};
-        if ((rc = make_tmap(&tq, qf, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, dims, strides, box,
-                            CU_TENSOR_MAP_SWIZZLE_64B, msg)))
-            return rc;
-        if ((rc = make_tmap(&tk, kf, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, dims, strides, box,
-                            CU_TENSOR_MAP_SWIZZLE_64B, msg)))
-            return rc;
+        ProfScope ps("feat", st);
+        if (wide) feat_kernel<true><<<fgrid, 256, 0, st>>>(fa);
+        else feat_kernel<false><<<fgrid, 256, 0, st>>>(fa);
+    }
+
+    CUtensorMap tq, tk, tvh, tvl;
+    {
+        const uint64_t dims[3] = {(uint64_t)fw, (uint64_t)T, (uint64_t)BH};
+        const uint64_t strides[2] = {(uint64_t)fw * 2, (uint64_t)T * fw * 2};
+        const uint32_t box[3] = {(uint32_t)fw, 128, 1};
+        const CUtensorMapSwizzle fsw = wide ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+        if ((rc = make_tmap(&tq, qf, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, dims, strides, box, fsw, msg))) return rc;
+        if ((rc = make_tmap(&tk, kf, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, dims, strides, box, fsw, msg))) return rc;
         const uint64_t vdims[3] = {(uint64_t)hdp, (uint64_t)T, (uint64_t)BH};
         const uint64_t vstr[2] = {(uint64_t)hdp * 2, (uint64_t)T * hdp * 2};
         const uint32_t vbox[3] = {64, 128, 1};
-        if ((rc = make_tmap(&tv, vb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, vdims, vstr, vbox,
+        if ((rc = make_tmap(&tvh, vh, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, vdims, vstr, vbox,
                             CU_TENSOR_MAP_SWIZZLE_128B, msg)))
+            return rc;
+        tvl = tvh;
+        if (wide && (rc = make_tmap(&tvl, vl, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, vdims, vstr, vbox,
+                                    CU_TENSOR_MAP_SWIZZLE_128B, msg)))
             return rc;
     }
     AttnTcArgs aa{(int)BH, H, T, hd, n_qt, m0, sp, cn, cm, sv, ob, E, fl, dev_err};
     const unsigned grid = (unsigned)(BH * n_qt);
     if (hdp == 64) {
-        cudaFuncSetAttribute(attn_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnSmem<64>::BYTES);
-        attn_tc_kernel<64><<<grid, 128, AttnSmem<64>::BYTES, st>>>(tq, tk, tv, aa, hdn);
+        if (wide) launch_attn_tc<64, true>(tq, tk, tvh, tvl, aa, hdn, grid, st);
+        else launch_attn_tc<64, false>(tq, tk, tvh, tvl, aa, hdn, grid, st);
     } else {
-        cudaFuncSetAttribute(attn_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             AttnSmem<128>::BYTES);
-        attn_tc_kernel<128><<<grid, 128, AttnSmem<128>::BYTES, st>>>(tq, tk, tv, aa, hdn);
+        if (wide) launch_attn_tc<128, true>(tq, tk, tvh, tvl, aa, hdn, grid, st);
+        else launch_attn_tc<128, false>(tq, tk, tvh, tvl, aa, hdn, grid, st);
     }
-    launch_attn_simt_fallback_bf16(sv, content, content ? t.C : 0, cscale, t.harmonic_n, B, H, T, hd, ob, fl, st);
-
-    // out_proj: y = o W_o^T + b_o
-    CUtensorMap ta, tb;
     {
-        const uint64_t adims[2] = {(uint64_t)E, (uint64_t)R};
-        const uint64_t astr[1] = {(uint64_t)E * 2};
-        const uint32_t abox[2] = {GBK, GBM};
-        if ((rc = make_tmap(&ta, ob, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, adims, astr, abox,
-                            CU_TENSOR_MAP_SWIZZLE_128B, msg)))
-            return rc;
-        const uint64_t bdims[2] = {(uint64_t)E, (uint64_t)E};
-        const uint32_t bbox[2] = {GBK, GBN};
-        if ((rc = make_tmap(&tb, t.w_o, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, bdims, astr, bbox,
-                            CU_TENSOR_MAP_SWIZZLE_128B, msg)))
-            return rc;
+        if (wide)
+            launch_attn_simt_fallback_f32(sv, content, content ? t.C : 0, cscale, t.harmonic_n, B, H, T, hd,
+                                          (float *)ob, fl, st);
+        else
+            launch_attn_simt_fallback_bf16(sv, content, content ? t.C : 0, cscale, t.harmonic_n, B, H, T, hd,
+                                           (__nv_bfloat16 *)ob, fl, st);
     }
-    cudaFuncSetAttribute(gemm_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, G_SMEM);
-    dim3 gg((unsigned)((R + GBM - 1) / GBM), (unsigned)((E + GBN - 1) / GBN));
-    gemm_bf16_kernel<<<gg, 128, G_SMEM, st>>>(ta, tb, t.b_o, y, (int)R, E, E, E, dev_err);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) {
-        *msg = std::string("tensor path launch failed: ") + cudaGetErrorString(e);
-        return WB_ECUDA;
-    }
-    return WB_OK;
+    // out_proj: y = o W_o^T + b_o
+    return launch_gemm(wide, ob, wide ? (const void *)t.w_o32 : (const void *)t.w_o, t.b_o, y, (int)R, E, E, E,
+                       dev_err, st, msg);
 }
 
 int tc_gemm_bf16(const __nv_bfloat16 *A, const __nv_bfloat16 *B, const float *bias, float *C, int M, int N, int K,
                  uint32_t *dev_err, cudaStream_t st, std::string *msg) {
-    if (M <= 0 || N <= 0 || K <= 0 || K % 8) {
-        *msg = "bad GEMM shape (K must be a positive multiple of 8)";
-        return WB_EINVAL;
-    }
-    CUtensorMap ta, tb;
-    int rc;
-    const uint64_t adims[2] = {(uint64_t)K, (uint64_t)M};
-    const uint64_t str[1] = {(uint64_t)K * 2};
-    const uint32_t abox[2] = {GBK, GBM};
-    if ((rc = make_tmap(&ta, A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, adims, str, abox, CU_TENSOR_MAP_SWIZZLE_128B,
-                        msg)))
-        return rc;
-    const uint64_t bdims[2] = {(uint64_t)K, (uint64_t)N};
-    const uint32_t bbox[2] = {GBK, GBN};
-    if ((rc = make_tmap(&tb, B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, bdims, str, bbox, CU_TENSOR_MAP_SWIZZLE_128B,
-                        msg)))
-        return rc;
-    cudaFuncSetAttribute(gemm_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, G_SMEM);
-    dim3 gg((unsigned)((M + GBM - 1) / GBM), (unsigned)((N + GBN - 1) / GBN));
-    gemm_bf16_kernel<<<gg, 128, G_SMEM, st>>>(ta, tb, bias, C, M, N, K, N, dev_err);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) {
-        *msg = std::string("gemm launch failed: ") + cudaGetErrorString(e);
-        return WB_ECUDA;
-    }
-    return WB_OK;
+    return launch_gemm(false, A, B, bias, C, M, N, K, N, dev_err, st, msg);
+}
+
+int tc_gemm_tf32(const float *A, const float *B, const float *bias, float *C, int M, int N, int K, uint32_t *dev_err,
+                 cudaStream_t st, std::string *msg) {
+    return launch_gemm(true, A, B, bias, C, M, N, K, N, dev_err, st, msg);
 }
 
 int tc_attn_forward(const TcLayerWeights &t, const float *x, int B, int T, bool use_content, float *y,

@@ -15,6 +15,8 @@ struct TcLayerWeights {
     const float *b_o = nullptr;        // [E] out_proj bias
     const float *wo_t = nullptr;       // [E][E] out_proj, input-major fp32 (decode rows)
     __nv_bfloat16 *w_o = nullptr;      // [E][E] out_proj rows, bf16 (K-major B operand)
+    float *w_o32 = nullptr;            // [E][E] out_proj rows, fp32 (tf32 B operand, wide layers)
+    bool wide = true;                  // split precision: hi/lo features and values, tf32 out_proj
 };
 
 int tc_layer_upload(TcLayerWeights *t, const wb_attn_weights_desc *w, std::string *msg);
@@ -27,6 +29,8 @@ int tc_kv_prefill(const TcLayerWeights &t, const WbSeqView &sv, const float *x, 
                   Workspace *ws, uint32_t *dev_err, int sm_count, cudaStream_t st, std::string *msg);
 int tc_gemm_bf16(const __nv_bfloat16 *A, const __nv_bfloat16 *B, const float *bias, float *C, int M, int N, int K,
                  uint32_t *dev_err, cudaStream_t st, std::string *msg);
+int tc_gemm_tf32(const float *A, const float *B, const float *bias, float *C, int M, int N, int K, uint32_t *dev_err,
+                 cudaStream_t st, std::string *msg);
 int tc_kv_decode(const TcLayerWeights &t, const WbSeqView &sv, const int32_t *len, int cap, const float *x,
                  int n_seq, float *y, Workspace *ws, uint32_t *dev_err, int sm_count, cudaStream_t st,
                  std::string *msg);

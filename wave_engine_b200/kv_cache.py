@@ -30,6 +30,7 @@ class KvCache:
         _lib.call("wb_kv_cache_create", self.ctx.handle, n_layers, n_head, head_dim, max_seqs, max_ctx,
                   C.byref(h))
         self.handle = h
+        self.ctx.adopt(self)
 
     def close(self) -> None:
         if self.handle:
@@ -49,6 +50,11 @@ class KvCache:
 
     def reset_seq(self, seq: int) -> None:
         _lib.call("wb_kv_cache_reset_seq", self.handle, seq)
+
+    def reset(self) -> None:
+        """Empty every slot (every sequence, every layer)."""
+        for s in range(self.max_seqs):
+            self.reset_seq(s)
 
     def load(self, layer: int, seq: int, phases, values) -> None:
         """Fill one slot from phases [H][n] and values [H][n][hd]."""
@@ -77,7 +83,7 @@ class KvCache:
             return seq_ids
         return np.ascontiguousarray(np.atleast_1d(np.asarray(seq_ids)), dtype=np.int32)
 
-    def prefill(self, layer_idx: int, weights, x, seq_ids=(0,), *, path: str = "tensor"):
+    def prefill(self, layer_idx: int, weights, x, seq_ids=(0,), *, path: str = "tensor", out=None):
         """Prompt attention (kv_cache.rs:121-193) of x [n_seq][T][E] (or
         [T][E] for one sequence) into empty slots; returns y shaped like x."""
         if not is_torch(x):
@@ -88,13 +94,13 @@ class KvCache:
         if int(ids.shape[0]) != n_seq:
             raise ValueError("one seq id per sequence")
         layer = device_layer(weights, self.ctx)
-        y = _empty_like_input(x, tuple(x.shape))
+        y = _empty_like_input(x, tuple(x.shape)) if out is None else out
         self.ctx.use_torch_stream(x, y)
         _lib.call("wb_kv_prefill", self.ctx.handle, self.handle, layer_idx, layer.handle, ptr_of(ids, np.int32),
                   n_seq, ptr_of(x), T, PATHS[path], ptr_of(y))
         return y
 
-    def forward_one(self, layer_idx: int, weights, x, seq_ids=(0,), *, path: str = "tensor"):
+    def forward_one(self, layer_idx: int, weights, x, seq_ids=(0,), *, path: str = "tensor", out=None):
         """One new position per sequence (kv_cache.rs:263-335): x [n_seq][E]
         (or [E]); appends to each slot and returns y shaped like x."""
         if not is_torch(x):
@@ -105,7 +111,7 @@ class KvCache:
         if int(ids.shape[0]) != n_seq:
             raise ValueError("one seq id per sequence")
         layer = device_layer(weights, self.ctx)
-        y = _empty_like_input(x, tuple(x.shape))
+        y = _empty_like_input(x, tuple(x.shape)) if out is None else out
         self.ctx.use_torch_stream(x, y)
         _lib.call("wb_kv_decode", self.ctx.handle, self.handle, layer_idx, layer.handle, ptr_of(ids, np.int32),
                   n_seq, ptr_of(x), PATHS[path], ptr_of(y))

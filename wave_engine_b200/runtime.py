@@ -9,6 +9,7 @@ from __future__ import annotations
 
 import ctypes as C
 import threading
+import weakref
 
 import numpy as np
 
@@ -47,9 +48,16 @@ class Context:
         h = C.c_void_p()
         _lib.call("wb_context_create", device, C.byref(h))
         self.handle = h
+        self._children = weakref.WeakSet()  # layers / caches to release first
+
+    def adopt(self, obj) -> None:
+        self._children.add(obj)
 
     def close(self) -> None:
+        """Release every layer and cache of this context, then the context."""
         if self.handle:
+            for ch in list(self._children):
+                ch.close()
             _lib.lib().wb_context_destroy(self.handle)
             self.handle = None
 
@@ -69,6 +77,20 @@ class Context:
         v = C.c_uint32(0)
         _lib.call("wb_context_take_device_error", self.handle, C.byref(v))
         return int(v.value)
+
+    def profile(self, name_filter: str | None = "") -> None:
+        """Time named kernels with CUDA events ("" = all, None = off)."""
+        _lib.call("wb_context_profile", self.handle, None if name_filter is None else name_filter.encode())
+
+    def profile_report(self) -> dict:
+        """{kernel: (launches, total_ms)} since the last report (synchronises)."""
+        buf = C.create_string_buffer(1 << 16)
+        _lib.call("wb_context_profile_report", self.handle, buf, len(buf))
+        out = {}
+        for line in buf.value.decode().splitlines():
+            name, n, ms = line.split("\t")
+            out[name] = (int(n), float(ms))
+        return out
 
     def use_torch_stream(self, *tensors):
         """Run on torch's current stream when any argument is a CUDA tensor."""
@@ -110,6 +132,7 @@ class AttnLayer:
         _lib.call("wb_attn_layer_create", ctx.handle, C.byref(desc), C.byref(h))
         self.handle = h
         self._keep = None
+        ctx.adopt(self)
 
     def close(self) -> None:
         if self.handle:
@@ -131,6 +154,6 @@ def device_layer(weights, ctx: Context) -> AttnLayer:
         return weights
     key = id(ctx)
     lay = weights._device.get(key)
-    if lay is None or lay.ctx is not ctx:
+    if lay is None or lay.ctx is not ctx or not lay.handle:
         lay = weights._device[key] = AttnLayer(ctx, weights)
     return lay
