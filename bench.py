@@ -167,18 +167,59 @@ def run_ours(args):
     x_pre = torch.randn((L, B, T, E), generator=g, device=dev)
     x_dec = torch.randn((S, L, B, E), generator=g, device=dev)
     y_pre = torch.empty((B, T, E), device=dev)
-    y_dec = torch.empty((B, E), device=dev)
-    ids = np.arange(B, dtype=np.int32)
+    x_stage = torch.empty((L, B, E), device=dev)   # one decode step's per-layer inputs
+    y_stage = torch.empty((L, B, E), device=dev)
+    ids_dev = torch.arange(B, dtype=torch.int32, device=dev)
+    ids_host = np.arange(B, dtype=np.int32)
 
-    def step(xp, xd, yp, yd, ev=None):
+    def prefill(xp, yp, ids):
         cache.reset()
         for l in range(L):
             cache.prefill(l, layers[l], xp[l], ids, out=yp)
+
+    def decode_layers(xs, ys, ids):
+        for l in range(L):
+            cache.forward_one(l, layers[l], xs[l], ids, out=ys[l])
+
+    def check_err(where):
+        code = ctx.take_device_error()
+        if code:
+            names = {1: "tma timeout", 2: "mma timeout", 4: "softmax timeout", 8: "bounds", 16: "decode timeout"}
+            raise RuntimeError(f"device error word 0x{code:x} ({[v for k, v in names.items() if code & k]}) "
+                               f"after {where}")
+
+    # eager reference step: allocates workspaces, counts launches, gives the
+    # per-kernel breakdown (profiled, untimed)
+    ctx.profile("")
+    prefill(x_pre, y_pre, ids_dev)
+    check_err("eager prefill")
+    for s in range(S):
+        decode_layers(x_dec[s], y_stage, ids_dev)
+    breakdown = ctx.profile_report()
+    ctx.profile(None)
+    check_err("eager decode")
+    launches_prefill = sum(n for k, (n, _) in breakdown.items() if not k.startswith("decode"))
+    launches_decode_step = sum(n for k, (n, _) in breakdown.items() if k.startswith("decode")) // S
+
+    # one decode step (24 layers) as a CUDA graph, replayed once per token
+    graph = torch.cuda.CUDAGraph()
+    prefill(x_pre, y_pre, ids_dev)
+    x_stage.copy_(x_dec[0])
+    cap_stream = torch.cuda.Stream(dev)
+    cap_stream.wait_stream(stream)
+    with torch.cuda.graph(graph, stream=cap_stream):
+        decode_layers(x_stage, y_stage, ids_dev)
+    stream.wait_stream(cap_stream)
+    ctx.set_stream(stream.cuda_stream)
+    check_err("graph capture")
+
+    def step(ev=None):
+        prefill(x_pre, y_pre, ids_dev)
         if ev is not None:
             ev.record(stream)
         for s in range(S):
-            for l in range(L):
-                cache.forward_one(l, layers[l], xd[s, l], ids, out=yd)
+            x_stage.copy_(x_dec[s])
+            graph.replay()
 
     def barrier():
         torch.cuda.synchronize()
@@ -194,18 +235,18 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    # launch count of one step (every named kernel of the library)
-    ctx.profile("")
-    step(x_pre, x_dec, y_pre, y_dec)
-    launches_per_step = sum(n for n, _ in ctx.profile_report().values())
-    ctx.profile(None)
+    for w in range(args.warmup):
+        step()
+        barrier()
+        check_err(f"warm-up step {w}")
 
-    for _ in range(max(0, args.warmup - 1)):
-        step(x_pre, x_dec, y_pre, y_dec)
-    barrier()
-
-    dominant = args.roofline_kernel
-    ctx.profile(dominant)
+    if not args.no_prefill_profile:
+        ctx.profile("attn_tc")
+    if args.check_each_step:
+        for k in range(args.steps):
+            step()
+            barrier()
+            check_err(f"diagnostic step {k} (profiler {'off' if args.no_prefill_profile else 'on'})")
     clocks = Clocks(local)
     clocks.start()
     barrier()
@@ -216,45 +257,46 @@ def run_ours(args):
     e0.record(stream)
     for k in range(args.steps):
         starts[k].record(stream)
-        step(x_pre, x_dec, y_pre, y_dec, ev=mids[k])
+        step(ev=mids[k])
         ends[k].record(stream)
     e1.record(stream)
     barrier()
     clk = clocks.stop()
+    prof = ctx.profile_report() if not args.no_prefill_profile else {}
+    ctx.profile(None)
     ms_total = e0.elapsed_time(e1)
     pre_ms = sum(starts[k].elapsed_time(mids[k]) for k in range(args.steps)) / args.steps
     dec_ms = sum(mids[k].elapsed_time(ends[k]) for k in range(args.steps)) / args.steps
-    prof = ctx.profile_report()
-    ctx.profile(None)
     ms_step = max_over_ranks(ms_total / args.steps)
     pre_ms = max_over_ranks(pre_ms)
     dec_ms = max_over_ranks(dec_ms)
     tok_step = B * T + B * S
     value = world * tok_step / (ms_step / 1e3)
+    check_err("the timed region")
 
-    # roofline of the dominant kernel
+    # rooflines: decode (HBM) from the timed decode phase, prefill attention
+    # (tensor) from its CUDA-event timed launches
     hbm, bf16, peak_kind = peaks()
-    roof = None
-    if dominant in prof:
-        n, tot = prof[dominant]
-        per_launch_ms = tot / n
-        if "decode" in dominant:
-            bk = np.stack([np.stack([cache.read(l, b)[1] for b in range(B)]) for l in range(L)])
-            byts, unmasked, keys = decode_bytes_exact(bk, T, S, H, hd)
-            alg = byts / (S * L)
-            q_out = B * E * 4 * 2
-            alg += q_out
-            ach = alg / (per_launch_ms / 1e3) / 1e9
-            roof = {"kernel": dominant, "bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
-                    "frac": round(ach / hbm, 4), "traffic": None, "peak_kind": peak_kind,
-                    "algorithmic_bytes_per_launch": int(alg), "launch_ms": round(per_launch_ms, 5),
-                    "unmasked_key_fraction": round(unmasked / keys, 4)}
-        else:
-            fl = prefill_flops_per_layer(B, T, E, H, hd, C)
-            ach = fl / (per_launch_ms / 1e3) / 1e12
-            roof = {"kernel": dominant, "bound": "tensor", "achieved": round(ach, 2), "peak": bf16,
-                    "unit": "TFLOP/s", "frac": round(ach / bf16, 4), "traffic": None, "peak_kind": peak_kind,
-                    "launch_ms": round(per_launch_ms, 5)}
+    bk = np.stack([np.stack([cache.read(l, b)[1] for b in range(B)]) for l in range(L)])
+    byts, unmasked, keys = decode_bytes_exact(bk, T, S, H, hd)
+    per_launch_bytes = byts / (S * L) + 2 * B * E * 4
+    per_launch_ms = dec_ms / (S * L)
+    ach = per_launch_bytes / (per_launch_ms / 1e3) / 1e9
+    roof = {"kernel": "decode_fused", "bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
+            "frac": round(ach / hbm, 4), "traffic": None, "peak_kind": peak_kind,
+            "algorithmic_bytes_per_launch": int(per_launch_bytes), "launch_ms": round(per_launch_ms, 5),
+            "timing": "decode phase time / decode launches (includes the length-update kernel and the "
+                      "per-token input copy)",
+            "unmasked_key_fraction": round(unmasked / keys, 4)}
+    roof_prefill = None
+    if "attn_tc" in prof:
+        n, tot = prof["attn_tc"]
+        fl = prefill_flops_per_layer(B, T, E, H, hd, 0)  # serve prefill: no content bias
+        a_ms = tot / n
+        roof_prefill = {"kernel": "attn_tc", "bound": "tensor", "achieved": round(fl / (a_ms / 1e3) / 1e12, 2),
+                        "peak": bf16, "unit": "TFLOP/s",
+                        "frac": round(fl / (a_ms / 1e3) / 1e12 / bf16, 4), "launch_ms": round(a_ms, 4),
+                        "flops_per_launch": fl, "note": "whole-layer algorithmic FLOPs / attention kernel time"}
 
     # end to end through the public API with pinned host buffers
     e2e = None
@@ -262,22 +304,27 @@ def run_ours(args):
         xp_h = x_pre.cpu().pin_memory()
         xd_h = x_dec.cpu().pin_memory()
         yp_h = torch.empty((B, T, E)).pin_memory()
-        yd_h = torch.empty((B, E)).pin_memory()
-        del x_pre, x_dec
+        yd_h = torch.empty((L, B, E)).pin_memory()
         n_e2e = max(1, min(args.steps, args.e2e_steps))
-        step(xp_h, xd_h, yp_h, yd_h)
+
+        def step_host():
+            prefill(xp_h, yp_h, ids_host)
+            for s in range(S):
+                decode_layers(xd_h[s], yd_h, ids_host)
+
+        step_host()
         barrier()
         f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         f0.record(stream)
         for _ in range(n_e2e):
-            step(xp_h, xd_h, yp_h, yd_h)
+            step_host()
         f1.record(stream)
         barrier()
         e2e_ms = max_over_ranks(f0.elapsed_time(f1) / n_e2e)
         e2e = {"value": round(world * tok_step / (e2e_ms / 1e3), 1), "unit": "tok/s",
                "h2d_bytes_per_step": int(xp_h.numel() * 4 + xd_h.numel() * 4 + (L + S * L) * B * 4),
                "d2h_bytes_per_step": int((L * B * T * E + S * L * B * E) * 4), "ms_per_step": round(e2e_ms, 3),
-               "steps": n_e2e}
+               "steps": n_e2e, "api": "KvCache.prefill / forward_one per layer with pinned host x and y"}
 
     out = {
         "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
@@ -286,18 +333,21 @@ def run_ours(args):
         "data": "synthetic (seeded N(0,0.02) weights, N(0,1) layer inputs)",
         "config": {"workload": WORKLOAD, "n_embd": E, "n_head": H, "head_dim": hd, "layers": L, "batch_per_gpu": B,
                    "seq_len": T, "decode_steps": S, "content_dim": C,
-                   "l2": "inputs larger than L2 (100 MB per prefill layer input)",
+                   "l2": "inputs larger than L2 (100 MB per prefill layer input, 3 GB in all)",
+                   "decode": "one CUDA graph per decode step (24 fused kernels + length updates)",
                    "parallelism": f"dp{world} (sequences sharded, no collective)"},
         "prefill": {"tok_s": round(world * B * T / (pre_ms / 1e3), 1), "ms": round(pre_ms, 3)},
         "decode": {"tok_s": round(world * B * S / (dec_ms / 1e3), 1), "ms": round(dec_ms, 3)},
         "roofline": roof,
-        "kernel_ms": {k: round(v[1] / args.steps, 3) for k, v in prof.items()},
-        "gpu_launches": launches_per_step * args.steps,
+        "roofline_prefill": roof_prefill,
+        "kernel_ms_eager_step": {k: round(v[1], 3) for k, v in sorted(breakdown.items())},
+        "gpu_launches": (launches_prefill + launches_decode_step * S) * args.steps,
         "clocks": clk,
         "e2e": e2e,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
+    del graph
     if world > 1:
         import torch.distributed as dist
         dist.barrier()
@@ -407,8 +457,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--decode-steps", type=int, default=CFG["decode_steps"])
-    ap.add_argument("--roofline-kernel", default="decode_simt")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-prefill-profile", action="store_true")
+    ap.add_argument("--check-each-step", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=20.0)

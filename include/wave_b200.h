@@ -112,8 +112,11 @@ WB_API const char *wb_last_error(void);
  * device memory). */
 WB_API int wb_context_create(int device, wb_context **out);
 WB_API int wb_context_destroy(wb_context *ctx);
-/* Use an external cudaStream_t (NULL = the context's own stream). */
+/* Run later calls on an external cudaStream_t.  As everywhere in CUDA, NULL
+ * is the legacy default stream (e.g. torch's default stream), not the
+ * context's own stream; wb_context_own_stream returns the latter. */
 WB_API int wb_context_set_stream(wb_context *ctx, void *cuda_stream);
+WB_API void *wb_context_own_stream(wb_context *ctx);
 WB_API int wb_context_synchronize(wb_context *ctx);
 /* Device error word: non-zero when a bounded device-side wait gave up or a
  * kernel-side check failed since the last reset.  Resets it. */
@@ -160,7 +163,8 @@ WB_API int wb_kv_cache_create(wb_context *ctx, int n_layers, int n_head, int hea
 WB_API int wb_kv_cache_destroy(wb_kv_cache *cache);
 /* Number of cached positions of (layer, seq). */
 WB_API int wb_kv_cache_length(wb_kv_cache *cache, int layer, int seq, int *len_out);
-/* Empty a sequence slot in every layer (a new request). */
+/* Empty a sequence slot in every layer (a new request); seq = -1 empties
+ * every slot. */
 WB_API int wb_kv_cache_reset_seq(wb_kv_cache *cache, int seq);
 /* Load n positions of one (layer, seq) slot from raw arrays: phases
  * [n_head][n], values [n_head][n][head_dim] (host or device).  Buckets are
@@ -183,8 +187,14 @@ WB_API int wb_kv_prefill(wb_context *ctx, wb_kv_cache *cache, int layer_idx, con
 
 /* kv_cache.rs:263-335: one new position per sequence (x [n_seq][n_embd])
  * against slots seq_ids[i] of `layer_idx`; writes y [n_seq][n_embd] and
- * appends the new phase/bucket/value to each slot.  seq_ids may be host or
- * device memory. */
+ * appends the new phase/bucket/value to each slot.
+ * seq_ids in HOST memory are validated (range, duplicates, capacity) before
+ * any work is queued.  seq_ids in DEVICE memory are not read by the host:
+ * the call then does no host synchronisation and can be captured in a CUDA
+ * graph and replayed (lengths live on the device); the kernels check range
+ * and capacity and report violations through the device error word, and
+ * duplicate ids are the caller's responsibility.  The same holds for
+ * wb_kv_prefill, which additionally requires empty slots. */
 WB_API int wb_kv_decode(wb_context *ctx, wb_kv_cache *cache, int layer_idx, const wb_attn_layer *layer,
                  const int32_t *seq_ids, int n_seq, const float *x, int flags, float *y);
 

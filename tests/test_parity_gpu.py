@@ -198,3 +198,129 @@ def test_kv_cache_load_read_and_errors(ctx):
         cache.forward_one(0, w, x[:, 0].copy(), [5])  # seq id out of range
     cache.reset_seq(1)
     assert cache.n_cached(1, 1) == 0
+
+
+@pytest.mark.parametrize("E,H,ctx_len", [(168, 4, 700), (384, 8, 1100), (768, 12, 1300), (4096, 32, 520)])
+def test_fused_decode_long_context_matches_oracle(ctx, E, H, ctx_len):
+    """Fused decode over several 512-key splits, loaded caches, head dims 42/48/64/128."""
+    import wave_engine_b200 as wb
+    d = E // H
+    w = wb.gaussian_block_attn(E + 1, H, E, 0)
+    wp = w.packed()
+    g = np.random.default_rng(E)
+    n_seq, steps = 3, 3
+    cache = wb.KvCache(1, H, d, max_seqs=n_seq, max_ctx=ctx_len + steps, ctx=ctx)
+    states = []
+    for i in range(n_seq):
+        n = ctx_len - 97 * i
+        ph = np.arctan2(g.standard_normal((H, n)), g.standard_normal((H, n))).astype(np.float32)
+        vv = g.standard_normal((H, n, d)).astype(np.float32)
+        cache.load(0, i, ph, vv)
+        st = oracle.KvState(H, d, ctx_len + steps)
+        st.phases[:, :n] = ph
+        st.values[:, :n] = vv
+        st.buckets[:, :n] = oracle.phase_to_bucket(ph)
+        st.n.value = n
+        states.append(st)
+    x = g.standard_normal((steps, n_seq, E)).astype(np.float32)
+    for s in range(steps):
+        y = cache.forward_one(0, w, x[s], np.arange(n_seq, dtype=np.int32))
+        for i in range(n_seq):
+            oy = oracle.kv_decode(wp, x[s, i], states[i])
+            r = check(f"step {s} seq {i}", y[i], oy, TENSOR_TOL)
+            assert r.passed, str(r)
+    for i in range(n_seq):
+        ph, bk, vv = cache.read(0, i)
+        n = states[i].n_cached
+        assert ph.shape[1] == n
+        # the fused kernel sums the phase projection as a tree, not in the
+        # reference's sequential order: a few ulps of (r, s), ~1e-6 rad
+        assert phase_diff(ph, states[i].phases[:, :n]).max() <= 2e-5
+        assert check("appended values", vv, states[i].values[:, :n], (1e-5, 1e-5)).passed
+    assert ctx.take_device_error() == 0
+
+
+def test_fused_decode_from_empty_cache_and_device_ids(ctx):
+    """n_cached = 0 gives o = v_new (softmax over the self score only); device
+    seq ids skip host validation and still advance the lengths."""
+    import torch
+    import wave_engine_b200 as wb
+    w = wb.gaussian_block_attn(3, 12, 768, 0)
+    wp = w.packed()
+    cache = wb.KvCache(1, 12, 64, max_seqs=4, max_ctx=8, ctx=ctx)
+    x = np.random.default_rng(1).standard_normal((2, 768)).astype(np.float32)
+    ids = torch.tensor([3, 1], dtype=torch.int32, device="cuda")
+    xt = torch.from_numpy(x).cuda()
+    y = cache.forward_one(0, w, xt, ids)
+    torch.cuda.synchronize()
+    for i in range(2):
+        st = oracle.KvState(12, 64, 8)
+        oy = oracle.kv_decode(wp, x[i], st)
+        assert check("empty-cache decode", y[i].cpu().numpy(), oy, TENSOR_TOL).passed
+    assert cache.n_cached(0, 3) == 1 and cache.n_cached(0, 1) == 1 and cache.n_cached(0, 0) == 0
+    assert ctx.take_device_error() == 0
+
+
+def test_decode_graph_capture_replays_like_eager(ctx):
+    """A decode step captured in a CUDA graph (device ids, device buffers)
+    replays to the same outputs as eager calls on a twin cache."""
+    import torch
+    import wave_engine_b200 as wb
+    H, E, T, L = 12, 768, 200, 2
+    ws = [wb.gaussian_block_attn(50 + l, H, E, 16) for l in range(L)]
+    layers = [wb.AttnLayer(ctx, w) for w in ws]
+    g = torch.Generator(device="cuda").manual_seed(0)
+    xp = torch.randn((L, 4, T, E), generator=g, device="cuda")
+    xd = torch.randn((3, L, 4, E), generator=g, device="cuda")
+    ids = torch.arange(4, dtype=torch.int32, device="cuda")
+    caches = [wb.KvCache(L, H, 64, max_seqs=4, max_ctx=T + 3, ctx=ctx) for _ in range(2)]
+    yp = torch.empty((4, T, E), device="cuda")
+    for c in caches:
+        for l in range(L):
+            c.prefill(l, layers[l], xp[l], ids, out=yp)
+    stage = torch.empty((L, 4, E), device="cuda")
+    y_graph = torch.empty((L, 4, E), device="cuda")
+    y_eager = torch.empty((3, L, 4, E), device="cuda")
+    graph = torch.cuda.CUDAGraph()
+    stage.copy_(xd[0])
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    # eager step 0 on cache 1 first (allocates the decode scratch)
+    for l in range(L):
+        caches[1].forward_one(l, layers[l], xd[0, l], ids, out=y_eager[0, l])
+    torch.cuda.synchronize()
+    with torch.cuda.graph(graph, stream=s):
+        for l in range(L):
+            caches[0].forward_one(l, layers[l], stage[l], ids, out=y_graph[l])
+    torch.cuda.current_stream().wait_stream(s)
+    for step in range(3):
+        stage.copy_(xd[step])
+        graph.replay()
+        if step > 0:
+            for l in range(L):
+                caches[1].forward_one(l, layers[l], xd[step, l], ids, out=y_eager[step, l])
+        torch.cuda.synchronize()
+        assert torch.equal(y_graph, y_eager[step]), step
+    assert caches[0].n_cached(1, 2) == T + 3
+    del graph
+    assert ctx.take_device_error() == 0
+
+
+def test_tensor_path_fallback_tiles_for_unbounded_scores(ctx):
+    """Content weights 100x larger push |c_q|(max|c_k| - |c_q|)/4 past the
+    fixed-shift bound; those query tiles are recomputed by the fp32 SIMT
+    kernel and the result still matches the oracle."""
+    import wave_engine_b200 as wb
+    w, x = make_case(168, 4, 16, 2, 150, seed=77)
+    for hw in w.heads:
+        hw.content_proj_w = hw.content_proj_w * 100.0
+    w.invalidate()
+    ctx.profile("attn_simt_fallback")
+    y, _, _, ph = wb.wave_attention_forward(w, x, 84, path="tensor", return_phases=True, ctx=ctx)
+    rep = ctx.profile_report()
+    ctx.profile(None)
+    oy, _, _ = oracle_for(w.packed(), x, ph)
+    r = check("y (fallback tiles)", y, oy, TENSOR_TOL)
+    assert r.passed, str(r)
+    assert "attn_simt_fallback" in rep
+    assert ctx.take_device_error() == 0

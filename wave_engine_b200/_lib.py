@@ -34,6 +34,7 @@ SIGNATURES = {
     "wb_context_create": (C.c_int, [C.c_int, C.POINTER(_VP)]),
     "wb_context_destroy": (C.c_int, [_VP]),
     "wb_context_set_stream": (C.c_int, [_VP, _VP]),
+    "wb_context_own_stream": (_VP, [_VP]),
     "wb_context_synchronize": (C.c_int, [_VP]),
     "wb_context_take_device_error": (C.c_int, [_VP, C.POINTER(C.c_uint32)]),
     "wb_context_profile": (C.c_int, [_VP, C.c_char_p]),

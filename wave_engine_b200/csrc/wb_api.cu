@@ -4,7 +4,9 @@
 #include "wave_b200_testing.h"
 #include "wb_internal.h"
 #include "wb_tc.h"
+#include "wb_decode.h"
 
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -123,8 +125,19 @@ struct wb_kv_cache {
     float *theta = nullptr;
     uint8_t *bucket = nullptr;
     float *v = nullptr;
-    int32_t *len = nullptr;            // device [L][S]
+    int32_t *len = nullptr;            // device [L][S] (the truth)
+    wb::Workspace dscratch;            // fused decode partials + tickets, sized for (S, cap), zeroed
     std::vector<int32_t> len_host;     // host mirror [L][S]
+    bool len_stale = false;            // a call with device seq ids changed lengths on the device
+    int refresh(cudaStream_t st) {
+        if (!len_stale) return WB_OK;
+        if (cudaStreamSynchronize(st) != cudaSuccess ||
+            cudaMemcpy(len_host.data(), len, len_host.size() * sizeof(int32_t), cudaMemcpyDeviceToHost) !=
+                cudaSuccess)
+            return WB_ECUDA;
+        len_stale = false;
+        return WB_OK;
+    }
     WbSeqView view(int layer, const int32_t *slots) const {
         const long long per_layer = (long long)S * H * cap;
         WbSeqView s;
@@ -190,9 +203,11 @@ int wb_context_destroy(wb_context *ctx) {
 
 int wb_context_set_stream(wb_context *ctx, void *cuda_stream) {
     if (!ctx) return fail(WB_EINVAL, "ctx is NULL");
-    ctx->stream = cuda_stream ? (cudaStream_t)cuda_stream : ctx->own;
+    ctx->stream = (cudaStream_t)cuda_stream;  // NULL = the CUDA default (legacy) stream
     return WB_OK;
 }
+
+void *wb_context_own_stream(wb_context *ctx) { return ctx ? (void *)ctx->own : nullptr; }
 
 int wb_context_synchronize(wb_context *ctx) {
     if (!ctx) return fail(WB_EINVAL, "ctx is NULL");
@@ -478,6 +493,19 @@ int wb_kv_cache_create(wb_context *ctx, int n_layers, int n_head, int head_dim, 
         wb_kv_cache_destroy(c);
         return fail(WB_ENOMEM, "KV cache allocation failed (" + std::to_string(n * (5 + 4 * head_dim)) + " bytes)");
     }
+    {
+        std::string msg;
+        const size_t nb = wb::decode_scratch_bytes(max_seqs, n_head, head_dim, n_head * head_dim, max_ctx);
+        if (wb::ws_ensure(&c->dscratch, nb, &msg) != 0) {
+            wb_kv_cache_destroy(c);
+            return fail(WB_ENOMEM, msg);
+        }
+        if (cudaMemset(c->dscratch.p, 0, c->dscratch.n) != cudaSuccess) {
+            cudaGetLastError();
+            wb_kv_cache_destroy(c);
+            return fail(WB_ECUDA, "cudaMemset failed");
+        }
+    }
     if (cudaMemset(c->len, 0, (size_t)n_layers * max_seqs * sizeof(int32_t)) != cudaSuccess) {
         cudaGetLastError();
         wb_kv_cache_destroy(c);
@@ -495,6 +523,7 @@ int wb_kv_cache_destroy(wb_kv_cache *c) {
     if (c->bucket) cudaFree(c->bucket);
     if (c->v) cudaFree(c->v);
     if (c->len) cudaFree(c->len);
+    if (c->dscratch.p) cudaFree(c->dscratch.p);
     delete c;
     return WB_OK;
 }
@@ -502,14 +531,23 @@ int wb_kv_cache_destroy(wb_kv_cache *c) {
 int wb_kv_cache_length(wb_kv_cache *c, int layer, int seq, int *len_out) {
     if (!c || !len_out) return fail(WB_EINVAL, "NULL argument");
     if (layer < 0 || layer >= c->L || seq < 0 || seq >= c->S) return fail(WB_EINVAL, "layer/seq out of range");
+    DeviceGuard g(c->device);
+    if (c->refresh(c->ctx->stream) != WB_OK) return fail(WB_ECUDA, "reading cache lengths failed");
     *len_out = c->len_host[(size_t)layer * c->S + seq];
     return WB_OK;
 }
 
 int wb_kv_cache_reset_seq(wb_kv_cache *c, int seq) {
     if (!c) return fail(WB_EINVAL, "NULL argument");
-    if (seq < 0 || seq >= c->S) return fail(WB_EINVAL, "seq out of range");
+    if (seq < -1 || seq >= c->S) return fail(WB_EINVAL, "seq out of range");
     DeviceGuard g(c->device);
+    if (seq == -1) {  // every slot of every layer
+        WB_CUDA(cudaMemsetAsync(c->len, 0, c->len_host.size() * sizeof(int32_t), c->ctx->stream));
+        std::fill(c->len_host.begin(), c->len_host.end(), 0);
+        c->len_stale = false;
+        return WB_OK;
+    }
+    if (c->refresh(c->ctx->stream) != WB_OK) return fail(WB_ECUDA, "reading cache lengths failed");
     for (int l = 0; l < c->L; l++) {
         c->len_host[(size_t)l * c->S + seq] = 0;
         WB_CUDA(cudaMemsetAsync(c->len + (size_t)l * c->S + seq, 0, sizeof(int32_t), c->ctx->stream));
@@ -525,6 +563,7 @@ int wb_kv_cache_load(wb_context *ctx, wb_kv_cache *c, int layer, int seq, int n,
     if (n < 0 || n > c->cap) return fail(WB_EINVAL, "n exceeds cache capacity");
     DeviceGuard g(ctx->device);
     cudaStream_t st = ctx->stream;
+    if (c->refresh(st) != WB_OK) return fail(WB_ECUDA, "reading cache lengths failed");
     WbSeqView sv = c->view(layer, nullptr);
     const bool dev = is_device_ptr(phases);
     const cudaMemcpyKind kind = dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
@@ -552,6 +591,7 @@ int wb_kv_cache_read(wb_context *ctx, wb_kv_cache *c, int layer, int seq, float 
     DeviceGuard g(ctx->device);
     cudaStream_t st = ctx->stream;
     WB_CUDA(cudaStreamSynchronize(st));
+    if (c->refresh(st) != WB_OK) return fail(WB_ECUDA, "reading cache lengths failed");
     const int n = c->len_host[(size_t)layer * c->S + seq];
     WbSeqView sv = c->view(layer, nullptr);
     for (int h = 0; h < c->H && n > 0; h++) {
@@ -565,47 +605,67 @@ int wb_kv_cache_read(wb_context *ctx, wb_kv_cache *c, int layer, int seq, float 
     return WB_OK;
 }
 
-static int copy_seq_ids(wb_context *ctx, const int32_t *seq_ids, int n_seq, std::vector<int32_t> &host) {
-    host.resize(n_seq);
-    WB_CUDA(cudaMemcpy(host.data(), seq_ids, n_seq * sizeof(int32_t), cudaMemcpyDefault));
+// Sequence ids: host arrays are validated against the host length mirror
+// and copied to the context's staging buffer; device arrays are used as
+// they are (no host synchronisation, so the call can be captured in a CUDA
+// graph) and the kernels check slots and capacity on the device.
+struct SeqIds {
+    const int32_t *dev = nullptr;
+    std::vector<int32_t> host;
+    bool on_device = false;
+};
+
+static int check_host_ids(wb_kv_cache *c, int layer_idx, const int32_t *ids, int n_seq, bool prefill, int T) {
+    if (c->refresh(c->ctx->stream) != WB_OK) return fail(WB_ECUDA, "reading cache lengths failed");
+    for (int i = 0; i < n_seq; i++) {
+        if (ids[i] < 0 || ids[i] >= c->S) return fail(WB_EINVAL, "seq id out of range");
+        const int len = c->len_host[(size_t)layer_idx * c->S + ids[i]];
+        if (prefill && len != 0)
+            return fail(WB_EINVAL, "prefill needs an empty slot (kv_cache.rs prefill starts from KvCache::new)");
+        if (prefill && T > c->cap) return fail(WB_EINVAL, "seq_len exceeds cache capacity");
+        if (!prefill && len >= c->cap) return fail(WB_EINVAL, "cache slot is full");
+        for (int j = 0; j < i; j++)
+            if (ids[j] == ids[i]) return fail(WB_EINVAL, "duplicate seq id");
+    }
     return WB_OK;
 }
 
-int wb_kv_prefill(wb_context *ctx, wb_kv_cache *c, int layer_idx, const wb_attn_layer *L, const int32_t *seq_ids,
-                  int n_seq, const float *x, int T, int flags, float *y) {
+static int common_kv_checks(wb_context *ctx, wb_kv_cache *c, int layer_idx, const wb_attn_layer *L,
+                            const int32_t *seq_ids, const float *x, const float *y, int flags) {
     if (!ctx || !c || !L || !seq_ids || !x || !y) return fail(WB_EINVAL, "NULL argument");
     if (c->ctx != ctx || L->ctx != ctx) return fail(WB_EINVAL, "objects belong to another context");
     if (flags & ~(WB_PATH_EXACT | WB_NO_CONTENT)) return fail(WB_EINVAL, "unknown flag bits");
     if (layer_idx < 0 || layer_idx >= c->L) return fail(WB_EINVAL, "layer out of range");
     if (L->H != c->H || L->hd != c->hd) return fail(WB_EINVAL, "layer shape does not match cache");
+    return WB_OK;
+}
+
+int wb_kv_prefill(wb_context *ctx, wb_kv_cache *c, int layer_idx, const wb_attn_layer *L, const int32_t *seq_ids,
+                  int n_seq, const float *x, int T, int flags, float *y) {
+    WB_TRY(common_kv_checks(ctx, c, layer_idx, L, seq_ids, x, y, flags));
     if (n_seq < 0 || T < 0) return fail(WB_EINVAL, "negative n_seq or seq_len");
+    if (n_seq > c->S) return fail(WB_EINVAL, "more sequences than cache slots");
     if (n_seq == 0 || T == 0) return WB_OK;
     if (T > c->cap) return fail(WB_EINVAL, "seq_len exceeds cache capacity");
     DeviceGuard g(ctx->device);
     ProfBind pb(ctx);
-    std::vector<int32_t> ids;
-    WB_TRY(copy_seq_ids(ctx, seq_ids, n_seq, ids));
-    for (int i = 0; i < n_seq; i++) {
-        if (ids[i] < 0 || ids[i] >= c->S) return fail(WB_EINVAL, "seq id out of range");
-        if (c->len_host[(size_t)layer_idx * c->S + ids[i]] != 0)
-            return fail(WB_EINVAL, "prefill needs an empty slot (kv_cache.rs prefill starts from KvCache::new)");
-        for (int j = 0; j < i; j++)
-            if (ids[j] == ids[i]) return fail(WB_EINVAL, "duplicate seq id");
-    }
     cudaStream_t st = ctx->stream;
+    const bool ids_dev = is_device_ptr(seq_ids);
+    if (!ids_dev) WB_TRY(check_host_ids(c, layer_idx, seq_ids, n_seq, true, T));
     const long long R = (long long)n_seq * T;
     const int E = L->E, H = L->H, hd = L->hd;
     const bool x_dev = is_device_ptr(x), y_dev = is_device_ptr(y);
     Carve io;
     size_t o_x = x_dev ? 0 : io.take<float>(R * E);
     size_t o_y = y_dev ? 0 : io.take<float>(R * E);
-    size_t o_ids = io.take<int32_t>(n_seq);
-    WB_TRY(ensure(ctx->io, io.off));
+    size_t o_ids = ids_dev ? 0 : io.take<int32_t>(n_seq);
+    if (io.off) WB_TRY(ensure(ctx->io, io.off));
     char *iob = (char *)ctx->io.p;
     const float *xd = x_dev ? x : (const float *)(iob + o_x);
     float *yd = y_dev ? y : (float *)(iob + o_y);
-    int32_t *ids_d = (int32_t *)(iob + o_ids);
-    WB_CUDA(cudaMemcpyAsync(ids_d, ids.data(), n_seq * sizeof(int32_t), cudaMemcpyHostToDevice, st));
+    const int32_t *ids_d = ids_dev ? seq_ids : (const int32_t *)(iob + o_ids);
+    if (!ids_dev)
+        WB_CUDA(cudaMemcpyAsync((void *)ids_d, seq_ids, n_seq * sizeof(int32_t), cudaMemcpyHostToDevice, st));
     if (!x_dev) WB_CUDA(cudaMemcpyAsync((void *)xd, x, R * E * sizeof(float), cudaMemcpyHostToDevice, st));
     WbSeqView sv = c->view(layer_idx, ids_d);
     if (flags & WB_PATH_EXACT) {
@@ -622,13 +682,14 @@ int wb_kv_prefill(wb_context *ctx, wb_kv_cache *c, int layer_idx, const wb_attn_
         WB_CUDA(cudaGetLastError());
     } else {
         std::string msg;
-        int rc = wb::tc_kv_prefill(L->tc, sv, xd, n_seq, T, yd, &ctx->ws, ctx->dev_err,
-                                   ctx->sm_count, st, &msg);
+        int rc = wb::tc_kv_prefill(L->tc, sv, xd, n_seq, T, yd, &ctx->ws, ctx->dev_err, ctx->sm_count, st, &msg);
         if (rc != WB_OK) return fail(rc, msg);
     }
     wb::launch_len_update(c->len + (size_t)layer_idx * c->S, ids_d, n_seq, T, 1, st);
     WB_CUDA(cudaGetLastError());
-    for (int i = 0; i < n_seq; i++) c->len_host[(size_t)layer_idx * c->S + ids[i]] = T;
+    if (ids_dev) c->len_stale = true;
+    else
+        for (int i = 0; i < n_seq; i++) c->len_host[(size_t)layer_idx * c->S + seq_ids[i]] = T;
     if (!y_dev) {
         WB_CUDA(cudaMemcpyAsync(y, yd, R * E * sizeof(float), cudaMemcpyDeviceToHost, st));
         WB_CUDA(cudaStreamSynchronize(st));
@@ -638,36 +699,28 @@ int wb_kv_prefill(wb_context *ctx, wb_kv_cache *c, int layer_idx, const wb_attn_
 
 int wb_kv_decode(wb_context *ctx, wb_kv_cache *c, int layer_idx, const wb_attn_layer *L, const int32_t *seq_ids,
                  int n_seq, const float *x, int flags, float *y) {
-    if (!ctx || !c || !L || !seq_ids || !x || !y) return fail(WB_EINVAL, "NULL argument");
-    if (c->ctx != ctx || L->ctx != ctx) return fail(WB_EINVAL, "objects belong to another context");
-    if (flags & ~(WB_PATH_EXACT | WB_NO_CONTENT)) return fail(WB_EINVAL, "unknown flag bits");
-    if (layer_idx < 0 || layer_idx >= c->L) return fail(WB_EINVAL, "layer out of range");
-    if (L->H != c->H || L->hd != c->hd) return fail(WB_EINVAL, "layer shape does not match cache");
+    WB_TRY(common_kv_checks(ctx, c, layer_idx, L, seq_ids, x, y, flags));
     if (n_seq < 0) return fail(WB_EINVAL, "negative n_seq");
+    if (n_seq > c->S) return fail(WB_EINVAL, "more sequences than cache slots");
     if (n_seq == 0) return WB_OK;
     DeviceGuard g(ctx->device);
     ProfBind pb(ctx);
-    std::vector<int32_t> ids;
-    WB_TRY(copy_seq_ids(ctx, seq_ids, n_seq, ids));
-    for (int i = 0; i < n_seq; i++) {
-        if (ids[i] < 0 || ids[i] >= c->S) return fail(WB_EINVAL, "seq id out of range");
-        if (c->len_host[(size_t)layer_idx * c->S + ids[i]] >= c->cap) return fail(WB_EINVAL, "cache slot is full");
-        for (int j = 0; j < i; j++)
-            if (ids[j] == ids[i]) return fail(WB_EINVAL, "duplicate seq id");
-    }
     cudaStream_t st = ctx->stream;
+    const bool ids_dev = is_device_ptr(seq_ids);
+    if (!ids_dev) WB_TRY(check_host_ids(c, layer_idx, seq_ids, n_seq, false, 0));
     const int E = L->E, H = L->H, hd = L->hd;
     const bool x_dev = is_device_ptr(x), y_dev = is_device_ptr(y);
     Carve io;
     size_t o_x = x_dev ? 0 : io.take<float>((size_t)n_seq * E);
     size_t o_y = y_dev ? 0 : io.take<float>((size_t)n_seq * E);
-    size_t o_ids = io.take<int32_t>(n_seq);
-    WB_TRY(ensure(ctx->io, io.off));
+    size_t o_ids = ids_dev ? 0 : io.take<int32_t>(n_seq);
+    if (io.off) WB_TRY(ensure(ctx->io, io.off));
     char *iob = (char *)ctx->io.p;
     const float *xd = x_dev ? x : (const float *)(iob + o_x);
     float *yd = y_dev ? y : (float *)(iob + o_y);
-    int32_t *ids_d = (int32_t *)(iob + o_ids);
-    WB_CUDA(cudaMemcpyAsync(ids_d, ids.data(), n_seq * sizeof(int32_t), cudaMemcpyHostToDevice, st));
+    const int32_t *ids_d = ids_dev ? seq_ids : (const int32_t *)(iob + o_ids);
+    if (!ids_dev)
+        WB_CUDA(cudaMemcpyAsync((void *)ids_d, seq_ids, n_seq * sizeof(int32_t), cudaMemcpyHostToDevice, st));
     if (!x_dev) WB_CUDA(cudaMemcpyAsync((void *)xd, x, (size_t)n_seq * E * sizeof(float), cudaMemcpyHostToDevice, st));
     WbSeqView sv = c->view(layer_idx, ids_d);
     int32_t *len_l = c->len + (size_t)layer_idx * c->S;
@@ -691,16 +744,17 @@ int wb_kv_decode(wb_context *ctx, wb_kv_cache *c, int layer_idx, const wb_attn_l
         wb::launch_decode_simt(sv, len_l, th, vn, L->harmonic_n, n_seq, H, hd, o, st);
         wb::OutMap om{wb::OUT_DENSE, yd, E, sv, 0, 1};
         wb::launch_seqdot(o, n_seq, E, E, L->wo_t, E, L->bo, 0, om, st);
+        wb::launch_len_update(len_l, ids_d, n_seq, 1, 0, st);
         WB_CUDA(cudaGetLastError());
     } else {
         std::string msg;
-        int rc = wb::tc_kv_decode(L->tc, sv, len_l, c->cap, xd, n_seq, yd, &ctx->ws, ctx->dev_err,
-                                  ctx->sm_count, st, &msg);
+        int rc = wb::tc_kv_decode(L->tc, sv, len_l, c->cap, c->S, xd, n_seq, yd, c->dscratch.p, c->dscratch.n,
+                                  ctx->dev_err, st, &msg);
         if (rc != WB_OK) return fail(rc, msg);
     }
-    wb::launch_len_update(len_l, ids_d, n_seq, 1, 0, st);
-    WB_CUDA(cudaGetLastError());
-    for (int i = 0; i < n_seq; i++) c->len_host[(size_t)layer_idx * c->S + ids[i]] += 1;
+    if (ids_dev) c->len_stale = true;
+    else
+        for (int i = 0; i < n_seq; i++) c->len_host[(size_t)layer_idx * c->S + seq_ids[i]] += 1;
     if (!y_dev) {
         WB_CUDA(cudaMemcpyAsync(y, yd, (size_t)n_seq * E * sizeof(float), cudaMemcpyDeviceToHost, st));
         WB_CUDA(cudaStreamSynchronize(st));

@@ -116,12 +116,33 @@ __device__ __forceinline__ void store_out(float *p, float v) { *p = v; }
 __device__ __forceinline__ void store_out(__nv_bfloat16 *p, float v) { *p = __float2bfloat16_rn(v); }
 
 template <int DPL, class OutT>  // head dims per lane (hd <= 32*DPL)
+__device__ void attn_simt_query(const AttnSimtArgs &a, int b, int h, int q);
+
+// One warp per query (8 queries per CTA).
+template <int DPL, class OutT>
 __global__ void __launch_bounds__(256) attn_simt_kernel(AttnSimtArgs a) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
     const int q = blockIdx.x * 8 + warp;
-    const int h = blockIdx.y, b = blockIdx.z;
     if (q >= a.T) return;
-    if (a.tile_flags && !a.tile_flags[((long long)b * a.H + h) * ((a.T + 127) / 128) + q / 128]) return;
+    attn_simt_query<DPL, OutT>(a, blockIdx.z, blockIdx.y, q);
+}
+
+// Fallback over flagged 128-query tiles: one CTA per (b, h, tile); CTAs of
+// unflagged tiles exit at once, flagged ones loop their 8 warps over the
+// tile's queries.
+template <int DPL, class OutT>
+__global__ void __launch_bounds__(256) attn_simt_tiles_kernel(AttnSimtArgs a) {
+    const int n_qt = (a.T + 127) / 128;
+    const int tile = blockIdx.x % n_qt, bh = blockIdx.x / n_qt;
+    if (!a.tile_flags[(long long)bh * n_qt + tile]) return;
+    const int b = bh / a.H, h = bh - b * a.H;
+    const int warp = threadIdx.x >> 5;
+    for (int q = tile * 128 + warp; q < min(a.T, tile * 128 + 128); q += 8) attn_simt_query<DPL, OutT>(a, b, h, q);
+}
+
+template <int DPL, class OutT>
+__device__ void attn_simt_query(const AttnSimtArgs &a, int b, int h, int q) {
+    const int lane = threadIdx.x & 31;
     const long long base = wb_slot_base(a.sv, b, h);
     const float *theta = a.sv.theta + base;
     const uint8_t *bucket = a.sv.bucket + base;
@@ -203,6 +224,14 @@ __global__ void __launch_bounds__(256) attn_simt_kernel(AttnSimtArgs a) {
 template <class OutT>
 static void launch_attn_simt_t(const AttnSimtArgs &a, cudaStream_t st) {
     ProfScope ps(a.tile_flags ? "attn_simt_fallback" : "attn_simt", st);
+    if (a.tile_flags) {
+        const unsigned grid = (unsigned)((long long)a.B * a.H * ((a.T + 127) / 128));
+        if (a.hd <= 32) attn_simt_tiles_kernel<1, OutT><<<grid, 256, 0, st>>>(a);
+        else if (a.hd <= 64) attn_simt_tiles_kernel<2, OutT><<<grid, 256, 0, st>>>(a);
+        else if (a.hd <= 128) attn_simt_tiles_kernel<4, OutT><<<grid, 256, 0, st>>>(a);
+        else attn_simt_tiles_kernel<8, OutT><<<grid, 256, 0, st>>>(a);
+        return;
+    }
     dim3 grid((a.T + 7) / 8, a.H, a.B);
     if (a.hd <= 32) attn_simt_kernel<1, OutT><<<grid, 256, 0, st>>>(a);
     else if (a.hd <= 64) attn_simt_kernel<2, OutT><<<grid, 256, 0, st>>>(a);

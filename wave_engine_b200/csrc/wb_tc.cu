@@ -32,6 +32,7 @@
 // key is bucket-masked.
 #include "wb_ptx.cuh"
 #include "wb_tc.h"
+#include "wb_decode.h"
 
 #include <cudaTypedefs.h>
 
@@ -841,37 +842,18 @@ int tc_kv_prefill(const TcLayerWeights &t, const WbSeqView &sv, const float *x, 
     return tc_attention_core(t, sv, nullptr, n_seq, T, y, ws, lay, dev_err, st, msg);
 }
 
-int tc_kv_decode(const TcLayerWeights &t, const WbSeqView &sv, const int32_t *len, int cap, const float *x,
-                 int n_seq, float *y, Workspace *ws, uint32_t *dev_err, int sm_count, cudaStream_t st,
+int tc_kv_decode(const TcLayerWeights &t, const WbSeqView &sv, int32_t *len, int cap, int n_slots, const float *x,
+                 int n_seq, float *y, void *scratch, size_t scratch_bytes, uint32_t *dev_err, cudaStream_t st,
                  std::string *msg) {
-    (void)cap;
-    (void)dev_err;
-    (void)sm_count;
-    const int E = t.E, H = t.H, hd = t.hd;
-    Carve cv;
-    const size_t o_rs = cv.take<float>((size_t)n_seq * 2 * H);
-    const size_t o_th = cv.take<float>((size_t)n_seq * H);
-    const size_t o_vn = cv.take<float>((size_t)n_seq * H * hd);
-    const size_t o_o = cv.take<float>((size_t)n_seq * E);
-    if (ws_ensure(ws, cv.off, msg)) return WB_ENOMEM;
-    char *w = (char *)ws->p;
-    float *rs = (float *)(w + o_rs), *th = (float *)(w + o_th), *vn = (float *)(w + o_vn), *o = (float *)(w + o_o);
-    OutMap rm{OUT_DENSE, rs, 2LL * H, sv, 0, 1};
-    launch_seqdot(x, n_seq, E, E, t.pw.wrs_t, 2 * H, t.pw.brs, 1, rm, st);
-    launch_theta_only(rs, n_seq * H, th, st);
-    for (int h = 0; h < H; h++) {
-        OutMap vm{OUT_DENSE, vn + (size_t)h * hd, (long long)H * hd, sv, 0, 1};
-        launch_seqdot(x + (size_t)h * hd, n_seq, hd, E, t.pw.wv_t + (size_t)h * hd * hd, hd, t.pw.bv + (size_t)h * hd,
-                      0, vm, st);
+    if (t.hd > 128) {
+        *msg = "fast decode supports head_dim <= 128";
+        return WB_ENOTSUP;
     }
-    launch_decode_simt(sv, len, th, vn, t.harmonic_n, n_seq, H, hd, o, st);
-    OutMap om{OUT_DENSE, y, E, sv, 0, 1};
-    launch_seqdot(o, n_seq, E, E, t.wo_t, E, t.b_o, 0, om, st);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) {
-        *msg = std::string("decode launch failed: ") + cudaGetErrorString(e);
-        return WB_ECUDA;
-    }
+    DecodeLaunch L{sv, len, cap, n_slots, x, t.pw.wrs_t, t.pw.brs, t.pw.wv_t, t.pw.bv, t.wo_t, t.b_o, t.harmonic_n,
+                   n_seq, t.H, t.hd, t.E, y, dev_err};
+    int rc = launch_decode_fused(L, scratch, scratch_bytes, st, msg);
+    if (rc) return rc;
+    launch_len_update(len, sv.slot, n_seq, 1, 0, st);
     return WB_OK;
 }
 

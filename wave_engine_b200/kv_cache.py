@@ -53,8 +53,7 @@ class KvCache:
 
     def reset(self) -> None:
         """Empty every slot (every sequence, every layer)."""
-        for s in range(self.max_seqs):
-            self.reset_seq(s)
+        _lib.call("wb_kv_cache_reset_seq", self.handle, -1)
 
     def load(self, layer: int, seq: int, phases, values) -> None:
         """Fill one slot from phases [H][n] and values [H][n][hd]."""

@@ -68,7 +68,13 @@ class Context:
             pass
 
     def set_stream(self, cuda_stream: int | None) -> None:
-        _lib.call("wb_context_set_stream", self.handle, cuda_stream)
+        """Run later calls on this cudaStream_t handle; 0/None is CUDA's legacy
+        default stream (torch's default stream)."""
+        _lib.call("wb_context_set_stream", self.handle, cuda_stream or None)
+
+    def use_own_stream(self) -> None:
+        """Back to the context's private stream."""
+        _lib.call("wb_context_set_stream", self.handle, _lib.lib().wb_context_own_stream(self.handle))
 
     def synchronize(self) -> None:
         _lib.call("wb_context_synchronize", self.handle)
@@ -93,12 +99,12 @@ class Context:
         return out
 
     def use_torch_stream(self, *tensors):
-        """Run on torch's current stream when any argument is a CUDA tensor."""
+        """Run on torch's current stream when any argument is a CUDA tensor
+        (host-only calls keep the context's current stream)."""
         for t in tensors:
             if is_torch(t) and t.is_cuda:
                 self.set_stream(torch.cuda.current_stream(t.device).cuda_stream)
                 return
-        self.set_stream(None)
 
 
 _tls = threading.local()
