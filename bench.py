@@ -450,8 +450,47 @@ def run_reference(args):
     print(json.dumps(out), flush=True)
 
 
+def run_profile_case(args):
+    """Small single-GPU cases for ncu captures (no timing, a few hundred MB
+    on the device): 'decode' = 12 fused decode steps of one 768-dim layer,
+    32 sequences at ctx ~1100; 'prefill' = 3 tensor-path prefills of one
+    768-dim layer, 4 x 1024 tokens."""
+    import numpy as np
+    import torch
+    import wave_engine_b200 as wb
+    ctx = wb.Context(0)
+    ctx.set_stream(torch.cuda.current_stream().cuda_stream)
+    H, E, hd, C = CFG["n_head"], CFG["n_embd"], CFG["head_dim"], CFG["content_dim"]
+    w = wb.gaussian_block_attn(5, H, E, C)
+    lay = wb.AttnLayer(ctx, w)
+    g = torch.Generator(device="cuda").manual_seed(0)
+    if args.profile_case == "decode":
+        B, n = 32, 1100
+        cache = wb.KvCache(1, H, hd, max_seqs=B, max_ctx=n + 16, ctx=ctx)
+        rng = np.random.default_rng(0)
+        for b in range(B):
+            ph = np.arctan2(rng.standard_normal((H, n)), rng.standard_normal((H, n))).astype(np.float32)
+            cache.load(0, b, ph, rng.standard_normal((H, n, hd)).astype(np.float32))
+        ids = torch.arange(B, dtype=torch.int32, device="cuda")
+        x = torch.randn((12, B, E), generator=g, device="cuda")
+        y = torch.empty((B, E), device="cuda")
+        for s in range(12):
+            cache.forward_one(0, lay, x[s], ids, out=y)
+    else:
+        x = torch.randn((4, CFG["seq_len"], E), generator=g, device="cuda")
+        for _ in range(3):
+            wb.wave_attention_forward(lay, x, E // 2, ctx=ctx)
+    torch.cuda.synchronize()
+    err = ctx.take_device_error()
+    print(json.dumps({"profile_case": args.profile_case, "device_error": err}))
+    if err:
+        sys.exit(1)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--profile-case", choices=["decode", "prefill"], default=None,
+                    help="run a small case for an ncu capture instead of the benchmark")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
@@ -466,7 +505,9 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
-    if args.impl == "reference":
+    if args.profile_case:
+        run_profile_case(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

@@ -324,3 +324,34 @@ def test_tensor_path_fallback_tiles_for_unbounded_scores(ctx):
     assert r.passed, str(r)
     assert "attn_simt_fallback" in rep
     assert ctx.take_device_error() == 0
+
+
+def test_decode_batches_of_different_sizes_share_scratch(ctx):
+    """Decode calls with 3, then 1, then 2 sequences on one cache: the
+    scratch tickets must stay zeroed between calls of different batch."""
+    import wave_engine_b200 as wb
+    H, E, d = 12, 768, 64
+    w = wb.gaussian_block_attn(8, H, E, 0)
+    wp = w.packed()
+    g = np.random.default_rng(2)
+    cache = wb.KvCache(1, H, d, max_seqs=4, max_ctx=1400, ctx=ctx)
+    states = {}
+    for sidx in range(4):
+        n = 600 + 200 * sidx
+        ph = np.arctan2(g.standard_normal((H, n)), g.standard_normal((H, n))).astype(np.float32)
+        vv = g.standard_normal((H, n, d)).astype(np.float32)
+        cache.load(0, sidx, ph, vv)
+        st = oracle.KvState(H, d, 1400)
+        st.phases[:, :n] = ph
+        st.values[:, :n] = vv
+        st.buckets[:, :n] = oracle.phase_to_bucket(ph)
+        st.n.value = n
+        states[sidx] = st
+    for ids in ([0, 2, 3], [1], [3, 0], [2, 1, 0, 3]):
+        x = g.standard_normal((len(ids), E)).astype(np.float32)
+        y = cache.forward_one(0, w, x, np.array(ids, np.int32))
+        for j, sidx in enumerate(ids):
+            oy = oracle.kv_decode(wp, x[j], states[sidx])
+            r = check(f"ids {ids} seq {sidx}", y[j], oy, TENSOR_TOL)
+            assert r.passed, str(r)
+    assert ctx.take_device_error() == 0

@@ -1,34 +1,40 @@
-// wb_decode.cu -- fused KV-cache decode step (src/common/kv_cache.rs:263-335).
+// wb_decode.cu -- KV-cache decode step (src/common/kv_cache.rs:263-335).
 //
-// One launch per layer and decode step.  Grid (split, head, sequence):
+// Two launches per layer and decode step.
+//
+// decode_attn_kernel, grid (split, head, sequence), 512 keys per CTA:
 //   * every CTA projects the new position's phase theta_q = atan2(s, r)
 //     (kv_cache.rs:271) from the x row, then scans its split of the cached
-//     keys: the bucket byte and phase of every key (coalesced), the score
-//     cos(n (theta_q - theta_k)) only for keys in buckets b-1..b+1 or at the
-//     previous position (kv_cache.rs:285-298), and the fp32 value row only of
-//     those keys, streamed with 128-bit loads by groups of lanes.
+//     keys: the bucket byte and phase of every key (coalesced, issued up
+//     front), the score cos(n (theta_q - theta_k)) only for keys in buckets
+//     b-1..b+1 or at the previous position (kv_cache.rs:285-298), and the
+//     fp32 value row only of those keys, streamed with 128-bit loads by
+//     groups of lanes;
 //   * decode scores never exceed the self score 1.0 (kv_cache.rs:294), so the
 //     softmax uses the fixed shift 1: p = exp(s - 1) exactly as the
 //     reference's max-subtraction, and split partials (sum p, sum p v) merge
-//     by plain addition, in split order (deterministic).
-//   * the last CTA of a (sequence, head) -- an atomic ticket in scratch --
-//     merges the partials, adds the self term (p = 1, the new value
-//     v = Wv x_h + b), normalises, appends (phase, bucket, value) at
-//     position n, and multiplies its 64-wide slice into out_proj; the last
-//     head of a sequence sums the slices (head order) plus the bias into y.
-//     The cached length is advanced by a separate launch afterwards: a CTA
-//     of this launch that starts late must still see the old length.
-// Scratch: per (sequence, head, split) partials, per (sequence, head) slices
-// of y, and two ticket arrays that the kernel returns to zero.
+//     by plain addition, in split order (deterministic);
+//   * split 0 also computes the new value v = Wv x_h + b (kv_cache.rs:272-277);
+//     the last CTA of a (sequence, head) -- an atomic ticket in scratch --
+//     merges the partials, adds the self term (p = 1, v), normalises into
+//     the merged head output o, and appends (phase, bucket, value) at
+//     position n.
+// The caller then runs out_proj (kv_cache.rs:330-335) on the merged outputs
+// o and advances the cached lengths in a separate launch: a CTA of this
+// launch that starts late must still see the old length.
+// Scratch: partials, new values, merged outputs and a ticket array that the
+// kernel returns to zero.
 #include "wb_decode.h"
 #include "wb_ptx.cuh"
 
+#include <algorithm>
+
 namespace wb {
 
-static constexpr int DEC_THREADS = 256;
+static constexpr int DEC_THREADS = 128;
 static constexpr int DEC_WARPS = DEC_THREADS / 32;
-static constexpr int DEC_KEYS_PER_WARP = 256;
-static constexpr int DEC_CHUNK = DEC_WARPS * DEC_KEYS_PER_WARP;  // keys per CTA (2048)
+static constexpr int DEC_KEYS_PER_WARP = 128;
+static constexpr int DEC_CHUNK = DEC_WARPS * DEC_KEYS_PER_WARP;  // keys per CTA (512)
 
 struct DecodeArgs {
     WbSeqView sv;             // cache view of the layer (slot = seq ids)
@@ -41,10 +47,9 @@ struct DecodeArgs {
     const float *hn;          // [H]
     int n_seq, H, hd, E, nsplit;
     float *part;              // [n_seq][H][nsplit][hd + 1]
-    float *yh;                // [n_seq][H][E]
+    float *vnew;              // [n_seq][H][hd]
+    float *o;                 // [n_seq][E] merged, normalised head outputs
     unsigned int *ticket;     // [n_seq][H]
-    unsigned int *hticket;    // [n_seq]
-    float *y;                 // [n_seq][E]
     uint32_t *dev_err;
 };
 
@@ -85,7 +90,7 @@ __device__ __forceinline__ int lanes_per_key(int hd) {
 }
 
 template <int VEC>
-__global__ void __launch_bounds__(DEC_THREADS) decode_fused_kernel(DecodeArgs a) {
+__global__ void __launch_bounds__(DEC_THREADS) decode_attn_kernel(DecodeArgs a) {
     extern __shared__ float dsm[];
     const int split = blockIdx.x, h = blockIdx.y, i = blockIdx.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -117,8 +122,7 @@ __global__ void __launch_bounds__(DEC_THREADS) decode_fused_kernel(DecodeArgs a)
     const uint8_t *bucket = a.sv.bucket + base;
     const float *V = a.sv.v + base * hd;
     const int k0 = split * DEC_CHUNK + warp * DEC_KEYS_PER_WARP;
-    // issue this warp's key loads first (bucket byte + phase of every key;
-    // kv_cache.rs:285-292 reads both for the keys it scores)
+    // this warp's key loads go out first (bucket byte + phase of every key)
     constexpr int KR = DEC_KEYS_PER_WARP / 32;
     uint8_t kb[KR];
     float kth[KR];
@@ -129,28 +133,46 @@ __global__ void __launch_bounds__(DEC_THREADS) decode_fused_kernel(DecodeArgs a)
         kth[c] = k < n ? __ldg(theta + k) : 0.0f;
     }
 
-    // x row; theta_q (kv_cache.rs:271, tree-summed) and, in the merging CTA,
-    // the new value v = Wv x_h + b (kv_cache.rs:272-277)
+    // x row; theta_q (kv_cache.rs:271, tree-summed); split 0: the new value
+    // loads are issued in batches of 8 before any is used (each loop below
+    // would otherwise pay one memory round trip per iteration)
     const float *xr = a.x + (long long)i * E;
-    for (int j = tid; j < E; j += DEC_THREADS) xs[j] = __ldg(xr + j);
-    __syncthreads();
     float r = 0.0f, s = 0.0f;
-    for (int j = tid; j < E; j += DEC_THREADS) {
-        const float2 w = __ldg(reinterpret_cast<const float2 *>(a.wrs_t + ((long long)j * a.H + h) * 2));
-        r = fmaf(w.x, xs[j], r);
-        s = fmaf(w.y, xs[j], s);
+    for (int j0 = 0; j0 < E; j0 += 8 * DEC_THREADS) {
+        float xv[8];
+        float2 wv2[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            const int j = j0 + u * DEC_THREADS + tid;
+            xv[u] = j < E ? __ldg(xr + j) : 0.0f;
+            wv2[u] = j < E ? __ldg(reinterpret_cast<const float2 *>(a.wrs_t + ((long long)j * a.H + h) * 2))
+                           : make_float2(0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            const int j = j0 + u * DEC_THREADS + tid;
+            if (j < E) xs[j] = xv[u];
+            r = fmaf(wv2[u].x, xv[u], r);
+            s = fmaf(wv2[u].y, xv[u], s);
+        }
     }
-    // new value: P parts of hd/P inputs per output, P = threads / hd
-    const int P = DEC_THREADS / hd;
+    __syncthreads();
+    const int P = DEC_THREADS / hd;  // parts of hd/P inputs per new-value output
     const int vd = tid % hd, vq = tid / hd;
     const int kper = (hd + P - 1) / P;
     float vpar = 0.0f;
-    if (vq < P) {  // every CTA: the merging split is only known at the end
+    if (split == 0 && vq < P) {
         const float *xh = xs + h * hd;
         const float *wv = a.wv_t + (long long)h * hd * hd + vd;
         const int j0 = vq * kper, j1 = min(hd, j0 + kper);
-#pragma unroll 8
-        for (int j = j0; j < j1; j++) vpar = fmaf(__ldg(wv + (long long)j * hd), xh[j], vpar);
+        for (int jb = j0; jb < j1; jb += 16) {
+            float wl[16];
+#pragma unroll
+            for (int u = 0; u < 16; u++) wl[u] = jb + u < j1 ? __ldg(wv + (long long)(jb + u) * hd) : 0.0f;
+#pragma unroll
+            for (int u = 0; u < 16; u++)
+                if (jb + u < j1) vpar = fmaf(wl[u], xh[jb + u], vpar);
+        }
     }
     vpart[tid] = vpar;
 #pragma unroll
@@ -173,6 +195,12 @@ __global__ void __launch_bounds__(DEC_THREADS) decode_fused_kernel(DecodeArgs a)
     const int qb = phase_to_bucket(thq);
     const uint32_t amask = allowed_bucket_mask(qb);
     const float hn = a.hn[h];
+    float *vnew = a.vnew + ((long long)i * a.H + h) * hd;
+    if (split == 0 && tid < hd) {  // hd <= DEC_THREADS (checked at launch)
+        float v = a.bv[h * hd + tid];
+        for (int q = 0; q < P; q++) v += vpart[q * hd + tid];
+        vnew[tid] = v;
+    }
 
     // mask, score, p = exp(s - 1); compact (index, p) per warp
     int m = 0;
@@ -218,7 +246,6 @@ __global__ void __launch_bounds__(DEC_THREADS) decode_fused_kernel(DecodeArgs a)
             if (j < m && vact) VecT<VEC>::fma(acc, my_p[j], V + (long long)my_idx[j] * hd + vi * VEC);
         }
     }
-    // reduce over the key slots of the warp (lanes with the same vi)
     for (int o = G; o < 32; o <<= 1)
 #pragma unroll
         for (int u = 0; u < VEC; u++) acc[u] += __shfl_xor_sync(0xffffffffu, acc[u], o);
@@ -231,7 +258,7 @@ __global__ void __launch_bounds__(DEC_THREADS) decode_fused_kernel(DecodeArgs a)
     if (lane == 0) lpart[warp] = lsum;
     __syncthreads();
 
-    float *o_h = opart;  // merged head output [hd] (reuses warp 0's slot)
+    float od = 0.0f, lall = 0.0f;
     if (n_act > 1) {
         // several splits: partial -> scratch, the last split merges
         float *pdst = a.part + (((long long)i * a.H + h) * a.nsplit + split) * (hd + 1);
@@ -256,102 +283,213 @@ __global__ void __launch_bounds__(DEC_THREADS) decode_fused_kernel(DecodeArgs a)
         __syncthreads();
         if (!s_flag) return;
         __threadfence();
-    }
-    // ---- merge (i, h): sum partials, self term, normalise, append ----
-    {
-        const float *pp = a.part + ((long long)i * a.H + h) * a.nsplit * (hd + 1);
-        float od = 0.0f, vn = 0.0f, lall = 0.0f;
-        const int d = tid;
-        if (d < hd) {
-            if (n_act > 1) {
-                for (int sp = 0; sp < n_act; sp++) {
-                    od += __ldcg(pp + (long long)sp * (hd + 1) + d);
-                    lall += __ldcg(pp + (long long)sp * (hd + 1) + hd);
-                }
-            } else {
+        // merge the split partials in split order (hd <= DEC_THREADS: one
+        // column per thread); the loads of 8 splits go out together
+        if (tid < hd) {
+            const float *pp = a.part + ((long long)i * a.H + h) * a.nsplit * (hd + 1);
+            for (int sp0 = 0; sp0 < n_act; sp0 += 8) {
+                float ov[8], lv[8];
 #pragma unroll
-                for (int w = 0; w < DEC_WARPS; w++) {
-                    od += opart[w * hd + d];
-                    lall += lpart[w];
+                for (int u = 0; u < 8; u++) {
+                    const int sp = sp0 + u;
+                    ov[u] = sp < n_act ? __ldcg(pp + (long long)sp * (hd + 1) + tid) : 0.0f;
+                    lv[u] = sp < n_act ? __ldcg(pp + (long long)sp * (hd + 1) + hd) : 0.0f;
+                }
+#pragma unroll
+                for (int u = 0; u < 8; u++) {
+                    od += ov[u];
+                    lall += lv[u];
                 }
             }
-            vn = a.bv[h * hd + d];
-            for (int q = 0; q < P; q++) vn += vpart[q * hd + d];
         }
-        __syncthreads();  // opart is overwritten below
-        if (d < hd) {
-            // self term p = exp(1 - 1) = 1 (kv_cache.rs:294, :318)
-            o_h[d] = (od + vn) / (lall + 1.0f);
-            a.sv.v[(base + n) * hd + d] = vn;  // append value (kv_cache.rs:324)
+    } else if (tid < hd) {
+#pragma unroll
+        for (int w = 0; w < DEC_WARPS; w++) {
+            od += opart[w * hd + tid];
+            lall += lpart[w];
         }
     }
+    // ---- merge (i, h): self term p = exp(1 - 1) = 1 (kv_cache.rs:294, :318),
+    // normalise, append (kv_cache.rs:323-326)
+    if (tid < hd) {
+        const float vn = __ldcg(vnew + tid);
+        a.o[(long long)i * E + (long long)h * hd + tid] = (od + vn) / (lall + 1.0f);
+        a.sv.v[(base + n) * hd + tid] = vn;
+    }
     if (tid == 0) {
-        a.sv.theta[base + n] = thq;  // append phase and bucket (kv_cache.rs:323-326)
+        a.sv.theta[base + n] = thq;
         a.sv.bucket[base + n] = (uint8_t)qb;
         if (n_act > 1) a.ticket[(long long)i * a.H + h] = 0u;
     }
-    __syncthreads();
-    // this head's slice of out_proj: yh[c] = sum_d Wo[c][h*hd + d] o_h[d]
-    float *yh = a.yh + ((long long)i * a.H + h) * E;
-    const float *wo = a.wo_t + (long long)h * hd * E;
-    for (int c0 = tid; c0 < E; c0 += DEC_THREADS * 4) {
-        float acc2[4];
+}
+
+// out_proj of the step's rows (kv_cache.rs:330-335), y = o W_o^T + b, and
+// the length update.  Block = 8 rows x 32 columns; its 256 threads are 8
+// column quads x 32 K slices: thread (slice, quad) accumulates 8 rows x 4
+// columns over its slice (weights as float4 straight from global, o rows
+// staged in shared memory), then the 32 slice partials of every output are
+// summed in slice order.  Every load of a phase is issued before any is
+// used.  Block (0, 0) advances the lengths: every attention CTA of the step
+// (the previous launch) has read them.
+static constexpr int OUT_THREADS = 256;
+static constexpr int OUT_R = 8;                    // rows per block
+static constexpr int OUT_C = 32;                   // columns per block
+static constexpr int OUT_Q = OUT_C / 4;            // column quads
+static constexpr int OUT_S = OUT_THREADS / OUT_Q;  // K slices (32)
+static constexpr int OUT_KC = 2048;                // columns of o staged per pass (64 KB)
+
+struct DecodeOutArgs {
+    const float *o;     // [n][E]
+    const float *wo_t;  // [E(in)][E(out)]
+    const float *bo;    // [E]
+    float *y;           // [n][E]
+    int n, E;
+    int32_t *len;
+    const int32_t *slot;
+    int n_slots;
+};
+
+__global__ void __launch_bounds__(OUT_THREADS) decode_out_kernel(DecodeOutArgs a) {
+    extern __shared__ float osm[];
+    const int E = a.E, n = a.n;
+    const int c0 = blockIdx.x * OUT_C, r0 = blockIdx.y * OUT_R;
+    const int tid = threadIdx.x, ks = tid / OUT_Q, cq = tid % OUT_Q;
+    const int kc = min(E, OUT_KC);
+    float *os = osm;                 // [OUT_R][kc]
+    float *red = osm + OUT_R * kc;   // [OUT_S][OUT_R][OUT_C]
+    const int c = c0 + cq * 4;
+    const bool cvec = c + 3 < E && (E % 4 == 0);
+    float acc[OUT_R][4];
 #pragma unroll
-        for (int q = 0; q < 4; q++) acc2[q] = 0.0f;
-#pragma unroll 8
-        for (int dd = 0; dd < hd; dd++) {
-            const float od = o_h[dd];
-            const float *wr = wo + (long long)dd * E;
+    for (int r = 0; r < OUT_R; r++)
 #pragma unroll
-            for (int q = 0; q < 4; q++) {
-                const int c = c0 + q * DEC_THREADS;
-                if (c < E) acc2[q] = fmaf(__ldg(wr + c), od, acc2[q]);
+        for (int u = 0; u < 4; u++) acc[r][u] = 0.0f;
+    for (int kc0 = 0; kc0 < E; kc0 += kc) {
+        const int kn = min(kc, E - kc0);
+        __syncthreads();
+        // stage o rows r0..r0+7, columns kc0..kc0+kn (one batch per thread)
+        const int tot = OUT_R * kn;
+        for (int e0 = 0; e0 < tot; e0 += 16 * OUT_THREADS) {
+            float v[16];
+#pragma unroll
+            for (int u = 0; u < 16; u++) {
+                const int e = e0 + u * OUT_THREADS + tid;
+                const int r = e / kn;
+                v[u] = (e < tot && r0 + r < n) ? __ldcg(a.o + (long long)(r0 + r) * E + kc0 + (e - r * kn)) : 0.0f;
+            }
+#pragma unroll
+            for (int u = 0; u < 16; u++) {
+                const int e = e0 + u * OUT_THREADS + tid;
+                if (e < tot) os[(e / kn) * kc + (e % kn)] = v[u];
             }
         }
+        __syncthreads();
+        const int kslice = (kn + OUT_S - 1) / OUT_S;
+        const int k0 = ks * kslice, k1 = min(kn, k0 + kslice);
+        for (int kb = k0; kb < k1; kb += 12) {
+            float4 w[12];
 #pragma unroll
-        for (int q = 0; q < 4; q++) {
-            const int c = c0 + q * DEC_THREADS;
-            if (c < E) yh[c] = acc2[q];
+            for (int u = 0; u < 12; u++) {
+                const int k = kb + u;
+                w[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (k < k1) {
+                    const float *src = a.wo_t + (long long)(kc0 + k) * E + c;
+                    if (cvec) w[u] = __ldg(reinterpret_cast<const float4 *>(src));
+                    else {
+                        if (c < E) w[u].x = __ldg(src);
+                        if (c + 1 < E) w[u].y = __ldg(src + 1);
+                        if (c + 2 < E) w[u].z = __ldg(src + 2);
+                        if (c + 3 < E) w[u].w = __ldg(src + 3);
+                    }
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 12; u++) {
+                const int k = kb + u;
+                if (k >= k1) break;
+#pragma unroll
+                for (int r = 0; r < OUT_R; r++) {
+                    const float ov = os[r * kc + k];
+                    acc[r][0] = fmaf(w[u].x, ov, acc[r][0]);
+                    acc[r][1] = fmaf(w[u].y, ov, acc[r][1]);
+                    acc[r][2] = fmaf(w[u].z, ov, acc[r][2]);
+                    acc[r][3] = fmaf(w[u].w, ov, acc[r][3]);
+                }
+            }
         }
     }
-    __threadfence();
+#pragma unroll
+    for (int r = 0; r < OUT_R; r++)
+        *reinterpret_cast<float4 *>(red + (ks * OUT_R + r) * OUT_C + cq * 4) =
+            make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
     __syncthreads();
-    if (tid == 0) {
-        const unsigned t = atomicAdd(a.hticket + i, 1u);
-        s_flag = (t == (unsigned)(a.H - 1));
-    }
-    __syncthreads();
-    if (!s_flag) return;
-    __threadfence();
-    // last head of sequence i: y = b + sum_h yh (head order)
-    const float *yall = a.yh + (long long)i * a.H * E;
-    for (int c = tid; c < E; c += DEC_THREADS) {
+    {
+        const int r = tid / OUT_C, cc = tid % OUT_C;  // one output per thread
         float v = 0.0f;
 #pragma unroll 8
-        for (int hh = 0; hh < a.H; hh++) v += __ldcg(yall + (long long)hh * E + c);
-        a.y[(long long)i * E + c] = v + a.bo[c];
+        for (int q = 0; q < OUT_S; q++) v += red[(q * OUT_R + r) * OUT_C + cc];
+        if (r0 + r < n && c0 + cc < E) a.y[(long long)(r0 + r) * E + c0 + cc] = v + a.bo[c0 + cc];
     }
-    if (tid == 0) a.hticket[i] = 0u;
+    if (blockIdx.x == 0 && blockIdx.y == 0)
+        for (int i = tid; i < n; i += OUT_THREADS) {
+            const int slot = a.slot ? a.slot[i] : i;
+            if (slot >= 0 && slot < a.n_slots) a.len[slot] += 1;
+        }
+}
+
+int launch_decode_out(const float *o, const float *wo_t, const float *bo, float *y, int n, int E, int32_t *len,
+                      const int32_t *slot, int n_slots, cudaStream_t st, std::string *msg) {
+    ProfScope ps("decode_out", st);
+    DecodeOutArgs a{o, wo_t, bo, y, n, E, len, slot, n_slots};
+    const size_t smem = sizeof(float) * ((size_t)OUT_R * std::min(E, OUT_KC) + OUT_S * OUT_R * OUT_C);
+    cudaFuncSetAttribute(decode_out_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    dim3 grid((E + OUT_C - 1) / OUT_C, (n + OUT_R - 1) / OUT_R);
+    decode_out_kernel<<<grid, OUT_THREADS, smem, st>>>(a);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        *msg = std::string("decode out launch failed: ") + cudaGetErrorString(e);
+        return WB_ECUDA;
+    }
+    return WB_OK;
+}
+
+struct DecodeScratch {
+    size_t part, vnew, o, ticket, end;
+};
+static DecodeScratch decode_scratch_layout(int n_seq, int H, int hd, int E, int cap) {
+    const int nsplit = (cap + DEC_CHUNK - 1) / DEC_CHUNK;
+    Carve c;
+    DecodeScratch d;
+    d.part = c.take<float>((size_t)n_seq * H * nsplit * (hd + 1));
+    d.vnew = c.take<float>((size_t)n_seq * H * hd);
+    d.o = c.take<float>((size_t)n_seq * E);
+    d.ticket = c.take<unsigned int>((size_t)n_seq * H);
+    d.end = c.off;
+    return d;
 }
 
 size_t decode_scratch_bytes(int n_seq, int H, int hd, int E, int cap) {
-    const int nsplit = (cap + DEC_CHUNK - 1) / DEC_CHUNK;
-    Carve c;
-    c.take<float>((size_t)n_seq * H * nsplit * (hd + 1));
-    c.take<float>((size_t)n_seq * H * E);
-    c.take<unsigned int>((size_t)n_seq * H);
-    c.take<unsigned int>((size_t)n_seq);
-    return c.off;
+    return decode_scratch_layout(n_seq, H, hd, E, cap).end;
 }
 
-int launch_decode_fused(const DecodeLaunch &L, void *scratch, size_t scratch_bytes, cudaStream_t st,
-                        std::string *msg) {
+int launch_decode_attn(const DecodeLaunch &L, void *scratch, size_t scratch_bytes, float **o_out,
+                       cudaStream_t st, std::string *msg) {
     const int nsplit = (L.cap + DEC_CHUNK - 1) / DEC_CHUNK;
-    if (scratch_bytes < decode_scratch_bytes(L.n_seq, L.H, L.hd, L.E, L.cap)) {
+    // laid out for the cache's slot count (not this call's n_seq) so the
+    // zeroed tickets stay at fixed offsets whatever the batch of the call
+    if (L.n_seq > L.n_slots) {
+        *msg = "more sequences than cache slots";
+        return WB_EINVAL;
+    }
+    const DecodeScratch lay = decode_scratch_layout(L.n_slots, L.H, L.hd, L.E, L.cap);
+    if (scratch_bytes < lay.end) {
         *msg = "decode scratch too small";
         return WB_EINVAL;
     }
-    Carve c;
+    if (L.hd > DEC_THREADS) {
+        *msg = "decode supports head_dim <= 128";
+        return WB_ENOTSUP;
+    }
     char *s = (char *)scratch;
     DecodeArgs a;
     a.sv = L.sv;
@@ -371,25 +509,27 @@ int launch_decode_fused(const DecodeLaunch &L, void *scratch, size_t scratch_byt
     a.hd = L.hd;
     a.E = L.E;
     a.nsplit = nsplit;
-    a.part = (float *)(s + c.take<float>((size_t)L.n_seq * L.H * nsplit * (L.hd + 1)));
-    a.yh = (float *)(s + c.take<float>((size_t)L.n_seq * L.H * L.E));
-    a.ticket = (unsigned int *)(s + c.take<unsigned int>((size_t)L.n_seq * L.H));
-    a.hticket = (unsigned int *)(s + c.take<unsigned int>((size_t)L.n_seq));
-    a.y = L.y;
+    a.part = (float *)(s + lay.part);
+    a.vnew = (float *)(s + lay.vnew);
+    a.o = (float *)(s + lay.o);
+    *o_out = a.o;
+    a.ticket = (unsigned int *)(s + lay.ticket);
     a.dev_err = L.dev_err;
     const size_t smem = sizeof(float) * ((size_t)L.E + 2 * DEC_WARPS * DEC_KEYS_PER_WARP + DEC_WARPS * L.hd +
                                          DEC_WARPS + 2 * DEC_WARPS + DEC_THREADS);
     dim3 grid(nsplit, L.H, L.n_seq);
-    ProfScope ps("decode_fused", st);
-    if (L.hd % 4 == 0) {
-        cudaFuncSetAttribute(decode_fused_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        decode_fused_kernel<4><<<grid, DEC_THREADS, smem, st>>>(a);
-    } else if (L.hd % 2 == 0) {
-        cudaFuncSetAttribute(decode_fused_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        decode_fused_kernel<2><<<grid, DEC_THREADS, smem, st>>>(a);
-    } else {
-        cudaFuncSetAttribute(decode_fused_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        decode_fused_kernel<1><<<grid, DEC_THREADS, smem, st>>>(a);
+    {
+        ProfScope ps("decode_attn", st);
+        if (L.hd % 4 == 0) {
+            cudaFuncSetAttribute(decode_attn_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            decode_attn_kernel<4><<<grid, DEC_THREADS, smem, st>>>(a);
+        } else if (L.hd % 2 == 0) {
+            cudaFuncSetAttribute(decode_attn_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            decode_attn_kernel<2><<<grid, DEC_THREADS, smem, st>>>(a);
+        } else {
+            cudaFuncSetAttribute(decode_attn_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            decode_attn_kernel<1><<<grid, DEC_THREADS, smem, st>>>(a);
+        }
     }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {

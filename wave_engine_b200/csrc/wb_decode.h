@@ -12,7 +12,6 @@ struct DecodeLaunch {
     const float *x;
     const float *wrs_t, *brs, *wv_t, *bv, *wo_t, *bo, *hn;
     int n_seq, H, hd, E;
-    float *y;
     uint32_t *dev_err;
 };
 
@@ -20,7 +19,15 @@ struct DecodeLaunch {
 // ticket arrays inside must be zero before the first launch (the kernel
 // leaves them zero).
 size_t decode_scratch_bytes(int n_seq, int H, int hd, int E, int cap);
-int launch_decode_fused(const DecodeLaunch &L, void *scratch, size_t scratch_bytes, cudaStream_t st,
-                        std::string *msg);
+// Attention part of one decode step: writes the merged, normalised head
+// outputs o [n_seq][E] (inside scratch, returned in *o_out) and appends the
+// new position to every slot; out_proj and the length update follow.
+int launch_decode_attn(const DecodeLaunch &L, void *scratch, size_t scratch_bytes, float **o_out,
+                       cudaStream_t st, std::string *msg);
+
+// y = o W_o^T + b for the step's n rows (wo_t input-major), then
+// len[slot[i]] += 1 for every row.
+int launch_decode_out(const float *o, const float *wo_t, const float *bo, float *y, int n, int E, int32_t *len,
+                      const int32_t *slot, int n_slots, cudaStream_t st, std::string *msg);
 
 }  // namespace wb

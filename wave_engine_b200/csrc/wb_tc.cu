@@ -850,11 +850,12 @@ int tc_kv_decode(const TcLayerWeights &t, const WbSeqView &sv, int32_t *len, int
         return WB_ENOTSUP;
     }
     DecodeLaunch L{sv, len, cap, n_slots, x, t.pw.wrs_t, t.pw.brs, t.pw.wv_t, t.pw.bv, t.wo_t, t.b_o, t.harmonic_n,
-                   n_seq, t.H, t.hd, t.E, y, dev_err};
-    int rc = launch_decode_fused(L, scratch, scratch_bytes, st, msg);
+                   n_seq, t.H, t.hd, t.E, dev_err};
+    float *o = nullptr;
+    int rc = launch_decode_attn(L, scratch, scratch_bytes, &o, st, msg);
     if (rc) return rc;
-    launch_len_update(len, sv.slot, n_seq, 1, 0, st);
-    return WB_OK;
+    // out_proj (fp32) and lengths += 1
+    return launch_decode_out(o, t.wo_t, t.b_o, y, n_seq, t.E, len, sv.slot, n_slots, st, msg);
 }
 
 }  // namespace wb
