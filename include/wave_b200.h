@@ -198,6 +198,27 @@ WB_API int wb_kv_prefill(wb_context *ctx, wb_kv_cache *cache, int layer_idx, con
 WB_API int wb_kv_decode(wb_context *ctx, wb_kv_cache *cache, int layer_idx, const wb_attn_layer *layer,
                  const int32_t *seq_ids, int n_seq, const float *x, int flags, float *y);
 
+/* Size of the static device array behind wb_kv_decode_noalloc (4 MiB). */
+#define WB_NOALLOC_SCRATCH_BYTES (4u << 20)
+
+/* wb_kv_decode on the tensor path without allocating any device memory.
+ * No counterpart in the reference: it exists for callers that may not
+ * allocate at decode time (a server that reserves its device memory at
+ * start-up and forbids allocation per request, or decoding inside CUDA
+ * stream capture, where cudaMalloc is not allowed).  The kernels' scratch
+ * lives in one static device array of WB_NOALLOC_SCRATCH_BYTES per GPU,
+ * held until the process exits; a cache whose decode scratch
+ * (slots x heads x ceil(max_ctx/512) partial rows, plus per-slot values and
+ * outputs) exceeds it is rejected with WB_EINVAL.  seq_ids, x and y must be
+ * DEVICE pointers (nothing is staged) and are used as with device ids in
+ * wb_kv_decode.  The first call on each device resolves the array's device
+ * address (cudaGetSymbolAddress) and must come before any stream capture.
+ * All calls share the array: calls that overlap on the GPU race and must
+ * not be issued; the counters that must start at zero are cleared by each
+ * call. */
+WB_API int wb_kv_decode_noalloc(wb_context *ctx, wb_kv_cache *cache, int layer_idx, const wb_attn_layer *layer,
+                                const int32_t *seq_ids, int n_seq, const float *x, float *y);
+
 #ifdef __cplusplus
 }
 #endif

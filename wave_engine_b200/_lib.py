@@ -51,6 +51,7 @@ SIGNATURES = {
     "wb_kv_cache_read": (C.c_int, [_VP, _VP, C.c_int, C.c_int, _VP, _VP, _VP]),
     "wb_kv_prefill": (C.c_int, [_VP, _VP, C.c_int, _VP, _VP, C.c_int, _VP, C.c_int, C.c_int, _VP]),
     "wb_kv_decode": (C.c_int, [_VP, _VP, C.c_int, _VP, _VP, C.c_int, _VP, C.c_int, _VP]),
+    "wb_kv_decode_noalloc": (C.c_int, [_VP, _VP, C.c_int, _VP, _VP, C.c_int, _VP, _VP]),
     # include/wave_b200_testing.h
     "wb_test_gemm_bf16": (C.c_int, [_VP, _VP, _VP, _VP, _VP, C.c_int, C.c_int, C.c_int]),
     "wb_test_gemm_tf32": (C.c_int, [_VP, _VP, _VP, _VP, _VP, C.c_int, C.c_int, C.c_int]),

@@ -10,6 +10,7 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -782,3 +783,82 @@ int wb_test_gemm_tf32(wb_context *ctx, const float *A, const float *B, const flo
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// wb_kv_decode_noalloc: the tensor-path decode step with its scratch in a
+// file-scope device array instead of memory the library allocates.
+//
+// Who needs it: callers that may not allocate device memory at the point
+// where they decode -- a serving process that reserves its whole device
+// budget at start-up and forbids allocation on the request path, or code
+// that decodes inside CUDA stream capture, where cudaMalloc is not
+// permitted.  Everything else the call touches (weights, cache, x, y, seq
+// ids) was allocated by the caller beforehand.
+//
+// The array below is WB_NOALLOC_SCRATCH_BYTES on every GPU that loads this
+// library, held until the process exits.  Host code cannot use the name
+// g_wb_noalloc_scratch as a device address (on the host it is only a
+// stand-in symbol), so the first call on each device looks up the array's
+// device address with cudaGetSymbolAddress, with that device current, and
+// keeps it; make that first call before any stream capture.  Every call
+// shares the one array and it keeps the last call's contents: the ticket
+// counters the kernels rely on are cleared at the start of each call, and
+// calls that overlap on the GPU (two streams, two contexts on the same
+// device) race on the array and must not be issued.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) unsigned char g_wb_noalloc_scratch[WB_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void *g_noalloc_addr[kMaxDevices] = {};
+
+// Device address of the array on `device` (which must be current).
+int noalloc_scratch_address(int device, void **out) {
+    if (device < 0 || device >= kMaxDevices) return fail(WB_EINVAL, "device ordinal out of range");
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_addr[device]) {
+        void *p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_wb_noalloc_scratch);
+        if (e != cudaSuccess || !p)
+            return fail(WB_ECUDA, std::string("cudaGetSymbolAddress of the static decode scratch failed: ") +
+                                      cudaGetErrorString(e));
+        g_noalloc_addr[device] = p;
+    }
+    *out = g_noalloc_addr[device];
+    return WB_OK;
+}
+}  // namespace
+
+extern "C" int wb_kv_decode_noalloc(wb_context *ctx, wb_kv_cache *c, int layer_idx, const wb_attn_layer *L,
+                                    const int32_t *seq_ids, int n_seq, const float *x, float *y) {
+    if (!ctx || !c || !L || !seq_ids || !x || !y) return fail(WB_EINVAL, "NULL argument");
+    if (c->ctx != ctx || L->ctx != ctx) return fail(WB_EINVAL, "objects belong to another context");
+    if (layer_idx < 0 || layer_idx >= c->L) return fail(WB_EINVAL, "layer out of range");
+    if (L->H != c->H || L->hd != c->hd) return fail(WB_EINVAL, "layer shape does not match cache");
+    if (n_seq < 0 || n_seq > c->S) return fail(WB_EINVAL, "n_seq out of range for the cache");
+    if (n_seq == 0) return WB_OK;
+    if (!is_device_ptr(seq_ids) || !is_device_ptr(x) || !is_device_ptr(y))
+        return fail(WB_EINVAL, "wb_kv_decode_noalloc needs device pointers for seq_ids, x and y (no staging)");
+    const size_t need = wb::decode_scratch_bytes(c->S, c->H, c->hd, c->H * c->hd, c->cap);
+    if (need > WB_NOALLOC_SCRATCH_BYTES)
+        return fail(WB_EINVAL, "decode scratch for this cache needs " + std::to_string(need) +
+                                   " bytes, above the static limit of " +
+                                   std::to_string((size_t)WB_NOALLOC_SCRATCH_BYTES) +
+                                   " (fewer slots or a smaller capacity fit; wb_kv_decode has no limit)");
+    DeviceGuard g(ctx->device);
+    if (!g.ok) return fail(WB_ECUDA, "cudaSetDevice failed");
+    void *scratch = nullptr;
+    WB_TRY(noalloc_scratch_address(ctx->device, &scratch));
+    cudaStream_t st = ctx->stream;
+    size_t t_off = 0, t_bytes = 0;
+    wb::decode_scratch_tickets(c->S, c->H, c->hd, c->H * c->hd, c->cap, &t_off, &t_bytes);
+    WB_CUDA(cudaMemsetAsync((char *)scratch + t_off, 0, t_bytes, st));
+    WbSeqView sv = c->view(layer_idx, seq_ids);
+    std::string msg;
+    int rc = wb::tc_kv_decode(L->tc, sv, c->len + (size_t)layer_idx * c->S, c->cap, c->S, x, n_seq, y, scratch,
+                              WB_NOALLOC_SCRATCH_BYTES, ctx->dev_err, st, &msg);
+    if (rc != WB_OK) return fail(rc, msg);
+    c->len_stale = true;
+    return WB_OK;
+}

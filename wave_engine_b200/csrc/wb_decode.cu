@@ -472,6 +472,12 @@ size_t decode_scratch_bytes(int n_seq, int H, int hd, int E, int cap) {
     return decode_scratch_layout(n_seq, H, hd, E, cap).end;
 }
 
+void decode_scratch_tickets(int n_seq, int H, int hd, int E, int cap, size_t *offset, size_t *bytes) {
+    const DecodeScratch d = decode_scratch_layout(n_seq, H, hd, E, cap);
+    *offset = d.ticket;
+    *bytes = d.end - d.ticket;
+}
+
 int launch_decode_attn(const DecodeLaunch &L, void *scratch, size_t scratch_bytes, float **o_out,
                        cudaStream_t st, std::string *msg) {
     const int nsplit = (L.cap + DEC_CHUNK - 1) / DEC_CHUNK;

@@ -19,6 +19,9 @@ struct DecodeLaunch {
 // ticket arrays inside must be zero before the first launch (the kernel
 // leaves them zero).
 size_t decode_scratch_bytes(int n_seq, int H, int hd, int E, int cap);
+// Byte range of the ticket counters inside that scratch (must be zero
+// before a launch).
+void decode_scratch_tickets(int n_seq, int H, int hd, int E, int cap, size_t *offset, size_t *bytes);
 // Attention part of one decode step: writes the merged, normalised head
 // outputs o [n_seq][E] (inside scratch, returned in *o_out) and appends the
 // new position to every slot; out_proj and the length update follow.
