@@ -5,11 +5,14 @@ Tolerances: WB_PATH_EXACT (all-fp32 SIMT) max-abs 1e-5; WB_PATH_TENSOR
 (tcgen05 bf16 scores/PV, fp32 accumulation) max-abs 2e-3.
 
 Phases go through atan2f, whose CUDA and glibc implementations differ in the
-last bits, so a phase within a few ulps of a bucket boundary can land in the
-neighbouring bucket.  The comparison therefore checks the phases to 2e-6 rad,
-allows bucket differences only within 1e-5 rad of a boundary, and in that
-case recomputes the oracle with the GPU's phases (mask-conditioned parity) so
-that the rest of the math is still compared element by element.
+last bits, and the tensor path computes the phase projection (r, s) with
+3xTF32 tensor-core products summed in another order than the reference's
+sequential loop, so a phase lying very close to a bucket boundary can land
+in the neighbouring bucket.  The comparison therefore checks the phases (to
+2e-6 rad on the exact path, 5e-5 rad on the tensor path), allows bucket
+differences only that close to a boundary, and in that case recomputes the
+oracle with the GPU's phases (mask-conditioned parity) so that the rest of
+the math is still compared element by element.
 """
 from __future__ import annotations
 
@@ -36,19 +39,24 @@ def make_case(E, H, C, B, T, seed, init="gauss"):
     return w, x
 
 
-def oracle_for(wp, x, gpu_phases, use_content=True):
+PHASE_TOL = {"exact": 2e-6, "tensor": 5e-5}
+
+
+def oracle_for(wp, x, gpu_phases, use_content=True, path="tensor"):
     """Oracle outputs per sequence, conditioned on the GPU's buckets where
-    (and only where) a phase sits within 1e-5 rad of a bucket boundary."""
+    (and only where) a phase sits within twice the phase tolerance of a
+    bucket boundary."""
     if not use_content:
         wp = dict(wp, content_proj_w=None, content_proj_b=None)
+    tol = PHASE_TOL[path]
     ys, aws, flips = [], [], 0
     for b in range(x.shape[0]):
         y, aw, ph = oracle.attn_forward(wp, x[b], want_att_w=True, n_threads=NT)
         gp = gpu_phases[b]
-        assert phase_diff(gp, ph).max() <= 2e-6, f"phase mismatch {phase_diff(gp, ph).max()}"
+        assert phase_diff(gp, ph).max() <= tol, f"phase mismatch {phase_diff(gp, ph).max()}"
         diff = buckets_of(gp) != buckets_of(ph)
         if diff.any():
-            assert (boundary_distance(ph)[diff] < 1e-5).all(), "bucket differs away from a boundary"
+            assert (boundary_distance(ph)[diff] < 2 * tol).all(), "bucket differs away from a boundary"
             flips += int(diff.sum())
             y, aw, _ = oracle.attn_forward(wp, x[b], want_att_w=True, phase_override=gp, n_threads=NT)
         ys.append(y)
@@ -74,7 +82,7 @@ def test_exact_path_matches_oracle(ctx, E, H, C, B, T, init):
     w, x = make_case(E, H, C, B, T, seed=E + T, init=init)
     y, aw, _, ph = wb.wave_attention_forward(w, x, E // 2, path="exact", return_att_weights=True,
                                             return_phases=True, ctx=ctx)
-    oy, oaw, flips = oracle_for(w.packed(), x, ph)
+    oy, oaw, flips = oracle_for(w.packed(), x, ph, path="exact")
     r = check("y", y, oy, EXACT_TOL)
     assert r.passed, str(r)
     r = check("att_w", aw, oaw, EXACT_TOL)
@@ -146,9 +154,9 @@ def test_kv_prefill_and_decode_match_oracle(ctx, path, tol, E, H):
         oy, st = oracle.kv_prefill(wp, x[i, :T], cap=T + steps)
         states.append(st)
         ph, bk, vv = cache.read(0, int(seq_ids[i]))
-        assert phase_diff(ph, st.phases[:, :T]).max() <= 2e-6
+        assert phase_diff(ph, st.phases[:, :T]).max() <= PHASE_TOL[path]
         same = bk == st.buckets[:, :T]
-        assert (same | (boundary_distance(st.phases[:, :T]) < 1e-5)).all()
+        assert (same | (boundary_distance(st.phases[:, :T]) < 2 * PHASE_TOL[path])).all()
         if same.all():
             r = check(f"prefill y seq{i}", y[i], oy, tol)
             assert r.passed, str(r)

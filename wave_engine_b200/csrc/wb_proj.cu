@@ -1,0 +1,424 @@
+// wb_proj.cu -- tensor-core projections for WB_PATH_TENSOR.
+//
+// One GEMM computes, for every row x (a position's n_embd vector), all the
+// per-head projections of src/common/attn.rs:121-165:
+//   columns [0, H*hd)            values   v = Wv_h x_h + b   (block diagonal)
+//   columns [H*hd, H*hd + H*C)   content  c = Wc_h x + b      (C = 0 or 16)
+//   columns [.., + 2H)           phase    (r, s) = Wp_h x + b
+// (the phase columns are kept in W but computed by phase_fma_kernel below).
+// The weight matrix W [N][E] holds the block-diagonal value weights densely
+// (zeros outside a head's block); a 128-column tile that only holds value
+// columns reads just the K range of its heads, so the zeros are not
+// multiplied.
+//
+// Precision: 3xTF32.  Each operand is split into a tf32 head (round to
+// nearest) and its fp32 remainder; on kind::tf32 tcgen05.mma the main
+// products Ah Bh accumulate in one TMEM accumulator and the corrections
+// Ah Bl + Al Bh -- about 2^-11 smaller -- in a second one, so the tensor
+// core's accumulation does not drop the corrections' low bits against the
+// large running sum; the epilogue adds the two in fp32.  Values and content
+// come out with ~1e-6 relative error.  The phase (r, s) decides a discrete
+// bucket, and the tensor core's own fp32 accumulation over hundreds of K
+// steps still moves it by up to ~1e-4 rad, so phases are computed by a
+// separate fp32 SIMT kernel (phase_fma_kernel) with a sequential sum over
+// the input index like the reference's loop.  The weight halves are
+// prepared on the host; the row halves are made in shared memory by two
+// converter warps.
+//
+// Warp roles per CTA (128 x 128 output tile, 128 threads): warp 0 lane 0
+// issues TMA loads (x tile, W head/remainder tiles) into a 3-stage ring,
+// warp 1 lane 0 issues the MMAs, warps 2-3 split the x tile; then all four
+// warps drain TMEM.  The epilogue writes values into the sequence view
+// (cache layout), content rows densely, and turns (r, s) into the phase
+// atan2f(s, r) and its bucket.
+#include "wb_proj.h"
+#include "wb_ptx.cuh"
+
+#include <cudaTypedefs.h>
+
+#include <cmath>
+#include <cstring>
+#include <vector>
+
+namespace wb {
+
+static constexpr int PBM = 128, PBN = 128, PBK = 32, PST = 3;
+static constexpr int P_TILE = PBM * PBK * 4;      // 16 KB (128 rows x 128 B)
+static constexpr int P_STAGE = 4 * P_TILE;        // A, A_lo, B_hi, B_lo
+static constexpr int P_SMEM = PST * P_STAGE + 256 + 1024;
+
+struct ProjArgs {
+    int R, E, H, hd, C, T;
+    int n_v, n_c, n_rs, N;  // column counts (n_v = H*hd, n_c = H*C, n_rs = 2H)
+    const float *bias;      // [N]
+    WbSeqView sv;           // values, phases, buckets (rows r = b*T + t)
+    float *content;         // [R][H*C] or nullptr
+    uint32_t *dev_err;
+};
+
+__device__ __forceinline__ uint32_t tf32_rna(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return r;
+}
+
+__global__ void __launch_bounds__(128, 1)
+    proj_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_wh,
+                   const __grid_constant__ CUtensorMap tm_wl, ProjArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sm + PST * P_STAGE);
+    uint64_t *full = bars, *conv = bars + PST, *empty = bars + 2 * PST, *done = bars + 3 * PST;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * PST + 1);
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const int n_tiles = (a.N + PBN - 1) / PBN;
+    const int nt = blockIdx.x % n_tiles, mt = blockIdx.x / n_tiles;
+    const int n0 = nt * PBN, m0 = mt * PBM;
+    // without a content output (the serve prefill) pure content tiles have
+    // nothing to do
+    if (!a.content && n0 >= a.n_v && n0 + PBN <= a.n_v + a.n_c) return;
+    // K range: value-only tiles need the inputs of their heads only
+    int k_lo = 0, k_hi = a.E;
+    if (n0 + PBN <= a.n_v) {
+        k_lo = (n0 / a.hd) * a.hd;
+        k_hi = min(a.E, ((n0 + PBN + a.hd - 1) / a.hd) * a.hd);
+    }
+    const int kb0 = k_lo / PBK, kb1 = (k_hi + PBK - 1) / PBK, nk = kb1 - kb0;
+
+    if (tid == 0) {
+        for (int i = 0; i < 3 * PST + 1; i++) ptx::mbar_init(bars + i, 1);
+        ptx::fence_mbar_init();
+    }
+    if (warp == 0) {
+        ptx::tmem_alloc(tmem_slot, 256);
+        ptx::tmem_relinquish();
+    }
+    ptx::tc_fence_before();
+    __syncthreads();
+    ptx::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;           // main products
+    const uint32_t tmem_c = tmem + PBN;         // corrections
+
+    if (tid == 0) {  // TMA producer
+        ptx::prefetch_tmap(&tm_x);
+        ptx::prefetch_tmap(&tm_wh);
+        ptx::prefetch_tmap(&tm_wl);
+        for (int i = 0; i < nk; i++) {
+            const int s = i % PST;
+            if (i >= PST && !ptx::mbar_wait(empty + s, ((i / PST) - 1) & 1)) {
+                atomicOr(a.dev_err, WB_DERR_TIMEOUT_MMA);
+                break;
+            }
+            uint8_t *st = sm + s * P_STAGE;
+            const int kx = (kb0 + i) * PBK;
+            ptx::mbar_arrive_expect_tx(full + s, 3 * P_TILE);
+            ptx::tma_load_2d(st, &tm_x, full + s, kx, m0);
+            ptx::tma_load_2d(st + 2 * P_TILE, &tm_wh, full + s, kx, n0);
+            ptx::tma_load_2d(st + 3 * P_TILE, &tm_wl, full + s, kx, n0);
+        }
+    } else if (tid == 32) {  // MMA issuer
+        constexpr uint32_t IDESC = ptx::idesc_tf32(PBM, PBN);
+        for (int i = 0; i < nk; i++) {
+            const int s = i % PST;
+            if (!ptx::mbar_wait(conv + s, (i / PST) & 1)) {
+                atomicOr(a.dev_err, WB_DERR_TIMEOUT_TMA);
+                break;
+            }
+            ptx::tc_fence_after();
+            const uint32_t base = ptx::smem_u32(sm + s * P_STAGE);
+            const uint32_t ah = base, al = base + P_TILE, bh = base + 2 * P_TILE, bl = base + 3 * P_TILE;
+#pragma unroll
+            for (int k = 0; k < 4; k++) {  // 8 tf32 = 32 bytes of K per instruction
+                const uint64_t dah = ptx::smem_desc(ah + k * 32, 16, 1024, ptx::UMMA_SW128);
+                const uint64_t dal = ptx::smem_desc(al + k * 32, 16, 1024, ptx::UMMA_SW128);
+                const uint64_t dbh = ptx::smem_desc(bh + k * 32, 16, 1024, ptx::UMMA_SW128);
+                const uint64_t dbl = ptx::smem_desc(bl + k * 32, 16, 1024, ptx::UMMA_SW128);
+                ptx::mma_tf32(tmem, dah, dbh, IDESC, (i > 0 || k > 0));
+                ptx::mma_tf32(tmem_c, dah, dbl, IDESC, (i > 0 || k > 0));
+                ptx::mma_tf32(tmem_c, dal, dbh, IDESC, 1);
+            }
+            ptx::mma_commit(empty + s);
+        }
+        ptx::mma_commit(done);
+    } else if (warp >= 2) {  // converters: x -> (tf32 head in place, remainder)
+        const int ct = tid - 64;
+        for (int i = 0; i < nk; i++) {
+            const int s = i % PST;
+            if (!ptx::mbar_wait(full + s, (i / PST) & 1)) {
+                if (ct == 0) atomicOr(a.dev_err, WB_DERR_TIMEOUT_TMA);
+                break;
+            }
+            float4 *A = reinterpret_cast<float4 *>(sm + s * P_STAGE);
+            float4 *Al = reinterpret_cast<float4 *>(sm + s * P_STAGE + P_TILE);
+#pragma unroll 4
+            for (int e = ct; e < P_TILE / 16; e += 64) {
+                const float4 v = A[e];
+                float4 h, l;
+                h.x = __uint_as_float(tf32_rna(v.x));
+                h.y = __uint_as_float(tf32_rna(v.y));
+                h.z = __uint_as_float(tf32_rna(v.z));
+                h.w = __uint_as_float(tf32_rna(v.w));
+                l.x = v.x - h.x;
+                l.y = v.y - h.y;
+                l.z = v.z - h.z;
+                l.w = v.w - h.w;
+                A[e] = h;
+                Al[e] = l;
+            }
+            ptx::fence_proxy_async_smem();
+            asm volatile("bar.sync 1, 64;" ::: "memory");
+            if (ct == 0) ptx::mbar_arrive(conv + s);
+        }
+    }
+
+    // epilogue: TMEM -> registers -> destinations by column kind
+    const bool fin = ptx::mbar_wait(done, 0);
+    if (!fin && tid == 0) atomicOr(a.dev_err, WB_DERR_TIMEOUT_MMA);
+    ptx::tc_fence_after();
+    if (fin) {
+        const int m = m0 + tid;
+        const int b = m / a.T, t = m - (m / a.T) * a.T;
+#pragma unroll 1
+        for (int c = 0; c < PBN / 32; c++) {
+            uint32_t r[32], rc[32];
+            ptx::tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + c * 32, r);
+            ptx::tmem_ld32(tmem_c + ((uint32_t)(warp * 32) << 16) + c * 32, rc);
+            ptx::tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; i++) r[i] = __float_as_uint(__uint_as_float(r[i]) + __uint_as_float(rc[i]));
+            if (m >= a.R) continue;
+#pragma unroll
+            for (int i = 0; i < 32; i++) {
+                const int n = n0 + c * 32 + i;
+                if (n >= a.N) break;
+                const float v = __uint_as_float(r[i]) + a.bias[n];
+                if (n < a.n_v) {
+                    const int h = n / a.hd, d = n - h * a.hd;
+                    a.sv.v[(wb_slot_base(a.sv, b, h) + t) * a.hd + d] = v;
+                } else if (n < a.n_v + a.n_c) {
+                    if (a.content) a.content[(long long)m * a.n_c + (n - a.n_v)] = v;
+                }
+            }
+        }
+    }
+    ptx::tc_fence_before();
+    __syncthreads();
+    if (warp == 0) ptx::tmem_dealloc(tmem, 256);
+}
+
+// ---------------------------------------------------------------------------
+// Phases: (r, s) = b + sum_j W[.][j] x[j] in fp32, j in order (attn.rs:124-127
+// with fused multiply-adds), then theta = atan2f(s, r) and its bucket
+// (attn.rs:127, :171-174).  One row per thread, 128 rows per CTA; x tiles of
+// 64 columns and the matching phase weights [64][H][2] are staged in shared
+// memory (x padded by one float per row against bank conflicts).
+// ---------------------------------------------------------------------------
+static constexpr int PH_ROWS = 128, PH_KC = 32;
+
+template <int PH_MAXO>  // 2 * max heads: 32 (H <= 16) or 64 (H <= 32)
+__global__ void __launch_bounds__(PH_ROWS) phase_fma_kernel(const float *__restrict__ x, const float *__restrict__ wrs_t,
+                                                           const float *__restrict__ brs, int R, int E, int H, int T,
+                                                           WbSeqView sv) {
+    __shared__ float xs[PH_ROWS * (PH_KC + 1)];
+    __shared__ __align__(16) float ws[PH_KC * PH_MAXO];
+    const int tid = threadIdx.x;
+    const int m0 = blockIdx.x * PH_ROWS;
+    const int NO = 2 * H;
+    float acc[PH_MAXO];
+#pragma unroll
+    for (int o = 0; o < PH_MAXO; o++) acc[o] = o < NO ? brs[o] : 0.0f;
+    for (int k0 = 0; k0 < E; k0 += PH_KC) {
+        const int kn = min(PH_KC, E - k0);
+        __syncthreads();
+        // x tile: each warp loads rows with lanes along k (coalesced), all
+        // loads of the thread issued before the stores
+        {
+            float v[PH_KC];  // PH_KC per thread
+#pragma unroll
+            for (int u = 0; u < PH_KC; u++) {
+                const int e = u * PH_ROWS + tid;  // e = row * 64 + k
+                const int row = e / PH_KC, k = e % PH_KC;
+                v[u] = (m0 + row < R && k < kn) ? __ldg(x + (long long)(m0 + row) * E + k0 + k) : 0.0f;
+            }
+#pragma unroll
+            for (int u = 0; u < PH_KC; u++) {
+                const int e = u * PH_ROWS + tid;
+                xs[(e / PH_KC) * (PH_KC + 1) + (e % PH_KC)] = v[u];
+            }
+        }
+        for (int e = tid; e < kn * NO; e += PH_ROWS) ws[(e / NO) * PH_MAXO + (e % NO)] = wrs_t[(long long)k0 * NO + e];
+        __syncthreads();
+        const float *xr = xs + tid * (PH_KC + 1);
+        for (int k = 0; k < kn; k++) {
+            const float xv = xr[k];
+            const float4 *w4 = reinterpret_cast<const float4 *>(ws + k * PH_MAXO);
+#pragma unroll
+            for (int o4 = 0; o4 < PH_MAXO / 4; o4++) {
+                if (o4 * 4 >= NO) break;
+                const float4 w = w4[o4];
+                acc[o4 * 4 + 0] = fmaf(w.x, xv, acc[o4 * 4 + 0]);
+                acc[o4 * 4 + 1] = fmaf(w.y, xv, acc[o4 * 4 + 1]);
+                acc[o4 * 4 + 2] = fmaf(w.z, xv, acc[o4 * 4 + 2]);
+                acc[o4 * 4 + 3] = fmaf(w.w, xv, acc[o4 * 4 + 3]);
+            }
+        }
+    }
+    const int m = m0 + tid;
+    if (m >= R) return;
+    const int b = m / T, t = m - b * T;
+#pragma unroll
+    for (int h = 0; h < PH_MAXO / 2; h++) {
+        if (h >= H) break;
+        const float th = atan2f(acc[2 * h + 1], acc[2 * h]);
+        const long long pos = wb_slot_base(sv, b, h) + t;
+        sv.theta[pos] = th;
+        sv.bucket[pos] = (uint8_t)phase_to_bucket(th);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+static PFN_cuTensorMapEncodeTiled_v12000 proj_encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
+        else
+            cudaGetLastError();
+    }
+    return fn;
+}
+
+static int tmap_2d_f32(CUtensorMap *m, const void *base, uint64_t inner, uint64_t outer, std::string *msg) {
+    auto fn = proj_encode_fn();
+    if (!fn) {
+        *msg = "cuTensorMapEncodeTiled unavailable";
+        return WB_ECUDA;
+    }
+    const uint64_t dims[2] = {inner, outer};
+    const uint64_t strides[1] = {inner * 4};
+    const uint32_t box[2] = {PBK, 128};
+    const uint32_t es[2] = {1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void *>(base), dims, strides, box, es,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        *msg = "cuTensorMapEncodeTiled (projection) failed with CUresult " + std::to_string((int)r);
+        return WB_ECUDA;
+    }
+    return WB_OK;
+}
+
+static float tf32_round_host(float x) {  // round to nearest, ties away (cvt.rna)
+    uint32_t u;
+    std::memcpy(&u, &x, 4);
+    if ((u & 0x7f800000u) != 0x7f800000u) {
+        u += 0x1000u;
+        u &= 0xffffe000u;
+    }
+    float r;
+    std::memcpy(&r, &u, 4);
+    return r;
+}
+
+int proj_weights_upload(ProjTcWeights *p, const wb_attn_weights_desc *w, std::string *msg) {
+    const int E = w->n_embd, H = w->n_head, hd = E / H, C = w->content_dim;
+    p->E = E;
+    p->H = H;
+    p->hd = hd;
+    p->C = C;
+    p->n_v = H * hd;
+    p->n_c = H * C;
+    p->n_rs = 2 * H;
+    p->N = p->n_v + p->n_c + p->n_rs;
+    const size_t N = p->N;
+    std::vector<float> W(N * E, 0.0f), bias(N, 0.0f);
+    for (int h = 0; h < H; h++)
+        for (int d = 0; d < hd; d++) {
+            const size_t row = (size_t)h * hd + d;
+            for (int j = 0; j < hd; j++) W[row * E + h * hd + j] = w->v_proj_w[((size_t)h * hd + d) * hd + j];
+            bias[row] = w->v_proj_b[h * hd + d];
+        }
+    for (int h = 0; h < H; h++)
+        for (int c = 0; c < C; c++) {
+            const size_t row = p->n_v + (size_t)h * C + c;
+            std::memcpy(&W[row * E], w->content_proj_w + ((size_t)h * C + c) * E, sizeof(float) * E);
+            bias[row] = w->content_proj_b[h * C + c];
+        }
+    for (int h = 0; h < H; h++)
+        for (int k = 0; k < 2; k++) {
+            const size_t row = p->n_v + p->n_c + (size_t)h * 2 + k;
+            std::memcpy(&W[row * E], w->phase_proj_w + ((size_t)h * 2 + k) * E, sizeof(float) * E);
+            bias[row] = w->phase_proj_b[h * 2 + k];
+        }
+    std::vector<float> Wh(N * E), Wl(N * E);
+    for (size_t i = 0; i < N * E; i++) {
+        Wh[i] = tf32_round_host(W[i]);
+        Wl[i] = W[i] - Wh[i];
+    }
+    if (cudaMalloc(&p->w_hi, N * E * 4) != cudaSuccess || cudaMalloc(&p->w_lo, N * E * 4) != cudaSuccess ||
+        cudaMalloc(&p->bias, N * 4) != cudaSuccess) {
+        cudaGetLastError();
+        *msg = "cudaMalloc for projection weights failed";
+        return WB_ENOMEM;
+    }
+    if (cudaMemcpy(p->w_hi, Wh.data(), N * E * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(p->w_lo, Wl.data(), N * E * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(p->bias, bias.data(), N * 4, cudaMemcpyHostToDevice) != cudaSuccess) {
+        *msg = "upload of projection weights failed";
+        return WB_ECUDA;
+    }
+    return WB_OK;
+}
+
+void proj_weights_free(ProjTcWeights *p) {
+    if (p->w_hi) cudaFree(p->w_hi);
+    if (p->w_lo) cudaFree(p->w_lo);
+    if (p->bias) cudaFree(p->bias);
+    p->w_hi = p->w_lo = p->bias = nullptr;
+}
+
+int launch_proj_tc(const ProjTcWeights &p, const float *wrs_t, const float *brs, const float *x, int B, int T,
+                   const WbSeqView &sv, float *content, uint32_t *dev_err, cudaStream_t st, std::string *msg) {
+    const long long R = (long long)B * T;
+    if (R <= 0) return WB_OK;
+    if ((p.E * 4) % 16) {
+        *msg = "n_embd must be a multiple of 4 for the tensor projections";
+        return WB_ENOTSUP;
+    }
+    CUtensorMap tx, th, tl;
+    int rc;
+    if ((rc = tmap_2d_f32(&tx, x, (uint64_t)p.E, (uint64_t)R, msg))) return rc;
+    if ((rc = tmap_2d_f32(&th, p.w_hi, (uint64_t)p.E, (uint64_t)p.N, msg))) return rc;
+    if ((rc = tmap_2d_f32(&tl, p.w_lo, (uint64_t)p.E, (uint64_t)p.N, msg))) return rc;
+    if (p.H > 32) {
+        *msg = "the tensor projections support up to 32 heads";
+        return WB_ENOTSUP;
+    }
+    // GEMM over the value and content columns only (phases below)
+    const int n_gemm = p.n_v + p.n_c;
+    ProjArgs a{(int)R, p.E, p.H, p.hd, p.C, T, p.n_v, p.n_c, p.n_rs, n_gemm, p.bias, sv, content, dev_err};
+    const int n_tiles = (n_gemm + PBN - 1) / PBN;
+    const unsigned grid = (unsigned)(((R + PBM - 1) / PBM) * n_tiles);
+    ProfScope ps("proj_tc", st);
+    cudaFuncSetAttribute(proj_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM);
+    proj_tc_kernel<<<grid, 128, P_SMEM, st>>>(tx, th, tl, a);
+    {
+        ProfScope pp("phase_fma", st);
+        const unsigned pg = (unsigned)((R + PH_ROWS - 1) / PH_ROWS);
+        if (p.H <= 16) phase_fma_kernel<32><<<pg, PH_ROWS, 0, st>>>(x, wrs_t, brs, (int)R, p.E, p.H, T, sv);
+        else phase_fma_kernel<64><<<pg, PH_ROWS, 0, st>>>(x, wrs_t, brs, (int)R, p.E, p.H, T, sv);
+    }
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        *msg = std::string("projection launch failed: ") + cudaGetErrorString(e);
+        return WB_ECUDA;
+    }
+    return WB_OK;
+}
+
+}  // namespace wb

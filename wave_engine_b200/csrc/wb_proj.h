@@ -1,0 +1,25 @@
+// wb_proj.h -- tensor-core (3xTF32) projections of the tensor path.
+#pragma once
+#include "wave_b200.h"
+#include "wb_internal.h"
+
+namespace wb {
+
+struct ProjTcWeights {
+    int E = 0, H = 0, hd = 0, C = 0;
+    int n_v = 0, n_c = 0, n_rs = 0, N = 0;  // value / content / phase column counts
+    float *w_hi = nullptr;                  // [N][E] tf32 heads of the weights
+    float *w_lo = nullptr;                  // [N][E] fp32 remainders
+    float *bias = nullptr;                  // [N]
+};
+
+int proj_weights_upload(ProjTcWeights *p, const wb_attn_weights_desc *w, std::string *msg);
+void proj_weights_free(ProjTcWeights *p);
+
+// Values into sv.v, phases + buckets into sv.theta / sv.bucket, content
+// vectors into content [R][H*C] (skipped when content is null) for the
+// R = B*T rows of x [R][E].  wrs_t/brs: phase weights [E][H][2] and biases.
+int launch_proj_tc(const ProjTcWeights &p, const float *wrs_t, const float *brs, const float *x, int B, int T,
+                   const WbSeqView &sv, float *content, uint32_t *dev_err, cudaStream_t st, std::string *msg);
+
+}  // namespace wb

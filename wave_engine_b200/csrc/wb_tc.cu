@@ -584,6 +584,10 @@ int tc_layer_upload(TcLayerWeights *t, const wb_attn_weights_desc *w, std::strin
     t->hd = w->n_embd / w->n_head;
     t->C = w->content_dim;
     t->wide = true;
+    {
+        int rc = proj_weights_upload(&t->proj, w, msg);
+        if (rc) return rc;
+    }
     const size_t n = (size_t)t->E * t->E;
     if (t->wide) {
         if (cudaMalloc(&t->w_o32, n * sizeof(float)) != cudaSuccess) {
@@ -619,6 +623,7 @@ int tc_layer_upload(TcLayerWeights *t, const wb_attn_weights_desc *w, std::strin
 }
 
 void tc_layer_free(TcLayerWeights *t) {
+    proj_weights_free(&t->proj);
     if (t->w_o) cudaFree(t->w_o);
     if (t->w_o32) cudaFree(t->w_o32);
     t->w_o = nullptr;
@@ -815,8 +820,10 @@ int tc_attn_forward(const TcLayerWeights &t, const float *x, int B, int T, bool 
     sv.cap = T;
     sv.slot = nullptr;
     float *content = use_content ? (float *)(w + o_ct) : nullptr;
-    launch_projections_exact(t.pw, x, B, T, sv, (float *)(w + o_rs), content, st);
-    int rc = tc_attention_core(t, sv, content, B, T, y, ws, lay, dev_err, st, msg);
+    (void)o_rs;
+    int rc = launch_proj_tc(t.proj, t.pw.wrs_t, t.pw.brs, x, B, T, sv, content, dev_err, st, msg);
+    if (rc) return rc;
+    rc = tc_attention_core(t, sv, content, B, T, y, ws, lay, dev_err, st, msg);
     if (rc) return rc;
     if (phases_out &&
         cudaMemcpyAsync(phases_out, sv.theta, R * H * sizeof(float), cudaMemcpyDeviceToDevice, st) != cudaSuccess) {
@@ -838,7 +845,9 @@ int tc_kv_prefill(const TcLayerWeights &t, const WbSeqView &sv, const float *x, 
     const size_t o_rs = cv.take<float>(R * 2 * t.H);
     const CoreLayout lay = core_layout(t, n_seq, T, cv.off);
     if (ws_ensure(ws, lay.end, msg)) return WB_ENOMEM;
-    launch_projections_exact(t.pw, x, n_seq, T, sv, (float *)((char *)ws->p + o_rs), nullptr, st);
+    (void)o_rs;
+    int rc = launch_proj_tc(t.proj, t.pw.wrs_t, t.pw.brs, x, n_seq, T, sv, nullptr, dev_err, st, msg);
+    if (rc) return rc;
     return tc_attention_core(t, sv, nullptr, n_seq, T, y, ws, lay, dev_err, st, msg);
 }
 

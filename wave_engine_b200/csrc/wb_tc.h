@@ -3,6 +3,7 @@
 #pragma once
 #include "wave_b200.h"
 #include "wb_internal.h"
+#include "wb_proj.h"
 
 #include <string>
 
@@ -11,6 +12,7 @@ namespace wb {
 struct TcLayerWeights {
     int E = 0, H = 0, hd = 0, C = 0;
     ProjWeights pw{};                  // fp32 projection weights (shared with the SIMT path)
+    ProjTcWeights proj;                // 3xTF32 tensor-core projection weights
     const float *harmonic_n = nullptr; // [H] softplus(harmonic_raw)
     const float *b_o = nullptr;        // [E] out_proj bias
     const float *wo_t = nullptr;       // [E][E] out_proj, input-major fp32 (decode rows)
