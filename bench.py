@@ -50,6 +50,31 @@ def dist_env():
     return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
 
 
+def max_over_ranks(value: float, world: int, device=None) -> float:
+    """Max of a per-rank number over all ranks (the step time of the slowest
+    rank); the identity on one rank."""
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def shard_sequences(ctx_lens, world: int):
+    """Split sequences over ranks so every rank gets about the same number of
+    cached keys (greedy: longest sequence to the least loaded rank).  Returns
+    one sorted index list per rank; every index appears exactly once."""
+    loads = [0] * world
+    shards = [[] for _ in range(world)]
+    for i in sorted(range(len(ctx_lens)), key=lambda j: (-ctx_lens[j], j)):
+        r = min(range(world), key=lambda q: (loads[q], q))
+        shards[r].append(i)
+        loads[r] += ctx_lens[i]
+    return [sorted(s) for s in shards]
+
+
 # ---------------------------------------------------------------------------
 # clocks during the timed region
 # ---------------------------------------------------------------------------
@@ -227,14 +252,6 @@ def run_ours(args):
             import torch.distributed as dist
             dist.barrier()
 
-    def max_over_ranks(v):
-        if world == 1:
-            return v
-        import torch.distributed as dist
-        t = torch.tensor([v], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
     for w in range(args.warmup):
         step()
         barrier()
@@ -267,9 +284,9 @@ def run_ours(args):
     ms_total = e0.elapsed_time(e1)
     pre_ms = sum(starts[k].elapsed_time(mids[k]) for k in range(args.steps)) / args.steps
     dec_ms = sum(mids[k].elapsed_time(ends[k]) for k in range(args.steps)) / args.steps
-    ms_step = max_over_ranks(ms_total / args.steps)
-    pre_ms = max_over_ranks(pre_ms)
-    dec_ms = max_over_ranks(dec_ms)
+    ms_step = max_over_ranks(ms_total / args.steps, world, dev)
+    pre_ms = max_over_ranks(pre_ms, world, dev)
+    dec_ms = max_over_ranks(dec_ms, world, dev)
     tok_step = B * T + B * S
     value = world * tok_step / (ms_step / 1e3)
     check_err("the timed region")
@@ -320,7 +337,7 @@ def run_ours(args):
             step_host()
         f1.record(stream)
         barrier()
-        e2e_ms = max_over_ranks(f0.elapsed_time(f1) / n_e2e)
+        e2e_ms = max_over_ranks(f0.elapsed_time(f1) / n_e2e, world, dev)
         e2e = {"value": round(world * tok_step / (e2e_ms / 1e3), 1), "unit": "tok/s",
                "h2d_bytes_per_step": int(xp_h.numel() * 4 + xd_h.numel() * 4 + (L + S * L) * B * 4),
                "d2h_bytes_per_step": int((L * B * T * E + S * L * B * E) * 4), "ms_per_step": round(e2e_ms, 3),
