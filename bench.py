@@ -467,6 +467,120 @@ def run_reference(args):
     print(json.dumps(out), flush=True)
 
 
+def run_decode_stress(args):
+    """256 concurrent sequences, contexts uniform in
+    [128, 4096], 12 heads x 64, fp32 KV cache of Gaussian values and uniform
+    phases, one new token per sequence per step through 24 layers.  Under
+    torchrun the sequences are split across ranks by cached keys.  One step
+    (24 layers) is a CUDA graph; inputs are per-step N(0,1) rows.  Prints its
+    own JSON line (metric: decode tok/s and HBM roofline)."""
+    import numpy as np
+    import torch
+    import wave_engine_b200 as wb
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+    E, H, hd, L = CFG["n_embd"], CFG["n_head"], CFG["head_dim"], CFG["n_layers"]
+    n_all, K, W = 256, args.steps, args.warmup
+    rng = np.random.default_rng(4)
+    lens_all = rng.integers(128, 4097, size=n_all).tolist()
+    mine = shard_sequences(lens_all, world)[rank]
+    lens = [lens_all[i] for i in mine]
+    B = len(mine)
+    cap = max(lens) + K + W + 1
+    ctx = wb.Context(local)
+    stream = torch.cuda.current_stream(dev)
+    ctx.set_stream(stream.cuda_stream)
+    layers = [wb.AttnLayer(ctx, wb.gaussian_block_attn(2000 + l, H, E, 0)) for l in range(L)]
+    cache = wb.KvCache(L, H, hd, max_seqs=B, max_ctx=cap, ctx=ctx)
+    g = torch.Generator(device=dev).manual_seed(99 + rank)
+    vpool = torch.randn((H, 4096, hd), generator=g, device=dev)
+    for l in range(L):
+        for b, n in enumerate(lens):
+            ph = torch.atan2(torch.randn((H, n), generator=g, device=dev), torch.randn((H, n), generator=g, device=dev))
+            cache.load(l, b, ph.contiguous(), vpool[:, :n].contiguous())
+    x = torch.randn((K + W, L, B, E), generator=g, device=dev)
+    ids = torch.arange(B, dtype=torch.int32, device=dev)
+    stage = torch.empty((L, B, E), device=dev)
+    y = torch.empty((L, B, E), device=dev)
+
+    def step_layers():
+        for l in range(L):
+            cache.forward_one(l, layers[l], stage[l], ids, out=y[l])
+
+    stage.copy_(x[0])
+    step_layers()  # eager: allocates the decode scratch
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    cs = torch.cuda.Stream(dev)
+    cs.wait_stream(stream)
+    with torch.cuda.graph(graph, stream=cs):
+        step_layers()
+    stream.wait_stream(cs)
+    ctx.set_stream(stream.cuda_stream)
+    for s in range(1, W):
+        stage.copy_(x[s])
+        graph.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    clocks = Clocks(local)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for s in range(W, W + K):
+        stage.copy_(x[s])
+        graph.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = max_over_ranks(e0.elapsed_time(e1) / K, world, dev)
+    code = ctx.take_device_error()
+    # exact algorithmic bytes of the timed steps from the cache's buckets
+    bks = []
+    for l in range(L):
+        for b in range(B):
+            bk = np.empty((H, cache.n_cached(l, b)), np.uint8)
+            from wave_engine_b200 import _lib
+            _lib.call("wb_kv_cache_read", ctx.handle, cache.handle, l, b, None, bk.ctypes.data, None)
+            bks.append((bk, lens[b] + W))
+    unm = 0
+    keys = 0
+    for bk, n0 in bks:
+        b64 = bk.astype(np.int64)
+        for p in range(n0, n0 + K):
+            qb = b64[:, p]
+            prev = b64[:, p - 1]
+            kb = b64[:, :p]
+            adj = (((kb - qb[:, None]) % 8)[:, :, None] == np.array([0, 1, 7])).any(-1)
+            pm = ~np.isin((prev - qb) % 8, (0, 1, 7))
+            unm += int(adj.sum() + pm.sum())
+            keys += H * p
+    byts = keys * 5 + unm * hd * 4 + K * L * B * E * 8
+    hbm, _, peak_kind = peaks()
+    ach = byts / K / (ms / 1e3) / 1e9
+    out = {"metric": "decode tok/s (decode stress, 768-dim, 256 seqs, ctx U[128,4096], fp32 KV)",
+           "value": round(n_all / (ms / 1e3), 1), "unit": "tok/s",
+           "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": round(ms, 3), "higher_is_better": True,
+           "scaling": "strong (256 sequences split by cached keys)", "seqs_this_rank": B,
+           "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
+                        "frac": round(ach / hbm, 4), "peak_kind": peak_kind,
+                        "algorithmic_bytes_per_step": int(byts / K), "unmasked_key_fraction": round(unm / keys, 4),
+                        "timing": "whole decode step (24 layers: attention + out_proj kernels) on this rank"},
+           "clocks": clk, "device_error": code}
+    del graph
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+
+
 def run_profile_case(args):
     """Small single-GPU cases for ncu captures (no timing, a few hundred MB
     on the device): 'decode' = 12 fused decode steps of one 768-dim layer,
@@ -481,7 +595,23 @@ def run_profile_case(args):
     w = wb.gaussian_block_attn(5, H, E, C)
     lay = wb.AttnLayer(ctx, w)
     g = torch.Generator(device="cuda").manual_seed(0)
-    if args.profile_case == "decode":
+    if args.profile_case == "decode-stress":
+        # one layer of the decode-stress workload (~3.3 GB on the device)
+        rng = np.random.default_rng(4)
+        lens = rng.integers(128, 4097, size=256).tolist()
+        B = 256
+        cache = wb.KvCache(1, H, hd, max_seqs=B, max_ctx=max(lens) + 16, ctx=ctx)
+        vpool = torch.randn((H, 4096, hd), generator=g, device="cuda")
+        for b, n in enumerate(lens):
+            ph = torch.atan2(torch.randn((H, n), generator=g, device="cuda"), torch.randn((H, n), generator=g, device="cuda"))
+            cache.load(0, b, ph.contiguous(), vpool[:, :n].contiguous())
+        lay0 = wb.AttnLayer(ctx, wb.gaussian_block_attn(5, H, E, 0))
+        ids = torch.arange(B, dtype=torch.int32, device="cuda")
+        x = torch.randn((6, B, E), generator=g, device="cuda")
+        y = torch.empty((B, E), device="cuda")
+        for s in range(6):
+            cache.forward_one(0, lay0, x[s], ids, out=y)
+    elif args.profile_case == "decode":
         B, n = 32, 1100
         cache = wb.KvCache(1, H, hd, max_seqs=B, max_ctx=n + 16, ctx=ctx)
         rng = np.random.default_rng(0)
@@ -506,7 +636,9 @@ def run_profile_case(args):
 
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
-    ap.add_argument("--profile-case", choices=["decode", "prefill"], default=None,
+    ap.add_argument("--workload", choices=["serve-768", "decode-stress"], default="serve-768",
+                    help="serve-768: BASELINE configs[2] (the default line); decode-stress: configs[3]")
+    ap.add_argument("--profile-case", choices=["decode", "decode-stress", "prefill"], default=None,
                     help="run a small case for an ncu capture instead of the benchmark")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=3)
@@ -524,6 +656,8 @@ def main():
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
     if args.profile_case:
         run_profile_case(args)
+    elif args.workload == "decode-stress" and args.impl == "ours":
+        run_decode_stress(args)
     elif args.impl == "reference":
         run_reference(args)
     else:
