@@ -127,7 +127,7 @@ struct wb_kv_cache {
     uint8_t *bucket = nullptr;
     float *v = nullptr;
     int32_t *len = nullptr;            // device [L][S] (the truth)
-    wb::Workspace dscratch;            // fused decode partials + tickets, sized for (S, cap), zeroed
+    wb::Workspace dscratch;            // decode partials + tickets, sized for (S, cap), zeroed
     std::vector<int32_t> len_host;     // host mirror [L][S]
     bool len_stale = false;            // a call with device seq ids changed lengths on the device
     int refresh(cudaStream_t st) {
@@ -686,7 +686,7 @@ int wb_kv_prefill(wb_context *ctx, wb_kv_cache *c, int layer_idx, const wb_attn_
         int rc = wb::tc_kv_prefill(L->tc, sv, xd, n_seq, T, yd, &ctx->ws, ctx->dev_err, ctx->sm_count, st, &msg);
         if (rc != WB_OK) return fail(rc, msg);
     }
-    wb::launch_len_update(c->len + (size_t)layer_idx * c->S, ids_d, n_seq, T, 1, st);
+    wb::launch_len_update(c->len + (size_t)layer_idx * c->S, ids_d, n_seq, T, 1, c->S, c->cap, st);
     WB_CUDA(cudaGetLastError());
     if (ids_dev) c->len_stale = true;
     else
@@ -745,12 +745,12 @@ int wb_kv_decode(wb_context *ctx, wb_kv_cache *c, int layer_idx, const wb_attn_l
         wb::launch_decode_simt(sv, len_l, th, vn, L->harmonic_n, n_seq, H, hd, o, st);
         wb::OutMap om{wb::OUT_DENSE, yd, E, sv, 0, 1};
         wb::launch_seqdot(o, n_seq, E, E, L->wo_t, E, L->bo, 0, om, st);
-        wb::launch_len_update(len_l, ids_d, n_seq, 1, 0, st);
+        wb::launch_len_update(len_l, ids_d, n_seq, 1, 0, c->S, c->cap, st);
         WB_CUDA(cudaGetLastError());
     } else {
         std::string msg;
         int rc = wb::tc_kv_decode(L->tc, sv, len_l, c->cap, c->S, xd, n_seq, yd, c->dscratch.p, c->dscratch.n,
-                                  ctx->dev_err, st, &msg);
+                                  ctx->dev_err, ctx->sm_count, st, &msg);
         if (rc != WB_OK) return fail(rc, msg);
     }
     if (ids_dev) c->len_stale = true;
@@ -857,7 +857,7 @@ extern "C" int wb_kv_decode_noalloc(wb_context *ctx, wb_kv_cache *c, int layer_i
     WbSeqView sv = c->view(layer_idx, seq_ids);
     std::string msg;
     int rc = wb::tc_kv_decode(L->tc, sv, c->len + (size_t)layer_idx * c->S, c->cap, c->S, x, n_seq, y, scratch,
-                              WB_NOALLOC_SCRATCH_BYTES, ctx->dev_err, st, &msg);
+                              WB_NOALLOC_SCRATCH_BYTES, ctx->dev_err, ctx->sm_count, st, &msg);
     if (rc != WB_OK) return fail(rc, msg);
     c->len_stale = true;
     return WB_OK;

@@ -3,13 +3,13 @@
 // Two launches per layer and decode step.
 //
 // decode_attn_kernel, grid (split, head, sequence), 512 keys per CTA:
-//   * every CTA projects the new position's phase theta_q = atan2(s, r)
+//   * every CTA projects the new position's phase theta_q = atan2f(s, r)
 //     (kv_cache.rs:271) from the x row, then scans its split of the cached
 //     keys: the bucket byte and phase of every key (coalesced, issued up
 //     front), the score cos(n (theta_q - theta_k)) only for keys in buckets
 //     b-1..b+1 or at the previous position (kv_cache.rs:285-298), and the
 //     fp32 value row only of those keys, streamed with 128-bit loads by
-//     groups of lanes;
+//     groups of lanes, U loads per lane in flight;
 //   * decode scores never exceed the self score 1.0 (kv_cache.rs:294), so the
 //     softmax uses the fixed shift 1: p = exp(s - 1) exactly as the
 //     reference's max-subtraction, and split partials (sum p, sum p v) merge
@@ -19,15 +19,19 @@
 //     merges the partials, adds the self term (p = 1, v), normalises into
 //     the merged head output o, and appends (phase, bucket, value) at
 //     position n.
-// The caller then runs out_proj (kv_cache.rs:330-335) on the merged outputs
-// o and advances the cached lengths in a separate launch: a CTA of this
-// launch that starts late must still see the old length.
+// decode_out_kernel runs out_proj (kv_cache.rs:330-335) on the merged
+// outputs o and advances the cached lengths.  It is launched as a
+// programmatic dependent of the attention grid: its first weight batch is
+// loaded while that grid finishes, and it waits for the grid's completion
+// before it reads o or touches a length (a CTA of the attention grid that
+// starts late must still see the old length).
 // Scratch: partials, new values, merged outputs and a ticket array that the
 // kernel returns to zero.
 #include "wb_decode.h"
 #include "wb_ptx.cuh"
 
 #include <algorithm>
+#include <cstdlib>
 
 namespace wb {
 
@@ -36,6 +40,25 @@ static constexpr int DEC_WARPS = DEC_THREADS / 32;
 static constexpr int DEC_KEYS_PER_WARP = 128;
 static constexpr int DEC_CHUNK = DEC_WARPS * DEC_KEYS_PER_WARP;  // keys per CTA (512)
 
+// cudaLaunchKernelEx, optionally with the programmatic-stream-serialization
+// attribute (the grid may begin while the previous grid of the stream runs;
+// it calls griddep_wait() before it reads anything that grid writes).
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                             bool dependent, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = dependent ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 struct DecodeArgs {
     WbSeqView sv;             // cache view of the layer (slot = seq ids)
     int32_t *len;             // [slots] cached positions (device truth)
@@ -43,7 +66,6 @@ struct DecodeArgs {
     const float *x;           // [n_seq][E]
     const float *wrs_t, *brs; // phase projection [E][H][2], [H][2]
     const float *wv_t, *bv;   // value projection [H][hd(in)][hd(out)], [H][hd]
-    const float *wo_t, *bo;   // out_proj [E(in)][E(out)], [E]
     const float *hn;          // [H]
     int n_seq, H, hd, E, nsplit;
     float *part;              // [n_seq][H][nsplit][hd + 1]
@@ -53,30 +75,25 @@ struct DecodeArgs {
     uint32_t *dev_err;
 };
 
+// VEC consecutive floats of a value row, through the read-only path.
 template <int VEC>
-struct VecT;
-template <>
-struct VecT<4> {
-    using T = float4;
-    __device__ static void fma(float *acc, float p, const float *src) {
-        const float4 v = __ldg(reinterpret_cast<const float4 *>(src));
-        acc[0] = fmaf(p, v.x, acc[0]);
-        acc[1] = fmaf(p, v.y, acc[1]);
-        acc[2] = fmaf(p, v.z, acc[2]);
-        acc[3] = fmaf(p, v.w, acc[3]);
+struct VRow {
+    float v[VEC];
+    __device__ __forceinline__ void load(const float *src) {
+        if constexpr (VEC == 4) {
+            const float4 t = __ldg(reinterpret_cast<const float4 *>(src));
+            v[0] = t.x;
+            v[1] = t.y;
+            v[2] = t.z;
+            v[3] = t.w;
+        } else if constexpr (VEC == 2) {
+            const float2 t = __ldg(reinterpret_cast<const float2 *>(src));
+            v[0] = t.x;
+            v[1] = t.y;
+        } else {
+            v[0] = __ldg(src);
+        }
     }
-};
-template <>
-struct VecT<2> {
-    __device__ static void fma(float *acc, float p, const float *src) {
-        const float2 v = __ldg(reinterpret_cast<const float2 *>(src));
-        acc[0] = fmaf(p, v.x, acc[0]);
-        acc[1] = fmaf(p, v.y, acc[1]);
-    }
-};
-template <>
-struct VecT<1> {
-    __device__ static void fma(float *acc, float p, const float *src) { acc[0] = fmaf(p, __ldg(src), acc[0]); }
 };
 
 // G lanes per key row: enough VEC-wide lanes to cover hd (rounded up to a
@@ -89,6 +106,23 @@ __device__ __forceinline__ int lanes_per_key(int hd) {
     return g;
 }
 
+// p = exp(cos(a) - 1): the argument reduced to [-pi, pi] by Cody-Waite
+// reduction with 2*pi split in two floats (hi = 2*pi rounded to float, lo =
+// the remainder), then the hardware approximations __cosf and __expf
+// (absolute error of a few 1e-7 on these ranges, far inside the 2e-3
+// tolerance of the tensor path).
+__device__ __forceinline__ float decode_weight(float arg) {
+    constexpr float kTwoPiHi = 6.28318548202514648f;    // float nearest 2*pi
+    constexpr float kTwoPiLo = -1.74845553146951e-07f;  // 2*pi - kTwoPiHi
+    constexpr float kInvTwoPi = 0.159154943091895336f;
+    const float k = rintf(arg * kInvTwoPi);
+    float r = fmaf(-k, kTwoPiHi, arg);
+    r = fmaf(-k, kTwoPiLo, r);
+    return __expf(__cosf(r) - 1.0f);
+}
+
+// VEC: floats per value load.
+static constexpr int DEC_U = 8;  // value loads per lane in flight (DEC_U * 32 / G rows per warp)
 template <int VEC>
 __global__ void __launch_bounds__(DEC_THREADS) decode_attn_kernel(DecodeArgs a) {
     extern __shared__ float dsm[];
@@ -104,11 +138,21 @@ __global__ void __launch_bounds__(DEC_THREADS) decode_attn_kernel(DecodeArgs a) 
     float *vpart = red + 2 * DEC_WARPS;                // [DEC_THREADS] new-value partial sums
     __shared__ int s_flag;
 
+    // the out_proj grid may launch and load its weights
+    ptx::griddep_launch_dependents();
     const int slot = a.sv.slot ? a.sv.slot[i] : i;
     if (slot < 0 || slot >= a.n_slots) {
         if (split == 0 && h == 0 && tid == 0) atomicOr(a.dev_err, WB_DERR_BOUNDS);
         return;
     }
+    const long long base = (long long)slot * a.sv.seq_stride + (long long)h * a.sv.cap;
+    const float *theta = a.sv.theta + base;
+    const uint8_t *bucket = a.sv.bucket + base;
+    const float *V = a.sv.v + base * hd;
+    const int k0 = split * DEC_CHUNK + warp * DEC_KEYS_PER_WARP;
+    constexpr int KR = DEC_KEYS_PER_WARP / 32;
+    uint8_t kb[KR];
+    float kth[KR];
     const int n = a.len[slot];
     if (n < 0 || n >= a.cap) {
         if (split == 0 && h == 0 && tid == 0) atomicOr(a.dev_err, WB_DERR_BOUNDS);
@@ -116,16 +160,7 @@ __global__ void __launch_bounds__(DEC_THREADS) decode_attn_kernel(DecodeArgs a) 
     }
     const int n_act = n > 0 ? (n + DEC_CHUNK - 1) / DEC_CHUNK : 1;
     if (split >= n_act) return;
-
-    const long long base = wb_slot_base(a.sv, i, h);
-    const float *theta = a.sv.theta + base;
-    const uint8_t *bucket = a.sv.bucket + base;
-    const float *V = a.sv.v + base * hd;
-    const int k0 = split * DEC_CHUNK + warp * DEC_KEYS_PER_WARP;
     // this warp's key loads go out first (bucket byte + phase of every key)
-    constexpr int KR = DEC_KEYS_PER_WARP / 32;
-    uint8_t kb[KR];
-    float kth[KR];
 #pragma unroll
     for (int c = 0; c < KR; c++) {
         const int k = k0 + c * 32 + lane;
@@ -215,7 +250,7 @@ __global__ void __launch_bounds__(DEC_THREADS) decode_attn_kernel(DecodeArgs a) 
         if (k < n) {
             ok = ((amask >> kb[c]) & 1u) || k == n - 1;
             if (ok) {
-                p = expf(cosf(__fmul_rn(hn, __fsub_rn(thq, kth[c]))) - 1.0f);
+                p = decode_weight(__fmul_rn(hn, __fsub_rn(thq, kth[c])));
                 ok = p > 0.0f;  // kv_cache.rs:315 skips zero weights
             }
         }
@@ -238,14 +273,25 @@ __global__ void __launch_bounds__(DEC_THREADS) decode_attn_kernel(DecodeArgs a) 
     float acc[VEC];
 #pragma unroll
     for (int u = 0; u < VEC; u++) acc[u] = 0.0f;
-    constexpr int U = 8;  // 8 * KPW rows in flight per warp
-    for (int b0 = 0; b0 < m; b0 += KPW * U) {
+    // U rows per lane, all U loads issued before the first is used; past
+    // the end of the list a lane re-reads the last kept row with weight 0
+    // (the loads stay unconditional so they can all be in flight)
+    if (vact)
+        for (int b0 = 0; b0 < m; b0 += KPW * DEC_U) {
+            VRow<VEC> rows[DEC_U];
+            float pr[DEC_U];
 #pragma unroll
-        for (int u = 0; u < U; u++) {
-            const int j = b0 + u * KPW + slotk;
-            if (j < m && vact) VecT<VEC>::fma(acc, my_p[j], V + (long long)my_idx[j] * hd + vi * VEC);
+            for (int u = 0; u < DEC_U; u++) {
+                const int j = b0 + u * KPW + slotk;
+                const int jj = min(j, m - 1);
+                rows[u].load(V + (long long)my_idx[jj] * hd + vi * VEC);
+                pr[u] = j < m ? my_p[jj] : 0.0f;
+            }
+#pragma unroll
+            for (int u = 0; u < DEC_U; u++)
+#pragma unroll
+                for (int e = 0; e < VEC; e++) acc[e] = fmaf(pr[u], rows[u].v[e], acc[e]);
         }
-    }
     for (int o = G; o < 32; o <<= 1)
 #pragma unroll
         for (int u = 0; u < VEC; u++) acc[u] += __shfl_xor_sync(0xffffffffu, acc[u], o);
@@ -328,26 +374,48 @@ __global__ void __launch_bounds__(DEC_THREADS) decode_attn_kernel(DecodeArgs a) 
 // column quads x 32 K slices: thread (slice, quad) accumulates 8 rows x 4
 // columns over its slice (weights as float4 straight from global, o rows
 // staged in shared memory), then the 32 slice partials of every output are
-// summed in slice order.  Every load of a phase is issued before any is
-// used.  Block (0, 0) advances the lengths: every attention CTA of the step
-// (the previous launch) has read them.
+// summed in slice order.  Every load of a batch is issued before any is
+// used; the first weight batch goes out before the dependency wait (the
+// weights are not written by the attention grid).  Block (0, 0) advances
+// the lengths: every attention CTA of the step has read them.
 static constexpr int OUT_THREADS = 256;
 static constexpr int OUT_R = 8;                    // rows per block
 static constexpr int OUT_C = 32;                   // columns per block
 static constexpr int OUT_Q = OUT_C / 4;            // column quads
 static constexpr int OUT_S = OUT_THREADS / OUT_Q;  // K slices (32)
 static constexpr int OUT_KC = 2048;                // columns of o staged per pass (64 KB)
+static constexpr int OUT_WB = 12;                  // weight float4 per batch
 
 struct DecodeOutArgs {
     const float *o;     // [n][E]
     const float *wo_t;  // [E(in)][E(out)]
     const float *bo;    // [E]
     float *y;           // [n][E]
-    int n, E;
+    int n, E, cap;
     int32_t *len;
     const int32_t *slot;
     int n_slots;
 };
+
+__device__ __forceinline__ void out_load_w(const DecodeOutArgs &a, int k_abs0, int kend_abs, int c, bool cvec,
+                                           float4 (&w)[OUT_WB]) {
+    const int E = a.E;
+#pragma unroll
+    for (int u = 0; u < OUT_WB; u++) {
+        const int k = k_abs0 + u;
+        w[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (k < kend_abs) {
+            const float *src = a.wo_t + (long long)k * E + c;
+            if (cvec) w[u] = __ldg(reinterpret_cast<const float4 *>(src));
+            else {
+                if (c < E) w[u].x = __ldg(src);
+                if (c + 1 < E) w[u].y = __ldg(src + 1);
+                if (c + 2 < E) w[u].z = __ldg(src + 2);
+                if (c + 3 < E) w[u].w = __ldg(src + 3);
+            }
+        }
+    }
+}
 
 __global__ void __launch_bounds__(OUT_THREADS) decode_out_kernel(DecodeOutArgs a) {
     extern __shared__ float osm[];
@@ -364,6 +432,14 @@ __global__ void __launch_bounds__(OUT_THREADS) decode_out_kernel(DecodeOutArgs a
     for (int r = 0; r < OUT_R; r++)
 #pragma unroll
         for (int u = 0; u < 4; u++) acc[r][u] = 0.0f;
+    // first weight batch of the first pass, then wait for the attention grid
+    float4 w[OUT_WB];
+    {
+        const int kslice = (kc + OUT_S - 1) / OUT_S;
+        const int k0 = ks * kslice, k1 = min(kc, k0 + kslice);
+        out_load_w(a, k0, k1, c, cvec, w);
+    }
+    ptx::griddep_wait();
     for (int kc0 = 0; kc0 < E; kc0 += kc) {
         const int kn = min(kc, E - kc0);
         __syncthreads();
@@ -386,25 +462,10 @@ __global__ void __launch_bounds__(OUT_THREADS) decode_out_kernel(DecodeOutArgs a
         __syncthreads();
         const int kslice = (kn + OUT_S - 1) / OUT_S;
         const int k0 = ks * kslice, k1 = min(kn, k0 + kslice);
-        for (int kb = k0; kb < k1; kb += 12) {
-            float4 w[12];
+        for (int kb = k0; kb < k1; kb += OUT_WB) {
+            if (kc0 > 0 || kb > k0) out_load_w(a, kc0 + kb, kc0 + k1, c, cvec, w);
 #pragma unroll
-            for (int u = 0; u < 12; u++) {
-                const int k = kb + u;
-                w[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (k < k1) {
-                    const float *src = a.wo_t + (long long)(kc0 + k) * E + c;
-                    if (cvec) w[u] = __ldg(reinterpret_cast<const float4 *>(src));
-                    else {
-                        if (c < E) w[u].x = __ldg(src);
-                        if (c + 1 < E) w[u].y = __ldg(src + 1);
-                        if (c + 2 < E) w[u].z = __ldg(src + 2);
-                        if (c + 3 < E) w[u].w = __ldg(src + 3);
-                    }
-                }
-            }
-#pragma unroll
-            for (int u = 0; u < 12; u++) {
+            for (int u = 0; u < OUT_WB; u++) {
                 const int k = kb + u;
                 if (k >= k1) break;
 #pragma unroll
@@ -433,19 +494,19 @@ __global__ void __launch_bounds__(OUT_THREADS) decode_out_kernel(DecodeOutArgs a
     if (blockIdx.x == 0 && blockIdx.y == 0)
         for (int i = tid; i < n; i += OUT_THREADS) {
             const int slot = a.slot ? a.slot[i] : i;
-            if (slot >= 0 && slot < a.n_slots) a.len[slot] += 1;
+            if (slot >= 0 && slot < a.n_slots && a.len[slot] < a.cap) a.len[slot] += 1;
         }
 }
 
-int launch_decode_out(const float *o, const float *wo_t, const float *bo, float *y, int n, int E, int32_t *len,
-                      const int32_t *slot, int n_slots, cudaStream_t st, std::string *msg) {
+int launch_decode_out(const float *o, const float *wo_t, const float *bo, float *y, int n, int E, int cap,
+                      int32_t *len, const int32_t *slot, int n_slots, cudaStream_t st, std::string *msg) {
     ProfScope ps("decode_out", st);
-    DecodeOutArgs a{o, wo_t, bo, y, n, E, len, slot, n_slots};
+    DecodeOutArgs a{o, wo_t, bo, y, n, E, cap, len, slot, n_slots};
     const size_t smem = sizeof(float) * ((size_t)OUT_R * std::min(E, OUT_KC) + OUT_S * OUT_R * OUT_C);
     cudaFuncSetAttribute(decode_out_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     dim3 grid((E + OUT_C - 1) / OUT_C, (n + OUT_R - 1) / OUT_R);
-    decode_out_kernel<<<grid, OUT_THREADS, smem, st>>>(a);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_ex(decode_out_kernel, grid, dim3(OUT_THREADS), smem, st, true, a);
+    if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) {
         *msg = std::string("decode out launch failed: ") + cudaGetErrorString(e);
         return WB_ECUDA;
@@ -478,6 +539,13 @@ void decode_scratch_tickets(int n_seq, int H, int hd, int E, int cap, size_t *of
     *bytes = d.end - d.ticket;
 }
 
+template <int VEC>
+static cudaError_t launch_attn(const DecodeArgs &a, dim3 grid, size_t smem, cudaStream_t st) {
+    cudaFuncSetAttribute(decode_attn_kernel<VEC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    decode_attn_kernel<VEC><<<grid, DEC_THREADS, smem, st>>>(a);
+    return cudaGetLastError();
+}
+
 int launch_decode_attn(const DecodeLaunch &L, void *scratch, size_t scratch_bytes, float **o_out,
                        cudaStream_t st, std::string *msg) {
     const int nsplit = (L.cap + DEC_CHUNK - 1) / DEC_CHUNK;
@@ -507,8 +575,6 @@ int launch_decode_attn(const DecodeLaunch &L, void *scratch, size_t scratch_byte
     a.brs = L.brs;
     a.wv_t = L.wv_t;
     a.bv = L.bv;
-    a.wo_t = L.wo_t;
-    a.bo = L.bo;
     a.hn = L.hn;
     a.n_seq = L.n_seq;
     a.H = L.H;
@@ -524,20 +590,13 @@ int launch_decode_attn(const DecodeLaunch &L, void *scratch, size_t scratch_byte
     const size_t smem = sizeof(float) * ((size_t)L.E + 2 * DEC_WARPS * DEC_KEYS_PER_WARP + DEC_WARPS * L.hd +
                                          DEC_WARPS + 2 * DEC_WARPS + DEC_THREADS);
     dim3 grid(nsplit, L.H, L.n_seq);
+    cudaError_t e;
     {
         ProfScope ps("decode_attn", st);
-        if (L.hd % 4 == 0) {
-            cudaFuncSetAttribute(decode_attn_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            decode_attn_kernel<4><<<grid, DEC_THREADS, smem, st>>>(a);
-        } else if (L.hd % 2 == 0) {
-            cudaFuncSetAttribute(decode_attn_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            decode_attn_kernel<2><<<grid, DEC_THREADS, smem, st>>>(a);
-        } else {
-            cudaFuncSetAttribute(decode_attn_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            decode_attn_kernel<1><<<grid, DEC_THREADS, smem, st>>>(a);
-        }
+        if (L.hd % 4 == 0) e = launch_attn<4>(a, grid, smem, st);
+        else if (L.hd % 2 == 0) e = launch_attn<2>(a, grid, smem, st);
+        else e = launch_attn<1>(a, grid, smem, st);
     }
-    cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         *msg = std::string("decode launch failed: ") + cudaGetErrorString(e);
         return WB_ECUDA;

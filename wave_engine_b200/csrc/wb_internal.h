@@ -97,7 +97,7 @@ void launch_decode_simt(const WbSeqView &sv, const int32_t *len, const float *th
                         const float *v_new, const float *harmonic_n, int n_seq, int H, int hd,
                         float *o, cudaStream_t st);
 void launch_theta_only(const float *rs, int n, float *theta, cudaStream_t st);
-void launch_len_update(int32_t *len, const int32_t *slots, int n_seq, int value, int set,
+void launch_len_update(int32_t *len, const int32_t *slots, int n_seq, int value, int set, int n_slots, int cap,
                        cudaStream_t st);
 void launch_bucket_from_theta(const float *theta, uint8_t *bucket, long long n, cudaStream_t st);
 

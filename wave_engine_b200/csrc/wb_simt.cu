@@ -389,15 +389,21 @@ void launch_theta_only(const float *rs, int n, float *theta, cudaStream_t st) {
 }
 
 // len[slot(i)] += delta (set = 0) or = value (set = 1) for each listed sequence.
-__global__ void len_update_kernel(int32_t *len, const int32_t *slots, int n_seq, int value, int set) {
+// len[slot] = value (set) or len[slot] += value, for slots inside [0,
+// n_slots); an increment stops at cap (a full cache was flagged already).
+__global__ void len_update_kernel(int32_t *len, const int32_t *slots, int n_seq, int value, int set, int n_slots,
+                                  int cap) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n_seq) return;
     const int s = slots ? slots[i] : i;
-    len[s] = set ? value : len[s] + value;
+    if (s < 0 || s >= n_slots) return;
+    if (set) len[s] = value;
+    else if (len[s] < cap) len[s] = min(cap, len[s] + value);
 }
-void launch_len_update(int32_t *len, const int32_t *slots, int n_seq, int value, int set,
+void launch_len_update(int32_t *len, const int32_t *slots, int n_seq, int value, int set, int n_slots, int cap,
                        cudaStream_t st) {
-    if (n_seq > 0) len_update_kernel<<<(n_seq + 127) / 128, 128, 0, st>>>(len, slots, n_seq, value, set);
+    if (n_seq > 0)
+        len_update_kernel<<<(n_seq + 127) / 128, 128, 0, st>>>(len, slots, n_seq, value, set, n_slots, cap);
 }
 
 // Bucket derivation for wb_kv_cache_load: bucket[i] = phase_to_bucket(theta[i]).

@@ -37,6 +37,7 @@
 #include <cudaTypedefs.h>
 
 #include <cmath>
+#include <cstdlib>
 
 namespace wb {
 
@@ -851,20 +852,34 @@ int tc_kv_prefill(const TcLayerWeights &t, const WbSeqView &sv, const float *x, 
     return tc_attention_core(t, sv, nullptr, n_seq, T, y, ws, lay, dev_err, st, msg);
 }
 
+// Rows from which the decode out_proj runs on the tensor-core GEMM (below
+// it the SIMT kernel, launched as a programmatic dependent, is faster: 32
+// rows take 9 us of a 27 us layer step on the SIMT kernel and 21 us on the
+// 128x128-tile GEMM; 256 rows take 49 us on the SIMT kernel and 33 us on
+// the GEMM, B200, graph-replayed steps).
+static constexpr int kDecodeGemmMinRows = 64;
+static int decode_gemm_min_rows() { return kDecodeGemmMinRows; }
+
 int tc_kv_decode(const TcLayerWeights &t, const WbSeqView &sv, int32_t *len, int cap, int n_slots, const float *x,
-                 int n_seq, float *y, void *scratch, size_t scratch_bytes, uint32_t *dev_err, cudaStream_t st,
-                 std::string *msg) {
+                 int n_seq, float *y, void *scratch, size_t scratch_bytes, uint32_t *dev_err, int sm_count,
+                 cudaStream_t st, std::string *msg) {
     if (t.hd > 128) {
         *msg = "fast decode supports head_dim <= 128";
         return WB_ENOTSUP;
     }
     DecodeLaunch L{sv, len, cap, n_slots, x, t.pw.wrs_t, t.pw.brs, t.pw.wv_t, t.pw.bv, t.wo_t, t.b_o, t.harmonic_n,
-                   n_seq, t.H, t.hd, t.E, dev_err};
+                   n_seq, t.H, t.hd, t.E, sm_count, dev_err};
     float *o = nullptr;
     int rc = launch_decode_attn(L, scratch, scratch_bytes, &o, st, msg);
     if (rc) return rc;
-    // out_proj (fp32) and lengths += 1
-    return launch_decode_out(o, t.wo_t, t.b_o, y, n_seq, t.E, len, sv.slot, n_slots, st, msg);
+    if (n_seq >= decode_gemm_min_rows()) {
+        // many rows: out_proj on the tcgen05 TF32 GEMM, then lengths += 1
+        launch_len_update(len, sv.slot, n_seq, 1, 0, n_slots, cap, st);
+        return launch_gemm(true, o, t.w_o32, t.b_o, y, n_seq, t.E, t.E, t.E, dev_err, st, msg);
+    }
+    // few rows: the SIMT out_proj kernel (programmatic dependent of the
+    // attention grid), which also advances the lengths
+    return launch_decode_out(o, t.wo_t, t.b_o, y, n_seq, t.E, cap, len, sv.slot, n_slots, st, msg);
 }
 
 }  // namespace wb

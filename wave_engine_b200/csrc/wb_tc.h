@@ -33,11 +33,12 @@ int tc_gemm_bf16(const __nv_bfloat16 *A, const __nv_bfloat16 *B, const float *bi
                  uint32_t *dev_err, cudaStream_t st, std::string *msg);
 int tc_gemm_tf32(const float *A, const float *B, const float *bias, float *C, int M, int N, int K, uint32_t *dev_err,
                  cudaStream_t st, std::string *msg);
-// Fused decode step (one kernel + a length update) for n_seq sequences of
-// one layer; scratch (the cache's, fixed size, tickets zero) holds the
+// Decode step for n_seq sequences of one layer: attention over the cache
+// with the new position appended, then out_proj and the length update;
+// scratch (the cache's, fixed size, tickets zero) holds the attention
 // kernel's partials.
 int tc_kv_decode(const TcLayerWeights &t, const WbSeqView &sv, int32_t *len, int cap, int n_slots, const float *x,
-                 int n_seq, float *y, void *scratch, size_t scratch_bytes, uint32_t *dev_err, cudaStream_t st,
-                 std::string *msg);
+                 int n_seq, float *y, void *scratch, size_t scratch_bytes, uint32_t *dev_err, int sm_count,
+                 cudaStream_t st, std::string *msg);
 
 }  // namespace wb
