@@ -42,6 +42,19 @@ __host__ __device__ inline float softplus_ref(float x) {
     return x > 20.0f ? x : logf(1.0f + expf(x));
 }
 
+// A warp's 32 x 32 fp32 block, thread = row with its 32 columns in r[],
+// written to the warp's buffer (32 rows padded to 33 floats: conflict-free
+// both ways) so that row j can then be read with the lanes along columns:
+// buf[j * 33 + lane].  Used by the tensor-core epilogues: a store
+// instruction then covers one contiguous 128-byte row segment instead of 32
+// rows.
+__device__ __forceinline__ void warp_stage32(float *buf, const uint32_t (&r)[32], int lane) {
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < 32; i++) buf[lane * 33 + i] = __uint_as_float(r[i]);
+    __syncwarp();
+}
+
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));

@@ -176,8 +176,16 @@ __global__ void __launch_bounds__(128, 1)
     if (!fin && tid == 0) atomicOr(a.dev_err, WB_DERR_TIMEOUT_MMA);
     ptx::tc_fence_after();
     if (fin) {
-        const int m = m0 + tid;
-        const int b = m / a.T, t = m - (m / a.T) * a.T;
+        // the pipeline stages are free (every MMA has completed): each warp
+        // stages its 32 rows chunk by chunk and stores them row by row, lane
+        // = column (a value row segment of one head, or a content row)
+        float *buf = reinterpret_cast<float *>(sm) + warp * 32 * 33;
+        const int lane = tid & 31;
+        // this lane's row (for the per-row cache offsets, shuffled below)
+        const int mr = m0 + warp * 32 + lane;
+        const int br = mr / a.T, tr = mr - br * a.T;
+        const long long slot_r = mr < a.R ? (a.sv.slot ? a.sv.slot[br] : br) : 0;
+        const long long row_off = slot_r * a.sv.seq_stride + tr;  // + h * cap per head
 #pragma unroll 1
         for (int c = 0; c < PBN / 32; c++) {
             uint32_t r[32], rc[32];
@@ -186,18 +194,20 @@ __global__ void __launch_bounds__(128, 1)
             ptx::tmem_ld_wait();
 #pragma unroll
             for (int i = 0; i < 32; i++) r[i] = __float_as_uint(__uint_as_float(r[i]) + __uint_as_float(rc[i]));
-            if (m >= a.R) continue;
-#pragma unroll
-            for (int i = 0; i < 32; i++) {
-                const int n = n0 + c * 32 + i;
-                if (n >= a.N) break;
-                const float v = __uint_as_float(r[i]) + a.bias[n];
-                if (n < a.n_v) {
-                    const int h = n / a.hd, d = n - h * a.hd;
-                    a.sv.v[(wb_slot_base(a.sv, b, h) + t) * a.hd + d] = v;
-                } else if (n < a.n_v + a.n_c) {
-                    if (a.content) a.content[(long long)m * a.n_c + (n - a.n_v)] = v;
-                }
+            warp_stage32(buf, r, lane);
+            const int n = n0 + c * 32 + lane;
+            const bool is_v = n < a.n_v, is_c = !is_v && n < a.n_v + a.n_c && a.content;
+            const float bv = n < a.N ? a.bias[n] : 0.0f;
+            const int h = is_v ? n / a.hd : 0, d = is_v ? n - h * a.hd : 0;
+            const long long hoff = (long long)h * a.sv.cap;
+#pragma unroll 4
+            for (int j = 0; j < 32; j++) {
+                const int m = m0 + warp * 32 + j;
+                const long long off = __shfl_sync(0xffffffffu, row_off, j);
+                if (m >= a.R) continue;
+                const float v = buf[j * 33 + lane] + bv;
+                if (is_v) a.sv.v[(off + hoff) * a.hd + d] = v;
+                else if (is_c) a.content[(long long)m * a.n_c + (n - a.n_v)] = v;
             }
         }
     }
@@ -209,70 +219,108 @@ __global__ void __launch_bounds__(128, 1)
 // ---------------------------------------------------------------------------
 // Phases: (r, s) = b + sum_j W[.][j] x[j] in fp32, j in order (attn.rs:124-127
 // with fused multiply-adds), then theta = atan2f(s, r) and its bucket
-// (attn.rs:127, :171-174).  One row per thread, 128 rows per CTA; x tiles of
-// 64 columns and the matching phase weights [64][H][2] are staged in shared
-// memory (x padded by one float per row against bank conflicts).
+// (attn.rs:127, :171-174).  Every output keeps one sequential sum in one
+// thread (the phase decides a discrete bucket, so the sum is not split).
+// CTA = 128 rows x all 2H outputs, 256 threads: thread (row pair p, output
+// group g) owns rows p and p + 64 and outputs g*OPT .. g*OPT + OPT - 1 (OPT
+// = 2H / 4 rounded up to even: whole (r, s) pairs).  x arrives in chunks of
+// PH_KC columns, staged in shared memory with rows padded to PH_KC + 1
+// floats (the lanes of a warp read 32 rows of one column: conflict-free);
+// the next chunk's loads are in flight while the current one is used.  The
+// chunk's phase weights [PH_KC][2H] sit beside it (read as broadcasts).
 // ---------------------------------------------------------------------------
-static constexpr int PH_ROWS = 128, PH_KC = 32;
+static constexpr int PH_ROWS = 128, PH_THREADS = 256;
 
-template <int PH_MAXO>  // 2 * max heads: 32 (H <= 16) or 64 (H <= 32)
-__global__ void __launch_bounds__(PH_ROWS) phase_fma_kernel(const float *__restrict__ x, const float *__restrict__ wrs_t,
-                                                           const float *__restrict__ brs, int R, int E, int H, int T,
-                                                           WbSeqView sv) {
-    __shared__ float xs[PH_ROWS * (PH_KC + 1)];
-    __shared__ __align__(16) float ws[PH_KC * PH_MAXO];
+template <int OPT, int KC>
+__global__ void __launch_bounds__(PH_THREADS, 3) phase_fma_kernel(const float *__restrict__ x,
+                                                                const float *__restrict__ wrs_t,
+                                                                const float *__restrict__ brs, int R, int E, int H,
+                                                                int T, WbSeqView sv) {
+    constexpr int WST = 4 * OPT;                        // weight row stride: 4 groups x OPT outputs
+    constexpr int RPL = PH_THREADS / KC;                // rows covered by one load instruction
+    constexpr int XLD = PH_ROWS / RPL;                  // x loads per thread per chunk
+    constexpr int WLD = (KC * WST + PH_THREADS - 1) / PH_THREADS;
+    __shared__ float xs[2][PH_ROWS * (KC + 1)];
+    __shared__ __align__(16) float ws[2][KC * WST];
     const int tid = threadIdx.x;
     const int m0 = blockIdx.x * PH_ROWS;
     const int NO = 2 * H;
-    float acc[PH_MAXO];
+    const int rp = tid % (PH_ROWS / 2), g = tid / (PH_ROWS / 2);
+    const int o0 = g * OPT;
+    float acc[2][OPT];
 #pragma unroll
-    for (int o = 0; o < PH_MAXO; o++) acc[o] = o < NO ? brs[o] : 0.0f;
-    for (int k0 = 0; k0 < E; k0 += PH_KC) {
-        const int kn = min(PH_KC, E - k0);
-        __syncthreads();
-        // x tile: each warp loads rows with lanes along k (coalesced), all
-        // loads of the thread issued before the stores
-        {
-            float v[PH_KC];  // PH_KC per thread
-#pragma unroll
-            for (int u = 0; u < PH_KC; u++) {
-                const int e = u * PH_ROWS + tid;  // e = row * 64 + k
-                const int row = e / PH_KC, k = e % PH_KC;
-                v[u] = (m0 + row < R && k < kn) ? __ldg(x + (long long)(m0 + row) * E + k0 + k) : 0.0f;
-            }
-#pragma unroll
-            for (int u = 0; u < PH_KC; u++) {
-                const int e = u * PH_ROWS + tid;
-                xs[(e / PH_KC) * (PH_KC + 1) + (e % PH_KC)] = v[u];
-            }
-        }
-        for (int e = tid; e < kn * NO; e += PH_ROWS) ws[(e / NO) * PH_MAXO + (e % NO)] = wrs_t[(long long)k0 * NO + e];
-        __syncthreads();
-        const float *xr = xs + tid * (PH_KC + 1);
-        for (int k = 0; k < kn; k++) {
-            const float xv = xr[k];
-            const float4 *w4 = reinterpret_cast<const float4 *>(ws + k * PH_MAXO);
-#pragma unroll
-            for (int o4 = 0; o4 < PH_MAXO / 4; o4++) {
-                if (o4 * 4 >= NO) break;
-                const float4 w = w4[o4];
-                acc[o4 * 4 + 0] = fmaf(w.x, xv, acc[o4 * 4 + 0]);
-                acc[o4 * 4 + 1] = fmaf(w.y, xv, acc[o4 * 4 + 1]);
-                acc[o4 * 4 + 2] = fmaf(w.z, xv, acc[o4 * 4 + 2]);
-                acc[o4 * 4 + 3] = fmaf(w.w, xv, acc[o4 * 4 + 3]);
-            }
-        }
+    for (int q = 0; q < OPT; q++) {
+        const float b = o0 + q < NO ? brs[o0 + q] : 0.0f;
+        acc[0][q] = b;
+        acc[1][q] = b;
     }
-    const int m = m0 + tid;
-    if (m >= R) return;
-    const int b = m / T, t = m - b * T;
+    // this thread's x loads: column lc of rows lr, lr + RPL, ... (one base
+    // pointer, constant stride); all of a chunk's loads go out together
+    const int lc = tid % KC, lr = tid / KC;
+    const long long xstride = (long long)RPL * E;
+    float xv[XLD];
+    float wv[WLD];
+    auto load_chunk = [&](int k0) {
+        const bool colok = k0 + lc < E;
+        const float *xp = x + (long long)(m0 + lr) * E + k0 + lc;
 #pragma unroll
-    for (int h = 0; h < PH_MAXO / 2; h++) {
-        if (h >= H) break;
-        const float th = atan2f(acc[2 * h + 1], acc[2 * h]);
-        const long long pos = wb_slot_base(sv, b, h) + t;
-        sv.theta[pos] = th;
-        sv.bucket[pos] = (uint8_t)phase_to_bucket(th);
+        for (int u = 0; u < XLD; u++)
+            xv[u] = (colok && m0 + lr + u * RPL < R) ? __ldg(xp + u * xstride) : 0.0f;
+#pragma unroll
+        for (int u = 0; u < WLD; u++) {
+            const int e = u * PH_THREADS + tid;
+            const int k = e / WST, o = e % WST;
+            wv[u] = (e < KC * WST && k0 + k < E && o < NO) ? __ldg(wrs_t + (long long)(k0 + k) * NO + o) : 0.0f;
+        }
+    };
+    auto store_chunk = [&](int buf) {
+#pragma unroll
+        for (int u = 0; u < XLD; u++) xs[buf][(lr + u * RPL) * (KC + 1) + lc] = xv[u];
+#pragma unroll
+        for (int u = 0; u < WLD; u++) {
+            const int e = u * PH_THREADS + tid;
+            if (e < KC * WST) ws[buf][e] = wv[u];
+        }
+    };
+    load_chunk(0);
+    store_chunk(0);
+    int buf = 0;
+    for (int k0 = 0; k0 < E; k0 += KC) {
+        __syncthreads();  // chunk `buf` stored; chunk buf ^ 1 free
+        const bool more = k0 + KC < E;
+        if (more) load_chunk(k0 + KC);
+        const int kn = min(KC, E - k0);
+        const float *x0 = xs[buf] + rp * (KC + 1);
+        const float *x1 = xs[buf] + (rp + PH_ROWS / 2) * (KC + 1);
+        const float *wr = ws[buf] + o0;
+        for (int k = 0; k < kn; k++) {
+            const float a0 = x0[k], a1 = x1[k];
+#pragma unroll
+            for (int q = 0; q < OPT; q += 2) {
+                const float2 w = *reinterpret_cast<const float2 *>(wr + k * WST + q);
+                acc[0][q] = fmaf(w.x, a0, acc[0][q]);
+                acc[0][q + 1] = fmaf(w.y, a0, acc[0][q + 1]);
+                acc[1][q] = fmaf(w.x, a1, acc[1][q]);
+                acc[1][q + 1] = fmaf(w.y, a1, acc[1][q + 1]);
+            }
+        }
+        if (more) store_chunk(buf ^ 1);
+        buf ^= 1;
+    }
+#pragma unroll
+    for (int rr = 0; rr < 2; rr++) {
+        const int m = m0 + rp + rr * (PH_ROWS / 2);
+        if (m >= R) continue;
+        const int b = m / T, t = m - b * T;
+#pragma unroll
+        for (int q = 0; q < OPT; q += 2) {
+            const int h = (o0 + q) / 2;
+            if (h >= H) break;
+            const float th = atan2f(acc[rr][q + 1], acc[rr][q]);
+            const long long pos = wb_slot_base(sv, b, h) + t;
+            sv.theta[pos] = th;
+            sv.bucket[pos] = (uint8_t)phase_to_bucket(th);
+        }
     }
 }
 
@@ -410,8 +458,12 @@ int launch_proj_tc(const ProjTcWeights &p, const float *wrs_t, const float *brs,
     {
         ProfScope pp("phase_fma", st);
         const unsigned pg = (unsigned)((R + PH_ROWS - 1) / PH_ROWS);
-        if (p.H <= 16) phase_fma_kernel<32><<<pg, PH_ROWS, 0, st>>>(x, wrs_t, brs, (int)R, p.E, p.H, T, sv);
-        else phase_fma_kernel<64><<<pg, PH_ROWS, 0, st>>>(x, wrs_t, brs, (int)R, p.E, p.H, T, sv);
+        if (p.H <= 12)
+            phase_fma_kernel<6, 32><<<pg, PH_THREADS, 0, st>>>(x, wrs_t, brs, (int)R, p.E, p.H, T, sv);
+        else if (p.H <= 16)
+            phase_fma_kernel<8, 32><<<pg, PH_THREADS, 0, st>>>(x, wrs_t, brs, (int)R, p.E, p.H, T, sv);
+        else
+            phase_fma_kernel<16, 16><<<pg, PH_THREADS, 0, st>>>(x, wrs_t, brs, (int)R, p.E, p.H, T, sv);
     }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {

@@ -102,102 +102,190 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
 }
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
+// Features of the attention core, one warp per 32 consecutive rows
+// i = bh * T + t (8 warps per CTA).  Lane l owns row i0 + l for the per-row
+// quantities (phase, bucket, content, self score, previous-position term);
+// its Q and K feature rows (FW bf16 each) are built in a per-warp shared
+// buffer (rows padded to 33 words: conflict-free) and leave as one
+// contiguous block of 32 rows (lanes along the words).  Value rows are
+// converted with the lanes along the row (VC floats per lane, 8 rows of
+// loads in flight).  The previous position's phase, bucket and content come
+// from the neighbouring lane (lane 0 loads them).
+static constexpr int FEAT_WARPS = 8;
+
 template <bool WIDE>
-__global__ void __launch_bounds__(256) feat_kernel(FeatArgs a) {
+__global__ void __launch_bounds__(FEAT_WARPS * 32) feat_kernel(FeatArgs a) {
     constexpr int FW = WIDE ? 64 : 32;        // feature width
     constexpr int BB = WIDE ? 54 : 22;        // first bucket column
-    const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
-    const long long BH = (long long)a.B * a.H;
-    if (i >= BH * a.T) return;
-    const int bh = (int)(i / a.T), t = (int)(i - (long long)bh * a.T);
+    constexpr int FWW = FW / 2;               // 32-bit words per feature row
+    constexpr int RS = FWW + 1;               // padded row stride (words)
+    __shared__ uint32_t fbuf[FEAT_WARPS][32 * RS];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const long long BH = (long long)a.B * a.H, total = BH * a.T;
+    const long long i0 = ((long long)blockIdx.x * FEAT_WARPS + warp) * 32;
+    if (i0 >= total) return;
+    const long long i = i0 + lane;
+    const bool live = i < total;
+    const long long ii = live ? i : total - 1;
+    const int bh = (int)(ii / a.T), t = (int)(ii - (long long)bh * a.T);
     const int b = bh / a.H, h = bh - b * a.H;
     const long long base = wb_slot_base(a.sv, b, h);
     const float th = a.sv.theta[base + t];
     const int bk = a.sv.bucket[base + t];
     const float n = a.hn[h];
+    const int C = a.content ? a.C : 0;
+    float c[16];
+    {
+        const float *cr = C ? a.content + ((long long)b * a.T + t) * ((long long)a.H * C) + (long long)h * C : nullptr;
+#pragma unroll
+        for (int d = 0; d < 16; d++) c[d] = (d < C) ? cr[d] : 0.0f;
+    }
+    float c2 = 0.0f;
+#pragma unroll
+    for (int d = 0; d < 16; d++) c2 = fmaf(c[d], c[d], c2);
     float sn, cs;
     sincosf(n * th, &sn, &cs);
     const float csh = bf16_round(cs), snh = bf16_round(sn);
     const float csl = cs - csh, snl = sn - snh;
-    float c[16];
-    float c2 = 0.0f;
-    const int C = a.content ? a.C : 0;
-#pragma unroll
-    for (int d = 0; d < 16; d++) {
-        c[d] = (d < C) ? a.content[((long long)b * a.T + t) * ((long long)a.H * C) + (long long)h * C + d] : 0.0f;
-        c2 = fmaf(c[d], c[d], c2);
-    }
-    float qv[FW], kv[FW];
-#pragma unroll
-    for (int u = 0; u < FW; u++) qv[u] = kv[u] = 0.0f;
-    qv[0] = csh; qv[1] = csl; qv[2] = csh; qv[3] = snh; qv[4] = snl; qv[5] = snh;
-    kv[0] = csh; kv[1] = csh; kv[2] = csl; kv[3] = snh; kv[4] = snh; kv[5] = snl;
-#pragma unroll
-    for (int d = 0; d < 16; d++) {
-        const float cq = c[d] * a.cscale;
-        if (WIDE) {
-            const float qh = bf16_round(cq), kh = bf16_round(c[d]);
-            qv[6 + 3 * d] = qh; qv[7 + 3 * d] = cq - qh; qv[8 + 3 * d] = qh;
-            kv[6 + 3 * d] = kh; kv[7 + 3 * d] = kh; kv[8 + 3 * d] = c[d] - kh;
-        } else {
-            qv[6 + d] = cq;
-            kv[6 + d] = c[d];
-        }
-    }
     const uint32_t allow = allowed_bucket_mask(bk);
+
+    // ---- Q and K feature rows through the warp's buffer
+    uint32_t *fb = fbuf[warp];
+    auto emit = [&](__nv_bfloat16 *dst) {
+        __syncwarp();
+        const long long words = min(32LL, total - i0) * FWW;
+        uint32_t *g = reinterpret_cast<uint32_t *>(dst + i0 * FW);
+        for (int w = lane; w < words; w += 32) g[w] = fb[(w / FWW) * RS + (w % FWW)];
+        __syncwarp();
+    };
+    {
+        uint32_t *row = fb + lane * RS;
+        float q[FW];
 #pragma unroll
-    for (int u = 0; u < 8; u++) {
-        qv[BB + u] = ((allow >> u) & 1u) ? 0.0f : MASK_BIAS;
-        kv[BB + u] = (bk == u) ? 1.0f : 0.0f;
-    }
-    uint4 *qd = reinterpret_cast<uint4 *>(a.qf + i * FW);
-    uint4 *kd = reinterpret_cast<uint4 *>(a.kf + i * FW);
+        for (int u = 0; u < FW; u++) q[u] = 0.0f;
+        q[0] = csh; q[1] = csl; q[2] = csh; q[3] = snh; q[4] = snl; q[5] = snh;
 #pragma unroll
-    for (int u = 0; u < FW / 8; u++) {
-        qd[u] = make_uint4(pack_bf16(qv[8 * u], qv[8 * u + 1]), pack_bf16(qv[8 * u + 2], qv[8 * u + 3]),
-                           pack_bf16(qv[8 * u + 4], qv[8 * u + 5]), pack_bf16(qv[8 * u + 6], qv[8 * u + 7]));
-        kd[u] = make_uint4(pack_bf16(kv[8 * u], kv[8 * u + 1]), pack_bf16(kv[8 * u + 2], kv[8 * u + 3]),
-                           pack_bf16(kv[8 * u + 4], kv[8 * u + 5]), pack_bf16(kv[8 * u + 6], kv[8 * u + 7]));
-    }
-    // values (hi, and lo in wide mode), zero padded to hdp
-    const float *vrow = a.sv.v + (base + t) * a.hd;
-    __nv_bfloat16 *vdh = a.vh + i * a.hdp;
-    __nv_bfloat16 *vdl = WIDE ? a.vl + i * a.hdp : nullptr;
-    for (int d = 0; d < a.hdp; d += 8) {
-        float v[8], vlo[8];
-#pragma unroll
-        for (int u = 0; u < 8; u++) {
-            v[u] = (d + u < a.hd) ? vrow[d + u] : 0.0f;
-            vlo[u] = v[u] - bf16_round(v[u]);
+        for (int d = 0; d < 16; d++) {
+            const float cq = c[d] * a.cscale;
+            if (WIDE) {
+                const float qh = bf16_round(cq);
+                q[6 + 3 * d] = qh; q[7 + 3 * d] = cq - qh; q[8 + 3 * d] = qh;
+            } else {
+                q[6 + d] = cq;
+            }
         }
-        *reinterpret_cast<uint4 *>(vdh + d) = make_uint4(pack_bf16(v[0], v[1]), pack_bf16(v[2], v[3]),
-                                                         pack_bf16(v[4], v[5]), pack_bf16(v[6], v[7]));
-        if (WIDE)
-            *reinterpret_cast<uint4 *>(vdl + d) = make_uint4(pack_bf16(vlo[0], vlo[1]), pack_bf16(vlo[2], vlo[3]),
-                                                             pack_bf16(vlo[4], vlo[5]), pack_bf16(vlo[6], vlo[7]));
-    }
-    // self score, previous-position term, content norm
-    const float self = 1.0f + c2 * a.cscale;
-    a.m0[i] = self;
-    const float cn = sqrtf(c2);
-    a.cnorm[i] = cn;
-    atomicMax(a.cmax + bh, __float_as_uint(cn));
-    float sp = -INFINITY;
-    if (t > 0) {
-        const int bkp = a.sv.bucket[base + t - 1];
-        if (!((allow >> bkp) & 1u)) {
-            sp = cosf(n * (th - a.sv.theta[base + t - 1]));
-            if (C) {
-                const float *cp = a.content + ((long long)b * a.T + t - 1) * ((long long)a.H * C) + (long long)h * C;
-                float dot = 0.0f;
 #pragma unroll
-                for (int d = 0; d < 16; d++)
-                    if (d < C) dot = fmaf(c[d], cp[d], dot);
-                sp += dot * a.cscale;
+        for (int u = 0; u < 8; u++) q[BB + u] = ((allow >> u) & 1u) ? 0.0f : MASK_BIAS;
+#pragma unroll
+        for (int w = 0; w < FWW; w++) row[w] = pack_bf16(q[2 * w], q[2 * w + 1]);
+        emit(a.qf);
+#pragma unroll
+        for (int u = 0; u < FW; u++) q[u] = 0.0f;
+        q[0] = csh; q[1] = csh; q[2] = csl; q[3] = snh; q[4] = snh; q[5] = snl;
+#pragma unroll
+        for (int d = 0; d < 16; d++) {
+            if (WIDE) {
+                const float kh = bf16_round(c[d]);
+                q[6 + 3 * d] = kh; q[7 + 3 * d] = kh; q[8 + 3 * d] = c[d] - kh;
+            } else {
+                q[6 + d] = c[d];
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 8; u++) q[BB + u] = (bk == u) ? 1.0f : 0.0f;
+#pragma unroll
+        for (int w = 0; w < FWW; w++) row[w] = pack_bf16(q[2 * w], q[2 * w + 1]);
+        emit(a.kf);
+    }
+
+    // ---- values: hi (and lo in wide mode), zero padded to hdp; lanes
+    // along the row, VC floats per lane
+    {
+        const int hd = a.hd, hdp = a.hdp;
+        const int nrows = (int)min(32LL, total - i0);
+        const long long vrow0 = base + t;  // this lane's value row (cache view)
+        for (int j0 = 0; j0 < nrows; j0 += 8) {
+            float2 v[8][2];
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                const int j = j0 + u;
+                const long long vr = __shfl_sync(0xffffffffu, vrow0, j & 31);
+                const float *src = a.sv.v + vr * hd;
+#pragma unroll
+                for (int q = 0; q < 2; q++) {
+                    const int col = (q * 32 + lane) * 2;  // columns col, col + 1
+                    float2 x2 = make_float2(0.f, 0.f);
+                    if (j < nrows && col < hdp) {
+                        if (col + 1 < hd) x2 = *reinterpret_cast<const float2 *>(src + col);
+                        else if (col < hd) x2.x = src[col];
+                    }
+                    v[u][q] = x2;
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                const int j = j0 + u;
+                if (j >= nrows) break;
+#pragma unroll
+                for (int q = 0; q < 2; q++) {
+                    const int col = (q * 32 + lane) * 2;
+                    if (col >= hdp) continue;
+                    const float2 x2 = v[u][q];
+                    const long long o = (i0 + j) * hdp + col;
+                    *reinterpret_cast<uint32_t *>(a.vh + o) = pack_bf16(x2.x, x2.y);
+                    if (WIDE)
+                        *reinterpret_cast<uint32_t *>(a.vl + o) =
+                            pack_bf16(x2.x - bf16_round(x2.x), x2.y - bf16_round(x2.y));
+                }
             }
         }
     }
-    a.sprev[i] = sp;
+
+    // ---- self score, content norm, previous-position term
+    const float self = 1.0f + c2 * a.cscale;
+    const float cn = sqrtf(c2);
+    // previous position: the lane below (same bh), lane 0 loads it
+    float thp = __shfl_up_sync(0xffffffffu, th, 1);
+    int bkp = __shfl_up_sync(0xffffffffu, bk, 1);
+    float cp[16];
+#pragma unroll
+    for (int d = 0; d < 16; d++) cp[d] = __shfl_up_sync(0xffffffffu, c[d], 1);
+    const int bh_below = __shfl_up_sync(0xffffffffu, bh, 1);
+    if (t > 0 && (lane == 0 || bh_below != bh)) {
+        thp = a.sv.theta[base + t - 1];
+        bkp = a.sv.bucket[base + t - 1];
+        const float *cr =
+            C ? a.content + ((long long)b * a.T + t - 1) * ((long long)a.H * C) + (long long)h * C : nullptr;
+#pragma unroll
+        for (int d = 0; d < 16; d++) cp[d] = (d < C) ? cr[d] : 0.0f;
+    }
+    float sp = -INFINITY;
+    if (t > 0 && !((allow >> bkp) & 1u)) {
+        sp = cosf(n * (th - thp));
+        if (C) {
+            float dot = 0.0f;
+#pragma unroll
+            for (int d = 0; d < 16; d++)
+                if (d < C) dot = fmaf(c[d], cp[d], dot);
+            sp += dot * a.cscale;
+        }
+    }
+    if (live) {
+        a.m0[i] = self;
+        a.cnorm[i] = cn;
+        a.sprev[i] = sp;
+    }
+    // per-(b, h) maximum content norm: one atomic per run of equal bh
+    float mx = live ? cn : 0.0f;
+    const unsigned same = __match_any_sync(0xffffffffu, bh);
+    const int leader = __ffs(same) - 1;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float other = __shfl_xor_sync(0xffffffffu, mx, o);
+        const int obh = __shfl_xor_sync(0xffffffffu, bh, o);
+        if (obh == bh) mx = fmaxf(mx, other);
+    }
+    if (lane == leader && live) atomicMax(a.cmax + bh, __float_as_uint(mx));
 }
 
 // ---------------------------------------------------------------------------
@@ -549,19 +637,22 @@ __global__ void __launch_bounds__(128, 1)
     if (!fin && tid == 0) atomicOr(dev_err, WB_DERR_TIMEOUT_MMA);
     ptx::tc_fence_after();
     if (fin) {
-        const int m = m0 + tid;
+        // the pipeline stages are free (every MMA has completed): each warp
+        // stages its 32 rows chunk by chunk and stores them row by row
+        float *buf = reinterpret_cast<float *>(sm) + warp * 32 * 33;
+        const int lane = tid & 31;
 #pragma unroll 1
         for (int c = 0; c < GBN / 32; c++) {
             uint32_t r[32];
             ptx::tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + c * 32, r);
             ptx::tmem_ld_wait();
-            if (m < M) {
-                float *dst = C + (long long)m * ldc + n0 + c * 32;
-#pragma unroll
-                for (int i = 0; i < 32; i++) {
-                    const int n = n0 + c * 32 + i;
-                    if (n < N) dst[i] = __uint_as_float(r[i]) + bias[n];
-                }
+            warp_stage32(buf, r, lane);
+            const int n = n0 + c * 32 + lane;
+            const float bv = n < N ? bias[n] : 0.0f;
+#pragma unroll 4
+            for (int j = 0; j < 32; j++) {
+                const int m = m0 + warp * 32 + j;
+                if (m < M && n < N) C[(long long)m * ldc + n] = buf[j * 33 + lane] + bv;
             }
         }
     }
@@ -732,11 +823,11 @@ static int tc_attention_core(const TcLayerWeights &t, const WbSeqView &sv, const
     }
     const float cscale = content ? 1.0f / std::sqrt((float)t.C) : 0.0f;
     FeatArgs fa{sv, content, content ? t.C : 0, cscale, t.harmonic_n, B, H, T, hd, hdp, qf, kf, vh, vl, m0, sp, cn, cm};
-    const unsigned fgrid = (unsigned)((BH * T + 255) / 256);
+    const unsigned fgrid = (unsigned)((BH * T + FEAT_WARPS * 32 - 1) / (FEAT_WARPS * 32));
     {
         ProfScope ps("feat", st);
-        if (wide) feat_kernel<true><<<fgrid, 256, 0, st>>>(fa);
-        else feat_kernel<false><<<fgrid, 256, 0, st>>>(fa);
+        if (wide) feat_kernel<true><<<fgrid, FEAT_WARPS * 32, 0, st>>>(fa);
+        else feat_kernel<false><<<fgrid, FEAT_WARPS * 32, 0, st>>>(fa);
     }
 
     CUtensorMap tq, tk, tvh, tvl;
