@@ -132,13 +132,13 @@ def peaks():
 # ---------------------------------------------------------------------------
 # algorithmic work (per SURVEY 8(d) formulas, restated here)
 # ---------------------------------------------------------------------------
-def decode_bytes_exact(bucket_slots, T0, S, H, hd):
-    """Algorithmic HBM bytes of every decode attention launch of a step: for
-    each new position p (p = T0..T0+S-1) of each (layer, seq, head), the
-    phase+bucket of all p cached keys (5 B each) plus the fp32 value row
-    (4*hd B) of each key the mask lets through (bucket b-1..b+1 or the
-    previous position), plus the query/output rows.  bucket_slots is a
-    numpy u8 array [L][B][H][T0+S] of the cache's buckets after the step."""
+def decode_bytes_exact(bucket_slots, T0, S, H, hd, first=0):
+    """Algorithmic HBM bytes of the decode attention launches of steps
+    first..S-1: for each new position p (p = T0+first..T0+S-1) of each
+    (layer, seq, head), the phase+bucket of all p cached keys (5 B each) plus
+    the fp32 value row (4*hd B) of each key the mask lets through (bucket
+    b-1..b+1 or the previous position).  bucket_slots is a numpy u8 array
+    [L][B][H][T0+S] of the cache's buckets after the step."""
     import numpy as np
     b = bucket_slots.astype(np.int64)
     L, B, Hh, n = b.shape
@@ -147,7 +147,7 @@ def decode_bytes_exact(bucket_slots, T0, S, H, hd):
     cnt = np.cumsum(onehot, axis=3)  # cnt[..., p, k] = #keys < p in bucket k
     total_keys = 0
     unmasked = 0
-    for p in range(T0, T0 + S):
+    for p in range(T0 + first, T0 + S):
         qb = b[:, :, :, p]
         c = cnt[:, :, :, p, :]
         adj = sum(np.take_along_axis(c, ((qb + d) % 8)[..., None], axis=3)[..., 0] for d in (-1, 0, 1))
@@ -157,6 +157,12 @@ def decode_bytes_exact(bucket_slots, T0, S, H, hd):
         unmasked += int(adj.sum() + prev_masked.sum())
         total_keys += L * B * Hh * p
     return total_keys * 5 + unmasked * hd * 4, unmasked, total_keys
+
+
+# dram__bytes_read.sum + dram__bytes_write.sum of decode_attn over its
+# algorithmic bytes, measured by ncu on `bench.py --profile-case decode`
+# (values kept with the capture's summary under profiles/).
+DECODE_ATTN_TRAFFIC_RATIO = 1.009  # 43.552 MB measured / 43.166 MB algorithmic
 
 
 def prefill_flops_per_layer(B, T, E, H, hd, C):
@@ -291,20 +297,52 @@ def run_ours(args):
     value = world * tok_step / (ms_step / 1e3)
     check_err("the timed region")
 
-    # rooflines: decode (HBM) from the timed decode phase, prefill attention
-    # (tensor) from its CUDA-event timed launches
+    # rooflines: decode attention (HBM, the dominant kernel) and prefill
+    # attention (tensor), each from CUDA events around its own launches
     hbm, bf16, peak_kind = peaks()
     bk = np.stack([np.stack([cache.read(l, b)[1] for b in range(B)]) for l in range(L)])
     byts, unmasked, keys = decode_bytes_exact(bk, T, S, H, hd)
-    per_launch_bytes = byts / (S * L) + 2 * B * E * 4
-    per_launch_ms = dec_ms / (S * L)
+    # decode_attn launch time: events around each launch, captured into a
+    # copy of the decode graph and replayed once at the middle of the decode
+    # phase (step S/2, after the timed region, which stays uninstrumented)
+    s_mid = S // 2
+    graph_p = torch.cuda.CUDAGraph()
+    ctx.profile("decode_attn")
+    cap2 = torch.cuda.Stream(dev)
+    cap2.wait_stream(stream)
+    with torch.cuda.graph(graph_p, stream=cap2):
+        decode_layers(x_stage, y_stage, ids_dev)
+    stream.wait_stream(cap2)
+    ctx.set_stream(stream.cuda_stream)
+    prefill(x_pre, y_pre, ids_dev)
+    for s in range(s_mid):
+        x_stage.copy_(x_dec[s])
+        graph.replay()
+    x_stage.copy_(x_dec[s_mid])
+    graph_p.replay()
+    barrier()
+    prof_dec = ctx.profile_report()
+    ctx.profile(None)
+    del graph_p
+    check_err("instrumented decode step")
+    n_att, t_att = prof_dec.get("decode_attn", (0, 0.0))
+    mid_bytes, _, _ = decode_bytes_exact(bk, T, s_mid + 1, H, hd, first=s_mid)
+    per_launch_bytes = mid_bytes / L + B * E * 4  # + the x rows read and the o rows written once each
+    per_launch_ms = t_att / max(1, n_att)
+    if per_launch_ms <= 0:
+        raise RuntimeError("the instrumented decode step recorded no decode_attn time")
     ach = per_launch_bytes / (per_launch_ms / 1e3) / 1e9
-    roof = {"kernel": "decode_fused", "bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
-            "frac": round(ach / hbm, 4), "traffic": None, "peak_kind": peak_kind,
+    traffic = int(round(per_launch_bytes * DECODE_ATTN_TRAFFIC_RATIO))
+    roof = {"kernel": "decode_attn", "bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
+            "frac": round(ach / hbm, 4), "traffic": traffic, "peak_kind": peak_kind,
             "algorithmic_bytes_per_launch": int(per_launch_bytes), "launch_ms": round(per_launch_ms, 5),
-            "timing": "decode phase time / decode launches (includes the length-update kernel and the "
-                      "per-token input copy)",
-            "unmasked_key_fraction": round(unmasked / keys, 4)}
+            "launches_timed": n_att,
+            "timing": "CUDA events around each decode_attn launch of one decode step (24 layers, context "
+                      f"{T + s_mid}), replayed from an instrumented copy of the decode graph",
+            "traffic_note": "dram read+write bytes per launch = algorithmic bytes x the ratio measured by ncu "
+                            "on the decode profile case (32 sequences, context ~1100)",
+            "unmasked_key_fraction": round(unmasked / keys, 4),
+            "decode_ms_per_layer_step": round(dec_ms / (S * L), 5)}
     roof_prefill = None
     if "attn_tc" in prof:
         n, tot = prof["attn_tc"]
@@ -592,6 +630,7 @@ def run_profile_case(args):
     ctx = wb.Context(0)
     ctx.set_stream(torch.cuda.current_stream().cuda_stream)
     H, E, hd, C = CFG["n_head"], CFG["n_embd"], CFG["head_dim"], CFG["content_dim"]
+    extra = {}
     w = wb.gaussian_block_attn(5, H, E, C)
     lay = wb.AttnLayer(ctx, w)
     g = torch.Generator(device="cuda").manual_seed(0)
@@ -611,6 +650,13 @@ def run_profile_case(args):
         y = torch.empty((B, E), device="cuda")
         for s in range(6):
             cache.forward_one(0, lay0, x[s], ids, out=y)
+        torch.cuda.synchronize()
+        per_step = [B * E * 4] * 6
+        for b, n in enumerate(lens):
+            bk = cache.read(0, b)[1][None, None]  # [1][1][H][n + 6]
+            for s in range(6):
+                per_step[s] += int(decode_bytes_exact(bk, n, s + 1, H, hd, first=s)[0])
+        extra["decode_attn_algorithmic_bytes"] = per_step
     elif args.profile_case == "decode":
         B, n = 32, 1100
         cache = wb.KvCache(1, H, hd, max_seqs=B, max_ctx=n + 16, ctx=ctx)
@@ -623,13 +669,17 @@ def run_profile_case(args):
         y = torch.empty((B, E), device="cuda")
         for s in range(12):
             cache.forward_one(0, lay, x[s], ids, out=y)
+        torch.cuda.synchronize()
+        bk = np.stack([np.stack([cache.read(0, b)[1] for b in range(B)])])
+        extra["decode_attn_algorithmic_bytes"] = [
+            int(decode_bytes_exact(bk, n, s + 1, H, hd, first=s)[0] + B * E * 4) for s in range(12)]
     else:
         x = torch.randn((4, CFG["seq_len"], E), generator=g, device="cuda")
         for _ in range(3):
             wb.wave_attention_forward(lay, x, E // 2, ctx=ctx)
     torch.cuda.synchronize()
     err = ctx.take_device_error()
-    print(json.dumps({"profile_case": args.profile_case, "device_error": err}))
+    print(json.dumps({"profile_case": args.profile_case, "device_error": err, **extra}))
     if err:
         sys.exit(1)
 

@@ -34,19 +34,29 @@ Profiler *&prof_current() {
     return p;
 }
 
+// Inside stream capture a plain record only orders the capture; an event
+// record node (timed at every replay of the graph) needs the external flag.
+static void record(cudaEvent_t e, cudaStream_t st) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(st, &cs) == cudaSuccess && cs == cudaStreamCaptureStatusActive)
+        cudaEventRecordWithFlags(e, st, cudaEventRecordExternal);
+    else
+        cudaEventRecord(e, st);
+}
+
 void prof_begin(const char *name, cudaStream_t st) {
     Profiler *p = prof_current();
     if (!p || (!p->filter.empty() && std::string(name).find(p->filter) == std::string::npos)) return;
     p->open_name = name;
     p->open_ev = p->get();
-    cudaEventRecord(p->open_ev, st);
+    record(p->open_ev, st);
 }
 
 void prof_end(cudaStream_t st) {
     Profiler *p = prof_current();
     if (!p || !p->open_name) return;
     cudaEvent_t b = p->get();
-    cudaEventRecord(b, st);
+    record(b, st);
     p->recs.push_back({p->open_name, p->open_ev, b});
     p->open_name = nullptr;
 }
