@@ -62,6 +62,30 @@ def max_over_ranks(value: float, world: int, device=None) -> float:
     return float(t.item())
 
 
+def gather_output_stats(tensors, world: int, device=None):
+    """Per-rank statistics of the rank's outputs -- [sum, sum of |y|, max |y|,
+    count of non-finite values] over the given tensors -- gathered from every
+    rank (all_gather: over NCCL on the GPUs, the only collective of the job
+    besides the timing reduction).  Returns one list per rank, rank order."""
+    import torch
+    st = torch.zeros(4, dtype=torch.float64, device=device)
+    for t in tensors:
+        td = t.detach().to(torch.float64)
+        fin = torch.isfinite(td)
+        tf = torch.where(fin, td, torch.zeros_like(td))
+        st[0] += tf.sum()
+        st[1] += tf.abs().sum()
+        if tf.numel():
+            st[2] = torch.maximum(st[2], tf.abs().max())
+        st[3] += (~fin).sum().to(torch.float64)
+    if world == 1:
+        return [[float(v) for v in st.tolist()]]
+    import torch.distributed as dist
+    out = [torch.zeros_like(st) for _ in range(world)]
+    dist.all_gather(out, st)
+    return [[float(v) for v in o.tolist()] for o in out]
+
+
 def shard_sequences(ctx_lens, world: int):
     """Split sequences over ranks so every rank gets about the same number of
     cached keys (greedy: longest sequence to the least loaded rank).  Returns
@@ -296,6 +320,8 @@ def run_ours(args):
     tok_step = B * T + B * S
     value = world * tok_step / (ms_step / 1e3)
     check_err("the timed region")
+    # every rank's output statistics of the last timed step, gathered to rank 0
+    out_stats = gather_output_stats([y_pre, y_stage], world, dev)
 
     # rooflines: decode attention (HBM, the dominant kernel) and prefill
     # attention (tensor), each from CUDA events around its own launches
@@ -394,6 +420,8 @@ def run_ours(args):
         "prefill": {"tok_s": round(world * B * T / (pre_ms / 1e3), 1), "ms": round(pre_ms, 3)},
         "decode": {"tok_s": round(world * B * S / (dec_ms / 1e3), 1), "ms": round(dec_ms, 3)},
         "roofline": roof,
+        "rank_output_stats": {"fields": ["sum", "sum_abs", "max_abs", "non_finite"],
+                              "tensors": "last prefill layer output + last decode step outputs", "ranks": out_stats},
         "roofline_prefill": roof_prefill,
         "kernel_ms_eager_step": {k: round(v[1], 3) for k, v in sorted(breakdown.items())},
         "gpu_launches": (launches_prefill + launches_decode_step * S) * args.steps,
@@ -506,7 +534,7 @@ def run_reference(args):
 
 
 def run_decode_stress(args):
-    """256 concurrent sequences, contexts uniform in
+    """Decode stress: 256 concurrent sequences, contexts uniform in
     [128, 4096], 12 heads x 64, fp32 KV cache of Gaussian values and uniform
     phases, one new token per sequence per step through 24 layers.  Under
     torchrun the sequences are split across ranks by cached keys.  One step
