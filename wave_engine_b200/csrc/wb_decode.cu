@@ -372,19 +372,20 @@ __global__ void __launch_bounds__(DEC_THREADS) decode_attn_kernel(DecodeArgs a) 
 // out_proj of the step's rows (kv_cache.rs:330-335), y = o W_o^T + b, and
 // the length update.  Block = 8 rows x 32 columns; its 256 threads are 8
 // column quads x 32 K slices: thread (slice, quad) accumulates 8 rows x 4
-// columns over its slice (weights as float4 straight from global, o rows
-// staged in shared memory), then the 32 slice partials of every output are
-// summed in slice order.  Every load of a batch is issued before any is
-// used; the first weight batch goes out before the dependency wait (the
-// weights are not written by the attention grid).  Block (0, 0) advances
-// the lengths: every attention CTA of the step has read them.
+// columns over its slice, then the 32 slice partials of every output are
+// summed in slice order.  The block's whole W_o column tile (K chunk of up
+// to OUT_KC inputs x 32 columns) is copied into shared memory with cp.async
+// before the dependency wait -- the attention grid does not write W_o, and
+// the copy holds no registers -- so after the wait only the o rows (one
+// batch of loads from L2) stand between the attention grid and the
+// arithmetic.  Block (0, 0) advances the lengths: every attention CTA of the
+// step has read them.
 static constexpr int OUT_THREADS = 256;
 static constexpr int OUT_R = 8;                    // rows per block
 static constexpr int OUT_C = 32;                   // columns per block
 static constexpr int OUT_Q = OUT_C / 4;            // column quads
 static constexpr int OUT_S = OUT_THREADS / OUT_Q;  // K slices (32)
-static constexpr int OUT_KC = 2048;                // columns of o staged per pass (64 KB)
-static constexpr int OUT_WB = 12;                  // weight float4 per batch
+static constexpr int OUT_KC = 1024;                // inputs per staged chunk (W tile 128 KB, o rows 32 KB)
 
 struct DecodeOutArgs {
     const float *o;     // [n][E]
@@ -397,84 +398,104 @@ struct DecodeOutArgs {
     int n_slots;
 };
 
-__device__ __forceinline__ void out_load_w(const DecodeOutArgs &a, int k_abs0, int kend_abs, int c, bool cvec,
-                                           float4 (&w)[OUT_WB]) {
+// W_o[k0 .. k0+kn)[c0 .. c0+32) -> ws[kn][32]: cp.async where the 16 bytes
+// are in range and aligned, plain loads (zero outside the matrix) elsewhere.
+__device__ __forceinline__ void out_stage_w(const DecodeOutArgs &a, float *ws, int k0, int kn, int c0) {
     const int E = a.E;
+    const bool vec = (E % 4) == 0 && c0 + OUT_C <= E;
+    for (int e = threadIdx.x; e < kn * OUT_Q; e += OUT_THREADS) {
+        const int kk = e / OUT_Q, cq = e % OUT_Q;
+        const int c = c0 + cq * 4;
+        float *dst = ws + kk * OUT_C + cq * 4;
+        const float *src = a.wo_t + (long long)(k0 + kk) * E + c;
+        if (vec) {
+            ptx::cp_async<16>(dst, src);
+        } else {
 #pragma unroll
-    for (int u = 0; u < OUT_WB; u++) {
-        const int k = k_abs0 + u;
-        w[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (k < kend_abs) {
-            const float *src = a.wo_t + (long long)k * E + c;
-            if (cvec) w[u] = __ldg(reinterpret_cast<const float4 *>(src));
-            else {
-                if (c < E) w[u].x = __ldg(src);
-                if (c + 1 < E) w[u].y = __ldg(src + 1);
-                if (c + 2 < E) w[u].z = __ldg(src + 2);
-                if (c + 3 < E) w[u].w = __ldg(src + 3);
-            }
+            for (int u = 0; u < 4; u++) dst[u] = c + u < E ? __ldg(src + u) : 0.0f;
         }
     }
+    ptx::cp_async_commit();
 }
 
 __global__ void __launch_bounds__(OUT_THREADS) decode_out_kernel(DecodeOutArgs a) {
-    extern __shared__ float osm[];
+    extern __shared__ __align__(16) float osm[];
     const int E = a.E, n = a.n;
     const int c0 = blockIdx.x * OUT_C, r0 = blockIdx.y * OUT_R;
     const int tid = threadIdx.x, ks = tid / OUT_Q, cq = tid % OUT_Q;
     const int kc = min(E, OUT_KC);
-    float *os = osm;                 // [OUT_R][kc]
-    float *red = osm + OUT_R * kc;   // [OUT_S][OUT_R][OUT_C]
-    const int c = c0 + cq * 4;
-    const bool cvec = c + 3 < E && (E % 4 == 0);
+    const int ost = ((kc + 3) & ~3) + 4;  // o row stride (floats; 16-byte rows, shifted banks)
+    float *ws = osm;                       // [kc][OUT_C]
+    float *os = ws + kc * OUT_C;           // [OUT_R][ost]
+    float *red = os + OUT_R * ost;         // [OUT_S][OUT_R][OUT_C]
     float acc[OUT_R][4];
 #pragma unroll
     for (int r = 0; r < OUT_R; r++)
 #pragma unroll
         for (int u = 0; u < 4; u++) acc[r][u] = 0.0f;
-    // first weight batch of the first pass, then wait for the attention grid
-    float4 w[OUT_WB];
-    {
-        const int kslice = (kc + OUT_S - 1) / OUT_S;
-        const int k0 = ks * kslice, k1 = min(kc, k0 + kslice);
-        out_load_w(a, k0, k1, c, cvec, w);
-    }
+    // W_o chunk 0 under the attention grid's tail
+    out_stage_w(a, ws, 0, kc, c0);
     ptx::griddep_wait();
     for (int kc0 = 0; kc0 < E; kc0 += kc) {
         const int kn = min(kc, E - kc0);
-        __syncthreads();
-        // stage o rows r0..r0+7, columns kc0..kc0+kn (one batch per thread)
-        const int tot = OUT_R * kn;
-        for (int e0 = 0; e0 < tot; e0 += 16 * OUT_THREADS) {
-            float v[16];
+        if (kc0 > 0) {
+            __syncthreads();  // previous chunk consumed
+            out_stage_w(a, ws, kc0, kn, c0);
+        }
+        // o rows r0..r0+7, inputs kc0..kc0+kn: one batch of float4 loads
+        // (L2: written by the attention grid), then the shared-memory stores
+        {
+            const int q4 = (kn + 3) / 4;  // float4 per row
+            constexpr int PER = 8;        // float4 per thread per batch
+            for (int e0 = 0; e0 < OUT_R * q4; e0 += PER * OUT_THREADS) {
+                float4 v[PER];
 #pragma unroll
-            for (int u = 0; u < 16; u++) {
-                const int e = e0 + u * OUT_THREADS + tid;
-                const int r = e / kn;
-                v[u] = (e < tot && r0 + r < n) ? __ldcg(a.o + (long long)(r0 + r) * E + kc0 + (e - r * kn)) : 0.0f;
-            }
+                for (int u = 0; u < PER; u++) {
+                    const int e = e0 + u * OUT_THREADS + tid;
+                    const int r = e / q4, k = (e - r * q4) * 4;
+                    v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (e < OUT_R * q4 && r0 + r < n) {
+                        const float *src = a.o + (long long)(r0 + r) * E + kc0 + k;
+                        if ((E % 4) == 0 && k + 3 < kn) v[u] = __ldcg(reinterpret_cast<const float4 *>(src));
+                        else {
+                            if (k < kn) v[u].x = __ldcg(src);
+                            if (k + 1 < kn) v[u].y = __ldcg(src + 1);
+                            if (k + 2 < kn) v[u].z = __ldcg(src + 2);
+                            if (k + 3 < kn) v[u].w = __ldcg(src + 3);
+                        }
+                    }
+                }
 #pragma unroll
-            for (int u = 0; u < 16; u++) {
-                const int e = e0 + u * OUT_THREADS + tid;
-                if (e < tot) os[(e / kn) * kc + (e % kn)] = v[u];
+                for (int u = 0; u < PER; u++) {
+                    const int e = e0 + u * OUT_THREADS + tid;
+                    if (e < OUT_R * q4) {
+                        const int r = e / q4, k = (e - r * q4) * 4;
+                        *reinterpret_cast<float4 *>(os + r * ost + k) = v[u];
+                    }
+                }
             }
         }
+        ptx::cp_async_wait<0>();
         __syncthreads();
-        const int kslice = (kn + OUT_S - 1) / OUT_S;
-        const int k0 = ks * kslice, k1 = min(kn, k0 + kslice);
-        for (int kb = k0; kb < k1; kb += OUT_WB) {
-            if (kc0 > 0 || kb > k0) out_load_w(a, kc0 + kb, kc0 + k1, c, cvec, w);
+        // this thread's K slice in steps of 4 inputs: 4 weight rows, 8 o quads
+        const int kslice = ((kn + OUT_S - 1) / OUT_S + 3) & ~3;
+        const int k0 = min(kn, ks * kslice), k1 = min(kn, k0 + kslice);
+        for (int k = k0; k < k1; k += 4) {
+            float4 w[4];
 #pragma unroll
-            for (int u = 0; u < OUT_WB; u++) {
-                const int k = kb + u;
-                if (k >= k1) break;
+            for (int u = 0; u < 4; u++)
+                w[u] = k + u < k1 ? *reinterpret_cast<const float4 *>(ws + (k + u) * OUT_C + cq * 4)
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-                for (int r = 0; r < OUT_R; r++) {
-                    const float ov = os[r * kc + k];
-                    acc[r][0] = fmaf(w[u].x, ov, acc[r][0]);
-                    acc[r][1] = fmaf(w[u].y, ov, acc[r][1]);
-                    acc[r][2] = fmaf(w[u].z, ov, acc[r][2]);
-                    acc[r][3] = fmaf(w[u].w, ov, acc[r][3]);
+            for (int r = 0; r < OUT_R; r++) {
+                const float4 o4 = *reinterpret_cast<const float4 *>(os + r * ost + k);
+                const float ov[4] = {o4.x, o4.y, o4.z, o4.w};
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    acc[r][0] = fmaf(w[u].x, ov[u], acc[r][0]);
+                    acc[r][1] = fmaf(w[u].y, ov[u], acc[r][1]);
+                    acc[r][2] = fmaf(w[u].z, ov[u], acc[r][2]);
+                    acc[r][3] = fmaf(w[u].w, ov[u], acc[r][3]);
                 }
             }
         }
@@ -502,7 +523,9 @@ int launch_decode_out(const float *o, const float *wo_t, const float *bo, float 
                       int32_t *len, const int32_t *slot, int n_slots, cudaStream_t st, std::string *msg) {
     ProfScope ps("decode_out", st);
     DecodeOutArgs a{o, wo_t, bo, y, n, E, cap, len, slot, n_slots};
-    const size_t smem = sizeof(float) * ((size_t)OUT_R * std::min(E, OUT_KC) + OUT_S * OUT_R * OUT_C);
+    const int kc = std::min(E, OUT_KC);
+    const int ost = ((kc + 3) & ~3) + 4;
+    const size_t smem = sizeof(float) * ((size_t)kc * OUT_C + (size_t)OUT_R * ost + (size_t)OUT_S * OUT_R * OUT_C);
     cudaFuncSetAttribute(decode_out_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     dim3 grid((E + OUT_C - 1) / OUT_C, (n + OUT_R - 1) / OUT_R);
     cudaError_t e = launch_ex(decode_out_kernel, grid, dim3(OUT_THREADS), smem, st, true, a);

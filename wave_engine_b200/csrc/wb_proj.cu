@@ -452,9 +452,11 @@ int launch_proj_tc(const ProjTcWeights &p, const float *wrs_t, const float *brs,
     ProjArgs a{(int)R, p.E, p.H, p.hd, p.C, T, p.n_v, p.n_c, p.n_rs, n_gemm, p.bias, sv, content, dev_err};
     const int n_tiles = (n_gemm + PBN - 1) / PBN;
     const unsigned grid = (unsigned)(((R + PBM - 1) / PBM) * n_tiles);
-    ProfScope ps("proj_tc", st);
-    cudaFuncSetAttribute(proj_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM);
-    proj_tc_kernel<<<grid, 128, P_SMEM, st>>>(tx, th, tl, a);
+    {
+        ProfScope ps("proj_tc", st);
+        cudaFuncSetAttribute(proj_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM);
+        proj_tc_kernel<<<grid, 128, P_SMEM, st>>>(tx, th, tl, a);
+    }
     {
         ProfScope pp("phase_fma", st);
         const unsigned pg = (unsigned)((R + PH_ROWS - 1) / PH_ROWS);
