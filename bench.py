@@ -1,8 +1,8 @@
 #!/usr/bin/env python3
 """Benchmark of the B200 wave-attention hot path (prefill + KV-cache decode).
 
-Workload (the configuration its metric is quoted
-on): the 768-dim production model -- n_embd 768, 12 heads of 64, 24 attention
+Workload (the configuration the headline metric is quoted on): the 768-dim
+production model -- n_embd 768, 12 heads of 64, 24 attention
 layers -- with batch 32: a 1024-token prefill through all 24 layers, then 256
 greedy decode steps, each one new position per sequence through all 24
 layers.  One bench step is that whole job.  Weights are seeded N(0, 0.02)
@@ -154,7 +154,7 @@ def peaks():
 
 
 # ---------------------------------------------------------------------------
-# algorithmic work (per SURVEY 8(d) formulas, restated here)
+# algorithmic work of the hot path (FLOP and byte formulas)
 # ---------------------------------------------------------------------------
 def decode_bytes_exact(bucket_slots, T0, S, H, hd, first=0):
     """Algorithmic HBM bytes of the decode attention launches of steps
@@ -533,6 +533,98 @@ def run_reference(args):
     print(json.dumps(out), flush=True)
 
 
+# prefill-only configurations: n_embd, heads, content dim, layers, batch, T
+PREFILL_CFGS = {
+    "prefill-168": dict(E=168, H=4, C=16, L=4, B=4, T=256,
+                        desc="168-dim research model (4 heads x 42, 4 layers): batch 4, 256-token prefill"),
+    "prefill-384": dict(E=384, H=8, C=16, L=6, B=16, T=512,
+                        desc="384-dim grammar model (8 heads x 48, 6 layers): batch 16, 512-token prefill"),
+    "prefill-4096": dict(E=4096, H=32, C=16, L=8, B=8, T=4096,
+                         desc="4096-dim wide model (32 heads x 128, 8 layers): batch 8, 4096-token prefill"),
+}
+
+
+def run_prefill_workload(args):
+    """Prefill through all attention layers of one of the prefill-only
+    configurations (tensor path, content projection on): seeded N(0, 0.02)
+    weights, seeded N(0, 1) per-layer inputs resident in HBM.  Prints its own
+    JSON line: prefill tok/s and the attention kernel's share of the dense
+    tensor peak (whole-layer algorithmic FLOPs / attention kernel time, and /
+    whole layer time)."""
+    import torch
+    import wave_engine_b200 as wb
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+    c = PREFILL_CFGS[args.workload]
+    E, H, C, L, B, T = c["E"], c["H"], c["C"], c["L"], c["B"], c["T"]
+    hd = E // H
+    ctx = wb.Context(local)
+    stream = torch.cuda.current_stream(dev)
+    ctx.set_stream(stream.cuda_stream)
+    layers = [wb.AttnLayer(ctx, wb.gaussian_block_attn(3000 + l, H, E, C)) for l in range(L)]
+    g = torch.Generator(device=dev).manual_seed(77 + rank)
+    x = torch.randn((L, B, T, E), generator=g, device=dev)
+
+    def step():
+        for l in range(L):
+            wb.wave_attention_forward(layers[l], x[l], E // 2, ctx=ctx)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    if ctx.take_device_error():
+        raise RuntimeError("device error during warm-up")
+    ctx.profile("attn_tc")
+    clocks = Clocks(local)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    barrier()
+    clk = clocks.stop()
+    prof = ctx.profile_report()
+    ctx.profile(None)
+    if ctx.take_device_error():
+        raise RuntimeError("device error in the timed region")
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world, dev)
+    hbm, bf16, peak_kind = peaks()
+    fl = prefill_flops_per_layer(B, T, E, H, hd, C)
+    n_att, t_att = prof.get("attn_tc", (0, 0.0))
+    a_ms = t_att / max(1, n_att)
+    layer_ms = ms / L
+    out = {"metric": f"attn prefill tok/s ({args.workload})", "value": round(world * B * T / (ms / 1e3), 1),
+           "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+           "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+           "dtype": "bf16 split (hi/lo) features and values, fp32 accumulation", "data": "synthetic",
+           "config": {"workload": c["desc"], "inputs": "per-layer inputs resident in HBM"},
+           "roofline": {"kernel": "attn_tc", "bound": "tensor", "peak": bf16, "unit": "TFLOP/s",
+                        "peak_kind": peak_kind, "achieved": round(fl / (a_ms / 1e3) / 1e12, 2) if a_ms else None,
+                        "frac": round(fl / (a_ms / 1e3) / 1e12 / bf16, 4) if a_ms else None,
+                        "launch_ms": round(a_ms, 4), "flops_per_layer": fl,
+                        "note": "whole-layer algorithmic FLOPs / attention kernel time (CUDA events)"},
+           "layer_roofline": {"achieved": round(fl / (layer_ms / 1e3) / 1e12, 2),
+                              "frac": round(fl / (layer_ms / 1e3) / 1e12 / bf16, 4), "layer_ms": round(layer_ms, 4),
+                              "note": "whole-layer algorithmic FLOPs / whole layer time"},
+           "clocks": clk}
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
 def run_decode_stress(args):
     """Decode stress: 256 concurrent sequences, contexts uniform in
     [128, 4096], 12 heads x 64, fp32 KV cache of Gaussian values and uniform
@@ -714,8 +806,10 @@ def run_profile_case(args):
 
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
-    ap.add_argument("--workload", choices=["serve-768", "decode-stress"], default="serve-768",
-                    help="serve-768: BASELINE configs[2] (the default line); decode-stress: configs[3]")
+    ap.add_argument("--workload", choices=["serve-768", "decode-stress"] + sorted(PREFILL_CFGS), default="serve-768",
+                    help="serve-768: the headline configuration (default); decode-stress: 256 sequences of "
+                         "context 128-4096; prefill-168/-384/-4096: prefill through all layers of the 168-, "
+                         "384- and 4096-dim models")
     ap.add_argument("--profile-case", choices=["decode", "decode-stress", "prefill"], default=None,
                     help="run a small case for an ncu capture instead of the benchmark")
     ap.add_argument("--gpus", type=int, default=1)
@@ -736,6 +830,8 @@ def main():
         run_profile_case(args)
     elif args.workload == "decode-stress" and args.impl == "ours":
         run_decode_stress(args)
+    elif args.workload in PREFILL_CFGS and args.impl == "ours":
+        run_prefill_workload(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

@@ -108,3 +108,46 @@ def test_oracle_init_block_attn_draw_order():
     assert np.array_equal(w["phase_proj_w"][0, 0, :3], np.array(draws, np.float32))
     assert np.all(np.abs(w["out_proj_w"]) <= 1 / np.sqrt(32) + 1e-7)
     assert np.all(w["phase_proj_b"] == 0) and np.all(w["out_proj_b"] == 0)
+
+
+# ---- seeded oracle dumps of the benchmark configurations at reduced size
+# (tests/golden/configs.npz, written by tests/golden/make_config_golden.py)
+
+def _configs():
+    from pathlib import Path
+    return np.load(Path(__file__).resolve().parent / "golden" / "configs.npz")
+
+
+def _sha(a):
+    import hashlib
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+@pytest.mark.parametrize("case", ["cfg1_168", "cfg2_384", "cfg3_768", "cfg5_4096"])
+def test_oracle_reproduces_config_fixture(case):
+    """The oracle recomputes the committed prefill dump bit for bit (a change
+    of the oracle's arithmetic or of the seeded inputs shows up here)."""
+    from tests.golden import config_cases as cc
+    fx = _configs()
+    name, E, H, C, B, T, init, seed = next(c for c in cc.PREFILL if c[0] == case)
+    w = cc.weights(init, seed, H, E, C)
+    x = cc.inputs(seed, B, T, E)
+    for b in range(B):
+        y, _, ph = oracle.attn_forward(w, x[b])
+        assert np.array_equal(y, fx[case + "/y"][b])
+        assert np.array_equal(ph, fx[case + "/phases"][b])
+    assert _sha(fx[case + "/y"]) == str(fx[case + "/y.sha256"])
+
+
+@pytest.mark.parametrize("case", ["cfg3_decode", "cfg4_ragged"])
+def test_oracle_reproduces_decode_fixture(case):
+    from tests.golden import config_cases as cc
+    fx = _configs()
+    name, E, H, lens, steps, seed = next(c for c in cc.DECODE if c[0] == case)
+    w = cc.weights("gauss", seed, H, E, 0)
+    x = cc.inputs(seed, len(lens), max(lens) + steps, E)
+    for b, n in enumerate(lens):
+        _, st = oracle.kv_prefill(w, x[b, :n], cap=n + steps)
+        for s in range(steps):
+            assert np.array_equal(oracle.kv_decode(w, x[b, n + s], st), fx[case + "/y"][s, b])
+    assert _sha(fx[case + "/y"]) == str(fx[case + "/y.sha256"])

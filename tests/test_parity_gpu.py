@@ -363,3 +363,61 @@ def test_decode_batches_of_different_sizes_share_scratch(ctx):
             r = check(f"ids {ids} seq {sidx}", y[j], oy, TENSOR_TOL)
             assert r.passed, str(r)
     assert ctx.take_device_error() == 0
+
+
+# ---- the GPU against the committed oracle dumps of the benchmark
+# configurations (tests/golden/configs.npz)
+
+def _configs():
+    from pathlib import Path
+    return np.load(Path(__file__).resolve().parent / "golden" / "configs.npz")
+
+
+@pytest.mark.parametrize("case", ["cfg1_168", "cfg2_384", "cfg3_768", "cfg5_4096"])
+@pytest.mark.parametrize("path,tol", [("exact", EXACT_TOL), ("tensor", TENSOR_TOL)])
+def test_config_fixture_prefill(ctx, case, path, tol):
+    """Prefill of each configuration (reduced T) against the fixture; where
+    a GPU phase lands in the neighbouring bucket (only next to a boundary)
+    the oracle is rerun with the GPU's phases for that sequence."""
+    import wave_engine_b200 as wb
+    from tests.golden import config_cases as cc
+    fx = _configs()
+    name, E, H, C, B, T, init, seed = next(c for c in cc.PREFILL if c[0] == case)
+    wp = cc.weights(init, seed, H, E, C)
+    w = wb.WaveAttnWeights.from_packed(wp)
+    x = cc.inputs(seed, B, T, E)
+    y, _, _, ph = wb.wave_attention_forward(w, x, E // 2, path=path, return_phases=True, ctx=ctx)
+    for b in range(B):
+        ref_ph = fx[case + "/phases"][b]
+        assert phase_diff(ph[b], ref_ph).max() <= PHASE_TOL[path]
+        diff = buckets_of(ph[b]) != buckets_of(ref_ph)
+        expect = fx[case + "/y"][b]
+        if diff.any():
+            assert (boundary_distance(ref_ph)[diff] < 2 * PHASE_TOL[path]).all()
+            expect, _, _ = oracle.attn_forward(wp, x[b], phase_override=ph[b], n_threads=NT)
+        r = check(f"{case} {path} seq{b}", y[b], expect, tol)
+        assert r.passed, str(r)
+    assert ctx.take_device_error() == 0
+
+
+@pytest.mark.parametrize("case", ["cfg3_decode", "cfg4_ragged"])
+@pytest.mark.parametrize("path,tol", [("exact", EXACT_TOL), ("tensor", TENSOR_TOL)])
+def test_config_fixture_decode(ctx, case, path, tol):
+    """Prompts of different lengths prefilled into their own slots, then
+    decode steps of all sequences together, against the fixture."""
+    import wave_engine_b200 as wb
+    from tests.golden import config_cases as cc
+    fx = _configs()
+    name, E, H, lens, steps, seed = next(c for c in cc.DECODE if c[0] == case)
+    w = wb.WaveAttnWeights.from_packed(cc.weights("gauss", seed, H, E, 0))
+    x = cc.inputs(seed, len(lens), max(lens) + steps, E)
+    cache = wb.KvCache(1, H, E // H, max_seqs=len(lens), max_ctx=max(lens) + steps, ctx=ctx)
+    for b, n in enumerate(lens):
+        cache.prefill(0, w, x[b:b + 1, :n].copy(), [b], path=path)
+    ids = list(range(len(lens)))
+    for s in range(steps):
+        xs = np.stack([x[b, n + s] for b, n in enumerate(lens)])
+        yd = cache.forward_one(0, w, xs, ids, path=path)
+        r = check(f"{case} {path} step{s}", yd, fx[case + "/y"][s], tol)
+        assert r.passed, str(r)
+    assert ctx.take_device_error() == 0
