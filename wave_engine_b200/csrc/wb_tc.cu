@@ -289,11 +289,10 @@ __global__ void __launch_bounds__(FEAT_WARPS * 32) feat_kernel(FeatArgs a) {
 }
 
 // ---------------------------------------------------------------------------
-// Attention kernel: one CTA = 128 queries of one (b, h); 128 threads, thread
-// i owns query row i (TMEM lane i).  Thread 0 also issues the TMA loads and
-// the tcgen05.mma instructions.  Per key tile j (keys 128j..128j+127):
-//   S = Qf Kf_j^T (TMEM, fp32) -> P = exp(S - s_self) (bf16, smem, masked
-//   causally on the diagonal tile) -> O += P V_j (TMEM, fp32).
+// Attention kernel: one CTA = 128 queries of one (b, h).  Per key tile j
+// (keys 128j..128j+127): S = Qf Kf_j^T (TMEM, fp32) -> P = exp(S - s_self)
+// (bf16, smem, masked causally on the diagonal tile) -> O += P V_j (TMEM,
+// fp32); roles below.
 // ---------------------------------------------------------------------------
 struct AttnTcArgs {
     int BH, H, T, hd, n_qt;
@@ -315,6 +314,8 @@ __device__ __forceinline__ float fast_exp2(float x) {
 template <int HDP, bool WIDE>
 struct AttnSmem {
     static constexpr int FW = WIDE ? 64 : 32;        // feature width
+    static constexpr int KVST = HDP == 64 ? 3 : 2;    // K/V ring stages
+    static constexpr int PB = HDP == 64 ? 2 : 1;      // P buffers
     static constexpr int Q_BYTES = QT * FW * 2;      // 8 / 16 KB
     static constexpr int K_BYTES = KT * FW * 2;      // 8 / 16 KB
     static constexpr int VPART = KT * HDP * 2;       // one bf16 value tile: 16 / 32 KB
@@ -322,236 +323,341 @@ struct AttnSmem {
     static constexpr int P_BYTES = QT * KT * 2;     // 32 KB
     static constexpr int OFF_Q = 0;
     static constexpr int OFF_K = OFF_Q + Q_BYTES;
-    static constexpr int OFF_V = OFF_K + 2 * K_BYTES;
-    static constexpr int OFF_P = OFF_V + 2 * V_BYTES;
-    static constexpr int OFF_BAR = OFF_P + P_BYTES;
-    static constexpr int BYTES = OFF_BAR + 128 + 1024;  // barriers + alignment slack
+    static constexpr int OFF_V = OFF_K + KVST * K_BYTES;
+    static constexpr int OFF_P = OFF_V + KVST * V_BYTES;
+    static constexpr int OFF_L = OFF_P + PB * P_BYTES;   // [2][QT] row-sum halves
+    static constexpr int OFF_BAR = OFF_L + 2 * QT * 4;
+    // barriers: q, kvfull[KVST], kvfree[KVST], sfull[2], pready[2], pfree[PB], ofull; then the TMEM slot
+    static constexpr int NBAR = 1 + 2 * KVST + 4 + PB + 1;
+    static constexpr int BYTES = OFF_BAR + NBAR * 8 + 16 + 1024;  // + alignment slack
+    static_assert(BYTES <= 232448, "attention shared memory above the 227 KB limit");
 };
 
+static constexpr int ATT_SOFTMAX_WARPS = 8;                     // two per TMEM lane group
+static constexpr int ATT_THREADS = (ATT_SOFTMAX_WARPS + 2) * 32;  // + TMA loader warp + MMA warp
+
+// Bounded mbarrier wait that also gives up once another role has raised the
+// CTA's abort flag (so one timeout does not chain into one per barrier).
+__device__ __forceinline__ bool att_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
+    if (ptx::mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (true) {
+        if (ptx::mbar_try_wait(bar, parity)) return true;
+        if (*abort_flag) return false;
+        if (clock64() - t0 > 4000000000LL) {
+            *abort_flag = 1;
+            return false;
+        }
+    }
+}
+
+// Attention core, warp-specialised.  One CTA = 128 queries of one (b, h).
+//   warp 8 (lane 0): TMA -- Q once, then K/V tiles into a KVST-stage ring.
+//   warp 9 (lane 0): tcgen05.mma -- S_j = Qf Kf_j^T into TMEM buffer j & 1
+//     (two tiles ahead of the softmax), O += P_j V_j (value hi and lo).
+//   warps 0-7: softmax of S_j (two warps per TMEM lane group: warps w and
+//     w + 4 own the same 32 query rows, key columns 0-63 and 64-127),
+//     P_j = exp2 of the fixed shift in bf16 into shared-memory buffer j % PB;
+//     then the epilogue (O / l plus the exact previous-position term).
+// The S double buffer lets QK_{j+2} and PV_j run while the softmax works on
+// S_{j+1}.
 template <int HDP, bool WIDE>
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(ATT_THREADS, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_vh, const __grid_constant__ CUtensorMap tm_vl,
                    AttnTcArgs a, int hdn) {
     using L = AttnSmem<HDP, WIDE>;
+    constexpr int KVST = L::KVST, PB = L::PB;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *bars = reinterpret_cast<uint64_t *>(sm + L::OFF_BAR);
-    uint64_t *full = bars;       // [2]
-    uint64_t *empty = bars + 2;  // [2]
-    uint64_t *qbar = bars + 4;
-    uint64_t *sbar = bars + 5;
-    uint64_t *obar = bars + 6;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 7);
+    uint64_t *qbar = bars;
+    uint64_t *kvfull = bars + 1;
+    uint64_t *kvfree = kvfull + KVST;
+    uint64_t *sfull = kvfree + KVST;  // [2]
+    uint64_t *pready = sfull + 2;     // [2]
+    uint64_t *pfree = pready + 2;     // [PB]
+    uint64_t *ofull = pfree + PB;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(ofull + 1);
+    float *lsum = reinterpret_cast<float *>(sm + L::OFF_L);  // [2][QT]
+    __shared__ int s_abort;
+    volatile int *abort_flag = &s_abort;
 
-    const int tid = threadIdx.x, warp = tid >> 5;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int bh = blockIdx.x % a.BH;
     const int qt = a.n_qt - 1 - (int)(blockIdx.x / a.BH);  // heaviest (longest) tiles first
     const int b = bh / a.H, h = bh - b * a.H;
-    const int q0 = qt * QT, row = tid, q = q0 + row;
+    const int q0 = qt * QT;
+    const bool softmax_warp = warp < ATT_SOFTMAX_WARPS;
+    const int row = tid & (QT - 1), half = (warp >> 2) & 1;  // softmax role: query row, key-column half
+    const int q = q0 + row;
     const long long rq = (long long)bh * a.T + q;
 
-    float m0 = 0.0f;
-    bool violate = false;
-    if (q < a.T) {
+    // per-row inputs of the softmax roles, requested first: the fixed shift,
+    // the bounded-score test, the previous-position score and the row's
+    // value base in the cache view
+    float m0 = 0.0f, cn = 0.0f, cm = 0.0f, sp = -INFINITY;
+    long long vbase = 0;
+    if (softmax_warp && q < a.T) {
         m0 = a.m0[rq];
-        const float cn = a.cnorm[rq], cm = __uint_as_float(a.cmax[bh]);
-        violate = 0.25f * cn * (cm - cn) > BOUND_LIMIT;
-    }
-    if (__syncthreads_or(violate)) {
-        if (tid == 0) a.tile_flags[(long long)bh * a.n_qt + qt] = 1;
-        return;
+        sp = a.sprev[rq];
+        vbase = wb_slot_base(a.sv, b, h);
+        if (half == 0) {
+            cn = a.cnorm[rq];
+            cm = __uint_as_float(a.cmax[bh]);
+        }
     }
     if (tid == 0) {
-        for (int i = 0; i < 7; i++) ptx::mbar_init(bars + i, 1);
+        for (int i = 0; i < L::NBAR; i++)  // pready counts every softmax thread, the rest one arrival
+            ptx::mbar_init(bars + i, (bars + i == pready || bars + i == pready + 1) ? ATT_SOFTMAX_WARPS * 32 : 1);
         ptx::fence_mbar_init();
+        s_abort = 0;
     }
-    if (warp == 0) {
-        ptx::tmem_alloc(tmem_slot, 256);
+    if (warp == ATT_SOFTMAX_WARPS) {
+        ptx::tmem_alloc(tmem_slot, 512);
         ptx::tmem_relinquish();
     }
     ptx::tc_fence_before();
     __syncthreads();
     ptx::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t S_t = tmem, O_t = tmem + 128;
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-
+    const uint32_t O_t = tmem + 256;
     const int n_kt = qt + 1;
-    constexpr uint32_t IDESC_QK = ptx::idesc_bf16(128, 128, 0, 0);
-    const uint32_t idesc_pv = ptx::idesc_bf16(128, hdn, 0, 1);
-    const uint32_t sQ = ptx::smem_u32(sm + L::OFF_Q);
-    const uint32_t sK0 = ptx::smem_u32(sm + L::OFF_K);
-    const uint32_t sV0 = ptx::smem_u32(sm + L::OFF_V);
-    const uint32_t sP = ptx::smem_u32(sm + L::OFF_P);
-    constexpr uint32_t STAGE_TX = L::K_BYTES + L::V_BYTES;
-
-    bool ok = true;
-    auto load_tile = [&](int j) {
-        const int s = j & 1;
-        ptx::mbar_arrive_expect_tx(full + s, STAGE_TX);
-        ptx::tma_load_3d(sm + L::OFF_K + s * L::K_BYTES, &tm_k, full + s, 0, j * KT, bh);
-#pragma unroll
-        for (int c = 0; c < HDP / 64; c++) {
-            ptx::tma_load_3d(sm + L::OFF_V + s * L::V_BYTES + c * (KT * 128), &tm_vh, full + s, c * 64, j * KT, bh);
-            if (WIDE)
-                ptx::tma_load_3d(sm + L::OFF_V + s * L::V_BYTES + L::VPART + c * (KT * 128), &tm_vl, full + s,
-                                 c * 64, j * KT, bh);
-        }
-    };
-    // Feature rows are 64 B (SW64, 8-row groups of 512 B) or 128 B (SW128,
-    // 1024 B groups); each MMA consumes 16 features = 32 B of the row.
     constexpr uint32_t F_SW = WIDE ? ptx::UMMA_SW128 : ptx::UMMA_SW64;
     constexpr uint32_t F_SBO = WIDE ? 1024 : 512;
-    auto issue_qk = [&](int j) {
-        const uint32_t sK = sK0 + (j & 1) * L::K_BYTES;
+    auto load_kv = [&](int j) {
+        const int s = j % KVST;
+        ptx::mbar_arrive_expect_tx(kvfull + s, L::K_BYTES + L::V_BYTES);
+        ptx::tma_load_3d(sm + L::OFF_K + s * L::K_BYTES, &tm_k, kvfull + s, 0, j * KT, bh);
+        uint8_t *vst = sm + L::OFF_V + s * L::V_BYTES;
 #pragma unroll
-        for (int kk = 0; kk < L::FW / 16; kk++) {
-            const uint64_t ad = ptx::smem_desc(sQ + kk * 32, 16, F_SBO, F_SW);
-            const uint64_t bd = ptx::smem_desc(sK + kk * 32, 16, F_SBO, F_SW);
-            ptx::mma_bf16(S_t, ad, bd, IDESC_QK, kk > 0);
+        for (int c = 0; c < HDP / 64; c++) {
+            ptx::tma_load_3d(vst + c * (KT * 128), &tm_vh, kvfull + s, c * 64, j * KT, bh);
+            if (WIDE) ptx::tma_load_3d(vst + L::VPART + c * (KT * 128), &tm_vl, kvfull + s, c * 64, j * KT, bh);
         }
-        ptx::mma_commit(sbar);
     };
-
-    if (tid == 0) {
+    // Q and the first ring stages go out before the bounded-score test
+    const int pre = min(KVST, n_kt);
+    if (warp == ATT_SOFTMAX_WARPS && lane == 0) {
         ptx::prefetch_tmap(&tm_q);
         ptx::prefetch_tmap(&tm_k);
         ptx::prefetch_tmap(&tm_vh);
         if (WIDE) ptx::prefetch_tmap(&tm_vl);
         ptx::mbar_arrive_expect_tx(qbar, L::Q_BYTES);
         ptx::tma_load_3d(sm + L::OFF_Q, &tm_q, qbar, 0, q0, bh);
-        load_tile(0);
-        if (n_kt > 1) load_tile(1);
-        if (ptx::mbar_wait(qbar, 0) && ptx::mbar_wait(full, 0)) {
-            ptx::tc_fence_after();
-            issue_qk(0);
-        } else {
-            ok = false;
-            atomicOr(a.dev_err, WB_DERR_TIMEOUT_TMA);
-        }
+        for (int j = 0; j < pre; j++) load_kv(j);
     }
-
-    const float LOG2E = 1.4426950408889634f;
-    const float nm0 = -m0 * LOG2E;
-    float l = 0.0f;
-    uint8_t *prow = sm + L::OFF_P + (row >> 3) * 1024 + (row & 7) * 128;
-    for (int j = 0; j < n_kt; j++) {
-        if (!ptx::mbar_wait(sbar, j & 1)) {
-            ok = false;
-            atomicOr(a.dev_err, WB_DERR_TIMEOUT_SOFTMAX);
+    const bool violate = softmax_warp && half == 0 && q < a.T && 0.25f * cn * (cm - cn) > BOUND_LIMIT;
+    if (__syncthreads_or(violate)) {
+        // the tile goes to the fp32 fallback: the copies already issued land
+        // before the CTA leaves
+        if (warp == ATT_SOFTMAX_WARPS && lane == 0) {
+            att_wait(qbar, 0, abort_flag);
+            for (int j = 0; j < pre; j++) att_wait(kvfull + j, 0, abort_flag);
         }
-        if (__syncthreads_or(!ok)) break;
-        ptx::tc_fence_after();
-        const bool diag = (j == qt);
-#pragma unroll
-        for (int c = 0; c < 4; c++) {
-            uint32_t r[32];
-            ptx::tmem_ld32(S_t + lane_base + c * 32, r);
-            ptx::tmem_ld_wait();
-            uint32_t pk[16];
-#pragma unroll
-            for (int i = 0; i < 16; i++) {
-                float e0 = fast_exp2(fmaf(__uint_as_float(r[2 * i]), LOG2E, nm0));
-                float e1 = fast_exp2(fmaf(__uint_as_float(r[2 * i + 1]), LOG2E, nm0));
-                if (diag) {
-                    if (c * 32 + 2 * i > row) e0 = 0.0f;
-                    if (c * 32 + 2 * i + 1 > row) e1 = 0.0f;
-                }
-                l += e0 + e1;
-                pk[i] = pack_bf16(e0, e1);
-            }
-            uint8_t *half = prow + (c >> 1) * (QT * 128);
-#pragma unroll
-            for (int u = 0; u < 4; u++) {
-                const int ch = (((c & 1) * 4) + u) ^ (row & 7);
-                *reinterpret_cast<uint4 *>(half + ch * 16) =
-                    make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
-            }
-        }
-        ptx::fence_proxy_async_smem();
+        if (tid == 0) a.tile_flags[(long long)bh * a.n_qt + qt] = 1;
         ptx::tc_fence_before();
         __syncthreads();
-        if (tid == 0 && ok) {
-            ptx::tc_fence_after();
-            const uint32_t sV = sV0 + (j & 1) * L::V_BYTES;
-#pragma unroll
-            for (int kk = 0; kk < KT / 16; kk++) {
-                const uint64_t ad = ptx::smem_desc(sP + (kk >> 2) * (QT * 128) + (kk & 3) * 32, 16, 1024,
-                                                   ptx::UMMA_SW128);
-                const uint64_t bd = ptx::smem_desc(sV + kk * 2048, KT * 128, 1024, ptx::UMMA_SW128);
-                ptx::mma_bf16(O_t, ad, bd, idesc_pv, (j > 0 || kk > 0));
-                if (WIDE) {
-                    const uint64_t bl = ptx::smem_desc(sV + L::VPART + kk * 2048, KT * 128, 1024, ptx::UMMA_SW128);
-                    ptx::mma_bf16(O_t, ad, bl, idesc_pv, 1);
-                }
-            }
-            ptx::mma_commit(empty + (j & 1));
-            if (j + 1 < n_kt) {
-                if (ptx::mbar_wait(full + ((j + 1) & 1), ((j + 1) >> 1) & 1)) {
-                    ptx::tc_fence_after();
-                    issue_qk(j + 1);
-                } else {
-                    ok = false;
-                    atomicOr(a.dev_err, WB_DERR_TIMEOUT_TMA);
-                }
-            } else {
-                ptx::mma_commit(obar);
-            }
-            if (ok && j + 2 < n_kt) {
-                if (ptx::mbar_wait(empty + (j & 1), (j >> 1) & 1)) {
-                    load_tile(j + 2);
-                } else {
-                    ok = false;
-                    atomicOr(a.dev_err, WB_DERR_TIMEOUT_MMA);
-                }
-            }
-        }
+        if (warp == ATT_SOFTMAX_WARPS) ptx::tmem_dealloc(tmem, 512);
+        return;
     }
 
-    // epilogue: O / l plus the previous-position term
-    bool done = ok && ptx::mbar_wait(obar, 0);
-    if (ok && !done) atomicOr(a.dev_err, WB_DERR_TIMEOUT_MMA);
-    ptx::tc_fence_after();
-    if (done) {
-        float o[HDP];
-#pragma unroll
-        for (int c = 0; c < HDP / 32; c++) {
-            uint32_t r[32];
-            ptx::tmem_ld32(O_t + lane_base + c * 32, r);
-            ptx::tmem_ld_wait();
-#pragma unroll
-            for (int i = 0; i < 32; i++) o[c * 32 + i] = __uint_as_float(r[i]);
-        }
-        if (q < a.T) {
-            const float sp = a.sprev[rq];
-            const long long vbase = wb_slot_base(a.sv, b, h);
-            if (sp > -INFINITY) {
-                const float e = __expf(sp - m0);
-                const float *vp = a.sv.v + (vbase + q - 1) * a.hd;
-                l += e;
-#pragma unroll
-                for (int d = 0; d < HDP; d++)
-                    if (d < a.hd) o[d] = fmaf(e, vp[d], o[d]);
+    if (warp == ATT_SOFTMAX_WARPS) {
+        // ---------------- TMA loader (stages from `pre` on)
+        if (lane == 0) {
+            for (int j = pre; j < n_kt; j++) {
+                const int s = j % KVST;
+                if (!att_wait(kvfree + s, ((j / KVST) - 1) & 1, abort_flag)) {
+                    atomicOr(a.dev_err, WB_DERR_TIMEOUT_MMA);
+                    break;
+                }
+                load_kv(j);
             }
-            const float inv = 1.0f / l;
-            const long long off = ((long long)b * a.T + q) * a.E + (long long)h * a.hd;
-            if (WIDE) {
-                float *dst = (float *)a.o + off;
+        }
+    } else if (warp == ATT_SOFTMAX_WARPS + 1) {
+        // ---------------- MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t IDESC_QK = ptx::idesc_bf16(128, 128, 0, 0);
+            const uint32_t idesc_pv = ptx::idesc_bf16(128, hdn, 0, 1);
+            const uint32_t sQ = ptx::smem_u32(sm + L::OFF_Q);
+            bool ok = att_wait(qbar, 0, abort_flag);
+            auto qk = [&](int j) {
+                const int s = j % KVST;
+                if (!att_wait(kvfull + s, (j / KVST) & 1, abort_flag)) return false;
+                ptx::tc_fence_after();
+                const uint32_t sK = ptx::smem_u32(sm + L::OFF_K + s * L::K_BYTES);
+                const uint32_t S_t = tmem + (uint32_t)((j & 1) * 128);
 #pragma unroll
-                for (int d = 0; d < HDP; d++)
-                    if (d < a.hd) dst[d] = o[d] * inv;
+                for (int kk = 0; kk < L::FW / 16; kk++) {
+                    const uint64_t ad = ptx::smem_desc(sQ + kk * 32, 16, F_SBO, F_SW);
+                    const uint64_t bd = ptx::smem_desc(sK + kk * 32, 16, F_SBO, F_SW);
+                    ptx::mma_bf16(S_t, ad, bd, IDESC_QK, kk > 0);
+                }
+                ptx::mma_commit(sfull + (j & 1));
+                return true;
+            };
+            if (ok) ok = qk(0);
+            if (ok && n_kt > 1) ok = qk(1);
+            for (int j = 0; ok && j < n_kt; j++) {
+                if (!att_wait(pready + (j & 1), (j >> 1) & 1, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                ptx::tc_fence_after();
+                const uint32_t sP = ptx::smem_u32(sm + L::OFF_P + (j % PB) * L::P_BYTES);
+                const uint32_t sV = ptx::smem_u32(sm + L::OFF_V + (j % KVST) * L::V_BYTES);
+#pragma unroll
+                for (int kk = 0; kk < KT / 16; kk++) {
+                    const uint64_t ad = ptx::smem_desc(sP + (kk >> 2) * (QT * 128) + (kk & 3) * 32, 16, 1024,
+                                                       ptx::UMMA_SW128);
+                    const uint64_t bd = ptx::smem_desc(sV + kk * 2048, KT * 128, 1024, ptx::UMMA_SW128);
+                    ptx::mma_bf16(O_t, ad, bd, idesc_pv, (j > 0 || kk > 0));
+                    if (WIDE) {
+                        const uint64_t bl =
+                            ptx::smem_desc(sV + L::VPART + kk * 2048, KT * 128, 1024, ptx::UMMA_SW128);
+                        ptx::mma_bf16(O_t, ad, bl, idesc_pv, 1);
+                    }
+                }
+                ptx::mma_commit(kvfree + (j % KVST));
+                ptx::mma_commit(pfree + (j % PB));
+                if (j + 2 < n_kt) ok = qk(j + 2);
+            }
+            if (ok) ptx::mma_commit(ofull);
+            else atomicOr(a.dev_err, WB_DERR_TIMEOUT_TMA);
+        }
+    } else {
+        // ---------------- softmax (warps 0-7)
+        const float LOG2E = 1.4426950408889634f;
+        const float nm0 = -m0 * LOG2E;
+        const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+        float l = 0.0f;
+        bool ok = true;
+        for (int j = 0; j < n_kt; j++) {
+            if (!att_wait(sfull + (j & 1), (j >> 1) & 1, abort_flag)) {
+                atomicOr(a.dev_err, WB_DERR_TIMEOUT_SOFTMAX);
+                ok = false;
+                break;
+            }
+            ptx::tc_fence_after();
+            const bool diag = (j == qt);
+            const uint32_t S_t = tmem + (uint32_t)((j & 1) * 128) + lane_base + half * 64;
+            uint32_t pk[2][16];
+#pragma unroll
+            for (int c = 0; c < 2; c++) {
+                uint32_t r[32];
+                ptx::tmem_ld32(S_t + c * 32, r);
+                ptx::tmem_ld_wait();
+                const int kbase = half * 64 + c * 32;
+#pragma unroll
+                for (int i = 0; i < 16; i++) {
+                    float e0 = fast_exp2(fmaf(__uint_as_float(r[2 * i]), LOG2E, nm0));
+                    float e1 = fast_exp2(fmaf(__uint_as_float(r[2 * i + 1]), LOG2E, nm0));
+                    if (diag) {
+                        if (kbase + 2 * i > row) e0 = 0.0f;
+                        if (kbase + 2 * i + 1 > row) e1 = 0.0f;
+                    }
+                    l += e0 + e1;
+                    pk[c][i] = pack_bf16(e0, e1);
+                }
+            }
+            // P buffer j % PB is free once PV_{j - PB} has completed
+            if (j >= PB && !att_wait(pfree + (j % PB), ((j / PB) - 1) & 1, abort_flag)) {
+                atomicOr(a.dev_err, WB_DERR_TIMEOUT_MMA);
+                ok = false;
+                break;
+            }
+            uint8_t *prow = sm + L::OFF_P + (j % PB) * L::P_BYTES + half * (QT * 128) + (row >> 3) * 1024 +
+                            (row & 7) * 128;
+#pragma unroll
+            for (int c = 0; c < 2; c++)
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    const int ch = (c * 4 + u) ^ (row & 7);
+                    *reinterpret_cast<uint4 *>(prow + ch * 16) =
+                        make_uint4(pk[c][4 * u], pk[c][4 * u + 1], pk[c][4 * u + 2], pk[c][4 * u + 3]);
+                }
+            ptx::fence_proxy_async_smem();
+            ptx::tc_fence_before();
+            ptx::mbar_arrive(pready + (j & 1));
+        }
+
+        // ---- epilogue: O / l plus the previous-position term; each thread
+        // its row and half of the O columns.  The previous value row's loads
+        // go out before the wait for the last PV.
+        constexpr int HC = HDP / 2;  // O columns per thread
+        const int d0 = half * HC;
+        float vprev[HC];
+        const bool has_prev = q < a.T && sp > -INFINITY;
+        if (has_prev) {
+            const float *vp = a.sv.v + (vbase + q - 1) * a.hd + d0;
+            if ((a.hd & 3) == 0 && d0 + HC <= a.hd) {
+#pragma unroll
+                for (int u = 0; u < HC / 4; u++) {
+                    const float4 t4 = __ldg(reinterpret_cast<const float4 *>(vp) + u);
+                    vprev[4 * u] = t4.x;
+                    vprev[4 * u + 1] = t4.y;
+                    vprev[4 * u + 2] = t4.z;
+                    vprev[4 * u + 3] = t4.w;
+                }
             } else {
-                __nv_bfloat16 *dst = (__nv_bfloat16 *)a.o + off;
 #pragma unroll
-                for (int d = 0; d < HDP; d++)
-                    if (d < a.hd) dst[d] = __float2bfloat16_rn(o[d] * inv);
+                for (int d = 0; d < HC; d++) vprev[d] = d0 + d < a.hd ? __ldg(vp + d) : 0.0f;
+            }
+        }
+        bool done = ok && att_wait(ofull, 0, abort_flag);
+        if (ok && !done) atomicOr(a.dev_err, WB_DERR_TIMEOUT_MMA);
+        lsum[half * QT + row] = l;
+        asm volatile("bar.sync 1, 256;" ::: "memory");
+        ptx::tc_fence_after();
+        if (done) {
+            float lt = lsum[row] + lsum[QT + row];
+            float o[HC];
+#pragma unroll
+            for (int c = 0; c < HC / 32; c++) {
+                uint32_t r[32];
+                ptx::tmem_ld32(O_t + lane_base + half * HC + c * 32, r);
+                ptx::tmem_ld_wait();
+#pragma unroll
+                for (int i = 0; i < 32; i++) o[c * 32 + i] = __uint_as_float(r[i]);
+            }
+            if (has_prev) {
+                const float e = __expf(sp - m0);
+                lt += e;
+#pragma unroll
+                for (int d = 0; d < HC; d++)
+                    if (d0 + d < a.hd) o[d] = fmaf(e, vprev[d], o[d]);
+            }
+            const float inv = 1.0f / lt;
+            if (WIDE) {
+                // the K/V ring is free (every MMA has completed): each warp
+                // stages its 32 rows x 32 columns and stores them row by row
+                float *buf = reinterpret_cast<float *>(sm + L::OFF_V) + warp * 32 * 33;
+#pragma unroll
+                for (int c = 0; c < HC / 32; c++) {
+                    uint32_t r[32];
+#pragma unroll
+                    for (int i = 0; i < 32; i++) r[i] = __float_as_uint(o[c * 32 + i] * inv);
+                    warp_stage32(buf, r, lane);
+                    const int d = d0 + c * 32 + lane;
+#pragma unroll 4
+                    for (int jr = 0; jr < 32; jr++) {
+                        const int qq = q0 + (warp & 3) * 32 + jr;
+                        if (qq < a.T && d < a.hd)
+                            reinterpret_cast<float *>(a.o)[((long long)b * a.T + qq) * a.E + (long long)h * a.hd + d] =
+                                buf[jr * 33 + lane];
+                    }
+                }
+            } else if (q < a.T) {
+                __nv_bfloat16 *dst = (__nv_bfloat16 *)a.o + ((long long)b * a.T + q) * a.E + (long long)h * a.hd;
+#pragma unroll
+                for (int d = 0; d < HC; d++)
+                    if (d0 + d < a.hd) dst[d0 + d] = __float2bfloat16_rn(o[d] * inv);
             }
         }
     }
     ptx::tc_fence_before();
     __syncthreads();
-    if (warp == 0) ptx::tmem_dealloc(tmem, 256);
+    if (warp == ATT_SOFTMAX_WARPS) ptx::tmem_dealloc(tmem, 512);
 }
 
 // ---------------------------------------------------------------------------
@@ -791,7 +897,7 @@ static void launch_attn_tc(const CUtensorMap &tq, const CUtensorMap &tk, const C
     using L = AttnSmem<HDP, WIDE>;
     ProfScope ps("attn_tc", st);
     cudaFuncSetAttribute(attn_tc_kernel<HDP, WIDE>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES);
-    attn_tc_kernel<HDP, WIDE><<<grid, 128, L::BYTES, st>>>(tq, tk, tvh, tvl, aa, hdn);
+    attn_tc_kernel<HDP, WIDE><<<grid, ATT_THREADS, L::BYTES, st>>>(tq, tk, tvh, tvl, aa, hdn);
 }
 
 // Runs features -> tcgen05 attention -> SIMT fallback for flagged tiles ->
