@@ -563,16 +563,28 @@ def run_prefill_workload(args):
     c = PREFILL_CFGS[args.workload]
     E, H, C, L, B, T = c["E"], c["H"], c["C"], c["L"], c["B"], c["T"]
     hd = E // H
+    by_heads = args.shard == "heads" and world > 1
+    if by_heads and H % world:
+        raise SystemExit(f"--shard heads needs the {H} heads to divide over {world} ranks")
+    h0, h1 = (rank * H // world, (rank + 1) * H // world) if by_heads else (0, H)
     ctx = wb.Context(local)
     stream = torch.cuda.current_stream(dev)
     ctx.set_stream(stream.cuda_stream)
     layers = [wb.AttnLayer(ctx, wb.gaussian_block_attn(3000 + l, H, E, C)) for l in range(L)]
     g = torch.Generator(device=dev).manual_seed(77 + rank)
+    if by_heads:
+        g = torch.Generator(device=dev).manual_seed(77)  # every rank holds the same inputs
     x = torch.randn((L, B, T, E), generator=g, device=dev)
 
     def step():
         for l in range(L):
-            wb.wave_attention_forward(layers[l], x[l], E // 2, ctx=ctx)
+            if by_heads:
+                # this rank's heads and their share of out_proj, then one
+                # all-reduce (sum) of the layer output over NCCL
+                y = wb.wave_attention_forward_heads(layers[l], x[l], E // 2, h0, h1, add_bias=(rank == 0), ctx=ctx)
+                torch.distributed.all_reduce(y)
+            else:
+                wb.wave_attention_forward(layers[l], x[l], E // 2, ctx=ctx)
 
     def barrier():
         torch.cuda.synchronize()
@@ -602,12 +614,18 @@ def run_prefill_workload(args):
     ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world, dev)
     hbm, bf16, peak_kind = peaks()
     fl = prefill_flops_per_layer(B, T, E, H, hd, C)
+    if by_heads:
+        fl //= world  # this rank's share of the layer
     n_att, t_att = prof.get("attn_tc", (0, 0.0))
     a_ms = t_att / max(1, n_att)
     layer_ms = ms / L
-    out = {"metric": f"attn prefill tok/s ({args.workload})", "value": round(world * B * T / (ms / 1e3), 1),
+    tokens = B * T if by_heads else world * B * T
+    out = {"metric": f"attn prefill tok/s ({args.workload})", "value": round(tokens / (ms / 1e3), 1),
            "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-           "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+           "ms_per_step": round(ms, 3), "higher_is_better": True,
+           "scaling": ("strong (heads split across ranks: each rank computes its heads and their share of "
+                       "out_proj; one NCCL all-reduce of the layer output)") if by_heads else "weak",
+           "vs_baseline": None,
            "dtype": "bf16 split (hi/lo) features and values, fp32 accumulation", "data": "synthetic",
            "config": {"workload": c["desc"], "inputs": "per-layer inputs resident in HBM"},
            "roofline": {"kernel": "attn_tc", "bound": "tensor", "peak": bf16, "unit": "TFLOP/s",
@@ -812,6 +830,9 @@ def main():
                          "384- and 4096-dim models")
     ap.add_argument("--profile-case", choices=["decode", "decode-stress", "prefill"], default=None,
                     help="run a small case for an ncu capture instead of the benchmark")
+    ap.add_argument("--shard", choices=["batch", "heads"], default="batch",
+                    help="prefill workloads under torchrun: every rank its own batch (weak scaling), or the heads "
+                         "of one batch split across ranks with an all-reduce of each layer output")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)

@@ -155,6 +155,18 @@ WB_API int wb_init_block_attn(uint64_t *rng_state, int n_head, int n_embd, int c
 WB_API int wb_attn_forward(wb_context *ctx, const wb_attn_layer *layer, const float *x, int batch,
                     int seq_len, int flags, float *y, float *att_w, float *phases_out);
 
+/* Head-sharded prefill (no counterpart in the reference, which runs all
+ * heads in one call): the forward of heads [head_begin, head_end) only,
+ * y_partial = o[:, heads] W_out[:, heads]^T, plus out_proj's bias when
+ * add_bias != 0.  Summing the y_partial of ranges that cover every head
+ * exactly once, with add_bias set on exactly one of them, gives
+ * wb_attn_forward's y (up to float summation order): the sharding of the
+ * 4096-dim model across GPUs by heads, with one all-reduce of y_partial.
+ * Tensor path only (flags: WB_NO_CONTENT); head_begin * head_dim must be a
+ * multiple of 4. */
+WB_API int wb_attn_forward_heads(wb_context *ctx, const wb_attn_layer *layer, const float *x, int batch,
+                                 int seq_len, int head_begin, int head_end, int add_bias, int flags, float *y_partial);
+
 /* ---- KV cache (kv_cache.rs:36-54) ------------------------------------- */
 /* One cache holds n_layers x max_seqs slots of capacity max_ctx positions,
  * each with per-head phases (f32), buckets (u8) and values (f32 [hd]). */

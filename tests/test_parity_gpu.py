@@ -421,3 +421,42 @@ def test_config_fixture_decode(ctx, case, path, tol):
         r = check(f"{case} {path} step{s}", yd, fx[case + "/y"][s], tol)
         assert r.passed, str(r)
     assert ctx.take_device_error() == 0
+
+
+@pytest.mark.parametrize("E,H,C,T,groups", [
+    (768, 12, 16, 130, [(0, 4), (4, 9), (9, 12)]),
+    (4096, 32, 16, 40, [(0, 8), (8, 16), (16, 24), (24, 32)]),
+])
+def test_head_ranges_sum_to_the_full_forward(ctx, E, H, C, T, groups):
+    """wb_attn_forward_heads over ranges that cover every head once (bias on
+    one of them) sums to wb_attn_forward's output (the same kernels on the
+    same phases; only out_proj's K is split).  The 768-dim full output is
+    also checked against the oracle here; the 4096-dim forward's oracle
+    parity is covered by the configuration fixture and the shape tests."""
+    import wave_engine_b200 as wb
+    w, x = make_case(E, H, C, 2, T, seed=E + T)
+    y, _, _, ph = wb.wave_attention_forward(w, x, E // 2, path="tensor", return_phases=True, ctx=ctx)
+    parts = [wb.wave_attention_forward_heads(w, x, E // 2, h0, h1, add_bias=(h0 == 0), ctx=ctx)
+             for h0, h1 in groups]
+    r = check("sum of head ranges vs full", np.sum(parts, axis=0), y, (2e-5, 0))
+    assert r.passed, str(r)
+    if E == 768:
+        oy, _, _ = oracle_for(w.packed(), x, ph)
+        r = check("full vs oracle", y, oy, TENSOR_TOL)
+        assert r.passed, str(r)
+    assert ctx.take_device_error() == 0
+
+
+def test_head_range_errors(ctx):
+    import wave_engine_b200 as wb
+    from wave_engine_b200 import _lib
+    w, x = make_case(168, 4, 16, 1, 8, seed=3)
+    with pytest.raises(wb.WaveB200Error) as e:   # 1 * 42 floats is not 16-byte aligned
+        wb.wave_attention_forward_heads(w, x, 84, 1, 3, add_bias=False, ctx=ctx)
+    assert e.value.code == _lib.WB_ENOTSUP
+    with pytest.raises(wb.WaveB200Error) as e:
+        wb.wave_attention_forward_heads(w, x, 84, 2, 2, add_bias=False, ctx=ctx)
+    assert e.value.code == _lib.WB_EINVAL
+    y = wb.wave_attention_forward_heads(w, x, 84, 0, 4, add_bias=True, ctx=ctx)
+    y_full, _, _ = wb.wave_attention_forward(w, x, 84, ctx=ctx)
+    assert np.allclose(y, y_full, atol=2e-5, rtol=0)

@@ -8,11 +8,12 @@ reference's interface for that path.
 """
 from .weights import CONTENT_DIM, Rng, WaveAttnHeadWeights, WaveAttnWeights, gaussian_block_attn, init_block_attn
 from .runtime import AttnLayer, Context, default_context
-from .attn import wave_attention_forward
+from .attn import wave_attention_forward, wave_attention_forward_heads
 from .kv_cache import KvCache
 from ._lib import WaveB200Error
 
 __all__ = [
     "CONTENT_DIM", "Rng", "WaveAttnHeadWeights", "WaveAttnWeights", "gaussian_block_attn", "init_block_attn",
-    "AttnLayer", "Context", "default_context", "wave_attention_forward", "KvCache", "WaveB200Error",
+    "AttnLayer", "Context", "default_context", "wave_attention_forward", "wave_attention_forward_heads", "KvCache",
+    "WaveB200Error",
 ]

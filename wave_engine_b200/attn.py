@@ -88,3 +88,31 @@ def wave_attention_forward(weights, x, n_bands: int, backend=None, return_pathwa
     if return_phases:
         return y, att, None, ph
     return y, att, None
+
+
+def wave_attention_forward_heads(weights, x, n_bands: int, head_begin: int, head_end: int, *, add_bias: bool,
+                                 use_content: bool = True, ctx: Context | None = None):
+    """Heads [head_begin, head_end) of the prefill forward (tensor path):
+    ``y_partial = o[:, heads] W_out[:, heads]^T`` (+ the out_proj bias when
+    ``add_bias``).  The sum over ranges that cover every head once, with the
+    bias added once, is ``wave_attention_forward``'s ``y``: the head-sharded
+    4096-dim model runs one range per GPU and all-reduces ``y_partial``.
+    No counterpart in the reference (attn.rs:90 runs every head)."""
+    if not is_torch(x):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+    elif x.dtype != torch.float32 or not x.is_contiguous():
+        x = x.contiguous().float()
+    if x.ndim not in (2, 3):
+        raise ValueError("x must be [T][n_embd] or [B][T][n_embd]")
+    B, T, E = (1, *x.shape) if x.ndim == 2 else tuple(x.shape)
+    if E != 2 * n_bands:
+        raise ValueError(f"n_embd mismatch: n_bands*2 = {2 * n_bands}, input has {E}")
+    if ctx is None:
+        dev = x.device.index if (is_torch(x) and x.is_cuda) else 0
+        ctx = default_context(dev or 0)
+    layer = device_layer(weights, ctx)
+    y = _empty_like_input(x, tuple(x.shape))
+    ctx.use_torch_stream(x, y)
+    _lib.call("wb_attn_forward_heads", ctx.handle, layer.handle, ptr_of(x), B, T, int(head_begin), int(head_end),
+              1 if add_bias else 0, 0 if use_content else _lib.WB_NO_CONTENT, ptr_of(y))
+    return y

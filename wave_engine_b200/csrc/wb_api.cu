@@ -387,6 +387,44 @@ static int run_projections_exact(wb_context *ctx, const wb_attn_layer *L, const 
     return WB_OK;
 }
 
+int wb_attn_forward_heads(wb_context *ctx, const wb_attn_layer *L, const float *x, int B, int T, int head_begin,
+                          int head_end, int add_bias, int flags, float *y) {
+    if (!ctx || !L || !x || !y) return fail(WB_EINVAL, "NULL argument");
+    if (L->ctx != ctx) return fail(WB_EINVAL, "layer belongs to another context");
+    if (flags & ~WB_NO_CONTENT) return fail(WB_EINVAL, "wb_attn_forward_heads takes WB_NO_CONTENT only (tensor path)");
+    if (head_begin < 0 || head_end > L->H || head_begin >= head_end) return fail(WB_EINVAL, "bad head range");
+    if (B < 0 || T < 0) return fail(WB_EINVAL, "negative batch or seq_len");
+    if (B == 0 || T == 0) return WB_OK;
+    const long long R = (long long)B * T;
+    if (R > (1LL << 30)) return fail(WB_EINVAL, "batch*seq_len too large");
+    DeviceGuard g(ctx->device);
+    ProfBind pb(ctx);
+    cudaStream_t st = ctx->stream;
+    const int E = L->E;
+    const bool use_content = L->C > 0 && !(flags & WB_NO_CONTENT);
+    const bool x_dev = is_device_ptr(x), y_dev = is_device_ptr(y);
+    Carve io;
+    size_t o_x = x_dev ? 0 : io.take<float>(R * E);
+    size_t o_y = y_dev ? 0 : io.take<float>(R * E);
+    WB_TRY(ensure(ctx->io, io.off));
+    char *iob = (char *)ctx->io.p;
+    const float *xd = x_dev ? x : (const float *)(iob + o_x);
+    float *yd = y_dev ? y : (float *)(iob + o_y);
+    if (!x_dev) WB_CUDA(cudaMemcpyAsync((void *)xd, x, R * E * sizeof(float), cudaMemcpyHostToDevice, st));
+    std::string msg;
+    const int rc = wb::tc_attn_forward(L->tc, xd, B, T, use_content, yd, nullptr, &ctx->ws, ctx->dev_err,
+                                       ctx->sm_count, st, &msg, head_begin, head_end, add_bias != 0);
+    if (rc != WB_OK) return fail(rc, msg);
+    if (!y_dev) {
+        WB_CUDA(cudaMemcpyAsync(y, yd, R * E * sizeof(float), cudaMemcpyDeviceToHost, st));
+        WB_CUDA(cudaStreamSynchronize(st));
+        uint32_t derr = 0;
+        WB_CUDA(cudaMemcpy(&derr, ctx->dev_err, sizeof(derr), cudaMemcpyDeviceToHost));
+        if (derr) return fail(WB_ETIMEOUT, "device-side check failed, error word " + std::to_string(derr));
+    }
+    return WB_OK;
+}
+
 int wb_attn_forward(wb_context *ctx, const wb_attn_layer *L, const float *x, int B, int T, int flags,
                     float *y, float *att_w, float *phases_out) {
     if (!ctx || !L || !x || !y) return fail(WB_EINVAL, "NULL argument");

@@ -50,6 +50,7 @@ static constexpr int P_SMEM = PST * P_STAGE + 256 + 1024;
 struct ProjArgs {
     int R, E, H, hd, C, T;
     int n_v, n_c, n_rs, N;  // column counts (n_v = H*hd, n_c = H*C, n_rs = 2H)
+    int v0, v1, c0, c1;     // value and content column windows of the heads computed
     const float *bias;      // [N]
     WbSeqView sv;           // values, phases, buckets (rows r = b*T + t)
     float *content;         // [R][H*C] or nullptr
@@ -71,17 +72,21 @@ __global__ void __launch_bounds__(128, 1)
     uint64_t *full = bars, *conv = bars + PST, *empty = bars + 2 * PST, *done = bars + 3 * PST;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * PST + 1);
     const int tid = threadIdx.x, warp = tid >> 5;
-    const int n_tiles = (a.N + PBN - 1) / PBN;
+    // tiles: the value window in PBN-column steps, then the content window
+    // (no content tiles without a content output, e.g. the serve prefill)
+    const int n_vt = (a.v1 - a.v0 + PBN - 1) / PBN;
+    const int n_ct = a.content ? (a.c1 - a.c0 + PBN - 1) / PBN : 0;
+    const int n_tiles = n_vt + n_ct;
     const int nt = blockIdx.x % n_tiles, mt = blockIdx.x / n_tiles;
-    const int n0 = nt * PBN, m0 = mt * PBM;
-    // without a content output (the serve prefill) pure content tiles have
-    // nothing to do
-    if (!a.content && n0 >= a.n_v && n0 + PBN <= a.n_v + a.n_c) return;
-    // K range: value-only tiles need the inputs of their heads only
+    const bool value_tile = nt < n_vt;
+    const int n0 = value_tile ? a.v0 + nt * PBN : a.c0 + (nt - n_vt) * PBN;
+    const int nend = value_tile ? min(a.v1, n0 + PBN) : min(a.c1, n0 + PBN);
+    const int m0 = mt * PBM;
+    // K range: value tiles need the inputs of their heads only
     int k_lo = 0, k_hi = a.E;
-    if (n0 + PBN <= a.n_v) {
+    if (value_tile) {
         k_lo = (n0 / a.hd) * a.hd;
-        k_hi = min(a.E, ((n0 + PBN + a.hd - 1) / a.hd) * a.hd);
+        k_hi = min(a.E, ((nend + a.hd - 1) / a.hd) * a.hd);
     }
     const int kb0 = k_lo / PBK, kb1 = (k_hi + PBK - 1) / PBK, nk = kb1 - kb0;
 
@@ -196,8 +201,8 @@ __global__ void __launch_bounds__(128, 1)
             for (int i = 0; i < 32; i++) r[i] = __float_as_uint(__uint_as_float(r[i]) + __uint_as_float(rc[i]));
             warp_stage32(buf, r, lane);
             const int n = n0 + c * 32 + lane;
-            const bool is_v = n < a.n_v, is_c = !is_v && n < a.n_v + a.n_c && a.content;
-            const float bv = n < a.N ? a.bias[n] : 0.0f;
+            const bool is_v = value_tile && n < nend, is_c = !value_tile && n < nend && a.content;
+            const float bv = n < nend ? a.bias[n] : 0.0f;
             const int h = is_v ? n / a.hd : 0, d = is_v ? n - h * a.hd : 0;
             const long long hoff = (long long)h * a.sv.cap;
 #pragma unroll 4
@@ -235,7 +240,7 @@ template <int OPT, int KC>
 __global__ void __launch_bounds__(PH_THREADS, 3) phase_fma_kernel(const float *__restrict__ x,
                                                                 const float *__restrict__ wrs_t,
                                                                 const float *__restrict__ brs, int R, int E, int H,
-                                                                int T, WbSeqView sv) {
+                                                                int T, WbSeqView sv, int h0, int Hg) {
     constexpr int WST = 4 * OPT;                        // weight row stride: 4 groups x OPT outputs
     constexpr int RPL = PH_THREADS / KC;                // rows covered by one load instruction
     constexpr int XLD = PH_ROWS / RPL;                  // x loads per thread per chunk
@@ -244,7 +249,11 @@ __global__ void __launch_bounds__(PH_THREADS, 3) phase_fma_kernel(const float *_
     __shared__ __align__(16) float ws[2][KC * WST];
     const int tid = threadIdx.x;
     const int m0 = blockIdx.x * PH_ROWS;
-    const int NO = 2 * H;
+    // outputs: (r, s) of heads h0 .. h0 + Hg - 1 (columns 2*h0 .. of the
+    // [E][2H] weight rows)
+    const int NO = 2 * Hg, NOT = 2 * H;
+    wrs_t += 2 * h0;
+    brs += 2 * h0;
     const int rp = tid % (PH_ROWS / 2), g = tid / (PH_ROWS / 2);
     const int o0 = g * OPT;
     float acc[2][OPT];
@@ -270,7 +279,7 @@ __global__ void __launch_bounds__(PH_THREADS, 3) phase_fma_kernel(const float *_
         for (int u = 0; u < WLD; u++) {
             const int e = u * PH_THREADS + tid;
             const int k = e / WST, o = e % WST;
-            wv[u] = (e < KC * WST && k0 + k < E && o < NO) ? __ldg(wrs_t + (long long)(k0 + k) * NO + o) : 0.0f;
+            wv[u] = (e < KC * WST && k0 + k < E && o < NO) ? __ldg(wrs_t + (long long)(k0 + k) * NOT + o) : 0.0f;
         }
     };
     auto store_chunk = [&](int buf) {
@@ -314,8 +323,9 @@ __global__ void __launch_bounds__(PH_THREADS, 3) phase_fma_kernel(const float *_
         const int b = m / T, t = m - b * T;
 #pragma unroll
         for (int q = 0; q < OPT; q += 2) {
-            const int h = (o0 + q) / 2;
-            if (h >= H) break;
+            const int hl = (o0 + q) / 2;
+            if (hl >= Hg) break;
+            const int h = h0 + hl;
             const float th = atan2f(acc[rr][q + 1], acc[rr][q]);
             const long long pos = wb_slot_base(sv, b, h) + t;
             sv.theta[pos] = th;
@@ -431,7 +441,8 @@ void proj_weights_free(ProjTcWeights *p) {
 }
 
 int launch_proj_tc(const ProjTcWeights &p, const float *wrs_t, const float *brs, const float *x, int B, int T,
-                   const WbSeqView &sv, float *content, uint32_t *dev_err, cudaStream_t st, std::string *msg) {
+                   const WbSeqView &sv, float *content, int h0, int Hg, uint32_t *dev_err, cudaStream_t st,
+                   std::string *msg) {
     const long long R = (long long)B * T;
     if (R <= 0) return WB_OK;
     if ((p.E * 4) % 16) {
@@ -449,8 +460,10 @@ int launch_proj_tc(const ProjTcWeights &p, const float *wrs_t, const float *brs,
     }
     // GEMM over the value and content columns only (phases below)
     const int n_gemm = p.n_v + p.n_c;
-    ProjArgs a{(int)R, p.E, p.H, p.hd, p.C, T, p.n_v, p.n_c, p.n_rs, n_gemm, p.bias, sv, content, dev_err};
-    const int n_tiles = (n_gemm + PBN - 1) / PBN;
+    const int v0 = h0 * p.hd, v1 = (h0 + Hg) * p.hd, c0 = p.n_v + h0 * p.C, c1 = p.n_v + (h0 + Hg) * p.C;
+    ProjArgs a{(int)R, p.E, p.H, p.hd, p.C, T, p.n_v, p.n_c, p.n_rs, n_gemm, v0, v1, c0, c1, p.bias, sv, content,
+               dev_err};
+    const int n_tiles = (v1 - v0 + PBN - 1) / PBN + (content ? (c1 - c0 + PBN - 1) / PBN : 0);
     const unsigned grid = (unsigned)(((R + PBM - 1) / PBM) * n_tiles);
     {
         ProfScope ps("proj_tc", st);
@@ -460,12 +473,12 @@ int launch_proj_tc(const ProjTcWeights &p, const float *wrs_t, const float *brs,
     {
         ProfScope pp("phase_fma", st);
         const unsigned pg = (unsigned)((R + PH_ROWS - 1) / PH_ROWS);
-        if (p.H <= 12)
-            phase_fma_kernel<6, 32><<<pg, PH_THREADS, 0, st>>>(x, wrs_t, brs, (int)R, p.E, p.H, T, sv);
-        else if (p.H <= 16)
-            phase_fma_kernel<8, 32><<<pg, PH_THREADS, 0, st>>>(x, wrs_t, brs, (int)R, p.E, p.H, T, sv);
+        if (Hg <= 12)
+            phase_fma_kernel<6, 32><<<pg, PH_THREADS, 0, st>>>(x, wrs_t, brs, (int)R, p.E, p.H, T, sv, h0, Hg);
+        else if (Hg <= 16)
+            phase_fma_kernel<8, 32><<<pg, PH_THREADS, 0, st>>>(x, wrs_t, brs, (int)R, p.E, p.H, T, sv, h0, Hg);
         else
-            phase_fma_kernel<16, 16><<<pg, PH_THREADS, 0, st>>>(x, wrs_t, brs, (int)R, p.E, p.H, T, sv);
+            phase_fma_kernel<16, 16><<<pg, PH_THREADS, 0, st>>>(x, wrs_t, brs, (int)R, p.E, p.H, T, sv, h0, Hg);
     }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {

@@ -109,7 +109,8 @@ struct AttnSimtArgs {
     int B, H, T, hd;
     void *o;         // [B*T][H*hd] merged heads (float or bf16)
     float *att_w;    // [B][H][T][T] or nullptr
-    const int *tile_flags;  // [B*H][ceil(T/128)]: only flagged query tiles (nullptr = all)
+    const int *tile_flags;  // [B*Hg][ceil(T/128)]: only flagged query tiles (nullptr = all)
+    int h0, Hg;             // tile mode: heads h0 .. h0 + Hg - 1 (rows bh = b * Hg + h - h0)
 };
 
 __device__ __forceinline__ void store_out(float *p, float v) { *p = v; }
@@ -135,7 +136,7 @@ __global__ void __launch_bounds__(256) attn_simt_tiles_kernel(AttnSimtArgs a) {
     const int n_qt = (a.T + 127) / 128;
     const int tile = blockIdx.x % n_qt, bh = blockIdx.x / n_qt;
     if (!a.tile_flags[(long long)bh * n_qt + tile]) return;
-    const int b = bh / a.H, h = bh - b * a.H;
+    const int b = bh / a.Hg, h = a.h0 + (bh - b * a.Hg);
     const int warp = threadIdx.x >> 5;
     for (int q = tile * 128 + warp; q < min(a.T, tile * 128 + 128); q += 8) attn_simt_query<DPL, OutT>(a, b, h, q);
 }
@@ -225,7 +226,7 @@ template <class OutT>
 static void launch_attn_simt_t(const AttnSimtArgs &a, cudaStream_t st) {
     ProfScope ps(a.tile_flags ? "attn_simt_fallback" : "attn_simt", st);
     if (a.tile_flags) {
-        const unsigned grid = (unsigned)((long long)a.B * a.H * ((a.T + 127) / 128));
+        const unsigned grid = (unsigned)((long long)a.B * a.Hg * ((a.T + 127) / 128));
         if (a.hd <= 32) attn_simt_tiles_kernel<1, OutT><<<grid, 256, 0, st>>>(a);
         else if (a.hd <= 64) attn_simt_tiles_kernel<2, OutT><<<grid, 256, 0, st>>>(a);
         else if (a.hd <= 128) attn_simt_tiles_kernel<4, OutT><<<grid, 256, 0, st>>>(a);
@@ -242,21 +243,21 @@ static void launch_attn_simt_t(const AttnSimtArgs &a, cudaStream_t st) {
 void launch_attn_simt(const WbSeqView &sv, const float *content, int C, float content_scale,
                       const float *harmonic_n, int B, int H, int T, int hd, float *o,
                       float *att_w, cudaStream_t st) {
-    AttnSimtArgs a{sv, content, C, content_scale, harmonic_n, B, H, T, hd, o, att_w, nullptr};
+    AttnSimtArgs a{sv, content, C, content_scale, harmonic_n, B, H, T, hd, o, att_w, nullptr, 0, H};
     launch_attn_simt_t<float>(a, st);
 }
 
 void launch_attn_simt_fallback_bf16(const WbSeqView &sv, const float *content, int C, float content_scale,
                                     const float *harmonic_n, int B, int H, int T, int hd, __nv_bfloat16 *o,
-                                    const int *tile_flags, cudaStream_t st) {
-    AttnSimtArgs a{sv, content, C, content_scale, harmonic_n, B, H, T, hd, o, nullptr, tile_flags};
+                                    const int *tile_flags, int h0, int Hg, cudaStream_t st) {
+    AttnSimtArgs a{sv, content, C, content_scale, harmonic_n, B, H, T, hd, o, nullptr, tile_flags, h0, Hg};
     launch_attn_simt_t<__nv_bfloat16>(a, st);
 }
 
 void launch_attn_simt_fallback_f32(const WbSeqView &sv, const float *content, int C, float content_scale,
                                    const float *harmonic_n, int B, int H, int T, int hd, float *o,
-                                   const int *tile_flags, cudaStream_t st) {
-    AttnSimtArgs a{sv, content, C, content_scale, harmonic_n, B, H, T, hd, o, nullptr, tile_flags};
+                                   const int *tile_flags, int h0, int Hg, cudaStream_t st) {
+    AttnSimtArgs a{sv, content, C, content_scale, harmonic_n, B, H, T, hd, o, nullptr, tile_flags, h0, Hg};
     launch_attn_simt_t<float>(a, st);
 }
 

@@ -90,6 +90,7 @@ struct FeatArgs {
     float cscale;
     const float *hn;
     int B, H, T, hd, hdp;
+    int Hg, h0;                   // heads computed: h0 .. h0 + Hg - 1 (rows bh = b * Hg + (h - h0))
     __nv_bfloat16 *qf, *kf;       // [BH][T][FW]
     __nv_bfloat16 *vh, *vl;       // [BH][T][hdp] value hi / lo (lo only in wide mode)
     float *m0, *sprev, *cnorm;    // [BH][T]
@@ -121,14 +122,14 @@ __global__ void __launch_bounds__(FEAT_WARPS * 32) feat_kernel(FeatArgs a) {
     constexpr int RS = FWW + 1;               // padded row stride (words)
     __shared__ uint32_t fbuf[FEAT_WARPS][32 * RS];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const long long BH = (long long)a.B * a.H, total = BH * a.T;
+    const long long BH = (long long)a.B * a.Hg, total = BH * a.T;
     const long long i0 = ((long long)blockIdx.x * FEAT_WARPS + warp) * 32;
     if (i0 >= total) return;
     const long long i = i0 + lane;
     const bool live = i < total;
     const long long ii = live ? i : total - 1;
     const int bh = (int)(ii / a.T), t = (int)(ii - (long long)bh * a.T);
-    const int b = bh / a.H, h = bh - b * a.H;
+    const int b = bh / a.Hg, h = a.h0 + (bh - b * a.Hg);
     const long long base = wb_slot_base(a.sv, b, h);
     const float th = a.sv.theta[base + t];
     const int bk = a.sv.bucket[base + t];
@@ -295,7 +296,8 @@ __global__ void __launch_bounds__(FEAT_WARPS * 32) feat_kernel(FeatArgs a) {
 // fp32); roles below.
 // ---------------------------------------------------------------------------
 struct AttnTcArgs {
-    int BH, H, T, hd, n_qt;
+    int BH, H, T, hd, n_qt;     // BH = B * Hg rows
+    int Hg, h0;                 // heads computed: h0 .. h0 + Hg - 1
     const float *m0, *sprev, *cnorm;
     const unsigned int *cmax;
     WbSeqView sv;               // fp32 values for the previous-position term
@@ -386,7 +388,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int bh = blockIdx.x % a.BH;
     const int qt = a.n_qt - 1 - (int)(blockIdx.x / a.BH);  // heaviest (longest) tiles first
-    const int b = bh / a.H, h = bh - b * a.H;
+    const int b = bh / a.Hg, h = a.h0 + (bh - b * a.Hg);
     const int q0 = qt * QT;
     const bool softmax_warp = warp < ATT_SOFTMAX_WARPS;
     const int row = tid & (QT - 1), half = (warp >> 2) & 1;  // softmax role: query row, key-column half
@@ -754,7 +756,7 @@ __global__ void __launch_bounds__(128, 1)
             ptx::tmem_ld_wait();
             warp_stage32(buf, r, lane);
             const int n = n0 + c * 32 + lane;
-            const float bv = n < N ? bias[n] : 0.0f;
+            const float bv = (bias && n < N) ? bias[n] : 0.0f;
 #pragma unroll 4
             for (int j = 0; j < 32; j++) {
                 const int m = m0 + warp * 32 + j;
@@ -832,10 +834,10 @@ void tc_layer_free(TcLayerWeights *t) {
 struct CoreLayout {
     size_t qf, kf, vh, vl, m0, sp, cn, cm, fl, o, end;
 };
-static CoreLayout core_layout(const TcLayerWeights &t, int B, int T, size_t off) {
+static CoreLayout core_layout(const TcLayerWeights &t, int B, int T, size_t off, int Hg) {
     const int hdp = t.hd <= 64 ? 64 : 128;
     const int fw = t.wide ? 64 : 32;
-    const long long BH = (long long)B * t.H, R = (long long)B * T;
+    const long long BH = (long long)B * Hg, R = (long long)B * T;
     const int n_qt = (T + QT - 1) / QT;
     Carve cv;
     cv.off = off;
@@ -855,12 +857,17 @@ static CoreLayout core_layout(const TcLayerWeights &t, int B, int T, size_t off)
 }
 
 // y = A W^T + bias on the tcgen05 GEMM: A [M][K] and W [N][K] bf16 (tf32 =
-// false) or fp32 (tf32 = true), K-major; C [M][ldc] fp32.
+// false) or fp32 (tf32 = true), K-major with row strides lda / ldw elements
+// (0 = K); C [M][ldc] fp32; bias may be null.
 static int launch_gemm(bool tf32, const void *A, const void *W, const float *bias, float *C, int M, int N, int K,
-                       long long ldc, uint32_t *dev_err, cudaStream_t st, std::string *msg) {
+                       long long ldc, uint32_t *dev_err, cudaStream_t st, std::string *msg, long long lda = 0,
+                       long long ldw = 0) {
     const int esz = tf32 ? 4 : 2;
-    if (M <= 0 || N <= 0 || K <= 0 || ((long long)K * esz) % 16) {
-        *msg = "bad GEMM shape (rows of A and W must be multiples of 16 bytes)";
+    if (!lda) lda = K;
+    if (!ldw) ldw = K;
+    if (M <= 0 || N <= 0 || K <= 0 || ((long long)K * esz) % 16 || (lda * esz) % 16 || (ldw * esz) % 16 ||
+        (reinterpret_cast<uintptr_t>(A) % 16) || (reinterpret_cast<uintptr_t>(W) % 16)) {
+        *msg = "bad GEMM shape (rows and bases of A and W must be 16-byte aligned)";
         return WB_EINVAL;
     }
     const CUtensorMapDataType dt = tf32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
@@ -868,12 +875,13 @@ static int launch_gemm(bool tf32, const void *A, const void *W, const float *bia
     CUtensorMap ta, tb;
     int rc;
     const uint64_t adims[2] = {(uint64_t)K, (uint64_t)M};
-    const uint64_t str[1] = {(uint64_t)K * esz};
+    const uint64_t astr[1] = {(uint64_t)lda * esz};
     const uint32_t abox[2] = {bk, GBM};
-    if ((rc = make_tmap(&ta, A, dt, 2, adims, str, abox, CU_TENSOR_MAP_SWIZZLE_128B, msg))) return rc;
+    if ((rc = make_tmap(&ta, A, dt, 2, adims, astr, abox, CU_TENSOR_MAP_SWIZZLE_128B, msg))) return rc;
     const uint64_t bdims[2] = {(uint64_t)K, (uint64_t)N};
+    const uint64_t bstr[1] = {(uint64_t)ldw * esz};
     const uint32_t bbox[2] = {bk, GBN};
-    if ((rc = make_tmap(&tb, W, dt, 2, bdims, str, bbox, CU_TENSOR_MAP_SWIZZLE_128B, msg))) return rc;
+    if ((rc = make_tmap(&tb, W, dt, 2, bdims, bstr, bbox, CU_TENSOR_MAP_SWIZZLE_128B, msg))) return rc;
     dim3 gg((unsigned)((M + GBM - 1) / GBM), (unsigned)((N + GBN - 1) / GBN));
     ProfScope ps(tf32 ? "gemm_tf32" : "gemm_bf16", st);
     if (tf32) {
@@ -905,14 +913,14 @@ static void launch_attn_tc(const CUtensorMap &tq, const CUtensorMap &tk, const C
 // use_content) content vectors in `content`.  The workspace must already
 // hold core_layout(...).end bytes.
 static int tc_attention_core(const TcLayerWeights &t, const WbSeqView &sv, const float *content, int B, int T,
-                             float *y, Workspace *ws, const CoreLayout &lay, uint32_t *dev_err, cudaStream_t st,
-                             std::string *msg) {
+                             int h0, int Hg, bool add_bias, float *y, Workspace *ws, const CoreLayout &lay,
+                             uint32_t *dev_err, cudaStream_t st, std::string *msg) {
     const int H = t.H, hd = t.hd, E = t.E;
     const bool wide = t.wide;
     const int hdp = hd <= 64 ? 64 : 128;
     const int hdn = (hd + 15) / 16 * 16;
     const int fw = wide ? 64 : 32;
-    const long long BH = (long long)B * H, R = (long long)B * T;
+    const long long BH = (long long)B * Hg, R = (long long)B * T;
     const int n_qt = (T + QT - 1) / QT;
     int rc;
     char *w = (char *)ws->p;
@@ -928,7 +936,8 @@ static int tc_attention_core(const TcLayerWeights &t, const WbSeqView &sv, const
         return WB_ECUDA;
     }
     const float cscale = content ? 1.0f / std::sqrt((float)t.C) : 0.0f;
-    FeatArgs fa{sv, content, content ? t.C : 0, cscale, t.harmonic_n, B, H, T, hd, hdp, qf, kf, vh, vl, m0, sp, cn, cm};
+    FeatArgs fa{sv, content, content ? t.C : 0, cscale, t.harmonic_n, B, H, T, hd, hdp, Hg, h0,
+                qf, kf, vh, vl, m0, sp, cn, cm};
     const unsigned fgrid = (unsigned)((BH * T + FEAT_WARPS * 32 - 1) / (FEAT_WARPS * 32));
     {
         ProfScope ps("feat", st);
@@ -955,7 +964,7 @@ static int tc_attention_core(const TcLayerWeights &t, const WbSeqView &sv, const
                                     CU_TENSOR_MAP_SWIZZLE_128B, msg)))
             return rc;
     }
-    AttnTcArgs aa{(int)BH, H, T, hd, n_qt, m0, sp, cn, cm, sv, ob, E, fl, dev_err};
+    AttnTcArgs aa{(int)BH, H, T, hd, n_qt, Hg, h0, m0, sp, cn, cm, sv, ob, E, fl, dev_err};
     const unsigned grid = (unsigned)(BH * n_qt);
     if (hdp == 64) {
         if (wide) launch_attn_tc<64, true>(tq, tk, tvh, tvl, aa, hdn, grid, st);
@@ -967,14 +976,22 @@ static int tc_attention_core(const TcLayerWeights &t, const WbSeqView &sv, const
     {
         if (wide)
             launch_attn_simt_fallback_f32(sv, content, content ? t.C : 0, cscale, t.harmonic_n, B, H, T, hd,
-                                          (float *)ob, fl, st);
+                                          (float *)ob, fl, h0, Hg, st);
         else
             launch_attn_simt_fallback_bf16(sv, content, content ? t.C : 0, cscale, t.harmonic_n, B, H, T, hd,
-                                           (__nv_bfloat16 *)ob, fl, st);
+                                           (__nv_bfloat16 *)ob, fl, h0, Hg, st);
     }
-    // out_proj: y = o W_o^T + b_o
-    return launch_gemm(wide, ob, wide ? (const void *)t.w_o32 : (const void *)t.w_o, t.b_o, y, (int)R, E, E, E,
-                       dev_err, st, msg);
+    // out_proj: y = o W_o^T (+ b_o), over the computed heads' columns of o
+    // and W_o (K = Hg * hd): the partial output of a head range
+    if (Hg == H)
+        return launch_gemm(wide, ob, wide ? (const void *)t.w_o32 : (const void *)t.w_o, add_bias ? t.b_o : nullptr,
+                           y, (int)R, E, E, E, dev_err, st, msg);
+    if (!wide) {
+        *msg = "head ranges need the split-precision layer";
+        return WB_ENOTSUP;
+    }
+    return launch_gemm(true, (const float *)ob + (size_t)h0 * hd, t.w_o32 + (size_t)h0 * hd,
+                       add_bias ? t.b_o : nullptr, y, (int)R, E, Hg * hd, E, dev_err, st, msg, E, E);
 }
 
 int tc_gemm_bf16(const __nv_bfloat16 *A, const __nv_bfloat16 *B, const float *bias, float *C, int M, int N, int K,
@@ -989,9 +1006,19 @@ int tc_gemm_tf32(const float *A, const float *B, const float *bias, float *C, in
 
 int tc_attn_forward(const TcLayerWeights &t, const float *x, int B, int T, bool use_content, float *y,
                     float *phases_out, Workspace *ws, uint32_t *dev_err, int sm_count, cudaStream_t st,
-                    std::string *msg) {
+                    std::string *msg, int h0, int h1, bool add_bias) {
     (void)sm_count;
     const int H = t.H, hd = t.hd;
+    if (h1 < 0) h1 = H;
+    if (h0 < 0 || h1 > H || h0 >= h1) {
+        *msg = "bad head range";
+        return WB_EINVAL;
+    }
+    const int Hg = h1 - h0;
+    if (Hg < H && ((size_t)h0 * hd * 4) % 16) {
+        *msg = "a head range must start at a multiple of 4 columns (head_begin * head_dim)";
+        return WB_ENOTSUP;
+    }
     const long long R = (long long)B * T;
     if ((t.E * 2) % 16) {
         *msg = "n_embd must be a multiple of 8 for the tensor path";
@@ -1007,7 +1034,7 @@ int tc_attn_forward(const TcLayerWeights &t, const float *x, int B, int T, bool 
     const size_t o_th = cv.take<float>(R * H);
     const size_t o_bk = cv.take<uint8_t>(R * H);
     const size_t o_v = cv.take<float>(R * H * hd);
-    const CoreLayout lay = core_layout(t, B, T, cv.off);
+    const CoreLayout lay = core_layout(t, B, T, cv.off, Hg);
     if (ws_ensure(ws, lay.end, msg)) return WB_ENOMEM;
     char *w = (char *)ws->p;
     WbSeqView sv;
@@ -1019,9 +1046,9 @@ int tc_attn_forward(const TcLayerWeights &t, const float *x, int B, int T, bool 
     sv.slot = nullptr;
     float *content = use_content ? (float *)(w + o_ct) : nullptr;
     (void)o_rs;
-    int rc = launch_proj_tc(t.proj, t.pw.wrs_t, t.pw.brs, x, B, T, sv, content, dev_err, st, msg);
+    int rc = launch_proj_tc(t.proj, t.pw.wrs_t, t.pw.brs, x, B, T, sv, content, h0, Hg, dev_err, st, msg);
     if (rc) return rc;
-    rc = tc_attention_core(t, sv, content, B, T, y, ws, lay, dev_err, st, msg);
+    rc = tc_attention_core(t, sv, content, B, T, h0, Hg, add_bias, y, ws, lay, dev_err, st, msg);
     if (rc) return rc;
     if (phases_out &&
         cudaMemcpyAsync(phases_out, sv.theta, R * H * sizeof(float), cudaMemcpyDeviceToDevice, st) != cudaSuccess) {
@@ -1041,12 +1068,12 @@ int tc_kv_prefill(const TcLayerWeights &t, const WbSeqView &sv, const float *x, 
     const long long R = (long long)n_seq * T;
     Carve cv;
     const size_t o_rs = cv.take<float>(R * 2 * t.H);
-    const CoreLayout lay = core_layout(t, n_seq, T, cv.off);
+    const CoreLayout lay = core_layout(t, n_seq, T, cv.off, t.H);
     if (ws_ensure(ws, lay.end, msg)) return WB_ENOMEM;
     (void)o_rs;
-    int rc = launch_proj_tc(t.proj, t.pw.wrs_t, t.pw.brs, x, n_seq, T, sv, nullptr, dev_err, st, msg);
+    int rc = launch_proj_tc(t.proj, t.pw.wrs_t, t.pw.brs, x, n_seq, T, sv, nullptr, 0, t.H, dev_err, st, msg);
     if (rc) return rc;
-    return tc_attention_core(t, sv, nullptr, n_seq, T, y, ws, lay, dev_err, st, msg);
+    return tc_attention_core(t, sv, nullptr, n_seq, T, 0, t.H, true, y, ws, lay, dev_err, st, msg);
 }
 
 // Rows from which the decode out_proj runs on the tensor-core GEMM (below

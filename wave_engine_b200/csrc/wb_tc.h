@@ -24,9 +24,12 @@ struct TcLayerWeights {
 int tc_layer_upload(TcLayerWeights *t, const wb_attn_weights_desc *w, std::string *msg);
 void tc_layer_free(TcLayerWeights *t);
 
+// Prefill forward of heads h0 .. h1 - 1 (h1 < 0: all heads); with a head
+// range y is that range's share of the output, o_range W_o[:, range]^T,
+// plus the bias when add_bias.
 int tc_attn_forward(const TcLayerWeights &t, const float *x, int B, int T, bool use_content, float *y,
                     float *phases_out, Workspace *ws, uint32_t *dev_err, int sm_count, cudaStream_t st,
-                    std::string *msg);
+                    std::string *msg, int h0 = 0, int h1 = -1, bool add_bias = true);
 int tc_kv_prefill(const TcLayerWeights &t, const WbSeqView &sv, const float *x, int n_seq, int T, float *y,
                   Workspace *ws, uint32_t *dev_err, int sm_count, cudaStream_t st, std::string *msg);
 int tc_gemm_bf16(const __nv_bfloat16 *A, const __nv_bfloat16 *B, const float *bias, float *C, int M, int N, int K,
