@@ -220,8 +220,9 @@ WB_API int wb_kv_decode(wb_context *ctx, wb_kv_cache *cache, int layer_idx, cons
  * stream capture, where cudaMalloc is not allowed).  The kernels' scratch
  * lives in one static device array of WB_NOALLOC_SCRATCH_BYTES per GPU,
  * held until the process exits; a cache whose decode scratch
- * (slots x heads x ceil(max_ctx/512) partial rows, plus per-slot values and
- * outputs) exceeds it is rejected with WB_EINVAL.  seq_ids, x and y must be
+ * (slots x heads x splits partial rows -- one split up to max_ctx 1536,
+ * else ceil(max_ctx/512) -- plus per-slot values and outputs) exceeds it is
+ * rejected with WB_EINVAL.  seq_ids, x and y must be
  * DEVICE pointers (nothing is staged) and are used as with device ids in
  * wb_kv_decode.  The first call on each device resolves the array's device
  * address (cudaGetSymbolAddress) and must come before any stream capture.

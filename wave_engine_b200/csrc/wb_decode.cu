@@ -2,7 +2,9 @@
 //
 // Two launches per layer and decode step.
 //
-// decode_attn_kernel, grid (split, head, sequence), 512 keys per CTA:
+// decode_attn_kernel, grid (split, head, sequence), 128 keys per warp; a
+// cache of up to 1536 keys takes one CTA of up to 12 warps per (sequence,
+// head), a longer one 4-warp CTAs of 512 keys (split partials, ticket merge):
 //   * every CTA projects the new position's phase theta_q = atan2f(s, r)
 //     (kv_cache.rs:271) from the x row, then scans its split of the cached
 //     keys: the bucket byte and phase of every key (coalesced, issued up
@@ -15,8 +17,9 @@
 //     reference's max-subtraction, and split partials (sum p, sum p v) merge
 //     by plain addition, in split order (deterministic);
 //   * split 0 also computes the new value v = Wv x_h + b (kv_cache.rs:272-277);
-//     the last CTA of a (sequence, head) -- an atomic ticket in scratch --
-//     merges the partials, adds the self term (p = 1, v), normalises into
+//     the warps of a CTA merge in shared memory, and with several splits the
+//     last CTA of a (sequence, head) -- an atomic ticket in scratch -- merges
+//     the split partials; it adds the self term (p = 1, v), normalises into
 //     the merged head output o, and appends (phase, bucket, value) at
 //     position n.
 // decode_out_kernel runs out_proj (kv_cache.rs:330-335) on the merged
@@ -35,10 +38,19 @@
 
 namespace wb {
 
-static constexpr int DEC_THREADS = 128;
-static constexpr int DEC_WARPS = DEC_THREADS / 32;
 static constexpr int DEC_KEYS_PER_WARP = 128;
-static constexpr int DEC_CHUNK = DEC_WARPS * DEC_KEYS_PER_WARP;  // keys per CTA (512)
+static constexpr int DEC_MAX_HD = 128;  // head_dim limit (one merge column per thread of a 4-warp CTA)
+
+// Warps per attention CTA, from the cache capacity.  Up to 1536 keys a
+// (sequence, head) is one CTA of up to 12 warps whose partials merge in
+// shared memory: no split partials in scratch, no ticket, one phase
+// projection.  Longer caches use 4-warp CTAs of 512 keys and the ticket
+// merge, which keeps many short CTAs in flight for long contexts.
+static int decode_warps(int cap) { return cap <= 512 ? 4 : cap <= 1024 ? 8 : cap <= 1536 ? 12 : 4; }
+static int decode_nsplit(int cap) {
+    const int chunk = decode_warps(cap) * DEC_KEYS_PER_WARP;
+    return (cap + chunk - 1) / chunk;
+}
 
 // cudaLaunchKernelEx, optionally with the programmatic-stream-serialization
 // attribute (the grid may begin while the previous grid of the stream runs;
@@ -123,8 +135,13 @@ __device__ __forceinline__ float decode_weight(float arg) {
 
 // VEC: floats per value load.
 static constexpr int DEC_U = 8;  // value loads per lane in flight (DEC_U * 32 / G rows per warp)
-template <int VEC>
-__global__ void __launch_bounds__(DEC_THREADS) decode_attn_kernel(DecodeArgs a) {
+// NW: warps per CTA (4, 8 or 12); the register cap keeps 9, 4 or 3 CTAs
+// per SM resident so a serve-sized grid is one wave.
+template <int VEC, int NW>
+__global__ void __launch_bounds__(NW * 32, NW == 12 ? 3 : (NW == 8 ? 4 : 9)) decode_attn_kernel(DecodeArgs a) {
+    constexpr int DEC_THREADS = NW * 32;
+    constexpr int DEC_WARPS = NW;
+    constexpr int DEC_CHUNK = NW * DEC_KEYS_PER_WARP;  // keys per CTA
     extern __shared__ float dsm[];
     const int split = blockIdx.x, h = blockIdx.y, i = blockIdx.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -541,7 +558,7 @@ struct DecodeScratch {
     size_t part, vnew, o, ticket, end;
 };
 static DecodeScratch decode_scratch_layout(int n_seq, int H, int hd, int E, int cap) {
-    const int nsplit = (cap + DEC_CHUNK - 1) / DEC_CHUNK;
+    const int nsplit = decode_nsplit(cap);
     Carve c;
     DecodeScratch d;
     d.part = c.take<float>((size_t)n_seq * H * nsplit * (hd + 1));
@@ -562,16 +579,26 @@ void decode_scratch_tickets(int n_seq, int H, int hd, int E, int cap, size_t *of
     *bytes = d.end - d.ticket;
 }
 
-template <int VEC>
-static cudaError_t launch_attn(const DecodeArgs &a, dim3 grid, size_t smem, cudaStream_t st) {
-    cudaFuncSetAttribute(decode_attn_kernel<VEC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    decode_attn_kernel<VEC><<<grid, DEC_THREADS, smem, st>>>(a);
+template <int VEC, int NW>
+static cudaError_t launch_attn(const DecodeArgs &a, dim3 grid, cudaStream_t st) {
+    const size_t smem = sizeof(float) * ((size_t)a.E + 2 * NW * DEC_KEYS_PER_WARP + NW * a.hd + NW + 2 * NW +
+                                         NW * 32);
+    cudaFuncSetAttribute(decode_attn_kernel<VEC, NW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    decode_attn_kernel<VEC, NW><<<grid, NW * 32, smem, st>>>(a);
     return cudaGetLastError();
+}
+
+template <int VEC>
+static cudaError_t launch_attn_nw(const DecodeArgs &a, int nw, dim3 grid, cudaStream_t st) {
+    if (nw == 12) return launch_attn<VEC, 12>(a, grid, st);
+    if (nw == 8) return launch_attn<VEC, 8>(a, grid, st);
+    return launch_attn<VEC, 4>(a, grid, st);
 }
 
 int launch_decode_attn(const DecodeLaunch &L, void *scratch, size_t scratch_bytes, float **o_out,
                        cudaStream_t st, std::string *msg) {
-    const int nsplit = (L.cap + DEC_CHUNK - 1) / DEC_CHUNK;
+    const int nsplit = decode_nsplit(L.cap);
+    const int nw = decode_warps(L.cap);
     // laid out for the cache's slot count (not this call's n_seq) so the
     // zeroed tickets stay at fixed offsets whatever the batch of the call
     if (L.n_seq > L.n_slots) {
@@ -583,7 +610,7 @@ int launch_decode_attn(const DecodeLaunch &L, void *scratch, size_t scratch_byte
         *msg = "decode scratch too small";
         return WB_EINVAL;
     }
-    if (L.hd > DEC_THREADS) {
+    if (L.hd > DEC_MAX_HD) {
         *msg = "decode supports head_dim <= 128";
         return WB_ENOTSUP;
     }
@@ -610,15 +637,13 @@ int launch_decode_attn(const DecodeLaunch &L, void *scratch, size_t scratch_byte
     *o_out = a.o;
     a.ticket = (unsigned int *)(s + lay.ticket);
     a.dev_err = L.dev_err;
-    const size_t smem = sizeof(float) * ((size_t)L.E + 2 * DEC_WARPS * DEC_KEYS_PER_WARP + DEC_WARPS * L.hd +
-                                         DEC_WARPS + 2 * DEC_WARPS + DEC_THREADS);
     dim3 grid(nsplit, L.H, L.n_seq);
     cudaError_t e;
     {
         ProfScope ps("decode_attn", st);
-        if (L.hd % 4 == 0) e = launch_attn<4>(a, grid, smem, st);
-        else if (L.hd % 2 == 0) e = launch_attn<2>(a, grid, smem, st);
-        else e = launch_attn<1>(a, grid, smem, st);
+        if (L.hd % 4 == 0) e = launch_attn_nw<4>(a, nw, grid, st);
+        else if (L.hd % 2 == 0) e = launch_attn_nw<2>(a, nw, grid, st);
+        else e = launch_attn_nw<1>(a, nw, grid, st);
     }
     if (e != cudaSuccess) {
         *msg = std::string("decode launch failed: ") + cudaGetErrorString(e);
