@@ -133,6 +133,32 @@ __device__ __forceinline__ float decode_weight(float arg) {
     return __expf(__cosf(r) - 1.0f);
 }
 
+// x row -> shared memory and this thread's partial sums of the phase
+// projection (r, s) = W_rs x (kv_cache.rs:271): elements tid, tid + THREADS,
+// ... summed in that order, XU loads of x and of W_rs in flight per batch.
+template <int XU, int THREADS>
+__device__ __forceinline__ void decode_x_phase(const float *xr, const float *wrs_t, int E, int H, int h, int tid,
+                                               float *xs, float &r, float &s) {
+    for (int j0 = 0; j0 < E; j0 += XU * THREADS) {
+        float xv[XU];
+        float2 wv2[XU];
+#pragma unroll
+        for (int u = 0; u < XU; u++) {
+            const int j = j0 + u * THREADS + tid;
+            xv[u] = j < E ? __ldg(xr + j) : 0.0f;
+            wv2[u] = j < E ? __ldg(reinterpret_cast<const float2 *>(wrs_t + ((long long)j * H + h) * 2))
+                           : make_float2(0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < XU; u++) {
+            const int j = j0 + u * THREADS + tid;
+            if (j < E) xs[j] = xv[u];
+            r = fmaf(wv2[u].x, xv[u], r);
+            s = fmaf(wv2[u].y, xv[u], s);
+        }
+    }
+}
+
 // VEC: floats per value load.
 static constexpr int DEC_U = 8;  // value loads per lane in flight (DEC_U * 32 / G rows per warp)
 // NW: warps per CTA (4, 8 or 12); the register cap keeps 9, 4 or 3 CTAs
@@ -157,6 +183,35 @@ __global__ void __launch_bounds__(NW * 32, NW == 12 ? 3 : (NW == 8 ? 4 : 9)) dec
 
     // the out_proj grid may launch and load its weights
     ptx::griddep_launch_dependents();
+    // ONE: one split per (sequence, head) (decode_warps); everything that
+    // does not depend on the cached state is loaded before the slot
+    constexpr bool ONE = NW > 4;
+    const float *xr = a.x + (long long)i * E;
+    // new value v = Wv x_h + b (kv_cache.rs:272-277): thread (vd, vq) sums
+    // inputs [vq * kper, (vq + 1) * kper) of output vd, in input order
+    const int P = DEC_THREADS / hd;
+    const int vd = tid % hd, vq = tid / hd;
+    const int kper = (hd + P - 1) / P;
+    constexpr int VN = NW == 8 ? 16 : 12;  // value weights held in registers (ONE)
+    const bool vearly = ONE && kper <= VN;
+    float wl0[ONE ? VN : 1];
+    float r = 0.0f, s = 0.0f;
+    float hn = 0.0f, br = 0.0f, bs = 0.0f;
+    float vpar = 0.0f;  // ONE: the bias b of output vd starts the slice-0 sum
+    if constexpr (ONE) {
+        hn = __ldg(a.hn + h);
+        br = __ldg(a.brs + h * 2);
+        bs = __ldg(a.brs + h * 2 + 1);
+        if (vq == 0) vpar = __ldg(a.bv + h * hd + vd);
+        if (vearly && vq < P) {
+            const float *wv = a.wv_t + (long long)h * hd * hd + vd;
+            const int j0 = vq * kper;
+#pragma unroll
+            for (int u = 0; u < VN; u++)
+                wl0[u] = u < kper && j0 + u < hd ? __ldg(wv + (long long)(j0 + u) * hd) : 0.0f;
+        }
+        decode_x_phase<NW == 8 ? 4 : 2, DEC_THREADS>(xr, a.wrs_t, E, a.H, h, tid, xs, r, s);
+    }
     const int slot = a.sv.slot ? a.sv.slot[i] : i;
     if (slot < 0 || slot >= a.n_slots) {
         if (split == 0 && h == 0 && tid == 0) atomicOr(a.dev_err, WB_DERR_BOUNDS);
@@ -171,62 +226,52 @@ __global__ void __launch_bounds__(NW * 32, NW == 12 ? 3 : (NW == 8 ? 4 : 9)) dec
     uint8_t kb[KR];
     float kth[KR];
     const int n = a.len[slot];
+    if constexpr (ONE) {
+        // the whole cache row is this CTA's: the key loads (bucket byte +
+        // phase) need only the slot, bounded by the allocated row, so they
+        // go out together with the length load; keys at or past n are
+        // dropped by the k < n test of the score loop
+#pragma unroll
+        for (int c = 0; c < KR; c++) {
+            const int k = k0 + c * 32 + lane;
+            kb[c] = k < a.sv.cap ? __ldg(bucket + k) : (uint8_t)0xFF;
+            kth[c] = k < a.sv.cap ? __ldg(theta + k) : 0.0f;
+        }
+    }
     if (n < 0 || n >= a.cap) {
         if (split == 0 && h == 0 && tid == 0) atomicOr(a.dev_err, WB_DERR_BOUNDS);
         return;
     }
     const int n_act = n > 0 ? (n + DEC_CHUNK - 1) / DEC_CHUNK : 1;
     if (split >= n_act) return;
-    // this warp's key loads go out first (bucket byte + phase of every key)
+    if constexpr (!ONE) {
+        // this warp's key loads, up to the length (most splits of a long
+        // cache hold no keys of a short sequence), then the x row
 #pragma unroll
-    for (int c = 0; c < KR; c++) {
-        const int k = k0 + c * 32 + lane;
-        kb[c] = k < n ? __ldg(bucket + k) : (uint8_t)0xFF;
-        kth[c] = k < n ? __ldg(theta + k) : 0.0f;
-    }
-
-    // x row; theta_q (kv_cache.rs:271, tree-summed); split 0: the new value
-    // loads are issued in batches of 8 before any is used (each loop below
-    // would otherwise pay one memory round trip per iteration)
-    const float *xr = a.x + (long long)i * E;
-    float r = 0.0f, s = 0.0f;
-    for (int j0 = 0; j0 < E; j0 += 8 * DEC_THREADS) {
-        float xv[8];
-        float2 wv2[8];
-#pragma unroll
-        for (int u = 0; u < 8; u++) {
-            const int j = j0 + u * DEC_THREADS + tid;
-            xv[u] = j < E ? __ldg(xr + j) : 0.0f;
-            wv2[u] = j < E ? __ldg(reinterpret_cast<const float2 *>(a.wrs_t + ((long long)j * a.H + h) * 2))
-                           : make_float2(0.f, 0.f);
+        for (int c = 0; c < KR; c++) {
+            const int k = k0 + c * 32 + lane;
+            kb[c] = k < n ? __ldg(bucket + k) : (uint8_t)0xFF;
+            kth[c] = k < n ? __ldg(theta + k) : 0.0f;
         }
+        decode_x_phase<8, DEC_THREADS>(xr, a.wrs_t, E, a.H, h, tid, xs, r, s);
+        __syncthreads();
+        // split 0: the new value, weight loads in batches of 16 before use
+        if (split == 0 && vq < P) {
+            const float *xh = xs + h * hd;
+            const float *wv = a.wv_t + (long long)h * hd * hd + vd;
+            const int j0 = vq * kper, j1 = min(hd, j0 + kper);
+            for (int jb = j0; jb < j1; jb += 16) {
+                float wl[16];
 #pragma unroll
-        for (int u = 0; u < 8; u++) {
-            const int j = j0 + u * DEC_THREADS + tid;
-            if (j < E) xs[j] = xv[u];
-            r = fmaf(wv2[u].x, xv[u], r);
-            s = fmaf(wv2[u].y, xv[u], s);
+                for (int u = 0; u < 16; u++) wl[u] = jb + u < j1 ? __ldg(wv + (long long)(jb + u) * hd) : 0.0f;
+#pragma unroll
+                for (int u = 0; u < 16; u++)
+                    if (jb + u < j1) vpar = fmaf(wl[u], xh[jb + u], vpar);
+            }
         }
+        vpart[tid] = vpar;
     }
-    __syncthreads();
-    const int P = DEC_THREADS / hd;  // parts of hd/P inputs per new-value output
-    const int vd = tid % hd, vq = tid / hd;
-    const int kper = (hd + P - 1) / P;
-    float vpar = 0.0f;
-    if (split == 0 && vq < P) {
-        const float *xh = xs + h * hd;
-        const float *wv = a.wv_t + (long long)h * hd * hd + vd;
-        const int j0 = vq * kper, j1 = min(hd, j0 + kper);
-        for (int jb = j0; jb < j1; jb += 16) {
-            float wl[16];
-#pragma unroll
-            for (int u = 0; u < 16; u++) wl[u] = jb + u < j1 ? __ldg(wv + (long long)(jb + u) * hd) : 0.0f;
-#pragma unroll
-            for (int u = 0; u < 16; u++)
-                if (jb + u < j1) vpar = fmaf(wl[u], xh[jb + u], vpar);
-        }
-    }
-    vpart[tid] = vpar;
+    // theta_q (tree-summed partials)
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
         r += __shfl_xor_sync(0xffffffffu, r, o);
@@ -237,7 +282,12 @@ __global__ void __launch_bounds__(NW * 32, NW == 12 ? 3 : (NW == 8 ? 4 : 9)) dec
         red[DEC_WARPS + warp] = s;
     }
     __syncthreads();
-    float rr = a.brs[h * 2], ss = a.brs[h * 2 + 1];
+    if constexpr (!ONE) {
+        hn = __ldg(a.hn + h);
+        br = __ldg(a.brs + h * 2);
+        bs = __ldg(a.brs + h * 2 + 1);
+    }
+    float rr = br, ss = bs;
 #pragma unroll
     for (int w = 0; w < DEC_WARPS; w++) {
         rr += red[w];
@@ -246,10 +296,34 @@ __global__ void __launch_bounds__(NW * 32, NW == 12 ? 3 : (NW == 8 ? 4 : 9)) dec
     const float thq = atan2f(ss, rr);
     const int qb = phase_to_bucket(thq);
     const uint32_t amask = allowed_bucket_mask(qb);
-    const float hn = a.hn[h];
     float *vnew = a.vnew + ((long long)i * a.H + h) * hd;
-    if (split == 0 && tid < hd) {  // hd <= DEC_THREADS (checked at launch)
-        float v = a.bv[h * hd + tid];
+    if constexpr (ONE) {
+        // the new value's partial sums, off the phase's path (the x row is
+        // in shared memory since the barrier above); summed at the merge
+        if (vq < P) {
+            const float *xh = xs + h * hd;
+            const int j0 = vq * kper;
+            if (vearly) {
+#pragma unroll
+                for (int u = 0; u < VN; u++)
+                    if (u < kper && j0 + u < hd) vpar = fmaf(wl0[u], xh[j0 + u], vpar);
+            } else {
+                const float *wv = a.wv_t + (long long)h * hd * hd + vd;
+                const int j1 = min(hd, j0 + kper);
+                for (int jb = j0; jb < j1; jb += 16) {
+                    float wl[16];
+#pragma unroll
+                    for (int u = 0; u < 16; u++)
+                        wl[u] = jb + u < j1 ? __ldg(wv + (long long)(jb + u) * hd) : 0.0f;
+#pragma unroll
+                    for (int u = 0; u < 16; u++)
+                        if (jb + u < j1) vpar = fmaf(wl[u], xh[jb + u], vpar);
+                }
+            }
+        }
+        vpart[tid] = vpar;
+    } else if (split == 0 && tid < hd) {  // hd <= DEC_MAX_HD <= DEC_THREADS (checked at launch)
+        float v = __ldg(a.bv + h * hd + tid);
         for (int q = 0; q < P; q++) v += vpart[q * hd + tid];
         vnew[tid] = v;
     }
@@ -375,7 +449,13 @@ __global__ void __launch_bounds__(NW * 32, NW == 12 ? 3 : (NW == 8 ? 4 : 9)) dec
     // ---- merge (i, h): self term p = exp(1 - 1) = 1 (kv_cache.rs:294, :318),
     // normalise, append (kv_cache.rs:323-326)
     if (tid < hd) {
-        const float vn = __ldcg(vnew + tid);
+        float vn;
+        if constexpr (ONE) {
+            vn = vpart[tid];  // slice 0 (with the bias), then the other slices
+            for (int q = 1; q < P; q++) vn += vpart[q * hd + tid];
+        } else {
+            vn = __ldcg(vnew + tid);
+        }
         a.o[(long long)i * E + (long long)h * hd + tid] = (od + vn) / (lall + 1.0f);
         a.sv.v[(base + n) * hd + tid] = vn;
     }
@@ -599,6 +679,10 @@ int launch_decode_attn(const DecodeLaunch &L, void *scratch, size_t scratch_byte
                        cudaStream_t st, std::string *msg) {
     const int nsplit = decode_nsplit(L.cap);
     const int nw = decode_warps(L.cap);
+    if (nw > 4 && nsplit != 1) {
+        *msg = "decode: internal split plan error";
+        return WB_EINVAL;
+    }
     // laid out for the cache's slot count (not this call's n_seq) so the
     // zeroed tickets stay at fixed offsets whatever the batch of the call
     if (L.n_seq > L.n_slots) {
