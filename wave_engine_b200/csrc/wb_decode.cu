@@ -138,8 +138,8 @@ __device__ __forceinline__ float decode_weight(float arg) {
 // ... summed in that order, XU loads of x and of W_rs in flight per batch.
 template <int XU, int THREADS>
 __device__ __forceinline__ void decode_x_phase(const float *xr, const float *wrs_t, int E, int H, int h, int tid,
-                                               float *xs, float &r, float &s) {
-    for (int j0 = 0; j0 < E; j0 += XU * THREADS) {
+                                               float *xs, float &r, float &s, int jbeg = 0) {
+    for (int j0 = jbeg; j0 < E; j0 += XU * THREADS) {
         float xv[XU];
         float2 wv2[XU];
 #pragma unroll
@@ -157,6 +157,29 @@ __device__ __forceinline__ void decode_x_phase(const float *xr, const float *wrs
             s = fmaf(wv2[u].y, xv[u], s);
         }
     }
+}
+
+// theta_q = atan2(s, r) of the CTA's partial sums (warp shuffles, then the
+// warps' sums in warp order after one barrier) plus the bias (br, bs).
+template <int NW>
+__device__ __forceinline__ float decode_theta_q(float r, float s, float br, float bs, float *red, int warp, int lane) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        r += __shfl_xor_sync(0xffffffffu, r, o);
+        s += __shfl_xor_sync(0xffffffffu, s, o);
+    }
+    if (lane == 0) {
+        red[warp] = r;
+        red[NW + warp] = s;
+    }
+    __syncthreads();
+    float rr = br, ss = bs;
+#pragma unroll
+    for (int w = 0; w < NW; w++) {
+        rr += red[w];
+        ss += red[NW + w];
+    }
+    return atan2f(ss, rr);
 }
 
 // VEC: floats per value load.
@@ -183,22 +206,35 @@ __global__ void __launch_bounds__(NW * 32, NW == 12 ? 3 : (NW == 8 ? 4 : 9)) dec
 
     // the out_proj grid may launch and load its weights
     ptx::griddep_launch_dependents();
-    // ONE: one split per (sequence, head) (decode_warps); everything that
-    // does not depend on the cached state is loaded before the slot
+    // ONE: one split per (sequence, head) (decode_warps).  The slot load
+    // goes first and everything that does not depend on the cached state is
+    // in flight with it; theta_q is ready after one barrier, before the
+    // length arrives.
     constexpr bool ONE = NW > 4;
     const float *xr = a.x + (long long)i * E;
+    const int slot = a.sv.slot ? a.sv.slot[i] : i;
     // new value v = Wv x_h + b (kv_cache.rs:272-277): thread (vd, vq) sums
     // inputs [vq * kper, (vq + 1) * kper) of output vd, in input order
     const int P = DEC_THREADS / hd;
     const int vd = tid % hd, vq = tid / hd;
     const int kper = (hd + P - 1) / P;
     constexpr int VN = NW == 8 ? 16 : 12;  // value weights held in registers (ONE)
+    constexpr int XU = NW == 8 ? 4 : 2;    // x elements per thread in the first batch (ONE)
     const bool vearly = ONE && kper <= VN;
     float wl0[ONE ? VN : 1];
+    float xv0[ONE ? XU : 1];
+    float2 wv0[ONE ? XU : 1];
     float r = 0.0f, s = 0.0f;
     float hn = 0.0f, br = 0.0f, bs = 0.0f;
     float vpar = 0.0f;  // ONE: the bias b of output vd starts the slice-0 sum
     if constexpr (ONE) {
+#pragma unroll
+        for (int u = 0; u < XU; u++) {
+            const int j = u * DEC_THREADS + tid;
+            xv0[u] = j < E ? __ldg(xr + j) : 0.0f;
+            wv0[u] = j < E ? __ldg(reinterpret_cast<const float2 *>(a.wrs_t + ((long long)j * a.H + h) * 2))
+                           : make_float2(0.f, 0.f);
+        }
         hn = __ldg(a.hn + h);
         br = __ldg(a.brs + h * 2);
         bs = __ldg(a.brs + h * 2 + 1);
@@ -210,9 +246,7 @@ __global__ void __launch_bounds__(NW * 32, NW == 12 ? 3 : (NW == 8 ? 4 : 9)) dec
             for (int u = 0; u < VN; u++)
                 wl0[u] = u < kper && j0 + u < hd ? __ldg(wv + (long long)(j0 + u) * hd) : 0.0f;
         }
-        decode_x_phase<NW == 8 ? 4 : 2, DEC_THREADS>(xr, a.wrs_t, E, a.H, h, tid, xs, r, s);
     }
-    const int slot = a.sv.slot ? a.sv.slot[i] : i;
     if (slot < 0 || slot >= a.n_slots) {
         if (split == 0 && h == 0 && tid == 0) atomicOr(a.dev_err, WB_DERR_BOUNDS);
         return;
@@ -226,6 +260,7 @@ __global__ void __launch_bounds__(NW * 32, NW == 12 ? 3 : (NW == 8 ? 4 : 9)) dec
     uint8_t kb[KR];
     float kth[KR];
     const int n = a.len[slot];
+    float thq;
     if constexpr (ONE) {
         // the whole cache row is this CTA's: the key loads (bucket byte +
         // phase) need only the slot, bounded by the allocated row, so they
@@ -237,6 +272,39 @@ __global__ void __launch_bounds__(NW * 32, NW == 12 ? 3 : (NW == 8 ? 4 : 9)) dec
             kb[c] = k < a.sv.cap ? __ldg(bucket + k) : (uint8_t)0xFF;
             kth[c] = k < a.sv.cap ? __ldg(theta + k) : 0.0f;
         }
+        // x row: the first batch (loaded above), then any further batches
+#pragma unroll
+        for (int u = 0; u < XU; u++) {
+            const int j = u * DEC_THREADS + tid;
+            if (j < E) xs[j] = xv0[u];
+            r = fmaf(wv0[u].x, xv0[u], r);
+            s = fmaf(wv0[u].y, xv0[u], s);
+        }
+        decode_x_phase<XU, DEC_THREADS>(xr, a.wrs_t, E, a.H, h, tid, xs, r, s, XU * DEC_THREADS);
+        thq = decode_theta_q<NW>(r, s, br, bs, red, warp, lane);  // barrier: xs visible too
+        // the new value's partial sums (summed at the merge)
+        if (vq < P) {
+            const float *xh = xs + h * hd;
+            const int j0 = vq * kper;
+            if (vearly) {
+#pragma unroll
+                for (int u = 0; u < VN; u++)
+                    if (u < kper && j0 + u < hd) vpar = fmaf(wl0[u], xh[j0 + u], vpar);
+            } else {
+                const float *wv = a.wv_t + (long long)h * hd * hd + vd;
+                const int j1 = min(hd, j0 + kper);
+                for (int jb = j0; jb < j1; jb += 16) {
+                    float wl[16];
+#pragma unroll
+                    for (int u = 0; u < 16; u++)
+                        wl[u] = jb + u < j1 ? __ldg(wv + (long long)(jb + u) * hd) : 0.0f;
+#pragma unroll
+                    for (int u = 0; u < 16; u++)
+                        if (jb + u < j1) vpar = fmaf(wl[u], xh[jb + u], vpar);
+                }
+            }
+        }
+        vpart[tid] = vpar;
     }
     if (n < 0 || n >= a.cap) {
         if (split == 0 && h == 0 && tid == 0) atomicOr(a.dev_err, WB_DERR_BOUNDS);
@@ -244,6 +312,7 @@ __global__ void __launch_bounds__(NW * 32, NW == 12 ? 3 : (NW == 8 ? 4 : 9)) dec
     }
     const int n_act = n > 0 ? (n + DEC_CHUNK - 1) / DEC_CHUNK : 1;
     if (split >= n_act) return;
+    float *vnew = a.vnew + ((long long)i * a.H + h) * hd;
     if constexpr (!ONE) {
         // this warp's key loads, up to the length (most splits of a long
         // cache hold no keys of a short sequence), then the x row
@@ -270,63 +339,16 @@ __global__ void __launch_bounds__(NW * 32, NW == 12 ? 3 : (NW == 8 ? 4 : 9)) dec
             }
         }
         vpart[tid] = vpar;
-    }
-    // theta_q (tree-summed partials)
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        r += __shfl_xor_sync(0xffffffffu, r, o);
-        s += __shfl_xor_sync(0xffffffffu, s, o);
-    }
-    if (lane == 0) {
-        red[warp] = r;
-        red[DEC_WARPS + warp] = s;
-    }
-    __syncthreads();
-    if constexpr (!ONE) {
         hn = __ldg(a.hn + h);
-        br = __ldg(a.brs + h * 2);
-        bs = __ldg(a.brs + h * 2 + 1);
+        thq = decode_theta_q<NW>(r, s, __ldg(a.brs + h * 2), __ldg(a.brs + h * 2 + 1), red, warp, lane);
+        if (split == 0 && tid < hd) {  // hd <= DEC_MAX_HD <= DEC_THREADS (checked at launch)
+            float v = __ldg(a.bv + h * hd + tid);
+            for (int q = 0; q < P; q++) v += vpart[q * hd + tid];
+            vnew[tid] = v;
+        }
     }
-    float rr = br, ss = bs;
-#pragma unroll
-    for (int w = 0; w < DEC_WARPS; w++) {
-        rr += red[w];
-        ss += red[DEC_WARPS + w];
-    }
-    const float thq = atan2f(ss, rr);
     const int qb = phase_to_bucket(thq);
     const uint32_t amask = allowed_bucket_mask(qb);
-    float *vnew = a.vnew + ((long long)i * a.H + h) * hd;
-    if constexpr (ONE) {
-        // the new value's partial sums, off the phase's path (the x row is
-        // in shared memory since the barrier above); summed at the merge
-        if (vq < P) {
-            const float *xh = xs + h * hd;
-            const int j0 = vq * kper;
-            if (vearly) {
-#pragma unroll
-                for (int u = 0; u < VN; u++)
-                    if (u < kper && j0 + u < hd) vpar = fmaf(wl0[u], xh[j0 + u], vpar);
-            } else {
-                const float *wv = a.wv_t + (long long)h * hd * hd + vd;
-                const int j1 = min(hd, j0 + kper);
-                for (int jb = j0; jb < j1; jb += 16) {
-                    float wl[16];
-#pragma unroll
-                    for (int u = 0; u < 16; u++)
-                        wl[u] = jb + u < j1 ? __ldg(wv + (long long)(jb + u) * hd) : 0.0f;
-#pragma unroll
-                    for (int u = 0; u < 16; u++)
-                        if (jb + u < j1) vpar = fmaf(wl[u], xh[jb + u], vpar);
-                }
-            }
-        }
-        vpart[tid] = vpar;
-    } else if (split == 0 && tid < hd) {  // hd <= DEC_MAX_HD <= DEC_THREADS (checked at launch)
-        float v = __ldg(a.bv + h * hd + tid);
-        for (int q = 0; q < P; q++) v += vpart[q * hd + tid];
-        vnew[tid] = v;
-    }
 
     // mask, score, p = exp(s - 1); compact (index, p) per warp
     int m = 0;
@@ -475,8 +497,9 @@ __global__ void __launch_bounds__(NW * 32, NW == 12 ? 3 : (NW == 8 ? 4 : 9)) dec
 // before the dependency wait -- the attention grid does not write W_o, and
 // the copy holds no registers -- so after the wait only the o rows (one
 // batch of loads from L2) stand between the attention grid and the
-// arithmetic.  Block (0, 0) advances the lengths: every attention CTA of the
-// step has read them.
+// arithmetic.  Block (0, 0) advances the lengths: it reads them (and the
+// bias) before the wait -- the attention grid only reads them -- and writes
+// them after it, when every attention CTA of the step has read them.
 static constexpr int OUT_THREADS = 256;
 static constexpr int OUT_R = 8;                    // rows per block
 static constexpr int OUT_C = 32;                   // columns per block
@@ -530,8 +553,24 @@ __global__ void __launch_bounds__(OUT_THREADS) decode_out_kernel(DecodeOutArgs a
     for (int r = 0; r < OUT_R; r++)
 #pragma unroll
         for (int u = 0; u < 4; u++) acc[r][u] = 0.0f;
-    // W_o chunk 0 under the attention grid's tail
+    // W_o chunk 0, this thread's bias and (block (0, 0)) the lengths to
+    // advance, under the attention grid's tail: that grid reads the lengths
+    // and writes none of these
     out_stage_w(a, ws, 0, kc, c0);
+    const int ro = tid / OUT_C, co = tid % OUT_C;  // this thread's output in the epilogue
+    const float bias = c0 + co < E ? __ldg(a.bo + c0 + co) : 0.0f;
+    const bool len_block = blockIdx.x == 0 && blockIdx.y == 0;
+    int lslot = -1, lnew = 0;
+    if (len_block && n <= OUT_THREADS && tid < n) {
+        const int sl = a.slot ? a.slot[tid] : tid;
+        if (sl >= 0 && sl < a.n_slots) {
+            const int cur = a.len[sl];
+            if (cur < a.cap) {
+                lslot = sl;
+                lnew = cur + 1;
+            }
+        }
+    }
     ptx::griddep_wait();
     for (int kc0 = 0; kc0 < E; kc0 += kc) {
         const int kn = min(kc, E - kc0);
@@ -603,17 +642,21 @@ __global__ void __launch_bounds__(OUT_THREADS) decode_out_kernel(DecodeOutArgs a
             make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
     __syncthreads();
     {
-        const int r = tid / OUT_C, cc = tid % OUT_C;  // one output per thread
-        float v = 0.0f;
+        float v = 0.0f;  // one output per thread
 #pragma unroll 8
-        for (int q = 0; q < OUT_S; q++) v += red[(q * OUT_R + r) * OUT_C + cc];
-        if (r0 + r < n && c0 + cc < E) a.y[(long long)(r0 + r) * E + c0 + cc] = v + a.bo[c0 + cc];
+        for (int q = 0; q < OUT_S; q++) v += red[(q * OUT_R + ro) * OUT_C + co];
+        if (r0 + ro < n && c0 + co < E) a.y[(long long)(r0 + ro) * E + c0 + co] = v + bias;
     }
-    if (blockIdx.x == 0 && blockIdx.y == 0)
-        for (int i = tid; i < n; i += OUT_THREADS) {
-            const int slot = a.slot ? a.slot[i] : i;
-            if (slot >= 0 && slot < a.n_slots && a.len[slot] < a.cap) a.len[slot] += 1;
+    if (len_block) {
+        if (n <= OUT_THREADS) {
+            if (lslot >= 0) a.len[lslot] = lnew;
+        } else {
+            for (int i = tid; i < n; i += OUT_THREADS) {
+                const int slot = a.slot ? a.slot[i] : i;
+                if (slot >= 0 && slot < a.n_slots && a.len[slot] < a.cap) a.len[slot] += 1;
+            }
         }
+    }
 }
 
 int launch_decode_out(const float *o, const float *wo_t, const float *bo, float *y, int n, int E, int cap,
