@@ -108,6 +108,7 @@ struct wb_attn_layer {
     float *harmonic_n = nullptr; // [H]
     // SIMT layouts (transposed so threads read consecutive outputs)
     float *wrs_t = nullptr, *brs = nullptr;  // [E][H][2], [H][2]
+    float *wrs_h = nullptr;                  // [H][E][2]: one head's phase weights contiguous (decode)
     float *wc_t = nullptr, *bc = nullptr;    // [E][H*C], [H*C]
     float *wv_t = nullptr, *bv = nullptr;    // [H][hd][hd] (in, out), [H][hd]
     float *wo_t = nullptr, *bo = nullptr;    // [E][E] (in, out), [E]
@@ -279,6 +280,10 @@ int wb_attn_layer_create(wb_context *ctx, const wb_attn_weights_desc *w, wb_attn
             brs[h * 2 + c] = w->phase_proj_b[h * 2 + c];
             for (int j = 0; j < E; j++) wrs[((size_t)j * H + h) * 2 + c] = w->phase_proj_w[((size_t)h * 2 + c) * E + j];
         }
+    std::vector<float> wrs_h((size_t)H * E * 2);
+    for (int h = 0; h < H; h++)
+        for (int j = 0; j < E; j++)
+            for (int c = 0; c < 2; c++) wrs_h[((size_t)h * E + j) * 2 + c] = w->phase_proj_w[((size_t)h * 2 + c) * E + j];
     std::vector<float> wc, bc;
     if (C) {
         wc.resize((size_t)E * H * C);
@@ -304,6 +309,7 @@ int wb_attn_layer_create(wb_context *ctx, const wb_attn_weights_desc *w, wb_attn
     int rc = WB_OK;
     if (rc == WB_OK) rc = upload(&L->harmonic_n, L->hn_host);
     if (rc == WB_OK) rc = upload(&L->wrs_t, wrs);
+    if (rc == WB_OK) rc = upload(&L->wrs_h, wrs_h);
     if (rc == WB_OK) rc = upload(&L->brs, brs);
     if (rc == WB_OK) rc = upload(&L->wc_t, wc);
     if (rc == WB_OK) rc = upload(&L->bc, bc);
@@ -317,6 +323,7 @@ int wb_attn_layer_create(wb_context *ctx, const wb_attn_weights_desc *w, wb_attn
         L->tc.harmonic_n = L->harmonic_n;
         L->tc.b_o = L->bo;
         L->tc.wo_t = L->wo_t;
+        L->tc.wrs_h = L->wrs_h;
         rc = wb::tc_layer_upload(&L->tc, w, &msg);
         if (rc != WB_OK) fail(rc, msg);
     }
@@ -331,7 +338,7 @@ int wb_attn_layer_create(wb_context *ctx, const wb_attn_weights_desc *w, wb_attn
 int wb_attn_layer_destroy(wb_attn_layer *L) {
     if (!L) return WB_OK;
     DeviceGuard g(L->device);
-    float *ptrs[] = {L->harmonic_n, L->wrs_t, L->brs, L->wc_t, L->bc, L->wv_t, L->bv, L->wo_t, L->bo};
+    float *ptrs[] = {L->harmonic_n, L->wrs_t, L->wrs_h, L->brs, L->wc_t, L->bc, L->wv_t, L->bv, L->wo_t, L->bo};
     for (float *p : ptrs)
         if (p) cudaFree(p);
     wb::tc_layer_free(&L->tc);

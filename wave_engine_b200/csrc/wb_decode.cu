@@ -76,7 +76,7 @@ struct DecodeArgs {
     int32_t *len;             // [slots] cached positions (device truth)
     int cap, n_slots;
     const float *x;           // [n_seq][E]
-    const float *wrs_t, *brs; // phase projection [E][H][2], [H][2]
+    const float *wrs_h, *brs; // phase projection [H][E][2] (a head's weights contiguous), [H][2]
     const float *wv_t, *bv;   // value projection [H][hd(in)][hd(out)], [H][hd]
     const float *hn;          // [H]
     int n_seq, H, hd, E, nsplit;
@@ -136,9 +136,10 @@ __device__ __forceinline__ float decode_weight(float arg) {
 // x row -> shared memory and this thread's partial sums of the phase
 // projection (r, s) = W_rs x (kv_cache.rs:271): elements tid, tid + THREADS,
 // ... summed in that order, XU loads of x and of W_rs in flight per batch.
+// wrs_h: head h's (r, s) weight pairs, [E][2] (coalesced float2 loads).
 template <int XU, int THREADS>
-__device__ __forceinline__ void decode_x_phase(const float *xr, const float *wrs_t, int E, int H, int h, int tid,
-                                               float *xs, float &r, float &s, int jbeg = 0) {
+__device__ __forceinline__ void decode_x_phase(const float *xr, const float *wrs_h, int E, int tid, float *xs,
+                                               float &r, float &s, int jbeg = 0) {
     for (int j0 = jbeg; j0 < E; j0 += XU * THREADS) {
         float xv[XU];
         float2 wv2[XU];
@@ -146,8 +147,7 @@ __device__ __forceinline__ void decode_x_phase(const float *xr, const float *wrs
         for (int u = 0; u < XU; u++) {
             const int j = j0 + u * THREADS + tid;
             xv[u] = j < E ? __ldg(xr + j) : 0.0f;
-            wv2[u] = j < E ? __ldg(reinterpret_cast<const float2 *>(wrs_t + ((long long)j * H + h) * 2))
-                           : make_float2(0.f, 0.f);
+            wv2[u] = j < E ? __ldg(reinterpret_cast<const float2 *>(wrs_h) + j) : make_float2(0.f, 0.f);
         }
 #pragma unroll
         for (int u = 0; u < XU; u++) {
@@ -212,6 +212,7 @@ __global__ void __launch_bounds__(NW * 32, NW == 12 ? 3 : (NW == 8 ? 4 : 9)) dec
     // length arrives.
     constexpr bool ONE = NW > 4;
     const float *xr = a.x + (long long)i * E;
+    const float *wrs = a.wrs_h + (long long)h * E * 2;
     const int slot = a.sv.slot ? a.sv.slot[i] : i;
     // new value v = Wv x_h + b (kv_cache.rs:272-277): thread (vd, vq) sums
     // inputs [vq * kper, (vq + 1) * kper) of output vd, in input order
@@ -232,8 +233,7 @@ __global__ void __launch_bounds__(NW * 32, NW == 12 ? 3 : (NW == 8 ? 4 : 9)) dec
         for (int u = 0; u < XU; u++) {
             const int j = u * DEC_THREADS + tid;
             xv0[u] = j < E ? __ldg(xr + j) : 0.0f;
-            wv0[u] = j < E ? __ldg(reinterpret_cast<const float2 *>(a.wrs_t + ((long long)j * a.H + h) * 2))
-                           : make_float2(0.f, 0.f);
+            wv0[u] = j < E ? __ldg(reinterpret_cast<const float2 *>(wrs) + j) : make_float2(0.f, 0.f);
         }
         hn = __ldg(a.hn + h);
         br = __ldg(a.brs + h * 2);
@@ -280,7 +280,7 @@ __global__ void __launch_bounds__(NW * 32, NW == 12 ? 3 : (NW == 8 ? 4 : 9)) dec
             r = fmaf(wv0[u].x, xv0[u], r);
             s = fmaf(wv0[u].y, xv0[u], s);
         }
-        decode_x_phase<XU, DEC_THREADS>(xr, a.wrs_t, E, a.H, h, tid, xs, r, s, XU * DEC_THREADS);
+        decode_x_phase<XU, DEC_THREADS>(xr, wrs, E, tid, xs, r, s, XU * DEC_THREADS);
         thq = decode_theta_q<NW>(r, s, br, bs, red, warp, lane);  // barrier: xs visible too
         // the new value's partial sums (summed at the merge)
         if (vq < P) {
@@ -322,7 +322,7 @@ __global__ void __launch_bounds__(NW * 32, NW == 12 ? 3 : (NW == 8 ? 4 : 9)) dec
             kb[c] = k < n ? __ldg(bucket + k) : (uint8_t)0xFF;
             kth[c] = k < n ? __ldg(theta + k) : 0.0f;
         }
-        decode_x_phase<8, DEC_THREADS>(xr, a.wrs_t, E, a.H, h, tid, xs, r, s);
+        decode_x_phase<8, DEC_THREADS>(xr, wrs, E, tid, xs, r, s);
         __syncthreads();
         // split 0: the new value, weight loads in batches of 16 before use
         if (split == 0 && vq < P) {
@@ -748,7 +748,7 @@ int launch_decode_attn(const DecodeLaunch &L, void *scratch, size_t scratch_byte
     a.cap = L.cap;
     a.n_slots = L.n_slots;
     a.x = L.x;
-    a.wrs_t = L.wrs_t;
+    a.wrs_h = L.wrs_h;
     a.brs = L.brs;
     a.wv_t = L.wv_t;
     a.bv = L.bv;

@@ -10,7 +10,7 @@ struct DecodeLaunch {
     int32_t *len;
     int cap, n_slots;
     const float *x;
-    const float *wrs_t, *brs, *wv_t, *bv, *wo_t, *bo, *hn;
+    const float *wrs_h, *brs, *wv_t, *bv, *wo_t, *bo, *hn;  // wrs_h: [H][E][2]
     int n_seq, H, hd, E;
     int sm_count;
     uint32_t *dev_err;

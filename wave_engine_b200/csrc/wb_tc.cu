@@ -1091,7 +1091,7 @@ int tc_kv_decode(const TcLayerWeights &t, const WbSeqView &sv, int32_t *len, int
         *msg = "fast decode supports head_dim <= 128";
         return WB_ENOTSUP;
     }
-    DecodeLaunch L{sv, len, cap, n_slots, x, t.pw.wrs_t, t.pw.brs, t.pw.wv_t, t.pw.bv, t.wo_t, t.b_o, t.harmonic_n,
+    DecodeLaunch L{sv, len, cap, n_slots, x, t.wrs_h, t.pw.brs, t.pw.wv_t, t.pw.bv, t.wo_t, t.b_o, t.harmonic_n,
                    n_seq, t.H, t.hd, t.E, sm_count, dev_err};
     float *o = nullptr;
     int rc = launch_decode_attn(L, scratch, scratch_bytes, &o, st, msg);
