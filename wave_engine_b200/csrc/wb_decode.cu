@@ -207,9 +207,9 @@ __global__ void __launch_bounds__(NW * 32, NW == 12 ? 3 : (NW == 8 ? 4 : 9)) dec
     // the out_proj grid may launch and load its weights
     ptx::griddep_launch_dependents();
     // ONE: one split per (sequence, head) (decode_warps).  The slot load
-    // goes first and everything that does not depend on the cached state is
-    // in flight with it; theta_q is ready after one barrier, before the
-    // length arrives.
+    // goes first with the x row and phase weights; the length and key loads
+    // follow as soon as the slot arrives, then the remaining weights;
+    // theta_q is ready after one barrier, before the length arrives.
     constexpr bool ONE = NW > 4;
     const float *xr = a.x + (long long)i * E;
     const float *wrs = a.wrs_h + (long long)h * E * 2;
@@ -234,17 +234,6 @@ __global__ void __launch_bounds__(NW * 32, NW == 12 ? 3 : (NW == 8 ? 4 : 9)) dec
             const int j = u * DEC_THREADS + tid;
             xv0[u] = j < E ? __ldg(xr + j) : 0.0f;
             wv0[u] = j < E ? __ldg(reinterpret_cast<const float2 *>(wrs) + j) : make_float2(0.f, 0.f);
-        }
-        hn = __ldg(a.hn + h);
-        br = __ldg(a.brs + h * 2);
-        bs = __ldg(a.brs + h * 2 + 1);
-        if (vq == 0) vpar = __ldg(a.bv + h * hd + vd);
-        if (vearly && vq < P) {
-            const float *wv = a.wv_t + (long long)h * hd * hd + vd;
-            const int j0 = vq * kper;
-#pragma unroll
-            for (int u = 0; u < VN; u++)
-                wl0[u] = u < kper && j0 + u < hd ? __ldg(wv + (long long)(j0 + u) * hd) : 0.0f;
         }
     }
     if (slot < 0 || slot >= a.n_slots) {
@@ -271,6 +260,19 @@ __global__ void __launch_bounds__(NW * 32, NW == 12 ? 3 : (NW == 8 ? 4 : 9)) dec
             const int k = k0 + c * 32 + lane;
             kb[c] = k < a.sv.cap ? __ldg(bucket + k) : (uint8_t)0xFF;
             kth[c] = k < a.sv.cap ? __ldg(theta + k) : 0.0f;
+        }
+        // the weights needed after theta_q, behind the slot-dependent loads
+        // in the memory pipeline
+        hn = __ldg(a.hn + h);
+        br = __ldg(a.brs + h * 2);
+        bs = __ldg(a.brs + h * 2 + 1);
+        if (vq == 0) vpar = __ldg(a.bv + h * hd + vd);
+        if (vearly && vq < P) {
+            const float *wv = a.wv_t + (long long)h * hd * hd + vd;
+            const int j0 = vq * kper;
+#pragma unroll
+            for (int u = 0; u < VN; u++)
+                wl0[u] = u < kper && j0 + u < hd ? __ldg(wv + (long long)(j0 + u) * hd) : 0.0f;
         }
         // x row: the first batch (loaded above), then any further batches
 #pragma unroll
