@@ -314,6 +314,52 @@ def test_decode_graph_capture_replays_like_eager(ctx):
     assert ctx.take_device_error() == 0
 
 
+@pytest.mark.parametrize("L", [1, 2, 3])
+def test_chained_decode_matches_unchained(ctx, L):
+    """Back-to-back decode calls (layer after layer, step after step) launch
+    each attention grid as a programmatic dependent of the previous layer's
+    out_proj.  The same steps with a torch kernel between the calls (nothing
+    chains) give bitwise the same outputs and lengths; with one layer the
+    consecutive steps of that layer must not chain at all."""
+    import torch
+    import wave_engine_b200 as wb
+    H, E, T, B, steps = 12, 768, 300, 4, 5
+    layers = [wb.AttnLayer(ctx, wb.gaussian_block_attn(70 + l, H, E, 16)) for l in range(L)]
+    g = torch.Generator(device="cuda").manual_seed(5)
+    xp = torch.randn((L, B, T, E), generator=g, device="cuda")
+    xd = torch.randn((steps, L, B, E), generator=g, device="cuda")
+    ids = torch.tensor([2, 0, 3, 1], dtype=torch.int32, device="cuda")
+    caches = [wb.KvCache(L, H, 64, max_seqs=B, max_ctx=T + steps, ctx=ctx) for _ in range(2)]
+    yp = torch.empty((B, T, E), device="cuda")
+    for c in caches:
+        for l in range(L):
+            c.prefill(l, layers[l], xp[l], ids, out=yp)
+    ys = [torch.empty((steps, L, B, E), device="cuda") for _ in range(2)]
+    bump = torch.zeros(1, device="cuda")
+    for s in range(steps):
+        for l in range(L):
+            caches[0].forward_one(l, layers[l], xd[s, l], ids, out=ys[0][s, l])
+    for s in range(steps):
+        for l in range(L):
+            caches[1].forward_one(l, layers[l], xd[s, l], ids, out=ys[1][s, l])
+            bump.add_(1.0)
+    torch.cuda.synchronize()
+    assert torch.equal(ys[0], ys[1])
+    for l in range(L):
+        assert all(caches[0].n_cached(l, i) == T + steps for i in range(B))
+    assert ctx.take_device_error() == 0
+    # the last step against the oracle (tensor-path tolerance)
+    for l in range(L):
+        wp = wb.gaussian_block_attn(70 + l, H, E, 16).packed()
+        xs = xp[l].cpu().numpy()
+        for i in range(B):
+            _, st = oracle.kv_prefill(wp, xs[i], cap=T + steps)
+            for s in range(steps):
+                od = oracle.kv_decode(wp, xd[s, l, i].cpu().numpy(), st)
+            r = check(f"layer {l} seq {i}", ys[0][steps - 1, l, i].cpu().numpy(), od, TENSOR_TOL)
+            assert r.passed, str(r)
+
+
 def test_tensor_path_fallback_tiles_for_unbounded_scores(ctx):
     """Content weights 100x larger push |c_q|(max|c_k| - |c_q|)/4 past the
     fixed-shift bound; those query tiles are recomputed by the fp32 SIMT

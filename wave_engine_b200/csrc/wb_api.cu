@@ -131,6 +131,19 @@ struct wb_kv_cache {
     wb::Workspace dscratch;            // decode partials + tickets, sized for (S, cap), zeroed
     std::vector<int32_t> len_host;     // host mirror [L][S]
     bool len_stale = false;            // a call with device seq ids changed lengths on the device
+    // The last decode of this cache whose final kernel was the SIMT out_proj
+    // (which lets a programmatic dependent launch before it completes): its
+    // layer and stream, or -1.  The next tensor-path decode launches its
+    // attention grid as such a dependent only on the same stream and for
+    // another layer: that grid reads the layer's lengths and keys before it
+    // waits, and the out_proj of the same layer may still be writing them.
+    int out_layer = -1;
+    cudaStream_t out_stream = nullptr;
+    bool chain_ok(int layer, cudaStream_t st) const { return out_layer >= 0 && out_layer != layer && out_stream == st; }
+    void note_decode(int layer, cudaStream_t st, bool ends_with_out) {
+        out_layer = ends_with_out ? layer : -1;
+        out_stream = st;
+    }
     int refresh(cudaStream_t st) {
         if (!len_stale) return WB_OK;
         if (cudaStreamSynchronize(st) != cudaSuccess ||
@@ -791,11 +804,15 @@ int wb_kv_decode(wb_context *ctx, wb_kv_cache *c, int layer_idx, const wb_attn_l
         wb::OutMap om{wb::OUT_DENSE, yd, E, sv, 0, 1};
         wb::launch_seqdot(o, n_seq, E, E, L->wo_t, E, L->bo, 0, om, st);
         wb::launch_len_update(len_l, ids_d, n_seq, 1, 0, c->S, c->cap, st);
+        c->note_decode(layer_idx, st, false);
         WB_CUDA(cudaGetLastError());
     } else {
         std::string msg;
+        bool ends_with_out = false;
         int rc = wb::tc_kv_decode(L->tc, sv, len_l, c->cap, c->S, xd, n_seq, yd, c->dscratch.p, c->dscratch.n,
-                                  ctx->dev_err, ctx->sm_count, st, &msg);
+                                  ctx->dev_err, ctx->sm_count, st, &msg, c->chain_ok(layer_idx, st),
+                                  &ends_with_out);
+        c->note_decode(layer_idx, st, ends_with_out);
         if (rc != WB_OK) return fail(rc, msg);
     }
     if (ids_dev) c->len_stale = true;
@@ -901,8 +918,11 @@ extern "C" int wb_kv_decode_noalloc(wb_context *ctx, wb_kv_cache *c, int layer_i
     WB_CUDA(cudaMemsetAsync((char *)scratch + t_off, 0, t_bytes, st));
     WbSeqView sv = c->view(layer_idx, seq_ids);
     std::string msg;
+    bool ends_with_out = false;
     int rc = wb::tc_kv_decode(L->tc, sv, c->len + (size_t)layer_idx * c->S, c->cap, c->S, x, n_seq, y, scratch,
-                              WB_NOALLOC_SCRATCH_BYTES, ctx->dev_err, ctx->sm_count, st, &msg);
+                              WB_NOALLOC_SCRATCH_BYTES, ctx->dev_err, ctx->sm_count, st, &msg, false,
+                              &ends_with_out);
+    c->note_decode(layer_idx, st, ends_with_out);
     if (rc != WB_OK) return fail(rc, msg);
     c->len_stale = true;
     return WB_OK;

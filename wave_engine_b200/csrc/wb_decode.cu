@@ -206,9 +206,15 @@ __global__ void __launch_bounds__(NW * 32, NW == 12 ? 3 : (NW == 8 ? 4 : 9)) dec
 
     // the out_proj grid may launch and load its weights
     ptx::griddep_launch_dependents();
+    // With DecodeLaunch::chain this grid is a programmatic dependent of the
+    // kernel before it in the stream -- the out_proj of another layer or
+    // cache, which lets it launch once the attention grid before that is
+    // complete: the slot, length, cached keys and weights, which that
+    // out_proj does not write, are loaded before griddepcontrol.wait; x,
+    // and every write, after it (without chain the wait returns at once).
     // ONE: one split per (sequence, head) (decode_warps).  The slot load
-    // goes first with the x row and phase weights; the length and key loads
-    // follow as soon as the slot arrives, then the remaining weights;
+    // goes first with the phase weights; the length and key loads follow as
+    // soon as the slot arrives, then the remaining weights, then x;
     // theta_q is ready after one barrier, before the length arrives.
     constexpr bool ONE = NW > 4;
     const float *xr = a.x + (long long)i * E;
@@ -232,7 +238,6 @@ __global__ void __launch_bounds__(NW * 32, NW == 12 ? 3 : (NW == 8 ? 4 : 9)) dec
 #pragma unroll
         for (int u = 0; u < XU; u++) {
             const int j = u * DEC_THREADS + tid;
-            xv0[u] = j < E ? __ldg(xr + j) : 0.0f;
             wv0[u] = j < E ? __ldg(reinterpret_cast<const float2 *>(wrs) + j) : make_float2(0.f, 0.f);
         }
     }
@@ -274,7 +279,14 @@ __global__ void __launch_bounds__(NW * 32, NW == 12 ? 3 : (NW == 8 ? 4 : 9)) dec
             for (int u = 0; u < VN; u++)
                 wl0[u] = u < kper && j0 + u < hd ? __ldg(wv + (long long)(j0 + u) * hd) : 0.0f;
         }
-        // x row: the first batch (loaded above), then any further batches
+        // x (and every write of this kernel) waits for the grid before
+        ptx::griddep_wait();
+#pragma unroll
+        for (int u = 0; u < XU; u++) {
+            const int j = u * DEC_THREADS + tid;
+            xv0[u] = j < E ? __ldg(xr + j) : 0.0f;
+        }
+        // x row: the first batch, then any further batches
 #pragma unroll
         for (int u = 0; u < XU; u++) {
             const int j = u * DEC_THREADS + tid;
@@ -324,6 +336,7 @@ __global__ void __launch_bounds__(NW * 32, NW == 12 ? 3 : (NW == 8 ? 4 : 9)) dec
             kb[c] = k < n ? __ldg(bucket + k) : (uint8_t)0xFF;
             kth[c] = k < n ? __ldg(theta + k) : 0.0f;
         }
+        ptx::griddep_wait();  // x (and every write) waits for the grid before
         decode_x_phase<8, DEC_THREADS>(xr, wrs, E, tid, xs, r, s);
         __syncthreads();
         // split 0: the new value, weight loads in batches of 16 before use
@@ -574,6 +587,10 @@ __global__ void __launch_bounds__(OUT_THREADS) decode_out_kernel(DecodeOutArgs a
         }
     }
     ptx::griddep_wait();
+    // the attention grid is complete, and with it (by the same wait in every
+    // grid of the chain) all earlier work of the stream: the next layer's
+    // attention grid may launch and load its slot, length and keys
+    ptx::griddep_launch_dependents();
     for (int kc0 = 0; kc0 < E; kc0 += kc) {
         const int kn = min(kc, E - kc0);
         if (kc0 > 0) {
@@ -705,19 +722,19 @@ void decode_scratch_tickets(int n_seq, int H, int hd, int E, int cap, size_t *of
 }
 
 template <int VEC, int NW>
-static cudaError_t launch_attn(const DecodeArgs &a, dim3 grid, cudaStream_t st) {
+static cudaError_t launch_attn(const DecodeArgs &a, dim3 grid, cudaStream_t st, bool chain) {
     const size_t smem = sizeof(float) * ((size_t)a.E + 2 * NW * DEC_KEYS_PER_WARP + NW * a.hd + NW + 2 * NW +
                                          NW * 32);
     cudaFuncSetAttribute(decode_attn_kernel<VEC, NW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    decode_attn_kernel<VEC, NW><<<grid, NW * 32, smem, st>>>(a);
-    return cudaGetLastError();
+    cudaError_t e = launch_ex(decode_attn_kernel<VEC, NW>, grid, dim3(NW * 32), smem, st, chain, a);
+    return e == cudaSuccess ? cudaGetLastError() : e;
 }
 
 template <int VEC>
-static cudaError_t launch_attn_nw(const DecodeArgs &a, int nw, dim3 grid, cudaStream_t st) {
-    if (nw == 12) return launch_attn<VEC, 12>(a, grid, st);
-    if (nw == 8) return launch_attn<VEC, 8>(a, grid, st);
-    return launch_attn<VEC, 4>(a, grid, st);
+static cudaError_t launch_attn_nw(const DecodeArgs &a, int nw, dim3 grid, cudaStream_t st, bool chain) {
+    if (nw == 12) return launch_attn<VEC, 12>(a, grid, st, chain);
+    if (nw == 8) return launch_attn<VEC, 8>(a, grid, st, chain);
+    return launch_attn<VEC, 4>(a, grid, st, chain);
 }
 
 int launch_decode_attn(const DecodeLaunch &L, void *scratch, size_t scratch_bytes, float **o_out,
@@ -770,9 +787,9 @@ int launch_decode_attn(const DecodeLaunch &L, void *scratch, size_t scratch_byte
     cudaError_t e;
     {
         ProfScope ps("decode_attn", st);
-        if (L.hd % 4 == 0) e = launch_attn_nw<4>(a, nw, grid, st);
-        else if (L.hd % 2 == 0) e = launch_attn_nw<2>(a, nw, grid, st);
-        else e = launch_attn_nw<1>(a, nw, grid, st);
+        if (L.hd % 4 == 0) e = launch_attn_nw<4>(a, nw, grid, st, L.chain);
+        else if (L.hd % 2 == 0) e = launch_attn_nw<2>(a, nw, grid, st, L.chain);
+        else e = launch_attn_nw<1>(a, nw, grid, st, L.chain);
     }
     if (e != cudaSuccess) {
         *msg = std::string("decode launch failed: ") + cudaGetErrorString(e);

@@ -14,6 +14,10 @@ struct DecodeLaunch {
     int n_seq, H, hd, E;
     int sm_count;
     uint32_t *dev_err;
+    // launch the attention grid as a programmatic dependent of the previous
+    // kernel in the stream; only when that kernel, if it is this library's
+    // decode out_proj, served another layer or cache (see tc_kv_decode)
+    bool chain;
 };
 
 // Scratch bytes the decode attention kernel needs for n_seq sequences; the

@@ -1086,13 +1086,14 @@ static int decode_gemm_min_rows() { return kDecodeGemmMinRows; }
 
 int tc_kv_decode(const TcLayerWeights &t, const WbSeqView &sv, int32_t *len, int cap, int n_slots, const float *x,
                  int n_seq, float *y, void *scratch, size_t scratch_bytes, uint32_t *dev_err, int sm_count,
-                 cudaStream_t st, std::string *msg) {
+                 cudaStream_t st, std::string *msg, bool chain, bool *ends_with_out) {
+    if (ends_with_out) *ends_with_out = false;
     if (t.hd > 128) {
         *msg = "fast decode supports head_dim <= 128";
         return WB_ENOTSUP;
     }
     DecodeLaunch L{sv, len, cap, n_slots, x, t.wrs_h, t.pw.brs, t.pw.wv_t, t.pw.bv, t.wo_t, t.b_o, t.harmonic_n,
-                   n_seq, t.H, t.hd, t.E, sm_count, dev_err};
+                   n_seq, t.H, t.hd, t.E, sm_count, dev_err, chain};
     float *o = nullptr;
     int rc = launch_decode_attn(L, scratch, scratch_bytes, &o, st, msg);
     if (rc) return rc;
@@ -1103,7 +1104,9 @@ int tc_kv_decode(const TcLayerWeights &t, const WbSeqView &sv, int32_t *len, int
     }
     // few rows: the SIMT out_proj kernel (programmatic dependent of the
     // attention grid), which also advances the lengths
-    return launch_decode_out(o, t.wo_t, t.b_o, y, n_seq, t.E, cap, len, sv.slot, n_slots, st, msg);
+    rc = launch_decode_out(o, t.wo_t, t.b_o, y, n_seq, t.E, cap, len, sv.slot, n_slots, st, msg);
+    if (rc == WB_OK && ends_with_out) *ends_with_out = true;
+    return rc;
 }
 
 }  // namespace wb

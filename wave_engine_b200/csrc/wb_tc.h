@@ -41,8 +41,12 @@ int tc_gemm_tf32(const float *A, const float *B, const float *bias, float *C, in
 // with the new position appended, then out_proj and the length update;
 // scratch (the cache's, fixed size, tickets zero) holds the attention
 // kernel's partials.
+// chain: the attention grid may launch as a programmatic dependent of the
+// kernel before it (allowed unless that kernel is the decode out_proj of
+// the same cache layer); *ends_with_out: the step's last kernel is the SIMT
+// decode out_proj (fewer than 64 rows), which lets such a dependent launch.
 int tc_kv_decode(const TcLayerWeights &t, const WbSeqView &sv, int32_t *len, int cap, int n_slots, const float *x,
                  int n_seq, float *y, void *scratch, size_t scratch_bytes, uint32_t *dev_err, int sm_count,
-                 cudaStream_t st, std::string *msg);
+                 cudaStream_t st, std::string *msg, bool chain = false, bool *ends_with_out = nullptr);
 
 }  // namespace wb
