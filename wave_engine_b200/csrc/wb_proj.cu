@@ -335,6 +335,208 @@ __global__ void __launch_bounds__(PH_THREADS, 3) phase_fma_kernel(const float *_
 }
 
 // ---------------------------------------------------------------------------
+// Values and phases in one fp32 pass over x, for head_dim 48 or 64 and at
+// most 16 heads computed -- the serve models.  The value
+// projection of a head is a 64x64 block on that head's 64 inputs
+// (attn.rs:155-165): too little work per row for a tensor-core tile to pay
+// for its pipeline, and exact in fp32 here.  CTA = 64 rows, 256 threads; the
+// x columns are walked in rounds of two heads' inputs (128 columns), x
+// staged transposed ([column][row]) in shared memory, the next round's x in
+// registers and its weights in flight (cp.async) while the current round is
+// used:
+//   values: thread (head of the pair, 4 rows, 8 outputs), one sequential
+//     fmaf sum per output over the head's inputs, + b (attn.rs:160-163);
+//   phases: thread (2 rows, 4 of the 2H outputs = 2 whole (r, s) pairs),
+//     b + the sequential fmaf sum over all E inputs, round after round in
+//     input order -- the same order as phase_fma_kernel -- then atan2f and
+//     the bucket.
+// ---------------------------------------------------------------------------
+static constexpr int VP_ROWS = 64, VP_THREADS = 256;
+static constexpr int VP_KCH = 128;  // x columns per round (two heads of <= 64)
+static constexpr int VP_XS = 68;    // floats per staged x column (64 rows + pad; 16-byte aligned)
+static constexpr int VP_OPT = 4;    // phase outputs per thread
+static constexpr int VP_NOP = 8 * VP_OPT;
+static constexpr int VP_SMEM = (2 * VP_KCH * VP_XS + 2 * 2 * 64 * 64 + 2 * VP_KCH * VP_NOP) * 4;
+
+struct VpArgs {
+    const float *x;            // [R][E]
+    const float *wv_t, *bv;    // [H][hd(in)][hd(out)], [H][hd]
+    const float *wrs_t, *brs;  // [E][H][2], [H][2]
+    int R, E, H, T, h0, Hg;
+    WbSeqView sv;
+};
+
+// HD: head_dim (48 or 64).  Thread (value role) outputs d = 4*dg + j and
+// 32 + 4*dg + j (j < 4): each of its two float4 weight loads and stores
+// covers 128 contiguous bytes across the 8 lanes of one row.
+template <int HD>
+__global__ void __launch_bounds__(VP_THREADS, 1) vproj_phase_kernel(VpArgs a) {
+    static_assert(HD % 4 == 0 && HD <= 64 && HD > 32, "value tiling assumes 32 < head_dim <= 64");
+    extern __shared__ __align__(16) float vsm[];
+    float *xs = vsm;                          // [2][KCH][XS]
+    float *wsv = xs + 2 * VP_KCH * VP_XS;     // [2][2 heads][64 in][64 out]
+    float *wrs = wsv + 2 * 2 * 64 * 64;       // [2][KCH][NOP]
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int m0 = blockIdx.x * VP_ROWS;
+    const int E = a.E, H = a.H, NO = 2 * a.Hg;
+    const int n_rounds = (H + 1) / 2;
+    // value role: head 2p + hl, rows rg*4 .. +3, outputs 4*dg + j and 32 + 4*dg + j
+    const int hl = tid >> 7, tq = tid & 127, rg = tq >> 3, dg = tq & 7;
+    const bool hi_ok = 32 + 4 * dg < HD;  // the second output quad exists
+    // phase role: rows 2*rp, 2*rp + 1, outputs g*OPT .. +OPT-1
+    const int rp = lane, g = warp;
+    // cache offsets (slot * seq_stride + t) of this thread's rows
+    long long vrow[4], prow[2];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int row = m0 + rg * 4 + i;
+        const int b = row < a.R ? row / a.T : 0, t = row - b * a.T;
+        vrow[i] = row < a.R ? (long long)(a.sv.slot ? a.sv.slot[b] : b) * a.sv.seq_stride + t : -1;
+    }
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+        const int row = m0 + 2 * rp + i;
+        const int b = row < a.R ? row / a.T : 0, t = row - b * a.T;
+        prow[i] = row < a.R ? (long long)(a.sv.slot ? a.sv.slot[b] : b) * a.sv.seq_stride + t : -1;
+    }
+    float ph[2][VP_OPT];
+#pragma unroll
+    for (int q = 0; q < VP_OPT; q++) {
+        const int o = g * VP_OPT + q;
+        const float b = o < NO ? __ldg(a.brs + 2 * a.h0 + o) : 0.0f;
+        ph[0][q] = b;
+        ph[1][q] = b;
+    }
+    // x: warp-instruction wi covers rows (wi & 7)*8 .. +7 and column quads
+    // (wi >> 3)*4 .. +3 (64 contiguous bytes per row)
+    float4 xr[8];
+    auto load_x = [&](int p) {
+        const int c0 = 2 * p * HD, kc = min(2, H - 2 * p) * HD;
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            const int wi = warp + 8 * u;
+            const int r = (wi & 7) * 8 + (lane >> 2), k = ((wi >> 3) * 4 + (lane & 3)) * 4;
+            const int row = m0 + r;
+            xr[u] = (k < kc && row < a.R) ? __ldg(reinterpret_cast<const float4 *>(a.x + (long long)row * E + c0 + k))
+                                          : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    };
+    auto store_x = [&](int buf, int p) {
+        const int kc = min(2, H - 2 * p) * HD;
+        float *d = xs + buf * VP_KCH * VP_XS;
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            const int wi = warp + 8 * u;
+            const int r = (wi & 7) * 8 + (lane >> 2), k = ((wi >> 3) * 4 + (lane & 3)) * 4;
+            if (k < kc) {
+                d[(k + 0) * VP_XS + r] = xr[u].x;
+                d[(k + 1) * VP_XS + r] = xr[u].y;
+                d[(k + 2) * VP_XS + r] = xr[u].z;
+                d[(k + 3) * VP_XS + r] = xr[u].w;
+            }
+        }
+    };
+    auto load_w = [&](int buf, int p) {
+        constexpr int Q4 = HD / 4, PER_HEAD = HD * Q4;  // float4 per weight row / per head
+        const int c0 = 2 * p * HD, nh = min(2, H - 2 * p), kc = nh * HD;
+        float *wv = wsv + buf * 2 * 64 * 64;
+        for (int e = tid; e < nh * PER_HEAD; e += VP_THREADS) {
+            const int hh = e / PER_HEAD, rem = e - hh * PER_HEAD, k = rem / Q4, dq = rem - k * Q4;
+            ptx::cp_async<16>(wv + (hh * 64 + k) * 64 + dq * 4, a.wv_t + ((long long)(2 * p + hh) * HD + k) * HD + dq * 4);
+        }
+        // phase weights: column o = lane (o < 2*Hg <= 32), rows k = warp, warp + 8, ...
+        float *wr = wrs + buf * VP_KCH * VP_NOP;
+        if (lane < NO)
+            for (int k = warp; k < kc; k += VP_THREADS / 32)
+                ptx::cp_async<4>(wr + k * VP_NOP + lane, a.wrs_t + (long long)(c0 + k) * 2 * H + 2 * a.h0 + lane);
+        ptx::cp_async_commit();
+    };
+    load_x(0);
+    store_x(0, 0);
+    load_w(0, 0);
+    for (int p = 0; p < n_rounds; p++) {
+        const int buf = p & 1;
+        ptx::cp_async_wait<0>();
+        __syncthreads();  // round p staged; the buffers of round p - 1 are free
+        const bool more = p + 1 < n_rounds;
+        if (more) {
+            load_x(p + 1);
+            load_w(buf ^ 1, p + 1);
+        }
+        const float *xb = xs + buf * VP_KCH * VP_XS;
+        {  // phases: this round's inputs, in order
+            const int kc = min(2, H - 2 * p) * HD;
+            const float *wr = wrs + buf * VP_KCH * VP_NOP + g * VP_OPT;
+            if (g * VP_OPT < NO)
+#pragma unroll 4
+                for (int k = 0; k < kc; k++) {
+                    const float2 xv = *reinterpret_cast<const float2 *>(xb + k * VP_XS + 2 * rp);
+                    const float4 w = *reinterpret_cast<const float4 *>(wr + k * VP_NOP);
+                    ph[0][0] = fmaf(w.x, xv.x, ph[0][0]);
+                    ph[0][1] = fmaf(w.y, xv.x, ph[0][1]);
+                    ph[0][2] = fmaf(w.z, xv.x, ph[0][2]);
+                    ph[0][3] = fmaf(w.w, xv.x, ph[0][3]);
+                    ph[1][0] = fmaf(w.x, xv.y, ph[1][0]);
+                    ph[1][1] = fmaf(w.y, xv.y, ph[1][1]);
+                    ph[1][2] = fmaf(w.z, xv.y, ph[1][2]);
+                    ph[1][3] = fmaf(w.w, xv.y, ph[1][3]);
+                }
+        }
+        const int h = 2 * p + hl;
+        if (h < H && h >= a.h0 && h < a.h0 + a.Hg) {  // values of head h
+            float acc[4][8];
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int j = 0; j < 8; j++) acc[i][j] = 0.0f;
+            const float *xh = xb + hl * HD * VP_XS + rg * 4;
+            const float *wh = wsv + buf * 2 * 64 * 64 + hl * 64 * 64 + 4 * dg;
+#pragma unroll 4
+            for (int k = 0; k < HD; k++) {
+                const float4 xv = *reinterpret_cast<const float4 *>(xh + k * VP_XS);
+                const float4 w0 = *reinterpret_cast<const float4 *>(wh + k * 64);
+                const float4 w1 = *reinterpret_cast<const float4 *>(wh + k * 64 + 32);
+                const float xi[4] = {xv.x, xv.y, xv.z, xv.w};
+                const float wj[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+                for (int i = 0; i < 4; i++)
+#pragma unroll
+                    for (int j = 0; j < 8; j++) acc[i][j] = fmaf(wj[j], xi[i], acc[i][j]);
+            }
+            const float4 b0 = __ldg(reinterpret_cast<const float4 *>(a.bv + h * HD + 4 * dg));
+            const float4 b1 = hi_ok ? __ldg(reinterpret_cast<const float4 *>(a.bv + h * HD + 32 + 4 * dg))
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+            const long long hoff = (long long)h * a.sv.cap;
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                if (vrow[i] < 0) continue;
+                float *dst = a.sv.v + (vrow[i] + hoff) * HD + 4 * dg;
+                *reinterpret_cast<float4 *>(dst) =
+                    make_float4(acc[i][0] + b0.x, acc[i][1] + b0.y, acc[i][2] + b0.z, acc[i][3] + b0.w);
+                if (hi_ok)
+                    *reinterpret_cast<float4 *>(dst + 32) =
+                        make_float4(acc[i][4] + b1.x, acc[i][5] + b1.y, acc[i][6] + b1.z, acc[i][7] + b1.w);
+            }
+        }
+        if (more) store_x(buf ^ 1, p + 1);
+    }
+#pragma unroll
+    for (int rr = 0; rr < 2; rr++) {
+        if (prow[rr] < 0) continue;
+#pragma unroll
+        for (int q = 0; q < VP_OPT; q += 2) {
+            const int hl2 = (g * VP_OPT + q) / 2;
+            if (hl2 >= a.Hg) break;
+            const int h = a.h0 + hl2;
+            const float th = atan2f(ph[rr][q + 1], ph[rr][q]);
+            const long long pos = prow[rr] + (long long)h * a.sv.cap;
+            a.sv.theta[pos] = th;
+            a.sv.bucket[pos] = (uint8_t)phase_to_bucket(th);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
 static PFN_cuTensorMapEncodeTiled_v12000 proj_encode_fn() {
@@ -440,11 +642,33 @@ void proj_weights_free(ProjTcWeights *p) {
     p->w_hi = p->w_lo = p->bias = nullptr;
 }
 
-int launch_proj_tc(const ProjTcWeights &p, const float *wrs_t, const float *brs, const float *x, int B, int T,
-                   const WbSeqView &sv, float *content, int h0, int Hg, uint32_t *dev_err, cudaStream_t st,
-                   std::string *msg) {
+int launch_proj_tc(const ProjTcWeights &p, const float *wrs_t, const float *brs, const float *wv_t, const float *bv,
+                   const float *x, int B, int T, const WbSeqView &sv, float *content, int h0, int Hg,
+                   uint32_t *dev_err, cudaStream_t st, std::string *msg) {
     const long long R = (long long)B * T;
     if (R <= 0) return WB_OK;
+    const bool simt_v = wv_t && bv && (p.hd == 64 || p.hd == 48) && Hg <= 16 && R <= INT32_MAX &&
+                        (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(bv) & 15) == 0;
+    if (simt_v) {
+        // values and phases in one fp32 pass; the GEMM below keeps only the
+        // content columns (if any)
+        VpArgs va{x, wv_t, bv, wrs_t, brs, (int)R, p.E, p.H, T, h0, Hg, sv};
+        ProfScope ps("proj_vphase", st);
+        const unsigned grid = (unsigned)((R + VP_ROWS - 1) / VP_ROWS);
+        if (p.hd == 64) {
+            cudaFuncSetAttribute(vproj_phase_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, VP_SMEM);
+            vproj_phase_kernel<64><<<grid, VP_THREADS, VP_SMEM, st>>>(va);
+        } else {
+            cudaFuncSetAttribute(vproj_phase_kernel<48>, cudaFuncAttributeMaxDynamicSharedMemorySize, VP_SMEM);
+            vproj_phase_kernel<48><<<grid, VP_THREADS, VP_SMEM, st>>>(va);
+        }
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) {
+            *msg = std::string("projection launch failed: ") + cudaGetErrorString(e);
+            return WB_ECUDA;
+        }
+        if (!content) return WB_OK;
+    }
     if ((p.E * 4) % 16) {
         *msg = "n_embd must be a multiple of 4 for the tensor projections";
         return WB_ENOTSUP;
@@ -460,7 +684,8 @@ int launch_proj_tc(const ProjTcWeights &p, const float *wrs_t, const float *brs,
     }
     // GEMM over the value and content columns only (phases below)
     const int n_gemm = p.n_v + p.n_c;
-    const int v0 = h0 * p.hd, v1 = (h0 + Hg) * p.hd, c0 = p.n_v + h0 * p.C, c1 = p.n_v + (h0 + Hg) * p.C;
+    const int v0 = h0 * p.hd, v1 = simt_v ? v0 : (h0 + Hg) * p.hd, c0 = p.n_v + h0 * p.C,
+              c1 = p.n_v + (h0 + Hg) * p.C;
     ProjArgs a{(int)R, p.E, p.H, p.hd, p.C, T, p.n_v, p.n_c, p.n_rs, n_gemm, v0, v1, c0, c1, p.bias, sv, content,
                dev_err};
     const int n_tiles = (v1 - v0 + PBN - 1) / PBN + (content ? (c1 - c0 + PBN - 1) / PBN : 0);
@@ -470,7 +695,7 @@ int launch_proj_tc(const ProjTcWeights &p, const float *wrs_t, const float *brs,
         cudaFuncSetAttribute(proj_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM);
         proj_tc_kernel<<<grid, 128, P_SMEM, st>>>(tx, th, tl, a);
     }
-    {
+    if (!simt_v) {
         ProfScope pp("phase_fma", st);
         const unsigned pg = (unsigned)((R + PH_ROWS - 1) / PH_ROWS);
         if (Hg <= 12)

@@ -1046,7 +1046,7 @@ int tc_attn_forward(const TcLayerWeights &t, const float *x, int B, int T, bool 
     sv.slot = nullptr;
     float *content = use_content ? (float *)(w + o_ct) : nullptr;
     (void)o_rs;
-    int rc = launch_proj_tc(t.proj, t.pw.wrs_t, t.pw.brs, x, B, T, sv, content, h0, Hg, dev_err, st, msg);
+    int rc = launch_proj_tc(t.proj, t.pw.wrs_t, t.pw.brs, t.pw.wv_t, t.pw.bv, x, B, T, sv, content, h0, Hg, dev_err, st, msg);
     if (rc) return rc;
     rc = tc_attention_core(t, sv, content, B, T, h0, Hg, add_bias, y, ws, lay, dev_err, st, msg);
     if (rc) return rc;
@@ -1071,7 +1071,7 @@ int tc_kv_prefill(const TcLayerWeights &t, const WbSeqView &sv, const float *x, 
     const CoreLayout lay = core_layout(t, n_seq, T, cv.off, t.H);
     if (ws_ensure(ws, lay.end, msg)) return WB_ENOMEM;
     (void)o_rs;
-    int rc = launch_proj_tc(t.proj, t.pw.wrs_t, t.pw.brs, x, n_seq, T, sv, nullptr, 0, t.H, dev_err, st, msg);
+    int rc = launch_proj_tc(t.proj, t.pw.wrs_t, t.pw.brs, t.pw.wv_t, t.pw.bv, x, n_seq, T, sv, nullptr, 0, t.H, dev_err, st, msg);
     if (rc) return rc;
     return tc_attention_core(t, sv, nullptr, n_seq, T, 0, t.H, true, y, ws, lay, dev_err, st, msg);
 }
