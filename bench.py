@@ -381,11 +381,13 @@ def run_ours(args):
 
     # end to end through the public API: every step copies all of its inputs
     # from pinned host memory and all of its outputs back, inside the timed
-    # region.  Inputs go up and outputs come down on a copy stream, a layer
-    # (prefill) or a chunk of 16 steps (decode) ahead of / behind the compute,
-    # which is what a serving loop feeding the library does; the compute is the
-    # same public calls (prefill per layer, the captured forward_one graph per
-    # decode step).
+    # region, the way a serving loop feeds the library: inputs go up on one
+    # copy stream into one of two device buffer sets (the next step's inputs
+    # travel while the current step computes), outputs come down on another
+    # a layer (prefill) or a chunk of 16 steps (decode) behind the compute.
+    # The compute is the same public calls (prefill per layer, the captured
+    # forward_one graph per decode step).  The first timed step's inputs are
+    # copied inside the timed region with nothing to hide behind.
     e2e = None
     e2e_sync = None
     if not args.no_e2e:
@@ -393,55 +395,76 @@ def run_ours(args):
         xd_h = x_dec.cpu().pin_memory()
         yp_h = torch.empty((L, B, T, E)).pin_memory()
         yd_h = torch.empty((S, L, B, E)).pin_memory()
-        xp_d = torch.empty_like(x_pre)
-        xd_d = torch.empty_like(x_dec)
-        yp_d = torch.empty((L, B, T, E), device=dev)
-        yd_d = torch.empty((S, L, B, E), device=dev)
-        copy = torch.cuda.Stream(dev)
-        ev_in = [torch.cuda.Event() for _ in range(L)]
-        ev_out = [torch.cuda.Event() for _ in range(L)]
+        xp_d = [torch.empty_like(x_pre) for _ in range(2)]
+        xd_d = [torch.empty_like(x_dec) for _ in range(2)]
+        yp_d = [torch.empty((L, B, T, E), device=dev) for _ in range(2)]
+        yd_d = [torch.empty((S, L, B, E), device=dev) for _ in range(2)]
+        c_in, c_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
         DCH = 16                                   # decode steps per copy chunk
         chunks = [(c, min(S, c + DCH)) for c in range(0, S, DCH)]
-        ev_dec = [torch.cuda.Event() for _ in chunks]
+        ev_in = [[torch.cuda.Event() for _ in range(L)] for _ in range(2)]
+        ev_dec = [[torch.cuda.Event() for _ in chunks] for _ in range(2)]
+        ev_out = [torch.cuda.Event() for _ in range(L)]
         ev_done = [torch.cuda.Event() for _ in chunks]
+        ev_in_free = [torch.cuda.Event() for _ in range(2)]   # compute done with input set
+        ev_out_free = [torch.cuda.Event() for _ in range(2)]  # copies done with output set
         n_e2e = max(1, min(args.steps, args.e2e_steps))
 
-        def step_e2e():
-            copy.wait_stream(stream)
-            with torch.cuda.stream(copy):
+        def inputs(k):
+            j = k % 2
+            if k >= 2:
+                c_in.wait_event(ev_in_free[j])
+            with torch.cuda.stream(c_in):
                 for l in range(L):
-                    xp_d[l].copy_(xp_h[l], non_blocking=True)
-                    ev_in[l].record(copy)
+                    xp_d[j][l].copy_(xp_h[l], non_blocking=True)
+                    ev_in[j][l].record(c_in)
                 for i, (a, b) in enumerate(chunks):
-                    xd_d[a:b].copy_(xd_h[a:b], non_blocking=True)
-                    ev_dec[i].record(copy)
+                    xd_d[j][a:b].copy_(xd_h[a:b], non_blocking=True)
+                    ev_dec[j][i].record(c_in)
+
+        def compute(k):
+            j = k % 2
+            if k >= 2:
+                stream.wait_event(ev_out_free[j])
             cache.reset()
             for l in range(L):
-                stream.wait_event(ev_in[l])
-                cache.prefill(l, layers[l], xp_d[l], ids_dev, out=yp_d[l])
+                stream.wait_event(ev_in[j][l])
+                cache.prefill(l, layers[l], xp_d[j][l], ids_dev, out=yp_d[j][l])
                 ev_out[l].record(stream)
-            with torch.cuda.stream(copy):
-                for l in range(L):
-                    copy.wait_event(ev_out[l])
-                    yp_h[l].copy_(yp_d[l], non_blocking=True)
+                c_out.wait_event(ev_out[l])
+                with torch.cuda.stream(c_out):
+                    yp_h[l].copy_(yp_d[j][l], non_blocking=True)
             for i, (a, b) in enumerate(chunks):
-                stream.wait_event(ev_dec[i])
+                stream.wait_event(ev_dec[j][i])
                 for s in range(a, b):
-                    x_stage.copy_(xd_d[s])
+                    x_stage.copy_(xd_d[j][s])
                     graph.replay()
-                    yd_d[s].copy_(y_stage)
+                    yd_d[j][s].copy_(y_stage)
                 ev_done[i].record(stream)
-                with torch.cuda.stream(copy):
-                    copy.wait_event(ev_done[i])
-                    yd_h[a:b].copy_(yd_d[a:b], non_blocking=True)
-            stream.wait_stream(copy)
+                c_out.wait_event(ev_done[i])
+                with torch.cuda.stream(c_out):
+                    yd_h[a:b].copy_(yd_d[j][a:b], non_blocking=True)
+            ev_in_free[j].record(stream)
+            ev_out_free[j].record(c_out)
 
-        step_e2e()
+        def run_e2e(n):
+            c_in.wait_stream(stream)
+            c_out.wait_stream(stream)
+            inputs(0)
+            if n > 1:
+                inputs(1)
+            for k in range(n):
+                compute(k)
+                if k + 2 < n:
+                    inputs(k + 2)
+            stream.wait_stream(c_in)
+            stream.wait_stream(c_out)
+
+        run_e2e(1)
         barrier()
         f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         f0.record(stream)
-        for _ in range(n_e2e):
-            step_e2e()
+        run_e2e(n_e2e)
         f1.record(stream)
         barrier()
         check_err("the end-to-end steps")
@@ -451,9 +474,10 @@ def run_ours(args):
                "d2h_bytes_per_step": int((yp_h.numel() + yd_h.numel()) * 4), "ms_per_step": round(e2e_ms, 3),
                "steps": n_e2e,
                "api": "KvCache.prefill per layer and the captured KvCache.forward_one graph per decode step, on "
-                      "device tensors; every layer input copied up from pinned host memory and every layer output "
-                      "copied back inside the timed region, on a copy stream overlapped with the compute (prefill per "
-                      "layer, decode in chunks of 16 steps)"}
+                      "device tensors; every input copied up from pinned host memory (the next step's during the "
+                      "current step, into a second buffer set) and every output copied back a layer / 16 decode "
+                      "steps behind the compute, all inside the timed region; the first step's inputs are not "
+                      "hidden"}
 
         # the same workload through the synchronous host-pointer calls (each
         # call copies its rows in and out and returns when y is on the host)
@@ -913,7 +937,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-prefill-profile", action="store_true")
     ap.add_argument("--check-each-step", action="store_true")
-    ap.add_argument("--e2e-steps", type=int, default=2)
+    ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
     args = ap.parse_args()
