@@ -640,6 +640,87 @@ PREFILL_CFGS = {
 }
 
 
+DOT_CFG = {"E": 768, "H": 12, "L": 4, "B": 32, "T": 1024,
+           "desc": "legacy dot-product attention (ComputeBackend::attention, compute.rs:357-414) at the 768-dim "
+                   "shape: batch 32 x 1024 tokens, 12 heads x 64, 4 layers; TF32 tensor-core projections, fp32 core"}
+
+
+def run_dot_workload(args):
+    """The legacy dot-product attention through wb_dot_attn_forward: seeded
+    N(0, 0.02) weights, N(0, 1) per-layer inputs resident in HBM.  Prints its
+    own JSON line: tok/s and the attention core's share of the fp32 CUDA-core
+    peak (it runs on the FMA pipes, not the tensor cores)."""
+    import torch
+    import wave_engine_b200 as wb
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+    c = DOT_CFG
+    E, H, L, B, T = c["E"], c["H"], c["L"], c["B"], c["T"]
+    hd = E // H
+    ctx = wb.Context(local)
+    stream = torch.cuda.current_stream(dev)
+    ctx.set_stream(stream.cuda_stream)
+    layers = [wb.DotAttnLayer(ctx, wb.gaussian_attention_weights(5000 + l, H, E)) for l in range(L)]
+    g = torch.Generator(device=dev).manual_seed(91 + rank)
+    x = torch.randn((L, B, T, E), generator=g, device=dev)
+    y = torch.empty((B, T, E), device=dev)
+
+    def step():
+        for l in range(L):
+            y.copy_(wb.attention(layers[l], x[l], ctx=ctx))
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    ctx.profile("dot_attn")
+    clocks = Clocks(local)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    barrier()
+    clk = clocks.stop()
+    prof = ctx.profile_report()
+    ctx.profile(None)
+    if ctx.take_device_error():
+        raise RuntimeError("device error in the timed region")
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world, dev)
+    pairs = B * H * T * (T + 1) // 2
+    core_fl = pairs * 2 * 2 * hd                                  # q.k and p.v per causal pair
+    layer_fl = 2 * B * T * E * 3 * E + core_fl + 2 * B * T * E * E  # c_attn + core + c_proj
+    n_att, t_att = prof.get("dot_attn", (0, 0.0))
+    a_ms = t_att / max(1, n_att)
+    fp32_peak = 148 * 128 * 2 * (clk.get("sm_max_mhz") or 1965) * 1e6 / 1e12
+    out = {"metric": "dot-product attention tok/s (dot-768)", "value": round(world * B * T / (ms / 1e3), 1),
+           "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+           "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+           "dtype": "fp32 (TF32 tensor-core projections)", "data": "synthetic",
+           "config": {"workload": c["desc"], "inputs": "per-layer inputs resident in HBM"},
+           "roofline": {"kernel": "dot_attn", "bound": "fma", "peak": round(fp32_peak, 1), "unit": "TFLOP/s",
+                        "peak_kind": "nominal (148 SMs x 128 fp32 lanes x 2 FLOP x max SM clock)",
+                        "achieved": round(core_fl / (a_ms / 1e3) / 1e12, 2) if a_ms else None,
+                        "frac": round(core_fl / (a_ms / 1e3) / 1e12 / fp32_peak, 4) if a_ms else None,
+                        "launch_ms": round(a_ms, 4), "flops_per_launch": core_fl},
+           "layer_ms": round(ms / L, 4), "layer_flops": layer_fl, "clocks": clk}
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
 def run_prefill_workload(args):
     """Prefill through all attention layers of one of the prefill-only
     configurations (tensor path, content projection on): seeded N(0, 0.02)
@@ -920,10 +1001,12 @@ def run_profile_case(args):
 
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
-    ap.add_argument("--workload", choices=["serve-768", "decode-stress"] + sorted(PREFILL_CFGS), default="serve-768",
+    ap.add_argument("--workload", choices=["serve-768", "decode-stress", "dot-768"] + sorted(PREFILL_CFGS),
+                    default="serve-768",
                     help="serve-768: the headline configuration (default); decode-stress: 256 sequences of "
                          "context 128-4096; prefill-168/-384/-4096: prefill through all layers of the 168-, "
-                         "384- and 4096-dim models")
+                         "384- and 4096-dim models; dot-768: the legacy dot-product attention at the 768-dim "
+                         "shape")
     ap.add_argument("--profile-case", choices=["decode", "decode-stress", "prefill"], default=None,
                     help="run a small case for an ncu capture instead of the benchmark")
     ap.add_argument("--shard", choices=["batch", "heads"], default="batch",
@@ -949,6 +1032,8 @@ def main():
         run_decode_stress(args)
     elif args.workload in PREFILL_CFGS and args.impl == "ours":
         run_prefill_workload(args)
+    elif args.workload == "dot-768" and args.impl == "ours":
+        run_dot_workload(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

@@ -76,6 +76,7 @@ extern "C" {
 typedef struct wb_context wb_context;
 typedef struct wb_attn_layer wb_attn_layer;
 typedef struct wb_kv_cache wb_kv_cache;
+typedef struct wb_dot_attn_layer wb_dot_attn_layer;
 
 /* Host-side view of one block's attention weights (attn.rs:19-46),
  * flattened per head.  All pointers are HOST memory and are only read
@@ -166,6 +167,26 @@ WB_API int wb_attn_forward(wb_context *ctx, const wb_attn_layer *layer, const fl
  * multiple of 4. */
 WB_API int wb_attn_forward_heads(wb_context *ctx, const wb_attn_layer *layer, const float *x, int batch,
                                  int seq_len, int head_begin, int head_end, int add_bias, int flags, float *y_partial);
+
+/* ---- Dot-product attention (compute.rs:43, :357-414) ------------------ */
+/* The legacy causal self-attention of ComputeBackend::attention
+ * (compute.rs:43 -> attention_cpu, compute.rs:357-414; the same math as
+ * model_forward.rs:124-180): q, k, v = c_attn(x); per head softmax(q k^T /
+ * sqrt(head_dim)) over keys <= the query, times v; y = c_proj(heads).
+ * Weights as AttentionWeights (model.rs:191-195): c_attn_w [3*n_embd][n_embd]
+ * and c_proj_w [n_embd][n_embd] in LinearWeights' [out][in] row-major layout
+ * (model.rs:177-180), biases [3*n_embd] and [n_embd]; host memory, copied.
+ * head_dim <= 128. */
+WB_API int wb_dot_attn_layer_create(wb_context *ctx, int n_head, int n_embd, const float *c_attn_w,
+                                    const float *c_attn_b, const float *c_proj_w, const float *c_proj_b,
+                                    wb_dot_attn_layer **out);
+WB_API int wb_dot_attn_layer_destroy(wb_dot_attn_layer *layer);
+/* x, y [batch][seq_len][n_embd], host or device.  flags: WB_PATH_EXACT runs
+ * both projections as the reference's sequential fp32 sums (model.rs:144-150);
+ * otherwise they run on the tensor cores in TF32 (n_embd a multiple of 4, a
+ * device x 16-byte aligned).  The attention core is fp32 on both paths. */
+WB_API int wb_dot_attn_forward(wb_context *ctx, const wb_dot_attn_layer *layer, const float *x, int batch,
+                               int seq_len, int flags, float *y);
 
 /* ---- KV cache (kv_cache.rs:36-54) ------------------------------------- */
 /* One cache holds n_layers x max_seqs slots of capacity max_ctx positions,

@@ -52,6 +52,7 @@ def lib():
         l.wo_softplus.argtypes = [C.c_float]
         l.wo_softplus.restype = C.c_float
         l.wo_init_block_attn.argtypes = [C.POINTER(C.c_uint64), C.c_int, C.c_int, C.c_int] + [_F] * 9
+        l.wo_dot_attn_forward.argtypes = [C.c_int, C.c_int, _F, _F, _F, _F, _F, C.c_int, _F]
         _lib = l
     return _lib
 
@@ -185,3 +186,15 @@ def init_block_attn(state: int, n_head: int, n_embd: int, content_dim: int) -> t
                                                    "v_proj_b", "content_proj_w", "content_proj_b",
                                                    "out_proj_w", "out_proj_b")])
     return w, s.value
+
+
+def dot_attn_forward(w: dict, x: np.ndarray) -> np.ndarray:
+    """Legacy dot-product attention (compute.rs:357-414) for one sequence x [T,E]; w as
+    AttentionWeights.packed() (c_attn_w [3E][E], c_attn_b, c_proj_w [E][E], c_proj_b, n_head)."""
+    x = _f32(x)
+    T, E = x.shape
+    y = np.empty((T, E), np.float32)
+    ws = [_f32(w[k]) for k in ("c_attn_w", "c_attn_b", "c_proj_w", "c_proj_b")]
+    if lib().wo_dot_attn_forward(int(w["n_head"]), E, *[_fp(a) for a in ws], _fp(x), T, _fp(y)) != 0:
+        raise RuntimeError("oracle wo_dot_attn_forward failed")
+    return y

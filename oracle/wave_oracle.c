@@ -24,6 +24,8 @@
  *   content_w [H][C][E]       content_b [H][C]      (C = 0 or 16)
  *   out_w [E][E]              out_b [E]
  *   x [T][E]  ->  y [T][E];   att_w [H][T][T] (optional)
+ * and, for the legacy dot-product attention (wo_dot_attn_forward, end of
+ * file): c_attn_w [3E][E], c_attn_b [3E], c_proj_w [E][E], c_proj_b [E].
  */
 #include <math.h>
 #include <pthread.h>
@@ -499,5 +501,68 @@ int wo_attn_forward_batch(const wo_weights *w, const float *x, int b, int t, flo
     for (int i = 0; i < n_threads; i++) pthread_create(&th[i], NULL, proj_worker, &pj);
     for (int i = 0; i < n_threads; i++) pthread_join(th[i], NULL);
     free(head_out); free(merged);
+    return 0;
+}
+
+/* ---------------------------------------------------------------------------
+ * Legacy dot-product attention: src/common/compute.rs:357-414 (attention_cpu,
+ * the CPU ComputeBackend::attention of compute.rs:43).  linear_fn is
+ * model.rs:144-150: y[i] = b[i] + (sum_j W[i][j] * x[j]), the sum sequential.
+ * c_attn_w [3E][E], c_attn_b [3E], c_proj_w [E][E], c_proj_b [E]; x, y [T][E].
+ * ------------------------------------------------------------------------- */
+static void dot_linear(const float *w, const float *b, int n_out, int n_in, const float *x, float *y) {
+    for (int i = 0; i < n_out; i++) {
+        float sum = 0.0f;
+        for (int j = 0; j < n_in; j++) sum += w[(size_t)i * n_in + j] * x[j];
+        y[i] = b[i] + sum;
+    }
+}
+
+int wo_dot_attn_forward(int n_head, int n_embd, const float *c_attn_w, const float *c_attn_b,
+                        const float *c_proj_w, const float *c_proj_b, const float *x, int t, float *y) {
+    const int E = n_embd, hd = E / n_head;
+    if (n_head <= 0 || E % n_head || t <= 0) return -1;
+    const float scale = 1.0f / sqrtf((float)hd); /* compute.rs:362 */
+    float *qkv = (float *)malloc(sizeof(float) * (size_t)t * 3 * E);
+    float *out = (float *)calloc((size_t)t * E, sizeof(float));
+    float *att = (float *)malloc(sizeof(float) * (size_t)t);
+    if (!qkv || !out || !att) {
+        free(qkv);
+        free(out);
+        free(att);
+        return -1;
+    }
+    for (int pos = 0; pos < t; pos++) /* compute.rs:368-375 */
+        dot_linear(c_attn_w, c_attn_b, 3 * E, E, x + (size_t)pos * E, qkv + (size_t)pos * 3 * E);
+    for (int head = 0; head < n_head; head++) { /* compute.rs:379-407 */
+        const int off = head * hd;
+        for (int qi = 0; qi < t; qi++) {
+            const float *q = qkv + (size_t)qi * 3 * E + off;
+            for (int ki = 0; ki <= qi; ki++) {
+                const float *k = qkv + (size_t)ki * 3 * E + E + off;
+                float dot = 0.0f;
+                for (int d = 0; d < hd; d++) dot += q[d] * k[d];
+                att[ki] = dot * scale;
+            }
+            float max_att = -INFINITY;
+            for (int ki = 0; ki <= qi; ki++) max_att = fmaxf(max_att, att[ki]);
+            float exp_sum = 0.0f;
+            for (int ki = 0; ki <= qi; ki++) {
+                att[ki] = expf(att[ki] - max_att);
+                exp_sum += att[ki];
+            }
+            for (int ki = 0; ki <= qi; ki++) att[ki] /= exp_sum;
+            for (int d = 0; d < hd; d++) {
+                float sum = 0.0f;
+                for (int ki = 0; ki <= qi; ki++) sum += att[ki] * qkv[(size_t)ki * 3 * E + 2 * E + off + d];
+                out[(size_t)qi * E + off + d] = sum;
+            }
+        }
+    }
+    for (int pos = 0; pos < t; pos++) /* compute.rs:410-412 */
+        dot_linear(c_proj_w, c_proj_b, E, E, out + (size_t)pos * E, y + (size_t)pos * E);
+    free(qkv);
+    free(out);
+    free(att);
     return 0;
 }

@@ -151,3 +151,45 @@ def test_oracle_reproduces_decode_fixture(case):
         for s in range(steps):
             assert np.array_equal(oracle.kv_decode(w, x[b, n + s], st), fx[case + "/y"][s, b])
     assert _sha(fx[case + "/y"]) == str(fx[case + "/y.sha256"])
+
+
+# ---------------------------------------------------------------------------
+# legacy dot-product attention (compute.rs:357-414)
+# ---------------------------------------------------------------------------
+def _dot_attn_f64(w, x):
+    """Float64 statement of attention_cpu (compute.rs:357-414) for checking the oracle."""
+    E = x.shape[1]
+    H = w["n_head"]
+    hd = E // H
+    T = x.shape[0]
+    qkv = x.astype(np.float64) @ w["c_attn_w"].T.astype(np.float64) + w["c_attn_b"]
+    q, k, v = qkv[:, :E], qkv[:, E:2 * E], qkv[:, 2 * E:]
+    o = np.zeros((T, E))
+    for h in range(H):
+        sl = slice(h * hd, (h + 1) * hd)
+        s = q[:, sl] @ k[:, sl].T / np.sqrt(hd)
+        s[np.triu_indices(T, 1)] = -np.inf
+        p = np.exp(s - s.max(1, keepdims=True))
+        p /= p.sum(1, keepdims=True)
+        o[:, sl] = p @ v[:, sl]
+    return o @ w["c_proj_w"].T.astype(np.float64) + w["c_proj_b"]
+
+
+def test_dot_attention_oracle_known_answers():
+    """T = 1: the one key has weight 1, so y = c_proj(v) with v = c_attn's v
+    rows; identical positions: every query averages identical values, so
+    every output row equals the first; and a random case against float64."""
+    import wave_engine_b200 as wb
+    w = wb.gaussian_attention_weights(11, 4, 32, bias_std=0.1).packed()
+    x1 = np.random.default_rng(0).standard_normal((1, 32)).astype(np.float32)
+    v = (x1.astype(np.float64) @ w["c_attn_w"][64:].T + w["c_attn_b"][64:])
+    y_kat = v @ w["c_proj_w"].T.astype(np.float64) + w["c_proj_b"]
+    r = check("t1", oracle.dot_attn_forward(w, x1), y_kat, KAT_TOL)
+    assert r.passed, str(r)
+    xs = np.repeat(x1, 7, axis=0)
+    ys = oracle.dot_attn_forward(w, xs)
+    r = check("same rows", ys, np.repeat(ys[:1], 7, axis=0), (1e-6, 0.0))
+    assert r.passed, str(r)
+    x = np.random.default_rng(1).standard_normal((23, 32)).astype(np.float32)
+    r = check("random", oracle.dot_attn_forward(w, x), _dot_attn_f64(w, x), (1e-5, 0.0))
+    assert r.passed, str(r)

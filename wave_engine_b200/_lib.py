@@ -44,6 +44,9 @@ SIGNATURES = {
     "wb_init_block_attn": (C.c_int, [C.POINTER(C.c_uint64), C.c_int, C.c_int, C.c_int] + [_VP] * 9),
     "wb_attn_forward": (C.c_int, [_VP, _VP, _VP, C.c_int, C.c_int, C.c_int, _VP, _VP, _VP]),
     "wb_attn_forward_heads": (C.c_int, [_VP, _VP, _VP, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _VP]),
+    "wb_dot_attn_layer_create": (C.c_int, [_VP, C.c_int, C.c_int, _VP, _VP, _VP, _VP, C.POINTER(_VP)]),
+    "wb_dot_attn_layer_destroy": (C.c_int, [_VP]),
+    "wb_dot_attn_forward": (C.c_int, [_VP, _VP, _VP, C.c_int, C.c_int, C.c_int, _VP]),
     "wb_kv_cache_create": (C.c_int, [_VP, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(_VP)]),
     "wb_kv_cache_destroy": (C.c_int, [_VP]),
     "wb_kv_cache_length": (C.c_int, [_VP, C.c_int, C.c_int, C.POINTER(C.c_int)]),

@@ -120,6 +120,14 @@ static wb::ProjWeights proj_weights(const wb_attn_layer *L) {
     return wb::ProjWeights{L->E, L->H, L->hd, L->C, L->wrs_t, L->brs, L->wc_t, L->bc, L->wv_t, L->bv};
 }
 
+struct wb_dot_attn_layer {
+    wb_context *ctx = nullptr;
+    int device = 0;
+    int E = 0, H = 0;
+    float *w_qkv = nullptr, *wt_qkv = nullptr, *b_qkv = nullptr;  // [3E][E] (GEMM), [E][3E] (SIMT), [3E]
+    float *w_o = nullptr, *wt_o = nullptr, *b_o = nullptr;        // [E][E], [E][E] transposed, [E]
+};
+
 struct wb_kv_cache {
     wb_context *ctx = nullptr;
     int device = 0;  // destroy must not touch ctx (it may already be gone)
@@ -521,6 +529,111 @@ int wb_attn_forward(wb_context *ctx, const wb_attn_layer *L, const float *x, int
     if (phases_out && !ph_dev)
         WB_CUDA(cudaMemcpyAsync(phases_out, iob + o_ph, R * H * sizeof(float), cudaMemcpyDeviceToHost, st));
     if (!y_dev || (att_w && !aw_dev) || (phases_out && !ph_dev)) {
+        WB_CUDA(cudaStreamSynchronize(st));
+        uint32_t derr = 0;
+        WB_CUDA(cudaMemcpy(&derr, ctx->dev_err, sizeof(derr), cudaMemcpyDeviceToHost));
+        if (derr) return fail(WB_ETIMEOUT, "device-side check failed, error word " + std::to_string(derr));
+    }
+    return WB_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Dot-product attention (compute.rs:357-414)
+// ---------------------------------------------------------------------------
+int wb_dot_attn_layer_create(wb_context *ctx, int n_head, int n_embd, const float *c_attn_w, const float *c_attn_b,
+                             const float *c_proj_w, const float *c_proj_b, wb_dot_attn_layer **out) {
+    if (!ctx || !c_attn_w || !c_attn_b || !c_proj_w || !c_proj_b || !out) return fail(WB_EINVAL, "NULL argument");
+    *out = nullptr;
+    if (n_head <= 0 || n_embd <= 0 || n_embd % n_head) return fail(WB_EINVAL, "n_embd must be a multiple of n_head");
+    if (n_embd / n_head > 128) return fail(WB_ENOTSUP, "dot-product attention supports head_dim <= 128");
+    DeviceGuard g(ctx->device);
+    const int E = n_embd;
+    std::vector<float> wq(c_attn_w, c_attn_w + (size_t)3 * E * E), bq(c_attn_b, c_attn_b + 3 * E);
+    std::vector<float> wo(c_proj_w, c_proj_w + (size_t)E * E), bo(c_proj_b, c_proj_b + E);
+    std::vector<float> wqt((size_t)E * 3 * E), wot((size_t)E * E);
+    for (int n = 0; n < 3 * E; n++)
+        for (int j = 0; j < E; j++) wqt[(size_t)j * 3 * E + n] = wq[(size_t)n * E + j];
+    for (int n = 0; n < E; n++)
+        for (int j = 0; j < E; j++) wot[(size_t)j * E + n] = wo[(size_t)n * E + j];
+    wb_dot_attn_layer *L = new wb_dot_attn_layer();
+    L->ctx = ctx;
+    L->device = ctx->device;
+    L->E = E;
+    L->H = n_head;
+    int rc = upload(&L->w_qkv, wq);
+    if (rc == WB_OK) rc = upload(&L->wt_qkv, wqt);
+    if (rc == WB_OK) rc = upload(&L->b_qkv, bq);
+    if (rc == WB_OK) rc = upload(&L->w_o, wo);
+    if (rc == WB_OK) rc = upload(&L->wt_o, wot);
+    if (rc == WB_OK) rc = upload(&L->b_o, bo);
+    if (rc != WB_OK) {
+        wb_dot_attn_layer_destroy(L);
+        return rc;
+    }
+    *out = L;
+    return WB_OK;
+}
+
+int wb_dot_attn_layer_destroy(wb_dot_attn_layer *L) {
+    if (!L) return WB_OK;
+    DeviceGuard g(L->device);
+    float *ptrs[] = {L->w_qkv, L->wt_qkv, L->b_qkv, L->w_o, L->wt_o, L->b_o};
+    for (float *p : ptrs)
+        if (p) cudaFree(p);
+    delete L;
+    return WB_OK;
+}
+
+int wb_dot_attn_forward(wb_context *ctx, const wb_dot_attn_layer *L, const float *x, int B, int T, int flags,
+                        float *y) {
+    if (!ctx || !L || !x || !y) return fail(WB_EINVAL, "NULL argument");
+    if (L->ctx != ctx) return fail(WB_EINVAL, "layer belongs to another context");
+    if (flags & ~WB_PATH_EXACT) return fail(WB_EINVAL, "unknown flag bits");
+    if (B < 0 || T < 0) return fail(WB_EINVAL, "negative batch or seq_len");
+    if (B == 0 || T == 0) return WB_OK;
+    const long long R = (long long)B * T;
+    if (R > (1LL << 30)) return fail(WB_EINVAL, "batch*seq_len too large");
+    const bool exact = flags & WB_PATH_EXACT;
+    const int E = L->E, H = L->H;
+    if (!exact && E % 4) return fail(WB_ENOTSUP, "the tensor path needs n_embd to be a multiple of 4");
+    DeviceGuard g(ctx->device);
+    ProfBind pb(ctx);
+    cudaStream_t st = ctx->stream;
+    const bool x_dev = is_device_ptr(x), y_dev = is_device_ptr(y);
+    Carve io;
+    size_t o_x = x_dev ? 0 : io.take<float>(R * E);
+    size_t o_y = y_dev ? 0 : io.take<float>(R * E);
+    WB_TRY(ensure(ctx->io, io.off));
+    char *iob = (char *)ctx->io.p;
+    const float *xd = x_dev ? x : (const float *)(iob + o_x);
+    float *yd = y_dev ? y : (float *)(iob + o_y);
+    if (!x_dev) WB_CUDA(cudaMemcpyAsync((void *)xd, x, R * E * sizeof(float), cudaMemcpyHostToDevice, st));
+    Carve c;
+    size_t o_qkv = c.take<float>(R * 3 * E);
+    size_t o_o = c.take<float>(R * E);
+    WB_TRY(ensure(ctx->ws, c.off));
+    float *qkv = (float *)((char *)ctx->ws.p + o_qkv), *o = (float *)((char *)ctx->ws.p + o_o);
+    std::string msg;
+    WbSeqView none{};
+    if (exact) {  // model.rs:144-150 linear: sequential products, then + bias
+        wb::OutMap om{wb::OUT_DENSE, qkv, 3LL * E, none, 0, T};
+        wb::launch_seqdot(xd, (int)R, E, E, L->wt_qkv, 3 * E, L->b_qkv, 0, om, st);
+    } else {
+        int rc = wb::tc_gemm_tf32(xd, L->w_qkv, L->b_qkv, qkv, (int)R, 3 * E, E, ctx->dev_err, st, &msg);
+        if (rc != WB_OK) return fail(rc, msg);
+    }
+    int rc = wb::launch_dot_attn(qkv, B, T, E, H, o, st, &msg);
+    if (rc != WB_OK) return fail(rc, msg);
+    if (exact) {
+        wb::OutMap om{wb::OUT_DENSE, yd, E, none, 0, T};
+        wb::launch_seqdot(o, (int)R, E, E, L->wt_o, E, L->b_o, 0, om, st);
+    } else {
+        rc = wb::tc_gemm_tf32(o, L->w_o, L->b_o, yd, (int)R, E, E, ctx->dev_err, st, &msg);
+        if (rc != WB_OK) return fail(rc, msg);
+    }
+    WB_CUDA(cudaGetLastError());
+    if (!y_dev) {
+        WB_CUDA(cudaMemcpyAsync(y, yd, R * E * sizeof(float), cudaMemcpyDeviceToHost, st));
         WB_CUDA(cudaStreamSynchronize(st));
         uint32_t derr = 0;
         WB_CUDA(cudaMemcpy(&derr, ctx->dev_err, sizeof(derr), cudaMemcpyDeviceToHost));

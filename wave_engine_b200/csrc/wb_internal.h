@@ -99,6 +99,9 @@ void launch_decode_simt(const WbSeqView &sv, const int32_t *len, const float *th
 void launch_theta_only(const float *rs, int n, float *theta, cudaStream_t st);
 void launch_len_update(int32_t *len, const int32_t *slots, int n_seq, int value, int set, int n_slots, int cap,
                        cudaStream_t st);
+// Causal dot-product attention core (compute.rs:357-414): qkv [B*T][3E] ->
+// o [B*T][E] (head-major columns).
+int launch_dot_attn(const float *qkv, int B, int T, int E, int H, float *o, cudaStream_t st, std::string *msg);
 void launch_bucket_from_theta(const float *theta, uint8_t *bucket, long long n, cudaStream_t st);
 
 }  // namespace wb
