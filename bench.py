@@ -183,6 +183,21 @@ def decode_bytes_exact(bucket_slots, T0, S, H, hd, first=0):
     return total_keys * 5 + unmasked * hd * 4, unmasked, total_keys
 
 
+def prefill_unmasked_pairs(bucket_slots, T):
+    """Causal pairs (q, k <= q) of a prefill of T positions that the wave
+    mask lets through: key bucket within one of the query's (attn.rs:185-
+    210; the query's own position included) or k = q - 1 (attn.rs:211-220).
+    bucket_slots: u8 [L][B][H][>= T] from the cache.  Returns (unmasked,
+    dense) summed over all layers, sequences and heads."""
+    import numpy as np
+    b = bucket_slots[..., :T].astype(np.int64)
+    cnt = np.cumsum(b[..., None] == np.arange(8), axis=3, dtype=np.int32)  # keys <= q per bucket
+    adj = sum(np.take_along_axis(cnt, ((b + d) % 8)[..., None], axis=4)[..., 0] for d in (-1, 0, 1))
+    prev_masked = ~np.isin((b[..., :-1] - b[..., 1:]) % 8, (0, 1, 7))
+    L, B, H = b.shape[:3]
+    return int(adj.sum() + prev_masked.sum()), L * B * H * T * (T + 1) // 2
+
+
 # dram__bytes_read.sum + dram__bytes_write.sum of decode_attn over its
 # algorithmic bytes, measured by ncu on `bench.py --profile-case decode`
 # (values kept with the capture's summary under profiles/).
@@ -328,6 +343,7 @@ def run_ours(args):
     hbm, bf16, peak_kind = peaks()
     bk = np.stack([np.stack([cache.read(l, b)[1] for b in range(B)]) for l in range(L)])
     byts, unmasked, keys = decode_bytes_exact(bk, T, S, H, hd)
+    unm_pairs, dense_pairs = prefill_unmasked_pairs(bk, T)
     # decode_attn launch time: events around each launch, captured into a
     # copy of the decode graph and replayed once at the middle of the decode
     # phase (step S/2, after the timed region, which stays uninstrumented)
@@ -377,7 +393,10 @@ def run_ours(args):
         roof_prefill = {"kernel": "attn_tc", "bound": "tensor", "achieved": round(fl / (a_ms / 1e3) / 1e12, 2),
                         "peak": bf16, "unit": "TFLOP/s",
                         "frac": round(fl / (a_ms / 1e3) / 1e12 / bf16, 4), "launch_ms": round(a_ms, 4),
-                        "flops_per_launch": fl, "note": "whole-layer algorithmic FLOPs / attention kernel time"}
+                        "flops_per_launch": fl, "note": "whole-layer algorithmic FLOPs / attention kernel time",
+                        "unmasked_pair_fraction": round(unm_pairs / dense_pairs, 4),
+                        "unmasked_pairs_per_layer": unm_pairs // L,
+                        "dense_pairs_per_layer": dense_pairs // L}
 
     # end to end through the public API: every step copies all of its inputs
     # from pinned host memory and all of its outputs back, inside the timed
