@@ -335,7 +335,7 @@ struct AttnSmem {
     static_assert(BYTES <= 232448, "attention shared memory above the 227 KB limit");
 };
 
-static constexpr int ATT_SOFTMAX_WARPS = 8;                     // two per TMEM lane group
+static constexpr int ATT_SOFTMAX_WARPS = 16;                    // four per TMEM lane group
 static constexpr int ATT_THREADS = (ATT_SOFTMAX_WARPS + 2) * 32;  // + TMA loader warp + MMA warp
 
 // Bounded mbarrier wait that also gives up once another role has raised the
@@ -354,11 +354,12 @@ __device__ __forceinline__ bool att_wait(uint64_t *bar, uint32_t parity, volatil
 }
 
 // Attention core, warp-specialised.  One CTA = 128 queries of one (b, h).
-//   warp 8 (lane 0): TMA -- Q once, then K/V tiles into a KVST-stage ring.
-//   warp 9 (lane 0): tcgen05.mma -- S_j = Qf Kf_j^T into TMEM buffer j & 1
+//   warp 16 (lane 0): TMA -- Q once, then K/V tiles into a KVST-stage ring.
+//   warp 17 (lane 0): tcgen05.mma -- S_j = Qf Kf_j^T into TMEM buffer j & 1
 //     (two tiles ahead of the softmax), O += P_j V_j (value hi and lo).
-//   warps 0-7: softmax of S_j (two warps per TMEM lane group: warps w and
-//     w + 4 own the same 32 query rows, key columns 0-63 and 64-127),
+//   warps 0-15: softmax of S_j (four warps per TMEM lane group: warps w,
+//     w + 4, w + 8, w + 12 own the same 32 query rows, key columns 0-31,
+//     32-63, 64-95, 96-127),
 //     P_j = exp2 of the fixed shift in bf16 into shared-memory buffer j % PB;
 //     then the epilogue (O / l plus the exact previous-position term).
 // The S double buffer lets QK_{j+2} and PV_j run while the softmax works on
@@ -391,7 +392,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     const int b = bh / a.Hg, h = a.h0 + (bh - b * a.Hg);
     const int q0 = qt * QT;
     const bool softmax_warp = warp < ATT_SOFTMAX_WARPS;
-    const int row = tid & (QT - 1), half = (warp >> 2) & 1;  // softmax role: query row, key-column half
+    const int row = tid & (QT - 1), quarter = (warp >> 2) & 3;  // softmax role: query row, key-column quarter
     const int q = q0 + row;
     const long long rq = (long long)bh * a.T + q;
 
@@ -404,7 +405,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         m0 = a.m0[rq];
         sp = a.sprev[rq];
         vbase = wb_slot_base(a.sv, b, h);
-        if (half == 0) {
+        if (quarter == 0) {
             cn = a.cnorm[rq];
             cm = __uint_as_float(a.cmax[bh]);
         }
@@ -449,7 +450,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         ptx::tma_load_3d(sm + L::OFF_Q, &tm_q, qbar, 0, q0, bh);
         for (int j = 0; j < pre; j++) load_kv(j);
     }
-    const bool violate = softmax_warp && half == 0 && q < a.T && 0.25f * cn * (cm - cn) > BOUND_LIMIT;
+    const bool violate = softmax_warp && quarter == 0 && q < a.T && 0.25f * cn * (cm - cn) > BOUND_LIMIT;
     if (__syncthreads_or(violate)) {
         // the tile goes to the fp32 fallback: the copies already issued land
         // before the CTA leaves
@@ -528,7 +529,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
             else atomicOr(a.dev_err, WB_DERR_TIMEOUT_TMA);
         }
     } else {
-        // ---------------- softmax (warps 0-7)
+        // ---------------- softmax (warps 0-15)
         const float LOG2E = 1.4426950408889634f;
         const float nm0 = -m0 * LOG2E;
         const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
@@ -542,14 +543,13 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
             }
             ptx::tc_fence_after();
             const bool diag = (j == qt);
-            const uint32_t S_t = tmem + (uint32_t)((j & 1) * 128) + lane_base + half * 64;
-            uint32_t pk[2][16];
-#pragma unroll
-            for (int c = 0; c < 2; c++) {
+            const uint32_t S_t = tmem + (uint32_t)((j & 1) * 128) + lane_base + quarter * 32;
+            uint32_t pk[16];
+            {
                 uint32_t r[32];
-                ptx::tmem_ld32(S_t + c * 32, r);
+                ptx::tmem_ld32(S_t, r);
                 ptx::tmem_ld_wait();
-                const int kbase = half * 64 + c * 32;
+                const int kbase = quarter * 32;
 #pragma unroll
                 for (int i = 0; i < 16; i++) {
                     float e0 = fast_exp2(fmaf(__uint_as_float(r[2 * i]), LOG2E, nm0));
@@ -559,7 +559,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                         if (kbase + 2 * i + 1 > row) e1 = 0.0f;
                     }
                     l += e0 + e1;
-                    pk[c][i] = pack_bf16(e0, e1);
+                    pk[i] = pack_bf16(e0, e1);
                 }
             }
             // P buffer j % PB is free once PV_{j - PB} has completed
@@ -568,26 +568,25 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                 ok = false;
                 break;
             }
-            uint8_t *prow = sm + L::OFF_P + (j % PB) * L::P_BYTES + half * (QT * 128) + (row >> 3) * 1024 +
+            // keys 64h..64h+63 of a row are one 128-byte swizzled row of
+            // region h; this quarter's 32 keys are chunks (quarter & 1)*4 ..
+            uint8_t *prow = sm + L::OFF_P + (j % PB) * L::P_BYTES + (quarter >> 1) * (QT * 128) + (row >> 3) * 1024 +
                             (row & 7) * 128;
 #pragma unroll
-            for (int c = 0; c < 2; c++)
-#pragma unroll
-                for (int u = 0; u < 4; u++) {
-                    const int ch = (c * 4 + u) ^ (row & 7);
-                    *reinterpret_cast<uint4 *>(prow + ch * 16) =
-                        make_uint4(pk[c][4 * u], pk[c][4 * u + 1], pk[c][4 * u + 2], pk[c][4 * u + 3]);
-                }
+            for (int u = 0; u < 4; u++) {
+                const int ch = ((quarter & 1) * 4 + u) ^ (row & 7);
+                *reinterpret_cast<uint4 *>(prow + ch * 16) = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+            }
             ptx::fence_proxy_async_smem();
             ptx::tc_fence_before();
             ptx::mbar_arrive(pready + (j & 1));
         }
 
         // ---- epilogue: O / l plus the previous-position term; each thread
-        // its row and half of the O columns.  The previous value row's loads
+        // its row and a quarter of the O columns.  The previous value row's loads
         // go out before the wait for the last PV.
-        constexpr int HC = HDP / 2;  // O columns per thread
-        const int d0 = half * HC;
+        constexpr int HC = HDP / 4;  // O columns per thread
+        const int d0 = quarter * HC;
         float vprev[HC];
         const bool has_prev = q < a.T && sp > -INFINITY;
         if (has_prev) {
@@ -608,19 +607,31 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         }
         bool done = ok && att_wait(ofull, 0, abort_flag);
         if (ok && !done) atomicOr(a.dev_err, WB_DERR_TIMEOUT_MMA);
-        lsum[half * QT + row] = l;
-        asm volatile("bar.sync 1, 256;" ::: "memory");
+        // the row's four partial sums meet in the P buffers (every MMA has
+        // completed once ofull has; lsum keeps two)
+        float *lsum4 = reinterpret_cast<float *>(sm + L::OFF_P);
+        lsum4[quarter * QT + row] = l;
+        asm volatile("bar.sync 1, %0;" ::"n"(ATT_SOFTMAX_WARPS * 32) : "memory");
         ptx::tc_fence_after();
+        (void)lsum;
         if (done) {
-            float lt = lsum[row] + lsum[QT + row];
+            float lt = (lsum4[row] + lsum4[QT + row]) + (lsum4[2 * QT + row] + lsum4[3 * QT + row]);
             float o[HC];
-#pragma unroll
-            for (int c = 0; c < HC / 32; c++) {
-                uint32_t r[32];
-                ptx::tmem_ld32(O_t + lane_base + half * HC + c * 32, r);
+            if constexpr (HC == 16) {
+                uint32_t r[16];
+                ptx::tmem_ld16(O_t + lane_base + d0, r);
                 ptx::tmem_ld_wait();
 #pragma unroll
-                for (int i = 0; i < 32; i++) o[c * 32 + i] = __uint_as_float(r[i]);
+                for (int i = 0; i < 16; i++) o[i] = __uint_as_float(r[i]);
+            } else {
+#pragma unroll
+                for (int c = 0; c < HC / 32; c++) {
+                    uint32_t r[32];
+                    ptx::tmem_ld32(O_t + lane_base + d0 + c * 32, r);
+                    ptx::tmem_ld_wait();
+#pragma unroll
+                    for (int i = 0; i < 32; i++) o[c * 32 + i] = __uint_as_float(r[i]);
+                }
             }
             if (has_prev) {
                 const float e = __expf(sp - m0);
@@ -630,7 +641,24 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                     if (d0 + d < a.hd) o[d] = fmaf(e, vprev[d], o[d]);
             }
             const float inv = 1.0f / lt;
-            if (WIDE) {
+            if (WIDE && HC == 16) {
+                // the K/V ring is free (every MMA has completed): each warp
+                // stages its 32 rows x 16 columns and stores two rows at a time
+                float *buf = reinterpret_cast<float *>(sm + L::OFF_V) + warp * 32 * 17;
+                __syncwarp();
+#pragma unroll
+                for (int i = 0; i < 16; i++) buf[lane * 17 + i] = o[i] * inv;
+                __syncwarp();
+                const int col = lane & 15, d = d0 + col;
+#pragma unroll 4
+                for (int it = 0; it < 16; it++) {
+                    const int jr = 2 * it + (lane >> 4);
+                    const int qq = q0 + (warp & 3) * 32 + jr;
+                    if (qq < a.T && d < a.hd)
+                        reinterpret_cast<float *>(a.o)[((long long)b * a.T + qq) * a.E + (long long)h * a.hd + d] =
+                            buf[jr * 17 + col];
+                }
+            } else if (WIDE) {
                 // the K/V ring is free (every MMA has completed): each warp
                 // stages its 32 rows x 32 columns and stores them row by row
                 float *buf = reinterpret_cast<float *>(sm + L::OFF_V) + warp * 32 * 33;
