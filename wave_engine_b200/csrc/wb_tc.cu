@@ -337,6 +337,7 @@ struct AttnSmem {
 
 static constexpr int ATT_SOFTMAX_WARPS = 16;                    // four per TMEM lane group
 static constexpr int ATT_THREADS = (ATT_SOFTMAX_WARPS + 2) * 32;  // + TMA loader warp + MMA warp
+static constexpr int ATT_GROUP = 16;                              // (sequence, head) rows per CTA group
 
 // Bounded mbarrier wait that also gives up once another role has raised the
 // CTA's abort flag (so one timeout does not chain into one per barrier).
@@ -387,8 +388,14 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     volatile int *abort_flag = &s_abort;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int bh = blockIdx.x % a.BH;
-    const int qt = a.n_qt - 1 - (int)(blockIdx.x / a.BH);  // heaviest (longest) tiles first
+    // CTAs walk the (sequence, head) rows in groups of ATT_GROUP, the longest
+    // query tiles of a group first: a group's key/value tiles (a few MB)
+    // stay in L2 while all of its query tiles read them
+    const int per_grp = ATT_GROUP * a.n_qt;
+    const int grp = blockIdx.x / per_grp, rr = blockIdx.x - grp * per_grp;
+    const int gsz = min(ATT_GROUP, a.BH - grp * ATT_GROUP);
+    const int bh = grp * ATT_GROUP + rr % gsz;
+    const int qt = a.n_qt - 1 - rr / gsz;
     const int b = bh / a.Hg, h = a.h0 + (bh - b * a.Hg);
     const int q0 = qt * QT;
     const bool softmax_warp = warp < ATT_SOFTMAX_WARPS;
