@@ -722,7 +722,9 @@ __global__ void __launch_bounds__(128, 1)
     uint64_t *full = bars, *empty = bars + GST, *done = bars + 2 * GST;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * GST + 1);
     const int tid = threadIdx.x, warp = tid >> 5;
-    const int m0 = blockIdx.x * GBM, n0 = blockIdx.y * GBN;
+    // column tiles vary fastest: the CTAs of one row tile run together and
+    // read its A rows from L2 after the first
+    const int m0 = blockIdx.y * GBM, n0 = blockIdx.x * GBN;
     const int nk = (K + GBK - 1) / GBK;
     if (tid == 0) {
         for (int i = 0; i < 2 * GST + 1; i++) ptx::mbar_init(bars + i, 1);
@@ -917,7 +919,11 @@ static int launch_gemm(bool tf32, const void *A, const void *W, const float *bia
     const uint64_t bstr[1] = {(uint64_t)ldw * esz};
     const uint32_t bbox[2] = {bk, GBN};
     if ((rc = make_tmap(&tb, W, dt, 2, bdims, bstr, bbox, CU_TENSOR_MAP_SWIZZLE_128B, msg))) return rc;
-    dim3 gg((unsigned)((M + GBM - 1) / GBM), (unsigned)((N + GBN - 1) / GBN));
+    if ((M + GBM - 1) / GBM > 65535) {
+        *msg = "GEMM with more than 65535 row tiles";
+        return WB_EINVAL;
+    }
+    dim3 gg((unsigned)((N + GBN - 1) / GBN), (unsigned)((M + GBM - 1) / GBM));
     ProfScope ps(tf32 ? "gemm_tf32" : "gemm_bf16", st);
     if (tf32) {
         cudaFuncSetAttribute(gemm_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, G_SMEM);
