@@ -327,8 +327,7 @@ struct AttnSmem {
     static constexpr int OFF_K = OFF_Q + Q_BYTES;
     static constexpr int OFF_V = OFF_K + KVST * K_BYTES;
     static constexpr int OFF_P = OFF_V + KVST * V_BYTES;
-    static constexpr int OFF_L = OFF_P + PB * P_BYTES;   // [2][QT] row-sum halves
-    static constexpr int OFF_BAR = OFF_L + 2 * QT * 4;
+    static constexpr int OFF_BAR = OFF_P + PB * P_BYTES;
     // barriers: q, kvfull[KVST], kvfree[KVST], sfull[2], pready[2], pfree[PB], ofull; then the TMEM slot
     static constexpr int NBAR = 1 + 2 * KVST + 4 + PB + 1;
     static constexpr int BYTES = OFF_BAR + NBAR * 8 + 16 + 1024;  // + alignment slack
@@ -383,7 +382,6 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     uint64_t *pfree = pready + 2;     // [PB]
     uint64_t *ofull = pfree + PB;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(ofull + 1);
-    float *lsum = reinterpret_cast<float *>(sm + L::OFF_L);  // [2][QT]
     __shared__ int s_abort;
     volatile int *abort_flag = &s_abort;
 
@@ -615,12 +613,11 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         bool done = ok && att_wait(ofull, 0, abort_flag);
         if (ok && !done) atomicOr(a.dev_err, WB_DERR_TIMEOUT_MMA);
         // the row's four partial sums meet in the P buffers (every MMA has
-        // completed once ofull has; lsum keeps two)
+        // completed once ofull has)
         float *lsum4 = reinterpret_cast<float *>(sm + L::OFF_P);
         lsum4[quarter * QT + row] = l;
         asm volatile("bar.sync 1, %0;" ::"n"(ATT_SOFTMAX_WARPS * 32) : "memory");
         ptx::tc_fence_after();
-        (void)lsum;
         if (done) {
             float lt = (lsum4[row] + lsum4[QT + row]) + (lsum4[2 * QT + row] + lsum4[3 * QT + row]);
             float o[HC];
