@@ -337,6 +337,7 @@ def run_ours(args):
     check_err("the timed region")
     # every rank's output statistics of the last timed step, gathered to rank 0
     out_stats = gather_output_stats([y_pre, y_stage], world, dev)
+    y_ref = y_stage.clone()  # the last decode step's outputs of the timed steps (for the end-to-end check)
 
     # rooflines: decode attention (HBM, the dominant kernel) and prefill
     # attention (tensor), each from CUDA events around its own launches
@@ -489,6 +490,7 @@ def run_ours(args):
         check_err("the end-to-end steps")
         e2e_ms = max_over_ranks(f0.elapsed_time(f1) / n_e2e, world, dev)
         e2e = {"value": round(world * tok_step / (e2e_ms / 1e3), 1), "unit": "tok/s",
+               "outputs_equal_device_run": bool(torch.equal(yd_h[S - 1], y_ref.cpu())),
                "h2d_bytes_per_step": int((xp_h.numel() + xd_h.numel()) * 4),
                "d2h_bytes_per_step": int((yp_h.numel() + yd_h.numel()) * 4), "ms_per_step": round(e2e_ms, 3),
                "steps": n_e2e,
