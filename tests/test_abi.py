@@ -60,6 +60,9 @@ def test_null_arguments_are_rejected():
     assert l.wb_attn_forward(None, None, None, 1, 1, 0, None, None, None) == _lib.WB_EINVAL
     assert l.wb_kv_decode(None, None, 0, None, None, 1, None, 0, None) == _lib.WB_EINVAL
     assert l.wb_attn_layer_destroy(None) == _lib.WB_OK
+    assert l.wb_dot_attn_layer_create(None, 4, 64, None, None, None, None, None) == _lib.WB_EINVAL
+    assert l.wb_dot_attn_forward(None, None, None, 1, 1, 0, None) == _lib.WB_EINVAL
+    assert l.wb_dot_attn_layer_destroy(None) == _lib.WB_OK
     assert l.wb_context_destroy(None) == _lib.WB_OK
 
 
