@@ -1055,6 +1055,10 @@ def main():
         run_prefill_workload(args)
     elif args.workload == "dot-768" and args.impl == "ours":
         run_dot_workload(args)
+    elif args.impl == "reference" and args.workload != "serve-768":
+        if int(os.environ.get("RANK", "0")) == 0:
+            print(json.dumps({"impl": "reference", "unavailable": f"the CPU reference arm times the serve-768 "
+                                                                  f"workload only, not {args.workload}"}))
     elif args.impl == "reference":
         run_reference(args)
     else:
