@@ -53,6 +53,13 @@ def lib():
         l.wo_softplus.restype = C.c_float
         l.wo_init_block_attn.argtypes = [C.POINTER(C.c_uint64), C.c_int, C.c_int, C.c_int] + [_F] * 9
         l.wo_dot_attn_forward.argtypes = [C.c_int, C.c_int, _F, _F, _F, _F, _F, C.c_int, _F]
+        l.wo_attn_backward_full.argtypes = [C.POINTER(_Weights), _F, C.c_int, _F] + [_F] * 10
+        l.wo_bwd_out_proj.argtypes = [_F, _F, _F, C.c_int, C.c_int, _F, _F, _F]
+        l.wo_bwd_value_aggregation.argtypes = [_F, _F, _F, C.c_int, C.c_int, _F, _F]
+        l.wo_bwd_softmax.argtypes = [_F, _F, C.c_int, _F]
+        l.wo_bwd_phase_projection.argtypes = [_F, _F, _F, _F, C.c_int, C.c_int, _F, _F, _F]
+        l.wo_bwd_value_projection.argtypes = [_F, _F, C.c_int, C.c_int, C.c_int, C.c_int, _F, _F, _F, _F]
+        l.wo_bwd_combine.argtypes = [_F, _F, _F, C.c_int, C.c_int, C.c_int, _F]
         _lib = l
     return _lib
 
@@ -198,3 +205,86 @@ def dot_attn_forward(w: dict, x: np.ndarray) -> np.ndarray:
     if lib().wo_dot_attn_forward(int(w["n_head"]), E, *[_fp(a) for a in ws], _fp(x), T, _fp(y)) != 0:
         raise RuntimeError("oracle wo_dot_attn_forward failed")
     return y
+
+
+# ---------------------------------------------------------------------------
+# attention backward (attn_backward.rs, attn.rs:346-430)
+# ---------------------------------------------------------------------------
+def attn_backward_full(w: dict, x: np.ndarray, d_y: np.ndarray) -> dict:
+    """wave_attention_backward_full (attn.rs:346-430) for one sequence x [T,E] and
+    the output gradient d_y [T,E]: d_normed (the input gradient) and every weight
+    gradient, in the layouts of WaveAttnWeights.packed()."""
+    p = _Packed(w)
+    x, d_y = _f32(x), _f32(d_y)
+    T, E = x.shape
+    H, Cd = p.H, p.C
+    hd = E // H
+    g = {"d_x": np.empty((T, E), np.float32), "out_proj_w": np.empty((E, E), np.float32),
+         "out_proj_b": np.empty(E, np.float32), "phase_proj_w": np.empty((H, 2, E), np.float32),
+         "phase_proj_b": np.empty((H, 2), np.float32), "v_proj_w": np.empty((H, hd, hd), np.float32),
+         "v_proj_b": np.empty((H, hd), np.float32),
+         "content_proj_w": np.empty((H, Cd, E), np.float32) if Cd else None,
+         "content_proj_b": np.empty((H, Cd), np.float32) if Cd else None,
+         "harmonic_raw": np.empty(H, np.float32)}
+    rc = lib().wo_attn_backward_full(C.byref(p.s), _fp(x), T, _fp(d_y), _fp(g["d_x"]), _fp(g["out_proj_w"]),
+                                     _fp(g["out_proj_b"]), _fp(g["phase_proj_w"]), _fp(g["phase_proj_b"]),
+                                     _fp(g["v_proj_w"]), _fp(g["v_proj_b"]), _fp(g["content_proj_w"]),
+                                     _fp(g["content_proj_b"]), _fp(g["harmonic_raw"]))
+    if rc != 0:
+        raise RuntimeError("oracle wo_attn_backward_full failed")
+    return g
+
+
+def bwd_out_proj(d_y, merged, w):
+    """attn_backward.rs:17-53 -> (d_out, d_w, d_b)."""
+    d_y, merged, w = _f32(d_y), _f32(merged), _f32(w)
+    t, n = d_y.shape
+    out = (np.empty((t, n), np.float32), np.empty((n, n), np.float32), np.empty(n, np.float32))
+    lib().wo_bwd_out_proj(_fp(d_y), _fp(merged), _fp(w), n, t, *[_fp(a) for a in out])
+    return out
+
+
+def bwd_value_aggregation(d_head, att_w, v):
+    """attn_backward.rs:72-105 -> (d_att_w, d_v)."""
+    d_head, att_w, v = _f32(d_head), _f32(att_w), _f32(v)
+    t, hd = d_head.shape
+    out = (np.empty((t, t), np.float32), np.empty((t, hd), np.float32))
+    lib().wo_bwd_value_aggregation(_fp(d_head), _fp(att_w), _fp(v), t, hd, *[_fp(a) for a in out])
+    return out
+
+
+def bwd_softmax(d_att_w, att_w):
+    """attn_backward.rs:109-122 -> d_scores."""
+    d_att_w, att_w = _f32(d_att_w), _f32(att_w)
+    t = att_w.shape[0]
+    out = np.empty((t, t), np.float32)
+    lib().wo_bwd_softmax(_fp(d_att_w), _fp(att_w), t, _fp(out))
+    return out
+
+
+def bwd_phase_projection(d_phases, x, pw, pb):
+    """attn_backward.rs:190-231 -> (d_x, d_w [2][n], d_b [2])."""
+    d_phases, x, pw, pb = _f32(d_phases), _f32(x), _f32(pw), _f32(pb)
+    t, n = x.shape
+    out = (np.empty((t, n), np.float32), np.empty((2, n), np.float32), np.empty(2, np.float32))
+    lib().wo_bwd_phase_projection(_fp(d_phases), _fp(x), _fp(pw), _fp(pb), n, t, *[_fp(a) for a in out])
+    return out
+
+
+def bwd_value_projection(d_v, x, offset, vw):
+    """attn_backward.rs:237-263 -> (d_x, d_w [hd][hd], d_b [hd])."""
+    d_v, x, vw = _f32(d_v), _f32(x), _f32(vw)
+    t, hd = d_v.shape
+    n = x.shape[1]
+    out = (np.empty((t, n), np.float32), np.empty((hd, hd), np.float32), np.empty(hd, np.float32))
+    lib().wo_bwd_value_projection(_fp(d_v), _fp(x), offset, hd, n, t, _fp(vw), *[_fp(a) for a in out])
+    return out
+
+
+def bwd_combine(dxp, dxv, dxc=None):
+    """attn_backward.rs:299-326: [H][t][n] input gradients -> d_normed [t][n]."""
+    dxp, dxv, dxc = _f32(dxp), _f32(dxv), _f32(dxc)
+    H, t, n = dxp.shape
+    out = np.empty((t, n), np.float32)
+    lib().wo_bwd_combine(_fp(dxp), _fp(dxv), _fp(dxc), H, t, n, _fp(out))
+    return out

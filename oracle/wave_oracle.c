@@ -26,6 +26,10 @@
  *   x [T][E]  ->  y [T][E];   att_w [H][T][T] (optional)
  * and, for the legacy dot-product attention (wo_dot_attn_forward, end of
  * file): c_attn_w [3E][E], c_attn_b [3E], c_proj_w [E][E], c_proj_b [E].
+ *
+ * The attention backward at the end of the file (attn_backward.rs, composed
+ * as attn.rs:346-430) is pinned by the reference's own known-answer tests
+ * (attn_backward.rs:336-430) and by finite differences of the forward.
  */
 #include <math.h>
 #include <pthread.h>
@@ -565,4 +569,261 @@ int wo_dot_attn_forward(int n_head, int n_embd, const float *c_attn_w, const flo
     free(out);
     free(att);
     return 0;
+}
+
+/* ---------------------------------------------------------------------------
+ * Attention backward (the next row of the path, not yet on the GPU):
+ * src/common/math/attn_backward.rs:17-328 (the primitives) composed as
+ * src/common/attn.rs:346-430 (wave_attention_backward_full).  Flat row-major
+ * arrays; every sum in the reference's loop order.  Outputs are overwritten.
+ * ------------------------------------------------------------------------- */
+
+/* attn_backward.rs:17-53: d_out = W^T d_y, d_w += d_y (x) merged, d_b += d_y. */
+void wo_bwd_out_proj(const float *d_y, const float *merged, const float *w, int n, int t, float *d_out,
+                     float *d_w, float *d_b) {
+    for (int pos = 0; pos < t; pos++)
+        for (int j = 0; j < n; j++) {
+            float sum = 0.0f;
+            for (int i = 0; i < n; i++) sum += w[(size_t)i * n + j] * d_y[(size_t)pos * n + i];
+            d_out[(size_t)pos * n + j] = sum;
+        }
+    memset(d_w, 0, sizeof(float) * (size_t)n * n);
+    for (int pos = 0; pos < t; pos++)
+        for (int i = 0; i < n; i++) {
+            const float dai = d_y[(size_t)pos * n + i];
+            if (fabsf(dai) < 1e-12f) continue;
+            for (int j = 0; j < n; j++) d_w[(size_t)i * n + j] += dai * merged[(size_t)pos * n + j];
+        }
+    memset(d_b, 0, sizeof(float) * (size_t)n);
+    for (int pos = 0; pos < t; pos++)
+        for (int i = 0; i < n; i++) d_b[i] += d_y[(size_t)pos * n + i];
+}
+
+/* attn_backward.rs:72-105: d_att_w[qi][ki] = d_head[qi] . v[ki] and
+ * d_v[ki] += att_w[qi][ki] d_head[qi], over kept pairs (att_w > 0). */
+void wo_bwd_value_aggregation(const float *d_head, const float *att_w, const float *v, int t, int hd,
+                              float *d_att_w, float *d_v) {
+    memset(d_att_w, 0, sizeof(float) * (size_t)t * t);
+    for (int qi = 0; qi < t; qi++)
+        for (int ki = 0; ki <= qi; ki++)
+            if (att_w[(size_t)qi * t + ki] > 0.0f) {
+                float dw = 0.0f;
+                for (int d = 0; d < hd; d++) dw += d_head[(size_t)qi * hd + d] * v[(size_t)ki * hd + d];
+                d_att_w[(size_t)qi * t + ki] = dw;
+            }
+    memset(d_v, 0, sizeof(float) * (size_t)t * hd);
+    for (int qi = 0; qi < t; qi++)
+        for (int ki = 0; ki <= qi; ki++)
+            if (att_w[(size_t)qi * t + ki] > 0.0f)
+                for (int d = 0; d < hd; d++)
+                    d_v[(size_t)ki * hd + d] += att_w[(size_t)qi * t + ki] * d_head[(size_t)qi * hd + d];
+}
+
+/* attn_backward.rs:109-122: d_score = a (d_a - sum_k a_k d_a_k). */
+void wo_bwd_softmax(const float *d_att_w, const float *att_w, int t, float *d_scores) {
+    memset(d_scores, 0, sizeof(float) * (size_t)t * t);
+    for (int qi = 0; qi < t; qi++) {
+        float ws = 0.0f;
+        for (int ki = 0; ki <= qi; ki++) ws += att_w[(size_t)qi * t + ki] * d_att_w[(size_t)qi * t + ki];
+        for (int ki = 0; ki <= qi; ki++)
+            d_scores[(size_t)qi * t + ki] = att_w[(size_t)qi * t + ki] * (d_att_w[(size_t)qi * t + ki] - ws);
+    }
+}
+
+/* attn_backward.rs:128-163: through cos(n (th_q - th_k)) + scale c_q . c_k. */
+static void bwd_score(const float *d_scores, const float *phases, float hn, const float *att_w,
+                      const float *content, int C, float content_scale, int t, float *d_delta,
+                      float *d_content, float *d_hn) {
+    memset(d_delta, 0, sizeof(float) * (size_t)t * t);
+    if (content) memset(d_content, 0, sizeof(float) * (size_t)t * C);
+    float dh = 0.0f;
+    for (int qi = 0; qi < t; qi++)
+        for (int ki = 0; ki <= qi; ki++)
+            if (att_w[(size_t)qi * t + ki] > 0.0f) {
+                const float ds = d_scores[(size_t)qi * t + ki];
+                const float delta = phases[qi] - phases[ki];
+                const float sin_nd = sinf(hn * delta);
+                d_delta[(size_t)qi * t + ki] = -sin_nd * hn * ds;
+                dh += -sin_nd * delta * ds;
+                if (content)
+                    for (int cd = 0; cd < C; cd++) {
+                        d_content[(size_t)qi * C + cd] += ds * content_scale * content[(size_t)ki * C + cd];
+                        d_content[(size_t)ki * C + cd] += ds * content_scale * content[(size_t)qi * C + cd];
+                    }
+            }
+    *d_hn = dh;
+}
+
+/* attn_backward.rs:169-184: delta = th_q - th_k. */
+static void bwd_phase_subtraction(const float *d_delta, const float *att_w, int t, float *d_phases) {
+    memset(d_phases, 0, sizeof(float) * (size_t)t);
+    for (int qi = 0; qi < t; qi++)
+        for (int ki = 0; ki <= qi; ki++)
+            if (att_w[(size_t)qi * t + ki] > 0.0f) {
+                d_phases[qi] += d_delta[(size_t)qi * t + ki];
+                d_phases[ki] -= d_delta[(size_t)qi * t + ki];
+            }
+}
+
+/* attn_backward.rs:190-231: through atan2(s, r), [r, s] = W x + b. */
+void wo_bwd_phase_projection(const float *d_phases, const float *x, const float *pw, const float *pb, int n, int t,
+                             float *d_x, float *d_w, float *d_b) {
+    memset(d_x, 0, sizeof(float) * (size_t)t * n);
+    memset(d_w, 0, sizeof(float) * (size_t)2 * n);
+    d_b[0] = d_b[1] = 0.0f;
+    for (int pos = 0; pos < t; pos++) {
+        const float dp = d_phases[pos];
+        if (fabsf(dp) < 1e-12f) continue;
+        float r = pb[0], s = pb[1];
+        for (int j = 0; j < n; j++) {
+            r += pw[j] * x[(size_t)pos * n + j];
+            s += pw[n + j] * x[(size_t)pos * n + j];
+        }
+        const float mag_sq = r * r + s * s;
+        if (mag_sq < 1e-8f) continue;
+        const float mag = fmaxf(mag_sq, 1e-12f);
+        const float d_r = dp * (-s / mag), d_s = dp * (r / mag);
+        for (int j = 0; j < n; j++) {
+            d_x[(size_t)pos * n + j] += pw[j] * d_r + pw[n + j] * d_s;
+            d_w[j] += d_r * x[(size_t)pos * n + j];
+            d_w[n + j] += d_s * x[(size_t)pos * n + j];
+        }
+        d_b[0] += d_r;
+        d_b[1] += d_s;
+    }
+}
+
+/* attn_backward.rs:237-263: through v = Wv x[off .. off+hd] + b. */
+void wo_bwd_value_projection(const float *d_v, const float *x, int off, int hd, int n, int t, const float *vw,
+                             float *d_x, float *d_w, float *d_b) {
+    memset(d_x, 0, sizeof(float) * (size_t)t * n);
+    memset(d_w, 0, sizeof(float) * (size_t)hd * hd);
+    memset(d_b, 0, sizeof(float) * (size_t)hd);
+    for (int pos = 0; pos < t; pos++)
+        for (int dd = 0; dd < hd; dd++) {
+            const float dv = d_v[(size_t)pos * hd + dd];
+            if (fabsf(dv) < 1e-12f) continue;
+            for (int j = 0; j < hd; j++) {
+                d_x[(size_t)pos * n + off + j] += vw[(size_t)dd * hd + j] * dv;
+                d_w[(size_t)dd * hd + j] += dv * x[(size_t)pos * n + off + j];
+            }
+            d_b[dd] += dv;
+        }
+}
+
+/* attn_backward.rs:269-293: through c = Wc x + b. */
+static void bwd_content_projection(const float *d_c, const float *x, const float *cw, int C, int n, int t,
+                                   float *d_x, float *d_w, float *d_b) {
+    memset(d_x, 0, sizeof(float) * (size_t)t * n);
+    memset(d_w, 0, sizeof(float) * (size_t)C * n);
+    memset(d_b, 0, sizeof(float) * (size_t)C);
+    for (int pos = 0; pos < t; pos++)
+        for (int cd = 0; cd < C; cd++) {
+            const float dc = d_c[(size_t)pos * C + cd];
+            if (fabsf(dc) < 1e-12f) continue;
+            for (int j = 0; j < n; j++) {
+                d_x[(size_t)pos * n + j] += cw[(size_t)cd * n + j] * dc;
+                d_w[(size_t)cd * n + j] += dc * x[(size_t)pos * n + j];
+            }
+            d_b[cd] += dc;
+        }
+}
+
+/* attn_backward.rs:299-326: d_normed = sum over heads of the three input
+ * gradients (phase + value first, then content where present). */
+void wo_bwd_combine(const float *dxp, const float *dxv, const float *dxc, int n_head, int t, int n, float *d_normed) {
+    memset(d_normed, 0, sizeof(float) * (size_t)t * n);
+    for (int h = 0; h < n_head; h++)
+        for (int pos = 0; pos < t; pos++) {
+            const size_t o = ((size_t)h * t + pos) * n;
+            for (int j = 0; j < n; j++) d_normed[(size_t)pos * n + j] += dxp[o + j] + dxv[o + j];
+            if (dxc)
+                for (int j = 0; j < n; j++) d_normed[(size_t)pos * n + j] += dxc[o + j];
+        }
+}
+
+/* attn.rs:346-430 wave_attention_backward_full for one sequence x [t][E] and
+ * the output gradient d_y [t][E]; the forward cache (WaveAttnCache,
+ * attn.rs:51-70) is recomputed with the forward's own arithmetic.  Weight
+ * gradients in the layouts of the weights (d_content_w / d_content_b may be
+ * NULL when content_dim = 0).  Returns 0, or -1 on bad arguments /
+ * allocation failure. */
+int wo_attn_backward_full(const wo_weights *w, const float *x, int t, const float *d_y, float *d_x, float *d_out_w,
+                          float *d_out_b, float *d_phase_w, float *d_phase_b, float *d_v_w, float *d_v_b,
+                          float *d_content_w, float *d_content_b, float *d_harmonic_raw) {
+    if (!w || t <= 0 || w->n_head <= 0 || w->n_embd % w->n_head) return -1;
+    const int E = w->n_embd, H = w->n_head, hd = E / H, C = w->content_dim;
+    const size_t tt = (size_t)t * t;
+    float *merged = (float *)calloc((size_t)t * E, sizeof(float));
+    float *head_out = (float *)malloc(sizeof(float) * (size_t)t * hd);
+    float *att_w = (float *)malloc(sizeof(float) * tt);
+    float *phases = (float *)malloc(sizeof(float) * (size_t)t);
+    float *v_all = (float *)malloc(sizeof(float) * (size_t)t * hd);
+    float *content = C ? (float *)malloc(sizeof(float) * (size_t)t * C) : NULL;
+    float *d_out = (float *)malloc(sizeof(float) * (size_t)t * E);
+    float *d_head = (float *)malloc(sizeof(float) * (size_t)t * hd);
+    float *d_att = (float *)malloc(sizeof(float) * tt);
+    float *d_v = (float *)malloc(sizeof(float) * (size_t)t * hd);
+    float *d_sc = (float *)malloc(sizeof(float) * tt);
+    float *d_delta = (float *)malloc(sizeof(float) * tt);
+    float *d_c = C ? (float *)malloc(sizeof(float) * (size_t)t * C) : NULL;
+    float *d_ph = (float *)malloc(sizeof(float) * (size_t)t);
+    float *dxp = (float *)malloc(sizeof(float) * (size_t)H * t * E);
+    float *dxv = (float *)malloc(sizeof(float) * (size_t)H * t * E);
+    float *dxc = C ? (float *)malloc(sizeof(float) * (size_t)H * t * E) : NULL;
+    int rc = 0;
+    if (!merged || !head_out || !att_w || !phases || !v_all || (C && (!content || !d_c || !dxc)) || !d_out ||
+        !d_head || !d_att || !d_v || !d_sc || !d_delta || !d_ph || !dxp || !dxv) {
+        rc = -1;
+        goto done;
+    }
+    /* the forward's merged head outputs (attn.rs:259-268) */
+    for (int h = 0; h < H; h++) {
+        attn_one_head(w, x, t, h, head_out, NULL, NULL, NULL);
+        for (int pos = 0; pos < t; pos++)
+            memcpy(merged + (size_t)pos * E + (size_t)h * hd, head_out + (size_t)pos * hd, sizeof(float) * hd);
+    }
+    wo_bwd_out_proj(d_y, merged, w->out_w, E, t, d_out, d_out_w, d_out_b);
+    for (int h = 0; h < H; h++) {
+        const float raw = w->harmonic_raw[h];
+        const float hn = wo_softplus(raw);
+        const float sig = 1.0f / (1.0f + expf(-raw));
+        const int off = h * hd;
+        /* cache of head h: phases, att_w, values, content (attn.rs:121-165) */
+        attn_one_head(w, x, t, h, head_out, att_w, NULL, phases);
+        for (int pos = 0; pos < t; pos++)
+            value_project(x + (size_t)pos * E + off, hd, w->v_w + (size_t)h * hd * hd, w->v_b + h * hd,
+                          v_all + (size_t)pos * hd);
+        if (C) {
+            const float *cw = w->content_w + (size_t)h * C * E, *cb = w->content_b + h * C;
+            for (int pos = 0; pos < t; pos++)
+                for (int d = 0; d < C; d++) {
+                    float sum = cb[d];
+                    for (int j = 0; j < E; j++) sum += cw[(size_t)d * E + j] * x[(size_t)pos * E + j];
+                    content[(size_t)pos * C + d] = sum;
+                }
+        }
+        const float cscale = C > 0 ? 1.0f / sqrtf((float)C) : 0.0f;
+        for (int pos = 0; pos < t; pos++) /* split_heads, attn_backward.rs:56-66 */
+            memcpy(d_head + (size_t)pos * hd, d_out + (size_t)pos * E + off, sizeof(float) * hd);
+        wo_bwd_value_aggregation(d_head, att_w, v_all, t, hd, d_att, d_v);
+        wo_bwd_softmax(d_att, att_w, t, d_sc);
+        float d_hn = 0.0f;
+        bwd_score(d_sc, phases, hn, att_w, content, C, cscale, t, d_delta, d_c, &d_hn);
+        bwd_phase_subtraction(d_delta, att_w, t, d_ph);
+        wo_bwd_phase_projection(d_ph, x, w->phase_w + (size_t)h * 2 * E, w->phase_b + h * 2, E, t,
+                                dxp + (size_t)h * t * E, d_phase_w + (size_t)h * 2 * E, d_phase_b + h * 2);
+        wo_bwd_value_projection(d_v, x, off, hd, E, t, w->v_w + (size_t)h * hd * hd, dxv + (size_t)h * t * E,
+                                d_v_w + (size_t)h * hd * hd, d_v_b + h * hd);
+        if (C)
+            bwd_content_projection(d_c, x, w->content_w + (size_t)h * C * E, C, E, t, dxc + (size_t)h * t * E,
+                                   d_content_w + (size_t)h * C * E, d_content_b + h * C);
+        d_harmonic_raw[h] = d_hn * sig;
+    }
+    wo_bwd_combine(dxp, dxv, dxc, H, t, E, d_x);
+done:
+    free(merged); free(head_out); free(att_w); free(phases); free(v_all); free(content); free(d_out);
+    free(d_head); free(d_att); free(d_v); free(d_sc); free(d_delta); free(d_c); free(d_ph); free(dxp); free(dxv);
+    free(dxc);
+    return rc;
 }
