@@ -237,8 +237,10 @@ WB_API int wb_kv_decode(wb_context *ctx, wb_kv_cache *cache, int layer_idx, cons
 /* wb_kv_decode on the tensor path without allocating any device memory.
  * No counterpart in the reference: it exists for callers that may not
  * allocate at decode time (a server that reserves its device memory at
- * start-up and forbids allocation per request, or decoding inside CUDA
- * stream capture, where cudaMalloc is not allowed).  The kernels' scratch
+ * start-up and forbids allocation per request; a host application whose own
+ * memory pool owns the device and forbids outside cudaMalloc; a latency-
+ * bound loop that cannot take cudaMalloc's implicit synchronisation or its
+ * failure mid-request).  The kernels' scratch
  * lives in one static device array of WB_NOALLOC_SCRATCH_BYTES per GPU,
  * held until the process exits; a cache whose decode scratch
  * (slots x heads x splits partial rows -- one split up to max_ctx 1536,

@@ -43,3 +43,17 @@ def test_decode_bytes_exact_matches_enumeration():
                 kept += sum(_kept(int(bk[l, b, h, p]), int(bk[l, b, h, k]), k, p) for k in range(p))
         assert (unmasked, keys) == (kept, total)
         assert byts == 5 * total + 4 * hd * kept
+
+
+def test_flop_formulas_match_the_configuration_table():
+    """The attention kernel is credited only with its own work, 2*P*(2+C+hd)
+    over the dense causal pairs; the whole layer adds the projections and
+    out_proj.  Figures of the 768-dim configuration (B 32, T 1024, 12 x 64,
+    C 16): 33.05 GFLOP of pairs inside 85.8 GFLOP per layer."""
+    import bench
+    core = bench.attn_core_flops(32, 1024, 12, 64, 16)
+    layer = bench.prefill_flops_per_layer(32, 1024, 768, 12, 64, 16)
+    assert core == 32 * 12 * 1024 * 1025 // 2 * 2 * (2 + 16 + 64)
+    assert abs(core / 1e9 - 33.05) < 0.01
+    assert abs(layer / 1e9 - 85.8) < 0.1
+    assert layer - core == 2 * 32 * 1024 * 768 * (12 * 18 + 64 + 768)

@@ -1,10 +1,11 @@
 """wb_kv_decode_noalloc: the decode step that allocates no device memory.
 
 Some callers cannot allocate at decode time -- a server that reserves all
-of its device memory when it starts and forbids allocation per request, or
-a decode issued inside CUDA stream capture, where cudaMalloc is not
-permitted.  For them the library keeps the decode kernels' scratch in one
-static device array (WB_NOALLOC_SCRATCH_BYTES per GPU).  These tests call
+of its device memory when it starts and forbids allocation per request, a
+host application whose own memory pool owns the device, or a latency-bound
+loop that cannot take cudaMalloc's implicit synchronisation.  For them the
+library keeps the decode kernels' scratch in one static device array
+(WB_NOALLOC_SCRATCH_BYTES per GPU).  These tests call
 that entry point through the C ABI and check it against the ordinary
 wb_kv_decode on a twin cache, for two decode calls in a row.
 
@@ -84,8 +85,9 @@ def test_noalloc_decode_rejects_oversize_and_host_buffers():
     ctx = wb.Context(0)
     w = wb.gaussian_block_attn(3, 1, 64, 0)
     layer = wb.AttnLayer(ctx, w)
-    # 1024 slots x 8192 positions needs ~4.8 MB of decode scratch > 4 MiB
-    big = wb.KvCache(1, 1, 64, max_seqs=1024, max_ctx=8192, ctx=ctx)
+    # 8192 one-position slots: a ~2 MB cache whose decode scratch (~6.4 MB:
+    # the partial row, new value and output row of every slot) exceeds 4 MiB
+    big = wb.KvCache(1, 1, 64, max_seqs=8192, max_ctx=1, ctx=ctx)
     ids = torch.zeros(1, dtype=torch.int32, device="cuda")
     x = torch.zeros((1, 64), device="cuda")
     y = torch.zeros((1, 64), device="cuda")

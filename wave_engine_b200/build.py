@@ -86,7 +86,7 @@ def build(verbose: bool = False, force: bool = False, ptxas_verbose: bool = Fals
     objs = [BUILD / (s.stem + ".o") for s in srcs]
     if force or jobs or not LIB.exists() or any(o.stat().st_mtime > LIB.stat().st_mtime for o in objs):
         tmp = LIB.with_suffix(".so.tmp")
-        cmd = [nvcc, *ARCH, "-shared", "-o", str(tmp), *map(str, objs), "-lcuda"]
+        cmd = [nvcc, *ARCH, "-shared", "-o", str(tmp), *map(str, objs)]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError("link failed:\n" + r.stdout + r.stderr)

@@ -965,9 +965,9 @@ int wb_test_gemm_tf32(wb_context *ctx, const float *A, const float *B, const flo
 //
 // Who needs it: callers that may not allocate device memory at the point
 // where they decode -- a serving process that reserves its whole device
-// budget at start-up and forbids allocation on the request path, or code
-// that decodes inside CUDA stream capture, where cudaMalloc is not
-// permitted.  Everything else the call touches (weights, cache, x, y, seq
+// budget at start-up and forbids allocation on the request path, a host
+// application whose own memory pool owns the device, or a latency-bound
+// loop that cannot take cudaMalloc's implicit synchronisation.  Everything else the call touches (weights, cache, x, y, seq
 // ids) was allocated by the caller beforehand.
 //
 // The array below is WB_NOALLOC_SCRATCH_BYTES on every GPU that loads this
