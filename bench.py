@@ -980,7 +980,8 @@ def run_profile_case(args):
     """Small single-GPU cases for ncu captures (no timing, a few hundred MB
     on the device): 'decode' = 12 fused decode steps of one 768-dim layer,
     32 sequences at ctx ~1100; 'prefill' = 3 tensor-path prefills of one
-    768-dim layer, 4 x 1024 tokens."""
+    768-dim layer, 4 x 1024 tokens (content on); 'prefill-serve' = 3 serve
+    prefills (KV cache, no content) of one 768-dim layer, 4 x 1024 tokens."""
     import numpy as np
     import torch
     import wave_engine_b200 as wb
@@ -1030,6 +1031,15 @@ def run_profile_case(args):
         bk = np.stack([np.stack([cache.read(0, b)[1] for b in range(B)])])
         extra["decode_attn_algorithmic_bytes"] = [
             int(decode_bytes_exact(bk, n, s + 1, H, hd, first=s)[0] + B * E * 4) for s in range(12)]
+    elif args.profile_case == "prefill-serve":
+        B = 4
+        cache = wb.KvCache(1, H, hd, max_seqs=B, max_ctx=CFG["seq_len"], ctx=ctx)
+        ids = torch.arange(B, dtype=torch.int32, device="cuda")
+        x = torch.randn((B, CFG["seq_len"], E), generator=g, device="cuda")
+        y = torch.empty_like(x)
+        for _ in range(3):
+            cache.reset()
+            cache.prefill(0, lay, x, ids, out=y)
     else:
         x = torch.randn((4, CFG["seq_len"], E), generator=g, device="cuda")
         for _ in range(3):
@@ -1049,7 +1059,7 @@ def main():
                          "context 128-4096; prefill-168/-384/-4096: prefill through all layers of the 168-, "
                          "384- and 4096-dim models; dot-768: the legacy dot-product attention at the 768-dim "
                          "shape")
-    ap.add_argument("--profile-case", choices=["decode", "decode-stress", "prefill"], default=None,
+    ap.add_argument("--profile-case", choices=["decode", "decode-stress", "prefill", "prefill-serve"], default=None,
                     help="run a small case for an ncu capture instead of the benchmark")
     ap.add_argument("--shard", choices=["batch", "heads"], default="batch",
                     help="prefill workloads under torchrun: every rank its own batch (weak scaling), or the heads "

@@ -83,10 +83,10 @@ void launch_projections_exact(const ProjWeights &w, const float *x, int B, int T
                               float *content, cudaStream_t st);
 void launch_attn_simt_fallback_f32(const WbSeqView &sv, const float *content, int C, float content_scale,
                                    const float *harmonic_n, int B, int H, int T, int hd, float *o,
-                                   const int *tile_flags, int h0, int Hg, cudaStream_t st);
+                                   const int *tile_list, int h0, int Hg, cudaStream_t st);
 void launch_attn_simt_fallback_bf16(const WbSeqView &sv, const float *content, int C, float content_scale,
                                     const float *harmonic_n, int B, int H, int T, int hd, __nv_bfloat16 *o,
-                                    const int *tile_flags, int h0, int Hg, cudaStream_t st);
+                                    const int *tile_list, int h0, int Hg, cudaStream_t st);
 void launch_seqdot(const float *X, int R, int K, long long ldx, const float *Wt, int N,
                    const float *bias, int bias_first, const OutMap &om, cudaStream_t st);
 void launch_phase(const float *rs, int R, int H, int T, const WbSeqView &sv, cudaStream_t st);

@@ -7,6 +7,8 @@
 // also produce the phases/buckets/values the KV cache stores.
 #include "wb_internal.h"
 
+#include <algorithm>
+
 namespace wb {
 
 // ---------------------------------------------------------------------------
@@ -109,7 +111,7 @@ struct AttnSimtArgs {
     int B, H, T, hd;
     void *o;         // [B*T][H*hd] merged heads (float or bf16)
     float *att_w;    // [B][H][T][T] or nullptr
-    const int *tile_flags;  // [B*Hg][ceil(T/128)]: only flagged query tiles (nullptr = all)
+    const int *tile_list;   // [0] = n, [1..n] = flagged query tiles b*Hg*n_qt + (h-h0)*n_qt + qt (nullptr = all)
     int h0, Hg;             // tile mode: heads h0 .. h0 + Hg - 1 (rows bh = b * Hg + h - h0)
 };
 
@@ -128,17 +130,21 @@ __global__ void __launch_bounds__(256) attn_simt_kernel(AttnSimtArgs a) {
     attn_simt_query<DPL, OutT>(a, blockIdx.z, blockIdx.y, q);
 }
 
-// Fallback over flagged 128-query tiles: one CTA per (b, h, tile); CTAs of
-// unflagged tiles exit at once, flagged ones loop their 8 warps over the
-// tile's queries.
+// Fallback over the flagged 128-query tiles listed by the tensor-core
+// kernel: a small fixed grid walks the list (CTA i takes entries i,
+// i + gridDim.x, ...), its 8 warps looping over a tile's queries.  With no
+// flagged tile every CTA reads the count and exits.
 template <int DPL, class OutT>
 __global__ void __launch_bounds__(256) attn_simt_tiles_kernel(AttnSimtArgs a) {
     const int n_qt = (a.T + 127) / 128;
-    const int tile = blockIdx.x % n_qt, bh = blockIdx.x / n_qt;
-    if (!a.tile_flags[(long long)bh * n_qt + tile]) return;
-    const int b = bh / a.Hg, h = a.h0 + (bh - b * a.Hg);
+    const int n = a.tile_list[0];
     const int warp = threadIdx.x >> 5;
-    for (int q = tile * 128 + warp; q < min(a.T, tile * 128 + 128); q += 8) attn_simt_query<DPL, OutT>(a, b, h, q);
+    for (int e = blockIdx.x; e < n; e += gridDim.x) {
+        const int t = a.tile_list[1 + e];
+        const int tile = t % n_qt, bh = t / n_qt;
+        const int b = bh / a.Hg, h = a.h0 + (bh - b * a.Hg);
+        for (int q = tile * 128 + warp; q < min(a.T, tile * 128 + 128); q += 8) attn_simt_query<DPL, OutT>(a, b, h, q);
+    }
 }
 
 template <int DPL, class OutT>
@@ -224,9 +230,9 @@ __device__ void attn_simt_query(const AttnSimtArgs &a, int b, int h, int q) {
 
 template <class OutT>
 static void launch_attn_simt_t(const AttnSimtArgs &a, cudaStream_t st) {
-    ProfScope ps(a.tile_flags ? "attn_simt_fallback" : "attn_simt", st);
-    if (a.tile_flags) {
-        const unsigned grid = (unsigned)((long long)a.B * a.Hg * ((a.T + 127) / 128));
+    ProfScope ps(a.tile_list ? "attn_simt_fallback" : "attn_simt", st);
+    if (a.tile_list) {
+        const unsigned grid = (unsigned)std::min<long long>(256, (long long)a.B * a.Hg * ((a.T + 127) / 128));
         if (a.hd <= 32) attn_simt_tiles_kernel<1, OutT><<<grid, 256, 0, st>>>(a);
         else if (a.hd <= 64) attn_simt_tiles_kernel<2, OutT><<<grid, 256, 0, st>>>(a);
         else if (a.hd <= 128) attn_simt_tiles_kernel<4, OutT><<<grid, 256, 0, st>>>(a);
@@ -249,15 +255,15 @@ void launch_attn_simt(const WbSeqView &sv, const float *content, int C, float co
 
 void launch_attn_simt_fallback_bf16(const WbSeqView &sv, const float *content, int C, float content_scale,
                                     const float *harmonic_n, int B, int H, int T, int hd, __nv_bfloat16 *o,
-                                    const int *tile_flags, int h0, int Hg, cudaStream_t st) {
-    AttnSimtArgs a{sv, content, C, content_scale, harmonic_n, B, H, T, hd, o, nullptr, tile_flags, h0, Hg};
+                                    const int *tile_list, int h0, int Hg, cudaStream_t st) {
+    AttnSimtArgs a{sv, content, C, content_scale, harmonic_n, B, H, T, hd, o, nullptr, tile_list, h0, Hg};
     launch_attn_simt_t<__nv_bfloat16>(a, st);
 }
 
 void launch_attn_simt_fallback_f32(const WbSeqView &sv, const float *content, int C, float content_scale,
                                    const float *harmonic_n, int B, int H, int T, int hd, float *o,
-                                   const int *tile_flags, int h0, int Hg, cudaStream_t st) {
-    AttnSimtArgs a{sv, content, C, content_scale, harmonic_n, B, H, T, hd, o, nullptr, tile_flags, h0, Hg};
+                                   const int *tile_list, int h0, int Hg, cudaStream_t st) {
+    AttnSimtArgs a{sv, content, C, content_scale, harmonic_n, B, H, T, hd, o, nullptr, tile_list, h0, Hg};
     launch_attn_simt_t<float>(a, st);
 }
 

@@ -303,7 +303,7 @@ struct AttnTcArgs {
     WbSeqView sv;               // fp32 values for the previous-position term
     void *o;                    // [B*T][E], bf16 (narrow) or fp32 (wide)
     int E;
-    int *tile_flags;            // [BH][n_qt]
+    int *tile_list;             // [0] = count, then flagged tiles bh * n_qt + qt
     uint32_t *dev_err;
 };
 
@@ -463,7 +463,10 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
             att_wait(qbar, 0, abort_flag);
             for (int j = 0; j < pre; j++) att_wait(kvfull + j, 0, abort_flag);
         }
-        if (tid == 0) a.tile_flags[(long long)bh * a.n_qt + qt] = 1;
+        if (tid == 0) {
+            const int e = atomicAdd(a.tile_list, 1);
+            a.tile_list[1 + e] = bh * a.n_qt + qt;
+        }
         ptx::tc_fence_before();
         __syncthreads();
         if (warp == ATT_SOFTMAX_WARPS) ptx::tmem_dealloc(tmem, 512);
@@ -884,7 +887,7 @@ static CoreLayout core_layout(const TcLayerWeights &t, int B, int T, size_t off,
     c.sp = cv.take<float>(BH * T);
     c.cn = cv.take<float>(BH * T);
     c.cm = cv.take<unsigned int>(BH);
-    c.fl = cv.take<int>(BH * n_qt);
+    c.fl = cv.take<int>(1 + BH * n_qt);
     c.o = t.wide ? cv.take<float>(R * t.E) : cv.take<__nv_bfloat16>(R * t.E);
     c.end = cv.off;
     return c;
@@ -969,7 +972,7 @@ static int tc_attention_core(const TcLayerWeights &t, const WbSeqView &sv, const
     unsigned int *cm = (unsigned int *)(w + lay.cm);
     int *fl = (int *)(w + lay.fl);
     if (cudaMemsetAsync(cm, 0, BH * sizeof(unsigned int), st) != cudaSuccess ||
-        cudaMemsetAsync(fl, 0, BH * n_qt * sizeof(int), st) != cudaSuccess) {
+        cudaMemsetAsync(fl, 0, sizeof(int), st) != cudaSuccess) {
         *msg = "cudaMemsetAsync failed";
         return WB_ECUDA;
     }
