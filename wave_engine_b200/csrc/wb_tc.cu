@@ -3,30 +3,31 @@
 // Wave attention scores are cos(n*(theta_q - theta_k)) + c_q.c_k/4 over
 // keys whose phase bucket is within one of the query's (src/common/attn.rs
 // :185-224).  By cos(a-b) = cos a cos b + sin a sin b the score is a dot
-// product of two 32-wide feature rows, so S = Qf Kf^T runs on tcgen05:
+// product of two feature rows, so S = Qf Kf^T runs on tcgen05.  Feature
+// columns (bf16):
 //
-//   cols  0..5   cos/sin(n theta) as a bf16 hi/lo split:
-//                Q = [cH, cL, cH, sH, sL, sH], K = [cH, cH, cL, sH, sH, sL]
-//                (products hi*hi + lo*hi + hi*lo: ~2^-16 relative error)
-//   cols  6..21  content: Q = c_q/4, K = c_k (bf16)
-//   cols 22..29  bucket mask: Q = 0 for the 3 allowed buckets, -512 for
-//                the other 5; K = one-hot of the key's bucket.  A masked
-//                key's score is pushed to about -512 and its exp is 0.
-//   cols 30..31  zero
+//   FW = 16 (no content: the serve prefill, --freeze-ode):
+//     0..5    cos/sin(n theta) as a bf16 hi/lo split:
+//             Q = [cH, cL, cH, sH, sL, sH], K = [cH, cH, cL, sH, sH, sL]
+//             (products hi*hi + lo*hi + hi*lo: ~2^-16 relative error)
+//     6..13   bucket mask: Q = 0 for the 3 allowed buckets, -512 for the
+//             other 5; K = one-hot of the key's bucket.  A masked key's
+//             score is pushed to about -512 and its exp is 0.
+//     14..15  zero
+//   FW = 64 (content): cos/sin at 0..5, content as hi/lo triples
+//     (Q = [qH, qL, qH] of c_q/4, K = [kH, kH, kL] of c_k) at 6..53, bucket
+//     mask at 54..61, zero at 62..63.
 //
-// Split precision (the default, "wide" in the code): 64 feature columns
-// with the content as a bf16 hi/lo split as well (cols 6..53, bucket mask at
-// 54..61), values as a bf16 hi/lo pair (two PV MMAs), an fp32 merged output
-// and a tf32 out_proj.  Single bf16 features/values/output (32 columns, the
-// layout above) keep ~3x less headroom: with the reference's own uniform
-// init (src/common/wave_model.rs:39-46) they exceed a 2e-3 max-abs error at
-// every model size, so that mode is only selectable for experiments.
+// Values enter PV as a bf16 hi + lo pair (two MMAs into one fp32
+// accumulator), the merged output is fp32 and out_proj is tf32.  Single
+// bf16 features/values exceed a 2e-3 max-abs error with the reference's own
+// uniform init (src/common/wave_model.rs:39-46) at every model size.
 //
 // Softmax needs no running max: every score is bounded by
 // 1 + |c_q| max_k|c_k| / 4 and the self score 1 + |c_q|^2/4 is always
 // present, so exp(s - s_self) neither overflows nor loses the row as long
 // as |c_q| (max|c_k| - |c_q|) / 4 <= 64.  Query tiles where that bound fails
-// are flagged and recomputed by the fp32 SIMT kernel.  The reference's
+// are listed and recomputed by the fp32 SIMT kernel.  The reference's
 // "always score the previous position" rule (attn.rs:212-221) is a single
 // extra term per query, added exactly in the epilogue when the previous
 // key is bucket-masked.
@@ -36,12 +37,13 @@
 
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdlib>
 
 namespace wb {
 
-static constexpr int QT = 128;      // queries per CTA (TMEM lanes)
+static constexpr int QT = 128;      // queries per work item (TMEM lanes)
 static constexpr int KT = 128;      // keys per tile
 static constexpr float MASK_BIAS = -512.0f;
 static constexpr float BOUND_LIMIT = 64.0f;
@@ -81,7 +83,7 @@ static int make_tmap(CUtensorMap *m, const void *base, CUtensorMapDataType dt, i
 }
 
 // ---------------------------------------------------------------------------
-// Feature pre-pass: one thread per (b, h, t).
+// Feature pre-pass.
 // ---------------------------------------------------------------------------
 struct FeatArgs {
     WbSeqView sv;
@@ -92,7 +94,7 @@ struct FeatArgs {
     int B, H, T, hd, hdp;
     int Hg, h0;                   // heads computed: h0 .. h0 + Hg - 1 (rows bh = b * Hg + (h - h0))
     __nv_bfloat16 *qf, *kf;       // [BH][T][FW]
-    __nv_bfloat16 *vh, *vl;       // [BH][T][hdp] value hi / lo (lo only in wide mode)
+    __nv_bfloat16 *vh, *vl;       // [BH][T][hdp] value hi / lo
     float *m0, *sprev, *cnorm;    // [BH][T]
     unsigned int *cmax;           // [BH], float bits
 };
@@ -107,19 +109,20 @@ __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(_
 // i = bh * T + t (8 warps per CTA).  Lane l owns row i0 + l for the per-row
 // quantities (phase, bucket, content, self score, previous-position term);
 // its Q and K feature rows (FW bf16 each) are built in a per-warp shared
-// buffer (rows padded to 33 words: conflict-free) and leave as one
+// buffer (rows padded by one word: conflict-free) and leave as one
 // contiguous block of 32 rows (lanes along the words).  Value rows are
-// converted with the lanes along the row (VC floats per lane, 8 rows of
-// loads in flight).  The previous position's phase, bucket and content come
-// from the neighbouring lane (lane 0 loads them).
+// converted with the lanes along the row (8 rows of loads in flight).  The
+// previous position's phase, bucket and content come from the neighbouring
+// lane (lane 0 loads them).
 static constexpr int FEAT_WARPS = 8;
 
-template <bool WIDE>
+template <int FW>
 __global__ void __launch_bounds__(FEAT_WARPS * 32) feat_kernel(FeatArgs a) {
-    constexpr int FW = WIDE ? 64 : 32;        // feature width
-    constexpr int BB = WIDE ? 54 : 22;        // first bucket column
+    static_assert(FW == 16 || FW == 64, "feature width 16 (no content) or 64 (content)");
+    constexpr int BB = FW == 64 ? 54 : 6;     // first bucket column
     constexpr int FWW = FW / 2;               // 32-bit words per feature row
     constexpr int RS = FWW + 1;               // padded row stride (words)
+    constexpr int NC = FW == 64 ? 16 : 0;     // content dims carried
     __shared__ uint32_t fbuf[FEAT_WARPS][32 * RS];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const long long BH = (long long)a.B * a.Hg, total = BH * a.T;
@@ -134,16 +137,16 @@ __global__ void __launch_bounds__(FEAT_WARPS * 32) feat_kernel(FeatArgs a) {
     const float th = a.sv.theta[base + t];
     const int bk = a.sv.bucket[base + t];
     const float n = a.hn[h];
-    const int C = a.content ? a.C : 0;
-    float c[16];
+    const int C = (NC && a.content) ? a.C : 0;
+    float c[NC > 0 ? NC : 1];
     {
         const float *cr = C ? a.content + ((long long)b * a.T + t) * ((long long)a.H * C) + (long long)h * C : nullptr;
 #pragma unroll
-        for (int d = 0; d < 16; d++) c[d] = (d < C) ? cr[d] : 0.0f;
+        for (int d = 0; d < NC; d++) c[d] = (d < C) ? cr[d] : 0.0f;
     }
     float c2 = 0.0f;
 #pragma unroll
-    for (int d = 0; d < 16; d++) c2 = fmaf(c[d], c[d], c2);
+    for (int d = 0; d < NC; d++) c2 = fmaf(c[d], c[d], c2);
     float sn, cs;
     sincosf(n * th, &sn, &cs);
     const float csh = bf16_round(cs), snh = bf16_round(sn);
@@ -166,14 +169,10 @@ __global__ void __launch_bounds__(FEAT_WARPS * 32) feat_kernel(FeatArgs a) {
         for (int u = 0; u < FW; u++) q[u] = 0.0f;
         q[0] = csh; q[1] = csl; q[2] = csh; q[3] = snh; q[4] = snl; q[5] = snh;
 #pragma unroll
-        for (int d = 0; d < 16; d++) {
+        for (int d = 0; d < NC; d++) {
             const float cq = c[d] * a.cscale;
-            if (WIDE) {
-                const float qh = bf16_round(cq);
-                q[6 + 3 * d] = qh; q[7 + 3 * d] = cq - qh; q[8 + 3 * d] = qh;
-            } else {
-                q[6 + d] = cq;
-            }
+            const float qh = bf16_round(cq);
+            q[6 + 3 * d] = qh; q[7 + 3 * d] = cq - qh; q[8 + 3 * d] = qh;
         }
 #pragma unroll
         for (int u = 0; u < 8; u++) q[BB + u] = ((allow >> u) & 1u) ? 0.0f : MASK_BIAS;
@@ -184,13 +183,9 @@ __global__ void __launch_bounds__(FEAT_WARPS * 32) feat_kernel(FeatArgs a) {
         for (int u = 0; u < FW; u++) q[u] = 0.0f;
         q[0] = csh; q[1] = csh; q[2] = csl; q[3] = snh; q[4] = snh; q[5] = snl;
 #pragma unroll
-        for (int d = 0; d < 16; d++) {
-            if (WIDE) {
-                const float kh = bf16_round(c[d]);
-                q[6 + 3 * d] = kh; q[7 + 3 * d] = kh; q[8 + 3 * d] = c[d] - kh;
-            } else {
-                q[6 + d] = c[d];
-            }
+        for (int d = 0; d < NC; d++) {
+            const float kh = bf16_round(c[d]);
+            q[6 + 3 * d] = kh; q[7 + 3 * d] = kh; q[8 + 3 * d] = c[d] - kh;
         }
 #pragma unroll
         for (int u = 0; u < 8; u++) q[BB + u] = (bk == u) ? 1.0f : 0.0f;
@@ -199,8 +194,7 @@ __global__ void __launch_bounds__(FEAT_WARPS * 32) feat_kernel(FeatArgs a) {
         emit(a.kf);
     }
 
-    // ---- values: hi (and lo in wide mode), zero padded to hdp; lanes
-    // along the row, VC floats per lane
+    // ---- values: hi and lo, zero padded to hdp; lanes along the row
     {
         const int hd = a.hd, hdp = a.hdp;
         const int nrows = (int)min(32LL, total - i0);
@@ -234,9 +228,8 @@ __global__ void __launch_bounds__(FEAT_WARPS * 32) feat_kernel(FeatArgs a) {
                     const float2 x2 = v[u][q];
                     const long long o = (i0 + j) * hdp + col;
                     *reinterpret_cast<uint32_t *>(a.vh + o) = pack_bf16(x2.x, x2.y);
-                    if (WIDE)
-                        *reinterpret_cast<uint32_t *>(a.vl + o) =
-                            pack_bf16(x2.x - bf16_round(x2.x), x2.y - bf16_round(x2.y));
+                    *reinterpret_cast<uint32_t *>(a.vl + o) =
+                        pack_bf16(x2.x - bf16_round(x2.x), x2.y - bf16_round(x2.y));
                 }
             }
         }
@@ -248,9 +241,9 @@ __global__ void __launch_bounds__(FEAT_WARPS * 32) feat_kernel(FeatArgs a) {
     // previous position: the lane below (same bh), lane 0 loads it
     float thp = __shfl_up_sync(0xffffffffu, th, 1);
     int bkp = __shfl_up_sync(0xffffffffu, bk, 1);
-    float cp[16];
+    float cp[NC > 0 ? NC : 1];
 #pragma unroll
-    for (int d = 0; d < 16; d++) cp[d] = __shfl_up_sync(0xffffffffu, c[d], 1);
+    for (int d = 0; d < NC; d++) cp[d] = __shfl_up_sync(0xffffffffu, c[d], 1);
     const int bh_below = __shfl_up_sync(0xffffffffu, bh, 1);
     if (t > 0 && (lane == 0 || bh_below != bh)) {
         thp = a.sv.theta[base + t - 1];
@@ -258,7 +251,7 @@ __global__ void __launch_bounds__(FEAT_WARPS * 32) feat_kernel(FeatArgs a) {
         const float *cr =
             C ? a.content + ((long long)b * a.T + t - 1) * ((long long)a.H * C) + (long long)h * C : nullptr;
 #pragma unroll
-        for (int d = 0; d < 16; d++) cp[d] = (d < C) ? cr[d] : 0.0f;
+        for (int d = 0; d < NC; d++) cp[d] = (d < C) ? cr[d] : 0.0f;
     }
     float sp = -INFINITY;
     if (t > 0 && !((allow >> bkp) & 1u)) {
@@ -266,7 +259,7 @@ __global__ void __launch_bounds__(FEAT_WARPS * 32) feat_kernel(FeatArgs a) {
         if (C) {
             float dot = 0.0f;
 #pragma unroll
-            for (int d = 0; d < 16; d++)
+            for (int d = 0; d < NC; d++)
                 if (d < C) dot = fmaf(c[d], cp[d], dot);
             sp += dot * a.cscale;
         }
@@ -277,33 +270,40 @@ __global__ void __launch_bounds__(FEAT_WARPS * 32) feat_kernel(FeatArgs a) {
         a.sprev[i] = sp;
     }
     // per-(b, h) maximum content norm: one atomic per run of equal bh
-    float mx = live ? cn : 0.0f;
-    const unsigned same = __match_any_sync(0xffffffffu, bh);
-    const int leader = __ffs(same) - 1;
+    if (NC) {
+        float mx = live ? cn : 0.0f;
+        const unsigned same = __match_any_sync(0xffffffffu, bh);
+        const int leader = __ffs(same) - 1;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        const float other = __shfl_xor_sync(0xffffffffu, mx, o);
-        const int obh = __shfl_xor_sync(0xffffffffu, bh, o);
-        if (obh == bh) mx = fmaxf(mx, other);
+        for (int o = 16; o > 0; o >>= 1) {
+            const float other = __shfl_xor_sync(0xffffffffu, mx, o);
+            const int obh = __shfl_xor_sync(0xffffffffu, bh, o);
+            if (obh == bh) mx = fmaxf(mx, other);
+        }
+        if (lane == leader && live) atomicMax(a.cmax + bh, __float_as_uint(mx));
     }
-    if (lane == leader && live) atomicMax(a.cmax + bh, __float_as_uint(mx));
 }
 
 // ---------------------------------------------------------------------------
-// Attention kernel: one CTA = 128 queries of one (b, h).  Per key tile j
-// (keys 128j..128j+127): S = Qf Kf_j^T (TMEM, fp32) -> P = exp(S - s_self)
-// (bf16, smem, masked causally on the diagonal tile) -> O += P V_j (TMEM,
-// fp32); roles below.
+// Attention core: a persistent, warp-specialised kernel.  One CTA per SM
+// walks work items -- 128 queries of one (sequence, head) -- handed out by
+// an atomic counter, in groups of ATT_GROUP (sequence, head) rows, the
+// longest query tiles of a group first (a group's key/value tiles stay in
+// L2 while its items read them).  Per key tile j of an item (keys
+// 128j..128j+127): S = Qf Kf_j^T (TMEM, fp32) -> P = exp(S - s_self) (bf16,
+// written back into the first half of each thread's own S columns) ->
+// O += P V_j (A from TMEM, V hi and lo from shared memory).
 // ---------------------------------------------------------------------------
 struct AttnTcArgs {
     int BH, H, T, hd, n_qt;     // BH = B * Hg rows
     int Hg, h0;                 // heads computed: h0 .. h0 + Hg - 1
+    int n_items;                // BH * n_qt
     const float *m0, *sprev, *cnorm;
     const unsigned int *cmax;
     WbSeqView sv;               // fp32 values for the previous-position term
-    void *o;                    // [B*T][E], bf16 (narrow) or fp32 (wide)
+    float *o;                   // [B*T][E] merged head outputs
     int E;
-    int *tile_list;             // [0] = count, then flagged tiles bh * n_qt + qt
+    int *sched;                 // [0] work counter, [1] fallback count, [2..] fallback tiles bh * n_qt + qt
     uint32_t *dev_err;
 };
 
@@ -313,30 +313,43 @@ __device__ __forceinline__ float fast_exp2(float x) {
     return y;
 }
 
-template <int HDP, bool WIDE>
-struct AttnSmem {
-    static constexpr int FW = WIDE ? 64 : 32;        // feature width
-    static constexpr int KVST = HDP == 64 ? 3 : 2;    // K/V ring stages
-    static constexpr int PB = HDP == 64 ? 2 : 1;      // P buffers
-    static constexpr int Q_BYTES = QT * FW * 2;      // 8 / 16 KB
-    static constexpr int K_BYTES = KT * FW * 2;      // 8 / 16 KB
-    static constexpr int VPART = KT * HDP * 2;       // one bf16 value tile: 16 / 32 KB
-    static constexpr int V_BYTES = VPART * (WIDE ? 2 : 1);  // hi (+ lo)
-    static constexpr int P_BYTES = QT * KT * 2;     // 32 KB
-    static constexpr int OFF_Q = 0;
-    static constexpr int OFF_K = OFF_Q + Q_BYTES;
-    static constexpr int OFF_V = OFF_K + KVST * K_BYTES;
-    static constexpr int OFF_P = OFF_V + KVST * V_BYTES;
-    static constexpr int OFF_BAR = OFF_P + PB * P_BYTES;
-    // barriers: q, kvfull[KVST], kvfree[KVST], sfull[2], pready[2], pfree[PB], ofull; then the TMEM slot
-    static constexpr int NBAR = 1 + 2 * KVST + 4 + PB + 1;
-    static constexpr int BYTES = OFF_BAR + NBAR * 8 + 16 + 1024;  // + alignment slack
-    static_assert(BYTES <= 232448, "attention shared memory above the 227 KB limit");
+static constexpr int ATT_SOFTMAX_WARPS = 16;  // four per TMEM lane group
+static constexpr int ATT_EPI_WARPS = 4;       // one per TMEM lane group
+static constexpr int ATT_W_PROD = ATT_SOFTMAX_WARPS + ATT_EPI_WARPS;  // TMA + work items
+static constexpr int ATT_W_MMA = ATT_W_PROD + 1;
+static constexpr int ATT_THREADS = (ATT_W_MMA + 1) * 32;              // 704
+static constexpr int ATT_GROUP = 16;          // (sequence, head) rows per item group
+static constexpr int ATT_SLOTS = 4;           // work-item descriptor ring
+
+// A published work item: its (sequence, head) row and query tile (bh < 0:
+// no more work) and the per-row fixed shift m0 and previous-position score.
+struct AttnItem {
+    int bh, qt, pad0, pad1;
+    float m0[QT];
+    float sp[QT];
 };
 
-static constexpr int ATT_SOFTMAX_WARPS = 16;                    // four per TMEM lane group
-static constexpr int ATT_THREADS = (ATT_SOFTMAX_WARPS + 2) * 32;  // + TMA loader warp + MMA warp
-static constexpr int ATT_GROUP = 16;                              // (sequence, head) rows per CTA group
+template <int HDP, int FW>
+struct AttnSmem {
+    static constexpr int ST = HDP == 128 ? 2 : (FW == 16 ? 4 : 3);  // K/V ring stages
+    static constexpr int Q_BYTES = QT * FW * 2;      // 4 / 16 KB
+    static constexpr int K_BYTES = KT * FW * 2;      // 4 / 16 KB
+    static constexpr int VPART = KT * HDP * 2;       // one bf16 value tile: 16 / 32 KB
+    static constexpr int V_BYTES = 2 * VPART;        // hi + lo
+    static constexpr int OFF_Q = 0;
+    static constexpr int OFF_K = OFF_Q + Q_BYTES;
+    static constexpr int OFF_V = OFF_K + ST * K_BYTES;
+    static constexpr int OFF_EPI = OFF_V + ST * V_BYTES;                 // epilogue staging, 32 x 33 floats per warp
+    static constexpr int OFF_SLOT = OFF_EPI + ATT_EPI_WARPS * 32 * 33 * 4;
+    static constexpr int OFF_LSUM = OFF_SLOT + ATT_SLOTS * (int)sizeof(AttnItem);  // [2][4][QT] row-sum partials
+    static constexpr int OFF_BAR = OFF_LSUM + 2 * 4 * QT * 4;
+    // barriers: qfull, qfree, kvfull[ST], kvfree[ST], sfull[2], pready[2],
+    // ofull[2], ofree[2], lready[2], itemfull[SLOTS], itemfree[SLOTS], mmadone
+    static constexpr int NBAR = 2 + 2 * ST + 10 + 2 * ATT_SLOTS + 1;
+    static constexpr int BYTES = OFF_BAR + NBAR * 8 + 16 + 1024;  // + TMEM slot, alignment slack
+    static_assert(BYTES <= 232448, "attention shared memory above the 227 KB limit");
+    static_assert(HDP * 2 + 256 <= 512, "TMEM: two S buffers and two O buffers");
+};
 
 // Bounded mbarrier wait that also gives up once another role has raised the
 // CTA's abort flag (so one timeout does not chain into one per barrier).
@@ -353,75 +366,59 @@ __device__ __forceinline__ bool att_wait(uint64_t *bar, uint32_t parity, volatil
     }
 }
 
-// Attention core, warp-specialised.  One CTA = 128 queries of one (b, h).
-//   warp 16 (lane 0): TMA -- Q once, then K/V tiles into a KVST-stage ring.
-//   warp 17 (lane 0): tcgen05.mma -- S_j = Qf Kf_j^T into TMEM buffer j & 1
-//     (two tiles ahead of the softmax), O += P_j V_j (value hi and lo).
-//   warps 0-15: softmax of S_j (four warps per TMEM lane group: warps w,
-//     w + 4, w + 8, w + 12 own the same 32 query rows, key columns 0-31,
-//     32-63, 64-95, 96-127),
-//     P_j = exp2 of the fixed shift in bf16 into shared-memory buffer j % PB;
-//     then the epilogue (O / l plus the exact previous-position term).
-// The S double buffer lets QK_{j+2} and PV_j run while the softmax works on
-// S_{j+1}.
-template <int HDP, bool WIDE>
+// Roles (704 threads):
+//   warps 0-15 (softmax): four per TMEM lane group (warps w, w+4, w+8, w+12
+//     own query rows 32(w&3)..+31, key columns 0-31, 32-63, 64-95, 96-127 of
+//     each S tile): P = exp2 of the fixed shift, causal mask on the diagonal
+//     tile, P (bf16) stored over the first 16 of the thread's own 32 S
+//     columns; the row-sum partials go to shared memory per item.
+//   warps 16-19 (epilogue): one per lane group: O / l plus the exact
+//     previous-position term, stored through per-warp staging -- item k's
+//     epilogue runs while the softmax warps work on item k+1 (O is double
+//     buffered in TMEM).
+//   warp 20 (producer): takes work items from the counter, tests the
+//     bounded-score condition (content only; failing tiles go to the
+//     fallback list), publishes the item (row, tile, m0 and previous-position
+//     scores of its 128 rows), then loads Q and the K/V tiles by TMA.
+//   warp 21 (MMA): lane 0 issues S_g = Qf Kf^T two tiles ahead of the
+//     softmax (S double buffered in TMEM) and O += P V (value hi and lo).
+// TMEM columns: S0 [0,128), S1 [128,256), O0 [256,256+HDP), O1 after it.
+template <int HDP, int FW>
 __global__ void __launch_bounds__(ATT_THREADS, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_vh, const __grid_constant__ CUtensorMap tm_vl,
                    AttnTcArgs a, int hdn) {
-    using L = AttnSmem<HDP, WIDE>;
-    constexpr int KVST = L::KVST, PB = L::PB;
+    using L = AttnSmem<HDP, FW>;
+    constexpr int ST = L::ST;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *bars = reinterpret_cast<uint64_t *>(sm + L::OFF_BAR);
-    uint64_t *qbar = bars;
-    uint64_t *kvfull = bars + 1;
-    uint64_t *kvfree = kvfull + KVST;
-    uint64_t *sfull = kvfree + KVST;  // [2]
-    uint64_t *pready = sfull + 2;     // [2]
-    uint64_t *pfree = pready + 2;     // [PB]
-    uint64_t *ofull = pfree + PB;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(ofull + 1);
+    uint64_t *qfull = bars, *qfree = bars + 1;
+    uint64_t *kvfull = bars + 2, *kvfree = kvfull + ST;
+    uint64_t *sfull = kvfree + ST, *pready = sfull + 2, *ofull = pready + 2, *ofree = ofull + 2;
+    uint64_t *lready = ofree + 2, *itemfull = lready + 2, *itemfree = itemfull + ATT_SLOTS;
+    uint64_t *mmadone = itemfree + ATT_SLOTS;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mmadone + 1);
+    AttnItem *slots = reinterpret_cast<AttnItem *>(sm + L::OFF_SLOT);
+    float *lsum = reinterpret_cast<float *>(sm + L::OFF_LSUM);
     __shared__ int s_abort;
     volatile int *abort_flag = &s_abort;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    // CTAs walk the (sequence, head) rows in groups of ATT_GROUP, the longest
-    // query tiles of a group first: a group's key/value tiles (a few MB)
-    // stay in L2 while all of its query tiles read them
-    const int per_grp = ATT_GROUP * a.n_qt;
-    const int grp = blockIdx.x / per_grp, rr = blockIdx.x - grp * per_grp;
-    const int gsz = min(ATT_GROUP, a.BH - grp * ATT_GROUP);
-    const int bh = grp * ATT_GROUP + rr % gsz;
-    const int qt = a.n_qt - 1 - rr / gsz;
-    const int b = bh / a.Hg, h = a.h0 + (bh - b * a.Hg);
-    const int q0 = qt * QT;
-    const bool softmax_warp = warp < ATT_SOFTMAX_WARPS;
-    const int row = tid & (QT - 1), quarter = (warp >> 2) & 3;  // softmax role: query row, key-column quarter
-    const int q = q0 + row;
-    const long long rq = (long long)bh * a.T + q;
-
-    // per-row inputs of the softmax roles, requested first: the fixed shift,
-    // the bounded-score test, the previous-position score and the row's
-    // value base in the cache view
-    float m0 = 0.0f, cn = 0.0f, cm = 0.0f, sp = -INFINITY;
-    long long vbase = 0;
-    if (softmax_warp && q < a.T) {
-        m0 = a.m0[rq];
-        sp = a.sprev[rq];
-        vbase = wb_slot_base(a.sv, b, h);
-        if (quarter == 0) {
-            cn = a.cnorm[rq];
-            cm = __uint_as_float(a.cmax[bh]);
-        }
-    }
     if (tid == 0) {
-        for (int i = 0; i < L::NBAR; i++)  // pready counts every softmax thread, the rest one arrival
-            ptx::mbar_init(bars + i, (bars + i == pready || bars + i == pready + 1) ? ATT_SOFTMAX_WARPS * 32 : 1);
+        for (int i = 0; i < L::NBAR; i++) {
+            uint64_t *bb = bars + i;
+            uint32_t cnt = 1;
+            if (bb == pready || bb == pready + 1 || bb == lready || bb == lready + 1) cnt = ATT_SOFTMAX_WARPS * 32;
+            else if (bb == ofree || bb == ofree + 1) cnt = ATT_EPI_WARPS * 32;
+            else if (bb >= itemfull && bb < itemfull + ATT_SLOTS) cnt = 32;
+            else if (bb >= itemfree && bb < itemfree + ATT_SLOTS) cnt = ATT_SOFTMAX_WARPS + ATT_EPI_WARPS + 1;
+            ptx::mbar_init(bb, cnt);
+        }
         ptx::fence_mbar_init();
         s_abort = 0;
     }
-    if (warp == ATT_SOFTMAX_WARPS) {
+    if (warp == ATT_W_MMA) {
         ptx::tmem_alloc(tmem_slot, 512);
         ptx::tmem_relinquish();
     }
@@ -429,272 +426,341 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     __syncthreads();
     ptx::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t O_t = tmem + 256;
-    const int n_kt = qt + 1;
-    constexpr uint32_t F_SW = WIDE ? ptx::UMMA_SW128 : ptx::UMMA_SW64;
-    constexpr uint32_t F_SBO = WIDE ? 1024 : 512;
-    auto load_kv = [&](int j) {
-        const int s = j % KVST;
-        ptx::mbar_arrive_expect_tx(kvfull + s, L::K_BYTES + L::V_BYTES);
-        ptx::tma_load_3d(sm + L::OFF_K + s * L::K_BYTES, &tm_k, kvfull + s, 0, j * KT, bh);
-        uint8_t *vst = sm + L::OFF_V + s * L::V_BYTES;
-#pragma unroll
-        for (int c = 0; c < HDP / 64; c++) {
-            ptx::tma_load_3d(vst + c * (KT * 128), &tm_vh, kvfull + s, c * 64, j * KT, bh);
-            if (WIDE) ptx::tma_load_3d(vst + L::VPART + c * (KT * 128), &tm_vl, kvfull + s, c * 64, j * KT, bh);
-        }
-    };
-    // Q and the first ring stages go out before the bounded-score test
-    const int pre = min(KVST, n_kt);
-    if (warp == ATT_SOFTMAX_WARPS && lane == 0) {
-        ptx::prefetch_tmap(&tm_q);
-        ptx::prefetch_tmap(&tm_k);
-        ptx::prefetch_tmap(&tm_vh);
-        if (WIDE) ptx::prefetch_tmap(&tm_vl);
-        ptx::mbar_arrive_expect_tx(qbar, L::Q_BYTES);
-        ptx::tma_load_3d(sm + L::OFF_Q, &tm_q, qbar, 0, q0, bh);
-        for (int j = 0; j < pre; j++) load_kv(j);
-    }
-    const bool violate = softmax_warp && quarter == 0 && q < a.T && 0.25f * cn * (cm - cn) > BOUND_LIMIT;
-    if (__syncthreads_or(violate)) {
-        // the tile goes to the fp32 fallback: the copies already issued land
-        // before the CTA leaves
-        if (warp == ATT_SOFTMAX_WARPS && lane == 0) {
-            att_wait(qbar, 0, abort_flag);
-            for (int j = 0; j < pre; j++) att_wait(kvfull + j, 0, abort_flag);
-        }
-        if (tid == 0) {
-            const int e = atomicAdd(a.tile_list, 1);
-            a.tile_list[1 + e] = bh * a.n_qt + qt;
-        }
-        ptx::tc_fence_before();
-        __syncthreads();
-        if (warp == ATT_SOFTMAX_WARPS) ptx::tmem_dealloc(tmem, 512);
-        return;
-    }
+    constexpr uint32_t F_SW = FW == 64 ? ptx::UMMA_SW128 : ptx::UMMA_SW32;
+    constexpr uint32_t F_SBO = FW == 64 ? 1024 : 256;  // 8 rows of the swizzle atom
 
-    if (warp == ATT_SOFTMAX_WARPS) {
-        // ---------------- TMA loader (stages from `pre` on)
+    if (warp == ATT_W_PROD) {
+        // ---------------- producer: work items, Q and K/V tiles
+        long long g = 0;  // global tile counter of this CTA
+        int k = 0;        // items published
+        const int per_grp = ATT_GROUP * a.n_qt;
         if (lane == 0) {
-            for (int j = pre; j < n_kt; j++) {
-                const int s = j % KVST;
-                if (!att_wait(kvfree + s, ((j / KVST) - 1) & 1, abort_flag)) {
-                    atomicOr(a.dev_err, WB_DERR_TIMEOUT_MMA);
-                    break;
-                }
-                load_kv(j);
-            }
+            ptx::prefetch_tmap(&tm_q);
+            ptx::prefetch_tmap(&tm_k);
+            ptx::prefetch_tmap(&tm_vh);
+            ptx::prefetch_tmap(&tm_vl);
         }
-    } else if (warp == ATT_SOFTMAX_WARPS + 1) {
+        for (;;) {
+            int item = 0;
+            if (lane == 0) item = atomicAdd(a.sched, 1);
+            item = __shfl_sync(0xffffffffu, item, 0);
+            const bool end = item >= a.n_items;
+            int bh = -1, qt = 0;
+            if (!end) {
+                const int grp = item / per_grp, rr = item - grp * per_grp;
+                const int gsz = min(ATT_GROUP, a.BH - grp * ATT_GROUP);
+                bh = grp * ATT_GROUP + rr % gsz;
+                qt = a.n_qt - 1 - rr / gsz;
+                if (FW == 64) {
+                    // bounded-score test of the tile's rows (content only)
+                    const float cm = __uint_as_float(__ldg(a.cmax + bh));
+                    bool violate = false;
+#pragma unroll
+                    for (int u = 0; u < 4; u++) {
+                        const int q = qt * QT + u * 32 + lane;
+                        if (q < a.T) {
+                            const float cn = __ldg(a.cnorm + (long long)bh * a.T + q);
+                            violate |= 0.25f * cn * (cm - cn) > BOUND_LIMIT;
+                        }
+                    }
+                    if (__any_sync(0xffffffffu, violate)) {
+                        if (lane == 0) {
+                            const int e = atomicAdd(a.sched + 1, 1);
+                            a.sched[2 + e] = bh * a.n_qt + qt;
+                        }
+                        continue;
+                    }
+                }
+            }
+            const int s = k % ATT_SLOTS;
+            if (k >= ATT_SLOTS && !att_wait(itemfree + s, ((k / ATT_SLOTS) - 1) & 1, abort_flag)) {
+                if (lane == 0) atomicOr(a.dev_err, WB_DERR_TIMEOUT_TMA);
+                break;
+            }
+            AttnItem *it = slots + s;
+            if (lane == 0) {
+                it->bh = bh;
+                it->qt = qt;
+            }
+            if (!end) {
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    const int r = u * 32 + lane, q = qt * QT + r;
+                    const long long rq = (long long)bh * a.T + q;
+                    it->m0[r] = q < a.T ? __ldg(a.m0 + rq) : 0.0f;
+                    it->sp[r] = q < a.T ? __ldg(a.sprev + rq) : -INFINITY;
+                }
+            }
+            ptx::mbar_arrive(itemfull + s);  // every lane: its writes are released
+            k++;
+            if (end) break;
+            if (lane == 0) {
+                bool ok = true;
+                if (k > 1 && !att_wait(qfree, (k - 2) & 1, abort_flag)) ok = false;
+                if (ok) {
+                    ptx::mbar_arrive_expect_tx(qfull, L::Q_BYTES);
+                    ptx::tma_load_3d(sm + L::OFF_Q, &tm_q, qfull, 0, qt * QT, bh);
+                }
+                for (int j = 0; ok && j <= qt; j++, g++) {
+                    const int st = (int)(g % ST);
+                    const long long f = g / ST;
+                    if (f >= 1 && !att_wait(kvfree + st, (uint32_t)((f - 1) & 1), abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    ptx::mbar_arrive_expect_tx(kvfull + st, L::K_BYTES + L::V_BYTES);
+                    ptx::tma_load_3d(sm + L::OFF_K + st * L::K_BYTES, &tm_k, kvfull + st, 0, j * KT, bh);
+                    uint8_t *vst = sm + L::OFF_V + st * L::V_BYTES;
+#pragma unroll
+                    for (int c = 0; c < HDP / 64; c++) {
+                        ptx::tma_load_3d(vst + c * (KT * 128), &tm_vh, kvfull + st, c * 64, j * KT, bh);
+                        ptx::tma_load_3d(vst + L::VPART + c * (KT * 128), &tm_vl, kvfull + st, c * 64, j * KT, bh);
+                    }
+                }
+                if (!ok) atomicOr(a.dev_err, WB_DERR_TIMEOUT_TMA);
+            }
+            g = __shfl_sync(0xffffffffu, g, 0);
+            if (*abort_flag) break;
+        }
+        // copies still in flight (only after an abort) land before the CTA
+        // leaves: wait for the last fill of every stage and the last Q
+        if (lane == 0 && *abort_flag) {
+            for (long long gg = g - 1; gg >= 0 && gg >= g - ST; gg--)
+                ptx::mbar_wait(kvfull + (gg % ST), (uint32_t)((gg / ST) & 1), 200000000LL);
+            if (k > 1) ptx::mbar_wait(qfull, (k - 2) & 1, 200000000LL);
+        }
+    } else if (warp == ATT_W_MMA) {
         // ---------------- MMA issuer
         if (lane == 0) {
             constexpr uint32_t IDESC_QK = ptx::idesc_bf16(128, 128, 0, 0);
             const uint32_t idesc_pv = ptx::idesc_bf16(128, hdn, 0, 1);
             const uint32_t sQ = ptx::smem_u32(sm + L::OFF_Q);
-            bool ok = att_wait(qbar, 0, abort_flag);
-            auto qk = [&](int j) {
-                const int s = j % KVST;
-                if (!att_wait(kvfull + s, (j / KVST) & 1, abort_flag)) return false;
+            int kq = 0, jq = 0;                // next QK: item, tile
+            long long gq = 0, gp = 0;          // next QK / PV global tile
+            int kp = 0, jp = 0;                // next PV: item, tile
+            bool qk_end = false, ok = true;
+            auto issue_qk = [&]() {
+                if (qk_end || !ok) return;
+                if (jq == 0) {
+                    if (!att_wait(itemfull + (kq % ATT_SLOTS), (kq / ATT_SLOTS) & 1, abort_flag)) {
+                        ok = false;
+                        return;
+                    }
+                    const AttnItem *it = slots + (kq % ATT_SLOTS);
+                    if (it->bh < 0) {
+                        qk_end = true;
+                        // the end marker's slot is never returned: nobody reads it again
+                        return;
+                    }
+                    if (!att_wait(qfull, kq & 1, abort_flag)) {
+                        ok = false;
+                        return;
+                    }
+                }
+                const int st = (int)(gq % ST);
+                if (!att_wait(kvfull + st, (uint32_t)((gq / ST) & 1), abort_flag)) {
+                    ok = false;
+                    return;
+                }
                 ptx::tc_fence_after();
-                const uint32_t sK = ptx::smem_u32(sm + L::OFF_K + s * L::K_BYTES);
-                const uint32_t S_t = tmem + (uint32_t)((j & 1) * 128);
+                const uint32_t sK = ptx::smem_u32(sm + L::OFF_K + st * L::K_BYTES);
+                const uint32_t S_t = tmem + (uint32_t)((gq & 1) * 128);
 #pragma unroll
-                for (int kk = 0; kk < L::FW / 16; kk++) {
+                for (int kk = 0; kk < FW / 16; kk++) {
                     const uint64_t ad = ptx::smem_desc(sQ + kk * 32, 16, F_SBO, F_SW);
                     const uint64_t bd = ptx::smem_desc(sK + kk * 32, 16, F_SBO, F_SW);
                     ptx::mma_bf16(S_t, ad, bd, IDESC_QK, kk > 0);
                 }
-                ptx::mma_commit(sfull + (j & 1));
-                return true;
+                ptx::mma_commit(sfull + (gq & 1));
+                gq++;
+                if (++jq == slots[kq % ATT_SLOTS].qt + 1) {
+                    ptx::mma_commit(qfree);  // Q of item kq no longer read
+                    kq++;
+                    jq = 0;
+                }
             };
-            if (ok) ok = qk(0);
-            if (ok && n_kt > 1) ok = qk(1);
-            for (int j = 0; ok && j < n_kt; j++) {
-                if (!att_wait(pready + (j & 1), (j >> 1) & 1, abort_flag)) {
+            issue_qk();
+            issue_qk();
+            while (ok && gp < gq) {
+                const int sl = kp % ATT_SLOTS;
+                const uint32_t O_t = tmem + 256 + (uint32_t)((kp & 1) * HDP);
+                if (jp == 0 && kp >= 2 && !att_wait(ofree + (kp & 1), ((kp - 2) >> 1) & 1, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                if (!att_wait(pready + (gp & 1), (uint32_t)((gp >> 1) & 1), abort_flag)) {
                     ok = false;
                     break;
                 }
                 ptx::tc_fence_after();
-                const uint32_t sP = ptx::smem_u32(sm + L::OFF_P + (j % PB) * L::P_BYTES);
-                const uint32_t sV = ptx::smem_u32(sm + L::OFF_V + (j % KVST) * L::V_BYTES);
+                const uint32_t P_t = tmem + (uint32_t)((gp & 1) * 128);
+                const uint32_t sV = ptx::smem_u32(sm + L::OFF_V + (int)(gp % ST) * L::V_BYTES);
 #pragma unroll
                 for (int kk = 0; kk < KT / 16; kk++) {
-                    const uint64_t ad = ptx::smem_desc(sP + (kk >> 2) * (QT * 128) + (kk & 3) * 32, 16, 1024,
-                                                       ptx::UMMA_SW128);
-                    const uint64_t bd = ptx::smem_desc(sV + kk * 2048, KT * 128, 1024, ptx::UMMA_SW128);
-                    ptx::mma_bf16(O_t, ad, bd, idesc_pv, (j > 0 || kk > 0));
-                    if (WIDE) {
-                        const uint64_t bl =
-                            ptx::smem_desc(sV + L::VPART + kk * 2048, KT * 128, 1024, ptx::UMMA_SW128);
-                        ptx::mma_bf16(O_t, ad, bl, idesc_pv, 1);
-                    }
+                    // keys 16kk..16kk+15: quarter kk/2 of the tile, packed two per column
+                    const uint32_t a_t = P_t + (uint32_t)(32 * (kk >> 1) + 8 * (kk & 1));
+                    const uint64_t bh_d = ptx::smem_desc(sV + kk * 2048, KT * 128, 1024, ptx::UMMA_SW128);
+                    const uint64_t bl_d = ptx::smem_desc(sV + L::VPART + kk * 2048, KT * 128, 1024, ptx::UMMA_SW128);
+                    ptx::mma_bf16_ta(O_t, a_t, bh_d, idesc_pv, (jp > 0 || kk > 0));
+                    ptx::mma_bf16_ta(O_t, a_t, bl_d, idesc_pv, 1);
                 }
-                ptx::mma_commit(kvfree + (j % KVST));
-                ptx::mma_commit(pfree + (j % PB));
-                if (j + 2 < n_kt) ok = qk(j + 2);
+                ptx::mma_commit(kvfree + (int)(gp % ST));
+                gp++;
+                if (++jp == slots[sl].qt + 1) {
+                    ptx::mma_commit(ofull + (kp & 1));
+                    ptx::mbar_arrive(itemfree + sl);
+                    kp++;
+                    jp = 0;
+                }
+                issue_qk();
             }
-            if (ok) ptx::mma_commit(ofull);
-            else atomicOr(a.dev_err, WB_DERR_TIMEOUT_TMA);
+            if (!ok) atomicOr(a.dev_err, WB_DERR_TIMEOUT_MMA);
+            // every MMA has completed before TMEM is released
+            ptx::mma_commit(mmadone);
+            ptx::mbar_wait(mmadone, 0, 200000000LL);
         }
-    } else {
-        // ---------------- softmax (warps 0-15)
+        __syncwarp();
+    } else if (warp < ATT_SOFTMAX_WARPS) {
+        // ---------------- softmax
         const float LOG2E = 1.4426950408889634f;
-        const float nm0 = -m0 * LOG2E;
+        const int row = tid & (QT - 1), quarter = (warp >> 2) & 3;
         const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-        float l = 0.0f;
-        bool ok = true;
-        for (int j = 0; j < n_kt; j++) {
-            if (!att_wait(sfull + (j & 1), (j >> 1) & 1, abort_flag)) {
+        const int kbase = quarter * 32;
+        long long g = 0;
+        for (int k = 0;; k++) {
+            const int sl = k % ATT_SLOTS;
+            if (!att_wait(itemfull + sl, (k / ATT_SLOTS) & 1, abort_flag)) {
                 atomicOr(a.dev_err, WB_DERR_TIMEOUT_SOFTMAX);
-                ok = false;
                 break;
             }
-            ptx::tc_fence_after();
-            const bool diag = (j == qt);
-            const uint32_t S_t = tmem + (uint32_t)((j & 1) * 128) + lane_base + quarter * 32;
-            uint32_t pk[16];
-            {
+            const AttnItem *it = slots + sl;
+            const int bh = it->bh, qt = it->qt;
+            const float nm0 = -it->m0[row] * LOG2E;
+            const float sp = it->sp[row];
+            __syncwarp();
+            if (bh < 0) break;
+            if (lane == 0) ptx::mbar_arrive(itemfree + sl);
+            // the previous position's weight when its bucket is masked
+            // (attn.rs:212-221): it replaces the ~0 of key q-1's column, in
+            // the diagonal tile or, for the tile's first row, in column 127
+            // of the tile before
+            const float ep = sp > -INFINITY ? fast_exp2(fmaf(sp, LOG2E, nm0)) : 0.0f;
+            float l = 0.0f;
+            bool ok = true;
+            for (int j = 0; j <= qt; j++, g++) {
+                if (!att_wait(sfull + (g & 1), (uint32_t)((g >> 1) & 1), abort_flag)) {
+                    atomicOr(a.dev_err, WB_DERR_TIMEOUT_SOFTMAX);
+                    ok = false;
+                    break;
+                }
+                ptx::tc_fence_after();
+                const uint32_t S_t = tmem + (uint32_t)((g & 1) * 128) + lane_base + kbase;
                 uint32_t r[32];
                 ptx::tmem_ld32(S_t, r);
                 ptx::tmem_ld_wait();
-                const int kbase = quarter * 32;
-#pragma unroll
-                for (int i = 0; i < 16; i++) {
-                    float e0 = fast_exp2(fmaf(__uint_as_float(r[2 * i]), LOG2E, nm0));
-                    float e1 = fast_exp2(fmaf(__uint_as_float(r[2 * i + 1]), LOG2E, nm0));
-                    if (diag) {
-                        if (kbase + 2 * i > row) e0 = 0.0f;
-                        if (kbase + 2 * i + 1 > row) e1 = 0.0f;
-                    }
-                    l += e0 + e1;
-                    pk[i] = pack_bf16(e0, e1);
+                uint32_t pk[16];
+                const bool diag = (j == qt);
+                int pcol = -1;
+                if (ep > 0.0f) {
+                    if (diag && row >= 1 && ((row - 1) >> 5) == quarter) pcol = (row - 1) & 31;
+                    else if (j + 1 == qt && row == 0 && quarter == 3) pcol = 31;
                 }
+                if (__any_sync(0xffffffffu, diag || pcol >= 0)) {
+#pragma unroll
+                    for (int i = 0; i < 16; i++) {
+                        float e0 = fast_exp2(fmaf(__uint_as_float(r[2 * i]), LOG2E, nm0));
+                        float e1 = fast_exp2(fmaf(__uint_as_float(r[2 * i + 1]), LOG2E, nm0));
+                        if (diag) {
+                            if (kbase + 2 * i > row) e0 = 0.0f;
+                            if (kbase + 2 * i + 1 > row) e1 = 0.0f;
+                        }
+                        if (2 * i == pcol) e0 = ep;
+                        if (2 * i + 1 == pcol) e1 = ep;
+                        l += e0 + e1;
+                        pk[i] = pack_bf16(e0, e1);
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 16; i++) {
+                        const float e0 = fast_exp2(fmaf(__uint_as_float(r[2 * i]), LOG2E, nm0));
+                        const float e1 = fast_exp2(fmaf(__uint_as_float(r[2 * i + 1]), LOG2E, nm0));
+                        l += e0 + e1;
+                        pk[i] = pack_bf16(e0, e1);
+                    }
+                }
+                ptx::tmem_st16(S_t, pk);
+                ptx::tmem_st_wait();
+                ptx::tc_fence_before();
+                ptx::mbar_arrive(pready + (g & 1));
             }
-            // P buffer j % PB is free once PV_{j - PB} has completed
-            if (j >= PB && !att_wait(pfree + (j % PB), ((j / PB) - 1) & 1, abort_flag)) {
-                atomicOr(a.dev_err, WB_DERR_TIMEOUT_MMA);
-                ok = false;
+            if (!ok) break;
+            // the item's row-sum partials; the buffer of item k-2 must have
+            // been read by its epilogue
+            if (k >= 2 && !att_wait(ofree + (k & 1), ((k - 2) >> 1) & 1, abort_flag)) {
+                atomicOr(a.dev_err, WB_DERR_TIMEOUT_SOFTMAX);
                 break;
             }
-            // keys 64h..64h+63 of a row are one 128-byte swizzled row of
-            // region h; this quarter's 32 keys are chunks (quarter & 1)*4 ..
-            uint8_t *prow = sm + L::OFF_P + (j % PB) * L::P_BYTES + (quarter >> 1) * (QT * 128) + (row >> 3) * 1024 +
-                            (row & 7) * 128;
-#pragma unroll
-            for (int u = 0; u < 4; u++) {
-                const int ch = ((quarter & 1) * 4 + u) ^ (row & 7);
-                *reinterpret_cast<uint4 *>(prow + ch * 16) = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
-            }
-            ptx::fence_proxy_async_smem();
-            ptx::tc_fence_before();
-            ptx::mbar_arrive(pready + (j & 1));
+            lsum[((k & 1) * 4 + quarter) * QT + row] = l;
+            ptx::mbar_arrive(lready + (k & 1));
         }
-
-        // ---- epilogue: O / l plus the previous-position term; each thread
-        // its row and a quarter of the O columns.  The previous value row's loads
-        // go out before the wait for the last PV.
-        constexpr int HC = HDP / 4;  // O columns per thread
-        const int d0 = quarter * HC;
-        float vprev[HC];
-        const bool has_prev = q < a.T && sp > -INFINITY;
-        if (has_prev) {
-            const float *vp = a.sv.v + (vbase + q - 1) * a.hd + d0;
-            if ((a.hd & 3) == 0 && d0 + HC <= a.hd) {
-#pragma unroll
-                for (int u = 0; u < HC / 4; u++) {
-                    const float4 t4 = __ldg(reinterpret_cast<const float4 *>(vp) + u);
-                    vprev[4 * u] = t4.x;
-                    vprev[4 * u + 1] = t4.y;
-                    vprev[4 * u + 2] = t4.z;
-                    vprev[4 * u + 3] = t4.w;
-                }
-            } else {
-#pragma unroll
-                for (int d = 0; d < HC; d++) vprev[d] = d0 + d < a.hd ? __ldg(vp + d) : 0.0f;
+    } else {
+        // ---------------- epilogue (warps 16-19): O / l
+        const int ew = warp - ATT_SOFTMAX_WARPS;  // lane group
+        const int row = ew * 32 + lane;
+        const uint32_t lane_base = (uint32_t)(ew * 32) << 16;
+        float *buf = reinterpret_cast<float *>(sm + L::OFF_EPI) + ew * 32 * 33;
+        for (int k = 0;; k++) {
+            const int sl = k % ATT_SLOTS;
+            if (!att_wait(itemfull + sl, (k / ATT_SLOTS) & 1, abort_flag)) {
+                atomicOr(a.dev_err, WB_DERR_TIMEOUT_SOFTMAX);
+                break;
             }
-        }
-        bool done = ok && att_wait(ofull, 0, abort_flag);
-        if (ok && !done) atomicOr(a.dev_err, WB_DERR_TIMEOUT_MMA);
-        // the row's four partial sums meet in the P buffers (every MMA has
-        // completed once ofull has)
-        float *lsum4 = reinterpret_cast<float *>(sm + L::OFF_P);
-        lsum4[quarter * QT + row] = l;
-        asm volatile("bar.sync 1, %0;" ::"n"(ATT_SOFTMAX_WARPS * 32) : "memory");
-        ptx::tc_fence_after();
-        if (done) {
-            float lt = (lsum4[row] + lsum4[QT + row]) + (lsum4[2 * QT + row] + lsum4[3 * QT + row]);
-            float o[HC];
-            if constexpr (HC == 16) {
-                uint32_t r[16];
-                ptx::tmem_ld16(O_t + lane_base + d0, r);
+            const AttnItem *it = slots + sl;
+            const int bh = it->bh, qt = it->qt;
+            __syncwarp();
+            if (bh < 0) break;
+            if (lane == 0) ptx::mbar_arrive(itemfree + sl);
+            const int b = bh / a.Hg, h = a.h0 + (bh - b * a.Hg);
+            const int q0 = qt * QT + ew * 32;  // this warp's first row
+            if (!att_wait(ofull + (k & 1), (k >> 1) & 1, abort_flag) ||
+                !att_wait(lready + (k & 1), (k >> 1) & 1, abort_flag)) {
+                atomicOr(a.dev_err, WB_DERR_TIMEOUT_MMA);
+                break;
+            }
+            ptx::tc_fence_after();
+            const float *ls = lsum + (k & 1) * 4 * QT + row;
+            const float inv = 1.0f / ((ls[0] + ls[QT]) + (ls[2 * QT] + ls[3 * QT]));
+            const uint32_t O_t = tmem + 256 + (uint32_t)((k & 1) * HDP) + lane_base;
+            float *orow0 = a.o + ((long long)b * a.T + q0) * a.E + (long long)h * a.hd;
+            const int nrow = min(32, a.T - q0);
+#pragma unroll 1
+            for (int hc = 0; hc < HDP / 64; hc++) {
+                uint32_t r[2][32];
+                ptx::tmem_ld32(O_t + hc * 64, r[0]);
+                ptx::tmem_ld32(O_t + hc * 64 + 32, r[1]);
                 ptx::tmem_ld_wait();
-#pragma unroll
-                for (int i = 0; i < 16; i++) o[i] = __uint_as_float(r[i]);
-            } else {
-#pragma unroll
-                for (int c = 0; c < HC / 32; c++) {
-                    uint32_t r[32];
-                    ptx::tmem_ld32(O_t + lane_base + d0 + c * 32, r);
-                    ptx::tmem_ld_wait();
-#pragma unroll
-                    for (int i = 0; i < 32; i++) o[c * 32 + i] = __uint_as_float(r[i]);
+                if (hc == HDP / 64 - 1) {
+                    // O buffer and row sums read: the MMA and softmax may reuse them
+                    ptx::tc_fence_before();
+                    ptx::mbar_arrive(ofree + (k & 1));
                 }
-            }
-            if (has_prev) {
-                const float e = __expf(sp - m0);
-                lt += e;
 #pragma unroll
-                for (int d = 0; d < HC; d++)
-                    if (d0 + d < a.hd) o[d] = fmaf(e, vprev[d], o[d]);
-            }
-            const float inv = 1.0f / lt;
-            if (WIDE && HC == 16) {
-                // the K/V ring is free (every MMA has completed): each warp
-                // stages its 32 rows x 16 columns and stores two rows at a time
-                float *buf = reinterpret_cast<float *>(sm + L::OFF_V) + warp * 32 * 17;
-                __syncwarp();
+                for (int c = 0; c < 2; c++) {
 #pragma unroll
-                for (int i = 0; i < 16; i++) buf[lane * 17 + i] = o[i] * inv;
-                __syncwarp();
-                const int col = lane & 15, d = d0 + col;
+                    for (int i = 0; i < 32; i++) r[c][i] = __float_as_uint(__uint_as_float(r[c][i]) * inv);
+                    warp_stage32(buf, r[c], lane);
+                    const int d = hc * 64 + c * 32 + lane;
+                    if (d < a.hd)
 #pragma unroll 4
-                for (int it = 0; it < 16; it++) {
-                    const int jr = 2 * it + (lane >> 4);
-                    const int qq = q0 + (warp & 3) * 32 + jr;
-                    if (qq < a.T && d < a.hd)
-                        reinterpret_cast<float *>(a.o)[((long long)b * a.T + qq) * a.E + (long long)h * a.hd + d] =
-                            buf[jr * 17 + col];
+                        for (int jr = 0; jr < nrow; jr++) orow0[(long long)jr * a.E + d] = buf[jr * 33 + lane];
                 }
-            } else if (WIDE) {
-                // the K/V ring is free (every MMA has completed): each warp
-                // stages its 32 rows x 32 columns and stores them row by row
-                float *buf = reinterpret_cast<float *>(sm + L::OFF_V) + warp * 32 * 33;
-#pragma unroll
-                for (int c = 0; c < HC / 32; c++) {
-                    uint32_t r[32];
-#pragma unroll
-                    for (int i = 0; i < 32; i++) r[i] = __float_as_uint(o[c * 32 + i] * inv);
-                    warp_stage32(buf, r, lane);
-                    const int d = d0 + c * 32 + lane;
-#pragma unroll 4
-                    for (int jr = 0; jr < 32; jr++) {
-                        const int qq = q0 + (warp & 3) * 32 + jr;
-                        if (qq < a.T && d < a.hd)
-                            reinterpret_cast<float *>(a.o)[((long long)b * a.T + qq) * a.E + (long long)h * a.hd + d] =
-                                buf[jr * 33 + lane];
-                    }
-                }
-            } else if (q < a.T) {
-                __nv_bfloat16 *dst = (__nv_bfloat16 *)a.o + ((long long)b * a.T + q) * a.E + (long long)h * a.hd;
-#pragma unroll
-                for (int d = 0; d < HC; d++)
-                    if (d0 + d < a.hd) dst[d0 + d] = __float2bfloat16_rn(o[d] * inv);
             }
         }
     }
+    __syncwarp();
     ptx::tc_fence_before();
     __syncthreads();
-    if (warp == ATT_SOFTMAX_WARPS) ptx::tmem_dealloc(tmem, 512);
+    if (warp == ATT_W_MMA) ptx::tmem_dealloc(tmem, 512);
 }
 
 // ---------------------------------------------------------------------------
@@ -810,50 +876,24 @@ __global__ void __launch_bounds__(128, 1)
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
-__global__ void f32_to_bf16_kernel(const float *in, __nv_bfloat16 *out, long long n) {
-    const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
-    if (i < n) out[i] = __float2bfloat16_rn(in[i]);
-}
 
 int tc_layer_upload(TcLayerWeights *t, const wb_attn_weights_desc *w, std::string *msg) {
     t->E = w->n_embd;
     t->H = w->n_head;
     t->hd = w->n_embd / w->n_head;
     t->C = w->content_dim;
-    t->wide = true;
     {
         int rc = proj_weights_upload(&t->proj, w, msg);
         if (rc) return rc;
     }
     const size_t n = (size_t)t->E * t->E;
-    if (t->wide) {
-        if (cudaMalloc(&t->w_o32, n * sizeof(float)) != cudaSuccess) {
-            cudaGetLastError();
-            *msg = "cudaMalloc for fp32 out_proj failed";
-            return WB_ENOMEM;
-        }
-        if (cudaMemcpy(t->w_o32, w->out_proj_w, n * sizeof(float), cudaMemcpyHostToDevice) != cudaSuccess) {
-            *msg = "upload of out_proj failed";
-            return WB_ECUDA;
-        }
-    }
-    float *tmp = nullptr;
-    if (cudaMalloc(&t->w_o, n * sizeof(__nv_bfloat16)) != cudaSuccess || cudaMalloc(&tmp, n * sizeof(float)) != cudaSuccess) {
+    if (cudaMalloc(&t->w_o32, n * sizeof(float)) != cudaSuccess) {
         cudaGetLastError();
-        if (tmp) cudaFree(tmp);
-        *msg = "cudaMalloc for bf16 out_proj failed";
+        *msg = "cudaMalloc for fp32 out_proj failed";
         return WB_ENOMEM;
     }
-    if (cudaMemcpy(tmp, w->out_proj_w, n * sizeof(float), cudaMemcpyHostToDevice) != cudaSuccess) {
-        cudaFree(tmp);
+    if (cudaMemcpy(t->w_o32, w->out_proj_w, n * sizeof(float), cudaMemcpyHostToDevice) != cudaSuccess) {
         *msg = "upload of out_proj failed";
-        return WB_ECUDA;
-    }
-    f32_to_bf16_kernel<<<(unsigned)((n + 255) / 256), 256>>>(tmp, t->w_o, (long long)n);
-    cudaError_t e = cudaDeviceSynchronize();
-    cudaFree(tmp);
-    if (e != cudaSuccess) {
-        *msg = std::string("bf16 conversion failed: ") + cudaGetErrorString(e);
         return WB_ECUDA;
     }
     return WB_OK;
@@ -861,19 +901,18 @@ int tc_layer_upload(TcLayerWeights *t, const wb_attn_weights_desc *w, std::strin
 
 void tc_layer_free(TcLayerWeights *t) {
     proj_weights_free(&t->proj);
-    if (t->w_o) cudaFree(t->w_o);
     if (t->w_o32) cudaFree(t->w_o32);
-    t->w_o = nullptr;
     t->w_o32 = nullptr;
 }
 
 // Workspace pieces of the attention core, carved after `off`.
 struct CoreLayout {
-    size_t qf, kf, vh, vl, m0, sp, cn, cm, fl, o, end;
+    size_t qf, kf, vh, vl, m0, sp, cn, cm, sched, o, end;
 };
-static CoreLayout core_layout(const TcLayerWeights &t, int B, int T, size_t off, int Hg) {
+static int core_fw(bool content) { return content ? 64 : 16; }
+static CoreLayout core_layout(const TcLayerWeights &t, int B, int T, size_t off, int Hg, bool content) {
     const int hdp = t.hd <= 64 ? 64 : 128;
-    const int fw = t.wide ? 64 : 32;
+    const int fw = core_fw(content);
     const long long BH = (long long)B * Hg, R = (long long)B * T;
     const int n_qt = (T + QT - 1) / QT;
     Carve cv;
@@ -882,13 +921,13 @@ static CoreLayout core_layout(const TcLayerWeights &t, int B, int T, size_t off,
     c.qf = cv.take<__nv_bfloat16>(BH * T * fw);
     c.kf = cv.take<__nv_bfloat16>(BH * T * fw);
     c.vh = cv.take<__nv_bfloat16>(BH * T * hdp);
-    c.vl = cv.take<__nv_bfloat16>(t.wide ? BH * T * hdp : 1);
+    c.vl = cv.take<__nv_bfloat16>(BH * T * hdp);
     c.m0 = cv.take<float>(BH * T);
     c.sp = cv.take<float>(BH * T);
     c.cn = cv.take<float>(BH * T);
     c.cm = cv.take<unsigned int>(BH);
-    c.fl = cv.take<int>(1 + BH * n_qt);
-    c.o = t.wide ? cv.take<float>(R * t.E) : cv.take<__nv_bfloat16>(R * t.E);
+    c.sched = cv.take<int>(2 + BH * n_qt);
+    c.o = cv.take<float>(R * t.E);
     c.end = cv.off;
     return c;
 }
@@ -940,39 +979,50 @@ static int launch_gemm(bool tf32, const void *A, const void *W, const float *bia
     return WB_OK;
 }
 
-template <int HDP, bool WIDE>
-static void launch_attn_tc(const CUtensorMap &tq, const CUtensorMap &tk, const CUtensorMap &tvh,
-                           const CUtensorMap &tvl, const AttnTcArgs &aa, int hdn, unsigned grid, cudaStream_t st) {
-    using L = AttnSmem<HDP, WIDE>;
+template <int HDP, int FW>
+static int launch_attn_tc(const CUtensorMap &tq, const CUtensorMap &tk, const CUtensorMap &tvh,
+                          const CUtensorMap &tvl, const AttnTcArgs &aa, int hdn, int sm_count, cudaStream_t st,
+                          std::string *msg) {
+    using L = AttnSmem<HDP, FW>;
+    const int grid = std::max(1, std::min(aa.n_items, sm_count));
     ProfScope ps("attn_tc", st);
-    cudaFuncSetAttribute(attn_tc_kernel<HDP, WIDE>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES);
-    attn_tc_kernel<HDP, WIDE><<<grid, ATT_THREADS, L::BYTES, st>>>(tq, tk, tvh, tvl, aa, hdn);
+    cudaFuncSetAttribute(attn_tc_kernel<HDP, FW>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES);
+    attn_tc_kernel<HDP, FW><<<grid, ATT_THREADS, L::BYTES, st>>>(tq, tk, tvh, tvl, aa, hdn);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        *msg = std::string("attention launch failed: ") + cudaGetErrorString(e);
+        return WB_ECUDA;
+    }
+    return WB_OK;
 }
 
-// Runs features -> tcgen05 attention -> SIMT fallback for flagged tiles ->
+// Runs features -> tcgen05 attention -> SIMT fallback for listed tiles ->
 // tcgen05 out_proj, given phases/buckets/values already in `sv` and (when
-// use_content) content vectors in `content`.  The workspace must already
-// hold core_layout(...).end bytes.
+// content is non-null) content vectors.  The workspace must already hold
+// core_layout(...).end bytes.
 static int tc_attention_core(const TcLayerWeights &t, const WbSeqView &sv, const float *content, int B, int T,
                              int h0, int Hg, bool add_bias, float *y, Workspace *ws, const CoreLayout &lay,
-                             uint32_t *dev_err, cudaStream_t st, std::string *msg) {
+                             uint32_t *dev_err, int sm_count, cudaStream_t st, std::string *msg) {
     const int H = t.H, hd = t.hd, E = t.E;
-    const bool wide = t.wide;
     const int hdp = hd <= 64 ? 64 : 128;
     const int hdn = (hd + 15) / 16 * 16;
-    const int fw = wide ? 64 : 32;
+    const int fw = core_fw(content != nullptr);
     const long long BH = (long long)B * Hg, R = (long long)B * T;
     const int n_qt = (T + QT - 1) / QT;
+    if (BH * n_qt > 0x7fffffffLL) {
+        *msg = "too many attention work items";
+        return WB_EINVAL;
+    }
     int rc;
     char *w = (char *)ws->p;
     __nv_bfloat16 *qf = (__nv_bfloat16 *)(w + lay.qf), *kf = (__nv_bfloat16 *)(w + lay.kf);
     __nv_bfloat16 *vh = (__nv_bfloat16 *)(w + lay.vh), *vl = (__nv_bfloat16 *)(w + lay.vl);
-    void *ob = (void *)(w + lay.o);
+    float *ob = (float *)(w + lay.o);
     float *m0 = (float *)(w + lay.m0), *sp = (float *)(w + lay.sp), *cn = (float *)(w + lay.cn);
     unsigned int *cm = (unsigned int *)(w + lay.cm);
-    int *fl = (int *)(w + lay.fl);
-    if (cudaMemsetAsync(cm, 0, BH * sizeof(unsigned int), st) != cudaSuccess ||
-        cudaMemsetAsync(fl, 0, sizeof(int), st) != cudaSuccess) {
+    int *sched = (int *)(w + lay.sched);
+    if ((content && cudaMemsetAsync(cm, 0, BH * sizeof(unsigned int), st) != cudaSuccess) ||
+        cudaMemsetAsync(sched, 0, 2 * sizeof(int), st) != cudaSuccess) {
         *msg = "cudaMemsetAsync failed";
         return WB_ECUDA;
     }
@@ -982,8 +1032,8 @@ static int tc_attention_core(const TcLayerWeights &t, const WbSeqView &sv, const
     const unsigned fgrid = (unsigned)((BH * T + FEAT_WARPS * 32 - 1) / (FEAT_WARPS * 32));
     {
         ProfScope ps("feat", st);
-        if (wide) feat_kernel<true><<<fgrid, FEAT_WARPS * 32, 0, st>>>(fa);
-        else feat_kernel<false><<<fgrid, FEAT_WARPS * 32, 0, st>>>(fa);
+        if (fw == 64) feat_kernel<64><<<fgrid, FEAT_WARPS * 32, 0, st>>>(fa);
+        else feat_kernel<16><<<fgrid, FEAT_WARPS * 32, 0, st>>>(fa);
     }
 
     CUtensorMap tq, tk, tvh, tvl;
@@ -991,7 +1041,7 @@ static int tc_attention_core(const TcLayerWeights &t, const WbSeqView &sv, const
         const uint64_t dims[3] = {(uint64_t)fw, (uint64_t)T, (uint64_t)BH};
         const uint64_t strides[2] = {(uint64_t)fw * 2, (uint64_t)T * fw * 2};
         const uint32_t box[3] = {(uint32_t)fw, 128, 1};
-        const CUtensorMapSwizzle fsw = wide ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+        const CUtensorMapSwizzle fsw = fw == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_32B;
         if ((rc = make_tmap(&tq, qf, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, dims, strides, box, fsw, msg))) return rc;
         if ((rc = make_tmap(&tk, kf, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, dims, strides, box, fsw, msg))) return rc;
         const uint64_t vdims[3] = {(uint64_t)hdp, (uint64_t)T, (uint64_t)BH};
@@ -1000,39 +1050,29 @@ static int tc_attention_core(const TcLayerWeights &t, const WbSeqView &sv, const
         if ((rc = make_tmap(&tvh, vh, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, vdims, vstr, vbox,
                             CU_TENSOR_MAP_SWIZZLE_128B, msg)))
             return rc;
-        tvl = tvh;
-        if (wide && (rc = make_tmap(&tvl, vl, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, vdims, vstr, vbox,
-                                    CU_TENSOR_MAP_SWIZZLE_128B, msg)))
+        if ((rc = make_tmap(&tvl, vl, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, vdims, vstr, vbox,
+                            CU_TENSOR_MAP_SWIZZLE_128B, msg)))
             return rc;
     }
-    AttnTcArgs aa{(int)BH, H, T, hd, n_qt, Hg, h0, m0, sp, cn, cm, sv, ob, E, fl, dev_err};
-    const unsigned grid = (unsigned)(BH * n_qt);
-    if (hdp == 64) {
-        if (wide) launch_attn_tc<64, true>(tq, tk, tvh, tvl, aa, hdn, grid, st);
-        else launch_attn_tc<64, false>(tq, tk, tvh, tvl, aa, hdn, grid, st);
-    } else {
-        if (wide) launch_attn_tc<128, true>(tq, tk, tvh, tvl, aa, hdn, grid, st);
-        else launch_attn_tc<128, false>(tq, tk, tvh, tvl, aa, hdn, grid, st);
-    }
-    {
-        if (wide)
-            launch_attn_simt_fallback_f32(sv, content, content ? t.C : 0, cscale, t.harmonic_n, B, H, T, hd,
-                                          (float *)ob, fl, h0, Hg, st);
-        else
-            launch_attn_simt_fallback_bf16(sv, content, content ? t.C : 0, cscale, t.harmonic_n, B, H, T, hd,
-                                           (__nv_bfloat16 *)ob, fl, h0, Hg, st);
-    }
+    AttnTcArgs aa{(int)BH, H, T, hd, n_qt, Hg, h0, (int)(BH * n_qt), m0, sp, cn, cm, sv, ob, E, sched, dev_err};
+    if (hdp == 64)
+        rc = fw == 64 ? launch_attn_tc<64, 64>(tq, tk, tvh, tvl, aa, hdn, sm_count, st, msg)
+                      : launch_attn_tc<64, 16>(tq, tk, tvh, tvl, aa, hdn, sm_count, st, msg);
+    else
+        rc = fw == 64 ? launch_attn_tc<128, 64>(tq, tk, tvh, tvl, aa, hdn, sm_count, st, msg)
+                      : launch_attn_tc<128, 16>(tq, tk, tvh, tvl, aa, hdn, sm_count, st, msg);
+    if (rc) return rc;
+    // query tiles whose scores may exceed the fixed-shift bound (content
+    // only): recomputed in fp32 from the list the attention kernel built
+    if (content)
+        launch_attn_simt_fallback_f32(sv, content, t.C, cscale, t.harmonic_n, B, H, T, hd, ob, sched + 1, h0, Hg,
+                                      st);
     // out_proj: y = o W_o^T (+ b_o), over the computed heads' columns of o
     // and W_o (K = Hg * hd): the partial output of a head range
     if (Hg == H)
-        return launch_gemm(wide, ob, wide ? (const void *)t.w_o32 : (const void *)t.w_o, add_bias ? t.b_o : nullptr,
-                           y, (int)R, E, E, E, dev_err, st, msg);
-    if (!wide) {
-        *msg = "head ranges need the split-precision layer";
-        return WB_ENOTSUP;
-    }
-    return launch_gemm(true, (const float *)ob + (size_t)h0 * hd, t.w_o32 + (size_t)h0 * hd,
-                       add_bias ? t.b_o : nullptr, y, (int)R, E, Hg * hd, E, dev_err, st, msg, E, E);
+        return launch_gemm(true, ob, t.w_o32, add_bias ? t.b_o : nullptr, y, (int)R, E, E, E, dev_err, st, msg);
+    return launch_gemm(true, ob + (size_t)h0 * hd, t.w_o32 + (size_t)h0 * hd, add_bias ? t.b_o : nullptr, y, (int)R,
+                       E, Hg * hd, E, dev_err, st, msg, E, E);
 }
 
 int tc_gemm_bf16(const __nv_bfloat16 *A, const __nv_bfloat16 *B, const float *bias, float *C, int M, int N, int K,
@@ -1048,7 +1088,6 @@ int tc_gemm_tf32(const float *A, const float *B, const float *bias, float *C, in
 int tc_attn_forward(const TcLayerWeights &t, const float *x, int B, int T, bool use_content, float *y,
                     float *phases_out, Workspace *ws, uint32_t *dev_err, int sm_count, cudaStream_t st,
                     std::string *msg, int h0, int h1, bool add_bias) {
-    (void)sm_count;
     const int H = t.H, hd = t.hd;
     if (h1 < 0) h1 = H;
     if (h0 < 0 || h1 > H || h0 >= h1) {
@@ -1075,7 +1114,7 @@ int tc_attn_forward(const TcLayerWeights &t, const float *x, int B, int T, bool 
     const size_t o_th = cv.take<float>(R * H);
     const size_t o_bk = cv.take<uint8_t>(R * H);
     const size_t o_v = cv.take<float>(R * H * hd);
-    const CoreLayout lay = core_layout(t, B, T, cv.off, Hg);
+    const CoreLayout lay = core_layout(t, B, T, cv.off, Hg, use_content);
     if (ws_ensure(ws, lay.end, msg)) return WB_ENOMEM;
     char *w = (char *)ws->p;
     WbSeqView sv;
@@ -1089,7 +1128,7 @@ int tc_attn_forward(const TcLayerWeights &t, const float *x, int B, int T, bool 
     (void)o_rs;
     int rc = launch_proj_tc(t.proj, t.pw.wrs_t, t.pw.brs, t.pw.wv_t, t.pw.bv, x, B, T, sv, content, h0, Hg, dev_err, st, msg);
     if (rc) return rc;
-    rc = tc_attention_core(t, sv, content, B, T, h0, Hg, add_bias, y, ws, lay, dev_err, st, msg);
+    rc = tc_attention_core(t, sv, content, B, T, h0, Hg, add_bias, y, ws, lay, dev_err, sm_count, st, msg);
     if (rc) return rc;
     if (phases_out &&
         cudaMemcpyAsync(phases_out, sv.theta, R * H * sizeof(float), cudaMemcpyDeviceToDevice, st) != cudaSuccess) {
@@ -1101,7 +1140,6 @@ int tc_attn_forward(const TcLayerWeights &t, const float *x, int B, int T, bool 
 
 int tc_kv_prefill(const TcLayerWeights &t, const WbSeqView &sv, const float *x, int n_seq, int T, float *y,
                   Workspace *ws, uint32_t *dev_err, int sm_count, cudaStream_t st, std::string *msg) {
-    (void)sm_count;
     if (t.hd > 128) {
         *msg = "WB_PATH_TENSOR supports head_dim <= 128";
         return WB_ENOTSUP;
@@ -1109,12 +1147,12 @@ int tc_kv_prefill(const TcLayerWeights &t, const WbSeqView &sv, const float *x, 
     const long long R = (long long)n_seq * T;
     Carve cv;
     const size_t o_rs = cv.take<float>(R * 2 * t.H);
-    const CoreLayout lay = core_layout(t, n_seq, T, cv.off, t.H);
+    const CoreLayout lay = core_layout(t, n_seq, T, cv.off, t.H, false);
     if (ws_ensure(ws, lay.end, msg)) return WB_ENOMEM;
     (void)o_rs;
     int rc = launch_proj_tc(t.proj, t.pw.wrs_t, t.pw.brs, t.pw.wv_t, t.pw.bv, x, n_seq, T, sv, nullptr, 0, t.H, dev_err, st, msg);
     if (rc) return rc;
-    return tc_attention_core(t, sv, nullptr, n_seq, T, 0, t.H, true, y, ws, lay, dev_err, st, msg);
+    return tc_attention_core(t, sv, nullptr, n_seq, T, 0, t.H, true, y, ws, lay, dev_err, sm_count, st, msg);
 }
 
 // Rows from which the decode out_proj runs on the tensor-core GEMM (below

@@ -17,9 +17,7 @@ struct TcLayerWeights {
     const float *b_o = nullptr;        // [E] out_proj bias
     const float *wo_t = nullptr;       // [E][E] out_proj, input-major fp32 (decode rows)
     const float *wrs_h = nullptr;      // [H][E][2] phase projection, one head's weights contiguous (decode)
-    __nv_bfloat16 *w_o = nullptr;      // [E][E] out_proj rows, bf16 (K-major B operand)
-    float *w_o32 = nullptr;            // [E][E] out_proj rows, fp32 (tf32 B operand, wide layers)
-    bool wide = true;                  // split precision: hi/lo features and values, tf32 out_proj
+    float *w_o32 = nullptr;            // [E][E] out_proj rows, fp32 (tf32 B operand)
 };
 
 int tc_layer_upload(TcLayerWeights *t, const wb_attn_weights_desc *w, std::string *msg);
