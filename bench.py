@@ -981,7 +981,8 @@ def run_profile_case(args):
     on the device): 'decode' = 12 fused decode steps of one 768-dim layer,
     32 sequences at ctx ~1100; 'prefill' = 3 tensor-path prefills of one
     768-dim layer, 4 x 1024 tokens (content on); 'prefill-serve' = 3 serve
-    prefills (KV cache, no content) of one 768-dim layer, 4 x 1024 tokens."""
+    prefills (KV cache, no content) of one 768-dim layer, 16 x 1024 tokens
+    (about 10 work items per SM, as in the benchmark's 20)."""
     import numpy as np
     import torch
     import wave_engine_b200 as wb
@@ -1032,7 +1033,7 @@ def run_profile_case(args):
         extra["decode_attn_algorithmic_bytes"] = [
             int(decode_bytes_exact(bk, n, s + 1, H, hd, first=s)[0] + B * E * 4) for s in range(12)]
     elif args.profile_case == "prefill-serve":
-        B = 4
+        B = 16
         cache = wb.KvCache(1, H, hd, max_seqs=B, max_ctx=CFG["seq_len"], ctx=ctx)
         ids = torch.arange(B, dtype=torch.int32, device="cuda")
         x = torch.randn((B, CFG["seq_len"], E), generator=g, device="cuda")

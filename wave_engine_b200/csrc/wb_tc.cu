@@ -336,19 +336,25 @@ struct AttnSmem {
     static constexpr int K_BYTES = KT * FW * 2;      // 4 / 16 KB
     static constexpr int VPART = KT * HDP * 2;       // one bf16 value tile: 16 / 32 KB
     static constexpr int V_BYTES = 2 * VPART;        // hi + lo
-    static constexpr int OFF_Q = 0;
-    static constexpr int OFF_K = OFF_Q + Q_BYTES;
+    static constexpr int OFF_Q = 0;                  // two Q buffers (items alternate)
+    static constexpr int OFF_K = OFF_Q + 2 * Q_BYTES;
     static constexpr int OFF_V = OFF_K + ST * K_BYTES;
     static constexpr int OFF_EPI = OFF_V + ST * V_BYTES;                 // epilogue staging, 32 x 33 floats per warp
     static constexpr int OFF_SLOT = OFF_EPI + ATT_EPI_WARPS * 32 * 33 * 4;
     static constexpr int OFF_LSUM = OFF_SLOT + ATT_SLOTS * (int)sizeof(AttnItem);  // [2][4][QT] row-sum partials
     static constexpr int OFF_BAR = OFF_LSUM + 2 * 4 * QT * 4;
-    // barriers: qfull, qfree, kvfull[ST], kvfree[ST], sfull[2], pready[2],
-    // ofull[2], ofree[2], lready[2], itemfull[SLOTS], itemfree[SLOTS], mmadone
-    static constexpr int NBAR = 2 + 2 * ST + 10 + 2 * ATT_SLOTS + 1;
+    // barriers: qfull[2], qfree[2], kvfull[ST], kvfree[ST], sfull[2], pready[2],
+    // ofull[2], ofree[2], lready[2], itemfull[SLOTS], itemfree[SLOTS], mmadone,
+    // sfree[2], pfree[2]
+    static constexpr int NBAR = 4 + 2 * ST + 10 + 2 * ATT_SLOTS + 1 + 4;
+    // TMEM columns: S0 [0,128), S1 [128,256), then OBUF O buffers of HDP
+    // columns, then P0, P1 (64 columns each: 128 bf16 keys packed in pairs)
+    static constexpr int OBUF = HDP == 64 ? 2 : 1;
+    static constexpr int O_COL = 256;
+    static constexpr int P_COL = O_COL + OBUF * HDP;
     static constexpr int BYTES = OFF_BAR + NBAR * 8 + 16 + 1024;  // + TMEM slot, alignment slack
     static_assert(BYTES <= 232448, "attention shared memory above the 227 KB limit");
-    static_assert(HDP * 2 + 256 <= 512, "TMEM: two S buffers and two O buffers");
+    static_assert(P_COL + 128 <= 512, "TMEM: two S, OBUF O and two P buffers");
 };
 
 // Bounded mbarrier wait that also gives up once another role has raised the
@@ -393,12 +399,13 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *bars = reinterpret_cast<uint64_t *>(sm + L::OFF_BAR);
-    uint64_t *qfull = bars, *qfree = bars + 1;
-    uint64_t *kvfull = bars + 2, *kvfree = kvfull + ST;
+    uint64_t *qfull = bars, *qfree = bars + 2;
+    uint64_t *kvfull = bars + 4, *kvfree = kvfull + ST;
     uint64_t *sfull = kvfree + ST, *pready = sfull + 2, *ofull = pready + 2, *ofree = ofull + 2;
     uint64_t *lready = ofree + 2, *itemfull = lready + 2, *itemfree = itemfull + ATT_SLOTS;
     uint64_t *mmadone = itemfree + ATT_SLOTS;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mmadone + 1);
+    uint64_t *sfree = mmadone + 1, *pfree = sfree + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(pfree + 2);
     AttnItem *slots = reinterpret_cast<AttnItem *>(sm + L::OFF_SLOT);
     float *lsum = reinterpret_cast<float *>(sm + L::OFF_LSUM);
     __shared__ int s_abort;
@@ -409,7 +416,9 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         for (int i = 0; i < L::NBAR; i++) {
             uint64_t *bb = bars + i;
             uint32_t cnt = 1;
-            if (bb == pready || bb == pready + 1 || bb == lready || bb == lready + 1) cnt = ATT_SOFTMAX_WARPS * 32;
+            if (bb == pready || bb == pready + 1 || bb == sfree || bb == sfree + 1)
+                cnt = ATT_SOFTMAX_WARPS / 2 * 32;  // one softmax group per tile
+            else if (bb == lready || bb == lready + 1) cnt = ATT_SOFTMAX_WARPS * 32;
             else if (bb == ofree || bb == ofree + 1) cnt = ATT_EPI_WARPS * 32;
             else if (bb >= itemfull && bb < itemfull + ATT_SLOTS) cnt = 32;
             else if (bb >= itemfree && bb < itemfree + ATT_SLOTS) cnt = ATT_SOFTMAX_WARPS + ATT_EPI_WARPS + 1;
@@ -496,10 +505,12 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
             if (end) break;
             if (lane == 0) {
                 bool ok = true;
-                if (k > 1 && !att_wait(qfree, (k - 2) & 1, abort_flag)) ok = false;
+                // Q of item i = k - 1 into buffer i & 1, free once item i - 2's QKs completed
+                const int i = k - 1, qb = i & 1;
+                if (i >= 2 && !att_wait(qfree + qb, ((i - 2) >> 1) & 1, abort_flag)) ok = false;
                 if (ok) {
-                    ptx::mbar_arrive_expect_tx(qfull, L::Q_BYTES);
-                    ptx::tma_load_3d(sm + L::OFF_Q, &tm_q, qfull, 0, qt * QT, bh);
+                    ptx::mbar_arrive_expect_tx(qfull + qb, L::Q_BYTES);
+                    ptx::tma_load_3d(sm + L::OFF_Q + qb * L::Q_BYTES, &tm_q, qfull + qb, 0, qt * QT, bh);
                 }
                 for (int j = 0; ok && j <= qt; j++, g++) {
                     const int st = (int)(g % ST);
@@ -527,92 +538,103 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         if (lane == 0 && *abort_flag) {
             for (long long gg = g - 1; gg >= 0 && gg >= g - ST; gg--)
                 ptx::mbar_wait(kvfull + (gg % ST), (uint32_t)((gg / ST) & 1), 200000000LL);
-            if (k > 1) ptx::mbar_wait(qfull, (k - 2) & 1, 200000000LL);
+            for (int i = k - 2; i >= 0 && i >= k - 3; i--) ptx::mbar_wait(qfull + (i & 1), (i >> 1) & 1, 200000000LL);
         }
     } else if (warp == ATT_W_MMA) {
         // ---------------- MMA issuer
         if (lane == 0) {
             constexpr uint32_t IDESC_QK = ptx::idesc_bf16(128, 128, 0, 0);
             const uint32_t idesc_pv = ptx::idesc_bf16(128, hdn, 0, 1);
-            const uint32_t sQ = ptx::smem_u32(sm + L::OFF_Q);
+            const uint32_t sQ0 = ptx::smem_u32(sm + L::OFF_Q);
             int kq = 0, jq = 0;                // next QK: item, tile
             long long gq = 0, gp = 0;          // next QK / PV global tile
             int kp = 0, jp = 0;                // next PV: item, tile
             bool qk_end = false, ok = true;
-            auto issue_qk = [&]() {
-                if (qk_end || !ok) return;
-                if (jq == 0) {
-                    if (!att_wait(itemfull + (kq % ATT_SLOTS), (kq / ATT_SLOTS) & 1, abort_flag)) {
-                        ok = false;
-                        return;
-                    }
-                    const AttnItem *it = slots + (kq % ATT_SLOTS);
-                    if (it->bh < 0) {
-                        qk_end = true;
-                        // the end marker's slot is never returned: nobody reads it again
-                        return;
-                    }
-                    if (!att_wait(qfull, kq & 1, abort_flag)) {
-                        ok = false;
-                        return;
-                    }
-                }
-                const int st = (int)(gq % ST);
-                if (!att_wait(kvfull + st, (uint32_t)((gq / ST) & 1), abort_flag)) {
-                    ok = false;
-                    return;
-                }
-                ptx::tc_fence_after();
-                const uint32_t sK = ptx::smem_u32(sm + L::OFF_K + st * L::K_BYTES);
-                const uint32_t S_t = tmem + (uint32_t)((gq & 1) * 128);
+            // Event loop: issue whichever of PV(gp) and QK(gq) has its inputs
+            // ready (non-blocking barrier tests), PV first.  QK(gq) writes S
+            // buffer gq & 1 once the softmax has read S(gq - 2) (sfree), so it
+            // can run ahead of PV(gq - 2); PV(gp) reads P buffer gp & 1.
+            int qstate = 0;  // QK(gq): 0 item descriptor, 1 Q tile, 2 S buffer, 3 K/V tile
+            long long t_last = clock64();
+            while (ok) {
+                bool did = false;
+                // ---- PV(gp)
+                if (gp < gq) {
+                    const int sl = kp % ATT_SLOTS;
+                    const int ob = kp % L::OBUF;
+                    const bool ready =
+                        (jp != 0 || kp < L::OBUF || ptx::mbar_test(ofree + ob, ((kp - L::OBUF) / L::OBUF) & 1)) &&
+                        ptx::mbar_test(pready + (gp & 1), (uint32_t)((gp >> 1) & 1));
+                    if (ready) {
+                        ptx::tc_fence_after();
+                        const uint32_t O_t = tmem + L::O_COL + (uint32_t)(ob * HDP);
+                        const uint32_t P_t = tmem + L::P_COL + (uint32_t)((gp & 1) * 64);
+                        const uint32_t sV = ptx::smem_u32(sm + L::OFF_V + (int)(gp % ST) * L::V_BYTES);
 #pragma unroll
-                for (int kk = 0; kk < FW / 16; kk++) {
-                    const uint64_t ad = ptx::smem_desc(sQ + kk * 32, 16, F_SBO, F_SW);
-                    const uint64_t bd = ptx::smem_desc(sK + kk * 32, 16, F_SBO, F_SW);
-                    ptx::mma_bf16(S_t, ad, bd, IDESC_QK, kk > 0);
+                        for (int kk = 0; kk < KT / 16; kk++) {
+                            // keys 16kk..16kk+15: packed two per column
+                            const uint32_t a_t = P_t + (uint32_t)(8 * kk);
+                            const uint64_t bh_d = ptx::smem_desc(sV + kk * 2048, KT * 128, 1024, ptx::UMMA_SW128);
+                            const uint64_t bl_d =
+                                ptx::smem_desc(sV + L::VPART + kk * 2048, KT * 128, 1024, ptx::UMMA_SW128);
+                            ptx::mma_bf16_ta(O_t, a_t, bh_d, idesc_pv, (jp > 0 || kk > 0));
+                            ptx::mma_bf16_ta(O_t, a_t, bl_d, idesc_pv, 1);
+                        }
+                        ptx::mma_commit(kvfree + (int)(gp % ST));
+                        ptx::mma_commit(pfree + (gp & 1));
+                        gp++;
+                        if (++jp == slots[sl].qt + 1) {
+                            ptx::mma_commit(ofull + ob);
+                            ptx::mbar_arrive(itemfree + sl);
+                            kp++;
+                            jp = 0;
+                        }
+                        did = true;
+                    }
                 }
-                ptx::mma_commit(sfull + (gq & 1));
-                gq++;
-                if (++jq == slots[kq % ATT_SLOTS].qt + 1) {
-                    ptx::mma_commit(qfree);  // Q of item kq no longer read
-                    kq++;
-                    jq = 0;
-                }
-            };
-            issue_qk();
-            issue_qk();
-            while (ok && gp < gq) {
-                const int sl = kp % ATT_SLOTS;
-                const uint32_t O_t = tmem + 256 + (uint32_t)((kp & 1) * HDP);
-                if (jp == 0 && kp >= 2 && !att_wait(ofree + (kp & 1), ((kp - 2) >> 1) & 1, abort_flag)) {
-                    ok = false;
-                    break;
-                }
-                if (!att_wait(pready + (gp & 1), (uint32_t)((gp >> 1) & 1), abort_flag)) {
-                    ok = false;
-                    break;
-                }
-                ptx::tc_fence_after();
-                const uint32_t P_t = tmem + (uint32_t)((gp & 1) * 128);
-                const uint32_t sV = ptx::smem_u32(sm + L::OFF_V + (int)(gp % ST) * L::V_BYTES);
+                // ---- QK(gq)
+                if (!qk_end) {
+                    if (qstate == 0 && jq == 0) {
+                        if (ptx::mbar_test(itemfull + (kq % ATT_SLOTS), (kq / ATT_SLOTS) & 1)) {
+                            if (slots[kq % ATT_SLOTS].bh < 0) qk_end = true;  // the end marker's slot is never returned
+                            else qstate = 1;
+                        }
+                    } else if (qstate == 0) {
+                        qstate = 2;
+                    }
+                    if (qstate == 1 && ptx::mbar_test(qfull + (kq & 1), (kq >> 1) & 1)) qstate = 2;
+                    if (qstate == 2 && (gq < 2 || ptx::mbar_test(sfree + (gq & 1), (uint32_t)(((gq - 2) >> 1) & 1))))
+                        qstate = 3;
+                    if (qstate == 3 && ptx::mbar_test(kvfull + (int)(gq % ST), (uint32_t)((gq / ST) & 1))) {
+                        ptx::tc_fence_after();
+                        const int st = (int)(gq % ST);
+                        const uint32_t sK = ptx::smem_u32(sm + L::OFF_K + st * L::K_BYTES);
+                        const uint32_t S_t = tmem + (uint32_t)((gq & 1) * 128);
+                        const uint32_t sQ = sQ0 + (uint32_t)((kq & 1) * L::Q_BYTES);
 #pragma unroll
-                for (int kk = 0; kk < KT / 16; kk++) {
-                    // keys 16kk..16kk+15: quarter kk/2 of the tile, packed two per column
-                    const uint32_t a_t = P_t + (uint32_t)(32 * (kk >> 1) + 8 * (kk & 1));
-                    const uint64_t bh_d = ptx::smem_desc(sV + kk * 2048, KT * 128, 1024, ptx::UMMA_SW128);
-                    const uint64_t bl_d = ptx::smem_desc(sV + L::VPART + kk * 2048, KT * 128, 1024, ptx::UMMA_SW128);
-                    ptx::mma_bf16_ta(O_t, a_t, bh_d, idesc_pv, (jp > 0 || kk > 0));
-                    ptx::mma_bf16_ta(O_t, a_t, bl_d, idesc_pv, 1);
+                        for (int kk = 0; kk < FW / 16; kk++) {
+                            const uint64_t ad = ptx::smem_desc(sQ + kk * 32, 16, F_SBO, F_SW);
+                            const uint64_t bd = ptx::smem_desc(sK + kk * 32, 16, F_SBO, F_SW);
+                            ptx::mma_bf16(S_t, ad, bd, IDESC_QK, kk > 0);
+                        }
+                        ptx::mma_commit(sfull + (gq & 1));
+                        gq++;
+                        if (++jq == slots[kq % ATT_SLOTS].qt + 1) {
+                            ptx::mma_commit(qfree + (kq & 1));  // Q of item kq no longer read
+                            kq++;
+                            jq = 0;
+                        }
+                        qstate = 0;
+                        did = true;
+                    }
                 }
-                ptx::mma_commit(kvfree + (int)(gp % ST));
-                gp++;
-                if (++jp == slots[sl].qt + 1) {
-                    ptx::mma_commit(ofull + (kp & 1));
-                    ptx::mbar_arrive(itemfree + sl);
-                    kp++;
-                    jp = 0;
+                if (qk_end && gp == gq) break;
+                if (did) {
+                    t_last = clock64();
+                } else if (*abort_flag || clock64() - t_last > 4000000000LL) {
+                    *abort_flag = 1;
+                    ok = false;
                 }
-                issue_qk();
             }
             if (!ok) atomicOr(a.dev_err, WB_DERR_TIMEOUT_MMA);
             // every MMA has completed before TMEM is released
@@ -621,11 +643,15 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         }
         __syncwarp();
     } else if (warp < ATT_SOFTMAX_WARPS) {
-        // ---------------- softmax
+        // ---------------- softmax: two groups of 8 warps take the key tiles
+        // in turn (group G the tiles g with g % 2 == G of the CTA's tile
+        // sequence), so one group's exponentials overlap the other's waits;
+        // within a group two warps per TMEM lane group each own 64 key
+        // columns, processed as two 32-column chunks
         const float LOG2E = 1.4426950408889634f;
-        const int row = tid & (QT - 1), quarter = (warp >> 2) & 3;
+        const int row = tid & (QT - 1);
+        const int grp = warp >> 3, half = (warp >> 2) & 1;
         const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-        const int kbase = quarter * 32;
         long long g = 0;
         for (int k = 0;; k++) {
             const int sl = k % ATT_SLOTS;
@@ -648,59 +674,79 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
             float l = 0.0f;
             bool ok = true;
             for (int j = 0; j <= qt; j++, g++) {
-                if (!att_wait(sfull + (g & 1), (uint32_t)((g >> 1) & 1), abort_flag)) {
+                if ((int)(g & 1) != grp) continue;
+                if (!att_wait(sfull + grp, (uint32_t)((g >> 1) & 1), abort_flag)) {
                     atomicOr(a.dev_err, WB_DERR_TIMEOUT_SOFTMAX);
                     ok = false;
                     break;
                 }
                 ptx::tc_fence_after();
-                const uint32_t S_t = tmem + (uint32_t)((g & 1) * 128) + lane_base + kbase;
-                uint32_t r[32];
-                ptx::tmem_ld32(S_t, r);
-                ptx::tmem_ld_wait();
-                uint32_t pk[16];
                 const bool diag = (j == qt);
-                int pcol = -1;
-                if (ep > 0.0f) {
-                    if (diag && row >= 1 && ((row - 1) >> 5) == quarter) pcol = (row - 1) & 31;
-                    else if (j + 1 == qt && row == 0 && quarter == 3) pcol = 31;
-                }
-                if (__any_sync(0xffffffffu, diag || pcol >= 0)) {
+                const uint32_t S_t = tmem + (uint32_t)(grp * 128 + half * 64) + lane_base;
+                uint32_t pk0[16], pk1[16];
+                auto exps = [&](const uint32_t (&r)[32], uint32_t (&pk)[16], int kbase) {
+                    int pcol = -1;
+                    if (ep > 0.0f) {
+                        if (diag && row >= 1 && ((row - 1) >> 5) == (kbase >> 5)) pcol = (row - 1) & 31;
+                        else if (j + 1 == qt && row == 0 && kbase == 96) pcol = 31;
+                    }
+                    if (__any_sync(0xffffffffu, diag || pcol >= 0)) {
 #pragma unroll
-                    for (int i = 0; i < 16; i++) {
-                        float e0 = fast_exp2(fmaf(__uint_as_float(r[2 * i]), LOG2E, nm0));
-                        float e1 = fast_exp2(fmaf(__uint_as_float(r[2 * i + 1]), LOG2E, nm0));
-                        if (diag) {
-                            if (kbase + 2 * i > row) e0 = 0.0f;
-                            if (kbase + 2 * i + 1 > row) e1 = 0.0f;
+                        for (int i = 0; i < 16; i++) {
+                            float e0 = fast_exp2(fmaf(__uint_as_float(r[2 * i]), LOG2E, nm0));
+                            float e1 = fast_exp2(fmaf(__uint_as_float(r[2 * i + 1]), LOG2E, nm0));
+                            if (diag) {
+                                if (kbase + 2 * i > row) e0 = 0.0f;
+                                if (kbase + 2 * i + 1 > row) e1 = 0.0f;
+                            }
+                            if (2 * i == pcol) e0 = ep;
+                            if (2 * i + 1 == pcol) e1 = ep;
+                            l += e0 + e1;
+                            pk[i] = pack_bf16(e0, e1);
                         }
-                        if (2 * i == pcol) e0 = ep;
-                        if (2 * i + 1 == pcol) e1 = ep;
-                        l += e0 + e1;
-                        pk[i] = pack_bf16(e0, e1);
-                    }
-                } else {
+                    } else {
 #pragma unroll
-                    for (int i = 0; i < 16; i++) {
-                        const float e0 = fast_exp2(fmaf(__uint_as_float(r[2 * i]), LOG2E, nm0));
-                        const float e1 = fast_exp2(fmaf(__uint_as_float(r[2 * i + 1]), LOG2E, nm0));
-                        l += e0 + e1;
-                        pk[i] = pack_bf16(e0, e1);
+                        for (int i = 0; i < 16; i++) {
+                            const float e0 = fast_exp2(fmaf(__uint_as_float(r[2 * i]), LOG2E, nm0));
+                            const float e1 = fast_exp2(fmaf(__uint_as_float(r[2 * i + 1]), LOG2E, nm0));
+                            l += e0 + e1;
+                            pk[i] = pack_bf16(e0, e1);
+                        }
                     }
+                };
+                {
+                    uint32_t r[32];
+                    ptx::tmem_ld32(S_t, r);
+                    ptx::tmem_ld_wait();
+                    exps(r, pk0, half * 64);
+                    ptx::tmem_ld32(S_t + 32, r);
+                    ptx::tmem_ld_wait();
+                    // S(g) is read: its buffer may take QK(g + 2)
+                    ptx::tc_fence_before();
+                    ptx::mbar_arrive(sfree + grp);
+                    exps(r, pk1, half * 64 + 32);
                 }
-                ptx::tmem_st16(S_t, pk);
+                // P buffer grp is free once PV(g - 2) has completed
+                if (g >= 2 && !att_wait(pfree + grp, (uint32_t)(((g - 2) >> 1) & 1), abort_flag)) {
+                    atomicOr(a.dev_err, WB_DERR_TIMEOUT_MMA);
+                    ok = false;
+                    break;
+                }
+                const uint32_t P_t = tmem + L::P_COL + (uint32_t)(grp * 64 + half * 32) + lane_base;
+                ptx::tmem_st16(P_t, pk0);
+                ptx::tmem_st16(P_t + 16, pk1);
                 ptx::tmem_st_wait();
                 ptx::tc_fence_before();
-                ptx::mbar_arrive(pready + (g & 1));
+                ptx::mbar_arrive(pready + grp);
             }
             if (!ok) break;
             // the item's row-sum partials; the buffer of item k-2 must have
             // been read by its epilogue
-            if (k >= 2 && !att_wait(ofree + (k & 1), ((k - 2) >> 1) & 1, abort_flag)) {
+            if (k >= 2 && !att_wait(ofree + (k - 2) % L::OBUF, ((k - 2) / L::OBUF) & 1, abort_flag)) {
                 atomicOr(a.dev_err, WB_DERR_TIMEOUT_SOFTMAX);
                 break;
             }
-            lsum[((k & 1) * 4 + quarter) * QT + row] = l;
+            lsum[((k & 1) * 4 + grp * 2 + half) * QT + row] = l;
             ptx::mbar_arrive(lready + (k & 1));
         }
     } else {
@@ -722,7 +768,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
             if (lane == 0) ptx::mbar_arrive(itemfree + sl);
             const int b = bh / a.Hg, h = a.h0 + (bh - b * a.Hg);
             const int q0 = qt * QT + ew * 32;  // this warp's first row
-            if (!att_wait(ofull + (k & 1), (k >> 1) & 1, abort_flag) ||
+            if (!att_wait(ofull + k % L::OBUF, (k / L::OBUF) & 1, abort_flag) ||
                 !att_wait(lready + (k & 1), (k >> 1) & 1, abort_flag)) {
                 atomicOr(a.dev_err, WB_DERR_TIMEOUT_MMA);
                 break;
@@ -730,7 +776,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
             ptx::tc_fence_after();
             const float *ls = lsum + (k & 1) * 4 * QT + row;
             const float inv = 1.0f / ((ls[0] + ls[QT]) + (ls[2 * QT] + ls[3 * QT]));
-            const uint32_t O_t = tmem + 256 + (uint32_t)((k & 1) * HDP) + lane_base;
+            const uint32_t O_t = tmem + L::O_COL + (uint32_t)((k % L::OBUF) * HDP) + lane_base;
             float *orow0 = a.o + ((long long)b * a.T + q0) * a.E + (long long)h * a.hd;
             const int nrow = min(32, a.T - q0);
 #pragma unroll 1
@@ -742,7 +788,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                 if (hc == HDP / 64 - 1) {
                     // O buffer and row sums read: the MMA and softmax may reuse them
                     ptx::tc_fence_before();
-                    ptx::mbar_arrive(ofree + (k & 1));
+                    ptx::mbar_arrive(ofree + k % L::OBUF);
                 }
 #pragma unroll
                 for (int c = 0; c < 2; c++) {
@@ -1075,6 +1121,196 @@ static int tc_attention_core(const TcLayerWeights &t, const WbSeqView &sv, const
                        E, Hg * hd, E, dev_err, st, msg, E, E);
 }
 
+// ---------------------------------------------------------------------------
+// Decode out_proj on the tensor cores (kv_cache.rs:330-335): y = o W_o^T + b
+// for the step's n < 64 rows, then lengths += 1.  The transposed product
+// y^T [E][n] = W_o [E][E] o^T: a CTA owns 128 output columns (M = 128 TMEM
+// lanes) and one of DO_KSPLIT slices of the inputs; the DO_KSPLIT CTAs of a
+// column tile form a thread-block cluster and sum their partial products
+// through distributed shared memory in rank order (deterministic).  The
+// kernel is a programmatic dependent of the attention grid: its W_o tile
+// (TMA), bias and the lengths to advance are read before griddepcontrol.wait,
+// the o rows (TMA) after it.  TF32 MMA, fp32 accumulation -- the same
+// precision as the out_proj GEMM of the prefill.
+// ---------------------------------------------------------------------------
+static constexpr int DO_KSPLIT = 4;   // cluster size: CTAs per column tile
+static constexpr int DO_KC_MAX = 256; // inputs per CTA (W tile <= 128 KB)
+static constexpr int DO_NMAX = 64;    // rows per call on this path
+
+struct DecodeOutTcArgs {
+    const float *bo;
+    float *y;
+    int n, N, E, KC;  // rows, rows padded to 16, n_embd, inputs per CTA
+    int cap, n_slots;
+    int32_t *len;
+    const int32_t *slot;
+    uint32_t *dev_err;
+};
+
+__global__ void __launch_bounds__(128, 1)
+    decode_out_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_o,
+                         DecodeOutTcArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const int nat = a.KC / 32;                     // 128-byte K atoms per CTA
+    const int W_BYTES = 128 * a.KC * 4;            // [nat][128 rows][32 fp32]
+    const int O_ATOM = a.N * 128;                  // [N rows][32 fp32]
+    uint8_t *sW = sm;
+    uint8_t *sO = sm + W_BYTES;
+    float *part = reinterpret_cast<float *>(sO + nat * O_ATOM);  // [N][128] this CTA's partial
+    uint64_t *bars = reinterpret_cast<uint64_t *>(part + a.N * 128);
+    uint64_t *wfull = bars, *ofull = bars + 1, *mdone = bars + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3);
+    const uint32_t rank = ptx::cluster_ctarank();
+    const int ct = blockIdx.x / DO_KSPLIT;         // column tile
+    const int c0 = ct * 128, k0 = (int)rank * a.KC;
+    const uint32_t tcols = a.N <= 32 ? 32 : 64;
+    if (tid == 0) {
+        for (int i = 0; i < 3; i++) ptx::mbar_init(bars + i, 1);
+        ptx::fence_mbar_init();
+    }
+    if (warp == 0) {
+        ptx::tmem_alloc(tmem_slot, tcols);
+        ptx::tmem_relinquish();
+    }
+    ptx::tc_fence_before();
+    __syncthreads();
+    ptx::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    // before the wait: the W_o tile, the bias, the lengths to advance
+    if (tid == 0) {
+        ptx::prefetch_tmap(&tm_w);
+        ptx::prefetch_tmap(&tm_o);
+        ptx::mbar_arrive_expect_tx(wfull, (uint32_t)W_BYTES);
+        for (int t = 0; t < nat; t++) ptx::tma_load_2d(sW + t * 16384, &tm_w, wfull, k0 + t * 32, c0);
+    }
+    const int col = c0 + tid;
+    const float bias = col < a.E ? __ldg(a.bo + col) : 0.0f;
+    const bool len_cta = blockIdx.x == 0;
+    int lslot = -1, lnew = 0;
+    if (len_cta && tid < a.n) {
+        const int sl = a.slot ? a.slot[tid] : tid;
+        if (sl >= 0 && sl < a.n_slots) {
+            const int cur = a.len[sl];
+            if (cur < a.cap) {
+                lslot = sl;
+                lnew = cur + 1;
+            }
+        }
+    }
+    ptx::griddep_wait();
+    // the attention grid is complete: the next grid of the stream may launch
+    ptx::griddep_launch_dependents();
+    bool ok = true;
+    if (tid == 0) {
+        ptx::mbar_arrive_expect_tx(ofull, (uint32_t)(nat * O_ATOM));
+        for (int t = 0; t < nat; t++) ptx::tma_load_2d(sO + t * O_ATOM, &tm_o, ofull, k0 + t * 32, 0);
+    } else if (tid == 32) {
+        const uint32_t idesc = ptx::idesc_tf32(128, a.N);
+        if (!ptx::mbar_wait(wfull, 0) || !ptx::mbar_wait(ofull, 0)) {
+            atomicOr(a.dev_err, WB_DERR_TIMEOUT_TMA);
+            ok = false;
+        } else {
+            ptx::tc_fence_after();
+            const uint32_t w0 = ptx::smem_u32(sW), o0 = ptx::smem_u32(sO);
+            for (int t = 0; t < nat; t++) {
+#pragma unroll
+                for (int k = 0; k < 4; k++) {  // 8 tf32 = 32 bytes of K per instruction
+                    const uint64_t ad = ptx::smem_desc(w0 + t * 16384 + k * 32, 16, 1024, ptx::UMMA_SW128);
+                    const uint64_t bd = ptx::smem_desc(o0 + t * O_ATOM + k * 32, 16, 1024, ptx::UMMA_SW128);
+                    ptx::mma_tf32(tmem, ad, bd, idesc, (t > 0 || k > 0));
+                }
+            }
+        }
+        ptx::mma_commit(mdone);
+    }
+    // partial y^T of this K slice: thread = output column (TMEM lane), its
+    // N rows -> part[r][tid]
+    const bool fin = ptx::mbar_wait(mdone, 0);
+    if (!fin && tid == 0) atomicOr(a.dev_err, WB_DERR_TIMEOUT_MMA);
+    ptx::tc_fence_after();
+    if (fin) {
+        const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+        for (int c = 0; c < a.N; c += 16) {
+            uint32_t r[16];
+            ptx::tmem_ld16(tmem + lane_base + c, r);
+            ptx::tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 16; i++) part[(c + i) * 128 + tid] = __uint_as_float(r[i]);
+        }
+    }
+    ptx::tc_fence_before();
+    ptx::cluster_sync();  // every CTA's partial is in its shared memory
+    // this CTA's share of the rows: sum the DO_KSPLIT partials in rank order
+    const int rows = (a.N + DO_KSPLIT - 1) / DO_KSPLIT;
+    const int r0 = (int)rank * rows, r1 = min(a.n, r0 + rows);
+    for (int r = r0; r < r1; r++) {
+        float v = 0.0f;
+#pragma unroll
+        for (int q = 0; q < DO_KSPLIT; q++) v += ptx::dsmem_ld(ptx::dsmem_addr(part + r * 128 + tid, (uint32_t)q));
+        if (col < a.E && fin) a.y[(long long)r * a.E + col] = v + bias;
+    }
+    if (len_cta && lslot >= 0) a.len[lslot] = lnew;
+    // after a timed-out wait the copies in flight land before the CTA leaves
+    if (tid == 32 && !ok) {
+        ptx::mbar_wait(wfull, 0, 200000000LL);
+        ptx::mbar_wait(ofull, 0, 200000000LL);
+    }
+    ptx::cluster_sync();  // no CTA leaves while another reads its partial
+    ptx::tc_fence_after();
+    if (warp == 0) ptx::tmem_dealloc(tmem, tcols);
+}
+
+// Whether the tensor-core decode out_proj covers this shape: n_embd a
+// multiple of 128 whose DO_KSPLIT slices are whole 32-input atoms of at
+// most DO_KC_MAX inputs, and fewer than DO_NMAX rows.
+static bool decode_out_tc_ok(int E, int n) {
+    return n >= 1 && n <= DO_NMAX && E % 128 == 0 && E % (DO_KSPLIT * 32) == 0 && E / DO_KSPLIT <= DO_KC_MAX;
+}
+
+static int launch_decode_out_tc(const float *o, const float *w_o32, const float *bo, float *y, int n, int E, int cap,
+                                int32_t *len, const int32_t *slot, int n_slots, uint32_t *dev_err, cudaStream_t st,
+                                std::string *msg) {
+    const int N = (n + 15) / 16 * 16, KC = E / DO_KSPLIT;
+    CUtensorMap tw, to;
+    int rc;
+    const uint64_t wd[2] = {(uint64_t)E, (uint64_t)E};
+    const uint64_t ws[1] = {(uint64_t)E * 4};
+    const uint32_t wb[2] = {32, 128};
+    if ((rc = make_tmap(&tw, w_o32, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, wd, ws, wb, CU_TENSOR_MAP_SWIZZLE_128B, msg)))
+        return rc;
+    const uint64_t od[2] = {(uint64_t)E, (uint64_t)n};
+    const uint32_t ob[2] = {32, (uint32_t)N};
+    if ((rc = make_tmap(&to, o, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, od, ws, ob, CU_TENSOR_MAP_SWIZZLE_128B, msg)))
+        return rc;
+    const size_t smem = (size_t)128 * KC * 4 + (size_t)(KC / 32) * N * 128 + (size_t)N * 128 * 4 + 64 + 1024;
+    DecodeOutTcArgs a{bo, y, n, N, E, KC, cap, n_slots, len, slot, dev_err};
+    cudaFuncSetAttribute(decode_out_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((E / 128) * DO_KSPLIT));
+    cfg.blockDim = dim3(128);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = DO_KSPLIT;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    ProfScope ps("decode_out", st);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, decode_out_tc_kernel, tw, to, a);
+    if (e == cudaSuccess) e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        *msg = std::string("decode out_proj launch failed: ") + cudaGetErrorString(e);
+        return WB_ECUDA;
+    }
+    return WB_OK;
+}
+
 int tc_gemm_bf16(const __nv_bfloat16 *A, const __nv_bfloat16 *B, const float *bias, float *C, int M, int N, int K,
                  uint32_t *dev_err, cudaStream_t st, std::string *msg) {
     return launch_gemm(false, A, B, bias, C, M, N, K, N, dev_err, st, msg);
@@ -1181,9 +1417,13 @@ int tc_kv_decode(const TcLayerWeights &t, const WbSeqView &sv, int32_t *len, int
         launch_len_update(len, sv.slot, n_seq, 1, 0, n_slots, cap, st);
         return launch_gemm(true, o, t.w_o32, t.b_o, y, n_seq, t.E, t.E, t.E, dev_err, st, msg);
     }
-    // few rows: the SIMT out_proj kernel (programmatic dependent of the
-    // attention grid), which also advances the lengths
-    rc = launch_decode_out(o, t.wo_t, t.b_o, y, n_seq, t.E, cap, len, sv.slot, n_slots, st, msg);
+    // few rows: the out_proj kernel (programmatic dependent of the attention
+    // grid), which also advances the lengths -- on the tensor cores where the
+    // shape allows, else the SIMT kernel
+    if (decode_out_tc_ok(t.E, n_seq))
+        rc = launch_decode_out_tc(o, t.w_o32, t.b_o, y, n_seq, t.E, cap, len, sv.slot, n_slots, dev_err, st, msg);
+    else
+        rc = launch_decode_out(o, t.wo_t, t.b_o, y, n_seq, t.E, cap, len, sv.slot, n_slots, st, msg);
     if (rc == WB_OK && ends_with_out) *ends_with_out = true;
     return rc;
 }
