@@ -539,6 +539,249 @@ __global__ void __launch_bounds__(VP_THREADS, 1) vproj_phase_kernel(VpArgs a) {
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
+// ---------------------------------------------------------------------------
+// Values and phases of a head_dim-64 layer without content, in one pass over
+// x (attn.rs:121-130, :155-165; kv_cache.rs:129-142): vphase_tc_kernel.
+// A CTA owns 128 rows and walks x one head's 64 input columns at a time
+// (chunk h), TMA'd into a 2-stage ring together with head h's value weights
+// (tf32 head and remainder) and the 64 phase-weight rows of those inputs:
+//   warps 2-9 (workers): the phase sums -- thread (row, output half) adds the
+//     chunk's 64 inputs to its H outputs (r, s of H/2 heads) with one fmaf
+//     per input in input order, the same sequential sum over the whole row
+//     as phase_fma_kernel; then they split the x chunk into tf32 head (in
+//     place) and remainder for the tensor core;
+//   warp 1 (MMA): values of head h, 3xTF32 on tcgen05: main = xh Wh, corr =
+//     xh Wl + xl Wh, into one of two TMEM buffer pairs;
+//   warps 10-13 (epilogue): value = main + corr + bias into the sequence
+//     view, overlapping the next chunk;
+//   warp 0: TMA producer.
+// After the last chunk the workers turn (r, s) into the phase and bucket.
+// ---------------------------------------------------------------------------
+static constexpr int VT_ROWS = 128;
+static constexpr int VT_THREADS = 14 * 32;
+static constexpr int VT_X = 128 * 64 * 4;          // x chunk (two 32-column SW128 atoms)
+static constexpr int VT_W = 64 * 64 * 4;           // one head's value weights (two atoms)
+static constexpr int VT_RS = 64 * 32 * 4;          // phase weights of 64 inputs, up to 16 heads
+static constexpr int VT_STAGE = 2 * VT_X + 2 * VT_W + VT_RS;
+static constexpr int VT_EPI = 4 * 32 * 33 * 4;
+static constexpr int VT_SMEM = 2 * VT_STAGE + VT_EPI + 128 + 1024;
+static_assert(VT_SMEM <= 232448, "vphase shared memory above the 227 KB limit");
+
+struct VtArgs {
+    int R, T, E;
+    const float *bias;  // value biases [H*64] (ProjTcWeights bias rows 0..n_v)
+    const float *brs;   // [H][2]
+    const float *wrs_t; // [E][H][2]
+    WbSeqView sv;
+    uint32_t *dev_err;
+};
+
+template <int H>
+__global__ void __launch_bounds__(VT_THREADS, 1)
+    vphase_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_wh,
+                     const __grid_constant__ CUtensorMap tm_wl, VtArgs a) {
+    static_assert(H % 4 == 0 && H <= 16, "heads per layer: a multiple of 4, at most 16");
+    constexpr int NO = H;  // (r, s) outputs per worker thread: H/2 heads
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sm + 2 * VT_STAGE + VT_EPI);
+    uint64_t *full = bars, *conv = bars + 2, *empty = bars + 4, *vfull = bars + 6, *vfree = bars + 8;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 10);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int m0 = blockIdx.x * VT_ROWS;
+    if (tid == 0) {
+        for (int i = 0; i < 10; i++) ptx::mbar_init(bars + i, (bars + i == vfree || bars + i == vfree + 1) ? 128 : 1);
+        ptx::fence_mbar_init();
+    }
+    if (warp == 1) {
+        ptx::tmem_alloc(tmem_slot, 256);
+        ptx::tmem_relinquish();
+    }
+    ptx::tc_fence_before();
+    __syncthreads();
+    ptx::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    auto stage = [&](int s) { return sm + s * VT_STAGE; };
+
+    if (warp == 0) {
+        // ---------------- producer
+        if (lane == 0) {
+            ptx::prefetch_tmap(&tm_x);
+            ptx::prefetch_tmap(&tm_wh);
+            ptx::prefetch_tmap(&tm_wl);
+            for (int h = 0; h < H; h++) {
+                const int s = h & 1;
+                if (h >= 2 && !ptx::mbar_wait(empty + s, ((h - 2) >> 1) & 1)) {
+                    atomicOr(a.dev_err, WB_DERR_TIMEOUT_MMA);
+                    break;
+                }
+                uint8_t *st = stage(s);
+                ptx::mbar_arrive_expect_tx(full + s, VT_X + 2 * VT_W + 64 * 2 * H * 4);
+                for (int t = 0; t < 2; t++) {
+                    ptx::tma_load_2d(st + t * (VT_X / 2), &tm_x, full + s, h * 64 + t * 32, m0);
+                    ptx::tma_load_2d(st + 2 * VT_X + t * (VT_W / 2), &tm_wh, full + s, h * 64 + t * 32, h * 64);
+                    ptx::tma_load_2d(st + 2 * VT_X + VT_W + t * (VT_W / 2), &tm_wl, full + s, h * 64 + t * 32, h * 64);
+                }
+                ptx::bulk_load(st + 2 * VT_X + 2 * VT_W, a.wrs_t + (size_t)h * 64 * 2 * H, 64 * 2 * H * 4, full + s);
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA: values of head h (3xTF32)
+        if (lane == 0) {
+            constexpr uint32_t IDESC = ptx::idesc_tf32(128, 64);
+            bool ok = true;
+            for (int h = 0; h < H && ok; h++) {
+                const int s = h & 1, b = h & 1;
+                if (!ptx::mbar_wait(conv + s, (h >> 1) & 1) ||
+                    (h >= 2 && !ptx::mbar_wait(vfree + b, ((h - 2) >> 1) & 1))) {
+                    atomicOr(a.dev_err, WB_DERR_TIMEOUT_TMA);
+                    ok = false;
+                    break;
+                }
+                ptx::tc_fence_after();
+                const uint32_t xh = ptx::smem_u32(stage(s)), xl = xh + VT_X;
+                const uint32_t wh = xh + 2 * VT_X, wl = wh + VT_W;
+                const uint32_t Dm = tmem + (uint32_t)(b * 128), Dc = Dm + 64;
+#pragma unroll
+                for (int t = 0; t < 2; t++)
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        const uint32_t ao = t * (VT_X / 2) + k * 32, bo = t * (VT_W / 2) + k * 32;
+                        const uint64_t dah = ptx::smem_desc(xh + ao, 16, 1024, ptx::UMMA_SW128);
+                        const uint64_t dal = ptx::smem_desc(xl + ao, 16, 1024, ptx::UMMA_SW128);
+                        const uint64_t dbh = ptx::smem_desc(wh + bo, 16, 1024, ptx::UMMA_SW128);
+                        const uint64_t dbl = ptx::smem_desc(wl + bo, 16, 1024, ptx::UMMA_SW128);
+                        ptx::mma_tf32(Dm, dah, dbh, IDESC, (t > 0 || k > 0));
+                        ptx::mma_tf32(Dc, dah, dbl, IDESC, (t > 0 || k > 0));
+                        ptx::mma_tf32(Dc, dal, dbh, IDESC, 1);
+                    }
+                ptx::mma_commit(empty + s);
+                ptx::mma_commit(vfull + b);
+            }
+        }
+        __syncwarp();
+    } else if (warp < 10) {
+        // ---------------- workers: phase sums, then the tf32 split of x
+        const int wt = tid - 64;                    // 0..255
+        const int row = wt & 127, oh = wt >> 7;     // output half: outputs oh*H .. oh*H + H - 1
+        float acc[NO];
+#pragma unroll
+        for (int o = 0; o < NO; o++) acc[o] = __ldg(a.brs + oh * NO + o);
+        bool ok = true;
+        for (int h = 0; h < H; h++) {
+            const int s = h & 1;
+            if (!ptx::mbar_wait(full + s, (h >> 1) & 1)) {
+                if (wt == 0) atomicOr(a.dev_err, WB_DERR_TIMEOUT_TMA);
+                ok = false;
+                break;
+            }
+            uint8_t *st = stage(s);
+            const float *wrs = reinterpret_cast<const float *>(st + 2 * VT_X + 2 * VT_W) + oh * NO;
+#pragma unroll 1
+            for (int t = 0; t < 2; t++) {
+                const uint8_t *xa = st + t * (VT_X / 2) + row * 128;
+#pragma unroll 2
+                for (int j = 0; j < 8; j++) {  // 16-byte chunk j: inputs 4j..4j+3 of this atom
+                    const float4 x4 = *reinterpret_cast<const float4 *>(xa + ((j ^ (row & 7)) << 4));
+                    const float xv[4] = {x4.x, x4.y, x4.z, x4.w};
+#pragma unroll
+                    for (int u = 0; u < 4; u++) {
+                        const float *wr = wrs + (t * 32 + j * 4 + u) * 2 * H;
+#pragma unroll
+                        for (int o4 = 0; o4 < NO / 4; o4++) {
+                            const float4 w4 = *reinterpret_cast<const float4 *>(wr + o4 * 4);
+                            acc[o4 * 4 + 0] = fmaf(w4.x, xv[u], acc[o4 * 4 + 0]);
+                            acc[o4 * 4 + 1] = fmaf(w4.y, xv[u], acc[o4 * 4 + 1]);
+                            acc[o4 * 4 + 2] = fmaf(w4.z, xv[u], acc[o4 * 4 + 2]);
+                            acc[o4 * 4 + 3] = fmaf(w4.w, xv[u], acc[o4 * 4 + 3]);
+                        }
+                    }
+                }
+            }
+            // every worker has read the chunk: split it (element-wise, the
+            // swizzled layout is kept) into the tf32 head and the remainder
+            asm volatile("bar.sync 1, 256;" ::: "memory");
+            float4 *X = reinterpret_cast<float4 *>(st);
+            float4 *XL = reinterpret_cast<float4 *>(st + VT_X);
+#pragma unroll 4
+            for (int e = wt; e < VT_X / 16; e += 256) {
+                const float4 v = X[e];
+                float4 hi, lo;
+                hi.x = __uint_as_float(tf32_rna(v.x));
+                hi.y = __uint_as_float(tf32_rna(v.y));
+                hi.z = __uint_as_float(tf32_rna(v.z));
+                hi.w = __uint_as_float(tf32_rna(v.w));
+                lo.x = v.x - hi.x;
+                lo.y = v.y - hi.y;
+                lo.z = v.z - hi.z;
+                lo.w = v.w - hi.w;
+                X[e] = hi;
+                XL[e] = lo;
+            }
+            ptx::fence_proxy_async_smem();
+            asm volatile("bar.sync 1, 256;" ::: "memory");
+            if (wt == 0) ptx::mbar_arrive(conv + s);
+        }
+        // phases and buckets of this thread's H/2 heads (attn.rs:127, :171-174)
+        const int m = m0 + row;
+        if (ok && m < a.R) {
+            const int b = m / a.T, t = m - b * a.T;
+            const long long base = (long long)(a.sv.slot ? a.sv.slot[b] : b) * a.sv.seq_stride + t;
+#pragma unroll
+            for (int i = 0; i < NO / 2; i++) {
+                const int hh = oh * (NO / 2) + i;
+                const float th = atan2f(acc[2 * i + 1], acc[2 * i]);
+                a.sv.theta[base + (long long)hh * a.sv.cap] = th;
+                a.sv.bucket[base + (long long)hh * a.sv.cap] = (uint8_t)phase_to_bucket(th);
+            }
+        }
+    } else {
+        // ---------------- value epilogue (warps 10-13: lane groups 2, 3, 0, 1)
+        const int q = warp & 3;
+        const int row = q * 32 + lane, m = m0 + row;
+        const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+        float *buf = reinterpret_cast<float *>(sm + 2 * VT_STAGE) + (warp - 10) * 32 * 33;
+        long long base = -1;
+        if (m < a.R) {
+            const int b = m / a.T, t = m - b * a.T;
+            base = (long long)(a.sv.slot ? a.sv.slot[b] : b) * a.sv.seq_stride + t;
+        }
+        for (int h = 0; h < H; h++) {
+            const int b = h & 1;
+            if (!ptx::mbar_wait(vfull + b, (h >> 1) & 1)) {
+                if (lane == 0) atomicOr(a.dev_err, WB_DERR_TIMEOUT_MMA);
+                break;
+            }
+            ptx::tc_fence_after();
+            const uint32_t Dm = tmem + (uint32_t)(b * 128) + lane_base;
+#pragma unroll 1
+            for (int c = 0; c < 2; c++) {
+                uint32_t r[32], rc[32];
+                ptx::tmem_ld32(Dm + c * 32, r);
+                ptx::tmem_ld32(Dm + 64 + c * 32, rc);
+                ptx::tmem_ld_wait();
+                if (c == 1) {
+                    ptx::tc_fence_before();
+                    ptx::mbar_arrive(vfree + b);
+                }
+#pragma unroll
+                for (int i = 0; i < 32; i++) r[i] = __float_as_uint(__uint_as_float(r[i]) + __uint_as_float(rc[i]));
+                warp_stage32(buf, r, lane);
+                const int d = c * 32 + lane;
+                const float bv = __ldg(a.bias + h * 64 + d);
+#pragma unroll 4
+                for (int jr = 0; jr < 32; jr++) {
+                    const long long rb = __shfl_sync(0xffffffffu, base, jr);
+                    if (rb >= 0) a.sv.v[(rb + (long long)h * a.sv.cap) * 64 + d] = buf[jr * 33 + lane] + bv;
+                }
+            }
+        }
+    }
+    ptx::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) ptx::tmem_dealloc(tmem, 256);
+}
+
 static PFN_cuTensorMapEncodeTiled_v12000 proj_encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
     if (!fn) {
@@ -553,7 +796,8 @@ static PFN_cuTensorMapEncodeTiled_v12000 proj_encode_fn() {
     return fn;
 }
 
-static int tmap_2d_f32(CUtensorMap *m, const void *base, uint64_t inner, uint64_t outer, std::string *msg) {
+static int tmap_2d_f32(CUtensorMap *m, const void *base, uint64_t inner, uint64_t outer, std::string *msg,
+                       uint32_t box_rows = 128) {
     auto fn = proj_encode_fn();
     if (!fn) {
         *msg = "cuTensorMapEncodeTiled unavailable";
@@ -561,7 +805,7 @@ static int tmap_2d_f32(CUtensorMap *m, const void *base, uint64_t inner, uint64_
     }
     const uint64_t dims[2] = {inner, outer};
     const uint64_t strides[1] = {inner * 4};
-    const uint32_t box[2] = {PBK, 128};
+    const uint32_t box[2] = {PBK, box_rows};
     const uint32_t es[2] = {1, 1};
     CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void *>(base), dims, strides, box, es,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -649,7 +893,34 @@ int launch_proj_tc(const ProjTcWeights &p, const float *wrs_t, const float *brs,
     if (R <= 0) return WB_OK;
     const bool simt_v = wv_t && bv && (p.hd == 64 || p.hd == 48) && Hg <= 16 && R <= INT32_MAX &&
                         (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(bv) & 15) == 0;
-    if (simt_v) {
+    const bool tc_v = simt_v && p.hd == 64 && h0 == 0 && Hg == p.H && (p.H == 8 || p.H == 12 || p.H == 16);
+    if (tc_v) {
+        // values (3xTF32 tcgen05) and phases (sequential fp32) in one pass
+        CUtensorMap tx, twh, twl;
+        int rc;
+        if ((rc = tmap_2d_f32(&tx, x, (uint64_t)p.E, (uint64_t)R, msg))) return rc;
+        if ((rc = tmap_2d_f32(&twh, p.w_hi, (uint64_t)p.E, (uint64_t)p.N, msg, 64))) return rc;
+        if ((rc = tmap_2d_f32(&twl, p.w_lo, (uint64_t)p.E, (uint64_t)p.N, msg, 64))) return rc;
+        VtArgs va{(int)R, T, p.E, p.bias, brs, wrs_t, sv, dev_err};
+        ProfScope ps("proj_vphase", st);
+        const unsigned grid = (unsigned)((R + VT_ROWS - 1) / VT_ROWS);
+        if (p.H == 8) {
+            cudaFuncSetAttribute(vphase_tc_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, VT_SMEM);
+            vphase_tc_kernel<8><<<grid, VT_THREADS, VT_SMEM, st>>>(tx, twh, twl, va);
+        } else if (p.H == 12) {
+            cudaFuncSetAttribute(vphase_tc_kernel<12>, cudaFuncAttributeMaxDynamicSharedMemorySize, VT_SMEM);
+            vphase_tc_kernel<12><<<grid, VT_THREADS, VT_SMEM, st>>>(tx, twh, twl, va);
+        } else {
+            cudaFuncSetAttribute(vphase_tc_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, VT_SMEM);
+            vphase_tc_kernel<16><<<grid, VT_THREADS, VT_SMEM, st>>>(tx, twh, twl, va);
+        }
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) {
+            *msg = std::string("projection launch failed: ") + cudaGetErrorString(e);
+            return WB_ECUDA;
+        }
+        if (!content) return WB_OK;
+    } else if (simt_v) {
         // values and phases in one fp32 pass; the GEMM below keeps only the
         // content columns (if any)
         VpArgs va{x, wv_t, bv, wrs_t, brs, (int)R, p.E, p.H, T, h0, Hg, sv};

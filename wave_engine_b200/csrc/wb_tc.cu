@@ -344,17 +344,16 @@ struct AttnSmem {
     static constexpr int OFF_LSUM = OFF_SLOT + ATT_SLOTS * (int)sizeof(AttnItem);  // [2][4][QT] row-sum partials
     static constexpr int OFF_BAR = OFF_LSUM + 2 * 4 * QT * 4;
     // barriers: qfull[2], qfree[2], kvfull[ST], kvfree[ST], sfull[2], pready[2],
-    // ofull[2], ofree[2], lready[2], itemfull[SLOTS], itemfree[SLOTS], mmadone,
-    // sfree[2], pfree[2]
-    static constexpr int NBAR = 4 + 2 * ST + 10 + 2 * ATT_SLOTS + 1 + 4;
-    // TMEM columns: S0 [0,128), S1 [128,256), then OBUF O buffers of HDP
-    // columns, then P0, P1 (64 columns each: 128 bf16 keys packed in pairs)
+    // ofull[2], ofree[2], lready[2], itemfull[SLOTS], itemfree[SLOTS], mmadone
+    static constexpr int NBAR = 4 + 2 * ST + 10 + 2 * ATT_SLOTS + 1;
+    // TMEM columns: S0 [0,128), S1 [128,256) (P(g) is written over the first
+    // half of each thread's S(g) columns), then OBUF O buffers of 2*HDP
+    // columns: the value-hi products in the first HDP, value-lo in the rest
     static constexpr int OBUF = HDP == 64 ? 2 : 1;
     static constexpr int O_COL = 256;
-    static constexpr int P_COL = O_COL + OBUF * HDP;
     static constexpr int BYTES = OFF_BAR + NBAR * 8 + 16 + 1024;  // + TMEM slot, alignment slack
     static_assert(BYTES <= 232448, "attention shared memory above the 227 KB limit");
-    static_assert(P_COL + 128 <= 512, "TMEM: two S, OBUF O and two P buffers");
+    static_assert(O_COL + OBUF * 2 * HDP <= 512, "TMEM: two S and OBUF O buffers");
 };
 
 // Bounded mbarrier wait that also gives up once another role has raised the
@@ -393,7 +392,7 @@ template <int HDP, int FW>
 __global__ void __launch_bounds__(ATT_THREADS, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_vh, const __grid_constant__ CUtensorMap tm_vl,
-                   AttnTcArgs a, int hdn) {
+                   AttnTcArgs a) {
     using L = AttnSmem<HDP, FW>;
     constexpr int ST = L::ST;
     extern __shared__ uint8_t smem_raw[];
@@ -404,8 +403,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     uint64_t *sfull = kvfree + ST, *pready = sfull + 2, *ofull = pready + 2, *ofree = ofull + 2;
     uint64_t *lready = ofree + 2, *itemfull = lready + 2, *itemfree = itemfull + ATT_SLOTS;
     uint64_t *mmadone = itemfree + ATT_SLOTS;
-    uint64_t *sfree = mmadone + 1, *pfree = sfree + 2;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(pfree + 2);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mmadone + 1);
     AttnItem *slots = reinterpret_cast<AttnItem *>(sm + L::OFF_SLOT);
     float *lsum = reinterpret_cast<float *>(sm + L::OFF_LSUM);
     __shared__ int s_abort;
@@ -416,8 +414,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         for (int i = 0; i < L::NBAR; i++) {
             uint64_t *bb = bars + i;
             uint32_t cnt = 1;
-            if (bb == pready || bb == pready + 1 || bb == sfree || bb == sfree + 1)
-                cnt = ATT_SOFTMAX_WARPS / 2 * 32;  // one softmax group per tile
+            if (bb == pready || bb == pready + 1) cnt = ATT_SOFTMAX_WARPS / 2 * 32;  // one softmax group per tile
             else if (bb == lready || bb == lready + 1) cnt = ATT_SOFTMAX_WARPS * 32;
             else if (bb == ofree || bb == ofree + 1) cnt = ATT_EPI_WARPS * 32;
             else if (bb >= itemfull && bb < itemfull + ATT_SLOTS) cnt = 32;
@@ -544,16 +541,21 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         // ---------------- MMA issuer
         if (lane == 0) {
             constexpr uint32_t IDESC_QK = ptx::idesc_bf16(128, 128, 0, 0);
-            const uint32_t idesc_pv = ptx::idesc_bf16(128, hdn, 0, 1);
+            // PV: N = 2*HDP, the value hi and lo tiles side by side (adjacent
+            // 64-column atoms of the stage), O hi | O lo
+            constexpr uint32_t IDESC_PV = ptx::idesc_bf16(128, 2 * HDP, 0, 1);
             const uint32_t sQ0 = ptx::smem_u32(sm + L::OFF_Q);
             int kq = 0, jq = 0;                // next QK: item, tile
             long long gq = 0, gp = 0;          // next QK / PV global tile
             int kp = 0, jp = 0;                // next PV: item, tile
             bool qk_end = false, ok = true;
             // Event loop: issue whichever of PV(gp) and QK(gq) has its inputs
-            // ready (non-blocking barrier tests), PV first.  QK(gq) writes S
-            // buffer gq & 1 once the softmax has read S(gq - 2) (sfree), so it
-            // can run ahead of PV(gq - 2); PV(gp) reads P buffer gp & 1.
+            // ready (non-blocking barrier tests), PV first.  Each tcgen05.mma
+            // costs the issuing thread far more than its tensor work at these
+            // sizes, so a tile is 8 PV MMAs (N = 2*HDP) and FW/16 QK MMAs, and
+            // the thread never blocks on one operation while the other could
+            // go.  QK(gq) writes S buffer gq & 1, which holds P(gq - 2) until
+            // PV(gq - 2) is issued (the tensor pipe executes in issue order).
             int qstate = 0;  // QK(gq): 0 item descriptor, 1 Q tile, 2 S buffer, 3 K/V tile
             long long t_last = clock64();
             while (ok) {
@@ -567,21 +569,17 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                         ptx::mbar_test(pready + (gp & 1), (uint32_t)((gp >> 1) & 1));
                     if (ready) {
                         ptx::tc_fence_after();
-                        const uint32_t O_t = tmem + L::O_COL + (uint32_t)(ob * HDP);
-                        const uint32_t P_t = tmem + L::P_COL + (uint32_t)((gp & 1) * 64);
-                        const uint32_t sV = ptx::smem_u32(sm + L::OFF_V + (int)(gp % ST) * L::V_BYTES);
+                        const uint32_t O_t = tmem + L::O_COL + (uint32_t)(ob * 2 * HDP);
+                        const uint32_t P_t = tmem + (uint32_t)((gp & 1) * 128);
+                        const uint64_t vd0 = ptx::smem_desc(ptx::smem_u32(sm + L::OFF_V + (int)(gp % ST) * L::V_BYTES),
+                                                            KT * 128, 1024, ptx::UMMA_SW128);
 #pragma unroll
                         for (int kk = 0; kk < KT / 16; kk++) {
-                            // keys 16kk..16kk+15: packed two per column
-                            const uint32_t a_t = P_t + (uint32_t)(8 * kk);
-                            const uint64_t bh_d = ptx::smem_desc(sV + kk * 2048, KT * 128, 1024, ptx::UMMA_SW128);
-                            const uint64_t bl_d =
-                                ptx::smem_desc(sV + L::VPART + kk * 2048, KT * 128, 1024, ptx::UMMA_SW128);
-                            ptx::mma_bf16_ta(O_t, a_t, bh_d, idesc_pv, (jp > 0 || kk > 0));
-                            ptx::mma_bf16_ta(O_t, a_t, bl_d, idesc_pv, 1);
+                            // keys 16kk..16kk+15: half kk/4 of the tile (its S columns 64h..), packed two per column
+                            const uint32_t a_t = P_t + (uint32_t)(64 * (kk >> 2) + 8 * (kk & 3));
+                            ptx::mma_bf16_ta(O_t, a_t, vd0 + (uint64_t)(kk * 2048 >> 4), IDESC_PV, (jp > 0 || kk > 0));
                         }
                         ptx::mma_commit(kvfree + (int)(gp % ST));
-                        ptx::mma_commit(pfree + (gp & 1));
                         gp++;
                         if (++jp == slots[sl].qt + 1) {
                             ptx::mma_commit(ofull + ob);
@@ -603,20 +601,19 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                         qstate = 2;
                     }
                     if (qstate == 1 && ptx::mbar_test(qfull + (kq & 1), (kq >> 1) & 1)) qstate = 2;
-                    if (qstate == 2 && (gq < 2 || ptx::mbar_test(sfree + (gq & 1), (uint32_t)(((gq - 2) >> 1) & 1))))
-                        qstate = 3;
+                    // S buffer gq & 1 holds P(gq - 2) until PV(gq - 2) is issued; the
+                    // tensor pipe runs QK(gq) after it in issue order
+                    if (qstate == 2 && gq <= gp + 1) qstate = 3;
                     if (qstate == 3 && ptx::mbar_test(kvfull + (int)(gq % ST), (uint32_t)((gq / ST) & 1))) {
                         ptx::tc_fence_after();
                         const int st = (int)(gq % ST);
                         const uint32_t sK = ptx::smem_u32(sm + L::OFF_K + st * L::K_BYTES);
                         const uint32_t S_t = tmem + (uint32_t)((gq & 1) * 128);
                         const uint32_t sQ = sQ0 + (uint32_t)((kq & 1) * L::Q_BYTES);
+                        const uint64_t ad0 = ptx::smem_desc(sQ, 16, F_SBO, F_SW), bd0 = ptx::smem_desc(sK, 16, F_SBO, F_SW);
 #pragma unroll
-                        for (int kk = 0; kk < FW / 16; kk++) {
-                            const uint64_t ad = ptx::smem_desc(sQ + kk * 32, 16, F_SBO, F_SW);
-                            const uint64_t bd = ptx::smem_desc(sK + kk * 32, 16, F_SBO, F_SW);
-                            ptx::mma_bf16(S_t, ad, bd, IDESC_QK, kk > 0);
-                        }
+                        for (int kk = 0; kk < FW / 16; kk++)
+                            ptx::mma_bf16(S_t, ad0 + (uint64_t)(kk * 2), bd0 + (uint64_t)(kk * 2), IDESC_QK, kk > 0);
                         ptx::mma_commit(sfull + (gq & 1));
                         gq++;
                         if (++jq == slots[kq % ATT_SLOTS].qt + 1) {
@@ -721,20 +718,11 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                     exps(r, pk0, half * 64);
                     ptx::tmem_ld32(S_t + 32, r);
                     ptx::tmem_ld_wait();
-                    // S(g) is read: its buffer may take QK(g + 2)
-                    ptx::tc_fence_before();
-                    ptx::mbar_arrive(sfree + grp);
                     exps(r, pk1, half * 64 + 32);
                 }
-                // P buffer grp is free once PV(g - 2) has completed
-                if (g >= 2 && !att_wait(pfree + grp, (uint32_t)(((g - 2) >> 1) & 1), abort_flag)) {
-                    atomicOr(a.dev_err, WB_DERR_TIMEOUT_MMA);
-                    ok = false;
-                    break;
-                }
-                const uint32_t P_t = tmem + L::P_COL + (uint32_t)(grp * 64 + half * 32) + lane_base;
-                ptx::tmem_st16(P_t, pk0);
-                ptx::tmem_st16(P_t + 16, pk1);
+                // P over the first half of this thread's (already read) S columns
+                ptx::tmem_st16(S_t, pk0);
+                ptx::tmem_st16(S_t + 16, pk1);
                 ptx::tmem_st_wait();
                 ptx::tc_fence_before();
                 ptx::mbar_arrive(pready + grp);
@@ -776,30 +764,29 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
             ptx::tc_fence_after();
             const float *ls = lsum + (k & 1) * 4 * QT + row;
             const float inv = 1.0f / ((ls[0] + ls[QT]) + (ls[2 * QT] + ls[3 * QT]));
-            const uint32_t O_t = tmem + L::O_COL + (uint32_t)((k % L::OBUF) * HDP) + lane_base;
+            const uint32_t O_t = tmem + L::O_COL + (uint32_t)((k % L::OBUF) * 2 * HDP) + lane_base;
             float *orow0 = a.o + ((long long)b * a.T + q0) * a.E + (long long)h * a.hd;
             const int nrow = min(32, a.T - q0);
 #pragma unroll 1
-            for (int hc = 0; hc < HDP / 64; hc++) {
-                uint32_t r[2][32];
-                ptx::tmem_ld32(O_t + hc * 64, r[0]);
-                ptx::tmem_ld32(O_t + hc * 64 + 32, r[1]);
+            for (int c = 0; c < HDP / 32; c++) {
+                // 32 output columns: value-hi products + value-lo products
+                uint32_t r[32], rl[32];
+                ptx::tmem_ld32(O_t + c * 32, r);
+                ptx::tmem_ld32(O_t + HDP + c * 32, rl);
                 ptx::tmem_ld_wait();
-                if (hc == HDP / 64 - 1) {
+                if (c == HDP / 32 - 1) {
                     // O buffer and row sums read: the MMA and softmax may reuse them
                     ptx::tc_fence_before();
                     ptx::mbar_arrive(ofree + k % L::OBUF);
                 }
 #pragma unroll
-                for (int c = 0; c < 2; c++) {
-#pragma unroll
-                    for (int i = 0; i < 32; i++) r[c][i] = __float_as_uint(__uint_as_float(r[c][i]) * inv);
-                    warp_stage32(buf, r[c], lane);
-                    const int d = hc * 64 + c * 32 + lane;
-                    if (d < a.hd)
+                for (int i = 0; i < 32; i++)
+                    r[i] = __float_as_uint((__uint_as_float(r[i]) + __uint_as_float(rl[i])) * inv);
+                warp_stage32(buf, r, lane);
+                const int d = c * 32 + lane;
+                if (d < a.hd)
 #pragma unroll 4
-                        for (int jr = 0; jr < nrow; jr++) orow0[(long long)jr * a.E + d] = buf[jr * 33 + lane];
-                }
+                    for (int jr = 0; jr < nrow; jr++) orow0[(long long)jr * a.E + d] = buf[jr * 33 + lane];
             }
         }
     }
@@ -1027,13 +1014,13 @@ static int launch_gemm(bool tf32, const void *A, const void *W, const float *bia
 
 template <int HDP, int FW>
 static int launch_attn_tc(const CUtensorMap &tq, const CUtensorMap &tk, const CUtensorMap &tvh,
-                          const CUtensorMap &tvl, const AttnTcArgs &aa, int hdn, int sm_count, cudaStream_t st,
+                          const CUtensorMap &tvl, const AttnTcArgs &aa, int sm_count, cudaStream_t st,
                           std::string *msg) {
     using L = AttnSmem<HDP, FW>;
     const int grid = std::max(1, std::min(aa.n_items, sm_count));
     ProfScope ps("attn_tc", st);
     cudaFuncSetAttribute(attn_tc_kernel<HDP, FW>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES);
-    attn_tc_kernel<HDP, FW><<<grid, ATT_THREADS, L::BYTES, st>>>(tq, tk, tvh, tvl, aa, hdn);
+    attn_tc_kernel<HDP, FW><<<grid, ATT_THREADS, L::BYTES, st>>>(tq, tk, tvh, tvl, aa);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         *msg = std::string("attention launch failed: ") + cudaGetErrorString(e);
@@ -1051,7 +1038,6 @@ static int tc_attention_core(const TcLayerWeights &t, const WbSeqView &sv, const
                              uint32_t *dev_err, int sm_count, cudaStream_t st, std::string *msg) {
     const int H = t.H, hd = t.hd, E = t.E;
     const int hdp = hd <= 64 ? 64 : 128;
-    const int hdn = (hd + 15) / 16 * 16;
     const int fw = core_fw(content != nullptr);
     const long long BH = (long long)B * Hg, R = (long long)B * T;
     const int n_qt = (T + QT - 1) / QT;
@@ -1102,11 +1088,11 @@ static int tc_attention_core(const TcLayerWeights &t, const WbSeqView &sv, const
     }
     AttnTcArgs aa{(int)BH, H, T, hd, n_qt, Hg, h0, (int)(BH * n_qt), m0, sp, cn, cm, sv, ob, E, sched, dev_err};
     if (hdp == 64)
-        rc = fw == 64 ? launch_attn_tc<64, 64>(tq, tk, tvh, tvl, aa, hdn, sm_count, st, msg)
-                      : launch_attn_tc<64, 16>(tq, tk, tvh, tvl, aa, hdn, sm_count, st, msg);
+        rc = fw == 64 ? launch_attn_tc<64, 64>(tq, tk, tvh, tvl, aa, sm_count, st, msg)
+                      : launch_attn_tc<64, 16>(tq, tk, tvh, tvl, aa, sm_count, st, msg);
     else
-        rc = fw == 64 ? launch_attn_tc<128, 64>(tq, tk, tvh, tvl, aa, hdn, sm_count, st, msg)
-                      : launch_attn_tc<128, 16>(tq, tk, tvh, tvl, aa, hdn, sm_count, st, msg);
+        rc = fw == 64 ? launch_attn_tc<128, 64>(tq, tk, tvh, tvl, aa, sm_count, st, msg)
+                      : launch_attn_tc<128, 16>(tq, tk, tvh, tvl, aa, sm_count, st, msg);
     if (rc) return rc;
     // query tiles whose scores may exceed the fixed-shift bound (content
     // only): recomputed in fp32 from the list the attention kernel built
@@ -1119,196 +1105,6 @@ static int tc_attention_core(const TcLayerWeights &t, const WbSeqView &sv, const
         return launch_gemm(true, ob, t.w_o32, add_bias ? t.b_o : nullptr, y, (int)R, E, E, E, dev_err, st, msg);
     return launch_gemm(true, ob + (size_t)h0 * hd, t.w_o32 + (size_t)h0 * hd, add_bias ? t.b_o : nullptr, y, (int)R,
                        E, Hg * hd, E, dev_err, st, msg, E, E);
-}
-
-// ---------------------------------------------------------------------------
-// Decode out_proj on the tensor cores (kv_cache.rs:330-335): y = o W_o^T + b
-// for the step's n < 64 rows, then lengths += 1.  The transposed product
-// y^T [E][n] = W_o [E][E] o^T: a CTA owns 128 output columns (M = 128 TMEM
-// lanes) and one of DO_KSPLIT slices of the inputs; the DO_KSPLIT CTAs of a
-// column tile form a thread-block cluster and sum their partial products
-// through distributed shared memory in rank order (deterministic).  The
-// kernel is a programmatic dependent of the attention grid: its W_o tile
-// (TMA), bias and the lengths to advance are read before griddepcontrol.wait,
-// the o rows (TMA) after it.  TF32 MMA, fp32 accumulation -- the same
-// precision as the out_proj GEMM of the prefill.
-// ---------------------------------------------------------------------------
-static constexpr int DO_KSPLIT = 4;   // cluster size: CTAs per column tile
-static constexpr int DO_KC_MAX = 256; // inputs per CTA (W tile <= 128 KB)
-static constexpr int DO_NMAX = 64;    // rows per call on this path
-
-struct DecodeOutTcArgs {
-    const float *bo;
-    float *y;
-    int n, N, E, KC;  // rows, rows padded to 16, n_embd, inputs per CTA
-    int cap, n_slots;
-    int32_t *len;
-    const int32_t *slot;
-    uint32_t *dev_err;
-};
-
-__global__ void __launch_bounds__(128, 1)
-    decode_out_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_o,
-                         DecodeOutTcArgs a) {
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    const int tid = threadIdx.x, warp = tid >> 5;
-    const int nat = a.KC / 32;                     // 128-byte K atoms per CTA
-    const int W_BYTES = 128 * a.KC * 4;            // [nat][128 rows][32 fp32]
-    const int O_ATOM = a.N * 128;                  // [N rows][32 fp32]
-    uint8_t *sW = sm;
-    uint8_t *sO = sm + W_BYTES;
-    float *part = reinterpret_cast<float *>(sO + nat * O_ATOM);  // [N][128] this CTA's partial
-    uint64_t *bars = reinterpret_cast<uint64_t *>(part + a.N * 128);
-    uint64_t *wfull = bars, *ofull = bars + 1, *mdone = bars + 2;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3);
-    const uint32_t rank = ptx::cluster_ctarank();
-    const int ct = blockIdx.x / DO_KSPLIT;         // column tile
-    const int c0 = ct * 128, k0 = (int)rank * a.KC;
-    const uint32_t tcols = a.N <= 32 ? 32 : 64;
-    if (tid == 0) {
-        for (int i = 0; i < 3; i++) ptx::mbar_init(bars + i, 1);
-        ptx::fence_mbar_init();
-    }
-    if (warp == 0) {
-        ptx::tmem_alloc(tmem_slot, tcols);
-        ptx::tmem_relinquish();
-    }
-    ptx::tc_fence_before();
-    __syncthreads();
-    ptx::tc_fence_after();
-    const uint32_t tmem = *tmem_slot;
-    // before the wait: the W_o tile, the bias, the lengths to advance
-    if (tid == 0) {
-        ptx::prefetch_tmap(&tm_w);
-        ptx::prefetch_tmap(&tm_o);
-        ptx::mbar_arrive_expect_tx(wfull, (uint32_t)W_BYTES);
-        for (int t = 0; t < nat; t++) ptx::tma_load_2d(sW + t * 16384, &tm_w, wfull, k0 + t * 32, c0);
-    }
-    const int col = c0 + tid;
-    const float bias = col < a.E ? __ldg(a.bo + col) : 0.0f;
-    const bool len_cta = blockIdx.x == 0;
-    int lslot = -1, lnew = 0;
-    if (len_cta && tid < a.n) {
-        const int sl = a.slot ? a.slot[tid] : tid;
-        if (sl >= 0 && sl < a.n_slots) {
-            const int cur = a.len[sl];
-            if (cur < a.cap) {
-                lslot = sl;
-                lnew = cur + 1;
-            }
-        }
-    }
-    ptx::griddep_wait();
-    // the attention grid is complete: the next grid of the stream may launch
-    ptx::griddep_launch_dependents();
-    bool ok = true;
-    if (tid == 0) {
-        ptx::mbar_arrive_expect_tx(ofull, (uint32_t)(nat * O_ATOM));
-        for (int t = 0; t < nat; t++) ptx::tma_load_2d(sO + t * O_ATOM, &tm_o, ofull, k0 + t * 32, 0);
-    } else if (tid == 32) {
-        const uint32_t idesc = ptx::idesc_tf32(128, a.N);
-        if (!ptx::mbar_wait(wfull, 0) || !ptx::mbar_wait(ofull, 0)) {
-            atomicOr(a.dev_err, WB_DERR_TIMEOUT_TMA);
-            ok = false;
-        } else {
-            ptx::tc_fence_after();
-            const uint32_t w0 = ptx::smem_u32(sW), o0 = ptx::smem_u32(sO);
-            for (int t = 0; t < nat; t++) {
-#pragma unroll
-                for (int k = 0; k < 4; k++) {  // 8 tf32 = 32 bytes of K per instruction
-                    const uint64_t ad = ptx::smem_desc(w0 + t * 16384 + k * 32, 16, 1024, ptx::UMMA_SW128);
-                    const uint64_t bd = ptx::smem_desc(o0 + t * O_ATOM + k * 32, 16, 1024, ptx::UMMA_SW128);
-                    ptx::mma_tf32(tmem, ad, bd, idesc, (t > 0 || k > 0));
-                }
-            }
-        }
-        ptx::mma_commit(mdone);
-    }
-    // partial y^T of this K slice: thread = output column (TMEM lane), its
-    // N rows -> part[r][tid]
-    const bool fin = ptx::mbar_wait(mdone, 0);
-    if (!fin && tid == 0) atomicOr(a.dev_err, WB_DERR_TIMEOUT_MMA);
-    ptx::tc_fence_after();
-    if (fin) {
-        const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-        for (int c = 0; c < a.N; c += 16) {
-            uint32_t r[16];
-            ptx::tmem_ld16(tmem + lane_base + c, r);
-            ptx::tmem_ld_wait();
-#pragma unroll
-            for (int i = 0; i < 16; i++) part[(c + i) * 128 + tid] = __uint_as_float(r[i]);
-        }
-    }
-    ptx::tc_fence_before();
-    ptx::cluster_sync();  // every CTA's partial is in its shared memory
-    // this CTA's share of the rows: sum the DO_KSPLIT partials in rank order
-    const int rows = (a.N + DO_KSPLIT - 1) / DO_KSPLIT;
-    const int r0 = (int)rank * rows, r1 = min(a.n, r0 + rows);
-    for (int r = r0; r < r1; r++) {
-        float v = 0.0f;
-#pragma unroll
-        for (int q = 0; q < DO_KSPLIT; q++) v += ptx::dsmem_ld(ptx::dsmem_addr(part + r * 128 + tid, (uint32_t)q));
-        if (col < a.E && fin) a.y[(long long)r * a.E + col] = v + bias;
-    }
-    if (len_cta && lslot >= 0) a.len[lslot] = lnew;
-    // after a timed-out wait the copies in flight land before the CTA leaves
-    if (tid == 32 && !ok) {
-        ptx::mbar_wait(wfull, 0, 200000000LL);
-        ptx::mbar_wait(ofull, 0, 200000000LL);
-    }
-    ptx::cluster_sync();  // no CTA leaves while another reads its partial
-    ptx::tc_fence_after();
-    if (warp == 0) ptx::tmem_dealloc(tmem, tcols);
-}
-
-// Whether the tensor-core decode out_proj covers this shape: n_embd a
-// multiple of 128 whose DO_KSPLIT slices are whole 32-input atoms of at
-// most DO_KC_MAX inputs, and fewer than DO_NMAX rows.
-static bool decode_out_tc_ok(int E, int n) {
-    return n >= 1 && n <= DO_NMAX && E % 128 == 0 && E % (DO_KSPLIT * 32) == 0 && E / DO_KSPLIT <= DO_KC_MAX;
-}
-
-static int launch_decode_out_tc(const float *o, const float *w_o32, const float *bo, float *y, int n, int E, int cap,
-                                int32_t *len, const int32_t *slot, int n_slots, uint32_t *dev_err, cudaStream_t st,
-                                std::string *msg) {
-    const int N = (n + 15) / 16 * 16, KC = E / DO_KSPLIT;
-    CUtensorMap tw, to;
-    int rc;
-    const uint64_t wd[2] = {(uint64_t)E, (uint64_t)E};
-    const uint64_t ws[1] = {(uint64_t)E * 4};
-    const uint32_t wb[2] = {32, 128};
-    if ((rc = make_tmap(&tw, w_o32, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, wd, ws, wb, CU_TENSOR_MAP_SWIZZLE_128B, msg)))
-        return rc;
-    const uint64_t od[2] = {(uint64_t)E, (uint64_t)n};
-    const uint32_t ob[2] = {32, (uint32_t)N};
-    if ((rc = make_tmap(&to, o, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, od, ws, ob, CU_TENSOR_MAP_SWIZZLE_128B, msg)))
-        return rc;
-    const size_t smem = (size_t)128 * KC * 4 + (size_t)(KC / 32) * N * 128 + (size_t)N * 128 * 4 + 64 + 1024;
-    DecodeOutTcArgs a{bo, y, n, N, E, KC, cap, n_slots, len, slot, dev_err};
-    cudaFuncSetAttribute(decode_out_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)((E / 128) * DO_KSPLIT));
-    cfg.blockDim = dim3(128);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[2];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = DO_KSPLIT;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[1].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 2;
-    ProfScope ps("decode_out", st);
-    cudaError_t e = cudaLaunchKernelEx(&cfg, decode_out_tc_kernel, tw, to, a);
-    if (e == cudaSuccess) e = cudaGetLastError();
-    if (e != cudaSuccess) {
-        *msg = std::string("decode out_proj launch failed: ") + cudaGetErrorString(e);
-        return WB_ECUDA;
-    }
-    return WB_OK;
 }
 
 int tc_gemm_bf16(const __nv_bfloat16 *A, const __nv_bfloat16 *B, const float *bias, float *C, int M, int N, int K,
@@ -1417,13 +1213,9 @@ int tc_kv_decode(const TcLayerWeights &t, const WbSeqView &sv, int32_t *len, int
         launch_len_update(len, sv.slot, n_seq, 1, 0, n_slots, cap, st);
         return launch_gemm(true, o, t.w_o32, t.b_o, y, n_seq, t.E, t.E, t.E, dev_err, st, msg);
     }
-    // few rows: the out_proj kernel (programmatic dependent of the attention
-    // grid), which also advances the lengths -- on the tensor cores where the
-    // shape allows, else the SIMT kernel
-    if (decode_out_tc_ok(t.E, n_seq))
-        rc = launch_decode_out_tc(o, t.w_o32, t.b_o, y, n_seq, t.E, cap, len, sv.slot, n_slots, dev_err, st, msg);
-    else
-        rc = launch_decode_out(o, t.wo_t, t.b_o, y, n_seq, t.E, cap, len, sv.slot, n_slots, st, msg);
+    // few rows: the SIMT out_proj kernel (programmatic dependent of the
+    // attention grid), which also advances the lengths
+    rc = launch_decode_out(o, t.wo_t, t.b_o, y, n_seq, t.E, cap, len, sv.slot, n_slots, st, msg);
     if (rc == WB_OK && ends_with_out) *ends_with_out = true;
     return rc;
 }
