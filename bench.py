@@ -445,7 +445,7 @@ def run_ours(args):
         ev_done = [torch.cuda.Event() for _ in chunks]
         ev_in_free = [torch.cuda.Event() for _ in range(2)]   # compute done with input set
         ev_out_free = [torch.cuda.Event() for _ in range(2)]  # copies done with output set
-        n_e2e = max(1, min(args.steps, args.e2e_steps))
+        n_e2e = max(1, args.e2e_steps)
 
         def inputs(k):
             j = k % 2
@@ -1073,7 +1073,9 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-prefill-profile", action="store_true")
     ap.add_argument("--check-each-step", action="store_true")
-    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--e2e-steps", type=int, default=8,
+                    help="consecutive steps of the pipelined end-to-end run (every step's copies are timed; only the "
+                         "first step's uploads have no compute to hide behind)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
     args = ap.parse_args()

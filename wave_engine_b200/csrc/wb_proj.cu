@@ -540,38 +540,34 @@ __global__ void __launch_bounds__(VP_THREADS, 1) vproj_phase_kernel(VpArgs a) {
 // host side
 // ---------------------------------------------------------------------------
 // ---------------------------------------------------------------------------
-// Values and phases of a head_dim-64 layer without content, in one pass over
-// x (attn.rs:121-130, :155-165; kv_cache.rs:129-142): vphase_tc_kernel.
-// A CTA owns 128 rows and walks x one head's 64 input columns at a time
-// (chunk h), TMA'd into a 2-stage ring together with head h's value weights
-// (tf32 head and remainder) and the 64 phase-weight rows of those inputs:
-//   warps 2-9 (workers): the phase sums -- thread (row, output half) adds the
-//     chunk's 64 inputs to its H outputs (r, s of H/2 heads) with one fmaf
-//     per input in input order, the same sequential sum over the whole row
-//     as phase_fma_kernel; then they split the x chunk into tf32 head (in
-//     place) and remainder for the tensor core;
-//   warp 1 (MMA): values of head h, 3xTF32 on tcgen05: main = xh Wh, corr =
-//     xh Wl + xl Wh, into one of two TMEM buffer pairs;
-//   warps 10-13 (epilogue): value = main + corr + bias into the sequence
-//     view, overlapping the next chunk;
-//   warp 0: TMA producer.
-// After the last chunk the workers turn (r, s) into the phase and bucket.
+// Values and phases of a head_dim-64 layer, in one pass over x (attn.rs
+// :121-130, :155-165; kv_cache.rs:129-142): vphase_tc_kernel.  A CTA owns
+// 128 rows and walks x one head's 64 input columns at a time (chunk h),
+// TMA'd into a 2-stage ring with the weights those inputs meet: head h's 64
+// value rows and the 2H phase rows (r, s of every head), as tf32 heads and
+// remainders.  One 3xTF32 tcgen05 MMA sequence per chunk (N = 64 + 32:
+// main = xh Wh, corr = xh Wl + xl Wh) gives head h's values and every
+// head's phase partial sums over the chunk's 64 inputs; the epilogue warps
+// store the values and add the phase partials to fp32 running sums in input
+// order (a 64-term tensor-core sum per chunk, then a sequential fp32 sum over
+// the chunks), and after the last chunk turn (r, s) into phase and bucket.
+//   warp 0: TMA producer; warp 1: MMA; warps 2-9: split x into tf32 head
+//   (in place) and remainder; warps 10-13: epilogue (TMEM lane groups).
 // ---------------------------------------------------------------------------
 static constexpr int VT_ROWS = 128;
 static constexpr int VT_THREADS = 14 * 32;
+static constexpr int VT_N = 96;                    // 64 value + up to 32 phase outputs
 static constexpr int VT_X = 128 * 64 * 4;          // x chunk (two 32-column SW128 atoms)
-static constexpr int VT_W = 64 * 64 * 4;           // one head's value weights (two atoms)
-static constexpr int VT_RS = 64 * 32 * 4;          // phase weights of 64 inputs, up to 16 heads
-static constexpr int VT_STAGE = 2 * VT_X + 2 * VT_W + VT_RS;
-static constexpr int VT_EPI = 4 * 32 * 33 * 4;
-static constexpr int VT_SMEM = 2 * VT_STAGE + VT_EPI + 128 + 1024;
+static constexpr int VT_WATOM = VT_N * 128;        // one K atom of the chunk's weights (96 rows)
+static constexpr int VT_W = 2 * VT_WATOM;          // chunk weights, one precision
+static constexpr int VT_STAGE = 2 * VT_X + 2 * VT_W;
+static constexpr int VT_SMEM = 2 * VT_STAGE + 128 + 1024;
 static_assert(VT_SMEM <= 232448, "vphase shared memory above the 227 KB limit");
 
 struct VtArgs {
     int R, T, E;
     const float *bias;  // value biases [H*64] (ProjTcWeights bias rows 0..n_v)
     const float *brs;   // [H][2]
-    const float *wrs_t; // [E][H][2]
     WbSeqView sv;
     uint32_t *dev_err;
 };
@@ -579,12 +575,12 @@ struct VtArgs {
 template <int H>
 __global__ void __launch_bounds__(VT_THREADS, 1)
     vphase_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_wh,
-                     const __grid_constant__ CUtensorMap tm_wl, VtArgs a) {
+                     const __grid_constant__ CUtensorMap tm_wl, int phase_row0, VtArgs a) {
     static_assert(H % 4 == 0 && H <= 16, "heads per layer: a multiple of 4, at most 16");
-    constexpr int NO = H;  // (r, s) outputs per worker thread: H/2 heads
+    constexpr int NP = 2 * H;  // phase outputs (r, s per head)
     extern __shared__ uint8_t smem_raw[];
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t *bars = reinterpret_cast<uint64_t *>(sm + 2 * VT_STAGE + VT_EPI);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sm + 2 * VT_STAGE);
     uint64_t *full = bars, *conv = bars + 2, *empty = bars + 4, *vfull = bars + 6, *vfree = bars + 8;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 10);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -594,7 +590,7 @@ __global__ void __launch_bounds__(VT_THREADS, 1)
         ptx::fence_mbar_init();
     }
     if (warp == 1) {
-        ptx::tmem_alloc(tmem_slot, 256);
+        ptx::tmem_alloc(tmem_slot, 512);
         ptx::tmem_relinquish();
     }
     ptx::tc_fence_before();
@@ -604,7 +600,7 @@ __global__ void __launch_bounds__(VT_THREADS, 1)
     auto stage = [&](int s) { return sm + s * VT_STAGE; };
 
     if (warp == 0) {
-        // ---------------- producer
+        // ---------------- producer: x chunk, value rows of head h, phase rows
         if (lane == 0) {
             ptx::prefetch_tmap(&tm_x);
             ptx::prefetch_tmap(&tm_wh);
@@ -616,44 +612,50 @@ __global__ void __launch_bounds__(VT_THREADS, 1)
                     break;
                 }
                 uint8_t *st = stage(s);
-                ptx::mbar_arrive_expect_tx(full + s, VT_X + 2 * VT_W + 64 * 2 * H * 4);
+                ptx::mbar_arrive_expect_tx(full + s, VT_X + 2 * VT_W);
                 for (int t = 0; t < 2; t++) {
-                    ptx::tma_load_2d(st + t * (VT_X / 2), &tm_x, full + s, h * 64 + t * 32, m0);
-                    ptx::tma_load_2d(st + 2 * VT_X + t * (VT_W / 2), &tm_wh, full + s, h * 64 + t * 32, h * 64);
-                    ptx::tma_load_2d(st + 2 * VT_X + VT_W + t * (VT_W / 2), &tm_wl, full + s, h * 64 + t * 32, h * 64);
+                    const int k = h * 64 + t * 32;
+                    ptx::tma_load_2d(st + t * (VT_X / 2), &tm_x, full + s, k, m0);
+                    uint8_t *wh = st + 2 * VT_X + t * VT_WATOM, *wl = wh + VT_W;
+                    // rows 0-63: head h's value outputs; rows 64-95: the phase
+                    // outputs of every head (zeros past the last row of W)
+                    ptx::tma_load_2d(wh, &tm_wh, full + s, k, h * 64);
+                    ptx::tma_load_2d(wh + 32 * 128, &tm_wh, full + s, k, h * 64 + 32);
+                    ptx::tma_load_2d(wh + 64 * 128, &tm_wh, full + s, k, phase_row0);
+                    ptx::tma_load_2d(wl, &tm_wl, full + s, k, h * 64);
+                    ptx::tma_load_2d(wl + 32 * 128, &tm_wl, full + s, k, h * 64 + 32);
+                    ptx::tma_load_2d(wl + 64 * 128, &tm_wl, full + s, k, phase_row0);
                 }
-                ptx::bulk_load(st + 2 * VT_X + 2 * VT_W, a.wrs_t + (size_t)h * 64 * 2 * H, 64 * 2 * H * 4, full + s);
             }
         }
     } else if (warp == 1) {
-        // ---------------- MMA: values of head h (3xTF32)
+        // ---------------- MMA: 3xTF32, N = 96 (values of head h | phase partials)
         if (lane == 0) {
-            constexpr uint32_t IDESC = ptx::idesc_tf32(128, 64);
-            bool ok = true;
-            for (int h = 0; h < H && ok; h++) {
+            constexpr uint32_t IDESC = ptx::idesc_tf32(128, VT_N);
+            for (int h = 0; h < H; h++) {
                 const int s = h & 1, b = h & 1;
                 if (!ptx::mbar_wait(conv + s, (h >> 1) & 1) ||
                     (h >= 2 && !ptx::mbar_wait(vfree + b, ((h - 2) >> 1) & 1))) {
                     atomicOr(a.dev_err, WB_DERR_TIMEOUT_TMA);
-                    ok = false;
                     break;
                 }
                 ptx::tc_fence_after();
                 const uint32_t xh = ptx::smem_u32(stage(s)), xl = xh + VT_X;
                 const uint32_t wh = xh + 2 * VT_X, wl = wh + VT_W;
-                const uint32_t Dm = tmem + (uint32_t)(b * 128), Dc = Dm + 64;
+                const uint32_t Dm = tmem + (uint32_t)(b * 256), Dc = Dm + 128;
+                const uint64_t dah0 = ptx::smem_desc(xh, 16, 1024, ptx::UMMA_SW128);
+                const uint64_t dal0 = ptx::smem_desc(xl, 16, 1024, ptx::UMMA_SW128);
+                const uint64_t dbh0 = ptx::smem_desc(wh, 16, 1024, ptx::UMMA_SW128);
+                const uint64_t dbl0 = ptx::smem_desc(wl, 16, 1024, ptx::UMMA_SW128);
 #pragma unroll
                 for (int t = 0; t < 2; t++)
 #pragma unroll
                     for (int k = 0; k < 4; k++) {
-                        const uint32_t ao = t * (VT_X / 2) + k * 32, bo = t * (VT_W / 2) + k * 32;
-                        const uint64_t dah = ptx::smem_desc(xh + ao, 16, 1024, ptx::UMMA_SW128);
-                        const uint64_t dal = ptx::smem_desc(xl + ao, 16, 1024, ptx::UMMA_SW128);
-                        const uint64_t dbh = ptx::smem_desc(wh + bo, 16, 1024, ptx::UMMA_SW128);
-                        const uint64_t dbl = ptx::smem_desc(wl + bo, 16, 1024, ptx::UMMA_SW128);
-                        ptx::mma_tf32(Dm, dah, dbh, IDESC, (t > 0 || k > 0));
-                        ptx::mma_tf32(Dc, dah, dbl, IDESC, (t > 0 || k > 0));
-                        ptx::mma_tf32(Dc, dal, dbh, IDESC, 1);
+                        const uint64_t ao = (uint64_t)((t * (VT_X / 2) + k * 32) >> 4);
+                        const uint64_t bo = (uint64_t)((t * VT_WATOM + k * 32) >> 4);
+                        ptx::mma_tf32(Dm, dah0 + ao, dbh0 + bo, IDESC, (t > 0 || k > 0));
+                        ptx::mma_tf32(Dc, dah0 + ao, dbl0 + bo, IDESC, (t > 0 || k > 0));
+                        ptx::mma_tf32(Dc, dal0 + ao, dbh0 + bo, IDESC, 1);
                     }
                 ptx::mma_commit(empty + s);
                 ptx::mma_commit(vfull + b);
@@ -661,48 +663,16 @@ __global__ void __launch_bounds__(VT_THREADS, 1)
         }
         __syncwarp();
     } else if (warp < 10) {
-        // ---------------- workers: phase sums, then the tf32 split of x
-        const int wt = tid - 64;                    // 0..255
-        const int row = wt & 127, oh = wt >> 7;     // output half: outputs oh*H .. oh*H + H - 1
-        float acc[NO];
-#pragma unroll
-        for (int o = 0; o < NO; o++) acc[o] = __ldg(a.brs + oh * NO + o);
-        bool ok = true;
+        // ---------------- workers: x -> tf32 head (in place) and remainder
+        const int wt = tid - 64;  // 0..255
         for (int h = 0; h < H; h++) {
             const int s = h & 1;
             if (!ptx::mbar_wait(full + s, (h >> 1) & 1)) {
                 if (wt == 0) atomicOr(a.dev_err, WB_DERR_TIMEOUT_TMA);
-                ok = false;
                 break;
             }
-            uint8_t *st = stage(s);
-            const float *wrs = reinterpret_cast<const float *>(st + 2 * VT_X + 2 * VT_W) + oh * NO;
-#pragma unroll 1
-            for (int t = 0; t < 2; t++) {
-                const uint8_t *xa = st + t * (VT_X / 2) + row * 128;
-#pragma unroll 2
-                for (int j = 0; j < 8; j++) {  // 16-byte chunk j: inputs 4j..4j+3 of this atom
-                    const float4 x4 = *reinterpret_cast<const float4 *>(xa + ((j ^ (row & 7)) << 4));
-                    const float xv[4] = {x4.x, x4.y, x4.z, x4.w};
-#pragma unroll
-                    for (int u = 0; u < 4; u++) {
-                        const float *wr = wrs + (t * 32 + j * 4 + u) * 2 * H;
-#pragma unroll
-                        for (int o4 = 0; o4 < NO / 4; o4++) {
-                            const float4 w4 = *reinterpret_cast<const float4 *>(wr + o4 * 4);
-                            acc[o4 * 4 + 0] = fmaf(w4.x, xv[u], acc[o4 * 4 + 0]);
-                            acc[o4 * 4 + 1] = fmaf(w4.y, xv[u], acc[o4 * 4 + 1]);
-                            acc[o4 * 4 + 2] = fmaf(w4.z, xv[u], acc[o4 * 4 + 2]);
-                            acc[o4 * 4 + 3] = fmaf(w4.w, xv[u], acc[o4 * 4 + 3]);
-                        }
-                    }
-                }
-            }
-            // every worker has read the chunk: split it (element-wise, the
-            // swizzled layout is kept) into the tf32 head and the remainder
-            asm volatile("bar.sync 1, 256;" ::: "memory");
-            float4 *X = reinterpret_cast<float4 *>(st);
-            float4 *XL = reinterpret_cast<float4 *>(st + VT_X);
+            float4 *X = reinterpret_cast<float4 *>(stage(s));
+            float4 *XL = reinterpret_cast<float4 *>(stage(s) + VT_X);
 #pragma unroll 4
             for (int e = wt; e < VT_X / 16; e += 256) {
                 const float4 v = X[e];
@@ -722,64 +692,78 @@ __global__ void __launch_bounds__(VT_THREADS, 1)
             asm volatile("bar.sync 1, 256;" ::: "memory");
             if (wt == 0) ptx::mbar_arrive(conv + s);
         }
-        // phases and buckets of this thread's H/2 heads (attn.rs:127, :171-174)
-        const int m = m0 + row;
-        if (ok && m < a.R) {
-            const int b = m / a.T, t = m - b * a.T;
-            const long long base = (long long)(a.sv.slot ? a.sv.slot[b] : b) * a.sv.seq_stride + t;
-#pragma unroll
-            for (int i = 0; i < NO / 2; i++) {
-                const int hh = oh * (NO / 2) + i;
-                const float th = atan2f(acc[2 * i + 1], acc[2 * i]);
-                a.sv.theta[base + (long long)hh * a.sv.cap] = th;
-                a.sv.bucket[base + (long long)hh * a.sv.cap] = (uint8_t)phase_to_bucket(th);
-            }
-        }
     } else {
-        // ---------------- value epilogue (warps 10-13: lane groups 2, 3, 0, 1)
+        // ---------------- epilogue (warps 10-13: lane groups 2, 3, 0, 1)
         const int q = warp & 3;
         const int row = q * 32 + lane, m = m0 + row;
         const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-        float *buf = reinterpret_cast<float *>(sm + 2 * VT_STAGE) + (warp - 10) * 32 * 33;
         long long base = -1;
         if (m < a.R) {
             const int b = m / a.T, t = m - b * a.T;
             base = (long long)(a.sv.slot ? a.sv.slot[b] : b) * a.sv.seq_stride + t;
         }
+        float acc[NP];
+#pragma unroll
+        for (int o = 0; o < NP; o++) acc[o] = __ldg(a.brs + o);
+        bool ok = true;
         for (int h = 0; h < H; h++) {
             const int b = h & 1;
             if (!ptx::mbar_wait(vfull + b, (h >> 1) & 1)) {
                 if (lane == 0) atomicOr(a.dev_err, WB_DERR_TIMEOUT_MMA);
+                ok = false;
                 break;
             }
             ptx::tc_fence_after();
-            const uint32_t Dm = tmem + (uint32_t)(b * 128) + lane_base;
+            const uint32_t Dm = tmem + (uint32_t)(b * 256) + lane_base, Dc = Dm + 128;
+            // phase partials of this chunk: columns 64 .. 64 + NP
+            {
+                uint32_t r[32], rc[32];
+                ptx::tmem_ld32(Dm + 64, r);
+                ptx::tmem_ld32(Dc + 64, rc);
+                ptx::tmem_ld_wait();
+#pragma unroll
+                for (int o = 0; o < NP; o++) acc[o] += __uint_as_float(r[o]) + __uint_as_float(rc[o]);
+            }
+            // values of head h: columns 0 .. 63
+            float *vrow = base >= 0 ? a.sv.v + (base + (long long)h * a.sv.cap) * 64 : nullptr;
 #pragma unroll 1
             for (int c = 0; c < 2; c++) {
                 uint32_t r[32], rc[32];
                 ptx::tmem_ld32(Dm + c * 32, r);
-                ptx::tmem_ld32(Dm + 64 + c * 32, rc);
+                ptx::tmem_ld32(Dc + c * 32, rc);
                 ptx::tmem_ld_wait();
                 if (c == 1) {
                     ptx::tc_fence_before();
                     ptx::mbar_arrive(vfree + b);
                 }
+                if (vrow) {
+                    const float4 *bias4 = reinterpret_cast<const float4 *>(a.bias + h * 64 + c * 32);
 #pragma unroll
-                for (int i = 0; i < 32; i++) r[i] = __float_as_uint(__uint_as_float(r[i]) + __uint_as_float(rc[i]));
-                warp_stage32(buf, r, lane);
-                const int d = c * 32 + lane;
-                const float bv = __ldg(a.bias + h * 64 + d);
-#pragma unroll 4
-                for (int jr = 0; jr < 32; jr++) {
-                    const long long rb = __shfl_sync(0xffffffffu, base, jr);
-                    if (rb >= 0) a.sv.v[(rb + (long long)h * a.sv.cap) * 64 + d] = buf[jr * 33 + lane] + bv;
+                    for (int i = 0; i < 8; i++) {
+                        const float4 bv = __ldg(bias4 + i);
+                        float4 v;
+                        v.x = __uint_as_float(r[4 * i]) + __uint_as_float(rc[4 * i]) + bv.x;
+                        v.y = __uint_as_float(r[4 * i + 1]) + __uint_as_float(rc[4 * i + 1]) + bv.y;
+                        v.z = __uint_as_float(r[4 * i + 2]) + __uint_as_float(rc[4 * i + 2]) + bv.z;
+                        v.w = __uint_as_float(r[4 * i + 3]) + __uint_as_float(rc[4 * i + 3]) + bv.w;
+                        reinterpret_cast<float4 *>(vrow + c * 32)[i] = v;
+                    }
                 }
+            }
+        }
+        // phases and buckets of every head of this row (attn.rs:127, :171-174)
+        if (ok && base >= 0) {
+#pragma unroll
+            for (int hh = 0; hh < H; hh++) {
+                const float th = atan2f(acc[2 * hh + 1], acc[2 * hh]);
+                a.sv.theta[base + (long long)hh * a.sv.cap] = th;
+                a.sv.bucket[base + (long long)hh * a.sv.cap] = (uint8_t)phase_to_bucket(th);
             }
         }
     }
     ptx::tc_fence_before();
     __syncthreads();
-    if (warp == 1) ptx::tmem_dealloc(tmem, 256);
+    if (warp == 1) ptx::tmem_dealloc(tmem, 512);
 }
 
 static PFN_cuTensorMapEncodeTiled_v12000 proj_encode_fn() {
@@ -893,26 +877,32 @@ int launch_proj_tc(const ProjTcWeights &p, const float *wrs_t, const float *brs,
     if (R <= 0) return WB_OK;
     const bool simt_v = wv_t && bv && (p.hd == 64 || p.hd == 48) && Hg <= 16 && R <= INT32_MAX &&
                         (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(bv) & 15) == 0;
-    const bool tc_v = simt_v && p.hd == 64 && h0 == 0 && Hg == p.H && (p.H == 8 || p.H == 12 || p.H == 16);
+    // head_dim 64: values and phases on the tensor cores.  Every chunk's MMA
+    // covers all heads' phases, so a head range runs the whole layer (the
+    // rows of other heads are written but not read): the same kernel and
+    // the same numbers as the full forward
+    const bool tc_v = simt_v && p.hd == 64 && (p.H == 8 || p.H == 12 || p.H == 16);
     if (tc_v) {
-        // values (3xTF32 tcgen05) and phases (sequential fp32) in one pass
+        // values (3xTF32 tcgen05) and phase partial sums in one pass
         CUtensorMap tx, twh, twl;
         int rc;
         if ((rc = tmap_2d_f32(&tx, x, (uint64_t)p.E, (uint64_t)R, msg))) return rc;
-        if ((rc = tmap_2d_f32(&twh, p.w_hi, (uint64_t)p.E, (uint64_t)p.N, msg, 64))) return rc;
-        if ((rc = tmap_2d_f32(&twl, p.w_lo, (uint64_t)p.E, (uint64_t)p.N, msg, 64))) return rc;
-        VtArgs va{(int)R, T, p.E, p.bias, brs, wrs_t, sv, dev_err};
+        // 32-row boxes: value rows load as two boxes of 32 (64 rows), phase rows as one
+        if ((rc = tmap_2d_f32(&twh, p.w_hi, (uint64_t)p.E, (uint64_t)p.N, msg, 32))) return rc;
+        if ((rc = tmap_2d_f32(&twl, p.w_lo, (uint64_t)p.E, (uint64_t)p.N, msg, 32))) return rc;
+        VtArgs va{(int)R, T, p.E, p.bias, brs, sv, dev_err};
+        const int phase_row0 = p.n_v + p.n_c;  // the 2H phase rows of W (the last rows: 32-row boxes read zeros past them)
         ProfScope ps("proj_vphase", st);
         const unsigned grid = (unsigned)((R + VT_ROWS - 1) / VT_ROWS);
         if (p.H == 8) {
             cudaFuncSetAttribute(vphase_tc_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, VT_SMEM);
-            vphase_tc_kernel<8><<<grid, VT_THREADS, VT_SMEM, st>>>(tx, twh, twl, va);
+            vphase_tc_kernel<8><<<grid, VT_THREADS, VT_SMEM, st>>>(tx, twh, twl, phase_row0, va);
         } else if (p.H == 12) {
             cudaFuncSetAttribute(vphase_tc_kernel<12>, cudaFuncAttributeMaxDynamicSharedMemorySize, VT_SMEM);
-            vphase_tc_kernel<12><<<grid, VT_THREADS, VT_SMEM, st>>>(tx, twh, twl, va);
+            vphase_tc_kernel<12><<<grid, VT_THREADS, VT_SMEM, st>>>(tx, twh, twl, phase_row0, va);
         } else {
             cudaFuncSetAttribute(vphase_tc_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, VT_SMEM);
-            vphase_tc_kernel<16><<<grid, VT_THREADS, VT_SMEM, st>>>(tx, twh, twl, va);
+            vphase_tc_kernel<16><<<grid, VT_THREADS, VT_SMEM, st>>>(tx, twh, twl, phase_row0, va);
         }
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) {

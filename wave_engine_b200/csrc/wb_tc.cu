@@ -362,7 +362,7 @@ __device__ __forceinline__ bool att_wait(uint64_t *bar, uint32_t parity, volatil
     if (ptx::mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
     while (true) {
-        if (ptx::mbar_try_wait(bar, parity)) return true;
+        if (ptx::mbar_try_wait_sleep(bar, parity, 20000)) return true;
         if (*abort_flag) return false;
         if (clock64() - t0 > 4000000000LL) {
             *abort_flag = 1;
