@@ -17,6 +17,11 @@
  *                        WaveAttnWeights (device-resident copy)
  *   wb_kv_cache_*     <- src/common/kv_cache.rs:36-54 HeadCache/LayerCache/
  *                        KvCache (device-resident, one slot per sequence)
+ *   wb_attn_forward_cache <- src/common/attn.rs:90 with return_pathway_cache
+ *                        = true (WaveAttnCache, attn.rs:51-70)
+ *   wb_attn_backward  <- src/common/attn.rs:346 wave_attention_backward_full
+ *                        and :432 wave_attention_backward_pathway (caller:
+ *                        src/candle_tier/custom_attn.rs:132 bwd)
  *
  * Conventions
  *   - Every function returns int status: WB_OK (0) or a negative WB_E*.
@@ -156,6 +161,57 @@ WB_API int wb_init_block_attn(uint64_t *rng_state, int n_head, int n_embd, int c
 WB_API int wb_attn_forward(wb_context *ctx, const wb_attn_layer *layer, const float *x, int batch,
                     int seq_len, int flags, float *y, float *att_w, float *phases_out);
 
+/* ---- forward cache and backward (attn.rs:51-70, :346-430) ------------- */
+/* The WaveAttnCache of attn.rs:51-70 for a batch of sequences (each array
+ * stacks the reference's per-sequence arrays over the batch):
+ *   phases     [batch][n_head][seq_len]            (cache.phases)
+ *   phase_rs   [batch][n_head][seq_len][2]         (cache.phase_rs: (r, s))
+ *   v_all      [batch][n_head][seq_len][head_dim]  (cache.v_all)
+ *   content    [batch][n_head][seq_len][content_dim] or NULL without content
+ *   att_w      [batch][n_head][seq_len][seq_len]   (cache.att_w, 0 above the
+ *              diagonal and for masked keys)
+ *   out_merged [batch][seq_len][n_embd]            (cache.out_merged)
+ * cache.normed is the forward's x; cache.content_scale is 1/sqrt(C). */
+typedef struct {
+    float *phases;
+    float *phase_rs;
+    float *v_all;
+    float *content;
+    float *att_w;
+    float *out_merged;
+} wb_attn_cache_desc;
+
+/* Weight gradients in the layouts of wb_attn_weights_desc (WaveAttnGrads,
+ * attn.rs:346-430), summed over the batch; NULL entries are not computed. */
+typedef struct {
+    float *harmonic_raw;
+    float *phase_proj_w;
+    float *phase_proj_b;
+    float *v_proj_w;
+    float *v_proj_b;
+    float *content_proj_w;
+    float *content_proj_b;
+    float *out_proj_w;
+    float *out_proj_b;
+} wb_attn_grads_desc;
+
+/* attn.rs:90 wave_attention_forward with return_pathway_cache = true: y as
+ * wb_attn_forward's WB_PATH_EXACT (all-fp32 SIMT) and the cache above.
+ * flags: WB_NO_CONTENT. */
+WB_API int wb_attn_forward_cache(wb_context *ctx, const wb_attn_layer *layer, const float *x, int batch,
+                                 int seq_len, int flags, float *y, const wb_attn_cache_desc *cache);
+
+/* attn.rs:346-430 wave_attention_backward_full from the cache and the output
+ * gradient d_y [batch][seq_len][n_embd]: the input gradient d_x (d_normed)
+ * and, when grads is non-NULL, the weight gradients summed over the batch.
+ * With grads NULL this is wave_attention_backward_pathway (attn.rs:432).
+ * x is the forward's input (cache.normed).  fp32 on the GPU; the sums run in
+ * another order than the reference's loops (see the tests' tolerance).
+ * flags: WB_NO_CONTENT (as in the forward).  head_dim <= 128. */
+WB_API int wb_attn_backward(wb_context *ctx, const wb_attn_layer *layer, const float *x, const float *d_y,
+                            int batch, int seq_len, int flags, const wb_attn_cache_desc *cache, float *d_x,
+                            const wb_attn_grads_desc *grads);
+
 /* Head-sharded prefill (no counterpart in the reference, which runs all
  * heads in one call): the forward of heads [head_begin, head_end) only,
  * y_partial = o[:, heads] W_out[:, heads]^T, plus out_proj's bias when
@@ -199,6 +255,31 @@ WB_API int wb_kv_cache_length(wb_kv_cache *cache, int layer, int seq, int *len_o
 /* Empty a sequence slot in every layer (a new request); seq = -1 empties
  * every slot. */
 WB_API int wb_kv_cache_reset_seq(wb_kv_cache *cache, int seq);
+
+/* Paged KV cache (multi-request serving: src/serve_tier/inference.rs:44
+ * creates one KvCache per request; here the requests share one pool).  Each
+ * layer's storage is a pool of n_pages pages, a page holding WB_KV_PAGE
+ * positions of every head; a slot's positions 128p .. 128p+127 live in the
+ * page its page table maps p to.  A slot holds no positions until
+ * wb_kv_seq_reserve gives it pages; a prefill or decode past a slot's
+ * reserved pages fails with WB_EINVAL (host seq ids) or, with device seq
+ * ids, is not written and sets bit 0x8 (bounds) of the device error word.
+ * max_ctx (a slot's most positions) rounds up to whole pages.  Every other
+ * call works on a paged cache as on a contiguous one, with the same results
+ * bit for bit. */
+#define WB_KV_PAGE 128
+WB_API int wb_kv_cache_create_paged(wb_context *ctx, int n_layers, int n_head, int head_dim, int max_seqs,
+                                    int max_ctx, int n_pages, wb_kv_cache **out);
+/* Reserve pages so that slot seq holds n_positions (<= max_ctx) in every
+ * layer; WB_ENOMEM (nothing reserved) when the pool is short.  Pages stay
+ * with the slot until wb_kv_seq_release.  No-op on a contiguous cache. */
+WB_API int wb_kv_seq_reserve(wb_kv_cache *cache, int seq, int n_positions);
+/* Empty slot seq in every layer and return its pages to the pool
+ * (synchronises the context's stream first).  On a contiguous cache:
+ * wb_kv_cache_reset_seq. */
+WB_API int wb_kv_seq_release(wb_kv_cache *cache, int seq);
+/* Pages in the pool's free list (0 for a contiguous cache). */
+WB_API int wb_kv_cache_free_pages(wb_kv_cache *cache, int *n_free);
 /* Load n positions of one (layer, seq) slot from raw arrays: phases
  * [n_head][n], values [n_head][n][head_dim] (host or device).  Buckets are
  * derived from the phases exactly as kv_cache.rs:66-70.  Replaces the slot's

@@ -25,6 +25,15 @@ WB_API int wb_test_gemm_bf16(wb_context *ctx, const uint16_t *A, const uint16_t 
 WB_API int wb_test_gemm_tf32(wb_context *ctx, const float *A, const float *B, const float *bias, float *C, int M,
                              int N, int K);
 
+/* The dot-product attention core alone (compute.rs:357-414, between c_attn
+ * and c_proj): qkv [B*T][3*n_embd] -> o [B*T][n_embd], DEVICE pointers.
+ * mode 0: the tensor-core core (head_dim <= 64) with its fp32 fallback for
+ * query tiles past the fixed-shift bound; 1: the same with every tile sent
+ * to the fallback; 2: the fp32 FMA core.  Asynchronous on the context's
+ * stream. */
+WB_API int wb_test_dot_core(wb_context *ctx, const float *qkv, int batch, int seq_len, int n_embd, int n_head,
+                            int mode, float *o);
+
 #ifdef __cplusplus
 }
 #endif

@@ -50,3 +50,59 @@ def test_dot_attention_torch_inputs_and_errors(ctx):
         wb.attention(w, x[:, :32], ctx=ctx)  # weights for another n_embd
     with pytest.raises(wb.WaveB200Error):
         wb.DotAttnLayer(ctx, wb.gaussian_attention_weights(1, 1, 132))  # head_dim 132 > 128
+
+
+def _dot_core_f64(qkv, H):
+    B, T, E3 = qkv.shape
+    E = E3 // 3
+    hd = E // H
+    o = np.zeros((B, T, E))
+    for b in range(B):
+        for h in range(H):
+            q = qkv[b, :, h * hd:(h + 1) * hd].astype(np.float64) / np.sqrt(hd)
+            k = qkv[b, :, E + h * hd:E + (h + 1) * hd].astype(np.float64)
+            v = qkv[b, :, 2 * E + h * hd:2 * E + (h + 1) * hd].astype(np.float64)
+            s = np.where(np.tri(T, dtype=bool), q @ k.T, -np.inf)
+            p = np.exp(s - s.max(1, keepdims=True))
+            o[b, :, h * hd:(h + 1) * hd] = (p @ v) / p.sum(1, keepdims=True)
+    return o
+
+
+@pytest.mark.parametrize("E,H,T", [(256, 4, 300), (168, 4, 129), (48, 6, 64)])
+def test_dot_core_on_tensor_cores_and_fallback_tiles(ctx, E, H, T):
+    """The attention core alone on a qkv built directly (no projection
+    error): the tcgen05 core (head_dim <= 64) within 2e-3 of a float64
+    statement; a (sequence, head) with magnitudes x30 fails the fixed-shift
+    bound and is recomputed by the fp32 core (bitwise equal to it there);
+    with every tile forced to the fallback the result equals the fp32 core
+    bit for bit."""
+    import torch
+    from wave_engine_b200 import _lib
+    B = 2
+    hd = E // H
+    g = np.random.default_rng(E + T)
+    qkv = (g.standard_normal((B, T, 3 * E)) * 0.55).astype(np.float32)
+    qkv[1, :, hd:2 * hd] *= 30.0           # q of head 1, sequence 1
+    qkv[1, :, E + hd:E + 2 * hd] *= 30.0   # its k
+    ref = _dot_core_f64(qkv, H)
+    q_d = torch.from_numpy(qkv).cuda()
+    outs = []
+    for mode in (0, 1, 2):
+        o = torch.full((B, T, E), float("nan"), device="cuda")
+        if mode == 0:
+            ctx.profile("dot_attn_fallback")
+        _lib.call("wb_test_dot_core", ctx.handle, q_d.data_ptr(), B, T, E, H, mode, o.data_ptr())
+        if mode == 0:
+            rep = ctx.profile_report()
+            ctx.profile(None)
+        torch.cuda.synchronize()
+        outs.append(o.cpu().numpy())
+    o_tc, o_all_fb, o_fma = outs
+    r = check("tensor-core core", o_tc, ref, TENSOR_TOL)
+    assert r.passed, str(r)
+    r = check("fp32 core", o_fma, ref, TENSOR_TOL)
+    assert r.passed, str(r)
+    assert np.array_equal(o_all_fb, o_fma)
+    assert np.array_equal(o_tc[1, :, hd:2 * hd], o_fma[1, :, hd:2 * hd]), "flagged head not from the fallback"
+    assert "dot_attn_fallback" in rep
+    assert ctx.take_device_error() == 0

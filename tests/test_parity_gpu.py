@@ -136,8 +136,6 @@ def test_argument_errors(ctx):
     w, x = make_case(168, 4, 16, 1, 8, seed=2)
     with pytest.raises(ValueError):
         wb.wave_attention_forward(w, x, 80, ctx=ctx)  # n_bands mismatch
-    with pytest.raises(NotImplementedError):
-        wb.wave_attention_forward(w, x, 84, return_pathway_cache=True, ctx=ctx)
     with pytest.raises(ValueError):
         wb.wave_attention_forward(w, x[0, :, :100], 50, ctx=ctx)  # weights for another n_embd
 

@@ -9,13 +9,16 @@ of ComputeBackend::attention (src/common/compute.rs:43, :357-414).
 """
 from .weights import CONTENT_DIM, Rng, WaveAttnHeadWeights, WaveAttnWeights, gaussian_block_attn, init_block_attn
 from .runtime import AttnLayer, Context, default_context
-from .attn import wave_attention_forward, wave_attention_forward_heads
+from .attn import (WaveAttnCache, wave_attention_backward_full, wave_attention_backward_pathway,
+                   wave_attention_forward, wave_attention_forward_heads)
 from .kv_cache import KvCache
 from .dot_attn import AttentionWeights, DotAttnLayer, attention, gaussian_attention_weights
 from ._lib import WaveB200Error
+from .checkpoint import WchkHeader, load_wchk_attention, read_wchk_header
 
 __all__ = [
     "CONTENT_DIM", "Rng", "WaveAttnHeadWeights", "WaveAttnWeights", "gaussian_block_attn", "init_block_attn",
     "AttnLayer", "Context", "default_context", "wave_attention_forward", "wave_attention_forward_heads", "KvCache",
-    "WaveB200Error", "AttentionWeights", "DotAttnLayer", "attention", "gaussian_attention_weights",
+    "WaveAttnCache", "wave_attention_backward_full", "wave_attention_backward_pathway",
+    "WaveB200Error", "WchkHeader", "load_wchk_attention", "read_wchk_header", "AttentionWeights", "DotAttnLayer", "attention", "gaussian_attention_weights",
 ]

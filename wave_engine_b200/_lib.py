@@ -51,14 +51,21 @@ SIGNATURES = {
     "wb_kv_cache_destroy": (C.c_int, [_VP]),
     "wb_kv_cache_length": (C.c_int, [_VP, C.c_int, C.c_int, C.POINTER(C.c_int)]),
     "wb_kv_cache_reset_seq": (C.c_int, [_VP, C.c_int]),
+    "wb_kv_cache_create_paged": (C.c_int, [_VP, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(_VP)]),
+    "wb_kv_seq_reserve": (C.c_int, [_VP, C.c_int, C.c_int]),
+    "wb_kv_seq_release": (C.c_int, [_VP, C.c_int]),
+    "wb_kv_cache_free_pages": (C.c_int, [_VP, C.POINTER(C.c_int)]),
     "wb_kv_cache_load": (C.c_int, [_VP, _VP, C.c_int, C.c_int, C.c_int, _VP, _VP]),
     "wb_kv_cache_read": (C.c_int, [_VP, _VP, C.c_int, C.c_int, _VP, _VP, _VP]),
     "wb_kv_prefill": (C.c_int, [_VP, _VP, C.c_int, _VP, _VP, C.c_int, _VP, C.c_int, C.c_int, _VP]),
     "wb_kv_decode": (C.c_int, [_VP, _VP, C.c_int, _VP, _VP, C.c_int, _VP, C.c_int, _VP]),
     "wb_kv_decode_noalloc": (C.c_int, [_VP, _VP, C.c_int, _VP, _VP, C.c_int, _VP, _VP]),
+    "wb_attn_forward_cache": (C.c_int, [_VP, _VP, _VP, C.c_int, C.c_int, C.c_int, _VP, _VP]),
+    "wb_attn_backward": (C.c_int, [_VP, _VP, _VP, _VP, C.c_int, C.c_int, C.c_int, _VP, _VP, _VP]),
     # include/wave_b200_testing.h
     "wb_test_gemm_bf16": (C.c_int, [_VP, _VP, _VP, _VP, _VP, C.c_int, C.c_int, C.c_int]),
     "wb_test_gemm_tf32": (C.c_int, [_VP, _VP, _VP, _VP, _VP, C.c_int, C.c_int, C.c_int]),
+    "wb_test_dot_core": (C.c_int, [_VP, _VP, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _VP]),
 }
 
 
@@ -70,6 +77,19 @@ class WeightsDesc(C.Structure):
         ("v_proj_w", _VP), ("v_proj_b", _VP), ("content_proj_w", _VP), ("content_proj_b", _VP),
         ("out_proj_w", _VP), ("out_proj_b", _VP),
     ]
+
+
+class CacheDesc(C.Structure):
+    """wb_attn_cache_desc (include/wave_b200.h)."""
+    _fields_ = [("phases", _VP), ("phase_rs", _VP), ("v_all", _VP), ("content", _VP), ("att_w", _VP),
+                ("out_merged", _VP)]
+
+
+class GradsDesc(C.Structure):
+    """wb_attn_grads_desc (include/wave_b200.h)."""
+    _fields_ = [("harmonic_raw", _VP), ("phase_proj_w", _VP), ("phase_proj_b", _VP), ("v_proj_w", _VP),
+                ("v_proj_b", _VP), ("content_proj_w", _VP), ("content_proj_b", _VP), ("out_proj_w", _VP),
+                ("out_proj_b", _VP)]
 
 
 class WaveB200Error(RuntimeError):

@@ -4,6 +4,7 @@
 #include "wave_b200_testing.h"
 #include "wb_internal.h"
 #include "wb_tc.h"
+#include "wb_bwd.h"
 #include "wb_decode.h"
 
 #include <algorithm>
@@ -58,6 +59,29 @@ struct DeviceGuard {
     }
 };
 
+// Where a caller's buffer lives.  Device (and managed) memory is used in
+// place.  Pinned host memory (cudaHostAlloc, cudaHostRegister) is read and
+// written by the copy engines without staging, and kernels may store to it
+// through its device alias.  Pageable memory goes through the driver's
+// staging copies.
+struct MemInfo {
+    bool device = false;
+    void *alias = nullptr;  // device address of pinned host memory, else nullptr
+};
+
+MemInfo mem_info(const void *p) {
+    MemInfo m;
+    if (!p) return m;
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return m;
+    }
+    m.device = a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+    if (a.type == cudaMemoryTypeHost) m.alias = a.devicePointer;
+    return m;
+}
+
 bool is_device_ptr(const void *p) {
     if (!p) return false;
     cudaPointerAttributes a;
@@ -91,7 +115,89 @@ struct wb_context {
     DevBuf io;    // staging of host inputs/outputs
     uint32_t *dev_err = nullptr;
     wb::Profiler *prof = nullptr;
+    // host-buffer pipelines: copies up, copies down, and their events
+    cudaStream_t cp_in = nullptr, cp_out = nullptr;
+    std::vector<cudaEvent_t> ev;
 };
+
+// Creates ctx's copy streams and at least n events on first need.
+static int copy_streams(wb_context *ctx, size_t n) {
+    if (!ctx->cp_in && cudaStreamCreateWithFlags(&ctx->cp_in, cudaStreamNonBlocking) != cudaSuccess)
+        return fail(WB_ECUDA, "copy stream creation failed");
+    if (!ctx->cp_out && cudaStreamCreateWithFlags(&ctx->cp_out, cudaStreamNonBlocking) != cudaSuccess)
+        return fail(WB_ECUDA, "copy stream creation failed");
+    while (ctx->ev.size() < n) {
+        cudaEvent_t e;
+        if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess)
+            return fail(WB_ECUDA, "event creation failed");
+        ctx->ev.push_back(e);
+    }
+    return WB_OK;
+}
+
+// One call over n_seq independent sequences whose input rows x and output
+// rows y (seq_elems floats per sequence each) may be host memory: the
+// sequences run in chunks, chunk i's rows going up on ctx->cp_in while
+// chunk i-1 computes on the call's stream (fn(first_seq, n_seqs)) and
+// chunk i-2's outputs come down on ctx->cp_out.  x_host / y_host are nullptr
+// where the caller's buffer is device memory (xd / yd are then that buffer);
+// otherwise xd / yd are device staging rows of the whole call.  On return
+// the call's stream is ordered after every copy (the caller synchronises it
+// when y is host memory).  Chunks hold >= 2 MB of rows and number <= 16.
+template <class F>
+static int run_chunked(wb_context *ctx, int n_seq, size_t seq_elems, const float *x_host, const float *xd,
+                       float *y_host, float *yd, F &&fn) {
+    cudaStream_t st = ctx->stream;
+    const size_t seq_b = seq_elems * sizeof(float);
+    const size_t min_seqs = (((size_t)2 << 20) + seq_b - 1) / seq_b;
+    const int g = (int)std::min<size_t>((size_t)n_seq, std::max<size_t>((n_seq + 15) / 16, min_seqs));
+    const int nch = (n_seq + g - 1) / g;
+    WB_TRY(copy_streams(ctx, 2 * (size_t)nch + 2));
+    cudaEvent_t *ev = ctx->ev.data();  // [0] start, [1] copies down done, [2 + i] up, [2 + nch + i] computed
+    WB_CUDA(cudaEventRecord(ev[0], st));
+    WB_CUDA(cudaStreamWaitEvent(ctx->cp_in, ev[0], 0));
+    WB_CUDA(cudaStreamWaitEvent(ctx->cp_out, ev[0], 0));
+    auto rows = [&](int i, size_t *off, size_t *bytes) {
+        const size_t s0 = (size_t)i * g;
+        *off = s0 * seq_elems;
+        *bytes = std::min<size_t>(g, n_seq - s0) * seq_b;
+    };
+    auto up = [&](int i) -> int {
+        size_t off, bytes;
+        rows(i, &off, &bytes);
+        if (x_host)
+            WB_CUDA(cudaMemcpyAsync((void *)(xd + off), x_host + off, bytes, cudaMemcpyHostToDevice, ctx->cp_in));
+        WB_CUDA(cudaEventRecord(ev[2 + i], ctx->cp_in));
+        return WB_OK;
+    };
+    auto down = [&](int i) -> int {
+        if (!y_host) return WB_OK;
+        size_t off, bytes;
+        rows(i, &off, &bytes);
+        WB_CUDA(cudaStreamWaitEvent(ctx->cp_out, ev[2 + nch + i], 0));
+        WB_CUDA(cudaMemcpyAsync(y_host + off, yd + off, bytes, cudaMemcpyDeviceToHost, ctx->cp_out));
+        return WB_OK;
+    };
+    int rc = up(0);
+    for (int i = 0; i < nch && rc == WB_OK; i++) {
+        rc = cudaStreamWaitEvent(st, ev[2 + i], 0) == cudaSuccess ? WB_OK : fail(WB_ECUDA, "stream wait failed");
+        if (rc == WB_OK) rc = fn(i * g, std::min(g, n_seq - i * g));
+        if (rc == WB_OK && cudaEventRecord(ev[2 + nch + i], st) != cudaSuccess)
+            rc = fail(WB_ECUDA, "event record failed");
+        if (rc == WB_OK && i + 1 < nch) rc = up(i + 1);
+        if (rc == WB_OK && i > 0) rc = down(i - 1);
+    }
+    if (rc == WB_OK) rc = down(nch - 1);
+    if (rc != WB_OK) {  // nothing the caller frees may still be in flight
+        cudaStreamSynchronize(ctx->cp_in);
+        cudaStreamSynchronize(ctx->cp_out);
+        cudaStreamSynchronize(st);
+        return rc;
+    }
+    WB_CUDA(cudaEventRecord(ev[1], ctx->cp_out));
+    WB_CUDA(cudaStreamWaitEvent(st, ev[1], 0));
+    return WB_OK;
+}
 
 // Makes ctx's profiler the calling thread's current one for one API call.
 struct ProfBind {
@@ -106,6 +212,7 @@ struct wb_attn_layer {
     int E = 0, H = 0, hd = 0, C = 0;
     std::vector<float> hn_host;  // softplus(harmonic_raw)
     float *harmonic_n = nullptr; // [H]
+    float *harmonic_raw = nullptr; // [H] (backward: d softplus = sigmoid(raw))
     // SIMT layouts (transposed so threads read consecutive outputs)
     float *wrs_t = nullptr, *brs = nullptr;  // [E][H][2], [H][2]
     float *wrs_h = nullptr;                  // [H][E][2]: one head's phase weights contiguous (decode)
@@ -147,6 +254,23 @@ struct wb_kv_cache {
     // waits, and the out_proj of the same layer may still be writing them.
     int out_layer = -1;
     cudaStream_t out_stream = nullptr;
+    // The device copy of the last host seq-id list a decode used and the
+    // stream it was uploaded on: a decode with the same list on the same
+    // stream reuses it instead of uploading the ids again.
+    int32_t *ids_mirror = nullptr;
+    std::vector<int32_t> ids_last;
+    cudaStream_t ids_stream = nullptr;
+    // Paged caches: each layer holds n_pages pages of WB_PAGE positions (all
+    // heads); a slot's positions 128p .. 128p+127 live in page
+    // pages[slot][p] (device table + host mirror, -1 unmapped), reserved by
+    // wb_kv_seq_reserve as a prefix p < reserved[slot] from a free list.
+    bool paged = false;
+    int n_pages = 0, max_pages = 0;
+    int32_t *pages = nullptr;
+    std::vector<int32_t> pages_host;
+    std::vector<int> reserved;
+    std::vector<int32_t> free_pages;
+    int seq_cap(int seq) const { return paged ? reserved[seq] * WB_PAGE : cap; }
     bool chain_ok(int layer, cudaStream_t st) const { return out_layer >= 0 && out_layer != layer && out_stream == st; }
     void note_decode(int layer, cudaStream_t st, bool ends_with_out) {
         out_layer = ends_with_out ? layer : -1;
@@ -162,15 +286,24 @@ struct wb_kv_cache {
         return WB_OK;
     }
     WbSeqView view(int layer, const int32_t *slots) const {
-        const long long per_layer = (long long)S * H * cap;
+        const long long per_layer = paged ? (long long)n_pages * H * WB_PAGE : (long long)S * H * cap;
         WbSeqView s;
         s.theta = theta + layer * per_layer;
         s.bucket = bucket + layer * per_layer;
         s.v = v + layer * per_layer * hd;
-        s.seq_stride = (long long)H * cap;
-        s.cap = cap;
+        s.seq_stride = paged ? (long long)H * WB_PAGE : (long long)H * cap;
+        s.cap = paged ? WB_PAGE : cap;
         s.slot = slots;
+        s.pages = paged ? pages : nullptr;
+        s.max_pages = max_pages;
         return s;
+    }
+    // the host index of (seq, head h, position t) of a layer view: see
+    // WbSeqView (the caller keeps t below seq_cap(seq))
+    long long host_pos(int seq, int h, int t) const {
+        if (!paged) return (long long)seq * H * cap + (long long)h * cap + t;
+        const int pg = pages_host[(size_t)seq * max_pages + (t >> WB_PAGE_SHIFT)];
+        return (long long)pg * H * WB_PAGE + (long long)h * WB_PAGE + (t & (WB_PAGE - 1));
     }
 };
 
@@ -218,6 +351,15 @@ int wb_context_destroy(wb_context *ctx) {
     if (ctx->ws.p) cudaFree(ctx->ws.p);
     if (ctx->io.p) cudaFree(ctx->io.p);
     if (ctx->dev_err) cudaFree(ctx->dev_err);
+    if (ctx->cp_in) {
+        cudaStreamSynchronize(ctx->cp_in);
+        cudaStreamDestroy(ctx->cp_in);
+    }
+    if (ctx->cp_out) {
+        cudaStreamSynchronize(ctx->cp_out);
+        cudaStreamDestroy(ctx->cp_out);
+    }
+    for (cudaEvent_t e : ctx->ev) cudaEventDestroy(e);
     if (ctx->own) cudaStreamDestroy(ctx->own);
     wb::prof_destroy(ctx->prof);
     delete ctx;
@@ -329,6 +471,7 @@ int wb_attn_layer_create(wb_context *ctx, const wb_attn_weights_desc *w, wb_attn
 
     int rc = WB_OK;
     if (rc == WB_OK) rc = upload(&L->harmonic_n, L->hn_host);
+    if (rc == WB_OK) rc = upload(&L->harmonic_raw, std::vector<float>(w->harmonic_raw, w->harmonic_raw + H));
     if (rc == WB_OK) rc = upload(&L->wrs_t, wrs);
     if (rc == WB_OK) rc = upload(&L->wrs_h, wrs_h);
     if (rc == WB_OK) rc = upload(&L->brs, brs);
@@ -359,7 +502,8 @@ int wb_attn_layer_create(wb_context *ctx, const wb_attn_weights_desc *w, wb_attn
 int wb_attn_layer_destroy(wb_attn_layer *L) {
     if (!L) return WB_OK;
     DeviceGuard g(L->device);
-    float *ptrs[] = {L->harmonic_n, L->wrs_t, L->wrs_h, L->brs, L->wc_t, L->bc, L->wv_t, L->bv, L->wo_t, L->bo};
+    float *ptrs[] = {L->harmonic_n, L->harmonic_raw, L->wrs_t, L->wrs_h, L->brs, L->wc_t, L->bc, L->wv_t, L->bv,
+                     L->wo_t, L->bo};
     for (float *p : ptrs)
         if (p) cudaFree(p);
     wb::tc_layer_free(&L->tc);
@@ -484,9 +628,12 @@ int wb_attn_forward(wb_context *ctx, const wb_attn_layer *L, const float *x, int
     const float *xd = x_dev ? x : (const float *)(iob + o_x);
     float *yd = y_dev ? y : (float *)(iob + o_y);
     float *awd = att_w ? (aw_dev ? att_w : (float *)(iob + o_aw)) : nullptr;
-    if (!x_dev) WB_CUDA(cudaMemcpyAsync((void *)xd, x, R * E * sizeof(float), cudaMemcpyHostToDevice, st));
+    const bool chunked = !exact && (!x_dev || !y_dev) && (!phases_out || ph_dev);
+    if (!x_dev && !chunked)
+        WB_CUDA(cudaMemcpyAsync((void *)xd, x, R * E * sizeof(float), cudaMemcpyHostToDevice, st));
 
     int rc;
+    bool y_down = false;  // y already copied to the host
     if (exact) {
         Carve c;
         size_t o_rs = c.take<float>(R * 2 * H);
@@ -516,6 +663,17 @@ int wb_attn_forward(wb_context *ctx, const wb_attn_layer *L, const float *x, int
             WB_CUDA(cudaMemcpyAsync(phd, sv.theta, R * H * sizeof(float), cudaMemcpyDeviceToDevice, st));
         }
         WB_CUDA(cudaGetLastError());
+    } else if (chunked) {
+        // host rows: sequence chunks, copies overlapped with the compute
+        const size_t seq_elems = (size_t)T * E;
+        WB_TRY(run_chunked(ctx, B, seq_elems, x_dev ? nullptr : x, xd, y_dev ? nullptr : y, yd, [&](int s0, int n) {
+            std::string msg;
+            const int r = wb::tc_attn_forward(L->tc, xd + s0 * seq_elems, n, T, use_content, yd + s0 * seq_elems,
+                                              phases_out ? phases_out + (size_t)s0 * H * T : nullptr, &ctx->ws,
+                                              ctx->dev_err, ctx->sm_count, st, &msg);
+            return r == WB_OK ? r : fail(r, msg);
+        }));
+        y_down = true;
     } else {
         std::string msg;
         float *phd = phases_out ? (ph_dev ? phases_out : (float *)(iob + o_ph)) : nullptr;
@@ -523,7 +681,7 @@ int wb_attn_forward(wb_context *ctx, const wb_attn_layer *L, const float *x, int
                                  ctx->sm_count, st, &msg);
         if (rc != WB_OK) return fail(rc, msg);
     }
-    if (!y_dev) WB_CUDA(cudaMemcpyAsync(y, yd, R * E * sizeof(float), cudaMemcpyDeviceToHost, st));
+    if (!y_dev && !y_down) WB_CUDA(cudaMemcpyAsync(y, yd, R * E * sizeof(float), cudaMemcpyDeviceToHost, st));
     if (att_w && !aw_dev)
         WB_CUDA(cudaMemcpyAsync(att_w, awd, (size_t)B * H * T * T * sizeof(float), cudaMemcpyDeviceToHost, st));
     if (phases_out && !ph_dev)
@@ -534,6 +692,144 @@ int wb_attn_forward(wb_context *ctx, const wb_attn_layer *L, const float *x, int
         WB_CUDA(cudaMemcpy(&derr, ctx->dev_err, sizeof(derr), cudaMemcpyDeviceToHost));
         if (derr) return fail(WB_ETIMEOUT, "device-side check failed, error word " + std::to_string(derr));
     }
+    return WB_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Forward with the backward's cache (attn.rs:90 with return_pathway_cache =
+// true) and the backward (attn.rs:346-430)
+// ---------------------------------------------------------------------------
+
+int wb_attn_forward_cache(wb_context *ctx, const wb_attn_layer *L, const float *x, int B, int T, int flags,
+                          float *y, const wb_attn_cache_desc *cache) {
+    if (!ctx || !L || !x || !y || !cache) return fail(WB_EINVAL, "NULL argument");
+    if (L->ctx != ctx) return fail(WB_EINVAL, "layer belongs to another context");
+    if (flags & ~WB_NO_CONTENT) return fail(WB_EINVAL, "wb_attn_forward_cache takes WB_NO_CONTENT only");
+    if (!cache->phases || !cache->phase_rs || !cache->v_all || !cache->att_w || !cache->out_merged)
+        return fail(WB_EINVAL, "missing cache array");
+    if (B < 0 || T < 0) return fail(WB_EINVAL, "negative batch or seq_len");
+    if (B == 0 || T == 0) return WB_OK;
+    const long long R = (long long)B * T;
+    if (R > (1LL << 30) || (long long)B * L->H * T * T > (1LL << 34)) return fail(WB_EINVAL, "batch*seq_len too large");
+    const int E = L->E, H = L->H, hd = L->hd, C = L->C;
+    const bool use_content = C > 0 && !(flags & WB_NO_CONTENT);
+    if (use_content && !cache->content) return fail(WB_EINVAL, "the layer has content: cache.content is required");
+    DeviceGuard g(ctx->device);
+    ProfBind pb(ctx);
+    cudaStream_t st = ctx->stream;
+    // outputs and their sizes
+    float *outs[6] = {y, cache->phases, cache->phase_rs, cache->v_all, use_content ? cache->content : nullptr,
+                      cache->out_merged};
+    const size_t out_n[6] = {(size_t)R * E, (size_t)R * H, (size_t)R * H * 2, (size_t)R * H * hd,
+                             (size_t)R * H * (use_content ? C : 0), (size_t)R * E};
+    const size_t aw_n = (size_t)B * H * T * T;
+    const bool x_dev = is_device_ptr(x), aw_dev = is_device_ptr(cache->att_w);
+    Carve io;
+    size_t o_x = x_dev ? 0 : io.take<float>(R * E);
+    size_t o_out[6];
+    for (int i = 0; i < 6; i++) o_out[i] = (outs[i] && !is_device_ptr(outs[i])) ? io.take<float>(out_n[i]) : 0;
+    size_t o_aw = aw_dev ? 0 : io.take<float>(aw_n);
+    WB_TRY(ensure(ctx->io, io.off));
+    char *iob = (char *)ctx->io.p;
+    const float *xd = x_dev ? x : (const float *)(iob + o_x);
+    float *outd[6];
+    for (int i = 0; i < 6; i++) outd[i] = !outs[i] ? nullptr : is_device_ptr(outs[i]) ? outs[i] : (float *)(iob + o_out[i]);
+    float *awd = aw_dev ? cache->att_w : (float *)(iob + o_aw);
+    if (!x_dev) WB_CUDA(cudaMemcpyAsync((void *)xd, x, R * E * sizeof(float), cudaMemcpyHostToDevice, st));
+    // the exact forward (WB_PATH_EXACT): its intermediates are the cache
+    Carve c;
+    size_t o_rs = c.take<float>(R * 2 * H);
+    size_t o_ct = c.take<float>(use_content ? R * H * C : 1);
+    size_t o_bk = c.take<uint8_t>(R * H);
+    WB_TRY(ensure(ctx->ws, c.off));
+    char *w = (char *)ctx->ws.p;
+    WbSeqView sv;
+    sv.theta = outd[1];  // [B][H][T]
+    sv.bucket = (uint8_t *)(w + o_bk);
+    sv.v = outd[3];      // [B][H][T][hd]
+    sv.seq_stride = (long long)H * T;
+    sv.cap = T;
+    sv.slot = nullptr;
+    float *rs = (float *)(w + o_rs), *content = (float *)(w + o_ct);
+    WB_TRY(run_projections_exact(ctx, L, xd, B, T, sv, rs, content, use_content));
+    wb::launch_attn_simt(sv, use_content ? content : nullptr, use_content ? C : 0,
+                         use_content ? 1.0f / std::sqrt((float)C) : 0.0f, L->harmonic_n, B, H, T, hd, outd[5], awd, st);
+    wb::OutMap om{wb::OUT_DENSE, outd[0], E, sv, 0, T};
+    wb::launch_seqdot(outd[5], (int)R, E, E, L->wo_t, E, L->bo, 0, om, st);
+    wb::launch_rows_to_heads(rs, B, T, H, 2, outd[2], st);
+    if (use_content) wb::launch_rows_to_heads(content, B, T, H, C, outd[4], st);
+    WB_CUDA(cudaGetLastError());
+    bool host_out = !aw_dev;
+    for (int i = 0; i < 6; i++)
+        if (outs[i] && !is_device_ptr(outs[i])) {
+            WB_CUDA(cudaMemcpyAsync(outs[i], outd[i], out_n[i] * sizeof(float), cudaMemcpyDeviceToHost, st));
+            host_out = true;
+        }
+    if (!aw_dev) WB_CUDA(cudaMemcpyAsync(cache->att_w, awd, aw_n * sizeof(float), cudaMemcpyDeviceToHost, st));
+    if (host_out) WB_CUDA(cudaStreamSynchronize(st));
+    return WB_OK;
+}
+
+int wb_attn_backward(wb_context *ctx, const wb_attn_layer *L, const float *x, const float *d_y, int B, int T,
+                     int flags, const wb_attn_cache_desc *cache, float *d_x, const wb_attn_grads_desc *grads) {
+    if (!ctx || !L || !x || !d_y || !cache || !d_x) return fail(WB_EINVAL, "NULL argument");
+    if (L->ctx != ctx) return fail(WB_EINVAL, "layer belongs to another context");
+    if (flags & ~WB_NO_CONTENT) return fail(WB_EINVAL, "wb_attn_backward takes WB_NO_CONTENT only");
+    if (!cache->phases || !cache->phase_rs || !cache->v_all || !cache->att_w || !cache->out_merged)
+        return fail(WB_EINVAL, "missing cache array");
+    if (B < 0 || T < 0) return fail(WB_EINVAL, "negative batch or seq_len");
+    if (B == 0 || T == 0) return WB_OK;
+    const long long R = (long long)B * T;
+    if (R > (1LL << 30) || (long long)B * L->H * T * T > (1LL << 34)) return fail(WB_EINVAL, "batch*seq_len too large");
+    const int E = L->E, H = L->H, hd = L->hd, C = L->C;
+    const bool use_content = C > 0 && !(flags & WB_NO_CONTENT);
+    if (use_content && !cache->content) return fail(WB_EINVAL, "the layer has content: cache.content is required");
+    if (hd > 128) return fail(WB_ENOTSUP, "the backward supports head_dim <= 128");
+    DeviceGuard g(ctx->device);
+    ProfBind pb(ctx);
+    cudaStream_t st = ctx->stream;
+    // inputs: x, d_y, the cache arrays
+    const float *ins[8] = {x, d_y, cache->phases, cache->phase_rs, cache->v_all, use_content ? cache->content : nullptr,
+                           cache->att_w, cache->out_merged};
+    const size_t in_n[8] = {(size_t)R * E, (size_t)R * E, (size_t)R * H, (size_t)R * H * 2, (size_t)R * H * hd,
+                            (size_t)R * H * (use_content ? C : 0), (size_t)B * H * T * T, (size_t)R * E};
+    // outputs: d_x and the gradients (any may be NULL)
+    wb_attn_grads_desc gz{};
+    const wb_attn_grads_desc &gd = grads ? *grads : gz;
+    float *outs[10] = {d_x, gd.harmonic_raw, gd.phase_proj_w, gd.phase_proj_b, gd.v_proj_w, gd.v_proj_b,
+                       use_content ? gd.content_proj_w : nullptr, use_content ? gd.content_proj_b : nullptr,
+                       gd.out_proj_w, gd.out_proj_b};
+    const size_t out_n[10] = {(size_t)R * E, (size_t)H, (size_t)H * 2 * E, (size_t)H * 2, (size_t)H * hd * hd,
+                              (size_t)H * hd, (size_t)H * C * E, (size_t)H * C, (size_t)E * E, (size_t)E};
+    Carve io;
+    size_t o_in[8], o_out[10];
+    for (int i = 0; i < 8; i++) o_in[i] = (ins[i] && !is_device_ptr(ins[i])) ? io.take<float>(in_n[i]) : 0;
+    for (int i = 0; i < 10; i++) o_out[i] = (outs[i] && !is_device_ptr(outs[i])) ? io.take<float>(out_n[i]) : 0;
+    const size_t o_scr = io.take<uint8_t>(wb::attn_backward_scratch_bytes(B, H, T, hd, use_content ? C : 0, E));
+    WB_TRY(ensure(ctx->io, io.off));
+    char *iob = (char *)ctx->io.p;
+    const float *ind[8];
+    for (int i = 0; i < 8; i++) {
+        ind[i] = !ins[i] ? nullptr : is_device_ptr(ins[i]) ? ins[i] : (const float *)(iob + o_in[i]);
+        if (ins[i] && !is_device_ptr(ins[i]))
+            WB_CUDA(cudaMemcpyAsync((void *)ind[i], ins[i], in_n[i] * sizeof(float), cudaMemcpyHostToDevice, st));
+    }
+    float *outd[10];
+    for (int i = 0; i < 10; i++) outd[i] = !outs[i] ? nullptr : is_device_ptr(outs[i]) ? outs[i] : (float *)(iob + o_out[i]);
+    wb::BwdLayer bl{E, H, hd, use_content ? C : 0, L->tc.w_o32, L->harmonic_n, L->harmonic_raw, L->wrs_t, L->wv_t,
+                    use_content ? L->wc_t : nullptr};
+    wb::BwdCache bc{ind[2], ind[3], ind[4], ind[5], ind[6], ind[7]};
+    wb::BwdGrads bg{outd[1], outd[2], outd[3], outd[4], outd[5], outd[6], outd[7], outd[8], outd[9]};
+    std::string msg;
+    int rc = wb::attn_backward(bl, bc, ind[0], ind[1], B, T, outd[0], bg, iob + o_scr, st, &msg);
+    if (rc != WB_OK) return fail(rc, msg);
+    bool host_out = false;
+    for (int i = 0; i < 10; i++)
+        if (outs[i] && !is_device_ptr(outs[i])) {
+            WB_CUDA(cudaMemcpyAsync(outs[i], outd[i], out_n[i] * sizeof(float), cudaMemcpyDeviceToHost, st));
+            host_out = true;
+        }
+    if (host_out) WB_CUDA(cudaStreamSynchronize(st));
     return WB_OK;
 }
 
@@ -608,9 +904,12 @@ int wb_dot_attn_forward(wb_context *ctx, const wb_dot_attn_layer *L, const float
     const float *xd = x_dev ? x : (const float *)(iob + o_x);
     float *yd = y_dev ? y : (float *)(iob + o_y);
     if (!x_dev) WB_CUDA(cudaMemcpyAsync((void *)xd, x, R * E * sizeof(float), cudaMemcpyHostToDevice, st));
+    // the tensor path's core runs on tcgen05 for head_dim <= 64
+    const bool tc_core = !exact && E / H <= 64;
     Carve c;
     size_t o_qkv = c.take<float>(R * 3 * E);
     size_t o_o = c.take<float>(R * E);
+    size_t o_core = tc_core ? c.take<char>(wb::tc_dot_core_bytes(B, T, H)) : 0;
     WB_TRY(ensure(ctx->ws, c.off));
     float *qkv = (float *)((char *)ctx->ws.p + o_qkv), *o = (float *)((char *)ctx->ws.p + o_o);
     std::string msg;
@@ -622,7 +921,9 @@ int wb_dot_attn_forward(wb_context *ctx, const wb_dot_attn_layer *L, const float
         int rc = wb::tc_gemm_tf32(xd, L->w_qkv, L->b_qkv, qkv, (int)R, 3 * E, E, ctx->dev_err, st, &msg);
         if (rc != WB_OK) return fail(rc, msg);
     }
-    int rc = wb::launch_dot_attn(qkv, B, T, E, H, o, st, &msg);
+    int rc = tc_core ? wb::tc_dot_attention(qkv, B, T, E, H, o, (char *)ctx->ws.p + o_core, 0, ctx->dev_err,
+                                            ctx->sm_count, st, &msg)
+                     : wb::launch_dot_attn(qkv, B, T, E, H, o, st, &msg);
     if (rc != WB_OK) return fail(rc, msg);
     if (exact) {
         wb::OutMap om{wb::OUT_DENSE, yd, E, none, 0, T};
@@ -645,29 +946,38 @@ int wb_dot_attn_forward(wb_context *ctx, const wb_dot_attn_layer *L, const float
 // ---------------------------------------------------------------------------
 // KV cache
 // ---------------------------------------------------------------------------
-int wb_kv_cache_create(wb_context *ctx, int n_layers, int n_head, int head_dim, int max_seqs, int max_ctx,
-                       wb_kv_cache **out) {
+static int kv_create(wb_context *ctx, int n_layers, int n_head, int head_dim, int max_seqs, int max_ctx, int n_pages,
+                     wb_kv_cache **out) {
     if (!ctx || !out) return fail(WB_EINVAL, "NULL argument");
     *out = nullptr;
-    if (n_layers <= 0 || n_head <= 0 || head_dim <= 0 || head_dim > 256 || max_seqs <= 0 || max_ctx <= 0)
+    if (n_layers <= 0 || n_head <= 0 || head_dim <= 0 || head_dim > 256 || max_seqs <= 0 || max_ctx <= 0 ||
+        n_pages < 0)
         return fail(WB_EINVAL, "bad cache dimensions");
     DeviceGuard g(ctx->device);
     wb_kv_cache *c = new wb_kv_cache();
     c->ctx = ctx;
     c->device = ctx->device;
     c->L = n_layers; c->H = n_head; c->hd = head_dim; c->S = max_seqs; c->cap = max_ctx;
-    const size_t n = (size_t)n_layers * max_seqs * n_head * max_ctx;
+    size_t n = (size_t)n_layers * max_seqs * n_head * max_ctx;
+    if (n_pages > 0) {
+        c->paged = true;
+        c->n_pages = n_pages;
+        c->max_pages = (max_ctx + WB_PAGE - 1) / WB_PAGE;
+        c->cap = c->max_pages * WB_PAGE;  // a slot's capacity: whole pages
+        n = (size_t)n_layers * n_pages * n_head * WB_PAGE;
+    }
     if (cudaMalloc(&c->theta, n * sizeof(float)) != cudaSuccess ||
         cudaMalloc(&c->bucket, n) != cudaSuccess ||
         cudaMalloc(&c->v, n * head_dim * sizeof(float)) != cudaSuccess ||
-        cudaMalloc(&c->len, (size_t)n_layers * max_seqs * sizeof(int32_t)) != cudaSuccess) {
+        cudaMalloc(&c->len, (size_t)n_layers * max_seqs * sizeof(int32_t)) != cudaSuccess ||
+        (c->paged && cudaMalloc(&c->pages, (size_t)max_seqs * c->max_pages * sizeof(int32_t)) != cudaSuccess)) {
         cudaGetLastError();
         wb_kv_cache_destroy(c);
         return fail(WB_ENOMEM, "KV cache allocation failed (" + std::to_string(n * (5 + 4 * head_dim)) + " bytes)");
     }
     {
         std::string msg;
-        const size_t nb = wb::decode_scratch_bytes(max_seqs, n_head, head_dim, n_head * head_dim, max_ctx);
+        const size_t nb = wb::decode_scratch_bytes(max_seqs, n_head, head_dim, n_head * head_dim, c->cap);
         if (wb::ws_ensure(&c->dscratch, nb, &msg) != 0) {
             wb_kv_cache_destroy(c);
             return fail(WB_ENOMEM, msg);
@@ -678,13 +988,81 @@ int wb_kv_cache_create(wb_context *ctx, int n_layers, int n_head, int head_dim, 
             return fail(WB_ECUDA, "cudaMemset failed");
         }
     }
-    if (cudaMemset(c->len, 0, (size_t)n_layers * max_seqs * sizeof(int32_t)) != cudaSuccess) {
+    if (cudaMemset(c->len, 0, (size_t)n_layers * max_seqs * sizeof(int32_t)) != cudaSuccess ||
+        (c->paged && cudaMemset(c->pages, 0xFF, (size_t)max_seqs * c->max_pages * sizeof(int32_t)) != cudaSuccess)) {
         cudaGetLastError();
         wb_kv_cache_destroy(c);
         return fail(WB_ECUDA, "cudaMemset failed");
     }
     c->len_host.assign((size_t)n_layers * max_seqs, 0);
+    if (c->paged) {
+        c->pages_host.assign((size_t)max_seqs * c->max_pages, -1);
+        c->reserved.assign(max_seqs, 0);
+        for (int p = n_pages - 1; p >= 0; p--) c->free_pages.push_back(p);  // pages 0, 1, ... handed out first
+    }
     *out = c;
+    return WB_OK;
+}
+
+int wb_kv_cache_create(wb_context *ctx, int n_layers, int n_head, int head_dim, int max_seqs, int max_ctx,
+                       wb_kv_cache **out) {
+    return kv_create(ctx, n_layers, n_head, head_dim, max_seqs, max_ctx, 0, out);
+}
+
+int wb_kv_cache_create_paged(wb_context *ctx, int n_layers, int n_head, int head_dim, int max_seqs, int max_ctx,
+                             int n_pages, wb_kv_cache **out) {
+    if (n_pages <= 0) return fail(WB_EINVAL, "n_pages must be positive");
+    return kv_create(ctx, n_layers, n_head, head_dim, max_seqs, max_ctx, n_pages, out);
+}
+
+int wb_kv_seq_reserve(wb_kv_cache *c, int seq, int n_positions) {
+    if (!c) return fail(WB_EINVAL, "NULL argument");
+    if (seq < 0 || seq >= c->S) return fail(WB_EINVAL, "seq out of range");
+    if (n_positions < 0 || n_positions > c->cap) return fail(WB_EINVAL, "n_positions exceeds the slot capacity");
+    if (!c->paged) return WB_OK;  // contiguous slots hold max_ctx positions already
+    const int need = (n_positions + WB_PAGE - 1) / WB_PAGE;
+    const int have = c->reserved[seq];
+    if (need <= have) return WB_OK;
+    if ((size_t)(need - have) > c->free_pages.size())
+        return fail(WB_ENOMEM, "out of KV pages (" + std::to_string(c->free_pages.size()) + " free, " +
+                                   std::to_string(need - have) + " needed)");
+    DeviceGuard g(c->device);
+    int32_t *row = c->pages_host.data() + (size_t)seq * c->max_pages;
+    for (int p = have; p < need; p++) {
+        row[p] = c->free_pages.back();
+        c->free_pages.pop_back();
+    }
+    c->reserved[seq] = need;
+    // kernels of earlier calls never read entries >= have (unmapped then),
+    // so the update goes in stream order without a wait
+    WB_CUDA(cudaMemcpyAsync(c->pages + (size_t)seq * c->max_pages + have, row + have, (need - have) * sizeof(int32_t),
+                            cudaMemcpyHostToDevice, c->ctx->stream));
+    return WB_OK;
+}
+
+int wb_kv_seq_release(wb_kv_cache *c, int seq) {
+    if (!c) return fail(WB_EINVAL, "NULL argument");
+    if (seq < 0 || seq >= c->S) return fail(WB_EINVAL, "seq out of range");
+    WB_TRY(wb_kv_cache_reset_seq(c, seq));
+    if (!c->paged || c->reserved[seq] == 0) return WB_OK;
+    DeviceGuard g(c->device);
+    // calls still in flight may read the slot's pages: the pages return to
+    // the free list once the stream has passed them
+    WB_CUDA(cudaStreamSynchronize(c->ctx->stream));
+    int32_t *row = c->pages_host.data() + (size_t)seq * c->max_pages;
+    for (int p = c->reserved[seq] - 1; p >= 0; p--) {
+        c->free_pages.push_back(row[p]);
+        row[p] = -1;
+    }
+    c->reserved[seq] = 0;
+    WB_CUDA(cudaMemcpy(c->pages + (size_t)seq * c->max_pages, row, c->max_pages * sizeof(int32_t),
+                       cudaMemcpyHostToDevice));
+    return WB_OK;
+}
+
+int wb_kv_cache_free_pages(wb_kv_cache *c, int *n_free) {
+    if (!c || !n_free) return fail(WB_EINVAL, "NULL argument");
+    *n_free = c->paged ? (int)c->free_pages.size() : 0;
     return WB_OK;
 }
 
@@ -695,6 +1073,8 @@ int wb_kv_cache_destroy(wb_kv_cache *c) {
     if (c->bucket) cudaFree(c->bucket);
     if (c->v) cudaFree(c->v);
     if (c->len) cudaFree(c->len);
+    if (c->ids_mirror) cudaFree(c->ids_mirror);
+    if (c->pages) cudaFree(c->pages);
     if (c->dscratch.p) cudaFree(c->dscratch.p);
     delete c;
     return WB_OK;
@@ -732,21 +1112,23 @@ int wb_kv_cache_load(wb_context *ctx, wb_kv_cache *c, int layer, int seq, int n,
     if (!ctx || !c || !phases || !values) return fail(WB_EINVAL, "NULL argument");
     if (c->ctx != ctx) return fail(WB_EINVAL, "cache belongs to another context");
     if (layer < 0 || layer >= c->L || seq < 0 || seq >= c->S) return fail(WB_EINVAL, "layer/seq out of range");
-    if (n < 0 || n > c->cap) return fail(WB_EINVAL, "n exceeds cache capacity");
+    if (n < 0 || n > c->seq_cap(seq)) return fail(WB_EINVAL, "n exceeds the slot's (reserved) capacity");
     DeviceGuard g(ctx->device);
     cudaStream_t st = ctx->stream;
     if (c->refresh(st) != WB_OK) return fail(WB_ECUDA, "reading cache lengths failed");
     WbSeqView sv = c->view(layer, nullptr);
-    const bool dev = is_device_ptr(phases);
-    const cudaMemcpyKind kind = dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+    const cudaMemcpyKind kind = is_device_ptr(phases) ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+    const cudaMemcpyKind vkind = is_device_ptr(values) ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+    // runs of positions contiguous in the view: the whole row, or one page
+    const int run = c->paged ? WB_PAGE : std::max(n, 1);
     for (int h = 0; h < c->H; h++) {
-        const long long base = (long long)seq * sv.seq_stride + (long long)h * c->cap;
-        if (n) {
-            WB_CUDA(cudaMemcpyAsync(sv.theta + base, phases + (size_t)h * n, n * sizeof(float), kind, st));
-            WB_CUDA(cudaMemcpyAsync(sv.v + base * c->hd, values + (size_t)h * n * c->hd,
-                                    (size_t)n * c->hd * sizeof(float),
-                                    is_device_ptr(values) ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, st));
-            wb::launch_bucket_from_theta(sv.theta + base, sv.bucket + base, n, st);
+        for (int t0 = 0; t0 < n; t0 += run) {
+            const int m = std::min(run, n - t0);
+            const long long base = c->host_pos(seq, h, t0);
+            WB_CUDA(cudaMemcpyAsync(sv.theta + base, phases + (size_t)h * n + t0, m * sizeof(float), kind, st));
+            WB_CUDA(cudaMemcpyAsync(sv.v + base * c->hd, values + ((size_t)h * n + t0) * c->hd,
+                                    (size_t)m * c->hd * sizeof(float), vkind, st));
+            wb::launch_bucket_from_theta(sv.theta + base, sv.bucket + base, m, st);
         }
     }
     const int32_t nn = n;
@@ -766,13 +1148,18 @@ int wb_kv_cache_read(wb_context *ctx, wb_kv_cache *c, int layer, int seq, float 
     if (c->refresh(st) != WB_OK) return fail(WB_ECUDA, "reading cache lengths failed");
     const int n = c->len_host[(size_t)layer * c->S + seq];
     WbSeqView sv = c->view(layer, nullptr);
+    const int run = c->paged ? WB_PAGE : std::max(n, 1);
     for (int h = 0; h < c->H && n > 0; h++) {
-        const long long base = (long long)seq * sv.seq_stride + (long long)h * c->cap;
-        if (phases) WB_CUDA(cudaMemcpy(phases + (size_t)h * n, sv.theta + base, n * sizeof(float), cudaMemcpyDefault));
-        if (buckets) WB_CUDA(cudaMemcpy(buckets + (size_t)h * n, sv.bucket + base, n, cudaMemcpyDefault));
-        if (values)
-            WB_CUDA(cudaMemcpy(values + (size_t)h * n * c->hd, sv.v + base * c->hd, (size_t)n * c->hd * sizeof(float),
-                               cudaMemcpyDefault));
+        for (int t0 = 0; t0 < n; t0 += run) {
+            const int m = std::min(run, n - t0);
+            const long long base = c->host_pos(seq, h, t0);
+            const size_t o = (size_t)h * n + t0;
+            if (phases) WB_CUDA(cudaMemcpy(phases + o, sv.theta + base, m * sizeof(float), cudaMemcpyDefault));
+            if (buckets) WB_CUDA(cudaMemcpy(buckets + o, sv.bucket + base, m, cudaMemcpyDefault));
+            if (values)
+                WB_CUDA(cudaMemcpy(values + o * c->hd, sv.v + base * c->hd, (size_t)m * c->hd * sizeof(float),
+                                   cudaMemcpyDefault));
+        }
     }
     return WB_OK;
 }
@@ -794,8 +1181,12 @@ static int check_host_ids(wb_kv_cache *c, int layer_idx, const int32_t *ids, int
         const int len = c->len_host[(size_t)layer_idx * c->S + ids[i]];
         if (prefill && len != 0)
             return fail(WB_EINVAL, "prefill needs an empty slot (kv_cache.rs prefill starts from KvCache::new)");
-        if (prefill && T > c->cap) return fail(WB_EINVAL, "seq_len exceeds cache capacity");
-        if (!prefill && len >= c->cap) return fail(WB_EINVAL, "cache slot is full");
+        if (prefill && T > c->seq_cap(ids[i]))
+            return fail(WB_EINVAL, c->paged ? "seq_len exceeds the slot's reserved pages (wb_kv_seq_reserve)"
+                                            : "seq_len exceeds cache capacity");
+        if (!prefill && len >= c->seq_cap(ids[i]))
+            return fail(WB_EINVAL, c->paged ? "the slot's reserved pages are full (wb_kv_seq_reserve)"
+                                            : "cache slot is full");
         for (int j = 0; j < i; j++)
             if (ids[j] == ids[i]) return fail(WB_EINVAL, "duplicate seq id");
     }
@@ -812,33 +1203,13 @@ static int common_kv_checks(wb_context *ctx, wb_kv_cache *c, int layer_idx, cons
     return WB_OK;
 }
 
-int wb_kv_prefill(wb_context *ctx, wb_kv_cache *c, int layer_idx, const wb_attn_layer *L, const int32_t *seq_ids,
-                  int n_seq, const float *x, int T, int flags, float *y) {
-    WB_TRY(common_kv_checks(ctx, c, layer_idx, L, seq_ids, x, y, flags));
-    if (n_seq < 0 || T < 0) return fail(WB_EINVAL, "negative n_seq or seq_len");
-    if (n_seq > c->S) return fail(WB_EINVAL, "more sequences than cache slots");
-    if (n_seq == 0 || T == 0) return WB_OK;
-    if (T > c->cap) return fail(WB_EINVAL, "seq_len exceeds cache capacity");
-    DeviceGuard g(ctx->device);
-    ProfBind pb(ctx);
+// Prefill of sequences whose rows (xd, yd) and slots (ids_d) are on the
+// device: the body of wb_kv_prefill for one chunk of its sequences.
+static int kv_prefill_rows(wb_context *ctx, wb_kv_cache *c, int layer_idx, const wb_attn_layer *L,
+                           const int32_t *ids_d, int n_seq, const float *xd, int T, int flags, float *yd) {
     cudaStream_t st = ctx->stream;
-    const bool ids_dev = is_device_ptr(seq_ids);
-    if (!ids_dev) WB_TRY(check_host_ids(c, layer_idx, seq_ids, n_seq, true, T));
     const long long R = (long long)n_seq * T;
     const int E = L->E, H = L->H, hd = L->hd;
-    const bool x_dev = is_device_ptr(x), y_dev = is_device_ptr(y);
-    Carve io;
-    size_t o_x = x_dev ? 0 : io.take<float>(R * E);
-    size_t o_y = y_dev ? 0 : io.take<float>(R * E);
-    size_t o_ids = ids_dev ? 0 : io.take<int32_t>(n_seq);
-    if (io.off) WB_TRY(ensure(ctx->io, io.off));
-    char *iob = (char *)ctx->io.p;
-    const float *xd = x_dev ? x : (const float *)(iob + o_x);
-    float *yd = y_dev ? y : (float *)(iob + o_y);
-    const int32_t *ids_d = ids_dev ? seq_ids : (const int32_t *)(iob + o_ids);
-    if (!ids_dev)
-        WB_CUDA(cudaMemcpyAsync((void *)ids_d, seq_ids, n_seq * sizeof(int32_t), cudaMemcpyHostToDevice, st));
-    if (!x_dev) WB_CUDA(cudaMemcpyAsync((void *)xd, x, R * E * sizeof(float), cudaMemcpyHostToDevice, st));
     WbSeqView sv = c->view(layer_idx, ids_d);
     if (flags & WB_PATH_EXACT) {
         Carve cv;
@@ -852,20 +1223,57 @@ int wb_kv_prefill(wb_context *ctx, wb_kv_cache *c, int layer_idx, const wb_attn_
         wb::OutMap om{wb::OUT_DENSE, yd, E, sv, 0, T};
         wb::launch_seqdot(o, (int)R, E, E, L->wo_t, E, L->bo, 0, om, st);
         WB_CUDA(cudaGetLastError());
-    } else {
-        std::string msg;
-        int rc = wb::tc_kv_prefill(L->tc, sv, xd, n_seq, T, yd, &ctx->ws, ctx->dev_err, ctx->sm_count, st, &msg);
-        if (rc != WB_OK) return fail(rc, msg);
+        return WB_OK;
     }
-    wb::launch_len_update(c->len + (size_t)layer_idx * c->S, ids_d, n_seq, T, 1, c->S, c->cap, st);
+    std::string msg;
+    int rc = wb::tc_kv_prefill(L->tc, sv, xd, n_seq, T, yd, &ctx->ws, ctx->dev_err, ctx->sm_count, st, &msg);
+    return rc == WB_OK ? rc : fail(rc, msg);
+}
+
+int wb_kv_prefill(wb_context *ctx, wb_kv_cache *c, int layer_idx, const wb_attn_layer *L, const int32_t *seq_ids,
+                  int n_seq, const float *x, int T, int flags, float *y) {
+    WB_TRY(common_kv_checks(ctx, c, layer_idx, L, seq_ids, x, y, flags));
+    if (n_seq < 0 || T < 0) return fail(WB_EINVAL, "negative n_seq or seq_len");
+    if (n_seq > c->S) return fail(WB_EINVAL, "more sequences than cache slots");
+    if (n_seq == 0 || T == 0) return WB_OK;
+    if (T > c->cap) return fail(WB_EINVAL, "seq_len exceeds cache capacity");
+    DeviceGuard g(ctx->device);
+    ProfBind pb(ctx);
+    cudaStream_t st = ctx->stream;
+    const bool ids_dev = is_device_ptr(seq_ids);
+    if (!ids_dev) WB_TRY(check_host_ids(c, layer_idx, seq_ids, n_seq, true, T));
+    const long long R = (long long)n_seq * T;
+    const int E = L->E;
+    const bool x_dev = is_device_ptr(x), y_dev = is_device_ptr(y);
+    Carve io;
+    size_t o_x = x_dev ? 0 : io.take<float>(R * E);
+    size_t o_y = y_dev ? 0 : io.take<float>(R * E);
+    size_t o_ids = ids_dev ? 0 : io.take<int32_t>(n_seq);
+    if (io.off) WB_TRY(ensure(ctx->io, io.off));
+    char *iob = (char *)ctx->io.p;
+    const float *xd = x_dev ? x : (const float *)(iob + o_x);
+    float *yd = y_dev ? y : (float *)(iob + o_y);
+    const int32_t *ids_d = ids_dev ? seq_ids : (const int32_t *)(iob + o_ids);
+    if (!ids_dev)
+        WB_CUDA(cudaMemcpyAsync((void *)ids_d, seq_ids, n_seq * sizeof(int32_t), cudaMemcpyHostToDevice, st));
+    if (x_dev && y_dev) {
+        WB_TRY(kv_prefill_rows(ctx, c, layer_idx, L, ids_d, n_seq, xd, T, flags, yd));
+    } else {
+        // host rows: sequence chunks, copies overlapped with the compute
+        const size_t seq_elems = (size_t)T * E;
+        WB_TRY(run_chunked(ctx, n_seq, seq_elems, x_dev ? nullptr : x, xd, y_dev ? nullptr : y, yd,
+                           [&](int s0, int n) {
+                               return kv_prefill_rows(ctx, c, layer_idx, L, ids_d + s0, n, xd + s0 * seq_elems,
+                                                      T, flags, yd + s0 * seq_elems);
+                           }));
+    }
+    wb::launch_len_update(c->len + (size_t)layer_idx * c->S, ids_d, n_seq, T, 1, c->S, c->cap, st, c->pages,
+                          c->max_pages);
     WB_CUDA(cudaGetLastError());
     if (ids_dev) c->len_stale = true;
     else
         for (int i = 0; i < n_seq; i++) c->len_host[(size_t)layer_idx * c->S + seq_ids[i]] = T;
-    if (!y_dev) {
-        WB_CUDA(cudaMemcpyAsync(y, yd, R * E * sizeof(float), cudaMemcpyDeviceToHost, st));
-        WB_CUDA(cudaStreamSynchronize(st));
-    }
+    if (!y_dev) WB_CUDA(cudaStreamSynchronize(st));
     return WB_OK;
 }
 
@@ -881,19 +1289,43 @@ int wb_kv_decode(wb_context *ctx, wb_kv_cache *c, int layer_idx, const wb_attn_l
     const bool ids_dev = is_device_ptr(seq_ids);
     if (!ids_dev) WB_TRY(check_host_ids(c, layer_idx, seq_ids, n_seq, false, 0));
     const int E = L->E, H = L->H, hd = L->hd;
-    const bool x_dev = is_device_ptr(x), y_dev = is_device_ptr(y);
+    const MemInfo xm = mem_info(x), ym = mem_info(y);
+    const bool x_dev = xm.device;
+    // pinned host y on the tensor path's plain-store out_proj: the kernel
+    // writes the caller's rows directly, with no copy back
+    const bool y_alias = !ym.device && ym.alias && !(flags & WB_PATH_EXACT) &&
+                         n_seq < wb::tc_decode_plain_store_rows();
+    const bool y_dev = ym.device || y_alias;
     Carve io;
     size_t o_x = x_dev ? 0 : io.take<float>((size_t)n_seq * E);
     size_t o_y = y_dev ? 0 : io.take<float>((size_t)n_seq * E);
-    size_t o_ids = ids_dev ? 0 : io.take<int32_t>(n_seq);
     if (io.off) WB_TRY(ensure(ctx->io, io.off));
     char *iob = (char *)ctx->io.p;
     const float *xd = x_dev ? x : (const float *)(iob + o_x);
-    float *yd = y_dev ? y : (float *)(iob + o_y);
-    const int32_t *ids_d = ids_dev ? seq_ids : (const int32_t *)(iob + o_ids);
-    if (!ids_dev)
-        WB_CUDA(cudaMemcpyAsync((void *)ids_d, seq_ids, n_seq * sizeof(int32_t), cudaMemcpyHostToDevice, st));
-    if (!x_dev) WB_CUDA(cudaMemcpyAsync((void *)xd, x, (size_t)n_seq * E * sizeof(float), cudaMemcpyHostToDevice, st));
+    float *yd = ym.device ? y : (y_alias ? (float *)ym.alias : (float *)(iob + o_y));
+    const int32_t *ids_d = seq_ids;
+    if (!ids_dev) {
+        const bool same = c->ids_mirror && c->ids_stream == st && c->ids_last.size() == (size_t)n_seq &&
+                          std::memcmp(c->ids_last.data(), seq_ids, n_seq * sizeof(int32_t)) == 0;
+        if (!same) {
+            if (!c->ids_mirror) WB_CUDA(cudaMalloc(&c->ids_mirror, (size_t)c->S * sizeof(int32_t)));
+            // decodes on another stream may still read the previous list
+            if (c->ids_stream && c->ids_stream != st) WB_CUDA(cudaStreamSynchronize(c->ids_stream));
+            WB_CUDA(cudaMemcpyAsync(c->ids_mirror, seq_ids, n_seq * sizeof(int32_t), cudaMemcpyHostToDevice, st));
+            c->ids_last.assign(seq_ids, seq_ids + n_seq);
+            c->ids_stream = st;
+        }
+        ids_d = c->ids_mirror;
+    }
+    if (!x_dev) {
+        const size_t nx = (size_t)n_seq * E;
+        if (xm.alias && nx % 4 == 0 && reinterpret_cast<uintptr_t>(xm.alias) % 16 == 0) {
+            wb::launch_copy_f4((const float *)xm.alias, (float *)xd, (long long)nx, st);  // pinned: read over the bus
+            WB_CUDA(cudaGetLastError());
+        } else {
+            WB_CUDA(cudaMemcpyAsync((void *)xd, x, nx * sizeof(float), cudaMemcpyHostToDevice, st));
+        }
+    }
     WbSeqView sv = c->view(layer_idx, ids_d);
     int32_t *len_l = c->len + (size_t)layer_idx * c->S;
     if (flags & WB_PATH_EXACT) {
@@ -913,10 +1345,10 @@ int wb_kv_decode(wb_context *ctx, wb_kv_cache *c, int layer_idx, const wb_attn_l
             wb::launch_seqdot(xd + (size_t)h * hd, n_seq, hd, E, L->wv_t + (size_t)h * hd * hd, hd,
                               L->bv + (size_t)h * hd, 0, vm, st);
         }
-        wb::launch_decode_simt(sv, len_l, th, vn, L->harmonic_n, n_seq, H, hd, o, st);
+        wb::launch_decode_simt(sv, len_l, th, vn, L->harmonic_n, n_seq, H, hd, o, ctx->dev_err, st);
         wb::OutMap om{wb::OUT_DENSE, yd, E, sv, 0, 1};
         wb::launch_seqdot(o, n_seq, E, E, L->wo_t, E, L->bo, 0, om, st);
-        wb::launch_len_update(len_l, ids_d, n_seq, 1, 0, c->S, c->cap, st);
+        wb::launch_len_update(len_l, ids_d, n_seq, 1, 0, c->S, c->cap, st, c->pages, c->max_pages);
         c->note_decode(layer_idx, st, false);
         WB_CUDA(cudaGetLastError());
     } else {
@@ -931,10 +1363,8 @@ int wb_kv_decode(wb_context *ctx, wb_kv_cache *c, int layer_idx, const wb_attn_l
     if (ids_dev) c->len_stale = true;
     else
         for (int i = 0; i < n_seq; i++) c->len_host[(size_t)layer_idx * c->S + seq_ids[i]] += 1;
-    if (!y_dev) {
-        WB_CUDA(cudaMemcpyAsync(y, yd, (size_t)n_seq * E * sizeof(float), cudaMemcpyDeviceToHost, st));
-        WB_CUDA(cudaStreamSynchronize(st));
-    }
+    if (!y_dev) WB_CUDA(cudaMemcpyAsync(y, yd, (size_t)n_seq * E * sizeof(float), cudaMemcpyDeviceToHost, st));
+    if (!ym.device) WB_CUDA(cudaStreamSynchronize(st));
     return WB_OK;
 }
 
@@ -945,6 +1375,23 @@ int wb_test_gemm_bf16(wb_context *ctx, const uint16_t *A, const uint16_t *B, con
     std::string msg;
     int rc = wb::tc_gemm_bf16((const __nv_bfloat16 *)A, (const __nv_bfloat16 *)B, bias, C, M, N, K, ctx->dev_err,
                               ctx->stream, &msg);
+    return rc == WB_OK ? rc : fail(rc, msg);
+}
+
+int wb_test_dot_core(wb_context *ctx, const float *qkv, int B, int T, int E, int H, int mode, float *o) {
+    if (!ctx || !qkv || !o) return fail(WB_EINVAL, "NULL argument");
+    if (B <= 0 || T <= 0 || H <= 0 || E <= 0 || E % H || mode < 0 || mode > 2) return fail(WB_EINVAL, "bad shape or mode");
+    DeviceGuard g(ctx->device);
+    ProfBind pb(ctx);
+    std::string msg;
+    int rc;
+    if (mode == 2) {
+        rc = wb::launch_dot_attn(qkv, B, T, E, H, o, ctx->stream, &msg);
+    } else {
+        WB_TRY(ensure(ctx->ws, wb::tc_dot_core_bytes(B, T, H)));
+        rc = wb::tc_dot_attention(qkv, B, T, E, H, o, ctx->ws.p, mode == 1, ctx->dev_err, ctx->sm_count, ctx->stream,
+                                  &msg);
+    }
     return rc == WB_OK ? rc : fail(rc, msg);
 }
 

@@ -71,18 +71,56 @@ __device__ __forceinline__ float warp_sum(float v) {
 // Per-sequence view of phases / buckets / values, shared by the attention
 // forward (temporary slots, one per batch element) and the KV cache (one
 // slot per sequence and layer).  Element (seq b, head h, pos t):
-//   theta [slot(b)*seq_stride + h*cap + t]
-//   bucket[slot(b)*seq_stride + h*cap + t]
-//   V     [(slot(b)*seq_stride + h*cap + t) * hd + dd]
+//   contiguous (pages == nullptr):
+//     theta [slot(b)*seq_stride + h*cap + t]     (seq_stride = n_head * cap)
+//   paged (a paged KV cache): position t lives in page
+//     pages[slot(b)*max_pages + t / WB_PAGE], each page holding WB_PAGE
+//     positions of every head:
+//     theta [page*seq_stride + h*cap + t % WB_PAGE]  (cap = WB_PAGE,
+//                                                     seq_stride = n_head * WB_PAGE)
+//   bucket at the same index, V at index * hd + dd.
+// Either way the index of (b, h, t) is row(b, t) + h * cap, which is what
+// the row-wise kernels use; a page id < 0 (unmapped) gives index -1.
+static constexpr int WB_PAGE = 128;  // positions per KV page (the decode kernel's keys per warp)
+static constexpr int WB_PAGE_SHIFT = 7;
+
 struct WbSeqView {
     float *theta;
     uint8_t *bucket;
     float *v;
-    long long seq_stride;  // = n_head * cap
-    int cap;               // positions per (seq, head)
-    const int32_t *slot;   // batch index -> slot (nullptr = identity)
+    long long seq_stride;
+    int cap;
+    const int32_t *slot;              // batch index -> slot (nullptr = identity)
+    const int32_t *pages = nullptr;   // paged: [slot][max_pages] page ids (-1 unmapped)
+    int max_pages = 0;
 };
 
+// index of (slot, head 0, position t), or -1 when t's page is unmapped
+__device__ __forceinline__ long long wb_row_slot(const WbSeqView &s, int slot, int t) {
+    if (s.pages) {
+        const int pg = s.pages[(long long)slot * s.max_pages + (t >> WB_PAGE_SHIFT)];
+        return pg < 0 ? -1LL : (long long)pg * s.seq_stride + (t & (WB_PAGE - 1));
+    }
+    return (long long)slot * s.seq_stride + t;
+}
+__device__ __forceinline__ long long wb_row(const WbSeqView &s, int b, int t) {
+    return wb_row_slot(s, s.slot ? s.slot[b] : b, t);
+}
+// index of (seq b, head h, position t), or -1 (unmapped page)
+__device__ __forceinline__ long long wb_pos(const WbSeqView &s, int b, int h, int t) {
+    const long long r = wb_row(s, b, t);
+    return r < 0 ? -1LL : r + (long long)h * s.cap;
+}
+
+// a slot of a paged cache may hold position t only when t's page is mapped
+// (always true without a page table)
+__device__ __forceinline__ bool wb_pos_mapped(const int32_t *pages, int max_pages, int slot, int t) {
+    if (!pages) return true;
+    const int p = t >> WB_PAGE_SHIFT;
+    return t >= 0 && p < max_pages && pages[(long long)slot * max_pages + p] >= 0;
+}
+
+// contiguous views only: index of (seq b, head h, position 0)
 __device__ __forceinline__ long long wb_slot_base(const WbSeqView &s, int b, int h) {
     int slot = s.slot ? s.slot[b] : b;
     return (long long)slot * s.seq_stride + (long long)h * s.cap;

@@ -245,11 +245,25 @@ __global__ void __launch_bounds__(NW * 32, NW == 12 ? 3 : (NW == 8 ? 4 : 9)) dec
         if (split == 0 && h == 0 && tid == 0) atomicOr(a.dev_err, WB_DERR_BOUNDS);
         return;
     }
-    const long long base = (long long)slot * a.sv.seq_stride + (long long)h * a.sv.cap;
-    const float *theta = a.sv.theta + base;
-    const uint8_t *bucket = a.sv.bucket + base;
-    const float *V = a.sv.v + base * hd;
     const int k0 = split * DEC_CHUNK + warp * DEC_KEYS_PER_WARP;
+    // this warp's keys k0 .. k0 + 127 sit at index kbase + k: the slot's
+    // contiguous row of head h, or (paged cache) one page of the slot's
+    // page table -- an unmapped page holds no keys (kmapped false)
+    long long kbase;
+    bool kmapped = true;
+    int kcap;  // positions the slot can hold
+    if (a.sv.pages) {
+        kcap = a.sv.max_pages << WB_PAGE_SHIFT;
+        const int pg = k0 < kcap ? __ldg(a.sv.pages + (long long)slot * a.sv.max_pages + (k0 >> WB_PAGE_SHIFT)) : -1;
+        kmapped = pg >= 0;
+        kbase = (long long)max(pg, 0) * a.sv.seq_stride + (long long)h * WB_PAGE - k0;
+    } else {
+        kcap = a.sv.cap;
+        kbase = (long long)slot * a.sv.seq_stride + (long long)h * a.sv.cap;
+    }
+    const float *theta = a.sv.theta + kbase;
+    const uint8_t *bucket = a.sv.bucket + kbase;
+    const float *V = a.sv.v + kbase * hd;
     constexpr int KR = DEC_KEYS_PER_WARP / 32;
     uint8_t kb[KR];
     float kth[KR];
@@ -263,8 +277,8 @@ __global__ void __launch_bounds__(NW * 32, NW == 12 ? 3 : (NW == 8 ? 4 : 9)) dec
 #pragma unroll
         for (int c = 0; c < KR; c++) {
             const int k = k0 + c * 32 + lane;
-            kb[c] = k < a.sv.cap ? __ldg(bucket + k) : (uint8_t)0xFF;
-            kth[c] = k < a.sv.cap ? __ldg(theta + k) : 0.0f;
+            kb[c] = kmapped && k < kcap ? __ldg(bucket + k) : (uint8_t)0xFF;
+            kth[c] = kmapped && k < kcap ? __ldg(theta + k) : 0.0f;
         }
         // the weights needed after theta_q, behind the slot-dependent loads
         // in the memory pipeline
@@ -333,8 +347,8 @@ __global__ void __launch_bounds__(NW * 32, NW == 12 ? 3 : (NW == 8 ? 4 : 9)) dec
 #pragma unroll
         for (int c = 0; c < KR; c++) {
             const int k = k0 + c * 32 + lane;
-            kb[c] = k < n ? __ldg(bucket + k) : (uint8_t)0xFF;
-            kth[c] = k < n ? __ldg(theta + k) : 0.0f;
+            kb[c] = kmapped && k < n ? __ldg(bucket + k) : (uint8_t)0xFF;
+            kth[c] = kmapped && k < n ? __ldg(theta + k) : 0.0f;
         }
         ptx::griddep_wait();  // x (and every write) waits for the grid before
         decode_x_phase<8, DEC_THREADS>(xr, wrs, E, tid, xs, r, s);
@@ -375,7 +389,7 @@ __global__ void __launch_bounds__(NW * 32, NW == 12 ? 3 : (NW == 8 ? 4 : 9)) dec
         const int k = k0 + c * 32 + lane;
         bool ok = false;
         float p = 0.0f;
-        if (k < n) {
+        if (k < n && kmapped) {
             ok = ((amask >> kb[c]) & 1u) || k == n - 1;
             if (ok) {
                 p = decode_weight(__fmul_rn(hn, __fsub_rn(thq, kth[c])));
@@ -484,7 +498,16 @@ __global__ void __launch_bounds__(NW * 32, NW == 12 ? 3 : (NW == 8 ? 4 : 9)) dec
         }
     }
     // ---- merge (i, h): self term p = exp(1 - 1) = 1 (kv_cache.rs:294, :318),
-    // normalise, append (kv_cache.rs:323-326)
+    // normalise, append (kv_cache.rs:323-326) at position n (a paged slot
+    // without a page reserved for n is flagged and not appended)
+    long long inew;
+    if (a.sv.pages) {
+        const long long r = wb_row_slot(a.sv, slot, n);
+        inew = r < 0 ? -1 : r + (long long)h * WB_PAGE;
+    } else {
+        inew = (long long)slot * a.sv.seq_stride + (long long)h * a.sv.cap + n;
+    }
+    if (inew < 0 && tid == 0) atomicOr(a.dev_err, WB_DERR_BOUNDS);
     if (tid < hd) {
         float vn;
         if constexpr (ONE) {
@@ -494,11 +517,13 @@ __global__ void __launch_bounds__(NW * 32, NW == 12 ? 3 : (NW == 8 ? 4 : 9)) dec
             vn = __ldcg(vnew + tid);
         }
         a.o[(long long)i * E + (long long)h * hd + tid] = (od + vn) / (lall + 1.0f);
-        a.sv.v[(base + n) * hd + tid] = vn;
+        if (inew >= 0) a.sv.v[inew * hd + tid] = vn;
     }
     if (tid == 0) {
-        a.sv.theta[base + n] = thq;
-        a.sv.bucket[base + n] = (uint8_t)qb;
+        if (inew >= 0) {
+            a.sv.theta[inew] = thq;
+            a.sv.bucket[inew] = (uint8_t)qb;
+        }
         if (n_act > 1) a.ticket[(long long)i * a.H + h] = 0u;
     }
 }
@@ -531,6 +556,8 @@ struct DecodeOutArgs {
     int32_t *len;
     const int32_t *slot;
     int n_slots;
+    const int32_t *pages;  // paged cache: lengths advance only into mapped pages
+    int max_pages;
 };
 
 // W_o[k0 .. k0+kn)[c0 .. c0+32) -> ws[kn][32]: cp.async where the 16 bytes
@@ -580,7 +607,7 @@ __global__ void __launch_bounds__(OUT_THREADS) decode_out_kernel(DecodeOutArgs a
         const int sl = a.slot ? a.slot[tid] : tid;
         if (sl >= 0 && sl < a.n_slots) {
             const int cur = a.len[sl];
-            if (cur < a.cap) {
+            if (cur < a.cap && wb_pos_mapped(a.pages, a.max_pages, sl, cur)) {
                 lslot = sl;
                 lnew = cur + 1;
             }
@@ -672,16 +699,19 @@ __global__ void __launch_bounds__(OUT_THREADS) decode_out_kernel(DecodeOutArgs a
         } else {
             for (int i = tid; i < n; i += OUT_THREADS) {
                 const int slot = a.slot ? a.slot[i] : i;
-                if (slot >= 0 && slot < a.n_slots && a.len[slot] < a.cap) a.len[slot] += 1;
+                if (slot >= 0 && slot < a.n_slots && a.len[slot] < a.cap &&
+                    wb_pos_mapped(a.pages, a.max_pages, slot, a.len[slot]))
+                    a.len[slot] += 1;
             }
         }
     }
 }
 
 int launch_decode_out(const float *o, const float *wo_t, const float *bo, float *y, int n, int E, int cap,
-                      int32_t *len, const int32_t *slot, int n_slots, cudaStream_t st, std::string *msg) {
+                      int32_t *len, const int32_t *slot, int n_slots, cudaStream_t st, std::string *msg,
+                      const int32_t *pages, int max_pages) {
     ProfScope ps("decode_out", st);
-    DecodeOutArgs a{o, wo_t, bo, y, n, E, cap, len, slot, n_slots};
+    DecodeOutArgs a{o, wo_t, bo, y, n, E, cap, len, slot, n_slots, pages, max_pages};
     const int kc = std::min(E, OUT_KC);
     const int ost = ((kc + 3) & ~3) + 4;
     const size_t smem = sizeof(float) * ((size_t)kc * OUT_C + (size_t)OUT_R * ost + (size_t)OUT_S * OUT_R * OUT_C);

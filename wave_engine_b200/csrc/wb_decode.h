@@ -34,9 +34,11 @@ int launch_decode_attn(const DecodeLaunch &L, void *scratch, size_t scratch_byte
                        cudaStream_t st, std::string *msg);
 
 // y = o W_o^T + b for the step's n rows (wo_t input-major), then
-// len[slot[i]] += 1 for every row whose length is below cap.  Launched as a
+// len[slot[i]] += 1 for every row whose length is below cap (and, with a
+// page table, whose next position's page is mapped).  Launched as a
 // programmatic dependent of the attention grid.
 int launch_decode_out(const float *o, const float *wo_t, const float *bo, float *y, int n, int E, int cap,
-                      int32_t *len, const int32_t *slot, int n_slots, cudaStream_t st, std::string *msg);
+                      int32_t *len, const int32_t *slot, int n_slots, cudaStream_t st, std::string *msg,
+                      const int32_t *pages = nullptr, int max_pages = 0);
 
 }  // namespace wb

@@ -16,17 +16,18 @@
 #include "wave_b200.h"
 #include "wb_internal.h"
 
+#include <algorithm>
+
 namespace wb {
 
 static constexpr int DQ = 64;   // queries per CTA
 static constexpr int DKT = 32;  // keys per shared-memory tile
 
+// One CTA's 64 queries q0 .. q0+63 of (sequence b, head h).
 template <int HALF>
-__global__ void __launch_bounds__(2 * DQ) dot_attn_kernel(const float *__restrict__ qkv, int T, int E, int H,
-                                                          int hd, float scale, float *__restrict__ o) {
-    __shared__ float ks[DKT][2 * HALF + 1];
-    __shared__ float vs[DKT][2 * HALF + 1];
-    const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+__device__ __forceinline__ void dot_attn_tile(const float *__restrict__ qkv, int T, int E, int hd, float scale,
+                                              float *__restrict__ o, int qt, int h, int b,
+                                              float (&ks)[DKT][2 * HALF + 1], float (&vs)[DKT][2 * HALF + 1]) {
     const int tid = threadIdx.x, half = tid & 1;
     const int q0 = qt * DQ, q = q0 + (tid >> 1);
     const bool qok = q < T;
@@ -42,6 +43,7 @@ __global__ void __launch_bounds__(2 * DQ) dot_attn_kernel(const float *__restric
     }
     // the tile columns past head_dim are never loaded: zero them once (a
     // thread's half past nd multiplies them by its zero q entries)
+    __syncthreads();  // the previous tile of this CTA consumed
     for (int e = tid; e < DKT * (2 * HALF - hd); e += 2 * DQ) {
         const int kk = e / (2 * HALF - hd), d = hd + e % (2 * HALF - hd);
         ks[kk][d] = 0.0f;
@@ -95,6 +97,32 @@ __global__ void __launch_bounds__(2 * DQ) dot_attn_kernel(const float *__restric
     }
 }
 
+template <int HALF>
+__global__ void __launch_bounds__(2 * DQ) dot_attn_kernel(const float *__restrict__ qkv, int T, int E, int H,
+                                                          int hd, float scale, float *__restrict__ o) {
+    __shared__ float ks[DKT][2 * HALF + 1];
+    __shared__ float vs[DKT][2 * HALF + 1];
+    dot_attn_tile<HALF>(qkv, T, E, hd, scale, o, blockIdx.x, blockIdx.y, blockIdx.z, ks, vs);
+}
+
+// The 128-query tiles listed in tiles[1 .. tiles[0]] (entries bh * n_qt128
+// + tile, bh = b * H + h), two 64-query halves each, over a grid-stride loop.
+template <int HALF>
+__global__ void __launch_bounds__(2 * DQ) dot_attn_tiles_kernel(const float *__restrict__ qkv, int T, int E, int H,
+                                                                int hd, float scale, float *__restrict__ o,
+                                                                const int *__restrict__ tiles) {
+    __shared__ float ks[DKT][2 * HALF + 1];
+    __shared__ float vs[DKT][2 * HALF + 1];
+    const int n = 2 * tiles[0];
+    const int n_qt = (T + 2 * DQ - 1) / (2 * DQ);
+    for (int e = blockIdx.x; e < n; e += gridDim.x) {
+        const int tile = tiles[1 + (e >> 1)];
+        const int bh = tile / n_qt, qt = 2 * (tile - bh * n_qt) + (e & 1);
+        if (qt * DQ >= T) continue;  // uniform over the CTA
+        dot_attn_tile<HALF>(qkv, T, E, hd, scale, o, qt, bh % H, bh / H, ks, vs);
+    }
+}
+
 int launch_dot_attn(const float *qkv, int B, int T, int E, int H, float *o, cudaStream_t st, std::string *msg) {
     const int hd = E / H;
     const int half = (hd + 1) / 2;
@@ -113,6 +141,29 @@ int launch_dot_attn(const float *qkv, int B, int T, int E, int H, float *o, cuda
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         *msg = std::string("dot attention launch failed: ") + cudaGetErrorString(e);
+        return WB_ECUDA;
+    }
+    return WB_OK;
+}
+
+int launch_dot_attn_tiles(const float *qkv, int B, int T, int E, int H, float *o, const int *tiles, int max_tiles,
+                          cudaStream_t st, std::string *msg) {
+    const int hd = E / H;
+    const int half = (hd + 1) / 2;
+    const float scale = 1.0f / sqrtf((float)hd);
+    const int grid = std::max(1, std::min(2 * max_tiles, 256));
+    ProfScope ps("dot_attn_fallback", st);
+    if (half <= 8) dot_attn_tiles_kernel<8><<<grid, 2 * DQ, 0, st>>>(qkv, T, E, H, hd, scale, o, tiles);
+    else if (half <= 16) dot_attn_tiles_kernel<16><<<grid, 2 * DQ, 0, st>>>(qkv, T, E, H, hd, scale, o, tiles);
+    else if (half <= 24) dot_attn_tiles_kernel<24><<<grid, 2 * DQ, 0, st>>>(qkv, T, E, H, hd, scale, o, tiles);
+    else if (half <= 32) dot_attn_tiles_kernel<32><<<grid, 2 * DQ, 0, st>>>(qkv, T, E, H, hd, scale, o, tiles);
+    else {
+        *msg = "listed dot-product attention tiles support head_dim <= 64";
+        return WB_ENOTSUP;
+    }
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        *msg = std::string("dot attention fallback launch failed: ") + cudaGetErrorString(e);
         return WB_ECUDA;
     }
     return WB_OK;

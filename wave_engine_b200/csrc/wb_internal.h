@@ -95,13 +95,20 @@ void launch_attn_simt(const WbSeqView &sv, const float *content, int C, float co
                       float *att_w, cudaStream_t st);
 void launch_decode_simt(const WbSeqView &sv, const int32_t *len, const float *theta_new,
                         const float *v_new, const float *harmonic_n, int n_seq, int H, int hd,
-                        float *o, cudaStream_t st);
+                        float *o, uint32_t *dev_err, cudaStream_t st);
 void launch_theta_only(const float *rs, int n, float *theta, cudaStream_t st);
+// dst[0 .. n) = src[0 .. n) with 16-byte loads; n a multiple of 4, both
+// 16-byte aligned (src may be the device alias of pinned host memory).
+void launch_copy_f4(const float *src, float *dst, long long n, cudaStream_t st);
 void launch_len_update(int32_t *len, const int32_t *slots, int n_seq, int value, int set, int n_slots, int cap,
-                       cudaStream_t st);
+                       cudaStream_t st, const int32_t *pages = nullptr, int max_pages = 0);
 // Causal dot-product attention core (compute.rs:357-414): qkv [B*T][3E] ->
 // o [B*T][E] (head-major columns).
 int launch_dot_attn(const float *qkv, int B, int T, int E, int H, float *o, cudaStream_t st, std::string *msg);
+// The same core for the 128-query tiles listed in tiles[1 .. tiles[0]]
+// (device; entries (b * H + h) * ceil(T / 128) + tile), at most max_tiles.
+int launch_dot_attn_tiles(const float *qkv, int B, int T, int E, int H, float *o, const int *tiles, int max_tiles,
+                          cudaStream_t st, std::string *msg);
 void launch_bucket_from_theta(const float *theta, uint8_t *bucket, long long n, cudaStream_t st);
 
 }  // namespace wb

@@ -189,8 +189,7 @@ __global__ void __launch_bounds__(128, 1)
         // this lane's row (for the per-row cache offsets, shuffled below)
         const int mr = m0 + warp * 32 + lane;
         const int br = mr / a.T, tr = mr - br * a.T;
-        const long long slot_r = mr < a.R ? (a.sv.slot ? a.sv.slot[br] : br) : 0;
-        const long long row_off = slot_r * a.sv.seq_stride + tr;  // + h * cap per head
+        const long long row_off = mr < a.R ? wb_row(a.sv, br, tr) : -1;  // + h * cap per head; -1: no cache row
 #pragma unroll 1
         for (int c = 0; c < PBN / 32; c++) {
             uint32_t r[32], rc[32];
@@ -211,7 +210,9 @@ __global__ void __launch_bounds__(128, 1)
                 const long long off = __shfl_sync(0xffffffffu, row_off, j);
                 if (m >= a.R) continue;
                 const float v = buf[j * 33 + lane] + bv;
-                if (is_v) a.sv.v[(off + hoff) * a.hd + d] = v;
+                if (is_v) {
+                    if (off >= 0) a.sv.v[(off + hoff) * a.hd + d] = v;
+                }
                 else if (is_c) a.content[(long long)m * a.n_c + (n - a.n_v)] = v;
             }
         }
@@ -327,7 +328,8 @@ __global__ void __launch_bounds__(PH_THREADS, 3) phase_fma_kernel(const float *_
             if (hl >= Hg) break;
             const int h = h0 + hl;
             const float th = atan2f(acc[rr][q + 1], acc[rr][q]);
-            const long long pos = wb_slot_base(sv, b, h) + t;
+            const long long pos = wb_pos(sv, b, h, t);
+            if (pos < 0) continue;
             sv.theta[pos] = th;
             sv.bucket[pos] = (uint8_t)phase_to_bucket(th);
         }
@@ -385,19 +387,19 @@ __global__ void __launch_bounds__(VP_THREADS, 1) vproj_phase_kernel(VpArgs a) {
     const bool hi_ok = 32 + 4 * dg < HD;  // the second output quad exists
     // phase role: rows 2*rp, 2*rp + 1, outputs g*OPT .. +OPT-1
     const int rp = lane, g = warp;
-    // cache offsets (slot * seq_stride + t) of this thread's rows
+    // cache row indices (wb_row: + h * cap per head, -1 = none) of this thread's rows
     long long vrow[4], prow[2];
 #pragma unroll
     for (int i = 0; i < 4; i++) {
         const int row = m0 + rg * 4 + i;
         const int b = row < a.R ? row / a.T : 0, t = row - b * a.T;
-        vrow[i] = row < a.R ? (long long)(a.sv.slot ? a.sv.slot[b] : b) * a.sv.seq_stride + t : -1;
+        vrow[i] = row < a.R ? wb_row(a.sv, b, t) : -1;
     }
 #pragma unroll
     for (int i = 0; i < 2; i++) {
         const int row = m0 + 2 * rp + i;
         const int b = row < a.R ? row / a.T : 0, t = row - b * a.T;
-        prow[i] = row < a.R ? (long long)(a.sv.slot ? a.sv.slot[b] : b) * a.sv.seq_stride + t : -1;
+        prow[i] = row < a.R ? wb_row(a.sv, b, t) : -1;
     }
     float ph[2][VP_OPT];
 #pragma unroll
@@ -700,7 +702,7 @@ __global__ void __launch_bounds__(VT_THREADS, 1)
         long long base = -1;
         if (m < a.R) {
             const int b = m / a.T, t = m - b * a.T;
-            base = (long long)(a.sv.slot ? a.sv.slot[b] : b) * a.sv.seq_stride + t;
+            base = wb_row(a.sv, b, t);
         }
         float acc[NP];
 #pragma unroll

@@ -223,6 +223,13 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, int a_mn, int b_
            | ((uint32_t)(M >> 4) << 24);  // M / 16
 }
 
+// The same for fp16 A and B (kind::f16, D fp32).
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N, int a_mn, int b_mn) {
+    return (1u << 4)                      // D format F32; A, B format F16 (0)
+           | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) | ((uint32_t)(N >> 3) << 17) |
+           ((uint32_t)(M >> 4) << 24);
+}
+
 // Instruction descriptor for kind::tf32 (A, B K-major tf32, D fp32).
 __host__ __device__ constexpr uint32_t idesc_tf32(int M, int N) {
     return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);

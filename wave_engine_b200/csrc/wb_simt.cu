@@ -52,8 +52,8 @@ __global__ void __launch_bounds__(256) seqdot_kernel(const float *__restrict__ X
                 om.y[(long long)r * om.ldy + n] = v;
             } else {  // OUT_SEQ_V: value row of head om.h into the sequence view
                 const int b = r / om.T, tt = r - b * om.T;
-                long long base = wb_slot_base(om.sv, b, om.h) + tt;
-                om.sv.v[base * N + n] = v;
+                const long long pos = wb_pos(om.sv, b, om.h, tt);
+                if (pos >= 0) om.sv.v[pos * N + n] = v;
             }
         }
     }
@@ -85,9 +85,10 @@ __global__ void phase_kernel(const float *__restrict__ rs, int R, int H, int T, 
     const float rr = rs[(long long)i * 2], ss = rs[(long long)i * 2 + 1];
     const float th = atan2f(ss, rr);
     const int b = r / T, t = r - b * T;
-    const long long base = wb_slot_base(sv, b, h) + t;
-    sv.theta[base] = th;
-    sv.bucket[base] = (uint8_t)phase_to_bucket(th);
+    const long long pos = wb_pos(sv, b, h, t);
+    if (pos < 0) return;
+    sv.theta[pos] = th;
+    sv.bucket[pos] = (uint8_t)phase_to_bucket(th);
 }
 
 void launch_phase(const float *rs, int R, int H, int T, const WbSeqView &sv, cudaStream_t st) {
@@ -150,13 +151,18 @@ __global__ void __launch_bounds__(256) attn_simt_tiles_kernel(AttnSimtArgs a) {
 template <int DPL, class OutT>
 __device__ void attn_simt_query(const AttnSimtArgs &a, int b, int h, int q) {
     const int lane = threadIdx.x & 31;
-    const long long base = wb_slot_base(a.sv, b, h);
-    const float *theta = a.sv.theta + base;
-    const uint8_t *bucket = a.sv.bucket + base;
-    const float *V = a.sv.v + base * a.hd;
+    // key k of (b, h) at index at(k): contiguous, or through the page table
+    const bool paged = a.sv.pages != nullptr;
+    const long long base = paged ? 0 : wb_slot_base(a.sv, b, h);
+    auto at = [&](int k) -> long long { return paged ? wb_pos(a.sv, b, h, k) : base + k; };
+    const float *theta = a.sv.theta;
+    const uint8_t *bucket = a.sv.bucket;
+    const float *V = a.sv.v;
     const float hn = a.harmonic_n[h];
-    const float thq = theta[q];
-    const uint32_t amask = allowed_bucket_mask(bucket[q]);
+    const long long iq = at(q);
+    if (iq < 0) return;  // unmapped page: nothing to attend from
+    const float thq = theta[iq];
+    const uint32_t amask = allowed_bucket_mask(bucket[iq]);
     const int C = a.C;
     const long long HC = (long long)a.H * C;
     const float *cq_ptr = C ? a.content + ((long long)b * a.T + q) * HC + (long long)h * C : nullptr;
@@ -166,9 +172,11 @@ __device__ void attn_simt_query(const AttnSimtArgs &a, int b, int h, int q) {
 
     auto score = [&](int k) -> float {
         if (k > q) return -INFINITY;
-        const bool ok = ((amask >> bucket[k]) & 1u) || k == q - 1;
+        const long long ik = at(k);
+        if (ik < 0) return -INFINITY;
+        const bool ok = ((amask >> bucket[ik]) & 1u) || k == q - 1;
         if (!ok) return -INFINITY;
-        float s = cosf(__fmul_rn(hn, __fsub_rn(thq, theta[k])));
+        float s = cosf(__fmul_rn(hn, __fsub_rn(thq, theta[ik])));
         if (C) {
             const float *ck = a.content + ((long long)b * a.T + k) * HC + (long long)h * C;
             float dot = 0.0f;
@@ -208,8 +216,8 @@ __device__ void attn_simt_query(const AttnSimtArgs &a, int b, int h, int q) {
         const int nk = min(32, q - k0 + 1);
         for (int j = 0; j < nk; j++) {
             const float pj = __shfl_sync(0xffffffffu, p, j);
-            if (pj > 0.0f) {
-                const float *vr = V + (long long)(k0 + j) * a.hd;
+            if (pj > 0.0f) {  // p > 0 only for mapped keys
+                const float *vr = V + at(k0 + j) * a.hd;
 #pragma unroll
                 for (int i = 0; i < DPL; i++) {
                     const int dd = lane + 32 * i;
@@ -299,6 +307,7 @@ struct DecodeSimtArgs {
     const float *harmonic_n;
     int n_seq, H, hd;
     float *o;                // [n_seq][H*hd]
+    uint32_t *dev_err;       // WB_DERR_BOUNDS: the appended position's page is unmapped
 };
 
 template <int DPL>
@@ -308,10 +317,19 @@ __global__ void __launch_bounds__(128) decode_simt_kernel(DecodeSimtArgs a) {
     if (h >= a.H) return;
     const int slot = a.sv.slot ? a.sv.slot[i] : i;
     const int n = a.len[slot];
-    const long long base = wb_slot_base(a.sv, i, h);
-    const float *theta = a.sv.theta + base;
-    const uint8_t *bucket = a.sv.bucket + base;
-    const float *V = a.sv.v + base * a.hd;
+    // key k at index at(k): contiguous, or through the page table (the
+    // caller reserved pages for every cached key and the appended one)
+    const bool paged = a.sv.pages != nullptr;
+    const long long base = paged ? 0 : wb_slot_base(a.sv, i, h);
+    auto at = [&](int k) -> long long { return paged ? wb_pos(a.sv, i, h, k) : base + k; };
+    const long long inew = (n < 0 || (!paged && n >= a.sv.cap)) ? -1 : at(n);
+    if (inew < 0) {
+        if (lane == 0) atomicOr(a.dev_err, WB_DERR_BOUNDS);
+        return;
+    }
+    const float *theta = a.sv.theta;
+    const uint8_t *bucket = a.sv.bucket;
+    const float *V = a.sv.v;
     const float hn = a.harmonic_n[h];
     const float ph = a.theta_new[(long long)i * a.H + h];
     const int qb = phase_to_bucket(ph);
@@ -319,8 +337,9 @@ __global__ void __launch_bounds__(128) decode_simt_kernel(DecodeSimtArgs a) {
     const float *vnew = a.v_new + ((long long)i * a.H + h) * a.hd;
 
     auto score = [&](int k) -> float {  // k < n
-        const bool ok = ((amask >> bucket[k]) & 1u) || k == n - 1;
-        return ok ? cosf(__fmul_rn(hn, __fsub_rn(ph, theta[k]))) : -INFINITY;
+        const long long ik = at(k);
+        const bool ok = ((amask >> bucket[ik]) & 1u) || k == n - 1;
+        return ok ? cosf(__fmul_rn(hn, __fsub_rn(ph, theta[ik]))) : -INFINITY;
     };
     float m = (lane == 0) ? 1.0f : -INFINITY;  // self score (kv_cache.rs:294)
     for (int k = lane; k < n; k += 32) m = fmaxf(m, score(k));
@@ -348,7 +367,7 @@ __global__ void __launch_bounds__(128) decode_simt_kernel(DecodeSimtArgs a) {
         for (int j = 0; j < nk; j++) {
             const float pj = __shfl_sync(0xffffffffu, p, j);
             if (pj > 0.0f) {
-                const float *vr = V + (long long)(k0 + j) * a.hd;
+                const float *vr = V + at(k0 + j) * a.hd;
 #pragma unroll
                 for (int u = 0; u < DPL; u++) {
                     const int dd = lane + 32 * u;
@@ -359,7 +378,7 @@ __global__ void __launch_bounds__(128) decode_simt_kernel(DecodeSimtArgs a) {
     }
     const float p_self = __fdiv_rn(e_self, es);
     float *orow = a.o + (long long)i * a.H * a.hd + (long long)h * a.hd;
-    float *vdst = a.sv.v + (base + n) * a.hd;
+    float *vdst = a.sv.v + inew * a.hd;
 #pragma unroll
     for (int u = 0; u < DPL; u++) {
         const int dd = lane + 32 * u;
@@ -369,15 +388,15 @@ __global__ void __launch_bounds__(128) decode_simt_kernel(DecodeSimtArgs a) {
         }
     }
     if (lane == 0) {
-        a.sv.theta[base + n] = ph;
-        a.sv.bucket[base + n] = (uint8_t)qb;
+        a.sv.theta[inew] = ph;
+        a.sv.bucket[inew] = (uint8_t)qb;
     }
 }
 
 void launch_decode_simt(const WbSeqView &sv, const int32_t *len, const float *theta_new,
                         const float *v_new, const float *harmonic_n, int n_seq, int H, int hd,
-                        float *o, cudaStream_t st) {
-    DecodeSimtArgs a{sv, len, theta_new, v_new, harmonic_n, n_seq, H, hd, o};
+                        float *o, uint32_t *dev_err, cudaStream_t st) {
+    DecodeSimtArgs a{sv, len, theta_new, v_new, harmonic_n, n_seq, H, hd, o, dev_err};
     dim3 grid((H + 3) / 4, n_seq);
     ProfScope ps("decode_simt", st);
     if (hd <= 32) decode_simt_kernel<1><<<grid, 128, 0, st>>>(a);
@@ -399,18 +418,37 @@ void launch_theta_only(const float *rs, int n, float *theta, cudaStream_t st) {
 // len[slot] = value (set) or len[slot] += value, for slots inside [0,
 // n_slots); an increment stops at cap (a full cache was flagged already).
 __global__ void len_update_kernel(int32_t *len, const int32_t *slots, int n_seq, int value, int set, int n_slots,
-                                  int cap) {
+                                  int cap, const int32_t *pages, int max_pages) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n_seq) return;
     const int s = slots ? slots[i] : i;
     if (s < 0 || s >= n_slots) return;
-    if (set) len[s] = value;
-    else if (len[s] < cap) len[s] = min(cap, len[s] + value);
+    // a paged slot never grows past its reserved pages (those writes were skipped)
+    if (set) {
+        if (value == 0 || wb_pos_mapped(pages, max_pages, s, value - 1)) len[s] = value;
+    } else if (len[s] < cap && wb_pos_mapped(pages, max_pages, s, len[s] + value - 1)) {
+        len[s] = min(cap, len[s] + value);
+    }
 }
 void launch_len_update(int32_t *len, const int32_t *slots, int n_seq, int value, int set, int n_slots, int cap,
-                       cudaStream_t st) {
+                       cudaStream_t st, const int32_t *pages, int max_pages) {
     if (n_seq > 0)
-        len_update_kernel<<<(n_seq + 127) / 128, 128, 0, st>>>(len, slots, n_seq, value, set, n_slots, cap);
+        len_update_kernel<<<(n_seq + 127) / 128, 128, 0, st>>>(len, slots, n_seq, value, set, n_slots, cap, pages,
+                                                               max_pages);
+}
+
+// n floats from pinned host memory (its device alias) to device memory, 16
+// bytes per load: one pass over the bus without a copy-engine transfer,
+// whose fixed cost dominates the few KB of a decode step's inputs.
+__global__ void copy_f4_kernel(const float4 *__restrict__ src, float4 *__restrict__ dst, long long n4) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x)
+        dst[i] = src[i];
+}
+void launch_copy_f4(const float *src, float *dst, long long n, cudaStream_t st) {
+    const long long n4 = n / 4;
+    if (n4 <= 0) return;
+    const int grid = (int)std::min<long long>(148, (n4 + 255) / 256);
+    copy_f4_kernel<<<grid, 256, 0, st>>>(reinterpret_cast<const float4 *>(src), reinterpret_cast<float4 *>(dst), n4);
 }
 
 // Bucket derivation for wb_kv_cache_load: bucket[i] = phase_to_bucket(theta[i]).

@@ -47,6 +47,10 @@ static constexpr int QT = 128;      // queries per work item (TMEM lanes)
 static constexpr int KT = 128;      // keys per tile
 static constexpr float MASK_BIAS = -512.0f;
 static constexpr float BOUND_LIMIT = 64.0f;
+// dot-product attention: P and the values in fp16 (10-bit mantissa: P is
+// 8x finer than in bf16, which a softmax sharper than wave attention's
+// needs within 2e-3), so P = exp(s - shift) must stay below fp16's 65504
+static constexpr float DOT_BOUND_LIMIT = 10.0f;
 
 // ---------------------------------------------------------------------------
 // Tensor maps (driver entry point fetched at run time; no libcuda link).
@@ -104,6 +108,11 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
     return *reinterpret_cast<uint32_t *>(&v);
 }
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+__device__ __forceinline__ uint32_t pack_f16(float lo, float hi) {
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&v);
+}
+__device__ __forceinline__ float f16_round(float x) { return __half2float(__float2half_rn(x)); }
 
 // Features of the attention core, one warp per 32 consecutive rows
 // i = bh * T + t (8 warps per CTA).  Lane l owns row i0 + l for the per-row
@@ -133,9 +142,11 @@ __global__ void __launch_bounds__(FEAT_WARPS * 32) feat_kernel(FeatArgs a) {
     const long long ii = live ? i : total - 1;
     const int bh = (int)(ii / a.T), t = (int)(ii - (long long)bh * a.T);
     const int b = bh / a.Hg, h = a.h0 + (bh - b * a.Hg);
-    const long long base = wb_slot_base(a.sv, b, h);
-    const float th = a.sv.theta[base + t];
-    const int bk = a.sv.bucket[base + t];
+    // cache index of this row (an unmapped page -- never reserved by the
+    // caller -- reads index 0 instead of faulting)
+    const long long it = max(0LL, wb_pos(a.sv, b, h, t));
+    const float th = a.sv.theta[it];
+    const int bk = a.sv.bucket[it];
     const float n = a.hn[h];
     const int C = (NC && a.content) ? a.C : 0;
     float c[NC > 0 ? NC : 1];
@@ -198,7 +209,7 @@ __global__ void __launch_bounds__(FEAT_WARPS * 32) feat_kernel(FeatArgs a) {
     {
         const int hd = a.hd, hdp = a.hdp;
         const int nrows = (int)min(32LL, total - i0);
-        const long long vrow0 = base + t;  // this lane's value row (cache view)
+        const long long vrow0 = it;  // this lane's value row (cache view)
         for (int j0 = 0; j0 < nrows; j0 += 8) {
             float2 v[8][2];
 #pragma unroll
@@ -246,8 +257,9 @@ __global__ void __launch_bounds__(FEAT_WARPS * 32) feat_kernel(FeatArgs a) {
     for (int d = 0; d < NC; d++) cp[d] = __shfl_up_sync(0xffffffffu, c[d], 1);
     const int bh_below = __shfl_up_sync(0xffffffffu, bh, 1);
     if (t > 0 && (lane == 0 || bh_below != bh)) {
-        thp = a.sv.theta[base + t - 1];
-        bkp = a.sv.bucket[base + t - 1];
+        const long long ip = max(0LL, wb_pos(a.sv, b, h, t - 1));
+        thp = a.sv.theta[ip];
+        bkp = a.sv.bucket[ip];
         const float *cr =
             C ? a.content + ((long long)b * a.T + t - 1) * ((long long)a.H * C) + (long long)h * C : nullptr;
 #pragma unroll
@@ -305,6 +317,8 @@ struct AttnTcArgs {
     int E;
     int *sched;                 // [0] work counter, [1] fallback count, [2..] fallback tiles bh * n_qt + qt
     uint32_t *dev_err;
+    int dot;                    // dot-product features: bound |q| max|k| - s_self instead of the content bound
+    float bound;                // a score may exceed the row's shift by at most this (else the tile falls back)
 };
 
 __device__ __forceinline__ float fast_exp2(float x) {
@@ -388,7 +402,7 @@ __device__ __forceinline__ bool att_wait(uint64_t *bar, uint32_t parity, volatil
 //   warp 21 (MMA): lane 0 issues S_g = Qf Kf^T two tiles ahead of the
 //     softmax (S double buffered in TMEM) and O += P V (value hi and lo).
 // TMEM columns: S0 [0,128), S1 [128,256), O0 [256,256+HDP), O1 after it.
-template <int HDP, int FW>
+template <int HDP, int FW, bool P16>
 __global__ void __launch_bounds__(ATT_THREADS, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_vh, const __grid_constant__ CUtensorMap tm_vl,
@@ -465,8 +479,10 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                     for (int u = 0; u < 4; u++) {
                         const int q = qt * QT + u * 32 + lane;
                         if (q < a.T) {
-                            const float cn = __ldg(a.cnorm + (long long)bh * a.T + q);
-                            violate |= 0.25f * cn * (cm - cn) > BOUND_LIMIT;
+                            const long long rq = (long long)bh * a.T + q;
+                            const float cn = __ldg(a.cnorm + rq);
+                            violate |= a.dot ? cn * cm - __ldg(a.m0 + rq) > a.bound
+                                             : 0.25f * cn * (cm - cn) > a.bound;
                         }
                     }
                     if (__any_sync(0xffffffffu, violate)) {
@@ -543,7 +559,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
             constexpr uint32_t IDESC_QK = ptx::idesc_bf16(128, 128, 0, 0);
             // PV: N = 2*HDP, the value hi and lo tiles side by side (adjacent
             // 64-column atoms of the stage), O hi | O lo
-            constexpr uint32_t IDESC_PV = ptx::idesc_bf16(128, 2 * HDP, 0, 1);
+            constexpr uint32_t IDESC_PV = P16 ? ptx::idesc_f16(128, 2 * HDP, 0, 1) : ptx::idesc_bf16(128, 2 * HDP, 0, 1);
             const uint32_t sQ0 = ptx::smem_u32(sm + L::OFF_Q);
             int kq = 0, jq = 0;                // next QK: item, tile
             long long gq = 0, gp = 0;          // next QK / PV global tile
@@ -699,7 +715,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                             if (2 * i == pcol) e0 = ep;
                             if (2 * i + 1 == pcol) e1 = ep;
                             l += e0 + e1;
-                            pk[i] = pack_bf16(e0, e1);
+                            pk[i] = P16 ? pack_f16(e0, e1) : pack_bf16(e0, e1);
                         }
                     } else {
 #pragma unroll
@@ -707,7 +723,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                             const float e0 = fast_exp2(fmaf(__uint_as_float(r[2 * i]), LOG2E, nm0));
                             const float e1 = fast_exp2(fmaf(__uint_as_float(r[2 * i + 1]), LOG2E, nm0));
                             l += e0 + e1;
-                            pk[i] = pack_bf16(e0, e1);
+                            pk[i] = P16 ? pack_f16(e0, e1) : pack_bf16(e0, e1);
                         }
                     }
                 };
@@ -1012,15 +1028,15 @@ static int launch_gemm(bool tf32, const void *A, const void *W, const float *bia
     return WB_OK;
 }
 
-template <int HDP, int FW>
+template <int HDP, int FW, bool P16 = false>
 static int launch_attn_tc(const CUtensorMap &tq, const CUtensorMap &tk, const CUtensorMap &tvh,
                           const CUtensorMap &tvl, const AttnTcArgs &aa, int sm_count, cudaStream_t st,
                           std::string *msg) {
     using L = AttnSmem<HDP, FW>;
     const int grid = std::max(1, std::min(aa.n_items, sm_count));
     ProfScope ps("attn_tc", st);
-    cudaFuncSetAttribute(attn_tc_kernel<HDP, FW>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES);
-    attn_tc_kernel<HDP, FW><<<grid, ATT_THREADS, L::BYTES, st>>>(tq, tk, tvh, tvl, aa);
+    cudaFuncSetAttribute(attn_tc_kernel<HDP, FW, P16>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES);
+    attn_tc_kernel<HDP, FW, P16><<<grid, ATT_THREADS, L::BYTES, st>>>(tq, tk, tvh, tvl, aa);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         *msg = std::string("attention launch failed: ") + cudaGetErrorString(e);
@@ -1086,7 +1102,8 @@ static int tc_attention_core(const TcLayerWeights &t, const WbSeqView &sv, const
                             CU_TENSOR_MAP_SWIZZLE_128B, msg)))
             return rc;
     }
-    AttnTcArgs aa{(int)BH, H, T, hd, n_qt, Hg, h0, (int)(BH * n_qt), m0, sp, cn, cm, sv, ob, E, sched, dev_err};
+    AttnTcArgs aa{(int)BH, H, T, hd, n_qt, Hg, h0, (int)(BH * n_qt), m0, sp, cn, cm, sv, ob, E, sched, dev_err, 0,
+                  BOUND_LIMIT};
     if (hdp == 64)
         rc = fw == 64 ? launch_attn_tc<64, 64>(tq, tk, tvh, tvl, aa, sm_count, st, msg)
                       : launch_attn_tc<64, 16>(tq, tk, tvh, tvl, aa, sm_count, st, msg);
@@ -1105,6 +1122,141 @@ static int tc_attention_core(const TcLayerWeights &t, const WbSeqView &sv, const
         return launch_gemm(true, ob, t.w_o32, add_bias ? t.b_o : nullptr, y, (int)R, E, E, E, dev_err, st, msg);
     return launch_gemm(true, ob + (size_t)h0 * hd, t.w_o32 + (size_t)h0 * hd, add_bias ? t.b_o : nullptr, y, (int)R,
                        E, Hg * hd, E, dev_err, st, msg, E, E);
+}
+
+// ---------------------------------------------------------------------------
+// Dot-product attention on the same core (compute.rs:357-414): per row
+// i = (b * H + h) * T + t, Qf = bf16(q / sqrt(d)) and Kf = bf16(k) padded
+// with zeros to 64 columns (no bucket columns: nothing is masked but the
+// causal triangle), values as fp16 hi / lo, and the fixed shift = the fp32
+// self score q.k_t / sqrt(d), which every row contains.  A score exceeds
+// the shift by at most |q| max_k|k| / sqrt(d) - s_self; query tiles where
+// that passes the bound go to the fp32 core through the fallback list.
+// ---------------------------------------------------------------------------
+struct DotFeatArgs {
+    const float *qkv;  // [B*T][3E]
+    int B, H, T, hd, E;
+    float scale;
+    __nv_bfloat16 *qf, *kf, *vh, *vl;  // [BH][T][64]
+    float *m0, *sprev, *cnorm;         // [BH][T]
+    unsigned int *cmax;                // [BH], float bits of max |k|
+};
+
+static constexpr int DOT_FEAT_WARPS = 8;
+
+__global__ void __launch_bounds__(DOT_FEAT_WARPS * 32) dot_feat_kernel(DotFeatArgs a) {
+    const int lane = threadIdx.x & 31;
+    const long long i = (long long)blockIdx.x * DOT_FEAT_WARPS + (threadIdx.x >> 5);
+    const long long BH = (long long)a.B * a.H;
+    if (i >= BH * a.T) return;
+    const long long bh = i / a.T;
+    const int t = (int)(i - bh * a.T);
+    const int b = (int)(bh / a.H), h = (int)(bh - (long long)b * a.H);
+    const float *row = a.qkv + ((long long)b * a.T + t) * 3LL * a.E + (long long)h * a.hd;
+    float q[2], k[2], v[2];
+#pragma unroll
+    for (int u = 0; u < 2; u++) {
+        const int d = 2 * lane + u;
+        const bool ok = d < a.hd;
+        q[u] = ok ? __ldg(row + d) * a.scale : 0.0f;
+        k[u] = ok ? __ldg(row + a.E + d) : 0.0f;
+        v[u] = ok ? __ldg(row + 2 * a.E + d) : 0.0f;
+    }
+    const float vh0 = f16_round(v[0]), vh1 = f16_round(v[1]);
+    reinterpret_cast<uint32_t *>(a.qf + i * 64)[lane] = pack_bf16(q[0], q[1]);
+    reinterpret_cast<uint32_t *>(a.kf + i * 64)[lane] = pack_bf16(k[0], k[1]);
+    reinterpret_cast<uint32_t *>(a.vh + i * 64)[lane] = pack_f16(vh0, vh1);  // fp16 hi / lo (P is fp16)
+    reinterpret_cast<uint32_t *>(a.vl + i * 64)[lane] = pack_f16(v[0] - vh0, v[1] - vh1);
+    float s = fmaf(q[0], k[0], q[1] * k[1]);
+    float qq = fmaf(q[0], q[0], q[1] * q[1]);
+    float kk = fmaf(k[0], k[0], k[1] * k[1]);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        s += __shfl_xor_sync(0xffffffffu, s, o);
+        qq += __shfl_xor_sync(0xffffffffu, qq, o);
+        kk += __shfl_xor_sync(0xffffffffu, kk, o);
+    }
+    if (lane == 0) {
+        a.m0[i] = s;
+        a.sprev[i] = -INFINITY;  // no previous-position rule
+        a.cnorm[i] = sqrtf(qq);
+        atomicMax(a.cmax + bh, __float_as_uint(sqrtf(kk)));  // non-negative floats order as their bits
+    }
+}
+
+size_t tc_dot_core_bytes(int B, int T, int H) {
+    TcLayerWeights t{};
+    t.E = 64 * H;
+    t.H = H;
+    t.hd = 64;
+    // the core layout without its merged-output rows (the caller owns o)
+    const CoreLayout c = core_layout(t, B, T, 0, H, true);
+    return c.o;
+}
+
+int tc_dot_attention(const float *qkv, int B, int T, int E, int H, float *o, void *ws, int force_fallback,
+                     uint32_t *dev_err, int sm_count, cudaStream_t st, std::string *msg) {
+    const int hd = E / H;
+    if (hd > 64) {
+        *msg = "the tensor-core dot-product core supports head_dim <= 64";
+        return WB_ENOTSUP;
+    }
+    const long long BH = (long long)B * H;
+    const int n_qt = (T + QT - 1) / QT;
+    if (BH * n_qt > 0x7fffffffLL) {
+        *msg = "too many attention work items";
+        return WB_EINVAL;
+    }
+    TcLayerWeights t{};
+    t.E = 64 * H;
+    t.H = H;
+    t.hd = 64;
+    const CoreLayout lay = core_layout(t, B, T, 0, H, true);
+    char *w = (char *)ws;
+    __nv_bfloat16 *qf = (__nv_bfloat16 *)(w + lay.qf), *kf = (__nv_bfloat16 *)(w + lay.kf);
+    __nv_bfloat16 *vh = (__nv_bfloat16 *)(w + lay.vh), *vl = (__nv_bfloat16 *)(w + lay.vl);
+    float *m0 = (float *)(w + lay.m0), *sp = (float *)(w + lay.sp), *cn = (float *)(w + lay.cn);
+    unsigned int *cm = (unsigned int *)(w + lay.cm);
+    int *sched = (int *)(w + lay.sched);
+    if (cudaMemsetAsync(cm, 0, BH * sizeof(unsigned int), st) != cudaSuccess ||
+        cudaMemsetAsync(sched, 0, 2 * sizeof(int), st) != cudaSuccess) {
+        *msg = "cudaMemsetAsync failed";
+        return WB_ECUDA;
+    }
+    DotFeatArgs fa{qkv, B, H, T, hd, E, 1.0f / std::sqrt((float)hd), qf, kf, vh, vl, m0, sp, cn, cm};
+    {
+        ProfScope ps("dot_feat", st);
+        const unsigned grid = (unsigned)((BH * T + DOT_FEAT_WARPS - 1) / DOT_FEAT_WARPS);
+        dot_feat_kernel<<<grid, DOT_FEAT_WARPS * 32, 0, st>>>(fa);
+    }
+    if (force_fallback) {
+        // testing: every tile fails the bound (|q| max|k| - s_self > limit)
+        if (cudaMemsetAsync(cm, 0x7f, BH * sizeof(unsigned int), st) != cudaSuccess) {
+            *msg = "cudaMemsetAsync failed";
+            return WB_ECUDA;
+        }
+    }
+    int rc;
+    CUtensorMap tq, tk, tvh, tvl;
+    {
+        const uint64_t dims[3] = {64, (uint64_t)T, (uint64_t)BH};
+        const uint64_t strides[2] = {128, (uint64_t)T * 128};
+        const uint32_t box[3] = {64, 128, 1};
+        if ((rc = make_tmap(&tq, qf, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, dims, strides, box,
+                            CU_TENSOR_MAP_SWIZZLE_128B, msg)) ||
+            (rc = make_tmap(&tk, kf, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, dims, strides, box,
+                            CU_TENSOR_MAP_SWIZZLE_128B, msg)) ||
+            (rc = make_tmap(&tvh, vh, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, dims, strides, box,
+                            CU_TENSOR_MAP_SWIZZLE_128B, msg)) ||
+            (rc = make_tmap(&tvl, vl, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, dims, strides, box,
+                            CU_TENSOR_MAP_SWIZZLE_128B, msg)))
+            return rc;
+    }
+    WbSeqView none{};
+    AttnTcArgs aa{(int)BH, H, T, hd, n_qt, H, 0, (int)(BH * n_qt), m0, sp, cn, cm, none, o, E, sched, dev_err, 1,
+                  DOT_BOUND_LIMIT};
+    if ((rc = launch_attn_tc<64, 64, true>(tq, tk, tvh, tvl, aa, sm_count, st, msg))) return rc;
+    return launch_dot_attn_tiles(qkv, B, T, E, H, o, sched + 1, (int)(BH * n_qt), st, msg);
 }
 
 int tc_gemm_bf16(const __nv_bfloat16 *A, const __nv_bfloat16 *B, const float *bias, float *C, int M, int N, int K,
@@ -1194,6 +1346,7 @@ int tc_kv_prefill(const TcLayerWeights &t, const WbSeqView &sv, const float *x, 
 // the GEMM, B200, graph-replayed steps).
 static constexpr int kDecodeGemmMinRows = 64;
 static int decode_gemm_min_rows() { return kDecodeGemmMinRows; }
+int tc_decode_plain_store_rows() { return kDecodeGemmMinRows; }
 
 int tc_kv_decode(const TcLayerWeights &t, const WbSeqView &sv, int32_t *len, int cap, int n_slots, const float *x,
                  int n_seq, float *y, void *scratch, size_t scratch_bytes, uint32_t *dev_err, int sm_count,
@@ -1210,12 +1363,13 @@ int tc_kv_decode(const TcLayerWeights &t, const WbSeqView &sv, int32_t *len, int
     if (rc) return rc;
     if (n_seq >= decode_gemm_min_rows()) {
         // many rows: out_proj on the tcgen05 TF32 GEMM, then lengths += 1
-        launch_len_update(len, sv.slot, n_seq, 1, 0, n_slots, cap, st);
+        launch_len_update(len, sv.slot, n_seq, 1, 0, n_slots, cap, st, sv.pages, sv.max_pages);
         return launch_gemm(true, o, t.w_o32, t.b_o, y, n_seq, t.E, t.E, t.E, dev_err, st, msg);
     }
     // few rows: the SIMT out_proj kernel (programmatic dependent of the
     // attention grid), which also advances the lengths
-    rc = launch_decode_out(o, t.wo_t, t.b_o, y, n_seq, t.E, cap, len, sv.slot, n_slots, st, msg);
+    rc = launch_decode_out(o, t.wo_t, t.b_o, y, n_seq, t.E, cap, len, sv.slot, n_slots, st, msg, sv.pages,
+                          sv.max_pages);
     if (rc == WB_OK && ends_with_out) *ends_with_out = true;
     return rc;
 }

@@ -47,4 +47,18 @@ int tc_kv_decode(const TcLayerWeights &t, const WbSeqView &sv, int32_t *len, int
                  int n_seq, float *y, void *scratch, size_t scratch_bytes, uint32_t *dev_err, int sm_count,
                  cudaStream_t st, std::string *msg, bool chain = false, bool *ends_with_out = nullptr);
 
+// Dot-product attention core (compute.rs:357-414) on the tcgen05 attention
+// kernel: qkv [B*T][3E] (device) -> o [B*T][E], head_dim <= 64 (WB_ENOTSUP
+// above).  ws: tc_dot_core_bytes(B, T, H) bytes of device scratch.  Query
+// tiles whose scores could overflow the fixed shift are recomputed by the
+// fp32 core; force_fallback (testing) sends every tile there.
+size_t tc_dot_core_bytes(int B, int T, int H);
+int tc_dot_attention(const float *qkv, int B, int T, int E, int H, float *o, void *ws, int force_fallback,
+                     uint32_t *dev_err, int sm_count, cudaStream_t st, std::string *msg);
+
+// Row counts below this have tc_kv_decode write y with plain stores of its
+// SIMT out_proj kernel (no tensor map), so y may then be the device alias of
+// pinned host memory.
+int tc_decode_plain_store_rows();
+
 }  // namespace wb

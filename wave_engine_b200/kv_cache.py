@@ -18,19 +18,47 @@ from .attn import PATHS, _empty_like_input
 from .runtime import Context, default_context, device_layer, is_torch, ptr_of
 
 
+PAGE = 128  # positions per page of a paged cache (WB_KV_PAGE)
+
+
 class KvCache:
-    """Device-resident cache: n_layers x max_seqs slots of max_ctx positions."""
+    """Device-resident cache: n_layers x max_seqs slots of max_ctx positions.
+
+    With ``n_pages`` the cache is paged: each layer's storage is a pool of
+    ``n_pages`` pages of 128 positions (all heads) that slots take as they
+    grow -- ``reserve(seq, n_positions)`` before a prefill or decode needs
+    them, ``release(seq)`` when the request ends.  Results are identical to
+    the contiguous cache's."""
 
     def __init__(self, n_layers: int, n_head: int, head_dim: int, max_seqs: int = 1, max_ctx: int = 256,
-                 ctx: Context | None = None):
+                 ctx: Context | None = None, n_pages: int | None = None):
         self.ctx = ctx or default_context(0)
         self.n_layers, self.n_head, self.head_dim = n_layers, n_head, head_dim
         self.max_seqs, self.max_ctx = max_seqs, max_ctx
+        self.paged = n_pages is not None
         h = C.c_void_p()
-        _lib.call("wb_kv_cache_create", self.ctx.handle, n_layers, n_head, head_dim, max_seqs, max_ctx,
-                  C.byref(h))
+        if self.paged:
+            _lib.call("wb_kv_cache_create_paged", self.ctx.handle, n_layers, n_head, head_dim, max_seqs, max_ctx,
+                      int(n_pages), C.byref(h))
+        else:
+            _lib.call("wb_kv_cache_create", self.ctx.handle, n_layers, n_head, head_dim, max_seqs, max_ctx,
+                      C.byref(h))
         self.handle = h
         self.ctx.adopt(self)
+
+    def reserve(self, seq: int, n_positions: int) -> None:
+        """Paged cache: pages so that slot ``seq`` holds ``n_positions``
+        (WaveB200Error when the pool is short).  No-op when contiguous."""
+        _lib.call("wb_kv_seq_reserve", self.handle, int(seq), int(n_positions))
+
+    def release(self, seq: int) -> None:
+        """Empty slot ``seq`` and return its pages to the pool."""
+        _lib.call("wb_kv_seq_release", self.handle, int(seq))
+
+    def free_pages(self) -> int:
+        v = C.c_int(0)
+        _lib.call("wb_kv_cache_free_pages", self.handle, C.byref(v))
+        return int(v.value)
 
     def close(self) -> None:
         if self.handle:
