@@ -240,7 +240,13 @@ def run_ours(args):
     stream = torch.cuda.current_stream(dev)
     ctx.set_stream(stream.cuda_stream)
     layers = [wb.AttnLayer(ctx, wb.gaussian_block_attn(1000 + l, H, E, C)) for l in range(L)]
-    cache = wb.KvCache(L, H, hd, max_seqs=B, max_ctx=T + S, ctx=ctx)
+    if args.kv == "paged":
+        # one pool of 128-position pages, every sequence's T + S reserved up front
+        cache = wb.KvCache(L, H, hd, max_seqs=B, max_ctx=T + S, ctx=ctx, n_pages=B * (-(-(T + S) // 128)))
+        for i in range(B):
+            cache.reserve(i, T + S)
+    else:
+        cache = wb.KvCache(L, H, hd, max_seqs=B, max_ctx=T + S, ctx=ctx)
     g = torch.Generator(device=dev).manual_seed(1234 + 7919 * rank)
     x_pre = torch.randn((L, B, T, E), generator=g, device=dev)
     x_dec = torch.randn((S, L, B, E), generator=g, device=dev)
@@ -549,6 +555,7 @@ def run_ours(args):
                    "seq_len": T, "decode_steps": S, "content_dim": C,
                    "l2": "inputs larger than L2 (100 MB per prefill layer input, 3 GB in all)",
                    "decode": "one CUDA graph per decode step (24 fused kernels + length updates)",
+                   "kv_cache": args.kv,
                    "parallelism": f"dp{world} (sequences sharded, no collective)"},
         "prefill": {"tok_s": round(world * B * T / (pre_ms / 1e3), 1), "ms": round(pre_ms, 3)},
         "decode": {"tok_s": round(world * B * S / (dec_ms / 1e3), 1), "ms": round(dec_ms, 3)},
@@ -1079,6 +1086,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=8,
                     help="consecutive steps of the pipelined end-to-end run (every step's copies are timed; only the "
                          "first step's uploads have no compute to hide behind)")
+    ap.add_argument("--kv", choices=["contiguous", "paged"], default="contiguous",
+                    help="serve-768's KV cache: fixed slots (default) or a pool of 128-position pages")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
     args = ap.parse_args()
