@@ -186,7 +186,7 @@ __device__ __forceinline__ float decode_theta_q(float r, float s, float br, floa
 static constexpr int DEC_U = 8;  // value loads per lane in flight (DEC_U * 32 / G rows per warp)
 // NW: warps per CTA (4, 8 or 12); the register cap keeps 9, 4 or 3 CTAs
 // per SM resident so a serve-sized grid is one wave.
-template <int VEC, int NW>
+template <int VEC, int NW, bool PAGED>
 __global__ void __launch_bounds__(NW * 32, NW == 12 ? 3 : (NW == 8 ? 4 : 9)) decode_attn_kernel(DecodeArgs a) {
     constexpr int DEC_THREADS = NW * 32;
     constexpr int DEC_WARPS = NW;
@@ -252,7 +252,7 @@ __global__ void __launch_bounds__(NW * 32, NW == 12 ? 3 : (NW == 8 ? 4 : 9)) dec
     long long kbase;
     bool kmapped = true;
     int kcap;  // positions the slot can hold
-    if (a.sv.pages) {
+    if constexpr (PAGED) {
         kcap = a.sv.max_pages << WB_PAGE_SHIFT;
         const int pg = k0 < kcap ? __ldg(a.sv.pages + (long long)slot * a.sv.max_pages + (k0 >> WB_PAGE_SHIFT)) : -1;
         kmapped = pg >= 0;
@@ -501,13 +501,13 @@ __global__ void __launch_bounds__(NW * 32, NW == 12 ? 3 : (NW == 8 ? 4 : 9)) dec
     // normalise, append (kv_cache.rs:323-326) at position n (a paged slot
     // without a page reserved for n is flagged and not appended)
     long long inew;
-    if (a.sv.pages) {
+    if constexpr (PAGED) {
         const long long r = wb_row_slot(a.sv, slot, n);
         inew = r < 0 ? -1 : r + (long long)h * WB_PAGE;
+        if (inew < 0 && tid == 0) atomicOr(a.dev_err, WB_DERR_BOUNDS);
     } else {
-        inew = (long long)slot * a.sv.seq_stride + (long long)h * a.sv.cap + n;
+        inew = kbase + n;  // 0 <= n < cap (checked above)
     }
-    if (inew < 0 && tid == 0) atomicOr(a.dev_err, WB_DERR_BOUNDS);
     if (tid < hd) {
         float vn;
         if constexpr (ONE) {
@@ -517,10 +517,10 @@ __global__ void __launch_bounds__(NW * 32, NW == 12 ? 3 : (NW == 8 ? 4 : 9)) dec
             vn = __ldcg(vnew + tid);
         }
         a.o[(long long)i * E + (long long)h * hd + tid] = (od + vn) / (lall + 1.0f);
-        if (inew >= 0) a.sv.v[inew * hd + tid] = vn;
+        if (!PAGED || inew >= 0) a.sv.v[inew * hd + tid] = vn;
     }
     if (tid == 0) {
-        if (inew >= 0) {
+        if (!PAGED || inew >= 0) {
             a.sv.theta[inew] = thq;
             a.sv.bucket[inew] = (uint8_t)qb;
         }
@@ -751,20 +751,27 @@ void decode_scratch_tickets(int n_seq, int H, int hd, int E, int cap, size_t *of
     *bytes = d.end - d.ticket;
 }
 
-template <int VEC, int NW>
+template <int VEC, int NW, bool PAGED>
 static cudaError_t launch_attn(const DecodeArgs &a, dim3 grid, cudaStream_t st, bool chain) {
     const size_t smem = sizeof(float) * ((size_t)a.E + 2 * NW * DEC_KEYS_PER_WARP + NW * a.hd + NW + 2 * NW +
                                          NW * 32);
-    cudaFuncSetAttribute(decode_attn_kernel<VEC, NW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    cudaError_t e = launch_ex(decode_attn_kernel<VEC, NW>, grid, dim3(NW * 32), smem, st, chain, a);
+    cudaFuncSetAttribute(decode_attn_kernel<VEC, NW, PAGED>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = launch_ex(decode_attn_kernel<VEC, NW, PAGED>, grid, dim3(NW * 32), smem, st, chain, a);
     return e == cudaSuccess ? cudaGetLastError() : e;
 }
 
+// the paged variant is a separate instantiation: its page lookups stay out
+// of the contiguous cache's kernel
 template <int VEC>
 static cudaError_t launch_attn_nw(const DecodeArgs &a, int nw, dim3 grid, cudaStream_t st, bool chain) {
-    if (nw == 12) return launch_attn<VEC, 12>(a, grid, st, chain);
-    if (nw == 8) return launch_attn<VEC, 8>(a, grid, st, chain);
-    return launch_attn<VEC, 4>(a, grid, st, chain);
+    if (a.sv.pages) {
+        if (nw == 12) return launch_attn<VEC, 12, true>(a, grid, st, chain);
+        if (nw == 8) return launch_attn<VEC, 8, true>(a, grid, st, chain);
+        return launch_attn<VEC, 4, true>(a, grid, st, chain);
+    }
+    if (nw == 12) return launch_attn<VEC, 12, false>(a, grid, st, chain);
+    if (nw == 8) return launch_attn<VEC, 8, false>(a, grid, st, chain);
+    return launch_attn<VEC, 4, false>(a, grid, st, chain);
 }
 
 int launch_decode_attn(const DecodeLaunch &L, void *scratch, size_t scratch_bytes, float **o_out,
