@@ -769,6 +769,88 @@ def run_dot_workload(args):
         torch.distributed.destroy_process_group()
 
 
+SERVE_MODEL_CFG = {"E": 768, "H": 12, "L": 24, "B": 32, "T": 1024, "S": 32, "M": 16, "rk4": 16, "V": 50257,
+                   "desc": "the whole 768-dim serve layer on the GPU (kv_cache.rs prefill / forward_one): embedding, "
+                           "per layer LayerNorm -> wave attention (KV cache) and LayerNorm -> dual-maestro Kerr-ODE "
+                           "FFN (maestro 16, RK4-16, AGC), residual; final LayerNorm and phase_native_decode over a "
+                           "50257-token table; batch 32 x 1024-token prefill, then 32 decode steps"}
+
+
+def run_serve_model_workload(args):
+    """The serve loop of kv_cache.rs through ServeSession: seeded synthetic
+    weights (N(0, 0.02) linear weights, the reference's ODE constants), a
+    random token batch.  Prints its own JSON line: tok/s of prefill + decode,
+    and the per-kernel time of one prefill and one decode step."""
+    import numpy as np
+    import torch
+    import wave_engine_b200 as wb
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    c = SERVE_MODEL_CFG
+    E, H, L, B, T, S, M, V = c["E"], c["H"], c["L"], c["B"], c["T"], c["S"], c["M"], c["V"]
+    ctx = wb.Context(local)
+    stream = torch.cuda.current_stream(dev)
+    ctx.set_stream(stream.cuda_stream)
+    g = np.random.default_rng(5 + rank)
+    blocks = [wb.ServeBlock(np.ones(E, np.float32), np.zeros(E, np.float32), np.ones(E, np.float32),
+                            np.zeros(E, np.float32), wb.gaussian_block_attn(1000 + l, H, E, 0),
+                            wb.gaussian_ffn(2000 + l, E, M, rk4_steps=c["rk4"])) for l in range(L)]
+    model = wb.ServeModel((g.standard_normal((V, E)) / np.sqrt(E)).astype(np.float32), None, blocks,
+                          np.ones(E, np.float32), np.zeros(E, np.float32),
+                          output_corrector=np.zeros(E // 2, np.float32))
+    sess = wb.ServeSession(model, max_seqs=B, max_ctx=T + S * (args.warmup + args.steps + 2), ctx=ctx)
+    tokens = g.integers(0, V, (B, T)).astype(np.int32)
+    steps_tok = g.integers(0, V, (S, B)).astype(np.int32)
+    ids = np.arange(B, dtype=np.int32)
+
+    def run():
+        sess.cache.reset()
+        sess.prefill(tokens, ids)
+        e_mid.record(stream)
+        for s in range(S):
+            sess.forward_one(steps_tok[s], np.full(B, T + s, np.int32), ids)
+
+    e_mid = torch.cuda.Event(enable_timing=True)
+    for _ in range(args.warmup):
+        run()
+    torch.cuda.synchronize()
+    clocks = Clocks(local)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    pre_ms = 0.0
+    e0.record(stream)
+    for _ in range(args.steps):
+        s0 = torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        run()
+        torch.cuda.synchronize()
+        pre_ms += s0.elapsed_time(e_mid)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    pre_ms /= args.steps
+    ctx.profile("")
+    run()
+    prof = ctx.profile_report()
+    ctx.profile(None)
+    if ctx.take_device_error():
+        raise RuntimeError("device error in the serve-model run")
+    out = {"metric": "serve-model tok/s (prefill + decode, whole serve layer on the GPU)",
+           "value": round(B * (T + S) / (ms / 1e3), 1), "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
+           "vs_baseline": None, "dtype": "fp32 io; bf16/tf32 tensor-core attention and GEMMs, fp32 FFN",
+           "data": "synthetic (seeded weights, random tokens)", "config": {"workload": c["desc"]},
+           "prefill": {"tok_s": round(B * T / (pre_ms / 1e3), 1), "ms": round(pre_ms, 3)},
+           "decode": {"tok_s": round(B * S / ((ms - pre_ms) / 1e3), 1), "ms": round(ms - pre_ms, 3)},
+           "kernel_ms_one_step": {k: round(v[1], 3) for k, v in sorted(prof.items())},
+           "agc": sess.agc.state(), "clocks": clk,
+           "note": "the synchronous sections: host seq-id validation per call; the step is eager (no CUDA graph)"}
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+
+
 def run_prefill_workload(args):
     """Prefill through all attention layers of one of the prefill-only
     configurations (tensor path, content projection on): seeded N(0, 0.02)
@@ -1064,12 +1146,12 @@ def run_profile_case(args):
 
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
-    ap.add_argument("--workload", choices=["serve-768", "decode-stress", "dot-768"] + sorted(PREFILL_CFGS),
+    ap.add_argument("--workload", choices=["serve-768", "decode-stress", "dot-768", "serve-model"] + sorted(PREFILL_CFGS),
                     default="serve-768",
                     help="serve-768: the headline configuration (default); decode-stress: 256 sequences of "
                          "context 128-4096; prefill-168/-384/-4096: prefill through all layers of the 168-, "
                          "384- and 4096-dim models; dot-768: the legacy dot-product attention at the 768-dim "
-                         "shape")
+                         "shape; serve-model: the whole serve layer (attention + FFN + decoder) on the GPU")
     ap.add_argument("--profile-case", choices=["decode", "decode-stress", "prefill", "prefill-serve"], default=None,
                     help="run a small case for an ncu capture instead of the benchmark")
     ap.add_argument("--shard", choices=["batch", "heads"], default="batch",
@@ -1101,6 +1183,8 @@ def main():
         run_prefill_workload(args)
     elif args.workload == "dot-768" and args.impl == "ours":
         run_dot_workload(args)
+    elif args.workload == "serve-model" and args.impl == "ours":
+        run_serve_model_workload(args)
     elif args.impl == "reference" and args.workload != "serve-768":
         if int(os.environ.get("RANK", "0")) == 0:
             print(json.dumps({"impl": "reference", "unavailable": f"the CPU reference arm times the serve-768 "

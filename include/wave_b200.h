@@ -22,6 +22,13 @@
  *   wb_attn_backward  <- src/common/attn.rs:346 wave_attention_backward_full
  *                        and :432 wave_attention_backward_pathway (caller:
  *                        src/candle_tier/custom_attn.rs:132 bwd)
+ *   wb_ffn_*, wb_agc_* <- src/common/ffn.rs:39-230 ffn_forward_via_backend as
+ *                        the serve tier calls it (kv_cache.rs:199-209,
+ *                        :341-351), agc.rs OdeAgc
+ *   wb_layer_norm     <- src/common/model.rs:154 layer_norm
+ *   wb_embed, wb_residual_add, wb_phase_native_decode, wb_lm_head
+ *                     <- the rest of kv_cache.rs prefill / forward_one
+ *                        (:106-113, :220, :18-33, :365-378)
  *
  * Conventions
  *   - Every function returns int status: WB_OK (0) or a negative WB_E*.
@@ -82,6 +89,8 @@ typedef struct wb_context wb_context;
 typedef struct wb_attn_layer wb_attn_layer;
 typedef struct wb_kv_cache wb_kv_cache;
 typedef struct wb_dot_attn_layer wb_dot_attn_layer;
+typedef struct wb_ffn_layer wb_ffn_layer;
+typedef struct wb_agc wb_agc;
 
 /* Host-side view of one block's attention weights (attn.rs:19-46),
  * flattened per head.  All pointers are HOST memory and are only read
@@ -335,6 +344,90 @@ WB_API int wb_kv_decode(wb_context *ctx, wb_kv_cache *cache, int layer_idx, cons
  * call. */
 WB_API int wb_kv_decode_noalloc(wb_context *ctx, wb_kv_cache *cache, int layer_idx, const wb_attn_layer *layer,
                                 const int32_t *seq_ids, int n_seq, const float *x, float *y);
+
+/* ---- the serve-tier layer around the attention ------------------------- */
+/* kv_cache.rs prefill (:93-236) and forward_one (:241-381) run, per layer,
+ *   normed = layer_norm(hidden, ln); attn = attention(normed)   (wb_kv_*)
+ *   normed_ffn = layer_norm(hidden, ln_ffn); ffn = FFN(normed_ffn)
+ *   hidden += attn + ffn
+ * and then layer_norm(hidden, ln_f) and a decoder.  The entries below are
+ * those steps; with device pointers they queue on the context's stream
+ * without host synchronisation, so a whole serve step stays on the GPU. */
+
+/* KerrDualMaestroWeights of one block (model.rs, wave_model.rs:134-170) as
+ * the serve tier runs it: ffn.rs:39-230 with a frozen ODE and no memory --
+ * maestro_in, the AGC, the stencil Kerr ODE (fft_ode.rs:171-250; the
+ * four-wave-mixing term is not part of that path), the corrector plate,
+ * maestro_out and out_proj.  Arrays are host or device memory, row-major
+ * [out][in] as the reference's Vec<Vec<f32>>; they are copied at creation. */
+typedef struct {
+    int n_embd;            /* 2 * n_bands */
+    int maestro_dim;
+    int rk4_steps;         /* KerrWeights::rk4_n_steps */
+    int use_corrector;     /* Dims::use_corrector (the corrector plate) */
+    int out_groups;        /* 1: dense out_proj; > 1: block-diagonal groups */
+    const float *mi_squeeze_w, *mi_squeeze_b;   /* maestro_in: [M][E], [M] */
+    const float *mi_process_w, *mi_process_b;   /*             [E][M], [E] */
+    const float *mo_squeeze_w, *mo_squeeze_b;   /* maestro_out */
+    const float *mo_process_w, *mo_process_b;
+    const float *gamma_raw, *omega;             /* [n_bands] */
+    float alpha, beta;
+    const float *phase_correction;              /* [n_bands] */
+    const float *rk4_weights;                   /* [4] */
+    const float *out_w, *out_b;  /* dense: [E][E], [E]; block-diagonal: per group [gs][gs] then [gs],
+                                    groups one after another in out_w (out_proj.rs flatten order), out_b NULL */
+} wb_ffn_weights_desc;
+
+WB_API int wb_ffn_layer_create(wb_context *ctx, const wb_ffn_weights_desc *w, wb_ffn_layer **out);
+WB_API int wb_ffn_layer_destroy(wb_ffn_layer *layer);
+
+/* agc.rs OdeAgc::from_coupling(alpha, beta) (OdeAgc::new() is 0.1, 0.1),
+ * device resident.  The reference keeps one process-wide instance that every
+ * FFN call updates (ffn.rs:76); pass the same wb_agc to every call to match
+ * it. */
+WB_API int wb_agc_create(wb_context *ctx, float alpha, float beta, wb_agc **out);
+WB_API int wb_agc_destroy(wb_agc *agc);
+/* state[8] = ema_mean, ema_var, headroom, decay, min_threshold,
+ * max_threshold, threshold, count (synchronises the context's stream). */
+WB_API int wb_agc_read(wb_agc *agc, float *state);
+
+/* y = FFN(x), x and y [n_rows][n_embd] host or device.  The rows are
+ * n_rows / rows_per_call consecutive reference calls (one request's rows
+ * each): the AGC observes them one after another, in order, exactly as
+ * that many ffn_forward_via_backend calls would.  flags: WB_PATH_EXACT runs
+ * out_proj as the reference's sequential fp32 sums; otherwise a dense
+ * out_proj (n_embd a multiple of 8) runs on the tcgen05 GEMM as a bf16x3
+ * product (hi.hi + lo.hi + hi.lo, ~16 mantissa bits). */
+WB_API int wb_ffn_forward(wb_context *ctx, const wb_ffn_layer *layer, wb_agc *agc, const float *x, int n_rows,
+                          int rows_per_call, int flags, float *y);
+
+/* model.rs:154 layer_norm of each row of n values; weight, bias [n]. */
+WB_API int wb_layer_norm(wb_context *ctx, const float *x, int n_rows, int n, const float *weight, const float *bias,
+                         float *y);
+
+/* hidden[i] += a[i] + b[i] (kv_cache.rs:220, :352); DEVICE pointers. */
+WB_API int wb_residual_add(wb_context *ctx, float *hidden, const float *a, const float *b, long long n);
+
+/* hidden[r] = wte[tokens[r]] + wpe[wpe_index[r]] (the wpe row only when
+ * wpe_index[r] < n_pos; wpe may be NULL).  kv_cache.rs prefill indexes wpe
+ * by the token id (:108-110), forward_one by the position (:254-256): pass
+ * the tokens or the positions as wpe_index.  wte [vocab][n_embd] and wpe
+ * [n_pos][n_embd] are DEVICE pointers; tokens, wpe_index and hidden host or
+ * device.  An out-of-range token sets bit 0x8 of the device error word. */
+WB_API int wb_embed(wb_context *ctx, const int32_t *tokens, const int32_t *wpe_index, int n_rows, const float *wte,
+                    int vocab, const float *wpe, int n_pos, int n_embd, float *hidden);
+
+/* kv_cache.rs:18-33 phase_native_decode of each row of hidden [n_rows]
+ * [n_embd]: every band rotated by corrector [n_embd/2], then logits[r][v] =
+ * rotated . wte[v].  wb_lm_head (kv_cache.rs:365-378): logits = hidden .
+ * lm_head[v].  The tables are DEVICE pointers; hidden and logits host or
+ * device.  flags: WB_PATH_EXACT (sequential fp32 sums) or, for n_embd a
+ * multiple of 8, the bf16x3 tensor-core product (the table is split into
+ * bf16 hi / lo in the context's workspace on every call). */
+WB_API int wb_phase_native_decode(wb_context *ctx, const float *hidden, int n_rows, int n_embd,
+                                  const float *corrector, const float *wte, int vocab, int flags, float *logits);
+WB_API int wb_lm_head(wb_context *ctx, const float *hidden, int n_rows, int n_embd, const float *lm_head, int vocab,
+                      int flags, float *logits);
 
 #ifdef __cplusplus
 }

@@ -288,3 +288,109 @@ def bwd_combine(dxp, dxv, dxc=None):
     out = np.empty((t, n), np.float32)
     lib().wo_bwd_combine(_fp(dxp), _fp(dxv), _fp(dxc), H, t, n, _fp(out))
     return out
+
+
+# ---------------------------------------------------------------------------
+# serve-tier layer around the attention (serve_oracle.c): LayerNorm, the
+# dual-maestro Kerr-ODE FFN with its AGC, phase_native_decode / lm_head and
+# the embedding, composed as kv_cache.rs prefill / forward_one
+# ---------------------------------------------------------------------------
+class AgcState(C.Structure):
+    """agc.rs OdeAgc (the reference keeps one process-wide instance)."""
+    _fields_ = [("ema_mean", C.c_float), ("ema_var", C.c_float), ("headroom", C.c_float), ("decay", C.c_float),
+                ("min_threshold", C.c_float), ("max_threshold", C.c_float), ("threshold", C.c_float),
+                ("count", C.c_int64)]
+
+
+class _Ffn(C.Structure):
+    _fields_ = [("n_embd", C.c_int), ("maestro_dim", C.c_int), ("out_groups", C.c_int), ("rk4_steps", C.c_int),
+                ("use_corrector", C.c_int),
+                ("mi_sq_w", _F), ("mi_sq_b", _F), ("mi_pr_w", _F), ("mi_pr_b", _F),
+                ("mo_sq_w", _F), ("mo_sq_b", _F), ("mo_pr_w", _F), ("mo_pr_b", _F),
+                ("gamma_raw", _F), ("omega", _F), ("alpha", C.c_float), ("beta", C.c_float),
+                ("phase_correction", _F), ("rk4_w", _F), ("op_w", _F), ("op_b", _F)]
+
+
+def _serve_lib():
+    l = lib()
+    if not getattr(l, "_serve_ready", False):
+        l.wo_layer_norm.argtypes = [_F, C.c_int, _F, _F, _F]
+        l.wo_agc_init.argtypes = [C.POINTER(AgcState), C.c_float, C.c_float]
+        l.wo_ffn_forward.argtypes = [C.POINTER(_Ffn), C.POINTER(AgcState), _F, C.c_int, _F]
+        l.wo_phase_native_decode.argtypes = [_F, _F, _F, C.c_int, C.c_int, _F]
+        l.wo_lm_head.argtypes = [_F, _F, C.c_int, C.c_int, _F]
+        l.wo_embed.argtypes = [_I, _I, C.c_int, _F, _F, C.c_int, C.c_int, _F]
+        l._serve_ready = True
+    return l
+
+
+def agc_new(alpha: float = 0.1, beta: float = 0.1) -> AgcState:
+    """agc.rs OdeAgc::new() (from_coupling(0.1, 0.1)) or from_coupling(alpha, beta)."""
+    a = AgcState()
+    _serve_lib().wo_agc_init(C.byref(a), alpha, beta)
+    return a
+
+
+def layer_norm(x: np.ndarray, w: np.ndarray, b: np.ndarray) -> np.ndarray:
+    """model.rs:154 over the last axis."""
+    x = _f32(x)
+    w, b = _f32(w), _f32(b)
+    n = x.shape[-1]
+    xs = np.ascontiguousarray(x.reshape(-1, n))
+    y = np.empty_like(xs)
+    l = _serve_lib()
+    for i in range(xs.shape[0]):
+        l.wo_layer_norm(_fp(xs[i]), n, _fp(w), _fp(b), _fp(y[i]))
+    return y.reshape(x.shape)
+
+
+def ffn_forward(f: dict, agc: AgcState, x: np.ndarray) -> np.ndarray:
+    """ffn.rs:39-230 as kv_cache.rs runs it (freeze_ode, stencil ODE, no
+    memory) for ONE reference call over the rows of x [t][E] -> y [t][E];
+    ``agc`` is updated in place.  ``f`` is KerrFfnWeights.packed()."""
+    keep = {k: _f32(v) for k, v in f.items() if isinstance(v, np.ndarray)}
+    E = int(f["n_embd"])
+    s = _Ffn(E, int(f["maestro_dim"]), int(f["out_groups"]), int(f["rk4_steps"]), int(f["use_corrector"]),
+             *[_fp(keep[k]) for k in ("mi_squeeze_w", "mi_squeeze_b", "mi_process_w", "mi_process_b",
+                                      "mo_squeeze_w", "mo_squeeze_b", "mo_process_w", "mo_process_b",
+                                      "gamma_raw", "omega")],
+             float(f["alpha"]), float(f["beta"]), _fp(keep["phase_correction"]), _fp(keep["rk4_weights"]),
+             _fp(keep["out_w"]), _fp(keep.get("out_b")))
+    x = _f32(x)
+    t = x.shape[0]
+    y = np.empty((t, E), np.float32)
+    if _serve_lib().wo_ffn_forward(C.byref(s), C.byref(agc), _fp(x), t, _fp(y)) != 0:
+        raise RuntimeError("oracle wo_ffn_forward failed")
+    return y
+
+
+def phase_native_decode(hidden: np.ndarray, corrector: np.ndarray, wte: np.ndarray) -> np.ndarray:
+    """kv_cache.rs:18-33 for one hidden row [E] -> logits [vocab]."""
+    hidden, corrector, wte = _f32(hidden), _f32(corrector), _f32(wte)
+    V, E = wte.shape
+    out = np.empty(V, np.float32)
+    _serve_lib().wo_phase_native_decode(_fp(hidden), _fp(corrector), _fp(wte), V, E // 2, _fp(out))
+    return out
+
+
+def lm_head(hidden: np.ndarray, w: np.ndarray) -> np.ndarray:
+    """kv_cache.rs:365-378 for one hidden row."""
+    hidden, w = _f32(hidden), _f32(w)
+    V, E = w.shape
+    out = np.empty(V, np.float32)
+    _serve_lib().wo_lm_head(_fp(hidden), _fp(w), V, E, _fp(out))
+    return out
+
+
+def embed(tokens, wpe_index, wte: np.ndarray, wpe) -> np.ndarray:
+    """kv_cache.rs:106-113 (prefill: the wpe row is the token id) and :252-256
+    (forward_one: the position)."""
+    tok = np.ascontiguousarray(tokens, np.int32)
+    idx = np.ascontiguousarray(wpe_index, np.int32)
+    wte = _f32(wte)
+    wpe = _f32(wpe) if wpe is not None and np.size(wpe) else None
+    E = wte.shape[1]
+    out = np.empty((tok.shape[0], E), np.float32)
+    _serve_lib().wo_embed(tok.ctypes.data_as(_I), idx.ctypes.data_as(_I), tok.shape[0], _fp(wte), _fp(wpe),
+                          0 if wpe is None else wpe.shape[0], E, _fp(out))
+    return out

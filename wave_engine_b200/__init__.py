@@ -15,10 +15,14 @@ from .kv_cache import KvCache
 from .dot_attn import AttentionWeights, DotAttnLayer, attention, gaussian_attention_weights
 from ._lib import WaveB200Error
 from .checkpoint import WchkHeader, load_wchk_attention, read_wchk_header
+from .serve import (Agc, FfnLayer, KerrFfnWeights, ServeBlock, ServeModel, ServeSession, embed, ffn_forward,
+                    gaussian_ffn, layer_norm, lm_head, phase_native_decode, residual_add)
 
 __all__ = [
     "CONTENT_DIM", "Rng", "WaveAttnHeadWeights", "WaveAttnWeights", "gaussian_block_attn", "init_block_attn",
     "AttnLayer", "Context", "default_context", "wave_attention_forward", "wave_attention_forward_heads", "KvCache",
     "WaveAttnCache", "wave_attention_backward_full", "wave_attention_backward_pathway",
+    "Agc", "FfnLayer", "KerrFfnWeights", "ServeBlock", "ServeModel", "ServeSession", "embed", "ffn_forward",
+    "gaussian_ffn", "layer_norm", "lm_head", "phase_native_decode", "residual_add",
     "WaveB200Error", "WchkHeader", "load_wchk_attention", "read_wchk_header", "AttentionWeights", "DotAttnLayer", "attention", "gaussian_attention_weights",
 ]

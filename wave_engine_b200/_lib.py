@@ -62,6 +62,17 @@ SIGNATURES = {
     "wb_kv_decode_noalloc": (C.c_int, [_VP, _VP, C.c_int, _VP, _VP, C.c_int, _VP, _VP]),
     "wb_attn_forward_cache": (C.c_int, [_VP, _VP, _VP, C.c_int, C.c_int, C.c_int, _VP, _VP]),
     "wb_attn_backward": (C.c_int, [_VP, _VP, _VP, _VP, C.c_int, C.c_int, C.c_int, _VP, _VP, _VP]),
+    "wb_ffn_layer_create": (C.c_int, [_VP, _VP, C.POINTER(_VP)]),
+    "wb_ffn_layer_destroy": (C.c_int, [_VP]),
+    "wb_agc_create": (C.c_int, [_VP, C.c_float, C.c_float, C.POINTER(_VP)]),
+    "wb_agc_destroy": (C.c_int, [_VP]),
+    "wb_agc_read": (C.c_int, [_VP, _VP]),
+    "wb_ffn_forward": (C.c_int, [_VP, _VP, _VP, _VP, C.c_int, C.c_int, C.c_int, _VP]),
+    "wb_layer_norm": (C.c_int, [_VP, _VP, C.c_int, C.c_int, _VP, _VP, _VP]),
+    "wb_residual_add": (C.c_int, [_VP, _VP, _VP, _VP, C.c_longlong]),
+    "wb_embed": (C.c_int, [_VP, _VP, _VP, C.c_int, _VP, C.c_int, _VP, C.c_int, C.c_int, _VP]),
+    "wb_phase_native_decode": (C.c_int, [_VP, _VP, C.c_int, C.c_int, _VP, _VP, C.c_int, C.c_int, _VP]),
+    "wb_lm_head": (C.c_int, [_VP, _VP, C.c_int, C.c_int, _VP, C.c_int, C.c_int, _VP]),
     # include/wave_b200_testing.h
     "wb_test_gemm_bf16": (C.c_int, [_VP, _VP, _VP, _VP, _VP, C.c_int, C.c_int, C.c_int]),
     "wb_test_gemm_tf32": (C.c_int, [_VP, _VP, _VP, _VP, _VP, C.c_int, C.c_int, C.c_int]),
@@ -90,6 +101,16 @@ class GradsDesc(C.Structure):
     _fields_ = [("harmonic_raw", _VP), ("phase_proj_w", _VP), ("phase_proj_b", _VP), ("v_proj_w", _VP),
                 ("v_proj_b", _VP), ("content_proj_w", _VP), ("content_proj_b", _VP), ("out_proj_w", _VP),
                 ("out_proj_b", _VP)]
+
+
+class FfnWeightsDesc(C.Structure):
+    """wb_ffn_weights_desc (include/wave_b200.h)."""
+    _fields_ = [("n_embd", C.c_int32), ("maestro_dim", C.c_int32), ("rk4_steps", C.c_int32),
+                ("use_corrector", C.c_int32), ("out_groups", C.c_int32),
+                ("mi_squeeze_w", _VP), ("mi_squeeze_b", _VP), ("mi_process_w", _VP), ("mi_process_b", _VP),
+                ("mo_squeeze_w", _VP), ("mo_squeeze_b", _VP), ("mo_process_w", _VP), ("mo_process_b", _VP),
+                ("gamma_raw", _VP), ("omega", _VP), ("alpha", C.c_float), ("beta", C.c_float),
+                ("phase_correction", _VP), ("rk4_weights", _VP), ("out_w", _VP), ("out_b", _VP)]
 
 
 class WaveB200Error(RuntimeError):

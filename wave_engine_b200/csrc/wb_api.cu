@@ -6,6 +6,7 @@
 #include "wb_tc.h"
 #include "wb_bwd.h"
 #include "wb_decode.h"
+#include "wb_serve.h"
 
 #include <algorithm>
 #include <cmath>
@@ -233,6 +234,24 @@ struct wb_dot_attn_layer {
     int E = 0, H = 0;
     float *w_qkv = nullptr, *wt_qkv = nullptr, *b_qkv = nullptr;  // [3E][E] (GEMM), [E][3E] (SIMT), [3E]
     float *w_o = nullptr, *wt_o = nullptr, *b_o = nullptr;        // [E][E], [E][E] transposed, [E]
+};
+
+struct wb_ffn_layer {
+    wb_context *ctx = nullptr;
+    int device = 0;  // destroy must not touch ctx
+    int E = 0, M = 0, nb = 0, steps = 0, corr = 0, groups = 1;
+    float alpha = 0.0f, beta = 0.0f;
+    float *mi_sq_w = nullptr, *mi_sq_b = nullptr, *mi_pr_w = nullptr, *mi_pr_b = nullptr;
+    float *mo_sq_w = nullptr, *mo_sq_b = nullptr, *mo_pr_w = nullptr, *mo_pr_b = nullptr;
+    float *gamma_raw = nullptr, *omega = nullptr, *phase_corr = nullptr, *rk4w = nullptr;
+    float *out_w = nullptr, *out_b = nullptr;
+    __nv_bfloat16 *out_hi = nullptr, *out_lo = nullptr;  // dense out_w as a bf16 split (tensor path)
+};
+
+struct wb_agc {
+    wb_context *ctx = nullptr;
+    int device = 0;
+    wb::AgcDev *dev = nullptr;
 };
 
 struct wb_kv_cache {
@@ -1376,6 +1395,345 @@ int wb_test_gemm_bf16(wb_context *ctx, const uint16_t *A, const uint16_t *B, con
     int rc = wb::tc_gemm_bf16((const __nv_bfloat16 *)A, (const __nv_bfloat16 *)B, bias, C, M, N, K, ctx->dev_err,
                               ctx->stream, &msg);
     return rc == WB_OK ? rc : fail(rc, msg);
+}
+
+// ---------------------------------------------------------------------------
+// the serve-tier layer around the attention
+// ---------------------------------------------------------------------------
+static int dev_copy(float **dst, const float *src, size_t n) {
+    *dst = nullptr;
+    if (!src || n == 0) return WB_OK;
+    if (cudaMalloc(dst, n * sizeof(float)) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(WB_ENOMEM, "cudaMalloc failed for FFN weights");
+    }
+    if (cudaMemcpy(*dst, src, n * sizeof(float), cudaMemcpyDefault) != cudaSuccess)
+        return fail(WB_ECUDA, "weight upload failed");
+    return WB_OK;
+}
+
+int wb_ffn_layer_destroy(wb_ffn_layer *f) {
+    if (!f) return WB_OK;
+    DeviceGuard g(f->device);
+    for (float *p : {f->mi_sq_w, f->mi_sq_b, f->mi_pr_w, f->mi_pr_b, f->mo_sq_w, f->mo_sq_b, f->mo_pr_w, f->mo_pr_b,
+                     f->gamma_raw, f->omega, f->phase_corr, f->rk4w, f->out_w, f->out_b})
+        if (p) cudaFree(p);
+    if (f->out_hi) cudaFree(f->out_hi);
+    delete f;
+    return WB_OK;
+}
+
+int wb_ffn_layer_create(wb_context *ctx, const wb_ffn_weights_desc *w, wb_ffn_layer **out) {
+    if (!ctx || !w || !out) return fail(WB_EINVAL, "NULL argument");
+    *out = nullptr;
+    const int E = w->n_embd, M = w->maestro_dim, G = w->out_groups;
+    if (E <= 0 || E % 2 || M <= 0 || w->rk4_steps <= 0 || G <= 0 || E % G)
+        return fail(WB_EINVAL, "bad FFN dimensions (n_embd even, maestro_dim > 0, rk4_steps > 0, groups divide n_embd)");
+    if (E / 2 > 4096) return fail(WB_ENOTSUP, "the ODE kernel supports up to 4096 bands");
+    if ((size_t)8 * (E + M) * sizeof(float) > 200 * 1024) return fail(WB_ENOTSUP, "n_embd too large for the maestro kernel");
+    if (!w->mi_squeeze_w || !w->mi_squeeze_b || !w->mi_process_w || !w->mi_process_b || !w->mo_squeeze_w ||
+        !w->mo_squeeze_b || !w->mo_process_w || !w->mo_process_b || !w->gamma_raw || !w->omega ||
+        !w->phase_correction || !w->rk4_weights || !w->out_w || (G == 1 && !w->out_b))
+        return fail(WB_EINVAL, "missing FFN weight array");
+    DeviceGuard g(ctx->device);
+    wb_ffn_layer *f = new wb_ffn_layer();
+    f->ctx = ctx;
+    f->device = ctx->device;
+    f->E = E; f->M = M; f->nb = E / 2; f->steps = w->rk4_steps; f->corr = w->use_corrector != 0; f->groups = G;
+    f->alpha = w->alpha; f->beta = w->beta;
+    const size_t me = (size_t)M * E, gs = E / G;
+    int rc = WB_OK;
+    auto up = [&](float **d, const float *src, size_t n) { if (rc == WB_OK) rc = dev_copy(d, src, n); };
+    up(&f->mi_sq_w, w->mi_squeeze_w, me); up(&f->mi_sq_b, w->mi_squeeze_b, M);
+    up(&f->mi_pr_w, w->mi_process_w, me); up(&f->mi_pr_b, w->mi_process_b, E);
+    up(&f->mo_sq_w, w->mo_squeeze_w, me); up(&f->mo_sq_b, w->mo_squeeze_b, M);
+    up(&f->mo_pr_w, w->mo_process_w, me); up(&f->mo_pr_b, w->mo_process_b, E);
+    up(&f->gamma_raw, w->gamma_raw, E / 2); up(&f->omega, w->omega, E / 2);
+    up(&f->phase_corr, w->phase_correction, E / 2); up(&f->rk4w, w->rk4_weights, 4);
+    if (G == 1) {
+        up(&f->out_w, w->out_w, (size_t)E * E);
+        up(&f->out_b, w->out_b, E);
+        if (rc == WB_OK && E % 8 == 0) {
+            if (cudaMalloc(&f->out_hi, (size_t)2 * E * E * sizeof(__nv_bfloat16)) != cudaSuccess) {
+                cudaGetLastError();
+                rc = fail(WB_ENOMEM, "cudaMalloc failed for FFN weights");
+            } else {
+                f->out_lo = f->out_hi + (size_t)E * E;
+                if (wb::split_bf16(f->out_w, (long long)E * E, f->out_hi, f->out_lo, 0) != WB_OK ||
+                    cudaDeviceSynchronize() != cudaSuccess)
+                    rc = fail(WB_ECUDA, "out_proj split failed");
+            }
+        }
+    } else {
+        up(&f->out_w, w->out_w, (size_t)G * (gs * gs + gs));
+    }
+    if (rc != WB_OK) {
+        wb_ffn_layer_destroy(f);
+        return rc;
+    }
+    *out = f;
+    return WB_OK;
+}
+
+int wb_agc_create(wb_context *ctx, float alpha, float beta, wb_agc **out) {
+    if (!ctx || !out) return fail(WB_EINVAL, "NULL argument");
+    *out = nullptr;
+    // agc.rs from_coupling -> with_ceiling
+    float ceiling = std::sqrt(1.57079637050628662109f / (alpha + 4.0f * beta));
+    ceiling = std::max(ceiling, 0.5f);
+    wb::AgcDev h{};
+    h.ema_mean = 1.0f;
+    h.ema_var = 0.5f;
+    h.headroom = 3.0f;
+    h.decay = 0.995f;
+    h.min_threshold = std::max(ceiling * 0.3f, 0.5f);
+    h.max_threshold = ceiling;
+    h.threshold = std::max(ceiling * 0.75f, 0.5f);
+    h.count = 0;
+    DeviceGuard g(ctx->device);
+    wb_agc *a = new wb_agc();
+    a->ctx = ctx;
+    a->device = ctx->device;
+    if (cudaMalloc(&a->dev, sizeof(wb::AgcDev)) != cudaSuccess ||
+        cudaMemcpy(a->dev, &h, sizeof(h), cudaMemcpyHostToDevice) != cudaSuccess) {
+        cudaGetLastError();
+        if (a->dev) cudaFree(a->dev);
+        delete a;
+        return fail(WB_ENOMEM, "AGC state allocation failed");
+    }
+    *out = a;
+    return WB_OK;
+}
+
+int wb_agc_destroy(wb_agc *a) {
+    if (!a) return WB_OK;
+    DeviceGuard g(a->device);
+    if (a->dev) cudaFree(a->dev);
+    delete a;
+    return WB_OK;
+}
+
+int wb_agc_read(wb_agc *a, float *state) {
+    if (!a || !state) return fail(WB_EINVAL, "NULL argument");
+    DeviceGuard g(a->device);
+    wb::AgcDev h{};
+    WB_CUDA(cudaStreamSynchronize(a->ctx->stream));
+    WB_CUDA(cudaMemcpy(&h, a->dev, sizeof(h), cudaMemcpyDeviceToHost));
+    const float v[8] = {h.ema_mean, h.ema_var, h.headroom, h.decay, h.min_threshold, h.max_threshold, h.threshold,
+                        (float)h.count};
+    memcpy(state, v, sizeof(v));
+    return WB_OK;
+}
+
+int wb_ffn_forward(wb_context *ctx, const wb_ffn_layer *f, wb_agc *agc, const float *x, int n_rows, int rows_per_call,
+                   int flags, float *y) {
+    if (!ctx || !f || !agc || !x || !y) return fail(WB_EINVAL, "NULL argument");
+    if (f->ctx != ctx || agc->ctx != ctx) return fail(WB_EINVAL, "objects belong to another context");
+    if (flags & ~WB_PATH_EXACT) return fail(WB_EINVAL, "unknown flag bits");
+    if (n_rows < 0) return fail(WB_EINVAL, "negative n_rows");
+    if (n_rows == 0) return WB_OK;
+    if (rows_per_call <= 0 || n_rows % rows_per_call) return fail(WB_EINVAL, "rows_per_call must divide n_rows");
+    const int n_seg = n_rows / rows_per_call;
+    if (n_seg > 65535) return fail(WB_EINVAL, "more than 65535 calls in one batch");
+    DeviceGuard g(ctx->device);
+    ProfBind pb(ctx);
+    cudaStream_t st = ctx->stream;
+    const long long R = n_rows;
+    const int E = f->E;
+    const bool x_dev = is_device_ptr(x), y_dev = is_device_ptr(y);
+    Carve io;
+    size_t o_x = x_dev ? 0 : io.take<float>(R * E);
+    size_t o_y = y_dev ? 0 : io.take<float>(R * E);
+    if (io.off) WB_TRY(ensure(ctx->io, io.off));
+    char *iob = (char *)ctx->io.p;
+    const float *xd = x_dev ? x : (const float *)(iob + o_x);
+    float *yd = y_dev ? y : (float *)(iob + o_y);
+    if (!x_dev) WB_CUDA(cudaMemcpyAsync((void *)xd, x, R * E * sizeof(float), cudaMemcpyHostToDevice, st));
+    const bool bf3 = !(flags & WB_PATH_EXACT) && f->out_hi;  // out_proj as a bf16x3 tensor-core product
+    Carve cv;
+    const size_t o_pre = cv.take<float>(R * E), o_ko = cv.take<float>(R * E), o_reg = cv.take<float>(R * E);
+    const size_t o_agc = cv.take<float>(wb::agc_scratch_floats(n_seg, (long long)rows_per_call * f->nb));
+    const size_t o_split = bf3 ? cv.take<__nv_bfloat16>(2 * R * E) : 0;
+    WB_TRY(ensure(ctx->ws, cv.off));
+    char *w = (char *)ctx->ws.p;
+    float *pre = (float *)(w + o_pre), *ko = (float *)(w + o_ko), *reg = (float *)(w + o_reg);
+    int rc;
+    // 1-2. maestro_in and precond = x + maestro_in(x) (ffn.rs:61-66)
+    wb::MaestroArgs mi{xd, nullptr, f->mi_sq_w, f->mi_sq_b, f->mi_pr_w, f->mi_pr_b, R, E, f->M, pre};
+    if ((rc = wb::launch_maestro(mi, st))) return fail(rc, "maestro_in launch failed");
+    // AGC (ffn.rs:69-79), one observation per reference call
+    float *thr = nullptr;
+    if ((rc = wb::launch_agc_observe(pre, n_seg, (long long)rows_per_call * f->nb, agc->dev, (float *)(w + o_agc),
+                                     &thr, st)))
+        return fail(rc, "AGC launch failed");
+    // 3. the frozen ODE (fft_ode.rs:171-250) and the corrector plate
+    int fft_len = 0;
+    if (f->nb >= 256) {
+        fft_len = 1;
+        while (fft_len < f->nb) fft_len <<= 1;
+    }
+    wb::OdeArgs oa{pre, thr, rows_per_call, f->gamma_raw, f->omega, f->rk4w, f->corr ? f->phase_corr : nullptr,
+                   f->alpha, f->beta, f->nb, f->steps, fft_len, ko};
+    if ((rc = wb::launch_kerr_ode(oa, R, st))) return fail(rc, "Kerr ODE launch failed");
+    // 4-5. maestro_out and regulated = kerr_out + maestro_out(kerr_out)
+    wb::MaestroArgs mo{ko, nullptr, f->mo_sq_w, f->mo_sq_b, f->mo_pr_w, f->mo_pr_b, R, E, f->M, reg};
+    if ((rc = wb::launch_maestro(mo, st))) return fail(rc, "maestro_out launch failed");
+    // 6. out_proj
+    if (!bf3) {
+        if ((rc = wb::launch_out_proj_exact(reg, R, E, f->groups, f->out_w, f->out_b, yd, st)))
+            return fail(rc, "out_proj launch failed");
+    } else {
+        std::string msg;
+        __nv_bfloat16 *a_hi = (__nv_bfloat16 *)(w + o_split), *a_lo = a_hi + R * E;
+        if ((rc = wb::split_bf16(reg, R * E, a_hi, a_lo, st))) return fail(rc, "split launch failed");
+        if ((rc = wb::tc_gemm_bf16x3(a_hi, a_lo, f->out_hi, f->out_lo, f->out_b, yd, (int)R, E, E, ctx->dev_err, st,
+                                     &msg)))
+            return fail(rc, msg);
+    }
+    if (!y_dev) {
+        WB_CUDA(cudaMemcpyAsync(y, yd, R * E * sizeof(float), cudaMemcpyDeviceToHost, st));
+        WB_CUDA(cudaStreamSynchronize(st));
+    }
+    return WB_OK;
+}
+
+int wb_layer_norm(wb_context *ctx, const float *x, int n_rows, int n, const float *weight, const float *bias,
+                  float *y) {
+    if (!ctx || !x || !weight || !bias || !y) return fail(WB_EINVAL, "NULL argument");
+    if (n_rows < 0 || n <= 0) return fail(WB_EINVAL, "bad shape");
+    if (n_rows == 0) return WB_OK;
+    DeviceGuard g(ctx->device);
+    ProfBind pb(ctx);
+    cudaStream_t st = ctx->stream;
+    const long long R = n_rows;
+    const bool x_dev = is_device_ptr(x), y_dev = is_device_ptr(y), w_dev = is_device_ptr(weight),
+               b_dev = is_device_ptr(bias);
+    Carve io;
+    size_t o_x = x_dev ? 0 : io.take<float>(R * n), o_y = y_dev ? 0 : io.take<float>(R * n);
+    size_t o_w = w_dev ? 0 : io.take<float>(n), o_b = b_dev ? 0 : io.take<float>(n);
+    if (io.off) WB_TRY(ensure(ctx->io, io.off));
+    char *iob = (char *)ctx->io.p;
+    const float *xd = x_dev ? x : (const float *)(iob + o_x);
+    const float *wd = w_dev ? weight : (const float *)(iob + o_w), *bd = b_dev ? bias : (const float *)(iob + o_b);
+    float *yd = y_dev ? y : (float *)(iob + o_y);
+    if (!x_dev) WB_CUDA(cudaMemcpyAsync((void *)xd, x, R * n * sizeof(float), cudaMemcpyHostToDevice, st));
+    if (!w_dev) WB_CUDA(cudaMemcpyAsync((void *)wd, weight, n * sizeof(float), cudaMemcpyHostToDevice, st));
+    if (!b_dev) WB_CUDA(cudaMemcpyAsync((void *)bd, bias, n * sizeof(float), cudaMemcpyHostToDevice, st));
+    if (wb::launch_layer_norm(xd, n_rows, n, wd, bd, yd, st)) return fail(WB_ECUDA, "layer_norm launch failed");
+    if (!y_dev) {
+        WB_CUDA(cudaMemcpyAsync(y, yd, R * n * sizeof(float), cudaMemcpyDeviceToHost, st));
+        WB_CUDA(cudaStreamSynchronize(st));
+    }
+    return WB_OK;
+}
+
+int wb_residual_add(wb_context *ctx, float *hidden, const float *a, const float *b, long long n) {
+    if (!ctx || !hidden || !a || !b) return fail(WB_EINVAL, "NULL argument");
+    if (n < 0) return fail(WB_EINVAL, "negative n");
+    if (!is_device_ptr(hidden) || !is_device_ptr(a) || !is_device_ptr(b))
+        return fail(WB_EINVAL, "wb_residual_add takes device pointers");
+    DeviceGuard g(ctx->device);
+    if (wb::launch_residual(hidden, a, b, n, ctx->stream)) return fail(WB_ECUDA, "residual launch failed");
+    return WB_OK;
+}
+
+int wb_embed(wb_context *ctx, const int32_t *tokens, const int32_t *wpe_index, int n_rows, const float *wte,
+             int vocab, const float *wpe, int n_pos, int n_embd, float *hidden) {
+    if (!ctx || !tokens || !wpe_index || !wte || !hidden) return fail(WB_EINVAL, "NULL argument");
+    if (n_rows < 0 || vocab <= 0 || n_embd <= 0 || n_pos < 0) return fail(WB_EINVAL, "bad shape");
+    if (n_rows == 0) return WB_OK;
+    if (!is_device_ptr(wte) || (wpe && !is_device_ptr(wpe)))
+        return fail(WB_EINVAL, "wte / wpe must be device pointers");
+    DeviceGuard g(ctx->device);
+    cudaStream_t st = ctx->stream;
+    const bool t_dev = is_device_ptr(tokens), i_dev = is_device_ptr(wpe_index), h_dev = is_device_ptr(hidden);
+    const long long R = n_rows;
+    Carve io;
+    size_t o_t = t_dev ? 0 : io.take<int32_t>(R), o_i = i_dev ? 0 : io.take<int32_t>(R);
+    size_t o_h = h_dev ? 0 : io.take<float>(R * n_embd);
+    if (io.off) WB_TRY(ensure(ctx->io, io.off));
+    char *iob = (char *)ctx->io.p;
+    const int32_t *td = t_dev ? tokens : (const int32_t *)(iob + o_t);
+    const int32_t *id = i_dev ? wpe_index : (const int32_t *)(iob + o_i);
+    float *hd = h_dev ? hidden : (float *)(iob + o_h);
+    if (!t_dev) WB_CUDA(cudaMemcpyAsync((void *)td, tokens, R * sizeof(int32_t), cudaMemcpyHostToDevice, st));
+    if (!i_dev) WB_CUDA(cudaMemcpyAsync((void *)id, wpe_index, R * sizeof(int32_t), cudaMemcpyHostToDevice, st));
+    if (wb::launch_embed(td, id, n_rows, n_embd, wte, vocab, wpe, wpe ? n_pos : 0, hd, ctx->dev_err, st))
+        return fail(WB_ECUDA, "embedding launch failed");
+    if (!h_dev) {
+        WB_CUDA(cudaMemcpyAsync(hidden, hd, R * n_embd * sizeof(float), cudaMemcpyDeviceToHost, st));
+        WB_CUDA(cudaStreamSynchronize(st));
+    }
+    return WB_OK;
+}
+
+// logits of rows of hidden (optionally rotated band by band first) against a
+// device vocabulary table [vocab][n_embd]
+static int vocab_logits(wb_context *ctx, const float *hidden, int n_rows, int n_embd, const float *corrector,
+                        const float *table, int vocab, int flags, float *logits) {
+    if (!ctx || !hidden || !table || !logits) return fail(WB_EINVAL, "NULL argument");
+    if (flags & ~WB_PATH_EXACT) return fail(WB_EINVAL, "unknown flag bits");
+    if (n_rows < 0 || n_embd <= 0 || n_embd % 2 || vocab <= 0) return fail(WB_EINVAL, "bad shape");
+    if (n_rows == 0) return WB_OK;
+    if (!is_device_ptr(table) || (corrector && !is_device_ptr(corrector)))
+        return fail(WB_EINVAL, "the vocabulary table and corrector must be device pointers");
+    DeviceGuard g(ctx->device);
+    ProfBind pb(ctx);
+    cudaStream_t st = ctx->stream;
+    const long long R = n_rows;
+    const bool h_dev = is_device_ptr(hidden), l_dev = is_device_ptr(logits);
+    Carve io;
+    size_t o_h = h_dev ? 0 : io.take<float>(R * n_embd), o_l = l_dev ? 0 : io.take<float>(R * vocab);
+    if (io.off) WB_TRY(ensure(ctx->io, io.off));
+    char *iob = (char *)ctx->io.p;
+    const float *hd = h_dev ? hidden : (const float *)(iob + o_h);
+    float *ld = l_dev ? logits : (float *)(iob + o_l);
+    if (!h_dev) WB_CUDA(cudaMemcpyAsync((void *)hd, hidden, R * n_embd * sizeof(float), cudaMemcpyHostToDevice, st));
+    const bool bf3 = !(flags & WB_PATH_EXACT) && n_embd % 8 == 0;  // bf16x3 tensor-core product
+    Carve cv;
+    const size_t o_rot = corrector ? cv.take<float>(R * n_embd) : 0;
+    const size_t o_a = bf3 ? cv.take<__nv_bfloat16>(2 * R * n_embd) : 0;
+    const size_t o_t = bf3 ? cv.take<__nv_bfloat16>(2 * (size_t)vocab * n_embd) : 0;
+    if (cv.off) WB_TRY(ensure(ctx->ws, cv.off));
+    char *w = (char *)ctx->ws.p;
+    const float *src = hd;
+    if (corrector) {
+        float *rot = (float *)(w + o_rot);
+        if (wb::launch_rotate_bands(hd, R, n_embd / 2, corrector, rot, st))
+            return fail(WB_ECUDA, "rotation launch failed");
+        src = rot;
+    }
+    int rc;
+    if (!bf3) {
+        rc = wb::launch_vocab_dot(src, n_rows, n_embd, table, vocab, ld, st);
+        if (rc) return fail(rc, "vocabulary dot launch failed");
+    } else {
+        std::string msg;
+        __nv_bfloat16 *a_hi = (__nv_bfloat16 *)(w + o_a), *a_lo = a_hi + R * n_embd;
+        __nv_bfloat16 *t_hi = (__nv_bfloat16 *)(w + o_t), *t_lo = t_hi + (size_t)vocab * n_embd;
+        if ((rc = wb::split_bf16(src, R * n_embd, a_hi, a_lo, st)) ||
+            (rc = wb::split_bf16(table, (long long)vocab * n_embd, t_hi, t_lo, st)))
+            return fail(rc, "split launch failed");
+        if ((rc = wb::tc_gemm_bf16x3(a_hi, a_lo, t_hi, t_lo, nullptr, ld, n_rows, vocab, n_embd, ctx->dev_err, st,
+                                     &msg)))
+            return fail(rc, msg);
+    }
+    if (!l_dev) {
+        WB_CUDA(cudaMemcpyAsync(logits, ld, R * vocab * sizeof(float), cudaMemcpyDeviceToHost, st));
+        WB_CUDA(cudaStreamSynchronize(st));
+    }
+    return WB_OK;
+}
+
+int wb_phase_native_decode(wb_context *ctx, const float *hidden, int n_rows, int n_embd, const float *corrector,
+                           const float *wte, int vocab, int flags, float *logits) {
+    if (!corrector) return fail(WB_EINVAL, "NULL corrector");
+    return vocab_logits(ctx, hidden, n_rows, n_embd, corrector, wte, vocab, flags, logits);
+}
+
+int wb_lm_head(wb_context *ctx, const float *hidden, int n_rows, int n_embd, const float *lm_head, int vocab,
+               int flags, float *logits) {
+    return vocab_logits(ctx, hidden, n_rows, n_embd, nullptr, lm_head, vocab, flags, logits);
 }
 
 int wb_test_dot_core(wb_context *ctx, const float *qkv, int B, int T, int E, int H, int mode, float *o) {

@@ -1,0 +1,561 @@
+// wb_serve.cu -- the serve-tier layer around the attention on the GPU
+// (src/common/kv_cache.rs prefill :93-236 and forward_one :241-381): token
+// embedding, LayerNorm (model.rs:154), the dual-maestro Kerr-ODE FFN as the
+// serve tier runs it (ffn.rs:39-230 with a frozen ODE, no memory and the
+// stencil ODE of fft_ode.rs:171-250), its adaptive gain control (agc.rs), the
+// parallel residual, and the decoders (phase_native_decode kv_cache.rs:18-33,
+// lm_head :365-378).
+//
+// These are row-wise and small next to the attention: maestro_dim is 16 at
+// the 768-dim scale, the ODE is 16 RK4 steps over n_bands coupled only to
+// their 4 neighbours.  The kernels keep the reference's arithmetic order --
+// sequential sums, products rounded before the add (__fmul_rn / __fadd_rn,
+// no contraction) -- so the all-fp32 path differs from the reference only by
+// the last bits of tanhf / sinf / cosf / expf / logf and by the order of the
+// LayerNorm and AGC reductions.  The large products (the FFN's out_proj and
+// the decoders' vocabulary GEMMs) run as bf16x3 products on the tcgen05 GEMM
+// (wb_tc.cu) unless the caller asks for WB_PATH_EXACT.
+#include "wave_b200.h"
+#include "wb_internal.h"
+#include "wb_serve.h"
+
+#include <algorithm>
+#include <cmath>
+
+namespace wb {
+
+#define FM __fmul_rn
+#define FA __fadd_rn
+
+// ---------------------------------------------------------------------------
+// LayerNorm: one warp per row, the row staged in shared memory by one batch
+// of loads, lane-strided partial sums combined by a fixed shuffle tree (mean,
+// then the variance about it), y = (x - mean) / sd * w + b.
+// ---------------------------------------------------------------------------
+__global__ void layer_norm_kernel(const float *__restrict__ x, int rows, int n, const float *__restrict__ w,
+                                  const float *__restrict__ b, float *__restrict__ y) {
+    extern __shared__ float lrow[];  // [warps][n]: the row staged by one batch of loads
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const long long row = (long long)blockIdx.x * (blockDim.x >> 5) + warp;
+    if (row >= rows) return;
+    const float *xr = x + row * n;
+    float *sr = lrow + (long long)warp * n;
+    if ((n & 3) == 0 && (reinterpret_cast<uintptr_t>(xr) & 15) == 0) {
+        for (int i = lane; i < n / 4; i += 32) reinterpret_cast<float4 *>(sr)[i] = __ldg(reinterpret_cast<const float4 *>(xr) + i);
+    } else {
+        for (int i = lane; i < n; i += 32) sr[i] = __ldg(xr + i);
+    }
+    __syncwarp();
+    float s = 0.0f;
+    for (int i = lane; i < n; i += 32) s = FA(s, sr[i]);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) s = FA(s, __shfl_xor_sync(0xffffffffu, s, o));
+    const float mean = __fdiv_rn(s, (float)n);
+    float v = 0.0f;
+    for (int i = lane; i < n; i += 32) {
+        const float d = __fsub_rn(sr[i], mean);
+        v = FA(v, FM(d, d));
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v = FA(v, __shfl_xor_sync(0xffffffffu, v, o));
+    const float sd = __fsqrt_rn(FA(__fdiv_rn(v, (float)n), 1e-5f));
+    float *yr = y + row * n;
+    for (int i = lane; i < n; i += 32) yr[i] = FA(FM(__fdiv_rn(__fsub_rn(sr[i], mean), sd), __ldg(w + i)), __ldg(b + i));
+}
+
+int launch_layer_norm(const float *x, int rows, int n, const float *w, const float *b, float *y, cudaStream_t st) {
+    if (rows <= 0) return WB_OK;
+    int warps = 8;
+    while (warps > 1 && (size_t)warps * n * sizeof(float) > 96 * 1024) warps >>= 1;
+    const size_t smem = (size_t)warps * n * sizeof(float);
+    if (smem > 200 * 1024) return WB_ENOTSUP;
+    ProfScope ps("layer_norm", st);
+    cudaFuncSetAttribute(layer_norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    layer_norm_kernel<<<(rows + warps - 1) / warps, warps * 32, smem, st>>>(x, rows, n, w, b, y);
+    return cudaGetLastError() == cudaSuccess ? WB_OK : WB_ECUDA;
+}
+
+// ---------------------------------------------------------------------------
+// Maestro (compute.rs:356-360 / ffn.rs:61-66, :185-191): y = base + process_1
+// . gelu(squeeze . x), squeeze [M][E] and process_1 [E][M] with biases; each
+// output one sequential sum, then bias + sum (compute.rs:441-452).  A CTA
+// takes up to 32 rows staged in shared memory, with both weight matrices
+// when they fit.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float gelu_ref(float v) {
+    // compute.rs:113-119: 0.5 v (1 + tanh(c (v + 0.044715 v^3)))
+    const float c = 0.7978845608f;
+    const float inner = FM(c, FA(v, FM(FM(FM(0.044715f, v), v), v)));
+    return FM(FM(0.5f, v), FA(1.0f, tanhf(inner)));
+}
+
+// rows per CTA and whether both weight matrices are staged in shared memory
+// (squeeze rows padded to E + 1 floats, process_1 rows to M + 1: the
+// threads of a warp read different rows at the same column without bank
+// conflicts)
+struct MaestroPlan {
+    int rows;
+    bool staged;
+    size_t smem;
+};
+
+static MaestroPlan maestro_plan(int E, int M) {
+    const size_t w = (size_t)M * (E + 1) + (size_t)E * (M + 1);
+    for (int r : {32, 16, 8}) {
+        const size_t smem = sizeof(float) * (w + (size_t)r * E + (size_t)r * M);
+        if (smem <= 200 * 1024) return {r, true, smem};
+    }
+    return {8, false, sizeof(float) * ((size_t)8 * E + 8 * M)};
+}
+
+__global__ void __launch_bounds__(256) maestro_kernel(MaestroArgs a, int mrows, int staged) {
+    extern __shared__ float msm[];
+    const int E = a.E, M = a.M;
+    float *xs = msm;                         // [mrows][E]
+    float *act = xs + (size_t)mrows * E;     // [mrows][M]
+    float *wsq = act + (size_t)mrows * M;    // [M][E + 1]   (staged)
+    float *wpr = wsq + (size_t)M * (E + 1);  // [E][M + 1]   (staged)
+    const long long r0 = (long long)blockIdx.x * mrows;
+    const int nr = (int)min((long long)mrows, a.rows - r0);
+    for (int e = threadIdx.x; e < nr * E; e += blockDim.x) xs[e] = a.x[r0 * E + e];
+    if (staged) {
+        for (int e = threadIdx.x; e < M * E; e += blockDim.x) {
+            const int m = e / E, j = e - m * E;
+            wsq[m * (E + 1) + j] = __ldg(a.sq_w + e);
+        }
+        for (int e = threadIdx.x; e < E * M; e += blockDim.x) {
+            const int i = e / M, m = e - i * M;
+            wpr[i * (M + 1) + m] = __ldg(a.pr_w + e);
+        }
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < nr * M; e += blockDim.x) {
+        const int r = e / M, m = e - r * M;
+        const float *xr = xs + r * E;
+        float s = 0.0f;
+        if (staged) {
+            const float *wr = wsq + m * (E + 1);
+            for (int j = 0; j < E; j++) s = FA(s, FM(wr[j], xr[j]));
+        } else {
+            const float *wr = a.sq_w + (long long)m * E;
+            for (int j = 0; j < E; j++) s = FA(s, FM(__ldg(wr + j), xr[j]));
+        }
+        act[r * M + m] = gelu_ref(FA(__ldg(a.sq_b + m), s));
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < nr * E; e += blockDim.x) {
+        const int r = e / E, i = e - r * E;
+        float s = 0.0f;
+        if (staged) {
+            const float *wr = wpr + i * (M + 1);
+            for (int m = 0; m < M; m++) s = FA(s, FM(wr[m], act[r * M + m]));
+        } else {
+            const float *wr = a.pr_w + (long long)i * M;
+            for (int m = 0; m < M; m++) s = FA(s, FM(__ldg(wr + m), act[r * M + m]));
+        }
+        const float out = FA(__ldg(a.pr_b + i), s);
+        const float base = a.base ? a.base[(r0 + r) * E + i] : xs[r * E + i];
+        a.y[(r0 + r) * E + i] = FA(base, out);
+    }
+}
+
+int launch_maestro(const MaestroArgs &a, cudaStream_t st) {
+    if (a.rows <= 0) return WB_OK;
+    const MaestroPlan p = maestro_plan(a.E, a.M);
+    if (p.smem > 200 * 1024) return WB_ENOTSUP;
+    ProfScope ps("maestro", st);
+    cudaFuncSetAttribute(maestro_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem);
+    maestro_kernel<<<(unsigned)((a.rows + p.rows - 1) / p.rows), 256, p.smem, st>>>(a, p.rows, p.staged ? 1 : 0);
+    return cudaGetLastError() == cudaSuccess ? WB_OK : WB_ECUDA;
+}
+
+// ---------------------------------------------------------------------------
+// AGC (agc.rs:134-213).  A call's rows form n_seg consecutive segments, each
+// one reference FFN call (one request's rows): per segment the statistics of
+// the band magnitudes that pass the 2 x ceiling filter, then one thread
+// applies the segments' EMA updates in order and records each segment's
+// threshold, which the ODE kernel uses for the knee compression of that
+// segment's rows.  Partial sums per block of a fixed grid, reduced in block
+// order (deterministic).
+// ---------------------------------------------------------------------------
+static constexpr int AGC_THREADS = 256, AGC_MAXB = 148;
+
+__device__ __forceinline__ float band_mag(const float *p) { return __fsqrt_rn(FA(FM(p[0], p[0]), FM(p[1], p[1]))); }
+
+// partial layout per segment: [0, B) sums, [B, 2B) counts, [2B, 3B) sums of
+// squared deviations, [3B] mean, [3B + 1] count, [3B + 2] variance (B =
+// blocks per segment).
+template <int PASS>
+__global__ void __launch_bounds__(AGC_THREADS) agc_partial_kernel(const float *__restrict__ pre, long long seg_mags,
+                                                                  const AgcDev *agc, float *partial) {
+    __shared__ float ss[AGC_THREADS], sc[AGC_THREADS];
+    const int B = gridDim.x, seg = blockIdx.y;
+    float *ps = partial + (long long)seg * (3 * B + 3);
+    const float *p = pre + (long long)seg * seg_mags * 2;
+    const float ceil2 = FM(agc->max_threshold, 2.0f);
+    const float mean = PASS == 1 ? ps[3 * B] : 0.0f;
+    float s = 0.0f, c = 0.0f;
+    for (long long i = blockIdx.x * (long long)AGC_THREADS + threadIdx.x; i < seg_mags;
+         i += (long long)B * AGC_THREADS) {
+        const float m = band_mag(p + 2 * i);
+        if (isfinite(m) && m < ceil2) {
+            if (PASS == 0) {
+                s = FA(s, m);
+                c = FA(c, 1.0f);
+            } else {
+                const float d = __fsub_rn(m, mean);
+                s = FA(s, FM(d, d));
+            }
+        }
+    }
+    ss[threadIdx.x] = s;
+    sc[threadIdx.x] = c;
+    __syncthreads();
+    for (int h = AGC_THREADS / 2; h; h >>= 1) {
+        if (threadIdx.x < h) {
+            ss[threadIdx.x] = FA(ss[threadIdx.x], ss[threadIdx.x + h]);
+            sc[threadIdx.x] = FA(sc[threadIdx.x], sc[threadIdx.x + h]);
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        if (PASS == 0) {
+            ps[blockIdx.x] = ss[0];
+            ps[B + blockIdx.x] = sc[0];
+        } else {
+            ps[2 * B + blockIdx.x] = ss[0];
+        }
+    }
+}
+
+// one warp per segment: the fixed-order sum of its B block partials (PASS 0:
+// sums and counts -> mean and count; PASS 1: squared deviations -> var)
+template <int PASS>
+__global__ void agc_reduce_kernel(float *partial, int n_seg, int B) {
+    const int lane = threadIdx.x & 31;
+    const int seg = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (seg >= n_seg) return;
+    float *ps = partial + (long long)seg * (3 * B + 3);
+    float s = 0.0f, c = 0.0f;
+    for (int i = lane; i < B; i += 32) {
+        if (PASS == 0) {
+            s = FA(s, ps[i]);
+            c = FA(c, ps[B + i]);
+        } else {
+            s = FA(s, ps[2 * B + i]);
+        }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        s = FA(s, __shfl_xor_sync(0xffffffffu, s, o));
+        c = FA(c, __shfl_xor_sync(0xffffffffu, c, o));
+    }
+    if (lane == 0) {
+        if (PASS == 0) {
+            ps[3 * B + 1] = c;
+            ps[3 * B] = c > 0.0f ? __fdiv_rn(s, c) : 0.0f;
+        } else {
+            ps[3 * B + 2] = ps[3 * B + 1] > 0.0f ? __fdiv_rn(s, ps[3 * B + 1]) : 0.0f;
+        }
+    }
+}
+
+// one thread: the segments' observations in order (agc.rs observe), each
+// segment's threshold recorded for its compression
+__global__ void agc_update_kernel(const float *partial, int n_seg, int B, AgcDev *agc, float *thresholds) {
+    if (threadIdx.x || blockIdx.x) return;
+    for (int seg = 0; seg < n_seg; seg++) {
+        const float *ps = partial + (long long)seg * (3 * B + 3);
+        const float c = ps[3 * B + 1];
+        if (c > 0.0f) {  // no clean magnitude: the state stays
+            const float mean = ps[3 * B], var = ps[3 * B + 2];
+            if (isfinite(mean) && isfinite(var)) {
+                agc->count += 1;
+                if (agc->count < 10) {
+                    agc->ema_mean = mean;
+                    agc->ema_var = var;
+                } else {
+                    agc->ema_mean = FA(FM(agc->decay, agc->ema_mean), FM(__fsub_rn(1.0f, agc->decay), mean));
+                    agc->ema_var = FA(FM(agc->decay, agc->ema_var), FM(__fsub_rn(1.0f, agc->decay), var));
+                }
+                const float sd = fmaxf(__fsqrt_rn(agc->ema_var), 0.01f);
+                agc->threshold =
+                    fminf(fmaxf(FA(agc->ema_mean, FM(agc->headroom, sd)), agc->min_threshold), agc->max_threshold);
+            }
+        }
+        thresholds[seg] = agc->threshold;
+    }
+}
+
+static int agc_blocks(long long seg_mags) {
+    return (int)std::max(1LL, std::min((long long)AGC_MAXB, (seg_mags + 8LL * AGC_THREADS - 1) / (8LL * AGC_THREADS)));
+}
+
+size_t agc_scratch_floats(int n_seg, long long seg_mags) {
+    return (size_t)n_seg * (3 * agc_blocks(seg_mags) + 3) + (size_t)n_seg;
+}
+
+int launch_agc_observe(const float *pre, int n_seg, long long seg_mags, AgcDev *agc, float *scratch,
+                       float **thresholds, cudaStream_t st) {
+    const int B = agc_blocks(seg_mags);
+    float *partial = scratch;
+    *thresholds = scratch + (size_t)n_seg * (3 * B + 3);
+    if (n_seg <= 0) return WB_OK;
+    if (n_seg > 65535) return WB_EINVAL;
+    ProfScope ps("agc", st);
+    const dim3 grid(B, n_seg);
+    const unsigned rgrid = (unsigned)((n_seg + 7) / 8);
+    agc_partial_kernel<0><<<grid, AGC_THREADS, 0, st>>>(pre, seg_mags, agc, partial);
+    agc_reduce_kernel<0><<<rgrid, 256, 0, st>>>(partial, n_seg, B);
+    agc_partial_kernel<1><<<grid, AGC_THREADS, 0, st>>>(pre, seg_mags, agc, partial);
+    agc_reduce_kernel<1><<<rgrid, 256, 0, st>>>(partial, n_seg, B);
+    agc_update_kernel<<<1, 32, 0, st>>>(partial, n_seg, B, agc, *thresholds);
+    return cudaGetLastError() == cudaSuccess ? WB_OK : WB_ECUDA;
+}
+
+// ---------------------------------------------------------------------------
+// Kerr ODE (fft_ode.rs:171-250 kerr_ode_fft): one CTA per position, threads
+// over bands (BPT bands each), the precond compressed by its segment's AGC
+// threshold on load, rk4_steps RK4 steps whose derivative reads the
+// neighbours' |z|^2 from shared memory -- the plain stencil (fft_ode.rs:
+// 123-141) below 256 bands, the FFT convolution's circular indexing over
+// next_pow2(n_bands) zero-padded points from 256 on -- then the corrector
+// plate (ffn.rs:162-181).
+// ---------------------------------------------------------------------------
+template <int BPT>
+__global__ void __launch_bounds__(1024) kerr_ode_kernel(OdeArgs a) {
+    extern __shared__ float msq[];  // [n_bands]
+    const int n = a.n_bands;
+    const long long row = blockIdx.x;
+    const float *pre = a.pre + row * 2 * n;
+    const float thr = a.thresholds[row / a.rows_per_seg];
+    const float dt = __fdiv_rn(1.0f, (float)a.steps);
+    const float hdt = FM(0.5f, dt);
+    const float w0 = a.rk4_w[0], w1 = a.rk4_w[1], w2 = a.rk4_w[2], w3 = a.rk4_w[3];
+    float r[BPT], s[BPT], g[BPT], om[BPT];
+    float k1r[BPT], k1s[BPT], k2r[BPT], k2s[BPT], k3r[BPT], k3s[BPT], k4r[BPT], k4s[BPT];
+#pragma unroll
+    for (int u = 0; u < BPT; u++) {
+        const int k = threadIdx.x + u * blockDim.x;
+        r[u] = s[u] = g[u] = om[u] = 0.0f;
+        if (k < n) {
+            r[u] = pre[2 * k];
+            s[u] = pre[2 * k + 1];
+            const float mag = __fsqrt_rn(FA(FM(r[u], r[u]), FM(s[u], s[u])));
+            if (mag > thr && mag > 0.001f) {  // agc.rs knee_compress
+                const float comp = FA(thr, FM(thr, tanhf(__fdiv_rn(__fsub_rn(mag, thr), thr))));
+                const float scale = __fdiv_rn(comp, mag);
+                r[u] = FM(r[u], scale);
+                s[u] = FM(s[u], scale);
+            }
+            g[u] = softplus_ref(a.gamma_raw[k]);
+            om[u] = a.omega[k];
+        }
+    }
+    const int L = a.fft_len;
+    auto eval = [&](const float(&vr)[BPT], const float(&vs)[BPT], float(&dr)[BPT], float(&ds)[BPT]) {
+#pragma unroll
+        for (int u = 0; u < BPT; u++) {
+            const int k = threadIdx.x + u * blockDim.x;
+            if (k < n) msq[k] = FA(FM(vr[u], vr[u]), FM(vs[u], vs[u]));
+        }
+        __syncthreads();
+#pragma unroll
+        for (int u = 0; u < BPT; u++) {
+            const int k = threadIdx.x + u * blockDim.x;
+            if (k >= n) continue;
+            float ns = 0.0f;
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                const int j = k + (q < 2 ? q - 2 : q - 1);  // k-2, k-1, k+1, k+2
+                const int jj = L ? (j & (L - 1)) : j;  // L is a power of two: the circular index
+                if (jj >= 0 && jj < n) ns = FA(ns, msq[jj]);
+            }
+            const float phi = FA(FA(om[u], FM(a.alpha, msq[k])), FM(a.beta, ns));
+            dr[u] = __fsub_rn(FM(-g[u], vr[u]), FM(phi, vs[u]));
+            ds[u] = FA(FM(-g[u], vs[u]), FM(phi, vr[u]));
+        }
+        __syncthreads();  // msq is rewritten by the next evaluation
+    };
+    float rt[BPT], st[BPT];
+    for (int step = 0; step < a.steps; step++) {
+        eval(r, s, k1r, k1s);
+#pragma unroll
+        for (int u = 0; u < BPT; u++) {
+            rt[u] = FA(r[u], FM(hdt, k1r[u]));
+            st[u] = FA(s[u], FM(hdt, k1s[u]));
+        }
+        eval(rt, st, k2r, k2s);
+#pragma unroll
+        for (int u = 0; u < BPT; u++) {
+            rt[u] = FA(r[u], FM(hdt, k2r[u]));
+            st[u] = FA(s[u], FM(hdt, k2s[u]));
+        }
+        eval(rt, st, k3r, k3s);
+#pragma unroll
+        for (int u = 0; u < BPT; u++) {
+            rt[u] = FA(r[u], FM(dt, k3r[u]));
+            st[u] = FA(s[u], FM(dt, k3s[u]));
+        }
+        eval(rt, st, k4r, k4s);
+#pragma unroll
+        for (int u = 0; u < BPT; u++) {
+            r[u] = FA(r[u], FM(dt, FA(FA(FA(FM(w0, k1r[u]), FM(w1, k2r[u])), FM(w2, k3r[u])), FM(w3, k4r[u]))));
+            s[u] = FA(s[u], FM(dt, FA(FA(FA(FM(w0, k1s[u]), FM(w1, k2s[u])), FM(w2, k3s[u])), FM(w3, k4s[u]))));
+        }
+    }
+    float *out = a.out + row * 2 * n;
+#pragma unroll
+    for (int u = 0; u < BPT; u++) {
+        const int k = threadIdx.x + u * blockDim.x;
+        if (k >= n) continue;
+        float ro = r[u], so = s[u];
+        if (a.corrector) {
+            const float sc = sinf(a.corrector[k]), cc = cosf(a.corrector[k]);
+            ro = __fsub_rn(FM(r[u], cc), FM(s[u], sc));
+            so = FA(FM(r[u], sc), FM(s[u], cc));
+        }
+        out[2 * k] = ro;
+        out[2 * k + 1] = so;
+    }
+}
+
+int launch_kerr_ode(const OdeArgs &a, long long rows, cudaStream_t st) {
+    if (rows <= 0) return WB_OK;
+    const int n = a.n_bands;
+    int bpt = 1;
+    while (n > 1024 * bpt && bpt < 4) bpt *= 2;
+    if (n > 1024 * bpt) return WB_ENOTSUP;
+    if (rows > 0x7fffffffLL) return WB_EINVAL;
+    const int threads = std::max(32, std::min(1024, ((n + bpt - 1) / bpt + 31) / 32 * 32));
+    const size_t smem = sizeof(float) * (size_t)n;
+    ProfScope ps("kerr_ode", st);
+    if (bpt == 1) kerr_ode_kernel<1><<<(unsigned)rows, threads, smem, st>>>(a);
+    else if (bpt == 2) kerr_ode_kernel<2><<<(unsigned)rows, threads, smem, st>>>(a);
+    else kerr_ode_kernel<4><<<(unsigned)rows, threads, smem, st>>>(a);
+    return cudaGetLastError() == cudaSuccess ? WB_OK : WB_ECUDA;
+}
+
+// ---------------------------------------------------------------------------
+// out_proj (out_proj.rs:24-40) on the exact path: dense y = b + sum (one
+// thread per output, sequential over the inputs), block-diagonal with the
+// sum started at the group's bias.
+// ---------------------------------------------------------------------------
+__global__ void out_proj_exact_kernel(const float *__restrict__ x, long long rows, int E, int groups,
+                                      const float *__restrict__ w, const float *__restrict__ b, float *__restrict__ y) {
+    const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    if (i >= rows * E) return;
+    const long long r = i / E;
+    const int o = (int)(i - r * E);
+    const float *xr = x + r * E;
+    if (groups <= 1) {
+        const float *wr = w + (long long)o * E;
+        float s = 0.0f;
+        for (int j = 0; j < E; j++) s = FA(s, FM(wr[j], xr[j]));
+        y[i] = FA(b[o], s);
+    } else {
+        const int gs = E / groups, gi = o / gs, oi = o - gi * gs;
+        const float *gw = w + (long long)gi * ((long long)gs * gs + gs);
+        float s = gw[(long long)gs * gs + oi];
+        const float *wr = gw + (long long)oi * gs;
+        for (int j = 0; j < gs; j++) s = FA(s, FM(wr[j], xr[gi * gs + j]));
+        y[i] = s;
+    }
+}
+
+int launch_out_proj_exact(const float *x, long long rows, int E, int groups, const float *w, const float *b, float *y,
+                          cudaStream_t st) {
+    const long long n = rows * E;
+    if (n <= 0) return WB_OK;
+    ProfScope ps("ffn_out_proj", st);
+    out_proj_exact_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(x, rows, E, groups, w, b, y);
+    return cudaGetLastError() == cudaSuccess ? WB_OK : WB_ECUDA;
+}
+
+// ---------------------------------------------------------------------------
+// Residual, embedding, decoders.
+// ---------------------------------------------------------------------------
+__global__ void residual_kernel(float *__restrict__ h, const float *__restrict__ a, const float *__restrict__ b,
+                                long long n) {
+    const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    if (i < n) h[i] = FA(h[i], FA(a[i], b[i]));  // kv_cache.rs:220: hidden += attn + ffn
+}
+
+int launch_residual(float *h, const float *a, const float *b, long long n, cudaStream_t st) {
+    if (n <= 0) return WB_OK;
+    residual_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(h, a, b, n);
+    return cudaGetLastError() == cudaSuccess ? WB_OK : WB_ECUDA;
+}
+
+__global__ void embed_kernel(const int32_t *__restrict__ tok, const int32_t *__restrict__ widx, int rows, int E,
+                             const float *__restrict__ wte, int vocab, const float *__restrict__ wpe, int n_pos,
+                             float *__restrict__ out, uint32_t *dev_err) {
+    const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    if (i >= (long long)rows * E) return;
+    const int r = (int)(i / E), j = (int)(i - (long long)r * E);
+    const int t = tok[r];
+    if (t < 0 || t >= vocab) {
+        if (j == 0) atomicOr(dev_err, WB_DERR_BOUNDS);
+        out[i] = 0.0f;
+        return;
+    }
+    float v = wte[(long long)t * E + j];
+    const int p = widx[r];
+    if (wpe && p >= 0 && p < n_pos) v = FA(v, wpe[(long long)p * E + j]);
+    out[i] = v;
+}
+
+int launch_embed(const int32_t *tok, const int32_t *widx, int rows, int E, const float *wte, int vocab,
+                 const float *wpe, int n_pos, float *out, uint32_t *dev_err, cudaStream_t st) {
+    const long long n = (long long)rows * E;
+    if (n <= 0) return WB_OK;
+    embed_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(tok, widx, rows, E, wte, vocab, wpe, n_pos, out,
+                                                             dev_err);
+    return cudaGetLastError() == cudaSuccess ? WB_OK : WB_ECUDA;
+}
+
+// phase_native_decode's corrector rotation (kv_cache.rs:19-26) of rows
+// [rows][2 n_bands].
+__global__ void rotate_bands_kernel(const float *__restrict__ x, long long rows, int n_bands,
+                                    const float *__restrict__ corr, float *__restrict__ y) {
+    const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    if (i >= rows * n_bands) return;
+    const int k = (int)(i % n_bands);
+    const float sc = sinf(corr[k]), cc = cosf(corr[k]);
+    const float r = x[2 * i], s = x[2 * i + 1];
+    y[2 * i] = __fsub_rn(FM(r, cc), FM(s, sc));
+    y[2 * i + 1] = FA(FM(r, sc), FM(s, cc));
+}
+
+int launch_rotate_bands(const float *x, long long rows, int n_bands, const float *corr, float *y, cudaStream_t st) {
+    const long long n = rows * n_bands;
+    if (n <= 0) return WB_OK;
+    rotate_bands_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(x, rows, n_bands, corr, y);
+    return cudaGetLastError() == cudaSuccess ? WB_OK : WB_ECUDA;
+}
+
+// logits[r][v] = sum_j x[r][j] * w[v][j], sequential over j (the exact path of
+// both decoders: kv_cache.rs:27-31, :370-374).
+__global__ void vocab_dot_kernel(const float *__restrict__ x, int rows, int E, const float *__restrict__ w, int vocab,
+                                 float *__restrict__ logits) {
+    const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    if (i >= (long long)rows * vocab) return;
+    const int r = (int)(i / vocab), v = (int)(i - (long long)r * vocab);
+    const float *xr = x + (long long)r * E, *wr = w + (long long)v * E;
+    float s = 0.0f;
+    for (int j = 0; j < E; j++) s = FA(s, FM(xr[j], wr[j]));
+    logits[i] = s;
+}
+
+int launch_vocab_dot(const float *x, int rows, int E, const float *w, int vocab, float *logits, cudaStream_t st) {
+    const long long n = (long long)rows * vocab;
+    if (n <= 0) return WB_OK;
+    ProfScope ps("vocab_dot", st);
+    vocab_dot_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(x, rows, E, w, vocab, logits);
+    return cudaGetLastError() == cudaSuccess ? WB_OK : WB_ECUDA;
+}
+
+#undef FM
+#undef FA
+
+}  // namespace wb

@@ -829,7 +829,7 @@ template <bool TF32>
 __global__ void __launch_bounds__(128, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                    const float *__restrict__ bias, float *__restrict__ C, int M, int N, int K, long long ldc,
-                   uint32_t *dev_err) {
+                   uint32_t *dev_err, int accumulate) {
     constexpr int GBK = TF32 ? 32 : 64;  // elements per K block
     extern __shared__ uint8_t smem_raw[];
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -912,7 +912,10 @@ __global__ void __launch_bounds__(128, 1)
 #pragma unroll 4
             for (int j = 0; j < 32; j++) {
                 const int m = m0 + warp * 32 + j;
-                if (m < M && n < N) C[(long long)m * ldc + n] = buf[j * 33 + lane] + bv;
+                if (m < M && n < N) {
+                    float *c = C + (long long)m * ldc + n;
+                    *c = accumulate ? *c + (buf[j * 33 + lane] + bv) : buf[j * 33 + lane] + bv;
+                }
             }
         }
     }
@@ -986,7 +989,7 @@ static CoreLayout core_layout(const TcLayerWeights &t, int B, int T, size_t off,
 // (0 = K); C [M][ldc] fp32; bias may be null.
 static int launch_gemm(bool tf32, const void *A, const void *W, const float *bias, float *C, int M, int N, int K,
                        long long ldc, uint32_t *dev_err, cudaStream_t st, std::string *msg, long long lda = 0,
-                       long long ldw = 0) {
+                       long long ldw = 0, int accumulate = 0) {
     const int esz = tf32 ? 4 : 2;
     if (!lda) lda = K;
     if (!ldw) ldw = K;
@@ -1015,10 +1018,10 @@ static int launch_gemm(bool tf32, const void *A, const void *W, const float *bia
     ProfScope ps(tf32 ? "gemm_tf32" : "gemm_bf16", st);
     if (tf32) {
         cudaFuncSetAttribute(gemm_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, G_SMEM);
-        gemm_tc_kernel<true><<<gg, 128, G_SMEM, st>>>(ta, tb, bias, C, M, N, K, ldc, dev_err);
+        gemm_tc_kernel<true><<<gg, 128, G_SMEM, st>>>(ta, tb, bias, C, M, N, K, ldc, dev_err, accumulate);
     } else {
         cudaFuncSetAttribute(gemm_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, G_SMEM);
-        gemm_tc_kernel<false><<<gg, 128, G_SMEM, st>>>(ta, tb, bias, C, M, N, K, ldc, dev_err);
+        gemm_tc_kernel<false><<<gg, 128, G_SMEM, st>>>(ta, tb, bias, C, M, N, K, ldc, dev_err, accumulate);
     }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
@@ -1267,6 +1270,34 @@ int tc_gemm_bf16(const __nv_bfloat16 *A, const __nv_bfloat16 *B, const float *bi
 int tc_gemm_tf32(const float *A, const float *B, const float *bias, float *C, int M, int N, int K, uint32_t *dev_err,
                  cudaStream_t st, std::string *msg) {
     return launch_gemm(true, A, B, bias, C, M, N, K, N, dev_err, st, msg);
+}
+
+// x -> hi = bf16(x), lo = bf16(x - hi): the two terms of a bf16 split whose
+// products hi.hi + lo.hi + hi.lo carry ~16 mantissa bits
+__global__ void split_bf16_kernel(const float *__restrict__ x, long long n, __nv_bfloat16 *__restrict__ hi,
+                                  __nv_bfloat16 *__restrict__ lo) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        const float v = x[i];
+        const __nv_bfloat16 h = __float2bfloat16_rn(v);
+        hi[i] = h;
+        lo[i] = __float2bfloat16_rn(v - __bfloat162float(h));
+    }
+}
+
+int split_bf16(const float *x, long long n, __nv_bfloat16 *hi, __nv_bfloat16 *lo, cudaStream_t st) {
+    if (n <= 0) return WB_OK;
+    const int grid = (int)std::min<long long>(4 * 148, (n + 255) / 256);
+    split_bf16_kernel<<<grid, 256, 0, st>>>(x, n, hi, lo);
+    return cudaGetLastError() == cudaSuccess ? WB_OK : WB_ECUDA;
+}
+
+int tc_gemm_bf16x3(const __nv_bfloat16 *A_hi, const __nv_bfloat16 *A_lo, const __nv_bfloat16 *W_hi,
+                   const __nv_bfloat16 *W_lo, const float *bias, float *C, int M, int N, int K, uint32_t *dev_err,
+                   cudaStream_t st, std::string *msg) {
+    int rc = launch_gemm(false, A_hi, W_hi, bias, C, M, N, K, N, dev_err, st, msg);
+    if (!rc) rc = launch_gemm(false, A_lo, W_hi, nullptr, C, M, N, K, N, dev_err, st, msg, 0, 0, 1);
+    if (!rc) rc = launch_gemm(false, A_hi, W_lo, nullptr, C, M, N, K, N, dev_err, st, msg, 0, 0, 1);
+    return rc;
 }
 
 int tc_attn_forward(const TcLayerWeights &t, const float *x, int B, int T, bool use_content, float *y,

@@ -35,6 +35,15 @@ int tc_gemm_bf16(const __nv_bfloat16 *A, const __nv_bfloat16 *B, const float *bi
                  uint32_t *dev_err, cudaStream_t st, std::string *msg);
 int tc_gemm_tf32(const float *A, const float *B, const float *bias, float *C, int M, int N, int K, uint32_t *dev_err,
                  cudaStream_t st, std::string *msg);
+
+// bf16 split of fp32 data (hi = bf16(x), lo = bf16(x - hi)) and the product
+// C = A W^T (+ bias) from the three terms A_hi W_hi + A_lo W_hi + A_hi W_lo on
+// the tcgen05 bf16 GEMM (~16 mantissa bits: the tensor path of the serve
+// layer's FFN out_proj and vocabulary products).  K a multiple of 8.
+int split_bf16(const float *x, long long n, __nv_bfloat16 *hi, __nv_bfloat16 *lo, cudaStream_t st);
+int tc_gemm_bf16x3(const __nv_bfloat16 *A_hi, const __nv_bfloat16 *A_lo, const __nv_bfloat16 *W_hi,
+                   const __nv_bfloat16 *W_lo, const float *bias, float *C, int M, int N, int K, uint32_t *dev_err,
+                   cudaStream_t st, std::string *msg);
 // Decode step for n_seq sequences of one layer: attention over the cache
 // with the new position appended, then out_proj and the length update;
 // scratch (the cache's, fixed size, tickets zero) holds the attention
