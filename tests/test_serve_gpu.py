@@ -175,3 +175,30 @@ def test_serve_session_matches_oracle(ctx, phase_native):
     assert st["count"] == agc.count
     assert abs(st["threshold"] - agc.threshold) <= 1e-5
     assert ctx.take_device_error() == 0
+
+
+def test_serve_decode_graph_equals_eager(ctx):
+    """forward_one captured in one CUDA graph (tensor path) gives the eager
+    calls' logits bit for bit over four replays."""
+    import wave_engine_b200 as wb
+    E, H, L, V, T = 768, 12, 2, 500, 40
+    m = _model(11, E, H, L, V, True)
+    g = np.random.default_rng(2)
+    tokens = g.integers(0, V, (3, T)).astype(np.int32)
+    steps = [g.integers(0, V, 3).astype(np.int32) for _ in range(4)]
+    ids = np.array([1, 0, 2], np.int32)
+    outs = []
+    for graph in (False, True):
+        sess = wb.ServeSession(m, max_seqs=3, max_ctx=T + 8, ctx=ctx)
+        sess.prefill(tokens, ids)
+        if graph:
+            sess.capture_decode(ids)
+        got = []
+        for s, tk in enumerate(steps):
+            pos = np.full(3, T + s, np.int32)
+            y = sess.forward_one_graph(tk, pos) if graph else sess.forward_one(tk, pos, ids)
+            got.append(y.cpu().numpy().copy())
+        outs.append(got)
+    for a, b in zip(*outs):
+        assert np.array_equal(a, b)
+    assert ctx.take_device_error() == 0

@@ -12,7 +12,7 @@
 // sequential sums, products rounded before the add (__fmul_rn / __fadd_rn,
 // no contraction) -- so the all-fp32 path differs from the reference only by
 // the last bits of tanhf / sinf / cosf / expf / logf and by the order of the
-// LayerNorm and AGC reductions.  The large products (the FFN's out_proj and
+// LayerNorm, maestro squeeze and AGC reductions.  The large products (the FFN's out_proj and
 // the decoders' vocabulary GEMMs) run as bf16x3 products on the tcgen05 GEMM
 // (wb_tc.cu) unless the caller asks for WB_PATH_EXACT.
 #include "wave_b200.h"
@@ -78,9 +78,7 @@ int launch_layer_norm(const float *x, int rows, int n, const float *w, const flo
 // ---------------------------------------------------------------------------
 // Maestro (compute.rs:356-360 / ffn.rs:61-66, :185-191): y = base + process_1
 // . gelu(squeeze . x), squeeze [M][E] and process_1 [E][M] with biases; each
-// output one sequential sum, then bias + sum (compute.rs:441-452).  A CTA
-// takes up to 32 rows staged in shared memory, with both weight matrices
-// when they fit.
+// output bias + sum (compute.rs:441-452).
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ float gelu_ref(float v) {
     // compute.rs:113-119: 0.5 v (1 + tanh(c (v + 0.044715 v^3)))
@@ -89,69 +87,59 @@ __device__ __forceinline__ float gelu_ref(float v) {
     return FM(FM(0.5f, v), FA(1.0f, tanhf(inner)));
 }
 
-// rows per CTA and whether both weight matrices are staged in shared memory
-// (squeeze rows padded to E + 1 floats, process_1 rows to M + 1: the
-// threads of a warp read different rows at the same column without bank
-// conflicts)
-struct MaestroPlan {
-    int rows;
-    bool staged;
-    size_t smem;
-};
+// A CTA takes MR rows (staged in shared memory).  squeeze: one warp per
+// (row, m) output, lanes along the inputs, the lane partials combined by a
+// fixed shuffle tree (deterministic; the squeeze sums differ from the
+// reference's sequential order by rounding only), then bias + sum and GELU.
+// process_1: one thread per (row, i) output, the M products summed in the
+// reference's order, then bias + sum and the residual base.
+static constexpr int MR = 4;  // most rows per CTA (1 when few rows: more CTAs)
 
-static MaestroPlan maestro_plan(int E, int M) {
-    const size_t w = (size_t)M * (E + 1) + (size_t)E * (M + 1);
-    for (int r : {32, 16, 8}) {
-        const size_t smem = sizeof(float) * (w + (size_t)r * E + (size_t)r * M);
-        if (smem <= 200 * 1024) return {r, true, smem};
-    }
-    return {8, false, sizeof(float) * ((size_t)8 * E + 8 * M)};
-}
-
-__global__ void __launch_bounds__(256) maestro_kernel(MaestroArgs a, int mrows, int staged) {
+__global__ void __launch_bounds__(256) maestro_kernel(MaestroArgs a, int mr) {
     extern __shared__ float msm[];
     const int E = a.E, M = a.M;
-    float *xs = msm;                         // [mrows][E]
-    float *act = xs + (size_t)mrows * E;     // [mrows][M]
-    float *wsq = act + (size_t)mrows * M;    // [M][E + 1]   (staged)
-    float *wpr = wsq + (size_t)M * (E + 1);  // [E][M + 1]   (staged)
-    const long long r0 = (long long)blockIdx.x * mrows;
-    const int nr = (int)min((long long)mrows, a.rows - r0);
-    for (int e = threadIdx.x; e < nr * E; e += blockDim.x) xs[e] = a.x[r0 * E + e];
-    if (staged) {
-        for (int e = threadIdx.x; e < M * E; e += blockDim.x) {
-            const int m = e / E, j = e - m * E;
-            wsq[m * (E + 1) + j] = __ldg(a.sq_w + e);
-        }
-        for (int e = threadIdx.x; e < E * M; e += blockDim.x) {
-            const int i = e / M, m = e - i * M;
-            wpr[i * (M + 1) + m] = __ldg(a.pr_w + e);
-        }
+    float *xs = msm;                  // [MR][E]
+    float *act = xs + (size_t)MR * E; // [MR][M]
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const long long r0 = (long long)blockIdx.x * mr;
+    const int nr = (int)min((long long)mr, a.rows - r0);
+    const float *xg = a.x + r0 * E;
+    if ((E & 3) == 0 && (reinterpret_cast<uintptr_t>(xg) & 15) == 0) {
+        for (int e = threadIdx.x; e < nr * E / 4; e += blockDim.x)
+            reinterpret_cast<float4 *>(xs)[e] = __ldg(reinterpret_cast<const float4 *>(xg) + e);
+    } else {
+        for (int e = threadIdx.x; e < nr * E; e += blockDim.x) xs[e] = __ldg(xg + e);
     }
     __syncthreads();
-    for (int e = threadIdx.x; e < nr * M; e += blockDim.x) {
-        const int r = e / M, m = e - r * M;
+    for (int t = warp; t < nr * M; t += nw) {
+        const int r = t / M, m = t - r * M;
+        const float *wr = a.sq_w + (long long)m * E;
         const float *xr = xs + r * E;
         float s = 0.0f;
-        if (staged) {
-            const float *wr = wsq + m * (E + 1);
-            for (int j = 0; j < E; j++) s = FA(s, FM(wr[j], xr[j]));
-        } else {
-            const float *wr = a.sq_w + (long long)m * E;
-            for (int j = 0; j < E; j++) s = FA(s, FM(__ldg(wr + j), xr[j]));
+        for (int j0 = lane; j0 < E; j0 += 8 * 32) {  // 8 loads in flight, then the sums in order
+            float wv[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) wv[u] = j0 + 32 * u < E ? __ldg(wr + j0 + 32 * u) : 0.0f;
+#pragma unroll
+            for (int u = 0; u < 8; u++)
+                if (j0 + 32 * u < E) s = FA(s, FM(wv[u], xr[j0 + 32 * u]));
         }
-        act[r * M + m] = gelu_ref(FA(__ldg(a.sq_b + m), s));
+#pragma unroll
+        for (int o = 16; o; o >>= 1) s = FA(s, __shfl_xor_sync(0xffffffffu, s, o));
+        if (lane == 0) act[r * M + m] = gelu_ref(FA(__ldg(a.sq_b + m), s));
     }
     __syncthreads();
     for (int e = threadIdx.x; e < nr * E; e += blockDim.x) {
         const int r = e / E, i = e - r * E;
+        const float *wr = a.pr_w + (long long)i * M;
         float s = 0.0f;
-        if (staged) {
-            const float *wr = wpr + i * (M + 1);
-            for (int m = 0; m < M; m++) s = FA(s, FM(wr[m], act[r * M + m]));
-        } else {
-            const float *wr = a.pr_w + (long long)i * M;
-            for (int m = 0; m < M; m++) s = FA(s, FM(__ldg(wr + m), act[r * M + m]));
+        for (int m0 = 0; m0 < M; m0 += 16) {  // 16 loads in flight, then the sums in order
+            float wv[16];
+#pragma unroll
+            for (int u = 0; u < 16; u++) wv[u] = m0 + u < M ? __ldg(wr + m0 + u) : 0.0f;
+#pragma unroll
+            for (int u = 0; u < 16; u++)
+                if (m0 + u < M) s = FA(s, FM(wv[u], act[r * M + m0 + u]));
         }
         const float out = FA(__ldg(a.pr_b + i), s);
         const float base = a.base ? a.base[(r0 + r) * E + i] : xs[r * E + i];
@@ -161,11 +149,12 @@ __global__ void __launch_bounds__(256) maestro_kernel(MaestroArgs a, int mrows, 
 
 int launch_maestro(const MaestroArgs &a, cudaStream_t st) {
     if (a.rows <= 0) return WB_OK;
-    const MaestroPlan p = maestro_plan(a.E, a.M);
-    if (p.smem > 200 * 1024) return WB_ENOTSUP;
+    const size_t smem = sizeof(float) * ((size_t)MR * a.E + (size_t)MR * a.M);
+    if (smem > 200 * 1024) return WB_ENOTSUP;
     ProfScope ps("maestro", st);
-    cudaFuncSetAttribute(maestro_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem);
-    maestro_kernel<<<(unsigned)((a.rows + p.rows - 1) / p.rows), 256, p.smem, st>>>(a, p.rows, p.staged ? 1 : 0);
+    const int mr = a.rows >= 4 * 148 ? MR : 1;
+    cudaFuncSetAttribute(maestro_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    maestro_kernel<<<(unsigned)((a.rows + mr - 1) / mr), 256, smem, st>>>(a, mr);
     return cudaGetLastError() == cudaSuccess ? WB_OK : WB_ECUDA;
 }
 

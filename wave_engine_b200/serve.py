@@ -353,6 +353,35 @@ class ServeSession:
         self._layers(hidden, n_seq, T, ids, True)
         return self._decode(hidden.view(n_seq, T, self.E)[:, T - 1].contiguous())
 
+    def capture_decode(self, seq_ids):
+        """Capture one forward_one step for the slots ``seq_ids`` in a CUDA
+        graph (every launch of every layer; tokens and positions through
+        static device buffers).  Call after a prefill has sized the context's
+        workspaces; then ``forward_one_graph`` replays it."""
+        ids = torch.as_tensor(np.ascontiguousarray(seq_ids, np.int32), device=self.dev)
+        n = int(ids.shape[0])
+        self._g_tok = torch.zeros(n, dtype=torch.int32, device=self.dev)
+        self._g_pos = torch.zeros(n, dtype=torch.int32, device=self.dev)
+        self._g_ids = ids
+        prev = torch.cuda.current_stream(self.dev)
+        torch.cuda.synchronize(self.dev)
+        self._graph = torch.cuda.CUDAGraph()
+        try:
+            with torch.cuda.graph(self._graph):
+                hidden = embed(self._g_tok, self._g_pos, self.wte, self.wpe, ctx=self.ctx)
+                self._layers(hidden, n, 1, self._g_ids, False)
+                self._g_logits = self._decode(hidden)
+        finally:
+            self.ctx.set_stream(prev.cuda_stream)
+
+    def forward_one_graph(self, tokens, positions):
+        """forward_one through the captured graph: logits [n][vocab] (the
+        graph's static output tensor, overwritten by the next replay)."""
+        self._g_tok.copy_(torch.as_tensor(np.ascontiguousarray(tokens, np.int32)))
+        self._g_pos.copy_(torch.as_tensor(np.ascontiguousarray(positions, np.int32)))
+        self._graph.replay()
+        return self._g_logits
+
     def forward_one(self, tokens, positions, seq_ids):
         """kv_cache.rs:241-381: one new token per request -> logits [n][vocab]."""
         tok = torch.as_tensor(np.ascontiguousarray(tokens, np.int32), device=self.dev)
