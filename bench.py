@@ -1084,7 +1084,9 @@ def run_profile_case(args):
     32 sequences at ctx ~1100; 'prefill' = 3 tensor-path prefills of one
     768-dim layer, 4 x 1024 tokens (content on); 'prefill-serve' = 3 serve
     prefills (KV cache, no content) of one 768-dim layer, 16 x 1024 tokens
-    (about 10 work items per SM, as in the benchmark's 20)."""
+    (about 10 work items per SM, as in the benchmark's 20); 'dot' = 3
+    dot-product attention forwards of one 768-dim layer, 16 x 1024 tokens;
+    'serve-ffn' = 3 serve-layer FFN calls on 16 x 1024 rows."""
     import numpy as np
     import torch
     import wave_engine_b200 as wb
@@ -1143,6 +1145,20 @@ def run_profile_case(args):
         for _ in range(3):
             cache.reset()
             cache.prefill(0, lay, x, ids, out=y)
+    elif args.profile_case == "dot":
+        # 3 dot-product attention forwards of one 768-dim layer, 16 x 1024 tokens
+        dl = wb.DotAttnLayer(ctx, wb.gaussian_attention_weights(5000, H, E))
+        x = torch.randn((16, CFG["seq_len"], E), generator=g, device="cuda")
+        for _ in range(3):
+            wb.attention(dl, x, ctx=ctx)
+        extra["attn_core_flops_per_launch"] = 16 * H * CFG["seq_len"] * (CFG["seq_len"] + 1) // 2 * 4 * hd
+    elif args.profile_case == "serve-ffn":
+        # 3 FFN calls (maestro 16, RK4-16) on 16 requests x 1024 rows of the 768-dim model
+        ffn = wb.FfnLayer(ctx, wb.gaussian_ffn(2000, E, 16))
+        agc = wb.Agc(ctx)
+        x = torch.randn((16 * CFG["seq_len"], E), generator=g, device="cuda")
+        for _ in range(3):
+            wb.ffn_forward(ffn, agc, x, rows_per_call=CFG["seq_len"], ctx=ctx)
     else:
         x = torch.randn((4, CFG["seq_len"], E), generator=g, device="cuda")
         for _ in range(3):
@@ -1162,7 +1178,8 @@ def main():
                          "context 128-4096; prefill-168/-384/-4096: prefill through all layers of the 168-, "
                          "384- and 4096-dim models; dot-768: the legacy dot-product attention at the 768-dim "
                          "shape; serve-model: the whole serve layer (attention + FFN + decoder) on the GPU")
-    ap.add_argument("--profile-case", choices=["decode", "decode-stress", "prefill", "prefill-serve"], default=None,
+    ap.add_argument("--profile-case", choices=["decode", "decode-stress", "prefill", "prefill-serve", "dot", "serve-ffn"],
+                    default=None,
                     help="run a small case for an ncu capture instead of the benchmark")
     ap.add_argument("--shard", choices=["batch", "heads"], default="batch",
                     help="prefill workloads under torchrun: every rank its own batch (weak scaling), or the heads "

@@ -38,7 +38,8 @@ def test_layer_norm_matches_oracle(ctx):
 def test_ffn_matches_oracle_over_a_sequence_of_calls(ctx, path, tol, E, groups):
     """Twelve calls of 3 rows each (the AGC's first nine observations replace
     its state, later ones are EMA updates), then one call holding four
-    requests of 2 rows (four reference calls in one launch).  168-dim: the
+    requests of 2 rows (four reference calls in one launch), then two requests
+    of 300 rows.  168-dim: the
     plain stencil (84 bands); 512: 256 bands, a power of two, where the
     reference's FFT convolution wraps around; 768: 384 bands padded to 512.
     Inputs of std 1.5 push magnitudes past the AGC threshold."""
@@ -58,8 +59,15 @@ def test_ffn_matches_oracle_over_a_sequence_of_calls(ctx, path, tol, E, groups):
     ref = np.concatenate([oracle.ffn_forward(wp, agc_o, x[2 * i:2 * i + 2]) for i in range(4)])
     r = check("four requests in one call", y, ref, tol)
     assert r.passed, str(r)
+    # two requests of 300 rows: the AGC statistics over several blocks per
+    # request, and (tensor path) the bf16x3 out_proj for 256 rows and more
+    x = (g.standard_normal((600, E)) * 1.5).astype(np.float32)
+    y = wb.ffn_forward(w, agc_g, x, rows_per_call=300, path=path, ctx=ctx)
+    ref = np.concatenate([oracle.ffn_forward(wp, agc_o, x[300 * i:300 * i + 300]) for i in range(2)])
+    r = check("two long requests", y, ref, tol)
+    assert r.passed, str(r)
     st = agc_g.state()
-    assert st["count"] == agc_o.count == 16
+    assert st["count"] == agc_o.count == 18
     for k in ("ema_mean", "ema_var", "threshold"):
         assert abs(st[k] - getattr(agc_o, k)) <= 1e-5 * max(1.0, abs(getattr(agc_o, k))), k
     assert ctx.take_device_error() == 0

@@ -276,6 +276,58 @@ __global__ void agc_update_kernel(const float *partial, int n_seg, int B, AgcDev
     }
 }
 
+// requests small enough for one block: both passes inside the block, the
+// block tree in a fixed order (deterministic), mean / count / variance
+// written where agc_update_kernel reads them (B = 1 layout)
+__global__ void __launch_bounds__(AGC_THREADS) agc_small_kernel(const float *__restrict__ pre, long long seg_mags,
+                                                                const AgcDev *agc, float *partial) {
+    __shared__ float ss[AGC_THREADS], sc[AGC_THREADS];
+    const int seg = blockIdx.x;
+    float *ps = partial + (long long)seg * 6;  // 3 * B + 3 with B = 1
+    const float *p = pre + (long long)seg * seg_mags * 2;
+    const float ceil2 = FM(agc->max_threshold, 2.0f);
+    float s = 0.0f, c = 0.0f;
+    for (long long i = threadIdx.x; i < seg_mags; i += AGC_THREADS) {
+        const float m = band_mag(p + 2 * i);
+        if (isfinite(m) && m < ceil2) {
+            s = FA(s, m);
+            c = FA(c, 1.0f);
+        }
+    }
+    ss[threadIdx.x] = s;
+    sc[threadIdx.x] = c;
+    __syncthreads();
+    for (int h = AGC_THREADS / 2; h; h >>= 1) {
+        if (threadIdx.x < h) {
+            ss[threadIdx.x] = FA(ss[threadIdx.x], ss[threadIdx.x + h]);
+            sc[threadIdx.x] = FA(sc[threadIdx.x], sc[threadIdx.x + h]);
+        }
+        __syncthreads();
+    }
+    const float cnt = sc[0];
+    const float mean = cnt > 0.0f ? __fdiv_rn(ss[0], cnt) : 0.0f;
+    __syncthreads();
+    float v = 0.0f;
+    for (long long i = threadIdx.x; i < seg_mags; i += AGC_THREADS) {
+        const float m = band_mag(p + 2 * i);
+        if (isfinite(m) && m < ceil2) {
+            const float d = __fsub_rn(m, mean);
+            v = FA(v, FM(d, d));
+        }
+    }
+    ss[threadIdx.x] = v;
+    __syncthreads();
+    for (int h = AGC_THREADS / 2; h; h >>= 1) {
+        if (threadIdx.x < h) ss[threadIdx.x] = FA(ss[threadIdx.x], ss[threadIdx.x + h]);
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        ps[3] = mean;
+        ps[4] = cnt;
+        ps[5] = cnt > 0.0f ? __fdiv_rn(ss[0], cnt) : 0.0f;
+    }
+}
+
 static int agc_blocks(long long seg_mags) {
     return (int)std::max(1LL, std::min((long long)AGC_MAXB, (seg_mags + 8LL * AGC_THREADS - 1) / (8LL * AGC_THREADS)));
 }
@@ -292,6 +344,11 @@ int launch_agc_observe(const float *pre, int n_seg, long long seg_mags, AgcDev *
     if (n_seg <= 0) return WB_OK;
     if (n_seg > 65535) return WB_EINVAL;
     ProfScope ps("agc", st);
+    if (B == 1) {  // small requests (a decode step): two launches
+        agc_small_kernel<<<n_seg, AGC_THREADS, 0, st>>>(pre, seg_mags, agc, partial);
+        agc_update_kernel<<<1, 32, 0, st>>>(partial, n_seg, B, agc, *thresholds);
+        return cudaGetLastError() == cudaSuccess ? WB_OK : WB_ECUDA;
+    }
     const dim3 grid(B, n_seg);
     const unsigned rgrid = (unsigned)((n_seg + 7) / 8);
     agc_partial_kernel<0><<<grid, AGC_THREADS, 0, st>>>(pre, seg_mags, agc, partial);
