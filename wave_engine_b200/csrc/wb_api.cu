@@ -241,6 +241,7 @@ struct wb_ffn_layer {
     int device = 0;  // destroy must not touch ctx
     int E = 0, M = 0, nb = 0, steps = 0, corr = 0, groups = 1;
     float alpha = 0.0f, beta = 0.0f;
+    // squeeze [M][E]; process_1 stored transposed, [M][E]
     float *mi_sq_w = nullptr, *mi_sq_b = nullptr, *mi_pr_w = nullptr, *mi_pr_b = nullptr;
     float *mo_sq_w = nullptr, *mo_sq_b = nullptr, *mo_pr_w = nullptr, *mo_pr_b = nullptr;
     float *gamma_raw = nullptr, *omega = nullptr, *phase_corr = nullptr, *rk4w = nullptr;
@@ -1445,9 +1446,20 @@ int wb_ffn_layer_create(wb_context *ctx, const wb_ffn_weights_desc *w, wb_ffn_la
     int rc = WB_OK;
     auto up = [&](float **d, const float *src, size_t n) { if (rc == WB_OK) rc = dev_copy(d, src, n); };
     up(&f->mi_sq_w, w->mi_squeeze_w, me); up(&f->mi_sq_b, w->mi_squeeze_b, M);
-    up(&f->mi_pr_w, w->mi_process_w, me); up(&f->mi_pr_b, w->mi_process_b, E);
+    // process_1 [E][M] is kept transposed ([M][E]): the maestro kernel's threads read a column each
+    std::vector<float> tr((size_t)M * E);
+    auto transpose = [&](const float *src) {
+        std::vector<float> h((size_t)M * E);
+        if (cudaMemcpy(h.data(), src, h.size() * sizeof(float), cudaMemcpyDefault) != cudaSuccess) rc = WB_ECUDA;
+        for (int i = 0; i < E; i++)
+            for (int m = 0; m < M; m++) tr[(size_t)m * E + i] = h[(size_t)i * M + m];
+        return tr.data();
+    };
+    if (rc == WB_OK) up(&f->mi_pr_w, transpose(w->mi_process_w), me);
+    up(&f->mi_pr_b, w->mi_process_b, E);
     up(&f->mo_sq_w, w->mo_squeeze_w, me); up(&f->mo_sq_b, w->mo_squeeze_b, M);
-    up(&f->mo_pr_w, w->mo_process_w, me); up(&f->mo_pr_b, w->mo_process_b, E);
+    if (rc == WB_OK) up(&f->mo_pr_w, transpose(w->mo_process_w), me);
+    up(&f->mo_pr_b, w->mo_process_b, E);
     up(&f->gamma_raw, w->gamma_raw, E / 2); up(&f->omega, w->omega, E / 2);
     up(&f->phase_corr, w->phase_correction, E / 2); up(&f->rk4w, w->rk4_weights, 4);
     if (G == 1) {

@@ -131,12 +131,12 @@ __global__ void __launch_bounds__(256) maestro_kernel(MaestroArgs a, int mr) {
     __syncthreads();
     for (int e = threadIdx.x; e < nr * E; e += blockDim.x) {
         const int r = e / E, i = e - r * E;
-        const float *wr = a.pr_w + (long long)i * M;
+        const float *wc = a.pr_wt + i;  // column i of the [M][E] copy: consecutive threads, consecutive words
         float s = 0.0f;
         for (int m0 = 0; m0 < M; m0 += 16) {  // 16 loads in flight, then the sums in order
             float wv[16];
 #pragma unroll
-            for (int u = 0; u < 16; u++) wv[u] = m0 + u < M ? __ldg(wr + m0 + u) : 0.0f;
+            for (int u = 0; u < 16; u++) wv[u] = m0 + u < M ? __ldg(wc + (long long)(m0 + u) * E) : 0.0f;
 #pragma unroll
             for (int u = 0; u < 16; u++)
                 if (m0 + u < M) s = FA(s, FM(wv[u], act[r * M + m0 + u]));
@@ -398,7 +398,21 @@ __global__ void __launch_bounds__(1024) kerr_ode_kernel(OdeArgs a) {
             om[u] = a.omega[k];
         }
     }
+    // each band's four neighbours (k-2, k-1, k+1, k+2) as shared-memory
+    // indices, -1 where the stencil has no neighbour: the plain stencil's
+    // edges, or a circular index landing in the FFT's zero padding
     const int L = a.fft_len;
+    int nb[BPT][4];
+#pragma unroll
+    for (int u = 0; u < BPT; u++) {
+        const int k = threadIdx.x + u * blockDim.x;
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const int j = k + (q < 2 ? q - 2 : q - 1);
+            const int jj = L ? (j & (L - 1)) : j;  // L is a power of two: the circular index
+            nb[u][q] = (k < n && jj >= 0 && jj < n) ? jj : -1;
+        }
+    }
     auto eval = [&](const float(&vr)[BPT], const float(&vs)[BPT], float(&dr)[BPT], float(&ds)[BPT]) {
 #pragma unroll
         for (int u = 0; u < BPT; u++) {
@@ -412,11 +426,8 @@ __global__ void __launch_bounds__(1024) kerr_ode_kernel(OdeArgs a) {
             if (k >= n) continue;
             float ns = 0.0f;
 #pragma unroll
-            for (int q = 0; q < 4; q++) {
-                const int j = k + (q < 2 ? q - 2 : q - 1);  // k-2, k-1, k+1, k+2
-                const int jj = L ? (j & (L - 1)) : j;  // L is a power of two: the circular index
-                if (jj >= 0 && jj < n) ns = FA(ns, msq[jj]);
-            }
+            for (int q = 0; q < 4; q++)
+                if (nb[u][q] >= 0) ns = FA(ns, msq[nb[u][q]]);
             const float phi = FA(FA(om[u], FM(a.alpha, msq[k])), FM(a.beta, ns));
             dr[u] = __fsub_rn(FM(-g[u], vr[u]), FM(phi, vs[u]));
             ds[u] = FA(FM(-g[u], vs[u]), FM(phi, vr[u]));

@@ -18,7 +18,7 @@ struct AgcDev {
 struct MaestroArgs {
     const float *x;       // [rows][E] input
     const float *base;    // [rows][E] residual base (nullptr: x)
-    const float *sq_w, *sq_b, *pr_w, *pr_b;  // squeeze [M][E] + [M], process_1 [E][M] + [E]
+    const float *sq_w, *sq_b, *pr_wt, *pr_b;  // squeeze [M][E] + [M], process_1 transposed [M][E] + [E]
     long long rows;
     int E, M;
     float *y;             // [rows][E] = base + process_1 . gelu(squeeze . x)

@@ -1147,43 +1147,54 @@ struct DotFeatArgs {
 
 static constexpr int DOT_FEAT_WARPS = 8;
 
+static constexpr int DOT_FEAT_ROWS = 4;  // rows per warp, their loads issued together
+
 __global__ void __launch_bounds__(DOT_FEAT_WARPS * 32) dot_feat_kernel(DotFeatArgs a) {
     const int lane = threadIdx.x & 31;
-    const long long i = (long long)blockIdx.x * DOT_FEAT_WARPS + (threadIdx.x >> 5);
-    const long long BH = (long long)a.B * a.H;
-    if (i >= BH * a.T) return;
-    const long long bh = i / a.T;
-    const int t = (int)(i - bh * a.T);
-    const int b = (int)(bh / a.H), h = (int)(bh - (long long)b * a.H);
-    const float *row = a.qkv + ((long long)b * a.T + t) * 3LL * a.E + (long long)h * a.hd;
-    float q[2], k[2], v[2];
+    const long long i0 = ((long long)blockIdx.x * DOT_FEAT_WARPS + (threadIdx.x >> 5)) * DOT_FEAT_ROWS;
+    const long long total = (long long)a.B * a.H * a.T;
+    float q[DOT_FEAT_ROWS][2], k[DOT_FEAT_ROWS][2], v[DOT_FEAT_ROWS][2];
 #pragma unroll
-    for (int u = 0; u < 2; u++) {
-        const int d = 2 * lane + u;
-        const bool ok = d < a.hd;
-        q[u] = ok ? __ldg(row + d) * a.scale : 0.0f;
-        k[u] = ok ? __ldg(row + a.E + d) : 0.0f;
-        v[u] = ok ? __ldg(row + 2 * a.E + d) : 0.0f;
-    }
-    const float vh0 = f16_round(v[0]), vh1 = f16_round(v[1]);
-    reinterpret_cast<uint32_t *>(a.qf + i * 64)[lane] = pack_bf16(q[0], q[1]);
-    reinterpret_cast<uint32_t *>(a.kf + i * 64)[lane] = pack_bf16(k[0], k[1]);
-    reinterpret_cast<uint32_t *>(a.vh + i * 64)[lane] = pack_f16(vh0, vh1);  // fp16 hi / lo (P is fp16)
-    reinterpret_cast<uint32_t *>(a.vl + i * 64)[lane] = pack_f16(v[0] - vh0, v[1] - vh1);
-    float s = fmaf(q[0], k[0], q[1] * k[1]);
-    float qq = fmaf(q[0], q[0], q[1] * q[1]);
-    float kk = fmaf(k[0], k[0], k[1] * k[1]);
+    for (int rr = 0; rr < DOT_FEAT_ROWS; rr++) {
+        const long long i = i0 + rr;
+        const long long bh = i / a.T;
+        const int t = (int)(i - bh * a.T);
+        const int b = (int)(bh / a.H), h = (int)(bh - (long long)b * a.H);
+        const float *row = a.qkv + ((long long)b * a.T + t) * 3LL * a.E + (long long)h * a.hd;
 #pragma unroll
-    for (int o = 16; o; o >>= 1) {
-        s += __shfl_xor_sync(0xffffffffu, s, o);
-        qq += __shfl_xor_sync(0xffffffffu, qq, o);
-        kk += __shfl_xor_sync(0xffffffffu, kk, o);
+        for (int u = 0; u < 2; u++) {
+            const int d = 2 * lane + u;
+            const bool ok = i < total && d < a.hd;
+            q[rr][u] = ok ? __ldg(row + d) * a.scale : 0.0f;
+            k[rr][u] = ok ? __ldg(row + a.E + d) : 0.0f;
+            v[rr][u] = ok ? __ldg(row + 2 * a.E + d) : 0.0f;
+        }
     }
-    if (lane == 0) {
-        a.m0[i] = s;
-        a.sprev[i] = -INFINITY;  // no previous-position rule
-        a.cnorm[i] = sqrtf(qq);
-        atomicMax(a.cmax + bh, __float_as_uint(sqrtf(kk)));  // non-negative floats order as their bits
+#pragma unroll
+    for (int rr = 0; rr < DOT_FEAT_ROWS; rr++) {
+        const long long i = i0 + rr;
+        if (i >= total) break;
+        const long long bh = i / a.T;
+        const float vh0 = f16_round(v[rr][0]), vh1 = f16_round(v[rr][1]);
+        reinterpret_cast<uint32_t *>(a.qf + i * 64)[lane] = pack_bf16(q[rr][0], q[rr][1]);
+        reinterpret_cast<uint32_t *>(a.kf + i * 64)[lane] = pack_bf16(k[rr][0], k[rr][1]);
+        reinterpret_cast<uint32_t *>(a.vh + i * 64)[lane] = pack_f16(vh0, vh1);  // fp16 hi / lo (P is fp16)
+        reinterpret_cast<uint32_t *>(a.vl + i * 64)[lane] = pack_f16(v[rr][0] - vh0, v[rr][1] - vh1);
+        float s = fmaf(q[rr][0], k[rr][0], q[rr][1] * k[rr][1]);
+        float qq = fmaf(q[rr][0], q[rr][0], q[rr][1] * q[rr][1]);
+        float kk = fmaf(k[rr][0], k[rr][0], k[rr][1] * k[rr][1]);
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            s += __shfl_xor_sync(0xffffffffu, s, o);
+            qq += __shfl_xor_sync(0xffffffffu, qq, o);
+            kk += __shfl_xor_sync(0xffffffffu, kk, o);
+        }
+        if (lane == 0) {
+            a.m0[i] = s;
+            a.sprev[i] = -INFINITY;  // no previous-position rule
+            a.cnorm[i] = sqrtf(qq);
+            atomicMax(a.cmax + bh, __float_as_uint(sqrtf(kk)));  // non-negative floats order as their bits
+        }
     }
 }
 
@@ -1229,7 +1240,8 @@ int tc_dot_attention(const float *qkv, int B, int T, int E, int H, float *o, voi
     DotFeatArgs fa{qkv, B, H, T, hd, E, 1.0f / std::sqrt((float)hd), qf, kf, vh, vl, m0, sp, cn, cm};
     {
         ProfScope ps("dot_feat", st);
-        const unsigned grid = (unsigned)((BH * T + DOT_FEAT_WARPS - 1) / DOT_FEAT_WARPS);
+        const long long per_block = (long long)DOT_FEAT_WARPS * DOT_FEAT_ROWS;
+        const unsigned grid = (unsigned)((BH * T + per_block - 1) / per_block);
         dot_feat_kernel<<<grid, DOT_FEAT_WARPS * 32, 0, st>>>(fa);
     }
     if (force_fallback) {
