@@ -741,8 +741,9 @@ def run_dot_workload(args):
     clk = clocks.stop()
     prof = ctx.profile_report()
     ctx.profile(None)
-    if ctx.take_device_error():
-        raise RuntimeError("device error in the timed region")
+    err = ctx.take_device_error()
+    if err:
+        raise RuntimeError(f"device error word {err:#x} in the timed region")
     ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world, dev)
     pairs = B * H * T * (T + 1) // 2
     core_fl = pairs * 2 * 2 * hd                                  # q.k and p.v per causal pair
@@ -911,8 +912,9 @@ def run_prefill_workload(args):
     for _ in range(args.warmup):
         step()
     barrier()
-    if ctx.take_device_error():
-        raise RuntimeError("device error during warm-up")
+    err = ctx.take_device_error()
+    if err:
+        raise RuntimeError(f"device error word {err:#x} during warm-up")
     ctx.profile("attn_tc")
     clocks = Clocks(local)
     clocks.start()
@@ -926,8 +928,9 @@ def run_prefill_workload(args):
     clk = clocks.stop()
     prof = ctx.profile_report()
     ctx.profile(None)
-    if ctx.take_device_error():
-        raise RuntimeError("device error in the timed region")
+    err = ctx.take_device_error()
+    if err:
+        raise RuntimeError(f"device error word {err:#x} in the timed region")
     ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world, dev)
     hbm, bf16, peak_kind = peaks()
     fl = prefill_flops_per_layer(B, T, E, H, hd, C)

@@ -97,6 +97,9 @@ def test_exact_path_matches_oracle(ctx, E, H, C, B, T, init):
     # wraps, the single P buffer is reused, diagonal tiles after j > 0
     (512, 4, 16, 2, 520),
     (4096, 32, 16, 1, 300),
+    # head_dim 128 with 320 work items: the persistent CTAs take two or three
+    # items each, so the single O buffer passes from item to item
+    (512, 4, 16, 16, 640),
 ])
 def test_tensor_path_matches_oracle(ctx, E, H, C, B, T):
     import wave_engine_b200 as wb
@@ -548,6 +551,9 @@ def test_config_fixture_decode(ctx, case, path, tol):
 @pytest.mark.parametrize("E,H,C,T,groups", [
     (768, 12, 16, 130, [(0, 4), (4, 9), (9, 12)]),
     (4096, 32, 16, 40, [(0, 8), (8, 16), (16, 24), (24, 32)]),
+    # the two-GPU split of the 4096-dim model at T = 1024: 256 work items
+    # per range, several per persistent CTA at head_dim 128
+    (4096, 32, 16, 1024, [(0, 16), (16, 32)]),
 ])
 def test_head_ranges_sum_to_the_full_forward(ctx, E, H, C, T, groups):
     """wb_attn_forward_heads over ranges that cover every head once (bias on

@@ -745,8 +745,14 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
             }
             if (!ok) break;
             // the item's row-sum partials; the buffer of item k-2 must have
-            // been read by its epilogue
-            if (k >= 2 && !att_wait(ofree + (k - 2) % L::OBUF, ((k - 2) / L::OBUF) & 1, abort_flag)) {
+            // been read by its epilogue.  A parity wait names one phase of
+            // ofree and must not fall two phases behind: with two O buffers
+            // ofree[k % 2] has completed at most the phase of item k-2 (item
+            // k's epilogue needs these row sums); with one, item k-1's
+            // epilogue may already be done too, so wait for that one (it
+            // follows item k-2's and needs nothing from this item)
+            constexpr int LAG = L::OBUF == 1 ? 1 : 2;
+            if (k >= LAG && !att_wait(ofree + (k - LAG) % L::OBUF, ((k - LAG) / L::OBUF) & 1, abort_flag)) {
                 atomicOr(a.dev_err, WB_DERR_TIMEOUT_SOFTMAX);
                 break;
             }
@@ -1147,54 +1153,91 @@ struct DotFeatArgs {
 
 static constexpr int DOT_FEAT_WARPS = 8;
 
-static constexpr int DOT_FEAT_ROWS = 4;  // rows per warp, their loads issued together
+// DOT_FEAT_ROWS consecutive input rows (b, t..t+R-1) per CTA (fewer when a
+// row is long): their 3E values are one contiguous stretch, read with
+// DOT_FEAT_U 16-byte loads per thread in flight (4-byte loads when the
+// stretch is not 16-byte aligned) into shared memory; then warp w takes heads
+// w, w + 8, ... of every row and raises max |k| of a head once per CTA (the
+// per-row atomics on one address per head serialised in L2 and took more
+// than half of the kernel's time)
+static constexpr int DOT_FEAT_ROWS = 4;
+static constexpr int DOT_FEAT_SMEM = 48 * 1024;
+static int dot_feat_rows(int E) {
+    return std::max(1, std::min(DOT_FEAT_ROWS, DOT_FEAT_SMEM / (3 * E * (int)sizeof(float))));
+}
 
-__global__ void __launch_bounds__(DOT_FEAT_WARPS * 32) dot_feat_kernel(DotFeatArgs a) {
-    const int lane = threadIdx.x & 31;
-    const long long i0 = ((long long)blockIdx.x * DOT_FEAT_WARPS + (threadIdx.x >> 5)) * DOT_FEAT_ROWS;
-    const long long total = (long long)a.B * a.H * a.T;
-    float q[DOT_FEAT_ROWS][2], k[DOT_FEAT_ROWS][2], v[DOT_FEAT_ROWS][2];
+__global__ void __launch_bounds__(DOT_FEAT_WARPS * 32) dot_feat_kernel(DotFeatArgs a, int rows) {
+    extern __shared__ float xs[];  // [rows][3E]
+    constexpr int NT = DOT_FEAT_WARPS * 32;
+    constexpr int U = 4;  // loads per thread per batch
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int n_tb = (a.T + rows - 1) / rows;  // row groups per sequence (a group stays within one)
+    const int b = blockIdx.x / n_tb, t0 = (blockIdx.x - b * n_tb) * rows;
+    const int nr = min(rows, a.T - t0);
+    const int n = 3 * a.E * nr;
+    const float *src_rows = a.qkv + ((long long)b * a.T + t0) * 3LL * a.E;
+    if ((n & 3) == 0 && (reinterpret_cast<uintptr_t>(src_rows) & 15) == 0) {
+        const float4 *src = reinterpret_cast<const float4 *>(src_rows);
+        float4 *dst = reinterpret_cast<float4 *>(xs);
+        const int n4 = n >> 2;
+        for (int j0 = tid; j0 < n4; j0 += U * NT) {
+            float4 r[U];
 #pragma unroll
-    for (int rr = 0; rr < DOT_FEAT_ROWS; rr++) {
-        const long long i = i0 + rr;
-        const long long bh = i / a.T;
-        const int t = (int)(i - bh * a.T);
-        const int b = (int)(bh / a.H), h = (int)(bh - (long long)b * a.H);
-        const float *row = a.qkv + ((long long)b * a.T + t) * 3LL * a.E + (long long)h * a.hd;
+            for (int u = 0; u < U; u++)
+                if (j0 + u * NT < n4) r[u] = __ldg(src + j0 + u * NT);
 #pragma unroll
-        for (int u = 0; u < 2; u++) {
-            const int d = 2 * lane + u;
-            const bool ok = i < total && d < a.hd;
-            q[rr][u] = ok ? __ldg(row + d) * a.scale : 0.0f;
-            k[rr][u] = ok ? __ldg(row + a.E + d) : 0.0f;
-            v[rr][u] = ok ? __ldg(row + 2 * a.E + d) : 0.0f;
+            for (int u = 0; u < U; u++)
+                if (j0 + u * NT < n4) dst[j0 + u * NT] = r[u];
+        }
+    } else {
+        for (int j0 = tid; j0 < n; j0 += U * NT) {
+            float r[U];
+#pragma unroll
+            for (int u = 0; u < U; u++)
+                if (j0 + u * NT < n) r[u] = __ldg(src_rows + j0 + u * NT);
+#pragma unroll
+            for (int u = 0; u < U; u++)
+                if (j0 + u * NT < n) xs[j0 + u * NT] = r[u];
         }
     }
+    __syncthreads();
+    for (int h = warp; h < a.H; h += DOT_FEAT_WARPS) {
+        const long long bh = (long long)b * a.H + h;
+        float kmax = 0.0f;
+        for (int r = 0; r < nr; r++) {
+            const long long i = bh * a.T + t0 + r;  // feature row
+            const float *row = xs + r * 3 * a.E + h * a.hd;
+            float q[2], k[2], v[2];
 #pragma unroll
-    for (int rr = 0; rr < DOT_FEAT_ROWS; rr++) {
-        const long long i = i0 + rr;
-        if (i >= total) break;
-        const long long bh = i / a.T;
-        const float vh0 = f16_round(v[rr][0]), vh1 = f16_round(v[rr][1]);
-        reinterpret_cast<uint32_t *>(a.qf + i * 64)[lane] = pack_bf16(q[rr][0], q[rr][1]);
-        reinterpret_cast<uint32_t *>(a.kf + i * 64)[lane] = pack_bf16(k[rr][0], k[rr][1]);
-        reinterpret_cast<uint32_t *>(a.vh + i * 64)[lane] = pack_f16(vh0, vh1);  // fp16 hi / lo (P is fp16)
-        reinterpret_cast<uint32_t *>(a.vl + i * 64)[lane] = pack_f16(v[rr][0] - vh0, v[rr][1] - vh1);
-        float s = fmaf(q[rr][0], k[rr][0], q[rr][1] * k[rr][1]);
-        float qq = fmaf(q[rr][0], q[rr][0], q[rr][1] * q[rr][1]);
-        float kk = fmaf(k[rr][0], k[rr][0], k[rr][1] * k[rr][1]);
+            for (int u = 0; u < 2; u++) {
+                const int d = 2 * lane + u;
+                const bool ok = d < a.hd;
+                q[u] = ok ? row[d] * a.scale : 0.0f;
+                k[u] = ok ? row[a.E + d] : 0.0f;
+                v[u] = ok ? row[2 * a.E + d] : 0.0f;
+            }
+            const float vh0 = f16_round(v[0]), vh1 = f16_round(v[1]);
+            reinterpret_cast<uint32_t *>(a.qf + i * 64)[lane] = pack_bf16(q[0], q[1]);
+            reinterpret_cast<uint32_t *>(a.kf + i * 64)[lane] = pack_bf16(k[0], k[1]);
+            reinterpret_cast<uint32_t *>(a.vh + i * 64)[lane] = pack_f16(vh0, vh1);  // fp16 hi / lo (P is fp16)
+            reinterpret_cast<uint32_t *>(a.vl + i * 64)[lane] = pack_f16(v[0] - vh0, v[1] - vh1);
+            float s = fmaf(q[0], k[0], q[1] * k[1]);
+            float qq = fmaf(q[0], q[0], q[1] * q[1]);
+            float kk = fmaf(k[0], k[0], k[1] * k[1]);
 #pragma unroll
-        for (int o = 16; o; o >>= 1) {
-            s += __shfl_xor_sync(0xffffffffu, s, o);
-            qq += __shfl_xor_sync(0xffffffffu, qq, o);
-            kk += __shfl_xor_sync(0xffffffffu, kk, o);
+            for (int o = 16; o; o >>= 1) {
+                s += __shfl_xor_sync(0xffffffffu, s, o);
+                qq += __shfl_xor_sync(0xffffffffu, qq, o);
+                kk += __shfl_xor_sync(0xffffffffu, kk, o);
+            }
+            kmax = fmaxf(kmax, sqrtf(kk));
+            if (lane == 0) {
+                a.m0[i] = s;
+                a.sprev[i] = -INFINITY;  // no previous-position rule
+                a.cnorm[i] = sqrtf(qq);
+            }
         }
-        if (lane == 0) {
-            a.m0[i] = s;
-            a.sprev[i] = -INFINITY;  // no previous-position rule
-            a.cnorm[i] = sqrtf(qq);
-            atomicMax(a.cmax + bh, __float_as_uint(sqrtf(kk)));  // non-negative floats order as their bits
-        }
+        if (lane == 0) atomicMax(a.cmax + bh, __float_as_uint(kmax));  // non-negative floats order as their bits
     }
 }
 
@@ -1240,9 +1283,16 @@ int tc_dot_attention(const float *qkv, int B, int T, int E, int H, float *o, voi
     DotFeatArgs fa{qkv, B, H, T, hd, E, 1.0f / std::sqrt((float)hd), qf, kf, vh, vl, m0, sp, cn, cm};
     {
         ProfScope ps("dot_feat", st);
-        const long long per_block = (long long)DOT_FEAT_WARPS * DOT_FEAT_ROWS;
-        const unsigned grid = (unsigned)((BH * T + per_block - 1) / per_block);
-        dot_feat_kernel<<<grid, DOT_FEAT_WARPS * 32, 0, st>>>(fa);
+        const int rows = dot_feat_rows(E);
+        const unsigned grid = (unsigned)((long long)B * ((T + rows - 1) / rows));
+        const size_t smem = (size_t)rows * 3 * E * sizeof(float);
+        if (smem > 48 * 1024 &&
+            cudaFuncSetAttribute(dot_feat_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+                cudaSuccess) {
+            *msg = "n_embd too large for the dot-product feature kernel";
+            return WB_EINVAL;
+        }
+        dot_feat_kernel<<<grid, DOT_FEAT_WARPS * 32, smem, st>>>(fa, rows);
     }
     if (force_fallback) {
         // testing: every tile fails the bound (|q| max|k| - s_self > limit)
