@@ -549,7 +549,7 @@ def run_ours(args):
     out = {
         "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_step, 3), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "fp32 io; bf16 hi/lo + tf32 tensor MMA, fp32 accumulate",
+        "vs_baseline": None, "dtype": "fp32 io; bf16 hi/lo features, fp16 P and values, tf32 projections, fp32 accumulate",
         "data": "synthetic (seeded N(0,0.02) weights, N(0,1) layer inputs)",
         "config": {"workload": WORKLOAD, "n_embd": E, "n_head": H, "head_dim": hd, "layers": L, "batch_per_gpu": B,
                    "seq_len": T, "decode_steps": S, "content_dim": C,
@@ -948,7 +948,7 @@ def run_prefill_workload(args):
            "scaling": ("strong (heads split across ranks: each rank computes its heads and their share of "
                        "out_proj; one NCCL all-reduce of the layer output)") if by_heads else "weak",
            "vs_baseline": None,
-           "dtype": "bf16 split (hi/lo) features and values, fp32 accumulation", "data": "synthetic",
+           "dtype": "bf16 split (hi/lo) features, fp16 P and values, fp32 accumulation", "data": "synthetic",
            "config": {"workload": c["desc"], "inputs": "per-layer inputs resident in HBM"},
            "roofline": {"kernel": "attn_tc", "bound": "tensor", "peak": bf16, "unit": "TFLOP/s",
                         "peak_kind": f"{peak_kind} bf16 dense, burst",

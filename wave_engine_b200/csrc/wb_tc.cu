@@ -46,11 +46,12 @@ namespace wb {
 static constexpr int QT = 128;      // queries per work item (TMEM lanes)
 static constexpr int KT = 128;      // keys per tile
 static constexpr float MASK_BIAS = -512.0f;
-static constexpr float BOUND_LIMIT = 64.0f;
-// dot-product attention: P and the values in fp16 (10-bit mantissa: P is
-// 8x finer than in bf16, which a softmax sharper than wave attention's
-// needs within 2e-3), so P = exp(s - shift) must stay below fp16's 65504
-static constexpr float DOT_BOUND_LIMIT = 10.0f;
+// P and the values enter the PV products in fp16 (11-bit significand: P and
+// a value each carry a relative rounding error of at most 2^-11, 8x finer
+// than bf16), so P = exp(s - shift) must stay below fp16's 65504: a tile
+// whose scores may exceed the fixed shift by more than this goes to the fp32
+// fallback
+static constexpr float BOUND_LIMIT = 10.0f;
 
 // ---------------------------------------------------------------------------
 // Tensor maps (driver entry point fetched at run time; no libcuda link).
@@ -98,7 +99,7 @@ struct FeatArgs {
     int B, H, T, hd, hdp;
     int Hg, h0;                   // heads computed: h0 .. h0 + Hg - 1 (rows bh = b * Hg + (h - h0))
     __nv_bfloat16 *qf, *kf;       // [BH][T][FW]
-    __nv_bfloat16 *vh, *vl;       // [BH][T][hdp] value hi / lo
+    __half *vh;                   // [BH][T][hdp] values (fp16)
     float *m0, *sprev, *cnorm;    // [BH][T]
     unsigned int *cmax;           // [BH], float bits
 };
@@ -205,7 +206,7 @@ __global__ void __launch_bounds__(FEAT_WARPS * 32) feat_kernel(FeatArgs a) {
         emit(a.kf);
     }
 
-    // ---- values: hi and lo, zero padded to hdp; lanes along the row
+    // ---- values in fp16, zero padded to hdp; lanes along the row
     {
         const int hd = a.hd, hdp = a.hdp;
         const int nrows = (int)min(32LL, total - i0);
@@ -238,9 +239,7 @@ __global__ void __launch_bounds__(FEAT_WARPS * 32) feat_kernel(FeatArgs a) {
                     if (col >= hdp) continue;
                     const float2 x2 = v[u][q];
                     const long long o = (i0 + j) * hdp + col;
-                    *reinterpret_cast<uint32_t *>(a.vh + o) = pack_bf16(x2.x, x2.y);
-                    *reinterpret_cast<uint32_t *>(a.vl + o) =
-                        pack_bf16(x2.x - bf16_round(x2.x), x2.y - bf16_round(x2.y));
+                    *reinterpret_cast<uint32_t *>(a.vh + o) = pack_f16(x2.x, x2.y);
                 }
             }
         }
@@ -302,9 +301,9 @@ __global__ void __launch_bounds__(FEAT_WARPS * 32) feat_kernel(FeatArgs a) {
 // an atomic counter, in groups of ATT_GROUP (sequence, head) rows, the
 // longest query tiles of a group first (a group's key/value tiles stay in
 // L2 while its items read them).  Per key tile j of an item (keys
-// 128j..128j+127): S = Qf Kf_j^T (TMEM, fp32) -> P = exp(S - s_self) (bf16,
+// 128j..128j+127): S = Qf Kf_j^T (TMEM, fp32) -> P = exp(S - s_self) (fp16,
 // written back into the first half of each thread's own S columns) ->
-// O += P V_j (A from TMEM, V hi and lo from shared memory).
+// O += P V_j (A from TMEM, the fp16 value tile from shared memory).
 // ---------------------------------------------------------------------------
 struct AttnTcArgs {
     int BH, H, T, hd, n_qt;     // BH = B * Hg rows
@@ -345,11 +344,14 @@ struct AttnItem {
 
 template <int HDP, int FW>
 struct AttnSmem {
-    static constexpr int ST = HDP == 128 ? 2 : (FW == 16 ? 4 : 3);  // K/V ring stages
     static constexpr int Q_BYTES = QT * FW * 2;      // 4 / 16 KB
     static constexpr int K_BYTES = KT * FW * 2;      // 4 / 16 KB
-    static constexpr int VPART = KT * HDP * 2;       // one bf16 value tile: 16 / 32 KB
-    static constexpr int V_BYTES = 2 * VPART;        // hi + lo
+    static constexpr int V_BYTES = KT * HDP * 2;     // one fp16 value tile: 16 / 32 KB
+    static constexpr int FIXED = 2 * Q_BYTES + ATT_EPI_WARPS * 32 * 33 * 4 + ATT_SLOTS * (int)sizeof(AttnItem) +
+                                 2 * 4 * QT * 4 + 512 + 16 + 1024;
+    // K/V ring stages: as many as shared memory holds, at most 6
+    static constexpr int ST_FIT = (232448 - FIXED) / (K_BYTES + V_BYTES);
+    static constexpr int ST = ST_FIT < 6 ? ST_FIT : 6;
     static constexpr int OFF_Q = 0;                  // two Q buffers (items alternate)
     static constexpr int OFF_K = OFF_Q + 2 * Q_BYTES;
     static constexpr int OFF_V = OFF_K + ST * K_BYTES;
@@ -357,17 +359,21 @@ struct AttnSmem {
     static constexpr int OFF_SLOT = OFF_EPI + ATT_EPI_WARPS * 32 * 33 * 4;
     static constexpr int OFF_LSUM = OFF_SLOT + ATT_SLOTS * (int)sizeof(AttnItem);  // [2][4][QT] row-sum partials
     static constexpr int OFF_BAR = OFF_LSUM + 2 * 4 * QT * 4;
-    // barriers: qfull[2], qfree[2], kvfull[ST], kvfree[ST], sfull[2], pready[2],
+    // TMEM columns: NS score buffers of 128 columns (P(g) is written over the
+    // first half of each thread's S(g) columns), then OBUF O buffers of HDP
+    // columns: three S buffers let QK run two tiles ahead of the PV that
+    // frees a buffer
+    static constexpr int NS = 3;
+    static constexpr int O_COL = NS * 128;
+    static constexpr int OBUF = (512 - O_COL) / HDP >= 2 ? 2 : 1;
+    // barriers: qfull[2], qfree[2], kvfull[ST], kvfree[ST], sfull[NS], pready[NS],
     // ofull[2], ofree[2], lready[2], itemfull[SLOTS], itemfree[SLOTS], mmadone
-    static constexpr int NBAR = 4 + 2 * ST + 10 + 2 * ATT_SLOTS + 1;
-    // TMEM columns: S0 [0,128), S1 [128,256) (P(g) is written over the first
-    // half of each thread's S(g) columns), then OBUF O buffers of 2*HDP
-    // columns: the value-hi products in the first HDP, value-lo in the rest
-    static constexpr int OBUF = HDP == 64 ? 2 : 1;
-    static constexpr int O_COL = 256;
+    static constexpr int NBAR = 4 + 2 * ST + 2 * NS + 6 + 2 * ATT_SLOTS + 1;
     static constexpr int BYTES = OFF_BAR + NBAR * 8 + 16 + 1024;  // + TMEM slot, alignment slack
+    static_assert(ST >= 2, "attention K/V ring below two stages");
+    static_assert(NBAR * 8 <= 512, "barrier space");
     static_assert(BYTES <= 232448, "attention shared memory above the 227 KB limit");
-    static_assert(O_COL + OBUF * 2 * HDP <= 512, "TMEM: two S and OBUF O buffers");
+    static_assert(O_COL + OBUF * HDP <= 512, "TMEM: NS S and OBUF O buffers");
 };
 
 // Bounded mbarrier wait that also gives up once another role has raised the
@@ -389,7 +395,7 @@ __device__ __forceinline__ bool att_wait(uint64_t *bar, uint32_t parity, volatil
 //   warps 0-15 (softmax): four per TMEM lane group (warps w, w+4, w+8, w+12
 //     own query rows 32(w&3)..+31, key columns 0-31, 32-63, 64-95, 96-127 of
 //     each S tile): P = exp2 of the fixed shift, causal mask on the diagonal
-//     tile, P (bf16) stored over the first 16 of the thread's own 32 S
+//     tile, P (fp16) stored over the first 16 of the thread's own 32 S
 //     columns; the row-sum partials go to shared memory per item.
 //   warps 16-19 (epilogue): one per lane group: O / l plus the exact
 //     previous-position term, stored through per-warp staging -- item k's
@@ -399,13 +405,13 @@ __device__ __forceinline__ bool att_wait(uint64_t *bar, uint32_t parity, volatil
 //     bounded-score condition (content only; failing tiles go to the
 //     fallback list), publishes the item (row, tile, m0 and previous-position
 //     scores of its 128 rows), then loads Q and the K/V tiles by TMA.
-//   warp 21 (MMA): lane 0 issues S_g = Qf Kf^T two tiles ahead of the
-//     softmax (S double buffered in TMEM) and O += P V (value hi and lo).
-// TMEM columns: S0 [0,128), S1 [128,256), O0 [256,256+HDP), O1 after it.
-template <int HDP, int FW, bool P16>
+//   warp 21 (MMA): lane 0 issues S_g = Qf Kf^T up to three tiles ahead of
+//     the softmax (three S buffers in TMEM) and O += P V.
+// TMEM columns: S0 [0,128), S1 [128,256), S2 [256,384), then the O buffers.
+template <int HDP, int FW>
 __global__ void __launch_bounds__(ATT_THREADS, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                   const __grid_constant__ CUtensorMap tm_vh, const __grid_constant__ CUtensorMap tm_vl,
+                   const __grid_constant__ CUtensorMap tm_v,
                    AttnTcArgs a) {
     using L = AttnSmem<HDP, FW>;
     constexpr int ST = L::ST;
@@ -414,7 +420,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     uint64_t *bars = reinterpret_cast<uint64_t *>(sm + L::OFF_BAR);
     uint64_t *qfull = bars, *qfree = bars + 2;
     uint64_t *kvfull = bars + 4, *kvfree = kvfull + ST;
-    uint64_t *sfull = kvfree + ST, *pready = sfull + 2, *ofull = pready + 2, *ofree = ofull + 2;
+    constexpr int NS = L::NS;
+    uint64_t *sfull = kvfree + ST, *pready = sfull + NS, *ofull = pready + NS, *ofree = ofull + 2;
     uint64_t *lready = ofree + 2, *itemfull = lready + 2, *itemfree = itemfull + ATT_SLOTS;
     uint64_t *mmadone = itemfree + ATT_SLOTS;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mmadone + 1);
@@ -428,7 +435,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         for (int i = 0; i < L::NBAR; i++) {
             uint64_t *bb = bars + i;
             uint32_t cnt = 1;
-            if (bb == pready || bb == pready + 1) cnt = ATT_SOFTMAX_WARPS / 2 * 32;  // one softmax group per tile
+            if (bb >= pready && bb < pready + NS) cnt = ATT_SOFTMAX_WARPS / 2 * 32;  // one softmax group per tile
             else if (bb == lready || bb == lready + 1) cnt = ATT_SOFTMAX_WARPS * 32;
             else if (bb == ofree || bb == ofree + 1) cnt = ATT_EPI_WARPS * 32;
             else if (bb >= itemfull && bb < itemfull + ATT_SLOTS) cnt = 32;
@@ -457,8 +464,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         if (lane == 0) {
             ptx::prefetch_tmap(&tm_q);
             ptx::prefetch_tmap(&tm_k);
-            ptx::prefetch_tmap(&tm_vh);
-            ptx::prefetch_tmap(&tm_vl);
+            ptx::prefetch_tmap(&tm_v);
         }
         for (;;) {
             int item = 0;
@@ -536,10 +542,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                     ptx::tma_load_3d(sm + L::OFF_K + st * L::K_BYTES, &tm_k, kvfull + st, 0, j * KT, bh);
                     uint8_t *vst = sm + L::OFF_V + st * L::V_BYTES;
 #pragma unroll
-                    for (int c = 0; c < HDP / 64; c++) {
-                        ptx::tma_load_3d(vst + c * (KT * 128), &tm_vh, kvfull + st, c * 64, j * KT, bh);
-                        ptx::tma_load_3d(vst + L::VPART + c * (KT * 128), &tm_vl, kvfull + st, c * 64, j * KT, bh);
-                    }
+                    for (int c = 0; c < HDP / 64; c++)
+                        ptx::tma_load_3d(vst + c * (KT * 128), &tm_v, kvfull + st, c * 64, j * KT, bh);
                 }
                 if (!ok) atomicOr(a.dev_err, WB_DERR_TIMEOUT_TMA);
             }
@@ -557,9 +561,9 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         // ---------------- MMA issuer
         if (lane == 0) {
             constexpr uint32_t IDESC_QK = ptx::idesc_bf16(128, 128, 0, 0);
-            // PV: N = 2*HDP, the value hi and lo tiles side by side (adjacent
-            // 64-column atoms of the stage), O hi | O lo
-            constexpr uint32_t IDESC_PV = P16 ? ptx::idesc_f16(128, 2 * HDP, 0, 1) : ptx::idesc_bf16(128, 2 * HDP, 0, 1);
+            // PV: fp16 P (TMEM) x the fp16 value tile (HDP/64 adjacent
+            // 64-column atoms of the stage, MN-major), N = HDP
+            constexpr uint32_t IDESC_PV = ptx::idesc_f16(128, HDP, 0, 1);
             const uint32_t sQ0 = ptx::smem_u32(sm + L::OFF_Q);
             int kq = 0, jq = 0;                // next QK: item, tile
             long long gq = 0, gp = 0;          // next QK / PV global tile
@@ -568,10 +572,10 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
             // Event loop: issue whichever of PV(gp) and QK(gq) has its inputs
             // ready (non-blocking barrier tests), PV first.  Each tcgen05.mma
             // costs the issuing thread far more than its tensor work at these
-            // sizes, so a tile is 8 PV MMAs (N = 2*HDP) and FW/16 QK MMAs, and
+            // sizes, so a tile is 8 PV MMAs (N = HDP) and FW/16 QK MMAs, and
             // the thread never blocks on one operation while the other could
-            // go.  QK(gq) writes S buffer gq & 1, which holds P(gq - 2) until
-            // PV(gq - 2) is issued (the tensor pipe executes in issue order).
+            // go.  QK(gq) writes S buffer gq % NS, which holds P(gq - NS) until
+            // PV(gq - NS) is issued (the tensor pipe executes in issue order).
             int qstate = 0;  // QK(gq): 0 item descriptor, 1 Q tile, 2 S buffer, 3 K/V tile
             long long t_last = clock64();
             while (ok) {
@@ -582,11 +586,11 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                     const int ob = kp % L::OBUF;
                     const bool ready =
                         (jp != 0 || kp < L::OBUF || ptx::mbar_test(ofree + ob, ((kp - L::OBUF) / L::OBUF) & 1)) &&
-                        ptx::mbar_test(pready + (gp & 1), (uint32_t)((gp >> 1) & 1));
+                        ptx::mbar_test(pready + (int)(gp % NS), (uint32_t)((gp / NS) & 1));
                     if (ready) {
                         ptx::tc_fence_after();
-                        const uint32_t O_t = tmem + L::O_COL + (uint32_t)(ob * 2 * HDP);
-                        const uint32_t P_t = tmem + (uint32_t)((gp & 1) * 128);
+                        const uint32_t O_t = tmem + L::O_COL + (uint32_t)(ob * HDP);
+                        const uint32_t P_t = tmem + (uint32_t)((gp % NS) * 128);
                         const uint64_t vd0 = ptx::smem_desc(ptx::smem_u32(sm + L::OFF_V + (int)(gp % ST) * L::V_BYTES),
                                                             KT * 128, 1024, ptx::UMMA_SW128);
 #pragma unroll
@@ -617,20 +621,20 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                         qstate = 2;
                     }
                     if (qstate == 1 && ptx::mbar_test(qfull + (kq & 1), (kq >> 1) & 1)) qstate = 2;
-                    // S buffer gq & 1 holds P(gq - 2) until PV(gq - 2) is issued; the
-                    // tensor pipe runs QK(gq) after it in issue order
-                    if (qstate == 2 && gq <= gp + 1) qstate = 3;
+                    // S buffer gq % NS holds P(gq - NS) until PV(gq - NS) is issued;
+                    // the tensor pipe runs QK(gq) after it in issue order
+                    if (qstate == 2 && gq <= gp + (NS - 1)) qstate = 3;
                     if (qstate == 3 && ptx::mbar_test(kvfull + (int)(gq % ST), (uint32_t)((gq / ST) & 1))) {
                         ptx::tc_fence_after();
                         const int st = (int)(gq % ST);
                         const uint32_t sK = ptx::smem_u32(sm + L::OFF_K + st * L::K_BYTES);
-                        const uint32_t S_t = tmem + (uint32_t)((gq & 1) * 128);
+                        const uint32_t S_t = tmem + (uint32_t)((gq % NS) * 128);
                         const uint32_t sQ = sQ0 + (uint32_t)((kq & 1) * L::Q_BYTES);
                         const uint64_t ad0 = ptx::smem_desc(sQ, 16, F_SBO, F_SW), bd0 = ptx::smem_desc(sK, 16, F_SBO, F_SW);
 #pragma unroll
                         for (int kk = 0; kk < FW / 16; kk++)
                             ptx::mma_bf16(S_t, ad0 + (uint64_t)(kk * 2), bd0 + (uint64_t)(kk * 2), IDESC_QK, kk > 0);
-                        ptx::mma_commit(sfull + (gq & 1));
+                        ptx::mma_commit(sfull + (int)(gq % NS));
                         gq++;
                         if (++jq == slots[kq % ATT_SLOTS].qt + 1) {
                             ptx::mma_commit(qfree + (kq & 1));  // Q of item kq no longer read
@@ -658,9 +662,10 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     } else if (warp < ATT_SOFTMAX_WARPS) {
         // ---------------- softmax: two groups of 8 warps take the key tiles
         // in turn (group G the tiles g with g % 2 == G of the CTA's tile
-        // sequence), so one group's exponentials overlap the other's waits;
-        // within a group two warps per TMEM lane group each own 64 key
-        // columns, processed as two 32-column chunks
+        // sequence; tile g sits in S buffer g % NS), so one group's
+        // exponentials overlap the other's waits; within a group two warps
+        // per TMEM lane group each own 64 key columns, processed as two
+        // 32-column chunks
         const float LOG2E = 1.4426950408889634f;
         const int row = tid & (QT - 1);
         const int grp = warp >> 3, half = (warp >> 2) & 1;
@@ -688,14 +693,15 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
             bool ok = true;
             for (int j = 0; j <= qt; j++, g++) {
                 if ((int)(g & 1) != grp) continue;
-                if (!att_wait(sfull + grp, (uint32_t)((g >> 1) & 1), abort_flag)) {
+                const int sb = (int)(g % NS);
+                if (!att_wait(sfull + sb, (uint32_t)((g / NS) & 1), abort_flag)) {
                     atomicOr(a.dev_err, WB_DERR_TIMEOUT_SOFTMAX);
                     ok = false;
                     break;
                 }
                 ptx::tc_fence_after();
                 const bool diag = (j == qt);
-                const uint32_t S_t = tmem + (uint32_t)(grp * 128 + half * 64) + lane_base;
+                const uint32_t S_t = tmem + (uint32_t)(sb * 128 + half * 64) + lane_base;
                 uint32_t pk0[16], pk1[16];
                 auto exps = [&](const uint32_t (&r)[32], uint32_t (&pk)[16], int kbase) {
                     int pcol = -1;
@@ -715,7 +721,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                             if (2 * i == pcol) e0 = ep;
                             if (2 * i + 1 == pcol) e1 = ep;
                             l += e0 + e1;
-                            pk[i] = P16 ? pack_f16(e0, e1) : pack_bf16(e0, e1);
+                            pk[i] = pack_f16(e0, e1);
                         }
                     } else {
 #pragma unroll
@@ -723,7 +729,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                             const float e0 = fast_exp2(fmaf(__uint_as_float(r[2 * i]), LOG2E, nm0));
                             const float e1 = fast_exp2(fmaf(__uint_as_float(r[2 * i + 1]), LOG2E, nm0));
                             l += e0 + e1;
-                            pk[i] = P16 ? pack_f16(e0, e1) : pack_bf16(e0, e1);
+                            pk[i] = pack_f16(e0, e1);
                         }
                     }
                 };
@@ -741,7 +747,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                 ptx::tmem_st16(S_t + 16, pk1);
                 ptx::tmem_st_wait();
                 ptx::tc_fence_before();
-                ptx::mbar_arrive(pready + grp);
+                ptx::mbar_arrive(pready + sb);
             }
             if (!ok) break;
             // the item's row-sum partials; the buffer of item k-2 must have
@@ -786,15 +792,14 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
             ptx::tc_fence_after();
             const float *ls = lsum + (k & 1) * 4 * QT + row;
             const float inv = 1.0f / ((ls[0] + ls[QT]) + (ls[2 * QT] + ls[3 * QT]));
-            const uint32_t O_t = tmem + L::O_COL + (uint32_t)((k % L::OBUF) * 2 * HDP) + lane_base;
+            const uint32_t O_t = tmem + L::O_COL + (uint32_t)((k % L::OBUF) * HDP) + lane_base;
             float *orow0 = a.o + ((long long)b * a.T + q0) * a.E + (long long)h * a.hd;
             const int nrow = min(32, a.T - q0);
 #pragma unroll 1
             for (int c = 0; c < HDP / 32; c++) {
-                // 32 output columns: value-hi products + value-lo products
-                uint32_t r[32], rl[32];
+                // 32 output columns
+                uint32_t r[32];
                 ptx::tmem_ld32(O_t + c * 32, r);
-                ptx::tmem_ld32(O_t + HDP + c * 32, rl);
                 ptx::tmem_ld_wait();
                 if (c == HDP / 32 - 1) {
                     // O buffer and row sums read: the MMA and softmax may reuse them
@@ -802,8 +807,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                     ptx::mbar_arrive(ofree + k % L::OBUF);
                 }
 #pragma unroll
-                for (int i = 0; i < 32; i++)
-                    r[i] = __float_as_uint((__uint_as_float(r[i]) + __uint_as_float(rl[i])) * inv);
+                for (int i = 0; i < 32; i++) r[i] = __float_as_uint(__uint_as_float(r[i]) * inv);
                 warp_stage32(buf, r, lane);
                 const int d = c * 32 + lane;
                 if (d < a.hd)
@@ -965,7 +969,7 @@ void tc_layer_free(TcLayerWeights *t) {
 
 // Workspace pieces of the attention core, carved after `off`.
 struct CoreLayout {
-    size_t qf, kf, vh, vl, m0, sp, cn, cm, sched, o, end;
+    size_t qf, kf, vh, m0, sp, cn, cm, sched, o, end;
 };
 static int core_fw(bool content) { return content ? 64 : 16; }
 static CoreLayout core_layout(const TcLayerWeights &t, int B, int T, size_t off, int Hg, bool content) {
@@ -978,8 +982,7 @@ static CoreLayout core_layout(const TcLayerWeights &t, int B, int T, size_t off,
     CoreLayout c;
     c.qf = cv.take<__nv_bfloat16>(BH * T * fw);
     c.kf = cv.take<__nv_bfloat16>(BH * T * fw);
-    c.vh = cv.take<__nv_bfloat16>(BH * T * hdp);
-    c.vl = cv.take<__nv_bfloat16>(BH * T * hdp);
+    c.vh = cv.take<__half>(BH * T * hdp);
     c.m0 = cv.take<float>(BH * T);
     c.sp = cv.take<float>(BH * T);
     c.cn = cv.take<float>(BH * T);
@@ -1037,15 +1040,14 @@ static int launch_gemm(bool tf32, const void *A, const void *W, const float *bia
     return WB_OK;
 }
 
-template <int HDP, int FW, bool P16 = false>
-static int launch_attn_tc(const CUtensorMap &tq, const CUtensorMap &tk, const CUtensorMap &tvh,
-                          const CUtensorMap &tvl, const AttnTcArgs &aa, int sm_count, cudaStream_t st,
-                          std::string *msg) {
+template <int HDP, int FW>
+static int launch_attn_tc(const CUtensorMap &tq, const CUtensorMap &tk, const CUtensorMap &tv, const AttnTcArgs &aa,
+                          int sm_count, cudaStream_t st, std::string *msg) {
     using L = AttnSmem<HDP, FW>;
     const int grid = std::max(1, std::min(aa.n_items, sm_count));
     ProfScope ps("attn_tc", st);
-    cudaFuncSetAttribute(attn_tc_kernel<HDP, FW, P16>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES);
-    attn_tc_kernel<HDP, FW, P16><<<grid, ATT_THREADS, L::BYTES, st>>>(tq, tk, tvh, tvl, aa);
+    cudaFuncSetAttribute(attn_tc_kernel<HDP, FW>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES);
+    attn_tc_kernel<HDP, FW><<<grid, ATT_THREADS, L::BYTES, st>>>(tq, tk, tv, aa);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         *msg = std::string("attention launch failed: ") + cudaGetErrorString(e);
@@ -1073,7 +1075,7 @@ static int tc_attention_core(const TcLayerWeights &t, const WbSeqView &sv, const
     int rc;
     char *w = (char *)ws->p;
     __nv_bfloat16 *qf = (__nv_bfloat16 *)(w + lay.qf), *kf = (__nv_bfloat16 *)(w + lay.kf);
-    __nv_bfloat16 *vh = (__nv_bfloat16 *)(w + lay.vh), *vl = (__nv_bfloat16 *)(w + lay.vl);
+    __half *vh = (__half *)(w + lay.vh);
     float *ob = (float *)(w + lay.o);
     float *m0 = (float *)(w + lay.m0), *sp = (float *)(w + lay.sp), *cn = (float *)(w + lay.cn);
     unsigned int *cm = (unsigned int *)(w + lay.cm);
@@ -1085,7 +1087,7 @@ static int tc_attention_core(const TcLayerWeights &t, const WbSeqView &sv, const
     }
     const float cscale = content ? 1.0f / std::sqrt((float)t.C) : 0.0f;
     FeatArgs fa{sv, content, content ? t.C : 0, cscale, t.harmonic_n, B, H, T, hd, hdp, Hg, h0,
-                qf, kf, vh, vl, m0, sp, cn, cm};
+                qf, kf, vh, m0, sp, cn, cm};
     const unsigned fgrid = (unsigned)((BH * T + FEAT_WARPS * 32 - 1) / (FEAT_WARPS * 32));
     {
         ProfScope ps("feat", st);
@@ -1093,7 +1095,7 @@ static int tc_attention_core(const TcLayerWeights &t, const WbSeqView &sv, const
         else feat_kernel<16><<<fgrid, FEAT_WARPS * 32, 0, st>>>(fa);
     }
 
-    CUtensorMap tq, tk, tvh, tvl;
+    CUtensorMap tq, tk, tv;
     {
         const uint64_t dims[3] = {(uint64_t)fw, (uint64_t)T, (uint64_t)BH};
         const uint64_t strides[2] = {(uint64_t)fw * 2, (uint64_t)T * fw * 2};
@@ -1104,21 +1106,18 @@ static int tc_attention_core(const TcLayerWeights &t, const WbSeqView &sv, const
         const uint64_t vdims[3] = {(uint64_t)hdp, (uint64_t)T, (uint64_t)BH};
         const uint64_t vstr[2] = {(uint64_t)hdp * 2, (uint64_t)T * hdp * 2};
         const uint32_t vbox[3] = {64, 128, 1};
-        if ((rc = make_tmap(&tvh, vh, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, vdims, vstr, vbox,
-                            CU_TENSOR_MAP_SWIZZLE_128B, msg)))
-            return rc;
-        if ((rc = make_tmap(&tvl, vl, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, vdims, vstr, vbox,
+        if ((rc = make_tmap(&tv, vh, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, vdims, vstr, vbox,
                             CU_TENSOR_MAP_SWIZZLE_128B, msg)))
             return rc;
     }
     AttnTcArgs aa{(int)BH, H, T, hd, n_qt, Hg, h0, (int)(BH * n_qt), m0, sp, cn, cm, sv, ob, E, sched, dev_err, 0,
                   BOUND_LIMIT};
     if (hdp == 64)
-        rc = fw == 64 ? launch_attn_tc<64, 64>(tq, tk, tvh, tvl, aa, sm_count, st, msg)
-                      : launch_attn_tc<64, 16>(tq, tk, tvh, tvl, aa, sm_count, st, msg);
+        rc = fw == 64 ? launch_attn_tc<64, 64>(tq, tk, tv, aa, sm_count, st, msg)
+                      : launch_attn_tc<64, 16>(tq, tk, tv, aa, sm_count, st, msg);
     else
-        rc = fw == 64 ? launch_attn_tc<128, 64>(tq, tk, tvh, tvl, aa, sm_count, st, msg)
-                      : launch_attn_tc<128, 16>(tq, tk, tvh, tvl, aa, sm_count, st, msg);
+        rc = fw == 64 ? launch_attn_tc<128, 64>(tq, tk, tv, aa, sm_count, st, msg)
+                      : launch_attn_tc<128, 16>(tq, tk, tv, aa, sm_count, st, msg);
     if (rc) return rc;
     // query tiles whose scores may exceed the fixed-shift bound (content
     // only): recomputed in fp32 from the list the attention kernel built
@@ -1137,7 +1136,7 @@ static int tc_attention_core(const TcLayerWeights &t, const WbSeqView &sv, const
 // Dot-product attention on the same core (compute.rs:357-414): per row
 // i = (b * H + h) * T + t, Qf = bf16(q / sqrt(d)) and Kf = bf16(k) padded
 // with zeros to 64 columns (no bucket columns: nothing is masked but the
-// causal triangle), values as fp16 hi / lo, and the fixed shift = the fp32
+// causal triangle), values in fp16, and the fixed shift = the fp32
 // self score q.k_t / sqrt(d), which every row contains.  A score exceeds
 // the shift by at most |q| max_k|k| / sqrt(d) - s_self; query tiles where
 // that passes the bound go to the fp32 core through the fallback list.
@@ -1146,7 +1145,8 @@ struct DotFeatArgs {
     const float *qkv;  // [B*T][3E]
     int B, H, T, hd, E;
     float scale;
-    __nv_bfloat16 *qf, *kf, *vh, *vl;  // [BH][T][64]
+    __nv_bfloat16 *qf, *kf;  // [BH][T][64]
+    __half *vh;              // [BH][T][64] values (fp16)
     float *m0, *sprev, *cnorm;         // [BH][T]
     unsigned int *cmax;                // [BH], float bits of max |k|
 };
@@ -1155,7 +1155,7 @@ static constexpr int DOT_FEAT_WARPS = 8;
 
 // DOT_FEAT_ROWS consecutive input rows (b, t..t+R-1) per CTA (fewer when a
 // row is long): their 3E values are one contiguous stretch, read with
-// DOT_FEAT_U 16-byte loads per thread in flight (4-byte loads when the
+// four 16-byte loads per thread in flight (4-byte loads when the
 // stretch is not 16-byte aligned) into shared memory; then warp w takes heads
 // w, w + 8, ... of every row and raises max |k| of a head once per CTA (the
 // per-row atomics on one address per head serialised in L2 and took more
@@ -1216,11 +1216,9 @@ __global__ void __launch_bounds__(DOT_FEAT_WARPS * 32) dot_feat_kernel(DotFeatAr
                 k[u] = ok ? row[a.E + d] : 0.0f;
                 v[u] = ok ? row[2 * a.E + d] : 0.0f;
             }
-            const float vh0 = f16_round(v[0]), vh1 = f16_round(v[1]);
             reinterpret_cast<uint32_t *>(a.qf + i * 64)[lane] = pack_bf16(q[0], q[1]);
             reinterpret_cast<uint32_t *>(a.kf + i * 64)[lane] = pack_bf16(k[0], k[1]);
-            reinterpret_cast<uint32_t *>(a.vh + i * 64)[lane] = pack_f16(vh0, vh1);  // fp16 hi / lo (P is fp16)
-            reinterpret_cast<uint32_t *>(a.vl + i * 64)[lane] = pack_f16(v[0] - vh0, v[1] - vh1);
+            reinterpret_cast<uint32_t *>(a.vh + i * 64)[lane] = pack_f16(v[0], v[1]);
             float s = fmaf(q[0], k[0], q[1] * k[1]);
             float qq = fmaf(q[0], q[0], q[1] * q[1]);
             float kk = fmaf(k[0], k[0], k[1] * k[1]);
@@ -1271,7 +1269,7 @@ int tc_dot_attention(const float *qkv, int B, int T, int E, int H, float *o, voi
     const CoreLayout lay = core_layout(t, B, T, 0, H, true);
     char *w = (char *)ws;
     __nv_bfloat16 *qf = (__nv_bfloat16 *)(w + lay.qf), *kf = (__nv_bfloat16 *)(w + lay.kf);
-    __nv_bfloat16 *vh = (__nv_bfloat16 *)(w + lay.vh), *vl = (__nv_bfloat16 *)(w + lay.vl);
+    __half *vh = (__half *)(w + lay.vh);
     float *m0 = (float *)(w + lay.m0), *sp = (float *)(w + lay.sp), *cn = (float *)(w + lay.cn);
     unsigned int *cm = (unsigned int *)(w + lay.cm);
     int *sched = (int *)(w + lay.sched);
@@ -1280,7 +1278,7 @@ int tc_dot_attention(const float *qkv, int B, int T, int E, int H, float *o, voi
         *msg = "cudaMemsetAsync failed";
         return WB_ECUDA;
     }
-    DotFeatArgs fa{qkv, B, H, T, hd, E, 1.0f / std::sqrt((float)hd), qf, kf, vh, vl, m0, sp, cn, cm};
+    DotFeatArgs fa{qkv, B, H, T, hd, E, 1.0f / std::sqrt((float)hd), qf, kf, vh, m0, sp, cn, cm};
     {
         ProfScope ps("dot_feat", st);
         const int rows = dot_feat_rows(E);
@@ -1302,7 +1300,7 @@ int tc_dot_attention(const float *qkv, int B, int T, int E, int H, float *o, voi
         }
     }
     int rc;
-    CUtensorMap tq, tk, tvh, tvl;
+    CUtensorMap tq, tk, tv;
     {
         const uint64_t dims[3] = {64, (uint64_t)T, (uint64_t)BH};
         const uint64_t strides[2] = {128, (uint64_t)T * 128};
@@ -1311,16 +1309,14 @@ int tc_dot_attention(const float *qkv, int B, int T, int E, int H, float *o, voi
                             CU_TENSOR_MAP_SWIZZLE_128B, msg)) ||
             (rc = make_tmap(&tk, kf, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, dims, strides, box,
                             CU_TENSOR_MAP_SWIZZLE_128B, msg)) ||
-            (rc = make_tmap(&tvh, vh, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, dims, strides, box,
-                            CU_TENSOR_MAP_SWIZZLE_128B, msg)) ||
-            (rc = make_tmap(&tvl, vl, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, dims, strides, box,
+            (rc = make_tmap(&tv, vh, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, dims, strides, box,
                             CU_TENSOR_MAP_SWIZZLE_128B, msg)))
             return rc;
     }
     WbSeqView none{};
     AttnTcArgs aa{(int)BH, H, T, hd, n_qt, H, 0, (int)(BH * n_qt), m0, sp, cn, cm, none, o, E, sched, dev_err, 1,
-                  DOT_BOUND_LIMIT};
-    if ((rc = launch_attn_tc<64, 64, true>(tq, tk, tvh, tvl, aa, sm_count, st, msg))) return rc;
+                  BOUND_LIMIT};
+    if ((rc = launch_attn_tc<64, 64>(tq, tk, tv, aa, sm_count, st, msg))) return rc;
     return launch_dot_attn_tiles(qkv, B, T, E, H, o, sched + 1, (int)(BH * n_qt), st, msg);
 }
 
