@@ -329,8 +329,9 @@ __device__ __forceinline__ float fast_exp2(float x) {
 static constexpr int ATT_SOFTMAX_WARPS = 16;  // four per TMEM lane group
 static constexpr int ATT_EPI_WARPS = 4;       // one per TMEM lane group
 static constexpr int ATT_W_PROD = ATT_SOFTMAX_WARPS + ATT_EPI_WARPS;  // TMA + work items
-static constexpr int ATT_W_MMA = ATT_W_PROD + 1;
-static constexpr int ATT_THREADS = (ATT_W_MMA + 1) * 32;              // 704
+static constexpr int ATT_W_MMA = ATT_W_PROD + 1;                      // PV issuer (and TMEM owner)
+static constexpr int ATT_W_QK = ATT_W_MMA + 1;                        // QK issuer
+static constexpr int ATT_THREADS = (ATT_W_QK + 1) * 32;               // 736
 static constexpr int ATT_GROUP = 16;          // (sequence, head) rows per item group
 static constexpr int ATT_SLOTS = 4;           // work-item descriptor ring
 
@@ -367,8 +368,9 @@ struct AttnSmem {
     static constexpr int O_COL = NS * 128;
     static constexpr int OBUF = (512 - O_COL) / HDP >= 2 ? 2 : 1;
     // barriers: qfull[2], qfree[2], kvfull[ST], kvfree[ST], sfull[NS], pready[NS],
-    // ofull[2], ofree[2], lready[2], itemfull[SLOTS], itemfree[SLOTS], mmadone
-    static constexpr int NBAR = 4 + 2 * ST + 2 * NS + 6 + 2 * ATT_SLOTS + 1;
+    // ofull[2], ofree[2], lready[2], itemfull[SLOTS], itemfree[SLOTS], mmadone,
+    // sfree[NS], qkdone
+    static constexpr int NBAR = 4 + 2 * ST + 2 * NS + 6 + 2 * ATT_SLOTS + 1 + NS + 1;
     static constexpr int BYTES = OFF_BAR + NBAR * 8 + 16 + 1024;  // + TMEM slot, alignment slack
     static_assert(ST >= 2, "attention K/V ring below two stages");
     static_assert(NBAR * 8 <= 512, "barrier space");
@@ -397,16 +399,20 @@ __device__ __forceinline__ bool att_wait(uint64_t *bar, uint32_t parity, volatil
 //     each S tile): P = exp2 of the fixed shift, causal mask on the diagonal
 //     tile, P (fp16) stored over the first 16 of the thread's own 32 S
 //     columns; the row-sum partials go to shared memory per item.
-//   warps 16-19 (epilogue): one per lane group: O / l plus the exact
-//     previous-position term, stored through per-warp staging -- item k's
+//   warps 16-19 (epilogue): one per lane group: O / l, stored through
+//     per-warp staging -- item k's
 //     epilogue runs while the softmax warps work on item k+1 (O is double
 //     buffered in TMEM).
 //   warp 20 (producer): takes work items from the counter, tests the
 //     bounded-score condition (content only; failing tiles go to the
 //     fallback list), publishes the item (row, tile, m0 and previous-position
 //     scores of its 128 rows), then loads Q and the K/V tiles by TMA.
-//   warp 21 (MMA): lane 0 issues S_g = Qf Kf^T up to three tiles ahead of
-//     the softmax (three S buffers in TMEM) and O += P V.
+//   warp 21 (PV): lane 0 issues O += P V per tile once P is ready; it owns
+//     TMEM.
+//   warp 22 (QK): lane 0 issues S_g = Qf Kf^T up to three tiles ahead of the
+//     PV (three S buffers in TMEM).
+// Roles 21 and 22 sit on their own schedulers' queues (warp % 4 = 1 and 2)
+// beside four softmax warps each.
 // TMEM columns: S0 [0,128), S1 [128,256), S2 [256,384), then the O buffers.
 template <int HDP, int FW>
 __global__ void __launch_bounds__(ATT_THREADS, 1)
@@ -424,7 +430,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     uint64_t *sfull = kvfree + ST, *pready = sfull + NS, *ofull = pready + NS, *ofree = ofull + 2;
     uint64_t *lready = ofree + 2, *itemfull = lready + 2, *itemfree = itemfull + ATT_SLOTS;
     uint64_t *mmadone = itemfree + ATT_SLOTS;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mmadone + 1);
+    uint64_t *sfree = mmadone + 1, *qkdone = sfree + NS;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(qkdone + 1);
     AttnItem *slots = reinterpret_cast<AttnItem *>(sm + L::OFF_SLOT);
     float *lsum = reinterpret_cast<float *>(sm + L::OFF_LSUM);
     __shared__ int s_abort;
@@ -558,105 +565,114 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
             for (int i = k - 2; i >= 0 && i >= k - 3; i--) ptx::mbar_wait(qfull + (i & 1), (i >> 1) & 1, 200000000LL);
         }
     } else if (warp == ATT_W_MMA) {
-        // ---------------- MMA issuer
+        // ---------------- PV issuer: per tile g in order, O += P(g) V(g)
+        // once P(g) is ready (and, on an item's first tile, its O buffer has
+        // been read); the commits free the K/V stage and, once the MMAs have
+        // read P(g), the S buffer g % NS for QK(g + NS).  QK and PV come
+        // from two threads that sleep in their own barrier waits: one thread
+        // polling for both fell ~1000 cycles behind a ready P on a scheduler
+        // it shares with four softmax warps, and one thread issuing both in a
+        // fixed order stalls PV behind a K/V tile still in flight.
         if (lane == 0) {
-            constexpr uint32_t IDESC_QK = ptx::idesc_bf16(128, 128, 0, 0);
-            // PV: fp16 P (TMEM) x the fp16 value tile (HDP/64 adjacent
-            // 64-column atoms of the stage, MN-major), N = HDP
+            // fp16 P (TMEM) x the fp16 value tile (HDP/64 adjacent 64-column
+            // atoms of the stage, MN-major), N = HDP
             constexpr uint32_t IDESC_PV = ptx::idesc_f16(128, HDP, 0, 1);
-            const uint32_t sQ0 = ptx::smem_u32(sm + L::OFF_Q);
-            int kq = 0, jq = 0;                // next QK: item, tile
-            long long gq = 0, gp = 0;          // next QK / PV global tile
-            int kp = 0, jp = 0;                // next PV: item, tile
-            bool qk_end = false, ok = true;
-            // Event loop: issue whichever of PV(gp) and QK(gq) has its inputs
-            // ready (non-blocking barrier tests), PV first.  Each tcgen05.mma
-            // costs the issuing thread far more than its tensor work at these
-            // sizes, so a tile is 8 PV MMAs (N = HDP) and FW/16 QK MMAs, and
-            // the thread never blocks on one operation while the other could
-            // go.  QK(gq) writes S buffer gq % NS, which holds P(gq - NS) until
-            // PV(gq - NS) is issued (the tensor pipe executes in issue order).
-            int qstate = 0;  // QK(gq): 0 item descriptor, 1 Q tile, 2 S buffer, 3 K/V tile
-            long long t_last = clock64();
-            while (ok) {
-                bool did = false;
-                // ---- PV(gp)
-                if (gp < gq) {
-                    const int sl = kp % ATT_SLOTS;
-                    const int ob = kp % L::OBUF;
-                    const bool ready =
-                        (jp != 0 || kp < L::OBUF || ptx::mbar_test(ofree + ob, ((kp - L::OBUF) / L::OBUF) & 1)) &&
-                        ptx::mbar_test(pready + (int)(gp % NS), (uint32_t)((gp / NS) & 1));
-                    if (ready) {
-                        ptx::tc_fence_after();
-                        const uint32_t O_t = tmem + L::O_COL + (uint32_t)(ob * HDP);
-                        const uint32_t P_t = tmem + (uint32_t)((gp % NS) * 128);
-                        const uint64_t vd0 = ptx::smem_desc(ptx::smem_u32(sm + L::OFF_V + (int)(gp % ST) * L::V_BYTES),
-                                                            KT * 128, 1024, ptx::UMMA_SW128);
-#pragma unroll
-                        for (int kk = 0; kk < KT / 16; kk++) {
-                            // keys 16kk..16kk+15: half kk/4 of the tile (its S columns 64h..), packed two per column
-                            const uint32_t a_t = P_t + (uint32_t)(64 * (kk >> 2) + 8 * (kk & 3));
-                            ptx::mma_bf16_ta(O_t, a_t, vd0 + (uint64_t)(kk * 2048 >> 4), IDESC_PV, (jp > 0 || kk > 0));
-                        }
-                        ptx::mma_commit(kvfree + (int)(gp % ST));
-                        gp++;
-                        if (++jp == slots[sl].qt + 1) {
-                            ptx::mma_commit(ofull + ob);
-                            ptx::mbar_arrive(itemfree + sl);
-                            kp++;
-                            jp = 0;
-                        }
-                        did = true;
+            long long gp = 0;
+            int kp = 0, jp = 0;
+            bool ok = true;
+            for (;;) {
+                const int sl = kp % ATT_SLOTS;
+                const int ob = kp % L::OBUF;
+                if (jp == 0) {
+                    if (!att_wait(itemfull + sl, (kp / ATT_SLOTS) & 1, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    if (slots[sl].bh < 0) break;  // the end marker's slot is never returned
+                    if (kp >= L::OBUF && !att_wait(ofree + ob, ((kp - L::OBUF) / L::OBUF) & 1, abort_flag)) {
+                        ok = false;
+                        break;
                     }
                 }
-                // ---- QK(gq)
-                if (!qk_end) {
-                    if (qstate == 0 && jq == 0) {
-                        if (ptx::mbar_test(itemfull + (kq % ATT_SLOTS), (kq / ATT_SLOTS) & 1)) {
-                            if (slots[kq % ATT_SLOTS].bh < 0) qk_end = true;  // the end marker's slot is never returned
-                            else qstate = 1;
-                        }
-                    } else if (qstate == 0) {
-                        qstate = 2;
-                    }
-                    if (qstate == 1 && ptx::mbar_test(qfull + (kq & 1), (kq >> 1) & 1)) qstate = 2;
-                    // S buffer gq % NS holds P(gq - NS) until PV(gq - NS) is issued;
-                    // the tensor pipe runs QK(gq) after it in issue order
-                    if (qstate == 2 && gq <= gp + (NS - 1)) qstate = 3;
-                    if (qstate == 3 && ptx::mbar_test(kvfull + (int)(gq % ST), (uint32_t)((gq / ST) & 1))) {
-                        ptx::tc_fence_after();
-                        const int st = (int)(gq % ST);
-                        const uint32_t sK = ptx::smem_u32(sm + L::OFF_K + st * L::K_BYTES);
-                        const uint32_t S_t = tmem + (uint32_t)((gq % NS) * 128);
-                        const uint32_t sQ = sQ0 + (uint32_t)((kq & 1) * L::Q_BYTES);
-                        const uint64_t ad0 = ptx::smem_desc(sQ, 16, F_SBO, F_SW), bd0 = ptx::smem_desc(sK, 16, F_SBO, F_SW);
-#pragma unroll
-                        for (int kk = 0; kk < FW / 16; kk++)
-                            ptx::mma_bf16(S_t, ad0 + (uint64_t)(kk * 2), bd0 + (uint64_t)(kk * 2), IDESC_QK, kk > 0);
-                        ptx::mma_commit(sfull + (int)(gq % NS));
-                        gq++;
-                        if (++jq == slots[kq % ATT_SLOTS].qt + 1) {
-                            ptx::mma_commit(qfree + (kq & 1));  // Q of item kq no longer read
-                            kq++;
-                            jq = 0;
-                        }
-                        qstate = 0;
-                        did = true;
-                    }
-                }
-                if (qk_end && gp == gq) break;
-                if (did) {
-                    t_last = clock64();
-                } else if (*abort_flag || clock64() - t_last > 4000000000LL) {
-                    *abort_flag = 1;
+                if (!att_wait(pready + (int)(gp % NS), (uint32_t)((gp / NS) & 1), abort_flag)) {
                     ok = false;
+                    break;
+                }
+                ptx::tc_fence_after();
+                const uint32_t O_t = tmem + L::O_COL + (uint32_t)(ob * HDP);
+                const uint32_t P_t = tmem + (uint32_t)((gp % NS) * 128);
+                const uint64_t vd0 = ptx::smem_desc(ptx::smem_u32(sm + L::OFF_V + (int)(gp % ST) * L::V_BYTES),
+                                                    KT * 128, 1024, ptx::UMMA_SW128);
+#pragma unroll
+                for (int kk = 0; kk < KT / 16; kk++) {
+                    // keys 16kk..16kk+15: half kk/4 of the tile (its S columns 64h..), packed two per column
+                    const uint32_t a_t = P_t + (uint32_t)(64 * (kk >> 2) + 8 * (kk & 3));
+                    ptx::mma_bf16_ta(O_t, a_t, vd0 + (uint64_t)(kk * 2048 >> 4), IDESC_PV, (jp > 0 || kk > 0));
+                }
+                ptx::mma_commit(kvfree + (int)(gp % ST));
+                ptx::mma_commit(sfree + (int)(gp % NS));
+                gp++;
+                if (++jp == slots[sl].qt + 1) {
+                    ptx::mma_commit(ofull + ob);
+                    ptx::mbar_arrive(itemfree + sl);
+                    kp++;
+                    jp = 0;
                 }
             }
             if (!ok) atomicOr(a.dev_err, WB_DERR_TIMEOUT_MMA);
-            // every MMA has completed before TMEM is released
+            // every MMA of this thread has completed before TMEM is released
             ptx::mma_commit(mmadone);
             ptx::mbar_wait(mmadone, 0, 200000000LL);
+        }
+        __syncwarp();
+    } else if (warp == ATT_W_QK) {
+        // ---------------- QK issuer: S(g) = Qf Kf_g^T into S buffer g % NS,
+        // once PV(g - NS) has read that buffer and K/V tile g has landed
+        if (lane == 0) {
+            constexpr uint32_t IDESC_QK = ptx::idesc_bf16(128, 128, 0, 0);
+            const uint32_t sQ0 = ptx::smem_u32(sm + L::OFF_Q);
+            long long gq = 0;
+            int kq = 0, jq = 0, qtk = 0;  // qtk: the item's last key tile, read while its slot is held
+            bool ok = true;
+            for (;;) {
+                const int sl = kq % ATT_SLOTS;
+                if (jq == 0) {
+                    if (!att_wait(itemfull + sl, (kq / ATT_SLOTS) & 1, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    if (slots[sl].bh < 0) break;
+                    qtk = slots[sl].qt;
+                    if (!att_wait(qfull + (kq & 1), (kq >> 1) & 1, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                }
+                if ((gq >= NS && !att_wait(sfree + (int)(gq % NS), (uint32_t)(((gq / NS) - 1) & 1), abort_flag)) ||
+                    !att_wait(kvfull + (int)(gq % ST), (uint32_t)((gq / ST) & 1), abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                ptx::tc_fence_after();
+                const int st = (int)(gq % ST);
+                const uint32_t sK = ptx::smem_u32(sm + L::OFF_K + st * L::K_BYTES);
+                const uint32_t S_t = tmem + (uint32_t)((gq % NS) * 128);
+                const uint32_t sQ = sQ0 + (uint32_t)((kq & 1) * L::Q_BYTES);
+                const uint64_t ad0 = ptx::smem_desc(sQ, 16, F_SBO, F_SW), bd0 = ptx::smem_desc(sK, 16, F_SBO, F_SW);
+#pragma unroll
+                for (int kk = 0; kk < FW / 16; kk++)
+                    ptx::mma_bf16(S_t, ad0 + (uint64_t)(kk * 2), bd0 + (uint64_t)(kk * 2), IDESC_QK, kk > 0);
+                ptx::mma_commit(sfull + (int)(gq % NS));
+                gq++;
+                if (++jq == qtk + 1) {
+                    ptx::mma_commit(qfree + (kq & 1));  // Q of item kq no longer read
+                    kq++;
+                    jq = 0;
+                }
+            }
+            if (!ok) atomicOr(a.dev_err, WB_DERR_TIMEOUT_MMA);
+            ptx::mma_commit(qkdone);
+            ptx::mbar_wait(qkdone, 0, 200000000LL);
         }
         __syncwarp();
     } else if (warp < ATT_SOFTMAX_WARPS) {
