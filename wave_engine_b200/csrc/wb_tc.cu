@@ -318,6 +318,7 @@ struct AttnTcArgs {
     uint32_t *dev_err;
     int dot;                    // dot-product features: bound |q| max|k| - s_self instead of the content bound
     float bound;                // a score may exceed the row's shift by at most this (else the tile falls back)
+    int o_tma;                  // o tiles leave by TMA stores through tm_o (head_dim a multiple of 32)
 };
 
 __device__ __forceinline__ float fast_exp2(float x) {
@@ -348,7 +349,10 @@ struct AttnSmem {
     static constexpr int Q_BYTES = QT * FW * 2;      // 4 / 16 KB
     static constexpr int K_BYTES = KT * FW * 2;      // 4 / 16 KB
     static constexpr int V_BYTES = KT * HDP * 2;     // one fp16 value tile: 16 / 32 KB
-    static constexpr int FIXED = 2 * Q_BYTES + ATT_EPI_WARPS * 32 * 33 * 4 + ATT_SLOTS * (int)sizeof(AttnItem) +
+    // epilogue staging per warp, 1024-byte aligned: a 32 x 32 fp32 tile in
+    // the 128-byte swizzle for the TMA store (4 KB), or 32 x 33 floats
+    static constexpr int EPI_WARP = 5120;
+    static constexpr int FIXED = 2 * Q_BYTES + ATT_EPI_WARPS * EPI_WARP + ATT_SLOTS * (int)sizeof(AttnItem) +
                                  2 * 4 * QT * 4 + 512 + 16 + 1024;
     // K/V ring stages: as many as shared memory holds, at most 6
     static constexpr int ST_FIT = (232448 - FIXED) / (K_BYTES + V_BYTES);
@@ -356,8 +360,8 @@ struct AttnSmem {
     static constexpr int OFF_Q = 0;                  // two Q buffers (items alternate)
     static constexpr int OFF_K = OFF_Q + 2 * Q_BYTES;
     static constexpr int OFF_V = OFF_K + ST * K_BYTES;
-    static constexpr int OFF_EPI = OFF_V + ST * V_BYTES;                 // epilogue staging, 32 x 33 floats per warp
-    static constexpr int OFF_SLOT = OFF_EPI + ATT_EPI_WARPS * 32 * 33 * 4;
+    static constexpr int OFF_EPI = OFF_V + ST * V_BYTES;                 // epilogue staging
+    static constexpr int OFF_SLOT = OFF_EPI + ATT_EPI_WARPS * EPI_WARP;
     static constexpr int OFF_LSUM = OFF_SLOT + ATT_SLOTS * (int)sizeof(AttnItem);  // [2][4][QT] row-sum partials
     static constexpr int OFF_BAR = OFF_LSUM + 2 * 4 * QT * 4;
     // TMEM columns: NS score buffers of 128 columns (P(g) is written over the
@@ -373,6 +377,8 @@ struct AttnSmem {
     static constexpr int NBAR = 4 + 2 * ST + 2 * NS + 6 + 2 * ATT_SLOTS + 1 + NS + 1;
     static constexpr int BYTES = OFF_BAR + NBAR * 8 + 16 + 1024;  // + TMEM slot, alignment slack
     static_assert(ST >= 2, "attention K/V ring below two stages");
+    static_assert(OFF_EPI % 1024 == 0 && EPI_WARP % 1024 == 0, "swizzled epilogue tiles need 1024-byte alignment");
+    static_assert(EPI_WARP >= 32 * 33 * 4, "epilogue staging");
     static_assert(NBAR * 8 <= 512, "barrier space");
     static_assert(BYTES <= 232448, "attention shared memory above the 227 KB limit");
     static_assert(O_COL + OBUF * HDP <= 512, "TMEM: NS S and OBUF O buffers");
@@ -417,7 +423,7 @@ __device__ __forceinline__ bool att_wait(uint64_t *bar, uint32_t parity, volatil
 template <int HDP, int FW>
 __global__ void __launch_bounds__(ATT_THREADS, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                   const __grid_constant__ CUtensorMap tm_v,
+                   const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
                    AttnTcArgs a) {
     using L = AttnSmem<HDP, FW>;
     constexpr int ST = L::ST;
@@ -473,21 +479,30 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
             ptx::prefetch_tmap(&tm_k);
             ptx::prefetch_tmap(&tm_v);
         }
-        for (;;) {
-            int item = 0;
-            if (lane == 0) item = atomicAdd(a.sched, 1);
-            item = __shfl_sync(0xffffffffu, item, 0);
-            const bool end = item >= a.n_items;
-            int bh = -1, qt = 0;
-            if (!end) {
+        // Work items are fetched one ahead of the one whose tiles are being
+        // issued: the counter's atomic for item k + 1 goes out when item k is
+        // taken, and item k + 1's row data (fixed shifts, previous-position
+        // scores) are loaded into registers before item k's K/V loop, so
+        // neither round trip stands between two items (items of one or two
+        // key tiles are common: a sequence's first query tiles).
+        // take(): the first item at or after `item` that the tensor path runs
+        // (content: tiles failing the bounded-score test go to the fallback
+        // list), bh = -1 past the end; its rows' data into m0v / spv.
+        auto take = [&](int item, int &bh, int &qt, float (&m0v)[4], float (&spv)[4]) {
+            for (;;) {
+                if (item >= a.n_items) {
+                    bh = -1;
+                    qt = 0;
+                    return;
+                }
                 const int grp = item / per_grp, rr = item - grp * per_grp;
                 const int gsz = min(ATT_GROUP, a.BH - grp * ATT_GROUP);
                 bh = grp * ATT_GROUP + rr % gsz;
                 qt = a.n_qt - 1 - rr / gsz;
+                bool violate = false;
                 if (FW == 64) {
                     // bounded-score test of the tile's rows (content only)
                     const float cm = __uint_as_float(__ldg(a.cmax + bh));
-                    bool violate = false;
 #pragma unroll
                     for (int u = 0; u < 4; u++) {
                         const int q = qt * QT + u * 32 + lane;
@@ -498,37 +513,56 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                                              : 0.25f * cn * (cm - cn) > a.bound;
                         }
                     }
-                    if (__any_sync(0xffffffffu, violate)) {
-                        if (lane == 0) {
-                            const int e = atomicAdd(a.sched + 1, 1);
-                            a.sched[2 + e] = bh * a.n_qt + qt;
-                        }
-                        continue;
-                    }
                 }
+                if (!__any_sync(0xffffffffu, violate)) break;
+                int nx = 0;
+                if (lane == 0) {
+                    const int e = atomicAdd(a.sched + 1, 1);
+                    a.sched[2 + e] = bh * a.n_qt + qt;
+                    nx = atomicAdd(a.sched, 1);
+                }
+                item = __shfl_sync(0xffffffffu, nx, 0);
             }
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int q = qt * QT + u * 32 + lane;
+                const long long rq = (long long)bh * a.T + q;
+                m0v[u] = q < a.T ? __ldg(a.m0 + rq) : 0.0f;
+                spv[u] = q < a.T ? __ldg(a.sprev + rq) : -INFINITY;
+            }
+        };
+        int nitem = 0;  // lane 0: the counter value for the item after the current one
+        if (lane == 0) nitem = atomicAdd(a.sched, 1);
+        int cbh, cqt;
+        float cm0[4], csp[4];
+        take(__shfl_sync(0xffffffffu, nitem, 0), cbh, cqt, cm0, csp);
+        if (lane == 0 && cbh >= 0) nitem = atomicAdd(a.sched, 1);
+        for (;;) {
             const int s = k % ATT_SLOTS;
             if (k >= ATT_SLOTS && !att_wait(itemfree + s, ((k / ATT_SLOTS) - 1) & 1, abort_flag)) {
                 if (lane == 0) atomicOr(a.dev_err, WB_DERR_TIMEOUT_TMA);
                 break;
             }
             AttnItem *it = slots + s;
+            const int bh = cbh, qt = cqt;
             if (lane == 0) {
                 it->bh = bh;
                 it->qt = qt;
             }
-            if (!end) {
+            if (bh >= 0) {
 #pragma unroll
                 for (int u = 0; u < 4; u++) {
-                    const int r = u * 32 + lane, q = qt * QT + r;
-                    const long long rq = (long long)bh * a.T + q;
-                    it->m0[r] = q < a.T ? __ldg(a.m0 + rq) : 0.0f;
-                    it->sp[r] = q < a.T ? __ldg(a.sprev + rq) : -INFINITY;
+                    it->m0[u * 32 + lane] = cm0[u];
+                    it->sp[u * 32 + lane] = csp[u];
                 }
             }
             ptx::mbar_arrive(itemfull + s);  // every lane: its writes are released
             k++;
-            if (end) break;
+            if (bh < 0) break;
+            // the next item (its counter value came back during this item's
+            // predecessor) and the counter for the one after it
+            take(__shfl_sync(0xffffffffu, nitem, 0), cbh, cqt, cm0, csp);
+            if (lane == 0 && cbh >= 0) nitem = atomicAdd(a.sched, 1);
             if (lane == 0) {
                 bool ok = true;
                 // Q of item i = k - 1 into buffer i & 1, free once item i - 2's QKs completed
@@ -705,7 +739,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
             // the diagonal tile or, for the tile's first row, in column 127
             // of the tile before
             const float ep = sp > -INFINITY ? fast_exp2(fmaf(sp, LOG2E, nm0)) : 0.0f;
-            float l = 0.0f;
+            const uint64_t l2e2 = ptx::f2_pack(LOG2E, LOG2E), nm2 = ptx::f2_pack(nm0, nm0);
+            uint64_t l2 = ptx::f2_pack(0.0f, 0.0f);  // row-sum partials of even and odd columns
             bool ok = true;
             for (int j = 0; j <= qt; j++, g++) {
                 if ((int)(g & 1) != grp) continue;
@@ -719,6 +754,16 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                 const bool diag = (j == qt);
                 const uint32_t S_t = tmem + (uint32_t)(sb * 128 + half * 64) + lane_base;
                 uint32_t pk0[16], pk1[16];
+                // exp2((s - shift) log2 e) of columns 2i, 2i+1 (the scaling as
+                // one packed fp32x2 FMA)
+                auto exp_pair = [&](const uint32_t (&r)[32], int i, float &e0, float &e1) {
+                    const uint64_t xv =
+                        ptx::f2_fma(ptx::f2_pack(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), l2e2, nm2);
+                    float x0, x1;
+                    ptx::f2_unpack(xv, x0, x1);
+                    e0 = fast_exp2(x0);
+                    e1 = fast_exp2(x1);
+                };
                 auto exps = [&](const uint32_t (&r)[32], uint32_t (&pk)[16], int kbase) {
                     int pcol = -1;
                     if (ep > 0.0f) {
@@ -728,23 +773,23 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                     if (__any_sync(0xffffffffu, diag || pcol >= 0)) {
 #pragma unroll
                         for (int i = 0; i < 16; i++) {
-                            float e0 = fast_exp2(fmaf(__uint_as_float(r[2 * i]), LOG2E, nm0));
-                            float e1 = fast_exp2(fmaf(__uint_as_float(r[2 * i + 1]), LOG2E, nm0));
+                            float e0, e1;
+                            exp_pair(r, i, e0, e1);
                             if (diag) {
                                 if (kbase + 2 * i > row) e0 = 0.0f;
                                 if (kbase + 2 * i + 1 > row) e1 = 0.0f;
                             }
                             if (2 * i == pcol) e0 = ep;
                             if (2 * i + 1 == pcol) e1 = ep;
-                            l += e0 + e1;
+                            l2 = ptx::f2_add(l2, ptx::f2_pack(e0, e1));
                             pk[i] = pack_f16(e0, e1);
                         }
                     } else {
 #pragma unroll
                         for (int i = 0; i < 16; i++) {
-                            const float e0 = fast_exp2(fmaf(__uint_as_float(r[2 * i]), LOG2E, nm0));
-                            const float e1 = fast_exp2(fmaf(__uint_as_float(r[2 * i + 1]), LOG2E, nm0));
-                            l += e0 + e1;
+                            float e0, e1;
+                            exp_pair(r, i, e0, e1);
+                            l2 = ptx::f2_add(l2, ptx::f2_pack(e0, e1));
                             pk[i] = pack_f16(e0, e1);
                         }
                     }
@@ -778,7 +823,9 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                 atomicOr(a.dev_err, WB_DERR_TIMEOUT_SOFTMAX);
                 break;
             }
-            lsum[((k & 1) * 4 + grp * 2 + half) * QT + row] = l;
+            float l0, l1;
+            ptx::f2_unpack(l2, l0, l1);
+            lsum[((k & 1) * 4 + grp * 2 + half) * QT + row] = l0 + l1;
             ptx::mbar_arrive(lready + (k & 1));
         }
     } else {
@@ -786,7 +833,9 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         const int ew = warp - ATT_SOFTMAX_WARPS;  // lane group
         const int row = ew * 32 + lane;
         const uint32_t lane_base = (uint32_t)(ew * 32) << 16;
-        float *buf = reinterpret_cast<float *>(sm + L::OFF_EPI) + ew * 32 * 33;
+        uint8_t *tbuf = sm + L::OFF_EPI + ew * L::EPI_WARP;
+        float *buf = reinterpret_cast<float *>(tbuf);
+        if (a.o_tma && lane == 0) ptx::prefetch_tmap(&tm_o);
         for (int k = 0;; k++) {
             const int sl = k % ATT_SLOTS;
             if (!att_wait(itemfull + sl, (k / ATT_SLOTS) & 1, abort_flag)) {
@@ -824,13 +873,37 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                 }
 #pragma unroll
                 for (int i = 0; i < 32; i++) r[i] = __float_as_uint(__uint_as_float(r[i]) * inv);
-                warp_stage32(buf, r, lane);
-                const int d = c * 32 + lane;
-                if (d < a.hd)
+                if (a.o_tma) {
+                    // the 32 x 32 tile through shared memory and one TMA store
+                    // (rows past T are clipped by the map): row `lane`, its
+                    // 16-byte chunk cc at chunk cc ^ (lane & 7) -- the 128-byte
+                    // swizzle, conflict-free for these row-per-lane writes.
+                    // The buffer's previous store must have read it first.
+                    if (lane == 0) ptx::bulk_wait_read<0>();
+                    __syncwarp();
+#pragma unroll
+                    for (int cc = 0; cc < 8; cc++) {
+                        float4 v4 = make_float4(__uint_as_float(r[4 * cc]), __uint_as_float(r[4 * cc + 1]),
+                                                __uint_as_float(r[4 * cc + 2]), __uint_as_float(r[4 * cc + 3]));
+                        *reinterpret_cast<float4 *>(tbuf + lane * 128 + ((cc ^ (lane & 7)) << 4)) = v4;
+                    }
+                    ptx::fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0 && q0 < a.T && c * 32 < a.hd) {
+                        ptx::tma_store_3d(&tm_o, tbuf, h * a.hd + c * 32, q0, b);
+                        ptx::bulk_commit();
+                    }
+                } else {
+                    warp_stage32(buf, r, lane);
+                    const int d = c * 32 + lane;
+                    if (d < a.hd)
 #pragma unroll 4
-                    for (int jr = 0; jr < nrow; jr++) orow0[(long long)jr * a.E + d] = buf[jr * 33 + lane];
+                        for (int jr = 0; jr < nrow; jr++) orow0[(long long)jr * a.E + d] = buf[jr * 33 + lane];
+                }
             }
         }
+        // every TMA store of this warp has written global memory
+        if (lane == 0) ptx::bulk_wait<0>();
     }
     __syncwarp();
     ptx::tc_fence_before();
@@ -1061,9 +1134,26 @@ static int launch_attn_tc(const CUtensorMap &tq, const CUtensorMap &tk, const CU
                           int sm_count, cudaStream_t st, std::string *msg) {
     using L = AttnSmem<HDP, FW>;
     const int grid = std::max(1, std::min(aa.n_items, sm_count));
+    // o [B][T][E] fp32 as 32 x 32 tiles for TMA stores, when a tile's
+    // columns start 16-byte aligned and stay inside one head (head_dim a
+    // multiple of 32); other head dims store rows from registers
+    AttnTcArgs a2 = aa;
+    CUtensorMap to;
+    memset(&to, 0, sizeof(to));
+    a2.o_tma = 0;
+    if (aa.hd % 32 == 0 && ((uintptr_t)aa.o & 15) == 0 && (aa.E * 4) % 16 == 0) {
+        const int B = aa.BH / aa.Hg;
+        const uint64_t dims[3] = {(uint64_t)aa.E, (uint64_t)aa.T, (uint64_t)B};
+        const uint64_t strides[2] = {(uint64_t)aa.E * 4, (uint64_t)aa.T * aa.E * 4};
+        const uint32_t box[3] = {32, 32, 1};
+        int rc = make_tmap(&to, aa.o, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, dims, strides, box,
+                           CU_TENSOR_MAP_SWIZZLE_128B, msg);
+        if (rc) return rc;
+        a2.o_tma = 1;
+    }
     ProfScope ps("attn_tc", st);
     cudaFuncSetAttribute(attn_tc_kernel<HDP, FW>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES);
-    attn_tc_kernel<HDP, FW><<<grid, ATT_THREADS, L::BYTES, st>>>(tq, tk, tv, aa);
+    attn_tc_kernel<HDP, FW><<<grid, ATT_THREADS, L::BYTES, st>>>(tq, tk, tv, to, a2);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         *msg = std::string("attention launch failed: ") + cudaGetErrorString(e);
