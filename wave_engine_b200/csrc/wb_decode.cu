@@ -185,8 +185,11 @@ __device__ __forceinline__ float decode_theta_q(float r, float s, float br, floa
 // VEC: floats per value load.
 static constexpr int DEC_U = 8;  // value loads per lane in flight (DEC_U * 32 / G rows per warp)
 // NW: warps per CTA (4, 8 or 12); the register cap keeps 9, 4 or 3 CTAs
-// per SM resident so a serve-sized grid is one wave.
-template <int VEC, int NW, bool PAGED>
+// per SM resident so a serve-sized grid is one wave.  HD: head_dim as a
+// compile-time constant (0: a.hd at run time) -- every thread derives its
+// roles from divisions by head_dim, which are shifts for a constant 64 and
+// software divide sequences otherwise.
+template <int VEC, int NW, bool PAGED, int HD>
 __global__ void __launch_bounds__(NW * 32, NW == 12 ? 3 : (NW == 8 ? 4 : 9)) decode_attn_kernel(DecodeArgs a) {
     constexpr int DEC_THREADS = NW * 32;
     constexpr int DEC_WARPS = NW;
@@ -194,7 +197,7 @@ __global__ void __launch_bounds__(NW * 32, NW == 12 ? 3 : (NW == 8 ? 4 : 9)) dec
     extern __shared__ float dsm[];
     const int split = blockIdx.x, h = blockIdx.y, i = blockIdx.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int E = a.E, hd = a.hd;
+    const int E = a.E, hd = HD ? HD : a.hd;
     float *xs = dsm;                                   // [E]
     int *lidx = reinterpret_cast<int *>(xs + E);       // [DEC_WARPS][DEC_KEYS_PER_WARP]
     float *lp = reinterpret_cast<float *>(lidx + DEC_WARPS * DEC_KEYS_PER_WARP);
@@ -751,13 +754,20 @@ void decode_scratch_tickets(int n_seq, int H, int hd, int E, int cap, size_t *of
     *bytes = d.end - d.ticket;
 }
 
-template <int VEC, int NW, bool PAGED>
-static cudaError_t launch_attn(const DecodeArgs &a, dim3 grid, cudaStream_t st, bool chain) {
+template <int VEC, int NW, bool PAGED, int HD>
+static cudaError_t launch_attn_hd(const DecodeArgs &a, dim3 grid, cudaStream_t st, bool chain) {
     const size_t smem = sizeof(float) * ((size_t)a.E + 2 * NW * DEC_KEYS_PER_WARP + NW * a.hd + NW + 2 * NW +
                                          NW * 32);
-    cudaFuncSetAttribute(decode_attn_kernel<VEC, NW, PAGED>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    cudaError_t e = launch_ex(decode_attn_kernel<VEC, NW, PAGED>, grid, dim3(NW * 32), smem, st, chain, a);
+    cudaFuncSetAttribute(decode_attn_kernel<VEC, NW, PAGED, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)smem);
+    cudaError_t e = launch_ex(decode_attn_kernel<VEC, NW, PAGED, HD>, grid, dim3(NW * 32), smem, st, chain, a);
     return e == cudaSuccess ? cudaGetLastError() : e;
+}
+template <int VEC, int NW, bool PAGED>
+static cudaError_t launch_attn(const DecodeArgs &a, dim3 grid, cudaStream_t st, bool chain) {
+    if constexpr (VEC == 4)
+        if (a.hd == 64) return launch_attn_hd<4, NW, PAGED, 64>(a, grid, st, chain);
+    return launch_attn_hd<VEC, NW, PAGED, 0>(a, grid, st, chain);
 }
 
 // the paged variant is a separate instantiation: its page lookups stay out
