@@ -202,6 +202,30 @@ def test_kv_decode_equals_prefill_last_row(ctx):
     assert r.passed, str(r)
 
 
+def test_tensor_decode_rejects_head_dims_its_value_stream_cannot_split(ctx):
+    """A tensor-path decode reads a value row with at most one warp's lanes,
+    VEC floats each: head_dim 66 (VEC 2, 33 lanes) is refused with
+    WB_ENOTSUP before any launch; the fp32 path decodes it against the
+    oracle."""
+    import wave_engine_b200 as wb
+    from wave_engine_b200 import _lib
+    w, x = make_case(132, 2, 0, 1, 9, seed=66)
+    c = wb.KvCache(1, 2, 66, max_seqs=1, max_ctx=16, ctx=ctx)
+    c.prefill(0, w, x[:, :8].copy(), [0], path="exact")
+    with pytest.raises(wb.WaveB200Error) as e:
+        c.forward_one(0, w, x[:, 8].copy(), [0], path="tensor")
+    assert e.value.code == _lib.WB_ENOTSUP
+    c.reset()
+    c.prefill(0, w, x[:, :8].copy(), [0], path="exact")
+    y = c.forward_one(0, w, x[:, 8].copy(), [0], path="exact")
+    wp = w.packed()
+    _, st = oracle.kv_prefill(wp, x[0, :8], cap=16)
+    oy = oracle.kv_decode(wp, x[0, 8], st)
+    r = check("hd 66 exact decode vs oracle", y.reshape(-1), oy.reshape(-1), EXACT_TOL)
+    assert r.passed, str(r)
+    assert ctx.take_device_error() == 0
+
+
 def test_kv_cache_load_read_and_errors(ctx):
     import wave_engine_b200 as wb
     H, d, n = 4, 42, 50

@@ -807,6 +807,14 @@ int launch_decode_attn(const DecodeLaunch &L, void *scratch, size_t scratch_byte
         *msg = "decode supports head_dim <= 128";
         return WB_ENOTSUP;
     }
+    {
+        // a value row is read by at most one warp's lanes, VEC floats each
+        const int vec = L.hd % 4 == 0 ? 4 : (L.hd % 2 == 0 ? 2 : 1);
+        if ((L.hd + vec - 1) / vec > 32) {
+            *msg = "decode supports head_dim that is a multiple of 4, even and <= 64, or <= 32";
+            return WB_ENOTSUP;
+        }
+    }
     char *s = (char *)scratch;
     DecodeArgs a;
     a.sv = L.sv;
