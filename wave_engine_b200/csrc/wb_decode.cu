@@ -42,11 +42,14 @@ static constexpr int DEC_KEYS_PER_WARP = 128;
 static constexpr int DEC_MAX_HD = 128;  // head_dim limit (one merge column per thread of a 4-warp CTA)
 
 // Warps per attention CTA, from the cache capacity.  Up to 1536 keys a
-// (sequence, head) is one CTA of up to 12 warps whose partials merge in
+// (sequence, head) is one CTA of up to 12 warps (4, 8, 10 or 12: warps past
+// the capacity would run the prologue for no keys) whose partials merge in
 // shared memory: no split partials in scratch, no ticket, one phase
 // projection.  Longer caches use 4-warp CTAs of 512 keys and the ticket
 // merge, which keeps many short CTAs in flight for long contexts.
-static int decode_warps(int cap) { return cap <= 512 ? 4 : cap <= 1024 ? 8 : cap <= 1536 ? 12 : 4; }
+static int decode_warps(int cap) {
+    return cap <= 512 ? 4 : cap <= 1024 ? 8 : cap <= 1280 ? 10 : cap <= 1536 ? 12 : 4;
+}
 static int decode_nsplit(int cap) {
     const int chunk = decode_warps(cap) * DEC_KEYS_PER_WARP;
     return (cap + chunk - 1) / chunk;
@@ -190,7 +193,7 @@ static constexpr int DEC_U = 8;  // value loads per lane in flight (DEC_U * 32 /
 // roles from divisions by head_dim, which are shifts for a constant 64 and
 // software divide sequences otherwise.
 template <int VEC, int NW, bool PAGED, int HD>
-__global__ void __launch_bounds__(NW * 32, NW == 12 ? 3 : (NW == 8 ? 4 : 9)) decode_attn_kernel(DecodeArgs a) {
+__global__ void __launch_bounds__(NW * 32, NW >= 10 ? 3 : (NW == 8 ? 4 : 9)) decode_attn_kernel(DecodeArgs a) {
     constexpr int DEC_THREADS = NW * 32;
     constexpr int DEC_WARPS = NW;
     constexpr int DEC_CHUNK = NW * DEC_KEYS_PER_WARP;  // keys per CTA
@@ -228,8 +231,10 @@ __global__ void __launch_bounds__(NW * 32, NW == 12 ? 3 : (NW == 8 ? 4 : 9)) dec
     const int P = DEC_THREADS / hd;
     const int vd = tid % hd, vq = tid / hd;
     const int kper = (hd + P - 1) / P;
-    constexpr int VN = NW == 8 ? 16 : 12;  // value weights held in registers (ONE)
-    constexpr int XU = NW == 8 ? 4 : 2;    // x elements per thread in the first batch (ONE)
+    // value weights held in registers (ONE: ceil(64 / (NW * 32 / 64)) for head_dim 64)
+    constexpr int VN = NW == 8 ? 16 : (NW == 10 ? 13 : 12);
+    // x elements per thread in the first batch (ONE: the whole 768-wide row)
+    constexpr int XU = NW == 8 ? 4 : (NW == 10 ? 3 : 2);
     const bool vearly = ONE && kper <= VN;
     float wl0[ONE ? VN : 1];
     float xv0[ONE ? XU : 1];
@@ -627,36 +632,31 @@ __global__ void __launch_bounds__(OUT_THREADS) decode_out_kernel(DecodeOutArgs a
             __syncthreads();  // previous chunk consumed
             out_stage_w(a, ws, kc0, kn, c0);
         }
-        // o rows r0..r0+7, inputs kc0..kc0+kn: one batch of float4 loads
-        // (L2: written by the attention grid), then the shared-memory stores
+        // o rows r0..r0+7, inputs kc0..kc0+kn: each thread one float4 of
+        // every row, all loads in flight together (L2: written by the
+        // attention grid), then the shared-memory stores
         {
             const int q4 = (kn + 3) / 4;  // float4 per row
-            constexpr int PER = 8;        // float4 per thread per batch
-            for (int e0 = 0; e0 < OUT_R * q4; e0 += PER * OUT_THREADS) {
-                float4 v[PER];
+            for (int qb = 0; qb < q4; qb += OUT_THREADS) {
+                const int kq = qb + tid, k = kq * 4;
+                if (kq < q4) {
+                    float4 v[OUT_R];
 #pragma unroll
-                for (int u = 0; u < PER; u++) {
-                    const int e = e0 + u * OUT_THREADS + tid;
-                    const int r = e / q4, k = (e - r * q4) * 4;
-                    v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-                    if (e < OUT_R * q4 && r0 + r < n) {
-                        const float *src = a.o + (long long)(r0 + r) * E + kc0 + k;
-                        if ((E % 4) == 0 && k + 3 < kn) v[u] = __ldcg(reinterpret_cast<const float4 *>(src));
-                        else {
-                            if (k < kn) v[u].x = __ldcg(src);
-                            if (k + 1 < kn) v[u].y = __ldcg(src + 1);
-                            if (k + 2 < kn) v[u].z = __ldcg(src + 2);
-                            if (k + 3 < kn) v[u].w = __ldcg(src + 3);
+                    for (int r = 0; r < OUT_R; r++) {
+                        v[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+                        if (r0 + r < n) {
+                            const float *src = a.o + (long long)(r0 + r) * E + kc0 + k;
+                            if ((E % 4) == 0 && k + 3 < kn) v[r] = __ldcg(reinterpret_cast<const float4 *>(src));
+                            else {
+                                if (k < kn) v[r].x = __ldcg(src);
+                                if (k + 1 < kn) v[r].y = __ldcg(src + 1);
+                                if (k + 2 < kn) v[r].z = __ldcg(src + 2);
+                                if (k + 3 < kn) v[r].w = __ldcg(src + 3);
+                            }
                         }
                     }
-                }
 #pragma unroll
-                for (int u = 0; u < PER; u++) {
-                    const int e = e0 + u * OUT_THREADS + tid;
-                    if (e < OUT_R * q4) {
-                        const int r = e / q4, k = (e - r * q4) * 4;
-                        *reinterpret_cast<float4 *>(os + r * ost + k) = v[u];
-                    }
+                    for (int r = 0; r < OUT_R; r++) *reinterpret_cast<float4 *>(os + r * ost + k) = v[r];
                 }
             }
         }
@@ -776,10 +776,12 @@ template <int VEC>
 static cudaError_t launch_attn_nw(const DecodeArgs &a, int nw, dim3 grid, cudaStream_t st, bool chain) {
     if (a.sv.pages) {
         if (nw == 12) return launch_attn<VEC, 12, true>(a, grid, st, chain);
+        if (nw == 10) return launch_attn<VEC, 10, true>(a, grid, st, chain);
         if (nw == 8) return launch_attn<VEC, 8, true>(a, grid, st, chain);
         return launch_attn<VEC, 4, true>(a, grid, st, chain);
     }
     if (nw == 12) return launch_attn<VEC, 12, false>(a, grid, st, chain);
+    if (nw == 10) return launch_attn<VEC, 10, false>(a, grid, st, chain);
     if (nw == 8) return launch_attn<VEC, 8, false>(a, grid, st, chain);
     return launch_attn<VEC, 4, false>(a, grid, st, chain);
 }
