@@ -162,10 +162,14 @@ __device__ __forceinline__ void decode_x_phase(const float *xr, const float *wrs
     }
 }
 
-// theta_q = atan2(s, r) of the CTA's partial sums (warp shuffles, then the
-// warps' sums in warp order after one barrier) plus the bias (br, bs).
+// theta_q = atan2(s, r) of the CTA's partial sums, in two steps: every
+// warp's shuffle sums go to red[] (lane 0), and after a barrier one warp
+// adds the bias and the warps' sums in warp order and leaves theta_q and
+// its bucket in red[2 NW], red[2 NW + 1] for all threads after the next
+// barrier -- the other warps meanwhile compute the new value's partials,
+// instead of each repeating the sums, atan2f and the bucket.
 template <int NW>
-__device__ __forceinline__ float decode_theta_q(float r, float s, float br, float bs, float *red, int warp, int lane) {
+__device__ __forceinline__ void decode_theta_partials(float r, float s, float *red, int warp, int lane) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
         r += __shfl_xor_sync(0xffffffffu, r, o);
@@ -175,14 +179,20 @@ __device__ __forceinline__ float decode_theta_q(float r, float s, float br, floa
         red[warp] = r;
         red[NW + warp] = s;
     }
-    __syncthreads();
+}
+template <int NW>
+__device__ __forceinline__ void decode_theta_finish(float *red, float br, float bs, int lane) {
     float rr = br, ss = bs;
 #pragma unroll
     for (int w = 0; w < NW; w++) {
         rr += red[w];
         ss += red[NW + w];
     }
-    return atan2f(ss, rr);
+    const float th = atan2f(ss, rr);
+    if (lane == 0) {
+        red[2 * NW] = th;
+        red[2 * NW + 1] = __int_as_float(phase_to_bucket(th));
+    }
 }
 
 // VEC: floats per value load.
@@ -206,8 +216,8 @@ __global__ void __launch_bounds__(NW * 32, NW >= 10 ? 3 : (NW == 8 ? 4 : 9)) dec
     float *lp = reinterpret_cast<float *>(lidx + DEC_WARPS * DEC_KEYS_PER_WARP);
     float *opart = lp + DEC_WARPS * DEC_KEYS_PER_WARP; // [DEC_WARPS][hd]
     float *lpart = opart + DEC_WARPS * hd;             // [DEC_WARPS]
-    float *red = lpart + DEC_WARPS;                    // [2 * DEC_WARPS] phase reduction
-    float *vpart = red + 2 * DEC_WARPS;                // [DEC_THREADS] new-value partial sums
+    float *red = lpart + DEC_WARPS;                    // [2 * DEC_WARPS + 2] phase reduction, theta_q, bucket
+    float *vpart = red + 2 * DEC_WARPS + 2;            // [DEC_THREADS] new-value partial sums
     __shared__ int s_flag;
 
     // the out_proj grid may launch and load its weights
@@ -277,6 +287,7 @@ __global__ void __launch_bounds__(NW * 32, NW >= 10 ? 3 : (NW == 8 ? 4 : 9)) dec
     float kth[KR];
     const int n = a.len[slot];
     float thq;
+    int qb;
     if constexpr (ONE) {
         // the whole cache row is this CTA's: the key loads (bucket byte +
         // phase) need only the slot, bounded by the allocated row, so they
@@ -317,7 +328,9 @@ __global__ void __launch_bounds__(NW * 32, NW >= 10 ? 3 : (NW == 8 ? 4 : 9)) dec
             s = fmaf(wv0[u].y, xv0[u], s);
         }
         decode_x_phase<XU, DEC_THREADS>(xr, wrs, E, tid, xs, r, s, XU * DEC_THREADS);
-        thq = decode_theta_q<NW>(r, s, br, bs, red, warp, lane);  // barrier: xs visible too
+        decode_theta_partials<NW>(r, s, red, warp, lane);
+        __syncthreads();  // xs and the warp partials visible
+        if (warp == 0) decode_theta_finish<NW>(red, br, bs, lane);
         // the new value's partial sums (summed at the merge)
         if (vq < P) {
             const float *xh = xs + h * hd;
@@ -341,6 +354,9 @@ __global__ void __launch_bounds__(NW * 32, NW >= 10 ? 3 : (NW == 8 ? 4 : 9)) dec
             }
         }
         vpart[tid] = vpar;
+        __syncthreads();  // theta_q and its bucket
+        thq = red[2 * NW];
+        qb = __float_as_int(red[2 * NW + 1]);
     }
     if (n < 0 || n >= a.cap) {
         if (split == 0 && h == 0 && tid == 0) atomicOr(a.dev_err, WB_DERR_BOUNDS);
@@ -360,7 +376,9 @@ __global__ void __launch_bounds__(NW * 32, NW >= 10 ? 3 : (NW == 8 ? 4 : 9)) dec
         }
         ptx::griddep_wait();  // x (and every write) waits for the grid before
         decode_x_phase<8, DEC_THREADS>(xr, wrs, E, tid, xs, r, s);
-        __syncthreads();
+        decode_theta_partials<NW>(r, s, red, warp, lane);
+        __syncthreads();  // xs and the warp partials visible
+        if (warp == 0) decode_theta_finish<NW>(red, __ldg(a.brs + h * 2), __ldg(a.brs + h * 2 + 1), lane);
         // split 0: the new value, weight loads in batches of 16 before use
         if (split == 0 && vq < P) {
             const float *xh = xs + h * hd;
@@ -377,14 +395,15 @@ __global__ void __launch_bounds__(NW * 32, NW >= 10 ? 3 : (NW == 8 ? 4 : 9)) dec
         }
         vpart[tid] = vpar;
         hn = __ldg(a.hn + h);
-        thq = decode_theta_q<NW>(r, s, __ldg(a.brs + h * 2), __ldg(a.brs + h * 2 + 1), red, warp, lane);
+        __syncthreads();  // theta_q, its bucket and the new value's partials
+        thq = red[2 * NW];
+        qb = __float_as_int(red[2 * NW + 1]);
         if (split == 0 && tid < hd) {  // hd <= DEC_MAX_HD <= DEC_THREADS (checked at launch)
             float v = __ldg(a.bv + h * hd + tid);
             for (int q = 0; q < P; q++) v += vpart[q * hd + tid];
             vnew[tid] = v;
         }
     }
-    const int qb = phase_to_bucket(thq);
     const uint32_t amask = allowed_bucket_mask(qb);
 
     // mask, score, p = exp(s - 1); compact (index, p) per warp
@@ -756,7 +775,7 @@ void decode_scratch_tickets(int n_seq, int H, int hd, int E, int cap, size_t *of
 
 template <int VEC, int NW, bool PAGED, int HD>
 static cudaError_t launch_attn_hd(const DecodeArgs &a, dim3 grid, cudaStream_t st, bool chain) {
-    const size_t smem = sizeof(float) * ((size_t)a.E + 2 * NW * DEC_KEYS_PER_WARP + NW * a.hd + NW + 2 * NW +
+    const size_t smem = sizeof(float) * ((size_t)a.E + 2 * NW * DEC_KEYS_PER_WARP + NW * a.hd + NW + 2 * NW + 2 +
                                          NW * 32);
     cudaFuncSetAttribute(decode_attn_kernel<VEC, NW, PAGED, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)smem);
