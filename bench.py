@@ -201,7 +201,7 @@ def prefill_unmasked_pairs(bucket_slots, T):
 # dram__bytes_read.sum + dram__bytes_write.sum of decode_attn over its
 # algorithmic bytes, measured by ncu on `bench.py --profile-case decode`
 # (values kept with the capture's summary under profiles/).
-DECODE_ATTN_TRAFFIC_RATIO = 1.009  # 43.552 MB measured / 43.166 MB algorithmic
+DECODE_ATTN_TRAFFIC_RATIO = 1.0024  # 43.268 MB measured / 43.166 MB algorithmic
 
 
 def prefill_flops_per_layer(B, T, E, H, hd, C):
