@@ -212,9 +212,9 @@ __global__ void __launch_bounds__(NW * 32, NW >= 10 ? 3 : (NW == 8 ? 4 : 9)) dec
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int E = a.E, hd = HD ? HD : a.hd;
     float *xs = dsm;                                   // [E]
-    int *lidx = reinterpret_cast<int *>(xs + E);       // [DEC_WARPS][DEC_KEYS_PER_WARP]
-    float *lp = reinterpret_cast<float *>(lidx + DEC_WARPS * DEC_KEYS_PER_WARP);
-    float *opart = lp + DEC_WARPS * DEC_KEYS_PER_WARP; // [DEC_WARPS][hd]
+    // [DEC_WARPS][DEC_KEYS_PER_WARP] kept keys: (value-row offset as int bits, p)
+    float2 *lkp = reinterpret_cast<float2 *>(xs + E);  // 8-byte aligned: E is even
+    float *opart = reinterpret_cast<float *>(lkp + DEC_WARPS * DEC_KEYS_PER_WARP);  // [DEC_WARPS][hd]
     float *lpart = opart + DEC_WARPS * hd;             // [DEC_WARPS]
     float *red = lpart + DEC_WARPS;                    // [2 * DEC_WARPS + 2] phase reduction, theta_q, bucket
     float *vpart = red + 2 * DEC_WARPS + 2;            // [DEC_THREADS] new-value partial sums
@@ -409,8 +409,7 @@ __global__ void __launch_bounds__(NW * 32, NW >= 10 ? 3 : (NW == 8 ? 4 : 9)) dec
     // mask, score, p = exp(s - 1); compact (index, p) per warp
     int m = 0;
     float lsum = 0.0f;
-    int *my_idx = lidx + warp * DEC_KEYS_PER_WARP;
-    float *my_p = lp + warp * DEC_KEYS_PER_WARP;
+    float2 *my_kp = lkp + warp * DEC_KEYS_PER_WARP;
 #pragma unroll
     for (int c = 0; c < KR; c++) {
         const int k = k0 + c * 32 + lane;
@@ -426,8 +425,7 @@ __global__ void __launch_bounds__(NW * 32, NW >= 10 ? 3 : (NW == 8 ? 4 : 9)) dec
         const unsigned bal = __ballot_sync(0xffffffffu, ok);
         if (ok) {
             const int pos = m + __popc(bal & ((1u << lane) - 1u));
-            my_idx[pos] = k;
-            my_p[pos] = p;
+            my_kp[pos] = make_float2(__int_as_float(k * hd), p);
         }
         m += __popc(bal);
         lsum += p;
@@ -437,30 +435,49 @@ __global__ void __launch_bounds__(NW * 32, NW >= 10 ? 3 : (NW == 8 ? 4 : 9)) dec
     // stream value rows of the kept keys: G lanes per row, VEC floats per lane
     const int G = lanes_per_key<VEC>(hd);
     const int KPW = 32 / G;
+    const int BATCH = KPW * DEC_U;  // rows per batch of loads (a power of two)
     const int slotk = lane / G, vi = lane - slotk * G;
     const bool vact = vi * VEC < hd;
     float acc[VEC];
 #pragma unroll
     for (int u = 0; u < VEC; u++) acc[u] = 0.0f;
-    // U rows per lane, all U loads issued before the first is used; past
-    // the end of the list a lane re-reads the last kept row with weight 0
-    // (the loads stay unconditional so they can all be in flight)
-    if (vact)
-        for (int b0 = 0; b0 < m; b0 += KPW * DEC_U) {
+    // PAD (the 64-register CTAs of 8 and 10 warps): the list padded to whole
+    // batches with weight-0 copies of the last kept row, so the loads of a
+    // batch need no bound; the 56-register CTAs clamp the index instead (the
+    // padded loop spills there).  Either way a batch's loads are all in
+    // flight before the first is used, and rows past the list re-read the
+    // last kept row with weight 0.
+    constexpr bool PAD = NW == 8 || NW == 10;
+    if (PAD && m > 0) {
+        const float2 last = make_float2(my_kp[m - 1].x, 0.0f);
+        for (int t = m + lane; t < ((m + BATCH - 1) & ~(BATCH - 1)); t += 32) my_kp[t] = last;
+        __syncwarp();
+    }
+    if (vact) {
+        const float *Vl = V + vi * VEC;
+        const float2 *lq = my_kp + slotk;
+        for (int b0 = 0; b0 < m; b0 += BATCH) {
             VRow<VEC> rows[DEC_U];
             float pr[DEC_U];
 #pragma unroll
             for (int u = 0; u < DEC_U; u++) {
-                const int j = b0 + u * KPW + slotk;
-                const int jj = min(j, m - 1);
-                rows[u].load(V + (long long)my_idx[jj] * hd + vi * VEC);
-                pr[u] = j < m ? my_p[jj] : 0.0f;
+                if constexpr (PAD) {
+                    const float2 e = lq[b0 + u * KPW];
+                    rows[u].load(Vl + __float_as_int(e.x));
+                    pr[u] = e.y;
+                } else {
+                    const int j = b0 + u * KPW + slotk;
+                    const float2 e = my_kp[min(j, m - 1)];
+                    rows[u].load(Vl + __float_as_int(e.x));
+                    pr[u] = j < m ? e.y : 0.0f;
+                }
             }
 #pragma unroll
             for (int u = 0; u < DEC_U; u++)
 #pragma unroll
                 for (int e = 0; e < VEC; e++) acc[e] = fmaf(pr[u], rows[u].v[e], acc[e]);
         }
+    }
     for (int o = G; o < 32; o <<= 1)
 #pragma unroll
         for (int u = 0; u < VEC; u++) acc[u] += __shfl_xor_sync(0xffffffffu, acc[u], o);
