@@ -197,13 +197,13 @@ __device__ __forceinline__ void decode_theta_finish(float *red, float br, float 
 
 // VEC: floats per value load.
 static constexpr int DEC_U = 8;  // value loads per lane in flight (DEC_U * 32 / G rows per warp)
-// NW: warps per CTA (4, 8 or 12); the register cap keeps 9, 4 or 3 CTAs
+// NW: warps per CTA (4, 8, 10 or 12); the register cap keeps 8, 4 or 3 CTAs
 // per SM resident so a serve-sized grid is one wave.  HD: head_dim as a
 // compile-time constant (0: a.hd at run time) -- every thread derives its
 // roles from divisions by head_dim, which are shifts for a constant 64 and
 // software divide sequences otherwise.
 template <int VEC, int NW, bool PAGED, int HD>
-__global__ void __launch_bounds__(NW * 32, NW >= 10 ? 3 : (NW == 8 ? 4 : 9)) decode_attn_kernel(DecodeArgs a) {
+__global__ void __launch_bounds__(NW * 32, NW >= 10 ? 3 : (NW == 8 ? 4 : 8)) decode_attn_kernel(DecodeArgs a) {
     constexpr int DEC_THREADS = NW * 32;
     constexpr int DEC_WARPS = NW;
     constexpr int DEC_CHUNK = NW * DEC_KEYS_PER_WARP;  // keys per CTA
@@ -441,13 +441,13 @@ __global__ void __launch_bounds__(NW * 32, NW >= 10 ? 3 : (NW == 8 ? 4 : 9)) dec
     float acc[VEC];
 #pragma unroll
     for (int u = 0; u < VEC; u++) acc[u] = 0.0f;
-    // PAD (the 64-register CTAs of 8 and 10 warps): the list padded to whole
-    // batches with weight-0 copies of the last kept row, so the loads of a
-    // batch need no bound; the 56-register CTAs clamp the index instead (the
-    // padded loop spills there).  Either way a batch's loads are all in
+    // PAD (the 64-register CTAs of 4, 8 and 10 warps): the list padded to
+    // whole batches with weight-0 copies of the last kept row, so the loads of
+    // a batch need no bound; the 56-register 12-warp CTAs clamp the index
+    // instead (the padded loop spills there).  Either way a batch's loads are all in
     // flight before the first is used, and rows past the list re-read the
     // last kept row with weight 0.
-    constexpr bool PAD = NW == 8 || NW == 10;
+    constexpr bool PAD = NW != 12;
     if (PAD && m > 0) {
         const float2 last = make_float2(my_kp[m - 1].x, 0.0f);
         for (int t = m + lane; t < ((m + BATCH - 1) & ~(BATCH - 1)); t += 32) my_kp[t] = last;
