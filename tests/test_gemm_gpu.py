@@ -6,8 +6,10 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 
+# fewer than 148 tiles of 128 x 128 take the 128 x 32 tiles; (2048, 1536, 512)
+# and (4096, 768, 768) are 192 wide tiles
 @pytest.mark.parametrize("M,N,K", [(128, 128, 64), (256, 768, 768), (300, 168, 168), (1000, 384, 384),
-                                   (129, 4096, 4096)])
+                                   (129, 4096, 4096), (2048, 1536, 512)])
 def test_gemm_bf16_matches_torch(ctx, M, N, K):
     import torch
     from wave_engine_b200 import _lib
@@ -25,7 +27,8 @@ def test_gemm_bf16_matches_torch(ctx, M, N, K):
     assert ctx.take_device_error() == 0
 
 
-@pytest.mark.parametrize("M,N,K", [(128, 128, 32), (300, 4096, 4096), (1000, 1536, 1536)])
+@pytest.mark.parametrize("M,N,K", [(128, 128, 32), (300, 4096, 4096), (1000, 1536, 1536), (4096, 768, 768),
+                                   (256, 720, 768)])
 def test_gemm_tf32_matches_torch(ctx, M, N, K):
     import torch
     from wave_engine_b200 import _lib

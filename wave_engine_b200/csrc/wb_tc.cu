@@ -920,32 +920,41 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
 // TF32 = true: A and B are fp32 in memory and the MMA is kind::tf32 (K = 8
 // per instruction); the 128-byte K block then holds 32 elements instead of 64.
 static constexpr int GBM = 128, GBN = 128, GST = 3;
+// narrow tiles for GEMMs whose 128 x 128 grid would leave most SMs idle
+// (the decode out_proj of 64-1000 rows): 4x the CTAs, a deeper TMA ring
+static constexpr int GBN_NARROW = 32, GST_NARROW = 6;
+template <int BN, int NST>
+struct GemmSmem {
+    static constexpr int STAGE = (GBM + BN) * 128;  // A and B rows of one 128-byte K block
+    static constexpr int BYTES = NST * STAGE + 128 + 1024;
+    static_assert(STAGE % 1024 == 0, "128-byte-swizzled operands need 1024-byte alignment");
+    static_assert(NST * STAGE >= 4 * 32 * 33 * 4, "epilogue staging reuses the ring");
+};
 static constexpr int G_ROW = 128;                       // bytes of one K block row
-static constexpr int G_STAGE = (GBM + GBN) * G_ROW;     // 32 KB
-static constexpr int G_SMEM = GST * G_STAGE + 128 + 1024;
 
-template <bool TF32>
+template <bool TF32, int BN = GBN, int NST = GST>
 __global__ void __launch_bounds__(128, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                    const float *__restrict__ bias, float *__restrict__ C, int M, int N, int K, long long ldc,
                    uint32_t *dev_err, int accumulate) {
     constexpr int GBK = TF32 ? 32 : 64;  // elements per K block
+    constexpr int STAGE = GemmSmem<BN, NST>::STAGE;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t *bars = reinterpret_cast<uint64_t *>(sm + GST * G_STAGE);
-    uint64_t *full = bars, *empty = bars + GST, *done = bars + 2 * GST;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * GST + 1);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sm + NST * STAGE);
+    uint64_t *full = bars, *empty = bars + NST, *done = bars + 2 * NST;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * NST + 1);
     const int tid = threadIdx.x, warp = tid >> 5;
     // column tiles vary fastest: the CTAs of one row tile run together and
     // read its A rows from L2 after the first
-    const int m0 = blockIdx.y * GBM, n0 = blockIdx.x * GBN;
+    const int m0 = blockIdx.y * GBM, n0 = blockIdx.x * BN;
     const int nk = (K + GBK - 1) / GBK;
     if (tid == 0) {
-        for (int i = 0; i < 2 * GST + 1; i++) ptx::mbar_init(bars + i, 1);
+        for (int i = 0; i < 2 * NST + 1; i++) ptx::mbar_init(bars + i, 1);
         ptx::fence_mbar_init();
     }
     if (warp == 0) {
-        ptx::tmem_alloc(tmem_slot, 128);
+        ptx::tmem_alloc(tmem_slot, BN);
         ptx::tmem_relinquish();
     }
     ptx::tc_fence_before();
@@ -957,28 +966,28 @@ __global__ void __launch_bounds__(128, 1)
         ptx::prefetch_tmap(&tm_a);
         ptx::prefetch_tmap(&tm_b);
         for (int kb = 0; kb < nk; kb++) {
-            const int s = kb % GST;
-            if (kb >= GST && !ptx::mbar_wait(empty + s, ((kb / GST) - 1) & 1)) {
+            const int s = kb % NST;
+            if (kb >= NST && !ptx::mbar_wait(empty + s, ((kb / NST) - 1) & 1)) {
                 atomicOr(dev_err, WB_DERR_TIMEOUT_MMA);
                 ok = false;
                 break;
             }
-            uint8_t *st = sm + s * G_STAGE;
-            ptx::mbar_arrive_expect_tx(full + s, G_STAGE);
+            uint8_t *st = sm + s * STAGE;
+            ptx::mbar_arrive_expect_tx(full + s, STAGE);
             ptx::tma_load_2d(st, &tm_a, full + s, kb * GBK, m0);
             ptx::tma_load_2d(st + GBM * G_ROW, &tm_b, full + s, kb * GBK, n0);
         }
     } else if (tid == 32) {
-        constexpr uint32_t IDESC = TF32 ? ptx::idesc_tf32(GBM, GBN) : ptx::idesc_bf16(GBM, GBN, 0, 0);
+        constexpr uint32_t IDESC = TF32 ? ptx::idesc_tf32(GBM, BN) : ptx::idesc_bf16(GBM, BN, 0, 0);
         for (int kb = 0; kb < nk; kb++) {
-            const int s = kb % GST;
-            if (!ptx::mbar_wait(full + s, (kb / GST) & 1)) {
+            const int s = kb % NST;
+            if (!ptx::mbar_wait(full + s, (kb / NST) & 1)) {
                 atomicOr(dev_err, WB_DERR_TIMEOUT_TMA);
                 ok = false;
                 break;
             }
             ptx::tc_fence_after();
-            const uint32_t sa = ptx::smem_u32(sm + s * G_STAGE), sb = sa + GBM * G_ROW;
+            const uint32_t sa = ptx::smem_u32(sm + s * STAGE), sb = sa + GBM * G_ROW;
 #pragma unroll
             for (int k = 0; k < 4; k++) {  // 32 bytes of K per instruction
                 const uint64_t ad = ptx::smem_desc(sa + k * 32, 16, 1024, ptx::UMMA_SW128);
@@ -1001,7 +1010,7 @@ __global__ void __launch_bounds__(128, 1)
         float *buf = reinterpret_cast<float *>(sm) + warp * 32 * 33;
         const int lane = tid & 31;
 #pragma unroll 1
-        for (int c = 0; c < GBN / 32; c++) {
+        for (int c = 0; c < BN / 32; c++) {
             uint32_t r[32];
             ptx::tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + c * 32, r);
             ptx::tmem_ld_wait();
@@ -1020,7 +1029,7 @@ __global__ void __launch_bounds__(128, 1)
     }
     ptx::tc_fence_before();
     __syncthreads();
-    if (warp == 0) ptx::tmem_dealloc(tmem, 128);
+    if (warp == 0) ptx::tmem_dealloc(tmem, BN);
     (void)ok;
 }
 
@@ -1106,20 +1115,31 @@ static int launch_gemm(bool tf32, const void *A, const void *W, const float *bia
     if ((rc = make_tmap(&ta, A, dt, 2, adims, astr, abox, CU_TENSOR_MAP_SWIZZLE_128B, msg))) return rc;
     const uint64_t bdims[2] = {(uint64_t)K, (uint64_t)N};
     const uint64_t bstr[1] = {(uint64_t)ldw * esz};
-    const uint32_t bbox[2] = {bk, GBN};
+    // 128 x 128 tiles, or 128 x 32 when the wide grid would fill fewer than
+    // the device's SMs
+    const long long wide_tiles = (long long)((N + GBN - 1) / GBN) * ((M + GBM - 1) / GBM);
+    const bool narrow = wide_tiles < 148;
+    const int bn = narrow ? GBN_NARROW : GBN;
+    const uint32_t bbox[2] = {bk, (uint32_t)bn};
     if ((rc = make_tmap(&tb, W, dt, 2, bdims, bstr, bbox, CU_TENSOR_MAP_SWIZZLE_128B, msg))) return rc;
     if ((M + GBM - 1) / GBM > 65535) {
         *msg = "GEMM with more than 65535 row tiles";
         return WB_EINVAL;
     }
-    dim3 gg((unsigned)((N + GBN - 1) / GBN), (unsigned)((M + GBM - 1) / GBM));
+    dim3 gg((unsigned)((N + bn - 1) / bn), (unsigned)((M + GBM - 1) / GBM));
     ProfScope ps(tf32 ? "gemm_tf32" : "gemm_bf16", st);
+    auto go = [&](auto kernel, int smem) {
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        kernel<<<gg, 128, smem, st>>>(ta, tb, bias, C, M, N, K, ldc, dev_err, accumulate);
+    };
+    using Wide = GemmSmem<GBN, GST>;
+    using Narrow = GemmSmem<GBN_NARROW, GST_NARROW>;
     if (tf32) {
-        cudaFuncSetAttribute(gemm_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, G_SMEM);
-        gemm_tc_kernel<true><<<gg, 128, G_SMEM, st>>>(ta, tb, bias, C, M, N, K, ldc, dev_err, accumulate);
+        if (narrow) go(gemm_tc_kernel<true, GBN_NARROW, GST_NARROW>, Narrow::BYTES);
+        else go(gemm_tc_kernel<true, GBN, GST>, Wide::BYTES);
     } else {
-        cudaFuncSetAttribute(gemm_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, G_SMEM);
-        gemm_tc_kernel<false><<<gg, 128, G_SMEM, st>>>(ta, tb, bias, C, M, N, K, ldc, dev_err, accumulate);
+        if (narrow) go(gemm_tc_kernel<false, GBN_NARROW, GST_NARROW>, Narrow::BYTES);
+        else go(gemm_tc_kernel<false, GBN, GST>, Wide::BYTES);
     }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
