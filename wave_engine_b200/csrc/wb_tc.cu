@@ -1115,8 +1115,8 @@ static int launch_gemm(bool tf32, const void *A, const void *W, const float *bia
     if ((rc = make_tmap(&ta, A, dt, 2, adims, astr, abox, CU_TENSOR_MAP_SWIZZLE_128B, msg))) return rc;
     const uint64_t bdims[2] = {(uint64_t)K, (uint64_t)N};
     const uint64_t bstr[1] = {(uint64_t)ldw * esz};
-    // 128 x 128 tiles, or 128 x 32 when the wide grid would fill fewer than
-    // the device's SMs
+    // 128 x 128 tiles, or 128 x 32 when the wide grid would be smaller than
+    // one CTA per SM of a B200 (148)
     const long long wide_tiles = (long long)((N + GBN - 1) / GBN) * ((M + GBM - 1) / GBM);
     const bool narrow = wide_tiles < 148;
     const int bn = narrow ? GBN_NARROW : GBN;
