@@ -27,6 +27,33 @@ namespace wb {
 #define FM __fmul_rn
 #define FA __fadd_rn
 
+// (r, s) pairs of the Kerr ODE as packed fp32x2 arithmetic: mul.rn / add.rn
+// .f32x2 round each half exactly as the scalar __fmul_rn / __fadd_rn, so the
+// results are those of the scalar statements beside each helper, with half
+// the instructions (the ODE kernel is issue-bound).
+// (o0, o1) = (FA(x0, FM(a, y0)), FA(x1, FM(a, y1)))
+__device__ __forceinline__ void pair_axpy(float &o0, float &o1, float x0, float x1, float a, float y0, float y1) {
+    asm("{\n .reg .b64 px, pa, py;\n mov.b64 px, {%2, %3};\n mov.b64 pa, {%4, %4};\n mov.b64 py, {%5, %6};\n"
+        " mul.rn.f32x2 py, pa, py;\n add.rn.f32x2 px, px, py;\n mov.b64 {%0, %1}, px;\n}\n"
+        : "=f"(o0), "=f"(o1)
+        : "f"(x0), "f"(x1), "f"(a), "f"(y0), "f"(y1));
+}
+// (x0, x1) += FM(dt, FA(FA(FA(FM(w0, k1), FM(w1, k2)), FM(w2, k3)), FM(w3, k4))), per half
+__device__ __forceinline__ void pair_rk4_combine(float &x0, float &x1, float dt, float w0, float w1, float w2, float w3,
+                                                 float k1a, float k1b, float k2a, float k2b, float k3a, float k3b,
+                                                 float k4a, float k4b) {
+    asm("{\n .reg .b64 px, pw, pk, pt, pu;\n"
+        " mov.b64 pw, {%3, %3};\n mov.b64 pk, {%7, %8};\n mul.rn.f32x2 pt, pw, pk;\n"
+        " mov.b64 pw, {%4, %4};\n mov.b64 pk, {%9, %10};\n mul.rn.f32x2 pu, pw, pk;\n add.rn.f32x2 pt, pt, pu;\n"
+        " mov.b64 pw, {%5, %5};\n mov.b64 pk, {%11, %12};\n mul.rn.f32x2 pu, pw, pk;\n add.rn.f32x2 pt, pt, pu;\n"
+        " mov.b64 pw, {%6, %6};\n mov.b64 pk, {%13, %14};\n mul.rn.f32x2 pu, pw, pk;\n add.rn.f32x2 pt, pt, pu;\n"
+        " mov.b64 pw, {%2, %2};\n mul.rn.f32x2 pt, pw, pt;\n"
+        " mov.b64 px, {%0, %1};\n add.rn.f32x2 px, px, pt;\n mov.b64 {%0, %1}, px;\n}\n"
+        : "+f"(x0), "+f"(x1)
+        : "f"(dt), "f"(w0), "f"(w1), "f"(w2), "f"(w3), "f"(k1a), "f"(k1b), "f"(k2a), "f"(k2b), "f"(k3a), "f"(k3b),
+          "f"(k4a), "f"(k4b));
+}
+
 // ---------------------------------------------------------------------------
 // LayerNorm: one warp per row, the row staged in shared memory by one batch
 // of loads, lane-strided partial sums combined by a fixed shuffle tree (mean,
@@ -438,28 +465,19 @@ __global__ void __launch_bounds__(1024) kerr_ode_kernel(OdeArgs a) {
     for (int step = 0; step < a.steps; step++) {
         eval(r, s, k1r, k1s);
 #pragma unroll
-        for (int u = 0; u < BPT; u++) {
-            rt[u] = FA(r[u], FM(hdt, k1r[u]));
-            st[u] = FA(s[u], FM(hdt, k1s[u]));
-        }
+        for (int u = 0; u < BPT; u++) pair_axpy(rt[u], st[u], r[u], s[u], hdt, k1r[u], k1s[u]);
         eval(rt, st, k2r, k2s);
 #pragma unroll
-        for (int u = 0; u < BPT; u++) {
-            rt[u] = FA(r[u], FM(hdt, k2r[u]));
-            st[u] = FA(s[u], FM(hdt, k2s[u]));
-        }
+        for (int u = 0; u < BPT; u++) pair_axpy(rt[u], st[u], r[u], s[u], hdt, k2r[u], k2s[u]);
         eval(rt, st, k3r, k3s);
 #pragma unroll
-        for (int u = 0; u < BPT; u++) {
-            rt[u] = FA(r[u], FM(dt, k3r[u]));
-            st[u] = FA(s[u], FM(dt, k3s[u]));
-        }
+        for (int u = 0; u < BPT; u++) pair_axpy(rt[u], st[u], r[u], s[u], dt, k3r[u], k3s[u]);
         eval(rt, st, k4r, k4s);
 #pragma unroll
-        for (int u = 0; u < BPT; u++) {
-            r[u] = FA(r[u], FM(dt, FA(FA(FA(FM(w0, k1r[u]), FM(w1, k2r[u])), FM(w2, k3r[u])), FM(w3, k4r[u]))));
-            s[u] = FA(s[u], FM(dt, FA(FA(FA(FM(w0, k1s[u]), FM(w1, k2s[u])), FM(w2, k3s[u])), FM(w3, k4s[u]))));
-        }
+        for (int u = 0; u < BPT; u++)
+            // r += FM(dt, FA(FA(FA(FM(w0, k1r), FM(w1, k2r)), FM(w2, k3r)), FM(w3, k4r))), s likewise
+            pair_rk4_combine(r[u], s[u], dt, w0, w1, w2, w3, k1r[u], k1s[u], k2r[u], k2s[u], k3r[u], k3s[u], k4r[u],
+                             k4s[u]);
     }
     float *out = a.out + row * 2 * n;
 #pragma unroll
