@@ -249,7 +249,10 @@ WB_API int wb_dot_attn_layer_destroy(wb_dot_attn_layer *layer);
 /* x, y [batch][seq_len][n_embd], host or device.  flags: WB_PATH_EXACT runs
  * both projections as the reference's sequential fp32 sums (model.rs:144-150);
  * otherwise they run on the tensor cores in TF32 (n_embd a multiple of 4, a
- * device x 16-byte aligned).  The attention core is fp32 on both paths. */
+ * device x 16-byte aligned).  The exact path's attention core is fp32; the
+ * tensor path's runs on tcgen05 (bf16 q/sqrt(d) and k, fp16 probabilities and
+ * values, features padded to 64 or 128 columns), and query tiles whose scores
+ * could leave the fixed shift's range are recomputed by the fp32 core. */
 WB_API int wb_dot_attn_forward(wb_context *ctx, const wb_dot_attn_layer *layer, const float *x, int batch,
                                int seq_len, int flags, float *y);
 

@@ -27,7 +27,7 @@ WB_API int wb_test_gemm_tf32(wb_context *ctx, const float *A, const float *B, co
 
 /* The dot-product attention core alone (compute.rs:357-414, between c_attn
  * and c_proj): qkv [B*T][3*n_embd] -> o [B*T][n_embd], DEVICE pointers.
- * mode 0: the tensor-core core (head_dim <= 64) with its fp32 fallback for
+ * mode 0: the tensor-core core (head_dim <= 128) with its fp32 fallback for
  * query tiles past the fixed-shift bound; 1: the same with every tile sent
  * to the fallback; 2: the fp32 FMA core.  Asynchronous on the context's
  * stream. */

@@ -2,8 +2,8 @@
 ComputeBackend::attention) against the CPU oracle, through the C ABI.
 
 Tolerances: WB_PATH_EXACT (sequential fp32 projections, fp32 attention core)
-max-abs 1e-5; WB_PATH_TENSOR (TF32 tensor-core projections, fp32 core)
-max-abs 2e-3."""
+max-abs 1e-5; WB_PATH_TENSOR (TF32 tensor-core projections, the tcgen05
+attention core for head_dim <= 128) max-abs 2e-3."""
 from __future__ import annotations
 
 import numpy as np
@@ -68,10 +68,17 @@ def _dot_core_f64(qkv, H):
     return o
 
 
-@pytest.mark.parametrize("E,H,T", [(256, 4, 300), (168, 4, 129), (48, 6, 64)])
+@pytest.mark.parametrize("E,H,T", [
+    (256, 4, 300),   # head_dim 64: 64-column features, several query and key tiles
+    (168, 4, 129),   # head_dim 42
+    (48, 6, 64),     # head_dim 8
+    (512, 4, 300),   # head_dim 128: 128-column features (two swizzle atoms), 2-stage K/V ring
+    (384, 4, 200),   # head_dim 96: padded to 128, TMA-stored output tiles
+    (200, 2, 150),   # head_dim 100: padded to 128, output rows stored from registers
+])
 def test_dot_core_on_tensor_cores_and_fallback_tiles(ctx, E, H, T):
     """The attention core alone on a qkv built directly (no projection
-    error): the tcgen05 core (head_dim <= 64) within 2e-3 of a float64
+    error): the tcgen05 core (head_dim <= 128) within 2e-3 of a float64
     statement; a (sequence, head) with magnitudes x30 fails the fixed-shift
     bound and is recomputed by the fp32 core (bitwise equal to it there);
     with every tile forced to the fallback the result equals the fp32 core

@@ -924,12 +924,12 @@ int wb_dot_attn_forward(wb_context *ctx, const wb_dot_attn_layer *L, const float
     const float *xd = x_dev ? x : (const float *)(iob + o_x);
     float *yd = y_dev ? y : (float *)(iob + o_y);
     if (!x_dev) WB_CUDA(cudaMemcpyAsync((void *)xd, x, R * E * sizeof(float), cudaMemcpyHostToDevice, st));
-    // the tensor path's core runs on tcgen05 for head_dim <= 64
-    const bool tc_core = !exact && E / H <= 64;
+    // the tensor path's core runs on tcgen05 (head_dim <= 128)
+    const bool tc_core = !exact && E / H <= 128;
     Carve c;
     size_t o_qkv = c.take<float>(R * 3 * E);
     size_t o_o = c.take<float>(R * E);
-    size_t o_core = tc_core ? c.take<char>(wb::tc_dot_core_bytes(B, T, H)) : 0;
+    size_t o_core = tc_core ? c.take<char>(wb::tc_dot_core_bytes(B, T, E, H)) : 0;
     WB_TRY(ensure(ctx->ws, c.off));
     float *qkv = (float *)((char *)ctx->ws.p + o_qkv), *o = (float *)((char *)ctx->ws.p + o_o);
     std::string msg;
@@ -1758,7 +1758,7 @@ int wb_test_dot_core(wb_context *ctx, const float *qkv, int B, int T, int E, int
     if (mode == 2) {
         rc = wb::launch_dot_attn(qkv, B, T, E, H, o, ctx->stream, &msg);
     } else {
-        WB_TRY(ensure(ctx->ws, wb::tc_dot_core_bytes(B, T, H)));
+        WB_TRY(ensure(ctx->ws, wb::tc_dot_core_bytes(B, T, E, H)));
         rc = wb::tc_dot_attention(qkv, B, T, E, H, o, ctx->ws.p, mode == 1, ctx->dev_err, ctx->sm_count, ctx->stream,
                                   &msg);
     }

@@ -157,8 +157,9 @@ int launch_dot_attn_tiles(const float *qkv, int B, int T, int E, int H, float *o
     else if (half <= 16) dot_attn_tiles_kernel<16><<<grid, 2 * DQ, 0, st>>>(qkv, T, E, H, hd, scale, o, tiles);
     else if (half <= 24) dot_attn_tiles_kernel<24><<<grid, 2 * DQ, 0, st>>>(qkv, T, E, H, hd, scale, o, tiles);
     else if (half <= 32) dot_attn_tiles_kernel<32><<<grid, 2 * DQ, 0, st>>>(qkv, T, E, H, hd, scale, o, tiles);
+    else if (half <= 64) dot_attn_tiles_kernel<64><<<grid, 2 * DQ, 0, st>>>(qkv, T, E, H, hd, scale, o, tiles);
     else {
-        *msg = "listed dot-product attention tiles support head_dim <= 64";
+        *msg = "listed dot-product attention tiles support head_dim <= 128";
         return WB_ENOTSUP;
     }
     cudaError_t e = cudaGetLastError();

@@ -346,8 +346,12 @@ struct AttnItem {
 
 template <int HDP, int FW>
 struct AttnSmem {
-    static constexpr int Q_BYTES = QT * FW * 2;      // 4 / 16 KB
-    static constexpr int K_BYTES = KT * FW * 2;      // 4 / 16 KB
+    // feature rows of FW = 128 (dot-product attention at head_dim 65-128)
+    // sit in two 64-column swizzle atoms, one 16 KB block per atom
+    static_assert(FW == 16 || FW == 64 || FW == 128, "feature width 16, 64 or 128");
+    static constexpr int FCH = FW > 64 ? FW / 64 : 1;  // TMA boxes per Q / K tile
+    static constexpr int Q_BYTES = QT * FW * 2;      // 4 / 16 / 32 KB
+    static constexpr int K_BYTES = KT * FW * 2;      // 4 / 16 / 32 KB
     static constexpr int V_BYTES = KT * HDP * 2;     // one fp16 value tile: 16 / 32 KB
     // epilogue staging per warp, 1024-byte aligned: a 32 x 32 fp32 tile in
     // the 128-byte swizzle for the TMA store (4 KB), or 32 x 33 floats
@@ -466,8 +470,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     __syncthreads();
     ptx::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    constexpr uint32_t F_SW = FW == 64 ? ptx::UMMA_SW128 : ptx::UMMA_SW32;
-    constexpr uint32_t F_SBO = FW == 64 ? 1024 : 256;  // 8 rows of the swizzle atom
+    constexpr uint32_t F_SW = FW >= 64 ? ptx::UMMA_SW128 : ptx::UMMA_SW32;
+    constexpr uint32_t F_SBO = FW >= 64 ? 1024 : 256;  // 8 rows of the swizzle atom
 
     if (warp == ATT_W_PROD) {
         // ---------------- producer: work items, Q and K/V tiles
@@ -500,8 +504,9 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                 bh = grp * ATT_GROUP + rr % gsz;
                 qt = a.n_qt - 1 - rr / gsz;
                 bool violate = false;
-                if (FW == 64) {
-                    // bounded-score test of the tile's rows (content only)
+                if (FW >= 64) {
+                    // bounded-score test of the tile's rows (content and
+                    // dot-product features)
                     const float cm = __uint_as_float(__ldg(a.cmax + bh));
 #pragma unroll
                     for (int u = 0; u < 4; u++) {
@@ -570,7 +575,10 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                 if (i >= 2 && !att_wait(qfree + qb, ((i - 2) >> 1) & 1, abort_flag)) ok = false;
                 if (ok) {
                     ptx::mbar_arrive_expect_tx(qfull + qb, L::Q_BYTES);
-                    ptx::tma_load_3d(sm + L::OFF_Q + qb * L::Q_BYTES, &tm_q, qfull + qb, 0, qt * QT, bh);
+#pragma unroll
+                    for (int c = 0; c < L::FCH; c++)
+                        ptx::tma_load_3d(sm + L::OFF_Q + qb * L::Q_BYTES + c * (QT * 128), &tm_q, qfull + qb, c * 64,
+                                         qt * QT, bh);
                 }
                 for (int j = 0; ok && j <= qt; j++, g++) {
                     const int st = (int)(g % ST);
@@ -580,7 +588,10 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                         break;
                     }
                     ptx::mbar_arrive_expect_tx(kvfull + st, L::K_BYTES + L::V_BYTES);
-                    ptx::tma_load_3d(sm + L::OFF_K + st * L::K_BYTES, &tm_k, kvfull + st, 0, j * KT, bh);
+#pragma unroll
+                    for (int c = 0; c < L::FCH; c++)
+                        ptx::tma_load_3d(sm + L::OFF_K + st * L::K_BYTES + c * (KT * 128), &tm_k, kvfull + st, c * 64,
+                                         j * KT, bh);
                     uint8_t *vst = sm + L::OFF_V + st * L::V_BYTES;
 #pragma unroll
                     for (int c = 0; c < HDP / 64; c++)
@@ -693,9 +704,12 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                 const uint32_t S_t = tmem + (uint32_t)((gq % NS) * 128);
                 const uint32_t sQ = sQ0 + (uint32_t)((kq & 1) * L::Q_BYTES);
                 const uint64_t ad0 = ptx::smem_desc(sQ, 16, F_SBO, F_SW), bd0 = ptx::smem_desc(sK, 16, F_SBO, F_SW);
+                // K = 16 per MMA: 32 bytes along a 128-byte swizzle row; past
+                // 64 columns the next atom block (QT / KT rows x 128 B)
 #pragma unroll
                 for (int kk = 0; kk < FW / 16; kk++)
-                    ptx::mma_bf16(S_t, ad0 + (uint64_t)(kk * 2), bd0 + (uint64_t)(kk * 2), IDESC_QK, kk > 0);
+                    ptx::mma_bf16(S_t, ad0 + (uint64_t)((kk >> 2) * (QT * 8) + (kk & 3) * 2),
+                                  bd0 + (uint64_t)((kk >> 2) * (KT * 8) + (kk & 3) * 2), IDESC_QK, kk > 0);
                 ptx::mma_commit(sfull + (int)(gq % NS));
                 gq++;
                 if (++jq == qtk + 1) {
@@ -1070,9 +1084,11 @@ struct CoreLayout {
     size_t qf, kf, vh, m0, sp, cn, cm, sched, o, end;
 };
 static int core_fw(bool content) { return content ? 64 : 16; }
-static CoreLayout core_layout(const TcLayerWeights &t, int B, int T, size_t off, int Hg, bool content) {
+// fw_dot: feature width of the dot-product core (64 or 128), 0 for wave attention
+static CoreLayout core_layout(const TcLayerWeights &t, int B, int T, size_t off, int Hg, bool content,
+                              int fw_dot = 0) {
     const int hdp = t.hd <= 64 ? 64 : 128;
-    const int fw = core_fw(content);
+    const int fw = fw_dot ? fw_dot : core_fw(content);
     const long long BH = (long long)B * Hg, R = (long long)B * T;
     const int n_qt = (T + QT - 1) / QT;
     Carve cv;
@@ -1271,8 +1287,8 @@ struct DotFeatArgs {
     const float *qkv;  // [B*T][3E]
     int B, H, T, hd, E;
     float scale;
-    __nv_bfloat16 *qf, *kf;  // [BH][T][64]
-    __half *vh;              // [BH][T][64] values (fp16)
+    __nv_bfloat16 *qf, *kf;  // [BH][T][FW]
+    __half *vh;              // [BH][T][FW] values (fp16)
     float *m0, *sprev, *cnorm;         // [BH][T]
     unsigned int *cmax;                // [BH], float bits of max |k|
 };
@@ -1292,7 +1308,12 @@ static int dot_feat_rows(int E) {
     return std::max(1, std::min(DOT_FEAT_ROWS, DOT_FEAT_SMEM / (3 * E * (int)sizeof(float))));
 }
 
+// FW = 64 (head_dim <= 64) or 128: each lane forms FW / 32 adjacent columns
+// of a row's features and values (zero past head_dim).
+template <int FW>
 __global__ void __launch_bounds__(DOT_FEAT_WARPS * 32) dot_feat_kernel(DotFeatArgs a, int rows) {
+    static_assert(FW == 64 || FW == 128, "dot-product feature width");
+    constexpr int EPL = FW / 32;  // columns per lane
     extern __shared__ float xs[];  // [rows][3E]
     constexpr int NT = DOT_FEAT_WARPS * 32;
     constexpr int U = 4;  // loads per thread per batch
@@ -1333,21 +1354,33 @@ __global__ void __launch_bounds__(DOT_FEAT_WARPS * 32) dot_feat_kernel(DotFeatAr
         for (int r = 0; r < nr; r++) {
             const long long i = bh * a.T + t0 + r;  // feature row
             const float *row = xs + r * 3 * a.E + h * a.hd;
-            float q[2], k[2], v[2];
+            float q[EPL], k[EPL], v[EPL];
 #pragma unroll
-            for (int u = 0; u < 2; u++) {
-                const int d = 2 * lane + u;
+            for (int u = 0; u < EPL; u++) {
+                const int d = EPL * lane + u;
                 const bool ok = d < a.hd;
                 q[u] = ok ? row[d] * a.scale : 0.0f;
                 k[u] = ok ? row[a.E + d] : 0.0f;
                 v[u] = ok ? row[2 * a.E + d] : 0.0f;
             }
-            reinterpret_cast<uint32_t *>(a.qf + i * 64)[lane] = pack_bf16(q[0], q[1]);
-            reinterpret_cast<uint32_t *>(a.kf + i * 64)[lane] = pack_bf16(k[0], k[1]);
-            reinterpret_cast<uint32_t *>(a.vh + i * 64)[lane] = pack_f16(v[0], v[1]);
-            float s = fmaf(q[0], k[0], q[1] * k[1]);
-            float qq = fmaf(q[0], q[0], q[1] * q[1]);
-            float kk = fmaf(k[0], k[0], k[1] * k[1]);
+            float s, qq, kk;
+            if constexpr (EPL == 2) {
+                reinterpret_cast<uint32_t *>(a.qf + i * FW)[lane] = pack_bf16(q[0], q[1]);
+                reinterpret_cast<uint32_t *>(a.kf + i * FW)[lane] = pack_bf16(k[0], k[1]);
+                reinterpret_cast<uint32_t *>(a.vh + i * FW)[lane] = pack_f16(v[0], v[1]);
+                s = fmaf(q[0], k[0], q[1] * k[1]);
+                qq = fmaf(q[0], q[0], q[1] * q[1]);
+                kk = fmaf(k[0], k[0], k[1] * k[1]);
+            } else {
+                reinterpret_cast<uint2 *>(a.qf + i * FW)[lane] =
+                    make_uint2(pack_bf16(q[0], q[1]), pack_bf16(q[2], q[3]));
+                reinterpret_cast<uint2 *>(a.kf + i * FW)[lane] =
+                    make_uint2(pack_bf16(k[0], k[1]), pack_bf16(k[2], k[3]));
+                reinterpret_cast<uint2 *>(a.vh + i * FW)[lane] = make_uint2(pack_f16(v[0], v[1]), pack_f16(v[2], v[3]));
+                s = fmaf(q[0], k[0], q[1] * k[1]) + fmaf(q[2], k[2], q[3] * k[3]);
+                qq = fmaf(q[0], q[0], q[1] * q[1]) + fmaf(q[2], q[2], q[3] * q[3]);
+                kk = fmaf(k[0], k[0], k[1] * k[1]) + fmaf(k[2], k[2], k[3] * k[3]);
+            }
 #pragma unroll
             for (int o = 16; o; o >>= 1) {
                 s += __shfl_xor_sync(0xffffffffu, s, o);
@@ -1365,23 +1398,28 @@ __global__ void __launch_bounds__(DOT_FEAT_WARPS * 32) dot_feat_kernel(DotFeatAr
     }
 }
 
-size_t tc_dot_core_bytes(int B, int T, int H) {
+// features and values padded to 64 columns up to head_dim 64, else 128
+static int dot_fw(int hd) { return hd <= 64 ? 64 : 128; }
+
+size_t tc_dot_core_bytes(int B, int T, int E, int H) {
+    const int fw = dot_fw(E / H);
     TcLayerWeights t{};
-    t.E = 64 * H;
+    t.E = fw * H;
     t.H = H;
-    t.hd = 64;
+    t.hd = fw;
     // the core layout without its merged-output rows (the caller owns o)
-    const CoreLayout c = core_layout(t, B, T, 0, H, true);
+    const CoreLayout c = core_layout(t, B, T, 0, H, true, fw);
     return c.o;
 }
 
 int tc_dot_attention(const float *qkv, int B, int T, int E, int H, float *o, void *ws, int force_fallback,
                      uint32_t *dev_err, int sm_count, cudaStream_t st, std::string *msg) {
     const int hd = E / H;
-    if (hd > 64) {
-        *msg = "the tensor-core dot-product core supports head_dim <= 64";
+    if (hd > 128) {
+        *msg = "the tensor-core dot-product core supports head_dim <= 128";
         return WB_ENOTSUP;
     }
+    const int fw = dot_fw(hd);
     const long long BH = (long long)B * H;
     const int n_qt = (T + QT - 1) / QT;
     if (BH * n_qt > 0x7fffffffLL) {
@@ -1389,10 +1427,10 @@ int tc_dot_attention(const float *qkv, int B, int T, int E, int H, float *o, voi
         return WB_EINVAL;
     }
     TcLayerWeights t{};
-    t.E = 64 * H;
+    t.E = fw * H;
     t.H = H;
-    t.hd = 64;
-    const CoreLayout lay = core_layout(t, B, T, 0, H, true);
+    t.hd = fw;
+    const CoreLayout lay = core_layout(t, B, T, 0, H, true, fw);
     char *w = (char *)ws;
     __nv_bfloat16 *qf = (__nv_bfloat16 *)(w + lay.qf), *kf = (__nv_bfloat16 *)(w + lay.kf);
     __half *vh = (__half *)(w + lay.vh);
@@ -1410,13 +1448,13 @@ int tc_dot_attention(const float *qkv, int B, int T, int E, int H, float *o, voi
         const int rows = dot_feat_rows(E);
         const unsigned grid = (unsigned)((long long)B * ((T + rows - 1) / rows));
         const size_t smem = (size_t)rows * 3 * E * sizeof(float);
+        auto kern = fw == 64 ? dot_feat_kernel<64> : dot_feat_kernel<128>;
         if (smem > 48 * 1024 &&
-            cudaFuncSetAttribute(dot_feat_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-                cudaSuccess) {
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
             *msg = "n_embd too large for the dot-product feature kernel";
             return WB_EINVAL;
         }
-        dot_feat_kernel<<<grid, DOT_FEAT_WARPS * 32, smem, st>>>(fa, rows);
+        kern<<<grid, DOT_FEAT_WARPS * 32, smem, st>>>(fa, rows);
     }
     if (force_fallback) {
         // testing: every tile fails the bound (|q| max|k| - s_self > limit)
@@ -1428,8 +1466,10 @@ int tc_dot_attention(const float *qkv, int B, int T, int E, int H, float *o, voi
     int rc;
     CUtensorMap tq, tk, tv;
     {
-        const uint64_t dims[3] = {64, (uint64_t)T, (uint64_t)BH};
-        const uint64_t strides[2] = {128, (uint64_t)T * 128};
+        // rows of fw bf16 / fp16; boxes of 64 columns (one 128-byte swizzle
+        // atom), two per tile at fw = 128
+        const uint64_t dims[3] = {(uint64_t)fw, (uint64_t)T, (uint64_t)BH};
+        const uint64_t strides[2] = {(uint64_t)fw * 2, (uint64_t)T * fw * 2};
         const uint32_t box[3] = {64, 128, 1};
         if ((rc = make_tmap(&tq, qf, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, dims, strides, box,
                             CU_TENSOR_MAP_SWIZZLE_128B, msg)) ||
@@ -1442,7 +1482,9 @@ int tc_dot_attention(const float *qkv, int B, int T, int E, int H, float *o, voi
     WbSeqView none{};
     AttnTcArgs aa{(int)BH, H, T, hd, n_qt, H, 0, (int)(BH * n_qt), m0, sp, cn, cm, none, o, E, sched, dev_err, 1,
                   BOUND_LIMIT};
-    if ((rc = launch_attn_tc<64, 64>(tq, tk, tv, aa, sm_count, st, msg))) return rc;
+    if ((rc = fw == 64 ? launch_attn_tc<64, 64>(tq, tk, tv, aa, sm_count, st, msg)
+                       : launch_attn_tc<128, 128>(tq, tk, tv, aa, sm_count, st, msg)))
+        return rc;
     return launch_dot_attn_tiles(qkv, B, T, E, H, o, sched + 1, (int)(BH * n_qt), st, msg);
 }
 

@@ -57,11 +57,12 @@ int tc_kv_decode(const TcLayerWeights &t, const WbSeqView &sv, int32_t *len, int
                  cudaStream_t st, std::string *msg, bool chain = false, bool *ends_with_out = nullptr);
 
 // Dot-product attention core (compute.rs:357-414) on the tcgen05 attention
-// kernel: qkv [B*T][3E] (device) -> o [B*T][E], head_dim <= 64 (WB_ENOTSUP
-// above).  ws: tc_dot_core_bytes(B, T, H) bytes of device scratch.  Query
-// tiles whose scores could overflow the fixed shift are recomputed by the
-// fp32 core; force_fallback (testing) sends every tile there.
-size_t tc_dot_core_bytes(int B, int T, int H);
+// kernel: qkv [B*T][3E] (device) -> o [B*T][E], head_dim <= 128 (WB_ENOTSUP
+// above; features and values padded to 64 or 128 columns).  ws:
+// tc_dot_core_bytes(B, T, E, H) bytes of device scratch.  Query tiles whose
+// scores could overflow the fixed shift are recomputed by the fp32 core;
+// force_fallback (testing) sends every tile there.
+size_t tc_dot_core_bytes(int B, int T, int E, int H);
 int tc_dot_attention(const float *qkv, int B, int T, int E, int H, float *o, void *ws, int force_fallback,
                      uint32_t *dev_err, int sm_count, cudaStream_t st, std::string *msg);
 
