@@ -1089,7 +1089,8 @@ def run_profile_case(args):
     prefills (KV cache, no content) of one 768-dim layer, 16 x 1024 tokens
     (about 10 work items per SM, as in the benchmark's 20); 'dot' = 3
     dot-product attention forwards of one 768-dim layer, 16 x 1024 tokens;
-    'serve-ffn' = 3 serve-layer FFN calls on 16 x 1024 rows."""
+    'dot-4096' = the same for one 4096-dim layer (32 heads x 128), 2 x 4096
+    tokens; 'serve-ffn' = 3 serve-layer FFN calls on 16 x 1024 rows."""
     import numpy as np
     import torch
     import wave_engine_b200 as wb
@@ -1155,6 +1156,14 @@ def run_profile_case(args):
         for _ in range(3):
             wb.attention(dl, x, ctx=ctx)
         extra["attn_core_flops_per_launch"] = 16 * H * CFG["seq_len"] * (CFG["seq_len"] + 1) // 2 * 4 * hd
+    elif args.profile_case == "dot-4096":
+        # 3 dot-product attention forwards of one 4096-dim layer (head_dim 128), 2 x 4096 tokens
+        H4, E4, T4 = 32, 4096, 4096
+        dl = wb.DotAttnLayer(ctx, wb.gaussian_attention_weights(5000, H4, E4))
+        x = torch.randn((2, T4, E4), generator=g, device="cuda")
+        for _ in range(3):
+            wb.attention(dl, x, ctx=ctx)
+        extra["attn_core_flops_per_launch"] = 2 * H4 * T4 * (T4 + 1) // 2 * 4 * (E4 // H4)
     elif args.profile_case == "serve-ffn":
         # 3 FFN calls (maestro 16, RK4-16) on 16 requests x 1024 rows of the 768-dim model
         ffn = wb.FfnLayer(ctx, wb.gaussian_ffn(2000, E, 16))
@@ -1181,7 +1190,7 @@ def main():
                          "context 128-4096; prefill-168/-384/-4096: prefill through all layers of the 168-, "
                          "384- and 4096-dim models; dot-768: the legacy dot-product attention at the 768-dim "
                          "shape; serve-model: the whole serve layer (attention + FFN + decoder) on the GPU")
-    ap.add_argument("--profile-case", choices=["decode", "decode-stress", "prefill", "prefill-serve", "dot", "serve-ffn"],
+    ap.add_argument("--profile-case", choices=["decode", "decode-stress", "prefill", "prefill-serve", "dot", "dot-4096", "serve-ffn"],
                     default=None,
                     help="run a small case for an ncu capture instead of the benchmark")
     ap.add_argument("--shard", choices=["batch", "heads"], default="batch",

@@ -113,3 +113,41 @@ def test_dot_core_on_tensor_cores_and_fallback_tiles(ctx, E, H, T):
     assert np.array_equal(o_tc[1, :, hd:2 * hd], o_fma[1, :, hd:2 * hd]), "flagged head not from the fallback"
     assert "dot_attn_fallback" in rep
     assert ctx.take_device_error() == 0
+
+
+@pytest.mark.parametrize("E,H,T", [(256, 4, 300), (512, 4, 300)])
+def test_dot_core_runtime_overflow_goes_to_fallback(ctx, E, H, T):
+    """A row whose largest score lies far above its shift (the largest of its
+    self, key-0 and previous-key scores) while the a-priori bound
+    |q| max|k| - shift stays below the limit: key 50 of (sequence 0, head 0)
+    scores ~20 above every sampled score for queries 60+, so its fp16
+    probability would overflow.  The softmax warps must list that query tile
+    at run time: its rows come from the fp32 core (bitwise), the rest stay
+    within 2e-3 of a float64 statement."""
+    import torch
+    from wave_engine_b200 import _lib
+    B = 2
+    hd = E // H
+    g = np.random.default_rng(E + 7)
+    qkv = (g.standard_normal((B, T, 3 * E)) * 0.55).astype(np.float32)
+    amp = np.sqrt(20.0 * np.sqrt(hd))            # q . k / sqrt(hd) ~ 20 on dim 0
+    qkv[0, :, E + 0] = 0.0                       # keys of head 0: nothing on dim 0 ...
+    qkv[0, 50, E + 0] = amp                      # ... except key 50
+    qkv[0, 60:, 0] = amp                         # queries 60+ point at it
+    qn = np.linalg.norm(qkv[0, :, :hd], axis=1) / np.sqrt(hd)
+    kmax = np.linalg.norm(qkv[0, :, E:E + hd], axis=1).max()
+    assert (qn * kmax).max() < 40.0              # the a-priori test passes these rows
+    ref = _dot_core_f64(qkv, H)
+    q_d = torch.from_numpy(qkv).cuda()
+    outs = []
+    for mode in (0, 2):
+        o = torch.full((B, T, E), float("nan"), device="cuda")
+        _lib.call("wb_test_dot_core", ctx.handle, q_d.data_ptr(), B, T, E, H, mode, o.data_ptr())
+        torch.cuda.synchronize()
+        outs.append(o.cpu().numpy())
+    o_tc, o_fma = outs
+    assert np.isfinite(o_tc).all()
+    assert np.array_equal(o_tc[0, :128, :hd], o_fma[0, :128, :hd]), "overflowing tile not from the fallback"
+    r = check("tensor-core core", o_tc, ref, TENSOR_TOL)
+    assert r.passed, str(r)
+    assert ctx.take_device_error() == 0

@@ -52,6 +52,13 @@ static constexpr float MASK_BIAS = -512.0f;
 // whose scores may exceed the fixed shift by more than this goes to the fp32
 // fallback
 static constexpr float BOUND_LIMIT = 10.0f;
+// Dot-product attention: the a-priori bound only keeps the fp32 exponentials
+// finite; whether a probability fits fp16 is checked per key tile at run time
+// (a thread's 64 probabilities of one tile summing past DOT_P_TILE_SUM, fp16's
+// largest finite value -- the only way one of them can exceed it -- sends the
+// query tile to the fp32 fallback).
+static constexpr float DOT_BOUND_LIMIT = 60.0f;
+static constexpr float DOT_P_TILE_SUM = 65504.0f;
 
 // ---------------------------------------------------------------------------
 // Tensor maps (driver entry point fetched at run time; no libcuda link).
@@ -316,9 +323,10 @@ struct AttnTcArgs {
     int E;
     int *sched;                 // [0] work counter, [1] fallback count, [2..] fallback tiles bh * n_qt + qt
     uint32_t *dev_err;
-    int dot;                    // dot-product features: bound |q| max|k| - s_self instead of the content bound
+    int dot;                    // dot-product features: bound |q| max|k| - shift instead of the content bound
     float bound;                // a score may exceed the row's shift by at most this (else the tile falls back)
     int o_tma;                  // o tiles leave by TMA stores through tm_o (head_dim a multiple of 32)
+    int *tflag;                 // dot: per-tile flags [BH * n_qt], zero at launch (tiles listed at run time)
 };
 
 __device__ __forceinline__ float fast_exp2(float x) {
@@ -755,7 +763,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
             const float ep = sp > -INFINITY ? fast_exp2(fmaf(sp, LOG2E, nm0)) : 0.0f;
             const uint64_t l2e2 = ptx::f2_pack(LOG2E, LOG2E), nm2 = ptx::f2_pack(nm0, nm0);
             uint64_t l2 = ptx::f2_pack(0.0f, 0.0f);  // row-sum partials of even and odd columns
-            bool ok = true;
+            bool ok = true, ovf = false;
             for (int j = 0; j <= qt; j++, g++) {
                 if ((int)(g & 1) != grp) continue;
                 const int sb = (int)(g % NS);
@@ -809,6 +817,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                     }
                 };
                 {
+                    const uint64_t l2_before = l2;
                     uint32_t r[32];
                     ptx::tmem_ld32(S_t, r);
                     ptx::tmem_ld_wait();
@@ -816,6 +825,14 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                     ptx::tmem_ld32(S_t + 32, r);
                     ptx::tmem_ld_wait();
                     exps(r, pk1, half * 64 + 32);
+                    if (a.dot) {
+                        // this tile's 64 probabilities of the row (the running
+                        // sums' increase): past the limit one may not fit fp16
+                        float b0, b1, a0, a1;
+                        ptx::f2_unpack(l2_before, b0, b1);
+                        ptx::f2_unpack(l2, a0, a1);
+                        ovf |= !((a0 - b0) + (a1 - b1) <= DOT_P_TILE_SUM);
+                    }
                 }
                 // P over the first half of this thread's (already read) S columns
                 ptx::tmem_st16(S_t, pk0);
@@ -836,6 +853,12 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
             if (k >= LAG && !att_wait(ofree + (k - LAG) % L::OBUF, ((k - LAG) / L::OBUF) & 1, abort_flag)) {
                 atomicOr(a.dev_err, WB_DERR_TIMEOUT_SOFTMAX);
                 break;
+            }
+            if (ovf) {
+                // dot-product features: the query tile goes to the fp32
+                // fallback list once (its O from this kernel is overwritten)
+                const int tile = bh * a.n_qt + qt;
+                if (atomicExch(a.tflag + tile, 1) == 0) a.sched[2 + atomicAdd(a.sched + 1, 1)] = tile;
             }
             float l0, l1;
             ptx::f2_unpack(l2, l0, l1);
@@ -1081,7 +1104,7 @@ void tc_layer_free(TcLayerWeights *t) {
 
 // Workspace pieces of the attention core, carved after `off`.
 struct CoreLayout {
-    size_t qf, kf, vh, m0, sp, cn, cm, sched, o, end;
+    size_t qf, kf, vh, m0, sp, cn, cm, sched, tflag, o, end;
 };
 static int core_fw(bool content) { return content ? 64 : 16; }
 // fw_dot: feature width of the dot-product core (64 or 128), 0 for wave attention
@@ -1102,6 +1125,7 @@ static CoreLayout core_layout(const TcLayerWeights &t, int B, int T, size_t off,
     c.cn = cv.take<float>(BH * T);
     c.cm = cv.take<unsigned int>(BH);
     c.sched = cv.take<int>(2 + BH * n_qt);
+    c.tflag = fw_dot ? cv.take<int>(BH * n_qt) : 0;
     c.o = cv.take<float>(R * t.E);
     c.end = cv.off;
     return c;
@@ -1295,101 +1319,147 @@ struct DotFeatArgs {
 
 static constexpr int DOT_FEAT_WARPS = 8;
 
-// DOT_FEAT_ROWS consecutive input rows (b, t..t+R-1) per CTA (fewer when a
-// row is long): their 3E values are one contiguous stretch, read with
-// four 16-byte loads per thread in flight (4-byte loads when the
-// stretch is not 16-byte aligned) into shared memory; then warp w takes heads
-// w, w + 8, ... of every row and raises max |k| of a head once per CTA (the
-// per-row atomics on one address per head serialised in L2 and took more
-// than half of the kernel's time)
+// DOT_FEAT_ROWS consecutive input rows (b, t..t+R-1) per CTA; warp w takes
+// heads w, w + 8, ... of those rows.  A warp loads the q, k and v slices of
+// all R rows of a head straight from global memory (3R loads per lane in
+// flight: 16- or 8-byte loads when the slice is a full, aligned FW-wide
+// run, else predicated 4-byte loads), then forms each row's features and
+// raises max |k| of the head once for the R rows (per-row atomics on one
+// address per head serialised in L2).
+// The row's fixed softmax shift m0 is the largest of the scores of four keys
+// it certainly sees (causal): its own, the previous one, key t0/2 and key 0
+// (t0 the row group's first row).  So the
+// row's largest probability is at least ~1 (no underflow); a shift far below
+// the row's true maximum shows at run time (DOT_P_TILE_SUM).
 static constexpr int DOT_FEAT_ROWS = 4;
-static constexpr int DOT_FEAT_SMEM = 48 * 1024;
-static int dot_feat_rows(int E) {
-    return std::max(1, std::min(DOT_FEAT_ROWS, DOT_FEAT_SMEM / (3 * E * (int)sizeof(float))));
-}
 
 // FW = 64 (head_dim <= 64) or 128: each lane forms FW / 32 adjacent columns
-// of a row's features and values (zero past head_dim).
+// of a row's features and values (zero past head_dim).  vec: hd == FW and
+// every slice start aligned to FW / 32 floats.
 template <int FW>
-__global__ void __launch_bounds__(DOT_FEAT_WARPS * 32) dot_feat_kernel(DotFeatArgs a, int rows) {
+__global__ void __launch_bounds__(DOT_FEAT_WARPS * 32) dot_feat_kernel(DotFeatArgs a, int vec) {
     static_assert(FW == 64 || FW == 128, "dot-product feature width");
     constexpr int EPL = FW / 32;  // columns per lane
-    extern __shared__ float xs[];  // [rows][3E]
-    constexpr int NT = DOT_FEAT_WARPS * 32;
-    constexpr int U = 4;  // loads per thread per batch
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int n_tb = (a.T + rows - 1) / rows;  // row groups per sequence (a group stays within one)
-    const int b = blockIdx.x / n_tb, t0 = (blockIdx.x - b * n_tb) * rows;
-    const int nr = min(rows, a.T - t0);
-    const int n = 3 * a.E * nr;
-    const float *src_rows = a.qkv + ((long long)b * a.T + t0) * 3LL * a.E;
-    if ((n & 3) == 0 && (reinterpret_cast<uintptr_t>(src_rows) & 15) == 0) {
-        const float4 *src = reinterpret_cast<const float4 *>(src_rows);
-        float4 *dst = reinterpret_cast<float4 *>(xs);
-        const int n4 = n >> 2;
-        for (int j0 = tid; j0 < n4; j0 += U * NT) {
-            float4 r[U];
-#pragma unroll
-            for (int u = 0; u < U; u++)
-                if (j0 + u * NT < n4) r[u] = __ldg(src + j0 + u * NT);
-#pragma unroll
-            for (int u = 0; u < U; u++)
-                if (j0 + u * NT < n4) dst[j0 + u * NT] = r[u];
-        }
-    } else {
-        for (int j0 = tid; j0 < n; j0 += U * NT) {
-            float r[U];
-#pragma unroll
-            for (int u = 0; u < U; u++)
-                if (j0 + u * NT < n) r[u] = __ldg(src_rows + j0 + u * NT);
-#pragma unroll
-            for (int u = 0; u < U; u++)
-                if (j0 + u * NT < n) xs[j0 + u * NT] = r[u];
-        }
-    }
-    __syncthreads();
-    for (int h = warp; h < a.H; h += DOT_FEAT_WARPS) {
-        const long long bh = (long long)b * a.H + h;
-        float kmax = 0.0f;
-        for (int r = 0; r < nr; r++) {
-            const long long i = bh * a.T + t0 + r;  // feature row
-            const float *row = xs + r * 3 * a.E + h * a.hd;
-            float q[EPL], k[EPL], v[EPL];
+    constexpr int R = DOT_FEAT_ROWS;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int n_tb = (a.T + R - 1) / R;  // row groups per sequence (a group stays within one)
+    const int b = blockIdx.x / n_tb, t0 = (blockIdx.x - b * n_tb) * R;
+    const int nr = min(R, a.T - t0);
+    const long long rs = 3LL * a.E;  // qkv row stride
+    const float *rows0 = a.qkv + ((long long)b * a.T + t0) * rs;
+    const float *seq0 = a.qkv + (long long)b * a.T * rs;
+    // EPL columns of a head slice starting at p (zero past head_dim or when !ok)
+    auto load_slice = [&](const float *p, bool ok, float (&dst)[EPL]) {
+        if (vec) {
+            if constexpr (EPL == 4) {
+                float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (ok) f = __ldg(reinterpret_cast<const float4 *>(p) + lane);
+                dst[0] = f.x, dst[1] = f.y, dst[2] = f.z, dst[3] = f.w;
+            } else {
+                float2 f = make_float2(0.f, 0.f);
+                if (ok) f = __ldg(reinterpret_cast<const float2 *>(p) + lane);
+                dst[0] = f.x, dst[1] = f.y;
+            }
+        } else {
 #pragma unroll
             for (int u = 0; u < EPL; u++) {
                 const int d = EPL * lane + u;
-                const bool ok = d < a.hd;
-                q[u] = ok ? row[d] * a.scale : 0.0f;
-                k[u] = ok ? row[a.E + d] : 0.0f;
-                v[u] = ok ? row[2 * a.E + d] : 0.0f;
+                dst[u] = ok && d < a.hd ? __ldg(p + d) : 0.0f;
             }
+        }
+    };
+    // lane-partial dot product in the order of the self score below
+    auto part_dot = [&](const float (&x)[EPL], const float (&y)[EPL]) {
+        float d = fmaf(x[0], y[0], x[1] * y[1]);
+        if constexpr (EPL == 4) d += fmaf(x[2], y[2], x[3] * y[3]);
+        return d;
+    };
+    for (int h = warp; h < a.H; h += DOT_FEAT_WARPS) {
+        const long long bh = (long long)b * a.H + h;
+        float q[R][EPL], k[R][EPL], v[R][EPL], k0[EPL], kh[EPL], kp[EPL];
+        // keys 0, t0 / 2 and t0 - 1 of the sequence (visible to every row of the group)
+        load_slice(seq0 + a.E + h * a.hd, true, k0);
+        load_slice(seq0 + (long long)(t0 >> 1) * rs + a.E + h * a.hd, true, kh);
+        load_slice(rows0 - rs + a.E + h * a.hd, t0 > 0, kp);
+#pragma unroll
+        for (int r = 0; r < R; r++) {
+            const float *row = rows0 + r * rs + h * a.hd;
+            const bool rok = r < nr;
+            if (vec) {
+                if constexpr (EPL == 4) {
+                    float4 z = make_float4(0.f, 0.f, 0.f, 0.f), fq = z, fk = z, fv = z;
+                    if (rok) {
+                        fq = __ldg(reinterpret_cast<const float4 *>(row) + lane);
+                        fk = __ldg(reinterpret_cast<const float4 *>(row + a.E) + lane);
+                        fv = __ldg(reinterpret_cast<const float4 *>(row + 2 * a.E) + lane);
+                    }
+                    q[r][0] = fq.x, q[r][1] = fq.y, q[r][2] = fq.z, q[r][3] = fq.w;
+                    k[r][0] = fk.x, k[r][1] = fk.y, k[r][2] = fk.z, k[r][3] = fk.w;
+                    v[r][0] = fv.x, v[r][1] = fv.y, v[r][2] = fv.z, v[r][3] = fv.w;
+                } else {
+                    float2 z = make_float2(0.f, 0.f), fq = z, fk = z, fv = z;
+                    if (rok) {
+                        fq = __ldg(reinterpret_cast<const float2 *>(row) + lane);
+                        fk = __ldg(reinterpret_cast<const float2 *>(row + a.E) + lane);
+                        fv = __ldg(reinterpret_cast<const float2 *>(row + 2 * a.E) + lane);
+                    }
+                    q[r][0] = fq.x, q[r][1] = fq.y;
+                    k[r][0] = fk.x, k[r][1] = fk.y;
+                    v[r][0] = fv.x, v[r][1] = fv.y;
+                }
+            } else {
+#pragma unroll
+                for (int u = 0; u < EPL; u++) {
+                    const int d = EPL * lane + u;
+                    const bool ok = rok && d < a.hd;
+                    q[r][u] = ok ? __ldg(row + d) : 0.0f;
+                    k[r][u] = ok ? __ldg(row + a.E + d) : 0.0f;
+                    v[r][u] = ok ? __ldg(row + 2 * a.E + d) : 0.0f;
+                }
+            }
+        }
+        float kmax = 0.0f;
+#pragma unroll
+        for (int r = 0; r < R; r++) {
+            if (r >= nr) break;
+            const long long i = bh * a.T + t0 + r;  // feature row
+#pragma unroll
+            for (int u = 0; u < EPL; u++) q[r][u] *= a.scale;
+            // scores against keys 0, t0 / 2 and the previous one (row t0 + r - 1)
+            float s0 = part_dot(q[r], k0), s1 = part_dot(q[r], kh);
+            float sq = r == 0 ? part_dot(q[r], kp) : part_dot(q[r], k[r > 0 ? r - 1 : 0]);
             float s, qq, kk;
             if constexpr (EPL == 2) {
-                reinterpret_cast<uint32_t *>(a.qf + i * FW)[lane] = pack_bf16(q[0], q[1]);
-                reinterpret_cast<uint32_t *>(a.kf + i * FW)[lane] = pack_bf16(k[0], k[1]);
-                reinterpret_cast<uint32_t *>(a.vh + i * FW)[lane] = pack_f16(v[0], v[1]);
-                s = fmaf(q[0], k[0], q[1] * k[1]);
-                qq = fmaf(q[0], q[0], q[1] * q[1]);
-                kk = fmaf(k[0], k[0], k[1] * k[1]);
+                reinterpret_cast<uint32_t *>(a.qf + i * FW)[lane] = pack_bf16(q[r][0], q[r][1]);
+                reinterpret_cast<uint32_t *>(a.kf + i * FW)[lane] = pack_bf16(k[r][0], k[r][1]);
+                reinterpret_cast<uint32_t *>(a.vh + i * FW)[lane] = pack_f16(v[r][0], v[r][1]);
+                s = fmaf(q[r][0], k[r][0], q[r][1] * k[r][1]);
+                qq = fmaf(q[r][0], q[r][0], q[r][1] * q[r][1]);
+                kk = fmaf(k[r][0], k[r][0], k[r][1] * k[r][1]);
             } else {
                 reinterpret_cast<uint2 *>(a.qf + i * FW)[lane] =
-                    make_uint2(pack_bf16(q[0], q[1]), pack_bf16(q[2], q[3]));
+                    make_uint2(pack_bf16(q[r][0], q[r][1]), pack_bf16(q[r][2], q[r][3]));
                 reinterpret_cast<uint2 *>(a.kf + i * FW)[lane] =
-                    make_uint2(pack_bf16(k[0], k[1]), pack_bf16(k[2], k[3]));
-                reinterpret_cast<uint2 *>(a.vh + i * FW)[lane] = make_uint2(pack_f16(v[0], v[1]), pack_f16(v[2], v[3]));
-                s = fmaf(q[0], k[0], q[1] * k[1]) + fmaf(q[2], k[2], q[3] * k[3]);
-                qq = fmaf(q[0], q[0], q[1] * q[1]) + fmaf(q[2], q[2], q[3] * q[3]);
-                kk = fmaf(k[0], k[0], k[1] * k[1]) + fmaf(k[2], k[2], k[3] * k[3]);
+                    make_uint2(pack_bf16(k[r][0], k[r][1]), pack_bf16(k[r][2], k[r][3]));
+                reinterpret_cast<uint2 *>(a.vh + i * FW)[lane] =
+                    make_uint2(pack_f16(v[r][0], v[r][1]), pack_f16(v[r][2], v[r][3]));
+                s = fmaf(q[r][0], k[r][0], q[r][1] * k[r][1]) + fmaf(q[r][2], k[r][2], q[r][3] * k[r][3]);
+                qq = fmaf(q[r][0], q[r][0], q[r][1] * q[r][1]) + fmaf(q[r][2], q[r][2], q[r][3] * q[r][3]);
+                kk = fmaf(k[r][0], k[r][0], k[r][1] * k[r][1]) + fmaf(k[r][2], k[r][2], k[r][3] * k[r][3]);
             }
 #pragma unroll
             for (int o = 16; o; o >>= 1) {
                 s += __shfl_xor_sync(0xffffffffu, s, o);
                 qq += __shfl_xor_sync(0xffffffffu, qq, o);
                 kk += __shfl_xor_sync(0xffffffffu, kk, o);
+                s0 += __shfl_xor_sync(0xffffffffu, s0, o);
+                s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+                sq += __shfl_xor_sync(0xffffffffu, sq, o);
             }
             kmax = fmaxf(kmax, sqrtf(kk));
             if (lane == 0) {
-                a.m0[i] = s;
+                // every sampled key is at or before the row (row 0 sees only itself)
+                a.m0[i] = t0 + r > 0 ? fmaxf(fmaxf(s, sq), fmaxf(s0, s1)) : s;
                 a.sprev[i] = -INFINITY;  // no previous-position rule
                 a.cnorm[i] = sqrtf(qq);
             }
@@ -1436,25 +1506,22 @@ int tc_dot_attention(const float *qkv, int B, int T, int E, int H, float *o, voi
     __half *vh = (__half *)(w + lay.vh);
     float *m0 = (float *)(w + lay.m0), *sp = (float *)(w + lay.sp), *cn = (float *)(w + lay.cn);
     unsigned int *cm = (unsigned int *)(w + lay.cm);
-    int *sched = (int *)(w + lay.sched);
+    int *sched = (int *)(w + lay.sched), *tflag = (int *)(w + lay.tflag);
     if (cudaMemsetAsync(cm, 0, BH * sizeof(unsigned int), st) != cudaSuccess ||
-        cudaMemsetAsync(sched, 0, 2 * sizeof(int), st) != cudaSuccess) {
+        cudaMemsetAsync(sched, 0, 2 * sizeof(int), st) != cudaSuccess ||
+        cudaMemsetAsync(tflag, 0, BH * n_qt * sizeof(int), st) != cudaSuccess) {
         *msg = "cudaMemsetAsync failed";
         return WB_ECUDA;
     }
     DotFeatArgs fa{qkv, B, H, T, hd, E, 1.0f / std::sqrt((float)hd), qf, kf, vh, m0, sp, cn, cm};
     {
         ProfScope ps("dot_feat", st);
-        const int rows = dot_feat_rows(E);
-        const unsigned grid = (unsigned)((long long)B * ((T + rows - 1) / rows));
-        const size_t smem = (size_t)rows * 3 * E * sizeof(float);
-        auto kern = fw == 64 ? dot_feat_kernel<64> : dot_feat_kernel<128>;
-        if (smem > 48 * 1024 &&
-            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
-            *msg = "n_embd too large for the dot-product feature kernel";
-            return WB_EINVAL;
-        }
-        kern<<<grid, DOT_FEAT_WARPS * 32, smem, st>>>(fa, rows);
+        const unsigned grid = (unsigned)((long long)B * ((T + DOT_FEAT_ROWS - 1) / DOT_FEAT_ROWS));
+        // full-width slices whose starts (row stride 3E, head offsets hd, the
+        // base) are aligned to the lane's FW / 32 floats load as vectors
+        const int vec = hd == fw && E % (fw / 32) == 0 && ((uintptr_t)qkv % (fw / 8)) == 0;
+        if (fw == 64) dot_feat_kernel<64><<<grid, DOT_FEAT_WARPS * 32, 0, st>>>(fa, vec);
+        else dot_feat_kernel<128><<<grid, DOT_FEAT_WARPS * 32, 0, st>>>(fa, vec);
     }
     if (force_fallback) {
         // testing: every tile fails the bound (|q| max|k| - s_self > limit)
@@ -1481,7 +1548,7 @@ int tc_dot_attention(const float *qkv, int B, int T, int E, int H, float *o, voi
     }
     WbSeqView none{};
     AttnTcArgs aa{(int)BH, H, T, hd, n_qt, H, 0, (int)(BH * n_qt), m0, sp, cn, cm, none, o, E, sched, dev_err, 1,
-                  BOUND_LIMIT};
+                  DOT_BOUND_LIMIT, 0, tflag};
     if ((rc = fw == 64 ? launch_attn_tc<64, 64>(tq, tk, tv, aa, sm_count, st, msg)
                        : launch_attn_tc<128, 128>(tq, tk, tv, aa, sm_count, st, msg)))
         return rc;
